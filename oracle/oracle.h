@@ -1,0 +1,70 @@
+/*
+ * CPU oracle for the speculative-decoding verify path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links, loads or
+ * calls this code; only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg use it, and only as the checker or the timed CPU baseline.
+ *
+ * It restates, in plain C compiled with -ffp-contract=off, the reference's CPU
+ * arithmetic for the path (Inferno.jl, paths relative to that project):
+ *   - dequantizers   src/Dequant.jl:304-321 (Q8_0), :325-375 (Q4_K),
+ *                    :379-441 (Q5_K), :558-601 (Q6_K)
+ *   - block layouts  src/kernels/quant_kernels.c:25-62
+ *   - GEMV           src/QuantsCPU.jl / src/ModelCPU.jl:285-379 (dequant, then dot)
+ *   - acceptance     src/SpeculativeDecoding.jl:20-104, src/CommonOps.jl:172-318
+ *                    (bug-fixed semantics, see accept.c)
+ *   - model forward  src/ModelCPU.jl:95-1020, src/FlashAttention.jl:19-84 (model.c)
+ * The K-quant encoders are this project's own (the reference has none).
+ */
+#ifndef INFERNO_ORACLE_H
+#define INFERNO_ORACLE_H
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GGML type ids, src/GGUF.jl:25-60 */
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q5_K = 13, OR_Q6_K = 14 };
+
+float    or_f16_to_f32(uint16_t h);
+uint16_t or_f32_to_f16(float f);              /* round to nearest even */
+
+/* bytes for one row of `cols` elements, 0 if cols is not a multiple of the block */
+int64_t  or_row_bytes(int type, int64_t cols);
+
+/* quantize rows x cols f32 (row-major) into GGUF blocks, own encoder */
+int or_quantize(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
+
+/* dequantize n elements of GGUF blocks to f32, bit-exact with src/Dequant.jl */
+int or_dequantize(int type, const uint8_t *blocks, int64_t n, float *out);
+
+/* Y[n][r] = sum_k W[r][k] * X[n][k]; W quantized rows x cols, X ncols x cols.
+ * or_gemm_f64 accumulates the dequantized f32 weights in double ("truth"),
+ * or_gemm_f32 accumulates in float, index order (the reference's fallback). */
+int or_gemm_f64(int type, const uint8_t *W, int64_t rows, int64_t cols,
+                const float *X, int ncols, double *Y);
+int or_gemm_f32(int type, const uint8_t *W, int64_t rows, int64_t cols,
+                const float *X, int ncols, float *Y);
+
+/* ---- acceptance (accept.c) ---- */
+float or_exp(float x);                          /* shared Cody-Waite exp */
+int   or_sample_from_probs(const float *probs, int n, float r);   /* 1-based, SpeculativeDecoding.jl:20-30 */
+void  or_chunk_stats(const float *row, int V, float inv_temp, float *cmax, float *csum);
+void  or_row_stats(const float *cmax, const float *csum, int nchunk, float inv_temp,
+                   float *rmax, float *rsum);
+int   or_accept(const float *target, const float *draft, const int32_t *draft_tokens,
+                const float *uniforms, int batch, int gamma, int vocab, float temperature,
+                int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out);
+int   or_accept_greedy(const float *target, const int32_t *draft_tokens, int batch,
+                       int gamma, int vocab, int32_t *accept_count, int32_t *out_tokens);
+int   or_argmax(const float *row, int n);
+
+#define OR_ACCEPT_CHUNK 2048   /* elements per statistics chunk */
+#define OR_ACCEPT_THREADS 256  /* lanes per chunk in the canonical reduction */
+
+#ifdef __cplusplus
+}
+#endif
+#endif
