@@ -1,0 +1,132 @@
+/*
+ * inferno_b200 — C ABI of the B200 (sm_100a) speculative-decoding verify path
+ * for Inferno.jl.  Plain pointers and sizes only; no CUDA or torch types.
+ *
+ * Conventions
+ *   - Every native entry point returns int: IFR_OK (0) or an IFR_ERR_* code;
+ *     ifr_last_error() gives this thread's message for the last failure.
+ *   - Sizes are validated before any launch; invalid ones return IFR_ERR_ARG.
+ *   - "dev" pointers are CUDA device pointers on the context's device; all
+ *     work is enqueued on the context's stream (asynchronous unless stated).
+ *   - Token ids are 0-based (the Julia side adds 1).
+ *   - Weight types are GGML type ids (src/GGUF.jl:25-60 of the reference).
+ *   - Activations X are column-major by token: X[n*cols + k] is element k of
+ *     verify column (token) n; outputs Y[n*rows + r].
+ */
+#ifndef INFERNO_B200_H
+#define INFERNO_B200_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* the library is built with hidden visibility; only these symbols export */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define IFR_OK 0
+#define IFR_ERR_ARG 1          /* invalid argument / size / type            */
+#define IFR_ERR_CUDA 2         /* CUDA runtime error (message has details)  */
+#define IFR_ERR_NOMEM 3        /* device allocation failed                  */
+#define IFR_ERR_TIMEOUT 4      /* a bounded device-side wait ran out        */
+#define IFR_ERR_UNSUPPORTED 5  /* not built for this device / type          */
+
+#define IFR_TYPE_F32 0
+#define IFR_TYPE_F16 1
+#define IFR_TYPE_Q8_0 8
+#define IFR_TYPE_Q4_K 12
+#define IFR_TYPE_Q5_K 13
+#define IFR_TYPE_Q6_K 14
+
+#define IFR_MAX_VERIFY_COLS 8  /* columns per pass of the small-N kernel */
+
+typedef struct ifr_ctx ifr_ctx;
+typedef struct ifr_tensor ifr_tensor;
+
+/* thread-local message of the last failing call on this thread ("" if none) */
+const char *ifr_last_error(void);
+/* library version, major*10000 + minor*100 + patch */
+int ifr_version(void);
+
+/* --- context: one device + one stream, one host thread at a time ---------
+ * Replaces the reference's process-global library handle and Q8_K buffer
+ * pool (src/QuantizedKernels.jl:22-72). */
+int ifr_ctx_create(int device, ifr_ctx **out);
+int ifr_ctx_destroy(ifr_ctx *ctx);
+/* use an external cudaStream_t (passed as void*); NULL restores the own one */
+int ifr_ctx_set_stream(ifr_ctx *ctx, void *cuda_stream);
+int ifr_ctx_get_stream(ifr_ctx *ctx, void **cuda_stream);
+/* pre-size the context's scratch for ifr_qgemm up to (cols, ncols) so that
+ * later calls allocate nothing (needed before CUDA graph capture) */
+int ifr_ctx_reserve(ifr_ctx *ctx, int64_t max_cols, int max_ncols);
+int ifr_sync(ifr_ctx *ctx);
+
+/* --- weights: device-resident quantized matrices -------------------------
+ * rows = outer (output) dim, cols = inner dim; bytes are GGUF blocks, row by
+ * row (src/LoaderCPU.jl:123-161 keeps the same bytes as Q*_Matrix).  The
+ * library owns the device copy (it may re-lay out blocks for the kernels;
+ * values are unchanged, see ifr_dequant).  Synchronous. */
+int ifr_weights_upload(ifr_ctx *ctx, int type, const void *host_bytes,
+                       int64_t rows, int64_t cols, ifr_tensor **out);
+int ifr_weights_from_device(ifr_ctx *ctx, int type, const void *dev_bytes,
+                            int64_t rows, int64_t cols, ifr_tensor **out);
+int ifr_tensor_free(ifr_tensor *t);
+int ifr_tensor_info(const ifr_tensor *t, int *type, int64_t *rows, int64_t *cols,
+                    int64_t *device_bytes);
+
+/* bit-exact dequantization to f32 [rows][cols] (dev_out), the values of
+ * src/Dequant.jl:304-601 (dequantize_q8_0/q4_k/q5_k/q6_k) */
+int ifr_dequant(ifr_ctx *ctx, const ifr_tensor *t, float *dev_out);
+
+/* Y = W * X for ncols verify columns (any ncols >= 1; passes of 8).
+ * f32 activations, exact fp16 hi/lo split on the tensor cores, f32
+ * accumulation.  Replaces q4_k_gemv/q5_k_gemv/q6_k_gemv/q8_0_gemv
+ * (src/kernels/quant_kernels.c:602-697), called once per column by the
+ * reference (src/ModelCPU.jl:285-379). */
+int ifr_qgemm(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
+              float *Y_dev);
+
+/* --- acceptance ------------------------------------------------------------
+ * Sampled verification (fixed semantics of src/SpeculativeDecoding.jl:37-104):
+ *   target  [batch][gamma+1][vocab] f32 logits (dev)
+ *   draft   [batch][gamma][vocab]   f32 logits (dev)
+ *   draft_tokens [batch][gamma] (dev) or NULL: drafts are then drawn from
+ *           softmax(draft/T) with u_d
+ *   uniforms [batch][2*gamma+1] (dev): u_d[gamma], u_a[gamma], u_rb
+ *   accept_count [batch], out_tokens [batch][gamma+1] (-1 past the emitted
+ *   tokens), draft_out [batch][gamma] or NULL.  Bit-exact with the oracle. */
+int ifr_accept(ifr_ctx *ctx, const float *target, const float *draft,
+               const int32_t *draft_tokens, const float *uniforms, int batch,
+               int gamma, int vocab, float temperature, int32_t *accept_count,
+               int32_t *out_tokens, int32_t *draft_out);
+/* greedy verification (src/ModelCPU.jl:2099-2115): accept while
+ * argmax(target[i]) == draft[i], then emit the target argmax */
+int ifr_accept_greedy(ifr_ctx *ctx, const float *target, const int32_t *draft_tokens,
+                      int batch, int gamma, int vocab, int32_t *accept_count,
+                      int32_t *out_tokens);
+
+/* --- legacy shims: the reference's C symbols, identical signatures --------
+ * src/kernels/quant_kernels.c:602-697, bound by src/QuantizedKernels.jl:90-145.
+ * HOST pointers; each call uploads W and x, runs ifr_qgemm on device 0 and
+ * copies out back (parity / drop-in, not speed).  q8_scratch is ignored: the
+ * activations stay f32.  On failure `out` is filled with NaN and the message
+ * is printed to stderr and kept in ifr_last_error(). */
+void q4_k_gemv(const uint8_t *weight, const float *x, float *out, void *q8_scratch,
+               int inner_dim, int outer_dim);
+void q5_k_gemv(const uint8_t *weight, const float *x, float *out, void *q8_scratch,
+               int inner_dim, int outer_dim);
+void q6_k_gemv(const uint8_t *weight, const float *x, float *out, void *q8_scratch,
+               int inner_dim, int outer_dim);
+void q8_0_gemv(const uint8_t *weight, const float *x, float *out, int inner_dim,
+               int outer_dim);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif

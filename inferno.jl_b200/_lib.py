@@ -1,0 +1,76 @@
+"""ctypes binding of libinferno_b200.so (C ABI in include/inferno_b200.h).
+
+Loading fails loudly: there is no CPU fallback for any entry point.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libinferno_b200.so")
+
+IFR_OK, IFR_ERR_ARG, IFR_ERR_CUDA, IFR_ERR_NOMEM, IFR_ERR_TIMEOUT, IFR_ERR_UNSUPPORTED = range(6)
+ERR_NAMES = {1: "IFR_ERR_ARG", 2: "IFR_ERR_CUDA", 3: "IFR_ERR_NOMEM", 4: "IFR_ERR_TIMEOUT",
+             5: "IFR_ERR_UNSUPPORTED"}
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 0, 1, 8, 12, 13, 14
+MAX_VERIFY_COLS = 8
+
+# every symbol the header declares, with (restype, argtypes)
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i = ctypes.c_int
+_f = ctypes.c_float
+SIGNATURES = {
+    "ifr_last_error": (ctypes.c_char_p, []),
+    "ifr_version": (_i, []),
+    "ifr_ctx_create": (_i, [_i, ctypes.POINTER(_vp)]),
+    "ifr_ctx_destroy": (_i, [_vp]),
+    "ifr_ctx_set_stream": (_i, [_vp, _vp]),
+    "ifr_ctx_get_stream": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "ifr_ctx_reserve": (_i, [_vp, _i64, _i]),
+    "ifr_sync": (_i, [_vp]),
+    "ifr_weights_upload": (_i, [_vp, _i, _vp, _i64, _i64, ctypes.POINTER(_vp)]),
+    "ifr_weights_from_device": (_i, [_vp, _i, _vp, _i64, _i64, ctypes.POINTER(_vp)]),
+    "ifr_tensor_free": (_i, [_vp]),
+    "ifr_tensor_info": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                             ctypes.POINTER(_i64)]),
+    "ifr_dequant": (_i, [_vp, _vp, _vp]),
+    "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "ifr_accept": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
+    "ifr_accept_greedy": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "q4_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),
+    "q5_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),
+    "q6_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),
+    "q8_0_gemv": (None, [_vp, _vp, _vp, _i, _i]),
+}
+
+_lib = None
+
+
+class IfrError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"{ERR_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+def load(path=None):
+    """Load the shared library (building it first if absent and nvcc exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = path or LIB_PATH
+    if not os.path.exists(path):
+        from . import build as _build
+        _build.build()
+    L = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc):
+    if rc != IFR_OK:
+        raise IfrError(rc, load().ifr_last_error().decode())
+    return rc

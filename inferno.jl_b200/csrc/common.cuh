@@ -1,0 +1,109 @@
+// Shared device helpers and the internal (C++) interface between the kernel
+// files and the C ABI in api.cu.  sm_100a only.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define IFR_DEV __device__ __forceinline__
+
+namespace ifr {
+
+// ---- device layouts of the quantized tensors --------------------------------
+// Q4_K, Q5_K: GGUF blocks unchanged, row-major (144 / 176 bytes per 256).
+// Q6_K: four planes per tensor (same 210 bytes per 256, re-laid out so that
+//   every load is 16-byte aligned and each lane's bytes are contiguous):
+//     ql  [rows][nb][128]  lane t's 32 bytes at 32t: ql'[32t+4k+j] = ql[16k+4t+j]
+//     qh  [rows][nb][64]   lane t's 16 bytes at 16t: qh'[16t+4k+j] = qh[16k+4t+j]
+//     sc  [rows][nb][16]   int8 group scales, unchanged
+//     d   [rows][nb]       f16 super-scale
+// Q8_0: two planes: qs [rows][nb][32] int8, d [rows][nb] f16.
+struct QTensor {
+    int type;
+    int64_t rows, cols;
+    int64_t nb;         // blocks per row (256-element for K-quants, 32 for Q8_0)
+    uint8_t *data;      // device base
+    int64_t bytes;      // device bytes
+    // plane offsets (bytes from data) for the planar types
+    int64_t off_ql, off_qh, off_sc, off_d;
+};
+
+int64_t raw_row_bytes(int type, int64_t cols);
+int64_t device_bytes(int type, int64_t rows, int64_t cols);
+
+// raw GGUF bytes on the device -> device layout (dst distinct from src)
+cudaError_t repack(const QTensor &t, const uint8_t *raw, cudaStream_t s);
+// bit-exact dequantization
+cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s);
+
+// activation packing scratch for the small-N tensor-core GEMV
+int64_t qgemm_scratch_bytes(int type, int64_t cols);
+// Y[ncols][rows] = W * X[ncols][cols], ncols <= 8 per call
+cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y,
+                        void *scratch, cudaStream_t s);
+
+cudaError_t accept_sampled(const float *target, const float *draft, const int32_t *draft_tokens,
+                           const float *uniforms, int batch, int gamma, int vocab, float T,
+                           int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out,
+                           void *scratch, cudaStream_t s);
+int64_t accept_scratch_bytes(int batch, int gamma, int vocab);
+cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int batch, int gamma,
+                          int vocab, int32_t *accept_count, int32_t *out_tokens, void *scratch,
+                          cudaStream_t s);
+int64_t accept_greedy_scratch_bytes(int batch, int gamma, int vocab);
+
+}  // namespace ifr
+
+// ---- small device utilities ---------------------------------------------------
+namespace ifr {
+
+IFR_DEV uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+    uint32_t r;
+    // (a & mask) | orv, one LOP3
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));
+    return r;
+}
+
+IFR_DEV uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+IFR_DEV uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+IFR_DEV uint32_t hmul2_u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// D = A(16x16 f16) * B(16x8 f16) + C, f32 accumulate
+IFR_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                      uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A(16x8 f16) * B(8x8 f16) + C, f32 accumulate
+IFR_DEV void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm(
+        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+
+IFR_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+IFR_DEV uint4 ldg_nc4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+IFR_DEV uint2 ldg_nc2(const void *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+
+}  // namespace ifr

@@ -1,0 +1,169 @@
+"""GPU parity: bit-exact dequantization and the small-N verify GEMV against
+the CPU oracle, through the C ABI (libinferno_b200.so)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = [12, 13, 14, 8]
+NAMES = {12: "Q4_K", 13: "Q5_K", 14: "Q6_K", 8: "Q8_0"}
+# f32 accumulation of exact products: norm-relative error per output column
+TOL = 2e-6
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def random_valid_blocks(O, rng, qt, rows, cols):
+    be, bb = O.BLOCK[qt]
+    nb = rows * cols // be
+    blk = rng.integers(0, 256, size=(nb, bb), dtype=np.uint8)
+    f16 = lambda: np.asarray(rng.normal(0, 0.01, nb), np.float16).view(np.uint8).reshape(nb, 2)  # noqa: E731
+    if qt in (12, 13):
+        blk[:, 0:2] = f16()
+        blk[:, 2:4] = f16()
+    elif qt == 14:
+        blk[:, 208:210] = f16()
+    else:
+        blk[:, 0:2] = f16()
+    return blk.ravel()
+
+
+@pytest.mark.parametrize("qt", FORMATS)
+def test_dequant_bit_exact(O, ctx, qt):
+    rng = np.random.default_rng(qt)
+    for rows, cols in ((16, 1024), (37, 2048)):
+        q = random_valid_blocks(O, rng, qt, rows, cols)
+        W = ctx.upload(qt, q, rows, cols)
+        got = ctx.dequant(W).cpu().numpy().ravel()
+        ref = O.dequantize(qt, q, rows * cols)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), NAMES[qt]
+    # encoder-made weights, and the golden gguf-py blocks
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "dequant_golden.npz"))
+    be, _ = O.BLOCK[qt]
+    cols = 256 if qt != 8 else 32
+    W = ctx.upload(qt, g[f"{NAMES[qt]}_blocks"], 64 * be // cols, cols)
+    got = ctx.dequant(W).cpu().numpy().ravel()
+    assert np.array_equal(got.view(np.uint32), g[f"{NAMES[qt]}_gguf_py"].view(np.uint32))
+
+
+SHAPES = [(256, 256), (1000, 1024), (96, 3584), (130, 4096)]
+
+
+@pytest.mark.parametrize("qt", FORMATS)
+@pytest.mark.parametrize("M,K", SHAPES)
+def test_qgemm_parity(O, ctx, qt, M, K):
+    torch = _torch()
+    rng = np.random.default_rng(M * 7 + K + qt)
+    q = O.quantize(qt, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    W = ctx.upload(qt, q, M, K)
+    X = rng.normal(0, 1, (8, K)).astype(np.float32)
+    ref = O.gemm_f64(qt, q, M, K, X)
+    Xd = torch.from_numpy(X).cuda()
+    for n in (1, 2, 3, 4, 5, 8):
+        Y = ctx.qgemm(W, Xd[:n].contiguous()).cpu().numpy()
+        err = O.norm_rel(Y, ref[:n])
+        assert err.max() < TOL, (NAMES[qt], M, K, n, err)
+
+
+@pytest.mark.parametrize("qt", FORMATS)
+def test_qgemm_random_blocks_and_scales(O, ctx, qt):
+    """raw random blocks (all scale/min bit patterns) and activations spanning
+    many binades, a zero column and a column of one huge element"""
+    torch = _torch()
+    rng = np.random.default_rng(100 + qt)
+    M, K = 200, 2048
+    q = random_valid_blocks(O, rng, qt, M, K)
+    W = ctx.upload(qt, q, M, K)
+    X = rng.normal(0, 1, (6, K)).astype(np.float32)
+    X[1] *= 1e-20
+    X[2] *= 1e20
+    X[3] = 0.0
+    X[4] = 0.0
+    X[4, 777] = 3e4
+    X[5] *= np.exp(rng.normal(0, 4, K)).astype(np.float32)
+    ref = O.gemm_f64(qt, q, M, K, X)
+    Y = ctx.qgemm(W, torch.from_numpy(X).cuda()).cpu().numpy()
+    assert np.all(Y[3] == 0.0)
+    keep = [0, 1, 2, 4, 5]
+    err = O.norm_rel(Y[keep], ref[keep])
+    assert err.max() < 1e-5, (NAMES[qt], err)
+
+
+def test_qgemm_q8_0_ragged_k(O, ctx):
+    """Q8_0 with K not a multiple of 256 (the config-5 draft has 1152)"""
+    torch = _torch()
+    rng = np.random.default_rng(5)
+    for M, K in ((77, 1152), (64, 32), (33, 288)):
+        q = O.quantize(8, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+        W = ctx.upload(8, q, M, K)
+        X = rng.normal(0, 1, (5, K)).astype(np.float32)
+        Y = ctx.qgemm(W, torch.from_numpy(X).cuda()).cpu().numpy()
+        assert O.norm_rel(Y, O.gemm_f64(8, q, M, K, X)).max() < TOL
+
+
+def test_qgemm_many_columns(O, ctx):
+    """more than 8 columns run in passes of 8"""
+    torch = _torch()
+    rng = np.random.default_rng(6)
+    M, K = 300, 1024
+    q = O.quantize(12, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    W = ctx.upload(12, q, M, K)
+    X = rng.normal(0, 1, (19, K)).astype(np.float32)
+    Y = ctx.qgemm(W, torch.from_numpy(X).cuda()).cpu().numpy()
+    assert O.norm_rel(Y, O.gemm_f64(12, q, M, K, X)).max() < TOL
+
+
+@pytest.mark.parametrize("qt", FORMATS)
+def test_qgemm_full_size_sampled_rows(O, ctx, qt):
+    """BASELINE sweep shape 151936 x 4096 at N=5: rows sampled across the
+    whole matrix (first, last, random) checked against the oracle"""
+    torch = _torch()
+    rng = np.random.default_rng(200 + qt)
+    M, K = 151936, 4096
+    rb = O.row_bytes(qt, K)
+    # encode a 4096-row pool and tile it (keeps the CPU encoder fast)
+    pool = O.quantize(qt, rng.normal(0, 0.02, (4096, K)).astype(np.float32)).reshape(4096, rb)
+    idx = rng.integers(0, 4096, M)
+    q = pool[idx].ravel()
+    W = ctx.upload(qt, q, M, K)
+    X = rng.normal(0, 1, (5, K)).astype(np.float32)
+    Y = ctx.qgemm(W, torch.from_numpy(X).cuda()).cpu().numpy()
+    rows = np.unique(np.concatenate([[0, 1, 15, 16, M - 1, M - 16], rng.integers(0, M, 200)]))
+    ref = O.gemm_f64(qt, pool[idx[rows]].ravel(), len(rows), K, X)
+    err = O.norm_rel(Y[:, rows], ref)
+    assert err.max() < TOL, (NAMES[qt], err)
+    del W
+
+
+def test_legacy_shims(O, pkg):
+    """the reference's own symbols (host pointers) through quantized_kernels"""
+    import importlib
+    qk = importlib.import_module("inferno_b200.quantized_kernels")
+    rng = np.random.default_rng(8)
+    M, K = 123, 1024
+    for qt, fn in ((12, qk.q4_k_gemv_), (13, qk.q5_k_gemv_), (14, qk.q6_k_gemv_), (8, qk.q8_0_gemv_)):
+        q = O.quantize(qt, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+        x = rng.normal(0, 1, K).astype(np.float32)
+        out = np.zeros(M, np.float32)
+        fn(out, q, x, K, M)
+        assert O.norm_rel(out, O.gemm_f64(qt, q, M, K, x)[0]).max() < TOL
+
+
+def test_argument_errors(O, ctx, pkg):
+    import ctypes
+    L = pkg.load()
+    rng = np.random.default_rng(9)
+    q = O.quantize(12, rng.normal(0, 0.02, (4, 256)).astype(np.float32))
+    h = ctypes.c_void_p()
+    qp = q.ctypes.data_as(ctypes.c_void_p)
+    assert L.ifr_weights_upload(ctx.handle, 12, qp, 4, 250, ctypes.byref(h)) == 1   # cols % 256
+    assert b"multiple" in L.ifr_last_error()
+    assert L.ifr_weights_upload(ctx.handle, 3, qp, 4, 256, ctypes.byref(h)) == 1    # type
+    assert b"unsupported weight type" in L.ifr_last_error()
+    assert L.ifr_weights_upload(ctx.handle, 12, qp, 0, 256, ctypes.byref(h)) == 1   # rows
+    W = ctx.upload(12, q, 4, 256)
+    assert L.ifr_qgemm(ctx.handle, W.handle, ctypes.c_void_p(16), 0, ctypes.c_void_p(16)) == 1

@@ -1,0 +1,149 @@
+"""CPU tests of the oracle against the golden fixtures and the reference's
+known answers (no GPU).  The oracle is the checker for every GPU parity test,
+so it is pinned here first."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+FORMATS = [("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14), ("Q8_0", 8)]
+
+
+@pytest.mark.parametrize("name,qt", FORMATS)
+def test_dequant_bit_exact_vs_gguf_py(O, name, qt):
+    """64 random valid blocks: bit-exact with gguf-py 0.19.0's dequantize."""
+    g = np.load(os.path.join(GOLD, "dequant_golden.npz"))
+    be, _ = O.BLOCK[qt]
+    got = O.dequantize(qt, g[f"{name}_blocks"], 64 * be)
+    assert np.array_equal(got.view(np.uint32), g[f"{name}_gguf_py"].view(np.uint32))
+
+
+@pytest.mark.parametrize("name,qt", FORMATS)
+def test_dequant_known_answer(O, name, qt):
+    """hand-built blocks with d = 1.0 (f16 0x3c00): values written out by hand"""
+    g = np.load(os.path.join(GOLD, "dequant_golden.npz"))
+    be, _ = O.BLOCK[qt]
+    got = O.dequantize(qt, g[f"{name}_ka_block"], be)
+    assert np.array_equal(got, g[f"{name}_ka_expected"])
+
+
+@pytest.mark.parametrize("name,qt", FORMATS)
+def test_gemv_vs_reference_c_kernel(O, name, qt):
+    """Oracle GEMV against outputs of the reference's own quant_kernels.c
+    (Q8_K activation rounding for the K-quants: within 2e-2 norm-relative;
+    Q8_0 keeps f32 activations: 1e-5)."""
+    g = np.load(os.path.join(GOLD, "gemv_golden.npz"))
+    M, K = int(g["M"]), int(g["K"])
+    Y = O.gemm_f64(qt, g[f"{name}_W"], M, K, g["X"])
+    tol = 1e-5 if qt == 8 else 2e-2
+    assert O.norm_rel(g[f"{name}_ref"], Y).max() < tol
+
+
+def test_gemv_f32_vs_f64(O):
+    rng = np.random.default_rng(1)
+    M, K = 64, 2048
+    q = O.quantize(12, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    X = rng.normal(0, 1, (3, K)).astype(np.float32)
+    assert O.norm_rel(O.gemm_f32(12, q, M, K, X), O.gemm_f64(12, q, M, K, X)).max() < 1e-5
+
+
+@pytest.mark.parametrize("name,qt", FORMATS)
+def test_encoder_round_trip(O, name, qt):
+    """own encoder: dequant(quant(w)) close to w, and re-encoding is stable"""
+    rng = np.random.default_rng(2)
+    w = rng.normal(0, 0.02, (8, 512)).astype(np.float32)
+    q = O.quantize(qt, w)
+    assert q.size == 8 * O.row_bytes(qt, 512)
+    d = O.dequantize(qt, q, w.size).reshape(w.shape)
+    rel = np.linalg.norm(d - w) / np.linalg.norm(w)
+    assert rel < {12: 0.1, 13: 0.05, 14: 0.03, 8: 0.01}[qt]
+
+
+def test_f16_conversion(O):
+    L = O.lib()
+    vals = np.array([0.0, 1.0, -2.5, 65504.0, 6.1035156e-05, 5.96e-08, 1e-9, 70000.0, 0.1],
+                    np.float32)
+    for v in vals:
+        assert L.or_f32_to_f16(float(v)) == int(np.float16(v).view(np.uint16))
+    for h in range(0, 0x7c00, 37):
+        assert L.or_f16_to_f32(h) == float(np.uint16(h).view(np.float16))
+
+
+def test_sample_from_probs_known_answers(O):
+    """tests/unit/test_speculative_decoding.jl:13-46 of the reference: the
+    answers hold for every draw r in (0, 1)"""
+    g = json.load(open(os.path.join(GOLD, "sampler_golden.json")))
+    for case in g["sample_from_probs"]:
+        for r in (1e-6, 0.3, 0.999):
+            assert O.sample_from_probs(case["probs"], r) == case["expect"]
+
+
+def test_exp_accuracy(O):
+    xs = np.concatenate([np.linspace(-87, 0, 4001), np.linspace(0, 88, 2001)]).astype(np.float32)
+    got = np.array([O.exp(v) for v in xs], np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    assert np.max(np.abs(got - ref) / ref) < 2e-7
+    assert O.exp(-100.0) == 0.0
+
+
+def _softmax(x, T):
+    z = (x - x.max()) / T
+    e = np.exp(z.astype(np.float64))
+    return e / e.sum()
+
+
+def test_accept_distribution_matches_target(O):
+    """Rejection sampling property: with drafts drawn from p_d, the first
+    emitted token is distributed as p_t (exact algorithm, tiny vocab)."""
+    rng = np.random.default_rng(3)
+    V, T, n = 6, 0.8, 40000
+    tl = rng.normal(0, 1.5, V).astype(np.float32)
+    dl = (tl + rng.normal(0, 1.0, V)).astype(np.float32)
+    tgt = np.broadcast_to(np.stack([tl, tl]), (n, 2, V)).copy()
+    dft = np.broadcast_to(dl, (n, 1, V)).copy()
+    u = rng.random((n, 3), dtype=np.float32)
+    acc, out, dtok = O.accept(tgt, dft, u, T)
+    first = out[:, 0]
+    emp = np.bincount(first, minlength=V) / n
+    pt = _softmax(tl, T)
+    assert np.abs(emp - pt).max() < 0.01
+    # drafts follow p_d
+    pd = _softmax(dl, T)
+    assert np.abs(np.bincount(dtok[:, 0], minlength=V) / n - pd).max() < 0.01
+    # accept rate = sum min(p_t, p_d)
+    assert abs(acc.mean() - np.minimum(pt, pd).sum()) < 0.01
+
+
+def test_accept_identical_distributions_accepts_all(O):
+    rng = np.random.default_rng(4)
+    B, G, V = 8, 4, 3000
+    tgt = rng.normal(0, 3, (B, G + 1, V)).astype(np.float32)
+    dft = tgt[:, :G].copy()
+    u = rng.random((B, 2 * G + 1), dtype=np.float32) * 0.999
+    acc, out, d = O.accept(tgt, dft, u, 0.8)
+    assert (acc == G).all()
+    assert (out[:, :G] == d).all() and (out[:, G] >= 0).all()
+
+
+def test_accept_greedy_semantics(O):
+    B, G, V = 3, 3, 10
+    tgt = np.zeros((B, G + 1, V), np.float32)
+    am = np.array([[1, 2, 3, 4], [1, 5, 3, 4], [7, 7, 7, 7]])
+    for b in range(B):
+        for i in range(G + 1):
+            tgt[b, i, am[b, i]] = 1.0
+    drafts = np.array([[1, 2, 3], [1, 2, 3], [0, 7, 7]], np.int32)
+    acc, out = O.accept_greedy(tgt, drafts)
+    assert acc.tolist() == [3, 1, 0]
+    assert out[0].tolist() == [1, 2, 3, 4]
+    assert out[1].tolist() == [1, 5, -1, -1]
+    assert out[2].tolist() == [7, -1, -1, -1]
+
+
+def test_argmax_ties_first_index(O):
+    L = O.lib()
+    import ctypes
+    a = np.array([0.0, 2.0, 1.0, 2.0], np.float32)
+    assert L.or_argmax(a.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), 4) == 1
