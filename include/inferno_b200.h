@@ -55,7 +55,8 @@ int ifr_version(void);
  * pool (src/QuantizedKernels.jl:22-72). */
 int ifr_ctx_create(int device, ifr_ctx **out);
 int ifr_ctx_destroy(ifr_ctx *ctx);
-/* use an external cudaStream_t (passed as void*); NULL restores the own one */
+/* enqueue on an external cudaStream_t (passed as void*; NULL = the CUDA
+ * default stream).  A new context starts on its own non-blocking stream. */
 int ifr_ctx_set_stream(ifr_ctx *ctx, void *cuda_stream);
 int ifr_ctx_get_stream(ifr_ctx *ctx, void **cuda_stream);
 /* pre-size the context's scratch for ifr_qgemm up to (cols, ncols) so that

@@ -159,7 +159,7 @@ int ifr_ctx_destroy(ifr_ctx *c) {
 
 int ifr_ctx_set_stream(ifr_ctx *c, void *s) {
     if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
-    c->stream = s ? (cudaStream_t)s : c->own;
+    c->stream = (cudaStream_t)s;  // CUDA's convention: NULL is the default stream
     return IFR_OK;
 }
 
