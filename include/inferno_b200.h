@@ -59,9 +59,12 @@ int ifr_ctx_destroy(ifr_ctx *ctx);
  * default stream).  A new context starts on its own non-blocking stream. */
 int ifr_ctx_set_stream(ifr_ctx *ctx, void *cuda_stream);
 int ifr_ctx_get_stream(ifr_ctx *ctx, void **cuda_stream);
-/* pre-size the context's scratch for ifr_qgemm up to (cols, ncols) so that
- * later calls allocate nothing (needed before CUDA graph capture) */
-int ifr_ctx_reserve(ifr_ctx *ctx, int64_t max_cols, int max_ncols);
+/* pre-size the context's scratch for ifr_accept / ifr_accept_greedy up to
+ * (batch, gamma, vocab) so later calls allocate nothing (e.g. before CUDA
+ * graph capture).  ifr_qgemm needs no scratch. */
+int ifr_ctx_reserve_accept(ifr_ctx *ctx, int batch, int gamma, int vocab);
+/* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
+ * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);
 
 /* --- weights: device-resident quantized matrices -------------------------
@@ -82,6 +85,7 @@ int ifr_tensor_info(const ifr_tensor *t, int *type, int64_t *rows, int64_t *cols
 int ifr_dequant(ifr_ctx *ctx, const ifr_tensor *t, float *dev_out);
 
 /* Y = W * X for ncols verify columns (any ncols >= 1; passes of 8).
+ * X must be 16-byte aligned.
  * f32 activations, exact fp16 hi/lo split on the tensor cores, f32
  * accumulation.  Replaces q4_k_gemv/q5_k_gemv/q6_k_gemv/q8_0_gemv
  * (src/kernels/quant_kernels.c:602-697), called once per column by the

@@ -94,8 +94,8 @@ class Context:
     def set_stream(self, stream):
         check(load().ifr_ctx_set_stream(self.handle, ctypes.c_void_p(stream.cuda_stream)))
 
-    def reserve(self, max_cols, max_ncols=MAX_VERIFY_COLS):
-        check(load().ifr_ctx_reserve(self.handle, int(max_cols), int(max_ncols)))
+    def reserve_accept(self, batch, gamma, vocab):
+        check(load().ifr_ctx_reserve_accept(self.handle, int(batch), int(gamma), int(vocab)))
 
     def sync(self):
         check(load().ifr_sync(self.handle))

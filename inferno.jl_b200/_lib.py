@@ -26,7 +26,7 @@ SIGNATURES = {
     "ifr_ctx_destroy": (_i, [_vp]),
     "ifr_ctx_set_stream": (_i, [_vp, _vp]),
     "ifr_ctx_get_stream": (_i, [_vp, ctypes.POINTER(_vp)]),
-    "ifr_ctx_reserve": (_i, [_vp, _i64, _i]),
+    "ifr_ctx_reserve_accept": (_i, [_vp, _i, _i, _i]),
     "ifr_sync": (_i, [_vp]),
     "ifr_weights_upload": (_i, [_vp, _i, _vp, _i64, _i64, ctypes.POINTER(_vp)]),
     "ifr_weights_from_device": (_i, [_vp, _i, _vp, _i64, _i64, ctypes.POINTER(_vp)]),

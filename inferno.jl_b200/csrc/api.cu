@@ -94,18 +94,9 @@ int make_tensor(int type, int64_t rows, int64_t cols, int device, ifr_tensor **o
     q.rows = rows;
     q.cols = cols;
     q.nb = type == IFR_TYPE_Q8_0 ? cols / 32 : cols / 256;
+    q.nrb = (rows + 15) / 16;
+    q.nu = (cols + 255) / 256;
     q.bytes = ifr::device_bytes(type, rows, cols);
-    const int64_t nblk = rows * q.nb;
-    q.off_ql = q.off_qh = q.off_sc = q.off_d = 0;
-    if (type == IFR_TYPE_Q6_K) {
-        q.off_ql = 0;
-        q.off_qh = nblk * 128;
-        q.off_sc = nblk * 192;
-        q.off_d = nblk * 208;
-    } else if (type == IFR_TYPE_Q8_0) {
-        q.off_ql = 0;
-        q.off_d = nblk * 32;
-    }
     cudaError_t e = cudaMalloc(&q.data, q.bytes);
     if (e != cudaSuccess) {
         delete t;
@@ -169,21 +160,22 @@ int ifr_ctx_get_stream(ifr_ctx *c, void **s) {
     return IFR_OK;
 }
 
-int ifr_ctx_reserve(ifr_ctx *c, int64_t max_cols, int max_ncols) {
-    if (!c || max_cols < 1 || max_ncols < 1) return fail(IFR_ERR_ARG, "invalid reserve arguments");
+int ifr_ctx_reserve_accept(ifr_ctx *c, int batch, int gamma, int vocab) {
+    if (!c || batch < 1 || gamma < 0 || gamma > 64 || vocab < 1)
+        return fail(IFR_ERR_ARG, "invalid reserve arguments");
     DeviceGuard g(c->device);
-    int64_t need = 0;
-    for (int t : {IFR_TYPE_Q4_K, IFR_TYPE_Q5_K, IFR_TYPE_Q6_K, IFR_TYPE_Q8_0}) {
-        int64_t b = ifr::qgemm_scratch_bytes(t, max_cols);
-        if (b > need) need = b;
-    }
-    return ensure_scratch(c, (size_t)need);
+    int64_t need = ifr::accept_scratch_bytes(batch, gamma < 1 ? 1 : gamma, vocab);
+    int64_t g2 = ifr::accept_greedy_scratch_bytes(batch, gamma, vocab);
+    return ensure_scratch(c, (size_t)(need > g2 ? need : g2));
 }
 
 int ifr_sync(ifr_ctx *c) {
     if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
     DeviceGuard g(c->device);
     IFR_CHECK_CUDA(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    int flag = 0;
+    IFR_CHECK_CUDA(ifr::read_device_error(&flag, c->stream), "read device error flag");
+    if (flag) return fail(IFR_ERR_TIMEOUT, "a bounded device-side wait ran out (pipeline stalled); results of the pending work are invalid");
     return IFR_OK;
 }
 
@@ -216,17 +208,12 @@ int ifr_weights_upload(ifr_ctx *c, int type, const void *host, int64_t rows, int
     ifr_tensor *t = nullptr;
     int rc = make_tensor(type, rows, cols, c->device, &t);
     if (rc) return rc;
-    cudaError_t e;
-    if (type == IFR_TYPE_Q4_K || type == IFR_TYPE_Q5_K) {
-        e = cudaMemcpy(t->q.data, host, raw, cudaMemcpyHostToDevice);
-    } else {
-        void *tmp = nullptr;
-        e = cudaMalloc(&tmp, raw);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, host, raw, cudaMemcpyHostToDevice, c->stream);
-        if (e == cudaSuccess) e = ifr::repack(t->q, (const uint8_t *)tmp, c->stream);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
-        if (tmp) cudaFree(tmp);
-    }
+    void *tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, raw);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, host, raw, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = ifr::repack(t->q, (const uint8_t *)tmp, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (tmp) cudaFree(tmp);
     if (e != cudaSuccess) {
         cudaFree(t->q.data);
         delete t;
@@ -265,13 +252,11 @@ int ifr_qgemm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float 
     if (!c || !W || !X || !Y) return fail(IFR_ERR_ARG, "NULL argument");
     if (ncols < 1) return fail(IFR_ERR_ARG, "ncols must be >= 1 (got %d)", ncols);
     if (W->device != c->device) return fail(IFR_ERR_ARG, "tensor lives on device %d, context on %d", W->device, c->device);
+    if (((uintptr_t)X & 15) || ((uintptr_t)Y & 3)) return fail(IFR_ERR_ARG, "X must be 16-byte and Y 4-byte aligned");
     DeviceGuard g(c->device);
-    int rc = ensure_scratch(c, (size_t)ifr::qgemm_scratch_bytes(W->q.type, W->q.cols));
-    if (rc) return rc;
     for (int n0 = 0; n0 < ncols; n0 += IFR_MAX_VERIFY_COLS) {
         int n = ncols - n0 < IFR_MAX_VERIFY_COLS ? ncols - n0 : IFR_MAX_VERIFY_COLS;
-        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows,
-                                        c->scratch, c->stream),
+        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, c->stream),
                        "qgemm launch");
     }
     return IFR_OK;

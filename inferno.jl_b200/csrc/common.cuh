@@ -9,23 +9,17 @@
 
 namespace ifr {
 
-// ---- device layouts of the quantized tensors --------------------------------
-// Q4_K, Q5_K: GGUF blocks unchanged, row-major (144 / 176 bytes per 256).
-// Q6_K: four planes per tensor (same 210 bytes per 256, re-laid out so that
-//   every load is 16-byte aligned and each lane's bytes are contiguous):
-//     ql  [rows][nb][128]  lane t's 32 bytes at 32t: ql'[32t+4k+j] = ql[16k+4t+j]
-//     qh  [rows][nb][64]   lane t's 16 bytes at 16t: qh'[16t+4k+j] = qh[16k+4t+j]
-//     sc  [rows][nb][16]   int8 group scales, unchanged
-//     d   [rows][nb]       f16 super-scale
-// Q8_0: two planes: qs [rows][nb][32] int8, d [rows][nb] f16.
+// ---- device layout of the quantized tensors (see tiles.cuh) ------------------
+// [row block of 16][unit of 256 columns][M-tile], same bytes as the GGUF
+// blocks, re-arranged per M-tile for the tensor-core GEMV.
 struct QTensor {
     int type;
     int64_t rows, cols;
-    int64_t nb;         // blocks per row (256-element for K-quants, 32 for Q8_0)
+    int64_t nb;         // GGUF blocks per row (256 elements, 32 for Q8_0)
+    int64_t nrb;        // row blocks of 16 (rows padded up)
+    int64_t nu;         // units of 256 columns (cols padded up for Q8_0)
     uint8_t *data;      // device base
     int64_t bytes;      // device bytes
-    // plane offsets (bytes from data) for the planar types
-    int64_t off_ql, off_qh, off_sc, off_d;
 };
 
 int64_t raw_row_bytes(int type, int64_t cols);
@@ -36,11 +30,10 @@ cudaError_t repack(const QTensor &t, const uint8_t *raw, cudaStream_t s);
 // bit-exact dequantization
 cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s);
 
-// activation packing scratch for the small-N tensor-core GEMV
-int64_t qgemm_scratch_bytes(int type, int64_t cols);
-// Y[ncols][rows] = W * X[ncols][cols], ncols <= 8 per call
-cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y,
-                        void *scratch, cudaStream_t s);
+// Y[ncols][rows] = W * X[ncols][cols], ncols <= 8 per call; X 16-byte aligned
+cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, cudaStream_t s);
+// device-side error flag set by bounded waits that ran out (read and cleared)
+cudaError_t read_device_error(int *flag, cudaStream_t s);
 
 cudaError_t accept_sampled(const float *target, const float *draft, const int32_t *draft_tokens,
                            const float *uniforms, int batch, int gamma, int vocab, float T,

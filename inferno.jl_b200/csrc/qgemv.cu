@@ -1,5 +1,6 @@
 // Small-N quantized GEMM ("verify GEMV"): Y[n][r] = sum_k W[r][k] X[n][k]
-// for N <= 8 verify columns, W in Q4_K / Q5_K / Q6_K / Q8_0.
+// for N <= 8 verify columns, W in Q4_K / Q5_K / Q6_K / Q8_0 (M-tile layout,
+// tiles.cuh).
 //
 // Replaces q4_k_gemv .. q8_0_gemv (reference src/kernels/quant_kernels.c:602-697),
 // which the reference calls once per token; here the N tokens of one verify
@@ -7,233 +8,203 @@
 //
 // Arithmetic (exact up to f32 accumulation):
 //   * weights are unpacked in registers to fp16 *integers* (magic-number
-//     trick, no conversions) and, for Q4_K/Q5_K, multiplied by their 6-bit
-//     sub-block scale with one fp16 FMA - the product sc*q <= 63*31 < 2048 is
-//     exact in fp16;
-//   * each f32 activation is scaled by a power of two per 256-element unit
-//     and split exactly into hi + lo fp16 halves, which become two B columns;
-//   * mma.sync m16n8k16 (fp16 x fp16 -> f32) forms sum_k A*B over a unit;
-//     the super-block scales d / dmin and the unit's power of two are applied
-//     to the f32 accumulators; the Q4_K/Q5_K "min" term is one more m16n8k8
-//     against per-sub-block activation sums.
-// The MMA k-order is a permutation of the elements chosen so that each lane's
-// loaded bytes feed its A fragment directly; pack_x writes B in the same order.
+//     trick) and, for Q4_K/Q5_K, multiplied by their 6-bit sub-block scale
+//     with one fp16 FMA - sc*q <= 63*31 < 2048 is exact in fp16;
+//   * each f32 activation is scaled by a power of two per 256-column unit and
+//     split exactly into hi + lo fp16 halves, which become two B columns;
+//   * mma.sync m16n8k16 (fp16 x fp16 -> f32) forms sum_k A*B over a unit; the
+//     super-block scales and the unit's power of two are applied to the f32
+//     accumulators; the Q4_K/Q5_K "min" term is one m16n8k8 against
+//     per-sub-block activation sums.
 //
-// Work split: 16-row tiles; the 8 warps of a CTA split the K units of WR
-// tiles (WR x WK = 8) and reduce through shared memory.
+// Data movement (one persistent CTA per SM, 8 consumer warps + 1 producer warp):
+//   * the producer streams weight stages (16 M-tiles = one row group x the
+//     units of one K pass) global -> shared with cp.async.bulk into a ring of
+//     S stages guarded by mbarriers, keeping ~S x 37..70 KB in flight per SM;
+//   * consumer warp w owns one unit of the pass (w % UW) and two M-tiles of
+//     the row group; its B fragments for that unit stay in registers for the
+//     whole pass, built straight from X (no separate packing launch);
+//   * the UW unit-warps of an M-tile pair reduce through shared memory; K
+//     passes accumulate into Y (read-modify-write by the same thread).
+// Every mbarrier wait is bounded (~2 s); on expiry the kernel records an
+// error flag, stops waiting and drains, and the host reports IFR_ERR_TIMEOUT.
 #include "common.cuh"
+#include "tiles.cuh"
 
 namespace ifr {
 
-constexpr int kThreads = 256;
+__device__ int g_dev_error = 0;
 
-// ---- MMA k-slot -> element index inside a 256-element chunk ----------------
-// slot 0..3 = kcol 2t, 2t+1, 2t+8, 2t+9 of the lane quad t = lane % 4.
-__host__ __device__ inline int elem_qk(int s, int t, int slot) {  // Q4_K / Q5_K
-    int c = s >> 3, w = (s >> 1) & 3, h = s & 1, p = t >> 1;
-    int j4 = 2 * c + p;
-    int l = 16 * (t & 1) + 4 * w + h + ((slot & 1) ? 2 : 0);
-    return 64 * j4 + ((slot & 2) ? 32 : 0) + l;
-}
-// sub-block fed to k-row (2t + kr) of the Q4_K/Q5_K min MMA
-__host__ __device__ inline int minsub_qk(int t, int kr) {
-    int p = t >> 1;
-    return (t & 1) ? (4 + 2 * p + kr) : (2 * p + kr);
-}
-__host__ __device__ inline int jmap(int slot) { return slot == 0 ? 0 : slot == 1 ? 2 : slot == 2 ? 1 : 3; }
-__host__ __device__ inline int elem_q6k(int s, int t, int slot) {
-    int n = s >> 3, qq = (s >> 1) & 3, b = s & 1;
-    return 128 * n + 32 * qq + 16 * b + 4 * t + jmap(slot);
-}
-__host__ __device__ inline int elem_q80(int s, int t, int slot) {  // s = step in the chunk
-    return 32 * (s >> 1) + 8 * t + 4 * (s & 1) + jmap(slot);
-}
+constexpr int kConsumers = 8;
+constexpr int kThreads = 32 * kConsumers;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
-// ---- scratch layout -----------------------------------------------------------
-struct XPack {
-    uint4 *xp;     // [chunk][8 step pairs][NT][32 lanes]  (B fragments, 2 steps each)
-    uint32_t *xm;  // [chunk][NT][32 lanes]                (min-MMA B fragment)
-    float *es;     // [unit][8 cols]                        (2^-e of each unit)
-};
+IFR_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-static inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
-
-int64_t qgemm_scratch_bytes(int type, int64_t cols) {
-    int64_t nch = (cols + 255) / 256;
-    int64_t nunits = type == 8 ? (cols + 31) / 32 : nch;
-    return align256(nch * 8 * 2 * 32 * 16) + align256(nch * 2 * 32 * 4) + align256(nunits * 8 * 4);
+IFR_DEV void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
 }
-
-static XPack carve(void *scratch, int type, int64_t cols) {
-    int64_t nch = (cols + 255) / 256;
-    char *p = (char *)scratch;
-    XPack x;
-    x.xp = (uint4 *)p;
-    p += align256(nch * 8 * 2 * 32 * 16);
-    x.xm = (uint32_t *)p;
-    p += align256(nch * 2 * 32 * 4);
-    x.es = (float *)p;
-    (void)type;
-    return x;
+IFR_DEV void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
 }
-
-IFR_DEV uint32_t pack_h2(__half lo, __half hi) {
-    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+IFR_DEV void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+IFR_DEV bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait: false (and the device error flag set) after ~2 s
+IFR_DEV bool mbar_wait(uint64_t *b, uint32_t parity) {
+    if (mbar_try_wait(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(b, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicExch(&g_dev_error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+IFR_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+IFR_DEV void consumer_bar() { __syncthreads(); }
+IFR_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 2^k for integer k in [-126, 127]
+IFR_DEV uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+IFR_DEV uint32_t u4w(const uint4 &v, int w) { return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w; }
+
 IFR_DEV float pow2i(int k) { return __int_as_float((k + 127) << 23); }
-
-// scale exponent so that max|x| * 2^e < 2^14 (fp16-safe with headroom)
+// exponent e so that max|x| * 2^e < 2^14 (fp16-safe with headroom)
 IFR_DEV int unit_exp(float m) {
     if (!(m > 0.f) || isinf(m)) return 0;
     int ex;
-    frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
-    int e = 14 - ex;
+    frexpf(m, &ex);
+    const int e = 14 - ex;
     return e < -100 ? -100 : (e > 100 ? 100 : e);
 }
+IFR_DEV uint32_t hi_lo_h2(float v) {  // (hi, lo) with v = hi + lo exactly up to f32 rounding of lo
+    const __half h = __float2half_rn(v);
+    const __half l = __float2half_rn(v - __half2float(h));
+    return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
+}
 
-// One CTA per 256-element chunk of K.  FMT: 12/13 (K-quants with mins), 14, 8.
-template <int FMT>
-__global__ void __launch_bounds__(kThreads) pack_x_kernel(const float *__restrict__ X, int ncols,
-                                                          int64_t K, int NT, XPack P) {
-    __shared__ __half xh[8][256], xl[8][256];
-    __shared__ float sc_s[8][8];  // [unit in chunk][col] scale 2^e
-    __shared__ float xsum[8][8];  // [col][sub-block] scaled sums (K-quants)
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t chunk = blockIdx.x;
-    const int64_t base = chunk * 256;
-    const int64_t k = base + tid;
-    float v[8];
-#pragma unroll
-    for (int c = 0; c < 8; c++) v[c] = (c < ncols && k < K) ? X[(int64_t)c * K + k] : 0.f;
+// ---- B fragments of one unit, built in registers ------------------------------
+// Lane L holds column 4*nt + L/8 as holder j = L%8 (tiles.cuh holder maps):
+// 32 scaled values as (hi, lo) pairs; fragments are gathered by shuffles.
+template <int FMT, int NT>
+struct BFrag {
+    uint32_t b[16][NT][2];  // per step: (k 2t,2t+1), (k 2t+8,2t+9) halves for B column g
+    uint32_t m[NT];         // min-MMA B fragment (Q4_K/Q5_K)
+    float es[NT];           // 2^-e of the unit for C column 4*nt + t
+};
 
-    // unit maxima -> power-of-two scales
-    if (FMT == 8) {
-        // unit = 32 elements = one warp
+template <int FMT, int NT>
+IFR_DEV void build_b(const float *__restrict__ X, int64_t K, int ncols, int64_t u, int lane,
+                     BFrag<FMT, NT> &F) {
+    const int g = lane >> 2, t = lane & 3, j = lane & 7;
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            float m = fabsf(v[c]);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) sc_s[warp][c] = pow2i(unit_exp(m));
-        }
-    } else {
-        __shared__ float wmax[8][8];
+    for (int nt = 0; nt < NT; nt++) {
+        const int col = 4 * nt + (lane >> 3);
+        float v[32];
+        const float *xc = X + (int64_t)col * K + u * 256;
+        const bool has = col < ncols;
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            float m = fabsf(v[c]);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) wmax[warp][c] = m;
-        }
-        __syncthreads();
-        if (tid < 8) {
-            float m = 0.f;
-            for (int w = 0; w < 8; w++) m = fmaxf(m, wmax[w][tid]);
-            sc_s[0][tid] = pow2i(unit_exp(m));
-        }
-    }
-    __syncthreads();
-    const int unit_in_chunk = (FMT == 8) ? warp : 0;
+        for (int r4 = 0; r4 < 8; r4++) {
+            const int e = elem_of_holder(FMT, j, 4 * r4);
+            const int64_t k = u * 256 + e;
+            if (has && k + 3 < K) {
+                const float4 q = __ldg(reinterpret_cast<const float4 *>(xc + e));
+                v[4 * r4] = q.x; v[4 * r4 + 1] = q.y; v[4 * r4 + 2] = q.z; v[4 * r4 + 3] = q.w;
+            } else {
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
-        float sv = v[c] * sc_s[unit_in_chunk][c];  // exact (power of two)
-        __half h = __float2half_rn(sv);
-        __half l = __float2half_rn(sv - __half2float(h));
-        xh[c][tid] = h;
-        xl[c][tid] = l;
-        v[c] = sv;
-    }
-    // unit scales out: es = 2^-e
-    if (FMT == 8) {
-        if (lane < 8) {
-            int64_t unit = chunk * 8 + warp;
-            if (unit * 32 < K) P.es[unit * 8 + lane] = 1.0f / sc_s[warp][lane];
-        }
-    } else {
-        if (tid < 8) P.es[chunk * 8 + tid] = 1.0f / sc_s[0][tid];
-        // per-sub-block sums of the scaled values, x 2^-5 for fp16 range
-        // thread layout: col = warp, sub-block = lane/4, quarter = lane%4
-        {
-            int c = warp, j = lane >> 2, q = lane & 3;
-            float s = 0.f;
-            for (int e = 0; e < 8; e++) s += __half2float(xh[c][32 * j + 8 * q + e]) +
-                                            __half2float(xl[c][32 * j + 8 * q + e]);
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            if (q == 0) xsum[c][j] = s * 0.03125f;
-        }
-    }
-    __syncthreads();
-
-    // B fragments: item = (step pair sp, lane) ; 8 x 32 = 256 items per nt
-    {
-        const int sp = tid >> 5, g = lane >> 2, t = lane & 3;
-        for (int nt = 0; nt < NT; nt++) {
-            const int col = 4 * nt + (g >> 1), part = g & 1;
-            uint32_t r[4];
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int s = 2 * sp + h;
-                __half e4[4];
-#pragma unroll
-                for (int slot = 0; slot < 4; slot++) {
-                    int e = (FMT == 14) ? elem_q6k(s, t, slot)
-                          : (FMT == 8)  ? elem_q80(s, t, slot)
-                                        : elem_qk(s, t, slot);
-                    e4[slot] = part ? xl[col][e] : xh[col][e];
-                }
-                r[2 * h] = pack_h2(e4[0], e4[1]);
-                r[2 * h + 1] = pack_h2(e4[2], e4[3]);
+                for (int i = 0; i < 4; i++) v[4 * r4 + i] = (has && k + i < K) ? __ldg(xc + e + i) : 0.f;
             }
-            P.xp[((chunk * 8 + sp) * NT + nt) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
         }
-    }
-    if (FMT == 12 || FMT == 13) {
-        if (tid < 32 * NT) {
-            const int nt = tid >> 5, g = lane >> 2, t = lane & 3;
-            const int col = 4 * nt + (g >> 1), part = g & 1;
-            __half hv[2];
+        float m = 0.f;
+#pragma unroll
+        for (int r = 0; r < 32; r++) m = fmaxf(m, fabsf(v[r]));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        const int ex = unit_exp(m);
+        const float scl = pow2i(ex);
+        F.es[nt] = __shfl_sync(0xffffffffu, pow2i(-ex), 8 * t);
+        uint32_t H[32];
+#pragma unroll
+        for (int r = 0; r < 32; r++) {
+            v[r] *= scl;  // exact
+            H[r] = hi_lo_h2(v[r]);
+        }
+        const int src_base = 8 * (g >> 1), part = g & 1;
+#pragma unroll
+        for (int s = 0; s < 16; s++) {
+            uint32_t hv[4];
+#pragma unroll
+            for (int slot = 0; slot < 4; slot++) {
+                const int src = src_base + holder_of(FMT, elem_of(FMT, s, t, slot));
+                const uint32_t w = __shfl_sync(0xffffffffu, H[slot_reg(FMT, s, slot)], src);
+                hv[slot] = part ? (w >> 16) : (w & 0xffffu);
+            }
+            F.b[s][nt][0] = hv[0] | (hv[1] << 16);
+            F.b[s][nt][1] = hv[2] | (hv[3] << 16);
+        }
+        if (FMT == 12 || FMT == 13) {
+            // sub-block sums: holder j has elements of sub-blocks j/2 (r < 16) and 4 + j/2
+            float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+            for (int r = 0; r < 16; r++) { p0 += v[r]; p1 += v[16 + r]; }
+            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+            uint32_t hm[2];
 #pragma unroll
             for (int kr = 0; kr < 2; kr++) {
-                float s = xsum[col][minsub_qk(t, kr)];
-                __half h = __float2half_rn(s);
-                hv[kr] = part ? __float2half_rn(s - __half2float(h)) : h;
+                const int src = src_base + 4 * (t >> 1) + 2 * kr;
+                const float a = __shfl_sync(0xffffffffu, p0, src);
+                const float b = __shfl_sync(0xffffffffu, p1, src);
+                const uint32_t w = hi_lo_h2(((t & 1) ? b : a) * 0.03125f);
+                hm[kr] = part ? (w >> 16) : (w & 0xffffu);
             }
-            P.xm[(chunk * NT + nt) * 32 + lane] = pack_h2(hv[0], hv[1]);
+            F.m[nt] = hm[0] | (hm[1] << 16);
         }
     }
 }
 
 // ---- fp16 constants from a byte ---------------------------------------------
-// (v, v) as f16x2 for an integer byte v < 1024
 IFR_DEV uint32_t bcast_byte_h2(uint32_t word, int byte) {
-    // place the byte in the low byte of both halves, add the 1024 magic, subtract it
-    uint32_t sel = (uint32_t)byte | (4u << 4) | ((uint32_t)byte << 8) | (4u << 12);
-    uint32_t x = __byte_perm(word, 0u, sel) | 0x64006400u;
-    return hsub2_u(x, 0x64006400u);
+    const uint32_t sel = (uint32_t)byte | (4u << 4) | ((uint32_t)byte << 8) | (4u << 12);
+    return hsub2_u(__byte_perm(word, 0u, sel) | 0x64006400u, 0x64006400u);
 }
-// (b0, b1) as f16x2 from the two low bytes of `word`
 IFR_DEV uint32_t bytes01_h2(uint32_t word) {
-    uint32_t x = __byte_perm(word, 0u, 0x4140u) | 0x64006400u;
-    return hsub2_u(x, 0x64006400u);
+    return hsub2_u(__byte_perm(word, 0u, 0x4140u) | 0x64006400u, 0x64006400u);
 }
-
 constexpr uint32_t kNegH1024 = 0xE400E400u;  // (-1024, -1024)
 constexpr uint32_t kH1_16 = 0x2C002C00u;     // (1/16, 1/16)
 constexpr uint32_t kNegH64 = 0xD400D400u;    // (-64, -64)
 
-// Per row of a Q4_K/Q5_K super-block, everything lane (g,t) needs.
 struct QKRow {
-    uint32_t klo[2], nlo[2], khi[2], nhi[2];  // per chunk c: low-nibble and high-nibble FMA constants
-    uint32_t mA;                              // min-MMA A fragment (2 mins)
+    uint32_t klo[2], nlo[2], khi[2], nhi[2];
+    uint32_t mA;
     float d, dm32;
 };
 
+// scales of the four sub-blocks lane quad t reads (2p, 2p+1, 4+2p, 5+2p)
 IFR_DEV void qk_row_consts(const uint4 &h, int t, QKRow &R) {
     const int p = t >> 1;
     const uint32_t A = h.y >> (16 * p), B = h.z >> (16 * p), C = h.w >> (16 * p);
-    const uint32_t sc_a = A & 0x3F3Fu;
-    const uint32_t m_a = B & 0x3F3Fu;
+    const uint32_t sc_a = A & 0x3F3Fu, m_a = B & 0x3F3Fu;
     const uint32_t sc_b = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
     const uint32_t m_b = ((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
 #pragma unroll
@@ -250,359 +221,329 @@ IFR_DEV void qk_row_consts(const uint4 &h, int t, QKRow &R) {
     R.dm32 = h2f((uint16_t)(h.x >> 16)) * 32.0f;
 }
 
-IFR_DEV uint32_t u4w(const uint4 &v, int w) { return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w; }
-
-// Q4_K / Q5_K kernel.  W raw blocks; nb super-blocks per row.
-template <bool Q5, int NT>
-__global__ void __launch_bounds__(kThreads) qgemv_qk_kernel(const uint8_t *__restrict__ W, int64_t M,
-                                                            int nb, XPack P, float *__restrict__ Y,
-                                                            int ncols, int WK) {
-    constexpr int BLK = Q5 ? 176 : 144;
-    constexpr int QS = Q5 ? 48 : 16;
-    __shared__ float red[8][NT * 4][32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// ---- one M-tile (16 rows x 256 columns) from shared memory --------------------
+template <int FMT, int NT>
+IFR_DEV void mtile_qk(const uint8_t *tile, int lane, const BFrag<FMT, NT> &F, float (&tot)[NT][4]) {
+    constexpr bool Q5 = FMT == 13;
     const int g = lane >> 2, t = lane & 3;
-    const int WR = 8 / WK, wr = warp / WK, wk = warp % WK;
-    const int64_t nrb = (M + 15) / 16;
-    const int64_t rowbytes = (int64_t)nb * BLK;
-
-    for (int64_t rb0 = (int64_t)blockIdx.x * WR; rb0 < nrb; rb0 += (int64_t)gridDim.x * WR) {
-        const int64_t rb = rb0 + wr;
-        float tot[NT][4];
+    const uint4 h0 = lds128(tile + qk_hdr(g)), h1 = lds128(tile + qk_hdr(g + 8));
+    uint4 q0[2], q1[2], qh0 = {}, qh1 = {};
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++)
+    for (int c = 0; c < 2; c++) {
+        q0[c] = lds128(tile + qk_qs(Q5, c, g, t));
+        q1[c] = lds128(tile + qk_qs(Q5, c, g + 8, t));
+    }
+    if (Q5) {
+        qh0 = lds128(tile + q5_qh(g, t & 1));
+        qh1 = lds128(tile + q5_qh(g + 8, t & 1));
+    }
+    QKRow R0, R1;
+    qk_row_consts(h0, t, R0);
+    qk_row_consts(h1, t, R1);
+    // two accumulator sets (even / odd words) halve the MMA dependency chains
+    float csc[2][NT][4], cm[NT][4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) tot[nt][i] = 0.f;
-        if (rb < nrb) {
-            const int64_t r0 = rb * 16 + g, r1 = r0 + 8;
-            const uint8_t *w0 = W + (r0 < M ? r0 : M - 1) * rowbytes;
-            const uint8_t *w1 = W + (r1 < M ? r1 : M - 1) * rowbytes;
-            for (int u = wk; u < nb; u += WK) {
-                const uint8_t *b0 = w0 + (int64_t)u * BLK, *b1 = w1 + (int64_t)u * BLK;
-                const uint4 h0 = ldg_nc4(b0), h1 = ldg_nc4(b1);
-                uint4 q0[2], q1[2], qh0, qh1;
-                q0[0] = ldg_nc4(b0 + QS + 16 * t);
-                q0[1] = ldg_nc4(b0 + QS + 64 + 16 * t);
-                q1[0] = ldg_nc4(b1 + QS + 16 * t);
-                q1[1] = ldg_nc4(b1 + QS + 64 + 16 * t);
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) csc[0][nt][i] = csc[1][nt][i] = cm[nt][i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+        const int j4 = 2 * c + (t >> 1);
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const uint32_t W0 = u4w(q0[c], w), W1 = u4w(q1[c], w);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t s0 = h ? (W0 >> 8) : W0, s1 = h ? (W1 >> 8) : W1;
+                uint32_t lo0 = lop_and_or(s0, 0x000F000Fu, 0x64006400u);
+                uint32_t hi0 = lop_and_or(s0, 0x00F000F0u, 0x64006400u);
+                uint32_t lo1 = lop_and_or(s1, 0x000F000Fu, 0x64006400u);
+                uint32_t hi1 = lop_and_or(s1, 0x00F000F0u, 0x64006400u);
                 if (Q5) {
-                    qh0 = ldg_nc4(b0 + 16 + 16 * (t & 1));
-                    qh1 = ldg_nc4(b1 + 16 + 16 * (t & 1));
+                    const uint32_t H0 = u4w(qh0, w) >> (8 * h + 2 * j4);
+                    const uint32_t H1 = u4w(qh1, w) >> (8 * h + 2 * j4);
+                    lo0 |= (H0 << 4) & 0x00100010u;
+                    hi0 |= (H0 << 7) & 0x01000100u;
+                    lo1 |= (H1 << 4) & 0x00100010u;
+                    hi1 |= (H1 << 7) & 0x01000100u;
                 }
-                const uint4 *xpu = P.xp + (int64_t)u * 8 * NT * 32 + lane;
-                uint32_t xmv[NT];
-                float esv[NT];
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    xmv[nt] = P.xm[((int64_t)u * NT + nt) * 32 + lane];
-                    esv[nt] = P.es[(int64_t)u * 8 + 4 * nt + t];
-                }
-                QKRow R0, R1;
-                qk_row_consts(h0, t, R0);
-                qk_row_consts(h1, t, R1);
-
-                float csc[NT][4], cm[NT][4];
+                const uint32_t a0 = hfma2_u(lo0, R0.klo[c], R0.nlo[c]);
+                const uint32_t a1 = hfma2_u(lo1, R1.klo[c], R1.nlo[c]);
+                const uint32_t a2 = hfma2_u(hi0, R0.khi[c], R0.nhi[c]);
+                const uint32_t a3 = hfma2_u(hi1, R1.khi[c], R1.nhi[c]);
+                const int s = 8 * c + 2 * w + h;
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                    for (int i = 0; i < 4; i++) csc[nt][i] = cm[nt][i] = 0.f;
-
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    const int j4 = 2 * c + (t >> 1);
-#pragma unroll
-                    for (int w = 0; w < 4; w++) {
-                        const uint32_t W0 = u4w(q0[c], w), W1 = u4w(q1[c], w);
-                        uint4 bb[NT];
-#pragma unroll
-                        for (int nt = 0; nt < NT; nt++) bb[nt] = xpu[(4 * c + w) * NT * 32 + nt * 32];
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const uint32_t s0 = h ? (W0 >> 8) : W0, s1 = h ? (W1 >> 8) : W1;
-                            uint32_t lo0 = lop_and_or(s0, 0x000F000Fu, 0x64006400u);
-                            uint32_t hi0 = lop_and_or(s0, 0x00F000F0u, 0x64006400u);
-                            uint32_t lo1 = lop_and_or(s1, 0x000F000Fu, 0x64006400u);
-                            uint32_t hi1 = lop_and_or(s1, 0x00F000F0u, 0x64006400u);
-                            if (Q5) {
-                                // fifth bit: qh[l] bit 2*j4 (low nibble) / 2*j4+1 (high nibble)
-                                const uint32_t H0 = (u4w(qh0, w) >> (8 * h + 2 * j4));
-                                const uint32_t H1 = (u4w(qh1, w) >> (8 * h + 2 * j4));
-                                lo0 |= (H0 << 4) & 0x00100010u;
-                                hi0 |= (H0 << 7) & 0x01000100u;
-                                lo1 |= (H1 << 4) & 0x00100010u;
-                                hi1 |= (H1 << 7) & 0x01000100u;
-                            }
-                            const uint32_t a0 = hfma2_u(lo0, R0.klo[c], R0.nlo[c]);
-                            const uint32_t a1 = hfma2_u(lo1, R1.klo[c], R1.nlo[c]);
-                            const uint32_t a2 = hfma2_u(hi0, R0.khi[c], R0.nhi[c]);
-                            const uint32_t a3 = hfma2_u(hi1, R1.khi[c], R1.nhi[c]);
-#pragma unroll
-                            for (int nt = 0; nt < NT; nt++) {
-                                const uint32_t bx = h ? bb[nt].z : bb[nt].x;
-                                const uint32_t by = h ? bb[nt].w : bb[nt].y;
-                                mma16816(csc[nt], a0, a1, a2, a3, bx, by);
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    mma1688(cm[nt], R0.mA, R1.mA, xmv[nt]);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float d = (i < 2) ? R0.d : R1.d, dm = (i < 2) ? R0.dm32 : R1.dm32;
-                        tot[nt][i] = fmaf(esv[nt], d * csc[nt][i] - dm * cm[nt][i], tot[nt][i]);
-                    }
-                }
+                    mma16816(csc[w & 1][nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
             }
         }
-        if (WK > 1) {
+    }
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++)
+    for (int nt = 0; nt < NT; nt++) {
+        mma1688(cm[nt], R0.mA, R1.mA, F.m[nt]);
 #pragma unroll
-                for (int i = 0; i < 4; i++) red[warp][nt * 4 + i][lane] = tot[nt][i];
-            __syncthreads();
-            if (wk == 0 && rb < nrb) {
-                for (int q = 1; q < WK; q++)
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++) tot[nt][i] += red[warp + q][nt * 4 + i][lane];
-            }
-            __syncthreads();
-        }
-        if (wk == 0 && rb < nrb) {
-            const int64_t r0 = rb * 16 + g, r1 = r0 + 8;
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                const int col = 4 * nt + t;
-                if (col < ncols) {
-                    if (r0 < M) Y[(int64_t)col * M + r0] = tot[nt][0] + tot[nt][1];
-                    if (r1 < M) Y[(int64_t)col * M + r1] = tot[nt][2] + tot[nt][3];
-                }
-            }
+        for (int i = 0; i < 4; i++) {
+            const float d = i < 2 ? R0.d : R1.d, dm = i < 2 ? R0.dm32 : R1.dm32;
+            tot[nt][i] = fmaf(F.es[nt], d * (csc[0][nt][i] + csc[1][nt][i]) - dm * cm[nt][i], tot[nt][i]);
         }
     }
 }
 
-// Q6_K kernel (planar, lane-permuted layout; see QTensor)
 template <int NT>
-__global__ void __launch_bounds__(kThreads) qgemv_q6k_kernel(const uint8_t *__restrict__ QL,
-                                                             const uint8_t *__restrict__ QH,
-                                                             const int8_t *__restrict__ SC,
-                                                             const uint16_t *__restrict__ DD,
-                                                             int64_t M, int nb, XPack P,
-                                                             float *__restrict__ Y, int ncols, int WK) {
-    __shared__ float red[8][NT * 4][32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<14, NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
-    const int WR = 8 / WK, wr = warp / WK, wk = warp % WK;
-    const int64_t nrb = (M + 15) / 16;
-
-    for (int64_t rb0 = (int64_t)blockIdx.x * WR; rb0 < nrb; rb0 += (int64_t)gridDim.x * WR) {
-        const int64_t rb = rb0 + wr;
-        float tot[NT][4];
+    const float d0 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g)));
+    const float d1 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g + 8)));
+    const uint4 sc0 = lds128(tile + q6_sc(g)), sc1 = lds128(tile + q6_sc(g + 8));
+    uint4 l0[2], l1[2];
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++)
+    for (int h = 0; h < 2; h++) {
+        l0[h] = lds128(tile + q6_ql(h, g, t));
+        l1[h] = lds128(tile + q6_ql(h, g + 8, t));
+    }
+    const uint4 hq0 = lds128(tile + q6_qh(g, t)), hq1 = lds128(tile + q6_qh(g + 8, t));
+    float acc[NT][4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) tot[nt][i] = 0.f;
-        if (rb < nrb) {
-            const int64_t r0 = rb * 16 + g, r1 = r0 + 8;
-            const int64_t i0 = (r0 < M ? r0 : M - 1) * nb, i1 = (r1 < M ? r1 : M - 1) * nb;
-            for (int u = wk; u < nb; u += WK) {
-                const int64_t blk0 = i0 + u, blk1 = i1 + u;
-                uint4 l0[2], l1[2];
-                l0[0] = ldg_nc4(QL + blk0 * 128 + 32 * t);
-                l0[1] = ldg_nc4(QL + blk0 * 128 + 32 * t + 16);
-                l1[0] = ldg_nc4(QL + blk1 * 128 + 32 * t);
-                l1[1] = ldg_nc4(QL + blk1 * 128 + 32 * t + 16);
-                const uint4 hq0 = ldg_nc4(QH + blk0 * 64 + 16 * t);
-                const uint4 hq1 = ldg_nc4(QH + blk1 * 64 + 16 * t);
-                const uint4 sc0 = ldg_nc4(SC + blk0 * 16), sc1 = ldg_nc4(SC + blk1 * 16);
-                const float d0 = h2f(__ldg(DD + blk0)), d1 = h2f(__ldg(DD + blk1));
-                const uint4 *xpu = P.xp + (int64_t)u * 8 * NT * 32 + lane;
-                float esv[NT];
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++) esv[nt] = P.es[(int64_t)u * 8 + 4 * nt + t];
-                float acc[NT][4];
+        for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++)
+    for (int s = 0; s < 16; s++) {
+        const int n = s >> 3, qq = (s >> 1) & 3, b = s & 1;
+        const int kw = 4 * n + 2 * (qq & 1) + b, kh = 2 * n + b;
+        const uint32_t WA0 = u4w(l0[kw >> 2], kw & 3), WA1 = u4w(l1[kw >> 2], kw & 3);
+        const uint32_t H0 = u4w(hq0, kh), H1 = u4w(hq1, kh);
+        const int ns = qq >= 2 ? 4 : 0, hs = 2 * qq;
+        const uint32_t x02_0 = ((WA0 >> ns) & 0x000F000Fu) | (((H0 >> hs) << 4) & 0x00300030u);
+        const uint32_t x13_0 = ((WA0 >> (ns + 8)) & 0x000F000Fu) | (((H0 >> (hs + 8)) << 4) & 0x00300030u);
+        const uint32_t x02_1 = ((WA1 >> ns) & 0x000F000Fu) | (((H1 >> hs) << 4) & 0x00300030u);
+        const uint32_t x13_1 = ((WA1 >> (ns + 8)) & 0x000F000Fu) | (((H1 >> (hs + 8)) << 4) & 0x00300030u);
+        const uint32_t a0 = hsub2_u(x02_0 | 0x64006400u, 0x64206420u);
+        const uint32_t a1 = hsub2_u(x02_1 | 0x64006400u, 0x64206420u);
+        const uint32_t a2 = hsub2_u(x13_0 | 0x64006400u, 0x64206420u);
+        const uint32_t a3 = hsub2_u(x13_1 | 0x64006400u, 0x64206420u);
+        const float f0 = (float)(int8_t)(u4w(sc0, s >> 2) >> (8 * (s & 3)));
+        const float f1 = (float)(int8_t)(u4w(sc1, s >> 2) >> (8 * (s & 3)));
 #pragma unroll
-                    for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
-#pragma unroll
-                for (int s = 0; s < 16; s++) {
-                    const int n = s >> 3, qq = (s >> 1) & 3, b = s & 1;
-                    const int kw = 4 * n + 2 * (qq & 1) + b;  // ql word (of 8)
-                    const int kh = 2 * n + b;                 // qh word (of 4)
-                    const uint32_t WA0 = u4w(l0[kw >> 2], kw & 3), WA1 = u4w(l1[kw >> 2], kw & 3);
-                    const uint32_t H0 = u4w(hq0, kh), H1 = u4w(hq1, kh);
-                    const int ns = (qq >= 2) ? 4 : 0;      // nibble shift
-                    const int hs = 2 * qq;                  // qh bit shift
-                    // bytes 0,2 -> kcols 2t,2t+1 ; bytes 1,3 -> kcols 2t+8,2t+9
-                    uint32_t x02_0 = ((WA0 >> ns) & 0x000F000Fu) | (((H0 >> hs) << 4) & 0x00300030u);
-                    uint32_t x13_0 = ((WA0 >> (ns + 8)) & 0x000F000Fu) | (((H0 >> (hs + 8)) << 4) & 0x00300030u);
-                    uint32_t x02_1 = ((WA1 >> ns) & 0x000F000Fu) | (((H1 >> hs) << 4) & 0x00300030u);
-                    uint32_t x13_1 = ((WA1 >> (ns + 8)) & 0x000F000Fu) | (((H1 >> (hs + 8)) << 4) & 0x00300030u);
-                    const uint32_t a0 = hsub2_u(x02_0 | 0x64006400u, 0x64206420u);
-                    const uint32_t a1 = hsub2_u(x02_1 | 0x64006400u, 0x64206420u);
-                    const uint32_t a2 = hsub2_u(x13_0 | 0x64006400u, 0x64206420u);
-                    const uint32_t a3 = hsub2_u(x13_1 | 0x64006400u, 0x64206420u);
-                    const float f0 = (float)(int8_t)(u4w(sc0, s >> 2) >> (8 * (s & 3)));
-                    const float f1 = (float)(int8_t)(u4w(sc1, s >> 2) >> (8 * (s & 3)));
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        const uint4 bb = xpu[(s >> 1) * NT * 32 + nt * 32];
-                        const uint32_t bx = (s & 1) ? bb.z : bb.x, by = (s & 1) ? bb.w : bb.y;
-                        float c[4] = {0.f, 0.f, 0.f, 0.f};
-                        mma16816(c, a0, a1, a2, a3, bx, by);
-                        acc[nt][0] = fmaf(f0, c[0], acc[nt][0]);
-                        acc[nt][1] = fmaf(f0, c[1], acc[nt][1]);
-                        acc[nt][2] = fmaf(f1, c[2], acc[nt][2]);
-                        acc[nt][3] = fmaf(f1, c[3], acc[nt][3]);
-                    }
-                }
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    tot[nt][0] = fmaf(esv[nt] * d0, acc[nt][0], tot[nt][0]);
-                    tot[nt][1] = fmaf(esv[nt] * d0, acc[nt][1], tot[nt][1]);
-                    tot[nt][2] = fmaf(esv[nt] * d1, acc[nt][2], tot[nt][2]);
-                    tot[nt][3] = fmaf(esv[nt] * d1, acc[nt][3], tot[nt][3]);
-                }
-            }
+        for (int nt = 0; nt < NT; nt++) {
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816(c, a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+            acc[nt][0] = fmaf(f0, c[0], acc[nt][0]);
+            acc[nt][1] = fmaf(f0, c[1], acc[nt][1]);
+            acc[nt][2] = fmaf(f1, c[2], acc[nt][2]);
+            acc[nt][3] = fmaf(f1, c[3], acc[nt][3]);
         }
-        if (WK > 1) {
+    }
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                for (int i = 0; i < 4; i++) red[warp][nt * 4 + i][lane] = tot[nt][i];
-            __syncthreads();
-            if (wk == 0 && rb < nrb) {
-                for (int q = 1; q < WK; q++)
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++) tot[nt][i] += red[warp + q][nt * 4 + i][lane];
-            }
-            __syncthreads();
-        }
-        if (wk == 0 && rb < nrb) {
-            const int64_t r0 = rb * 16 + g, r1 = r0 + 8;
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                const int col = 4 * nt + t;
-                if (col < ncols) {
-                    if (r0 < M) Y[(int64_t)col * M + r0] = tot[nt][0] + tot[nt][1];
-                    if (r1 < M) Y[(int64_t)col * M + r1] = tot[nt][2] + tot[nt][3];
-                }
-            }
-        }
+    for (int nt = 0; nt < NT; nt++) {
+        tot[nt][0] = fmaf(F.es[nt] * d0, acc[nt][0], tot[nt][0]);
+        tot[nt][1] = fmaf(F.es[nt] * d0, acc[nt][1], tot[nt][1]);
+        tot[nt][2] = fmaf(F.es[nt] * d1, acc[nt][2], tot[nt][2]);
+        tot[nt][3] = fmaf(F.es[nt] * d1, acc[nt][3], tot[nt][3]);
     }
 }
 
-// Q8_0 kernel (planar).  Iterates 256-element chunks (8 blocks) of K; a tail
-// chunk may hold fewer blocks.
 template <int NT>
-__global__ void __launch_bounds__(kThreads) qgemv_q80_kernel(const int8_t *__restrict__ QS,
-                                                             const uint16_t *__restrict__ DD,
-                                                             int64_t M, int nb, XPack P,
-                                                             float *__restrict__ Y, int ncols, int WK) {
-    __shared__ float red[8][NT * 4][32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<8, NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
-    const int WR = 8 / WK, wr = warp / WK, wk = warp % WK;
-    const int64_t nrb = (M + 15) / 16;
-    const int nch = (nb + 7) / 8;
-
-    for (int64_t rb0 = (int64_t)blockIdx.x * WR; rb0 < nrb; rb0 += (int64_t)gridDim.x * WR) {
-        const int64_t rb = rb0 + wr;
-        float tot[NT][4];
+    const uint4 dd0 = lds128(tile + q8_d(g)), dd1 = lds128(tile + q8_d(g + 8));
+    float acc[NT][4];
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++)
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-            for (int i = 0; i < 4; i++) tot[nt][i] = 0.f;
-        if (rb < nrb) {
-            const int64_t r0 = rb * 16 + g, r1 = r0 + 8;
-            const int64_t i0 = (r0 < M ? r0 : M - 1) * nb, i1 = (r1 < M ? r1 : M - 1) * nb;
-            for (int ch = wk; ch < nch; ch += WK) {
-                const int nblk = min(8, nb - 8 * ch);
-                uint2 q0[8], q1[8];
-                float d0[8], d1[8];
+        for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    if (j < nblk) {
-                        const int64_t bi0 = i0 + 8 * ch + j, bi1 = i1 + 8 * ch + j;
-                        q0[j] = ldg_nc2(QS + bi0 * 32 + 8 * t);
-                        q1[j] = ldg_nc2(QS + bi1 * 32 + 8 * t);
-                        d0[j] = h2f(__ldg(DD + bi0));
-                        d1[j] = h2f(__ldg(DD + bi1));
-                    }
-                }
-                const uint4 *xpu = P.xp + (int64_t)ch * 8 * NT * 32 + lane;
+    for (int q = 0; q < 4; q++) {
+        const uint4 p0 = lds128(tile + q8_qs(q, g, t)), p1 = lds128(tile + q8_qs(q, g + 8, t));
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    if (j < nblk) {
-                        float c[NT][4];
-#pragma unroll
-                        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                            for (int i = 0; i < 4; i++) c[nt][i] = 0.f;
-                        uint4 bb[NT];
-#pragma unroll
-                        for (int nt = 0; nt < NT; nt++) bb[nt] = xpu[j * NT * 32 + nt * 32];
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const uint32_t W0 = h ? q0[j].y : q0[j].x, W1 = h ? q1[j].y : q1[j].x;
-                            // int8 -> f16: (b ^ 0x80) | 0x6400 = 1152 + q, minus 1152
-                            const uint32_t a0 = hsub2_u(((W0 & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                            const uint32_t a1 = hsub2_u(((W1 & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                            const uint32_t a2 = hsub2_u((((W0 >> 8) & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                            const uint32_t a3 = hsub2_u((((W1 >> 8) & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-#pragma unroll
-                            for (int nt = 0; nt < NT; nt++) {
-                                const uint32_t bx = h ? bb[nt].z : bb[nt].x, by = h ? bb[nt].w : bb[nt].y;
-                                mma16816(c[nt], a0, a1, a2, a3, bx, by);
-                            }
-                        }
-                        const int64_t unit = 8 * (int64_t)ch + j;
-#pragma unroll
-                        for (int nt = 0; nt < NT; nt++) {
-                            const float es = P.es[unit * 8 + 4 * nt + t];
-                            tot[nt][0] = fmaf(es * d0[j], c[nt][0], tot[nt][0]);
-                            tot[nt][1] = fmaf(es * d0[j], c[nt][1], tot[nt][1]);
-                            tot[nt][2] = fmaf(es * d1[j], c[nt][2], tot[nt][2]);
-                            tot[nt][3] = fmaf(es * d1[j], c[nt][3], tot[nt][3]);
-                        }
-                    }
-                }
-            }
-        }
-        if (WK > 1) {
+        for (int bb = 0; bb < 2; bb++) {
+            const int bl = 2 * q + bb;
+            const float db0 = h2f((uint16_t)(u4w(dd0, bl >> 1) >> (16 * (bl & 1))));
+            const float db1 = h2f((uint16_t)(u4w(dd1, bl >> 1) >> (16 * (bl & 1))));
+            float c[NT][4];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) red[warp][nt * 4 + i][lane] = tot[nt][i];
-            __syncthreads();
-            if (wk == 0 && rb < nrb) {
-                for (int q = 1; q < WK; q++)
+                for (int i = 0; i < 4; i++) c[nt][i] = 0.f;
 #pragma unroll
-                    for (int nt = 0; nt < NT; nt++)
+            for (int h = 0; h < 2; h++) {
+                const uint32_t W0 = bb ? (h ? p0.w : p0.z) : (h ? p0.y : p0.x);
+                const uint32_t W1 = bb ? (h ? p1.w : p1.z) : (h ? p1.y : p1.x);
+                // int8 -> f16: (b ^ 0x80) | 0x6400 = 1152 + q, minus 1152
+                const uint32_t a0 = hsub2_u(((W0 & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
+                const uint32_t a1 = hsub2_u(((W1 & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
+                const uint32_t a2 = hsub2_u((((W0 >> 8) & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
+                const uint32_t a3 = hsub2_u((((W1 >> 8) & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
+                const int s = 2 * bl + h;
 #pragma unroll
-                        for (int i = 0; i < 4; i++) tot[nt][i] += red[warp + q][nt * 4 + i][lane];
+                for (int nt = 0; nt < NT; nt++) mma16816(c[nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
             }
-            __syncthreads();
-        }
-        if (wk == 0 && rb < nrb) {
-            const int64_t r0 = rb * 16 + g, r1 = r0 + 8;
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const int col = 4 * nt + t;
-                if (col < ncols) {
-                    if (r0 < M) Y[(int64_t)col * M + r0] = tot[nt][0] + tot[nt][1];
-                    if (r1 < M) Y[(int64_t)col * M + r1] = tot[nt][2] + tot[nt][3];
-                }
+                acc[nt][0] = fmaf(db0, c[nt][0], acc[nt][0]);
+                acc[nt][1] = fmaf(db0, c[nt][1], acc[nt][1]);
+                acc[nt][2] = fmaf(db1, c[nt][2], acc[nt][2]);
+                acc[nt][3] = fmaf(db1, c[nt][3], acc[nt][3]);
             }
         }
     }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) tot[nt][i] = fmaf(F.es[nt], acc[nt][i], tot[nt][i]);
+}
+
+struct GemvArgs {
+    const uint8_t *W;  // M-tiles
+    int64_t M, K;
+    int nrb, nu;       // row blocks of 16, units of 256
+    const float *X;    // [ncols][K]
+    int ncols;
+    float *Y;          // [ncols][M]
+    int UW, S;         // unit-warps per pass, ring stages
+    int sweep_rg;      // row groups per sweep (their sums fit the shared accumulator)
+};
+
+// Work order of one CTA: its contiguous range of row groups, cut into sweeps;
+// per sweep all K passes; per pass the sweep's row groups (one stage each).
+// Partial sums of a sweep live in shared memory, so no K pass touches global
+// memory until the sweep's rows are final.
+struct Order {
+    int rg_lo, rg_hi, sweep_rg, passes;
+    IFR_DEV int total() const {
+        int n = 0;
+        for (int sw = rg_lo; sw < rg_hi; sw += sweep_rg) n += passes * min(sweep_rg, rg_hi - sw);
+        return n;
+    }
+    // stage q -> (pass, row group)
+    IFR_DEV void at(int q, int &p, int &rg) const {
+        const int full = passes * sweep_rg;
+        const int sw = q / full, r = q % full;
+        const int sw_lo = rg_lo + sw * sweep_rg;
+        const int n = min(sweep_rg, rg_hi - sw_lo);
+        p = r / n;
+        rg = sw_lo + r % n;
+    }
+};
+
+// Issue the bulk copies of stage q into its ring slot (one thread).
+template <int MTB>
+IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring, uint64_t *full) {
+    constexpr int STAGE = 16 * MTB;
+    const int UW = a.UW, MTG = 16 / UW;
+    int p, rg;
+    o.at(q, p, rg);
+    const int s = q % a.S;
+    const int u0 = p * UW, nuh = min(UW, a.nu - u0);
+    const int nmt = min(MTG, a.nrb - rg * MTG);
+    fence_proxy_async();  // earlier generic reads of this slot before the async writes
+    mbar_expect_tx(full + s, (uint32_t)(nmt * nuh * MTB));
+    for (int m = 0; m < nmt; m++) {
+        const uint8_t *src = a.W + ((int64_t)(rg * MTG + m) * a.nu + u0) * MTB;
+        bulk_g2s(ring + (size_t)s * STAGE + (size_t)m * UW * MTB, src, (uint32_t)(nuh * MTB), full + s);
+    }
+}
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int MTB = mtile_bytes(FMT);
+    constexpr int STAGE = 16 * MTB;   // MTG * UW M-tiles
+    constexpr int NRED = 2 * NT * 4;  // floats per lane per warp in the reduction
+    const int UW = a.UW, MTG = 16 / UW;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *ring = smem + 128;
+    float *red = reinterpret_cast<float *>(ring + (size_t)a.S * STAGE);
+    float *acc = red + kConsumers * NRED * 32;  // [sweep_rg * MTG * 16 rows][8 cols]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nrg = (a.nrb + MTG - 1) / MTG;
+    Order o;
+    o.rg_lo = (int)((int64_t)blockIdx.x * nrg / gridDim.x);
+    o.rg_hi = (int)((int64_t)(blockIdx.x + 1) * nrg / gridDim.x);
+    o.sweep_rg = a.sweep_rg;
+    o.passes = (a.nu + UW - 1) / UW;
+    const int total = o.total();
+
+    if (tid == 0) {
+        for (int s = 0; s < a.S; s++) mbar_init(full + s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB>(a, o, q, ring, full);
+    }
+    __syncthreads();
+
+    const int ui = warp % UW, mp = warp / UW;
+    BFrag<FMT, NT> F;
+    int it = 0;
+    bool dead = false;
+    for (int sw = o.rg_lo; sw < o.rg_hi; sw += o.sweep_rg) {
+        const int sw_hi = min(o.rg_hi, sw + o.sweep_rg);
+        const int sw_rows = (sw_hi - sw) * MTG * 16;
+        for (int i = tid; i < sw_rows * 8; i += kThreads) acc[i] = 0.f;
+        for (int p = 0; p < o.passes; p++) {
+            const int64_t u = (int64_t)p * UW + ui;
+            const bool active = u < a.nu;
+            if (active) build_b<FMT, NT>(a.X, a.K, a.ncols, u, lane, F);
+            for (int rg = sw; rg < sw_hi; rg++, it++) {
+                const int s = it % a.S;
+                if (!dead && !mbar_wait(full + s, (uint32_t)(it / a.S) & 1)) dead = true;
+                float tot[2][NT][4];
+#pragma unroll
+                for (int mm = 0; mm < 2; mm++)
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) tot[mm][nt][i] = 0.f;
+                if (active && !dead) {
+                    const uint8_t *st = ring + (size_t)s * STAGE;
+#pragma unroll
+                    for (int mm = 0; mm < 2; mm++) {
+                        const int m = 2 * mp + mm;
+                        if (rg * MTG + m < a.nrb) {
+                            const uint8_t *tile = st + (size_t)(m * UW + ui) * MTB;
+                            if constexpr (FMT == 14) mtile_q6k<NT>(tile, lane, F, tot[mm]);
+                            else if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot[mm]);
+                            else mtile_qk<FMT, NT>(tile, lane, F, tot[mm]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int mm = 0; mm < 2; mm++)
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            red[((warp * 2 + mm) * NT * 4 + nt * 4 + i) * 32 + lane] = tot[mm][nt][i];
+                consumer_bar();  // slot s fully read; partials visible
+                if (tid == 0 && !dead && it + a.S < total) issue_stage<MTB>(a, o, it + a.S, ring, full);
+                // each thread owns outputs (m, row, col) = o, o + 256, ... in every pass
+                const int base = (rg - sw) * MTG * 16;
+                for (int oi = tid; oi < MTG * 128; oi += kThreads) {
+                    const int col = oi & 7, r16 = (oi >> 3) & 15, m = oi >> 7;
+                    const int nt = col >> 2;
+                    if (nt >= NT) continue;
+                    const int mmp = m >> 1, mm = m & 1, half = r16 >> 3;
+                    const int ln = 4 * (r16 & 7) + (col & 3);
+                    float v = 0.f;
+                    for (int q = 0; q < UW; q++) {
+                        const float *pp = red + (((mmp * UW + q) * 2 + mm) * NT * 4 + nt * 4 + 2 * half) * 32 + ln;
+                        v += pp[0] + pp[32];
+                    }
+                    acc[(base + m * 16 + r16) * 8 + col] += v;
+                }
+                consumer_bar();  // red reused by the next stage
+            }
+        }
+        // the sweep's rows are final: write Y (coalesced over rows)
+        const int64_t row0 = (int64_t)sw * MTG * 16;
+        for (int i = tid; i < sw_rows * a.ncols; i += kThreads) {
+            const int col = i / sw_rows, r = i % sw_rows;
+            if (row0 + r < a.M && !dead) a.Y[(int64_t)col * a.M + row0 + r] = acc[r * 8 + col];
+        }
+        consumer_bar();
+    }
+    // stages issued but not consumed (only after a timeout) must land before exit
+    if (tid == 0 && dead)
+        for (int q = it; q < min(it + a.S, total); q++) mbar_wait(full + (q % a.S), (uint32_t)(q / a.S) & 1);
 }
 
 static int num_sms() {
@@ -616,54 +557,56 @@ static int num_sms() {
     return n;
 }
 
-static int pick_wk(int units) {
-    int wk = 1;
-    while (wk < 8 && wk * 2 <= units) wk *= 2;
-    return wk;
+template <int FMT, int NT>
+static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, cudaStream_t s) {
+    constexpr int MTB = mtile_bytes(FMT);
+    constexpr int STAGE = 16 * MTB;
+    constexpr int kSmemMax = 227 * 1024;
+    int UW = 1;
+    while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
+    const int MTG = 16 / UW;
+    const int red = kConsumers * (2 * NT * 4) * 32 * 4;
+    const int64_t nrg = (T.nrb + MTG - 1) / MTG;
+    const int grid = (int)(nrg < num_sms() ? nrg : num_sms());
+    // ring stages first (2..5), then the shared accumulator gets the rest
+    int S = (kSmemMax - 128 - red - 16 * 1024) / STAGE;
+    S = S < 2 ? 2 : (S > 5 ? 5 : S);
+    const int acc_bytes_avail = kSmemMax - 128 - S * STAGE - red;
+    const int rg_bytes = MTG * 16 * 8 * 4;
+    const int64_t per_cta = (nrg + grid - 1) / grid;
+    int sweep_rg = acc_bytes_avail / rg_bytes;
+    if (sweep_rg < 1) return cudaErrorInvalidConfiguration;
+    if (sweep_rg > per_cta) sweep_rg = (int)per_cta;
+    const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, ncols, Y, UW, S, sweep_rg};
+    qgemv_kernel<FMT, NT><<<grid, kThreads, smem, s>>>(a);
+    return cudaGetLastError();
 }
 
-cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, void *scratch,
-                        cudaStream_t s) {
+cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, cudaStream_t s) {
     if (ncols < 1 || ncols > 8) return cudaErrorInvalidValue;
-    const int NT = ncols <= 4 ? 1 : 2;
-    const int64_t K = T.cols, M = T.rows;
-    const int64_t nch = (K + 255) / 256;
-    XPack P = carve(scratch, T.type, K);
+    const bool two = ncols > 4;
     switch (T.type) {
-    case 12: pack_x_kernel<12><<<(unsigned)nch, kThreads, 0, s>>>(X, ncols, K, NT, P); break;
-    case 13: pack_x_kernel<13><<<(unsigned)nch, kThreads, 0, s>>>(X, ncols, K, NT, P); break;
-    case 14: pack_x_kernel<14><<<(unsigned)nch, kThreads, 0, s>>>(X, ncols, K, NT, P); break;
-    case 8: pack_x_kernel<8><<<(unsigned)nch, kThreads, 0, s>>>(X, ncols, K, NT, P); break;
-    default: return cudaErrorInvalidValue;
+    case 12: return two ? launch<12, 2>(T, X, ncols, Y, s) : launch<12, 1>(T, X, ncols, Y, s);
+    case 13: return two ? launch<13, 2>(T, X, ncols, Y, s) : launch<13, 1>(T, X, ncols, Y, s);
+    case 14: return two ? launch<14, 2>(T, X, ncols, Y, s) : launch<14, 1>(T, X, ncols, Y, s);
+    case 8: return two ? launch<8, 2>(T, X, ncols, Y, s) : launch<8, 1>(T, X, ncols, Y, s);
     }
-    const int units = T.type == 8 ? (int)nch : (int)T.nb;
-    const int WK = pick_wk(units), WR = 8 / WK;
-    const int64_t nrb = (M + 15) / 16;
-    int64_t want = (nrb + WR - 1) / WR;
-    int64_t cap = (int64_t)num_sms() * 4;
-    const unsigned grid = (unsigned)(want < cap ? want : cap);
-    const int nb = (int)T.nb;
-#define IFR_LAUNCH_NT(KER, ...)                                                  \
-    do {                                                                         \
-        if (NT == 1) KER<1><<<grid, kThreads, 0, s>>>(__VA_ARGS__);              \
-        else KER<2><<<grid, kThreads, 0, s>>>(__VA_ARGS__);                      \
-    } while (0)
-    if (T.type == 12) {
-        if (NT == 1) qgemv_qk_kernel<false, 1><<<grid, kThreads, 0, s>>>(T.data, M, nb, P, Y, ncols, WK);
-        else qgemv_qk_kernel<false, 2><<<grid, kThreads, 0, s>>>(T.data, M, nb, P, Y, ncols, WK);
-    } else if (T.type == 13) {
-        if (NT == 1) qgemv_qk_kernel<true, 1><<<grid, kThreads, 0, s>>>(T.data, M, nb, P, Y, ncols, WK);
-        else qgemv_qk_kernel<true, 2><<<grid, kThreads, 0, s>>>(T.data, M, nb, P, Y, ncols, WK);
-    } else if (T.type == 14) {
-        IFR_LAUNCH_NT(qgemv_q6k_kernel, T.data + T.off_ql, T.data + T.off_qh,
-                      (const int8_t *)(T.data + T.off_sc), (const uint16_t *)(T.data + T.off_d), M,
-                      nb, P, Y, ncols, WK);
-    } else {
-        IFR_LAUNCH_NT(qgemv_q80_kernel, (const int8_t *)(T.data + T.off_ql),
-                      (const uint16_t *)(T.data + T.off_d), M, nb, P, Y, ncols, WK);
-    }
-#undef IFR_LAUNCH_NT
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t read_device_error(int *flag, cudaStream_t s) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(flag, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e;
 }
 
 }  // namespace ifr

@@ -1,10 +1,11 @@
-// Device layouts, re-layout (repack) of GGUF blocks, and the bit-exact
-// dequantization kernels.
+// Device layout (M-tiles, tiles.cuh): re-layout of GGUF blocks at upload, and
+// the bit-exact dequantization kernels.
 //
 // Dequantized values follow the reference's src/Dequant.jl exactly: f32
 // products rounded separately (no fused multiply-add, which Julia does not
 // form there), hence the explicit __fmul_rn/__fsub_rn.
 #include "common.cuh"
+#include "tiles.cuh"
 
 namespace ifr {
 
@@ -19,58 +20,75 @@ int64_t raw_row_bytes(int type, int64_t cols) {
 }
 
 int64_t device_bytes(int type, int64_t rows, int64_t cols) {
-    int64_t rb = raw_row_bytes(type, cols);
-    if (rb == 0) return 0;
-    int64_t b = rb * rows;
-    // planes are 16-byte aligned; leave room for the alignment of the d plane
-    return (b + 255) / 256 * 256 + 256;
+    if (raw_row_bytes(type, cols) == 0) return 0;
+    return (rows + 15) / 16 * ((cols + 255) / 256) * mtile_bytes(type);
 }
 
 // ---------------------------------------------------------------- repack ----
-
-// Q6_K: one thread per 16-byte destination piece of ql'/qh'
-__global__ void repack_q6k_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ ql,
-                                  uint8_t *__restrict__ qh, uint8_t *__restrict__ sc,
-                                  uint16_t *__restrict__ d, int64_t nblk) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= nblk) return;
-    const uint8_t *b = raw + i * 210;
-    uint8_t *qlo = ql + i * 128, *qho = qh + i * 64, *sco = sc + i * 16;
-    for (int t = 0; t < 4; t++)
-        for (int k = 0; k < 8; k++)
-            for (int j = 0; j < 4; j++) qlo[32 * t + 4 * k + j] = b[16 * k + 4 * t + j];
-    for (int t = 0; t < 4; t++)
-        for (int k = 0; k < 4; k++)
-            for (int j = 0; j < 4; j++) qho[16 * t + 4 * k + j] = b[128 + 16 * k + 4 * t + j];
-    for (int j = 0; j < 16; j++) sco[j] = b[192 + j];
-    d[i] = (uint16_t)(b[208] | (b[209] << 8));
-}
-
-__global__ void repack_q80_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ qs,
-                                  uint16_t *__restrict__ d, int64_t nblk) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= nblk) return;
-    const uint8_t *b = raw + i * 34;
-    d[i] = (uint16_t)(b[0] | (b[1] << 8));
-    uint8_t *o = qs + i * 32;
-    for (int j = 0; j < 32; j++) o[j] = b[2 + j];
+// one thread per (row, unit): scatter that row's bytes of the unit into its
+// M-tile; padding rows and missing Q8_0 blocks become zeros.
+template <int T>
+__global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ dst, int64_t rows,
+                              int64_t nrb, int64_t nu, int64_t nb_raw) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= nrb * 16 * nu) return;
+    const int64_t u = i % nu, row = i / nu;
+    const int r = (int)(row & 15);
+    uint8_t *tile = dst + ((row >> 4) * nu + u) * mtile_bytes(T);
+    const bool pad = row >= rows;
+    const int BB = raw_block_bytes(T);
+    if (T == 12 || T == 13) {
+        const uint8_t *b = raw + (row * nb_raw + u) * BB;
+        const int qs0 = T == 13 ? 48 : 16;
+        for (int k = 0; k < 16; k++) tile[qk_hdr(r) + k] = pad ? 0 : b[k];
+        if (T == 13)
+            for (int h = 0; h < 2; h++)
+                for (int k = 0; k < 16; k++) tile[q5_qh(r, h) + k] = pad ? 0 : b[16 + 16 * h + k];
+        for (int c = 0; c < 2; c++)
+            for (int t = 0; t < 4; t++)
+                for (int k = 0; k < 16; k++)
+                    tile[qk_qs(T == 13, c, r, t) + k] = pad ? 0 : b[qs0 + 64 * c + 16 * t + k];
+    } else if (T == 14) {
+        const uint8_t *b = raw + (row * nb_raw + u) * BB;
+        tile[q6_d(r)] = pad ? 0 : b[208];
+        tile[q6_d(r) + 1] = pad ? 0 : b[209];
+        for (int k = 0; k < 16; k++) tile[q6_sc(r) + k] = pad ? 0 : b[192 + k];
+        for (int t = 0; t < 4; t++) {
+            for (int h = 0; h < 2; h++)
+                for (int q = 0; q < 16; q++) {
+                    const int k = 4 * h + (q >> 2), j = q & 3;
+                    tile[q6_ql(h, r, t) + q] = pad ? 0 : b[16 * k + 4 * t + j];
+                }
+            for (int q = 0; q < 16; q++) {
+                const int k = q >> 2, j = q & 3;
+                tile[q6_qh(r, t) + q] = pad ? 0 : b[128 + 16 * k + 4 * t + j];
+            }
+        }
+    } else {  // Q8_0: unit u = raw blocks 8u .. 8u+7
+        for (int bl = 0; bl < 8; bl++) {
+            const int64_t rb = 8 * u + bl;
+            const bool miss = pad || rb >= nb_raw;
+            const uint8_t *b = raw + (row * nb_raw + rb) * BB;
+            tile[q8_d(r) + 2 * bl] = miss ? 0 : b[0];
+            tile[q8_d(r) + 2 * bl + 1] = miss ? 0 : b[1];
+            for (int t = 0; t < 4; t++)
+                for (int o = 0; o < 8; o++)
+                    tile[q8_qs(bl >> 1, r, t) + 8 * (bl & 1) + o] = miss ? 0 : b[2 + 8 * t + o];
+        }
+    }
 }
 
 cudaError_t repack(const QTensor &t, const uint8_t *raw, cudaStream_t s) {
-    int64_t nblk = t.rows * t.nb;
-    if (nblk == 0) return cudaSuccess;
-    int threads = 256;
-    unsigned grid = (unsigned)((nblk + threads - 1) / threads);
-    if (t.type == 14) {
-        repack_q6k_kernel<<<grid, threads, 0, s>>>(raw, t.data + t.off_ql, t.data + t.off_qh,
-                                                   t.data + t.off_sc,
-                                                   (uint16_t *)(t.data + t.off_d), nblk);
-    } else if (t.type == 8) {
-        repack_q80_kernel<<<grid, threads, 0, s>>>(raw, t.data + t.off_ql,
-                                                   (uint16_t *)(t.data + t.off_d), nblk);
-    } else {
-        return cudaMemcpyAsync(t.data, raw, raw_row_bytes(t.type, t.cols) * t.rows,
-                               cudaMemcpyDeviceToDevice, s);
+    const int64_t n = t.nrb * 16 * t.nu;
+    if (n == 0) return cudaSuccess;
+    const int threads = 128;
+    const unsigned grid = (unsigned)((n + threads - 1) / threads);
+    switch (t.type) {
+    case 12: repack_kernel<12><<<grid, threads, 0, s>>>(raw, t.data, t.rows, t.nrb, t.nu, t.nb); break;
+    case 13: repack_kernel<13><<<grid, threads, 0, s>>>(raw, t.data, t.rows, t.nrb, t.nu, t.nb); break;
+    case 14: repack_kernel<14><<<grid, threads, 0, s>>>(raw, t.data, t.rows, t.nrb, t.nu, t.nb); break;
+    case 8: repack_kernel<8><<<grid, threads, 0, s>>>(raw, t.data, t.rows, t.nrb, t.nu, t.nb); break;
+    default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
@@ -88,91 +106,77 @@ IFR_DEV void scale_min_k(int j, const uint8_t *s, uint32_t &sc, uint32_t &m) {
     }
 }
 
-// one thread per 32 elements; Q4_K (src/Dequant.jl:325-375), Q5_K (:379-441)
-template <bool Q5>
-__global__ void dequant_qk_kernel(const uint8_t *__restrict__ w, float *__restrict__ out,
-                                  int64_t nsub) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= nsub) return;
-    int64_t blk = i >> 3;
-    int sub = (int)(i & 7);  // sub-block of 32: group j = sub/2, high nibbles if odd
-    const uint8_t *b = w + blk * (Q5 ? 176 : 144);
-    float d = h2f((uint16_t)(b[0] | (b[1] << 8)));
-    float dmin = h2f((uint16_t)(b[2] | (b[3] << 8)));
-    uint32_t sc, m;
-    scale_min_k(sub, b + 4, sc, m);
-    float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
-    int j = sub >> 1, hi = sub & 1;
-    const uint8_t *qs = b + (Q5 ? 48 : 16) + 32 * j;
-    const uint8_t *qh = b + 16;
-    float *o = out + i * 32;
-    for (int l = 0; l < 32; l++) {
-        uint32_t q = hi ? (qs[l] >> 4) : (qs[l] & 0x0f);
-        if (Q5 && ((qh[l] >> (2 * j + hi)) & 1)) q += 16;
-        o[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
-    }
-}
+IFR_DEV float h2f_bytes(const uint8_t *p) { return h2f((uint16_t)(p[0] | (p[1] << 8))); }
 
-// Q6_K from the planar layout, one thread per 16-element group
-// (src/Dequant.jl:558-601: d * sc * q evaluated left to right)
-__global__ void dequant_q6k_kernel(const uint8_t *__restrict__ ql, const uint8_t *__restrict__ qh,
-                                   const int8_t *__restrict__ sc, const uint16_t *__restrict__ dd,
-                                   float *__restrict__ out, int64_t ngrp) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= ngrp) return;
-    int64_t blk = i >> 4;
-    int g = (int)(i & 15);
-    int n = g >> 3, qq = (g >> 1) & 3, bsel = g & 1;
-    float d = h2f(dd[blk]);
-    float ds = __fmul_rn(d, (float)sc[blk * 16 + g]);
-    const uint8_t *qlb = ql + blk * 128, *qhb = qh + blk * 64;
-    float *o = out + blk * 256 + 128 * n + 32 * qq + 16 * bsel;
-    for (int e = 0; e < 16; e++) {
-        int l = 16 * bsel + e;            // position inside the 32-run
-        int t = (l >> 2) & 3, j = l & 3;  // lane-permuted layout, see QTensor
-        int a = qq & 1;
-        int k = 4 * n + 2 * a + bsel;     // original ql offset 64n+32a+16b+4t+j = 16k+4t+j
-        uint8_t lb = qlb[32 * t + 4 * k + j];
-        uint32_t lo = (qq < 2) ? (lb & 0x0f) : (lb >> 4);
-        int kh = 2 * n + bsel;            // original qh offset 32n+16b+4t+j = 16kh+4t+j
-        uint8_t hb = qhb[16 * t + 4 * kh + j];
-        uint32_t h = (hb >> (2 * qq)) & 3;
-        int q = (int)(lo | (h << 4)) - 32;
-        o[e] = __fmul_rn(ds, (float)q);
+// one thread per (row, unit, 32-element sub-group); writes out[row][u*256 + ...]
+template <int T>
+__global__ void dequant_kernel(const uint8_t *__restrict__ w, float *__restrict__ out, int64_t rows,
+                               int64_t cols, int64_t nu, int64_t nb_raw) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= rows * nu * 8) return;
+    const int sub = (int)(i & 7);
+    const int64_t u = (i >> 3) % nu, row = (i >> 3) / nu;
+    const int r = (int)(row & 15);
+    const uint8_t *tile = w + ((row >> 4) * nu + u) * mtile_bytes(T);
+    float *o = out + row * cols + u * 256 + 32 * sub;
+    if (T == 12 || T == 13) {
+        // src/Dequant.jl:325-375 (Q4_K), :379-441 (Q5_K)
+        const uint8_t *hdr = tile + qk_hdr(r);
+        const float d = h2f_bytes(hdr), dmin = h2f_bytes(hdr + 2);
+        uint32_t sc, m;
+        scale_min_k(sub, hdr + 4, sc, m);
+        const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+        const int j = sub >> 1, hi = sub & 1;
+        for (int l = 0; l < 32; l++) {
+            const int byte = 32 * j + l;  // raw qs byte index
+            const int c = byte >> 6, t = (byte >> 4) & 3, k = byte & 15;
+            const uint8_t v = tile[qk_qs(T == 13, c, r, t) + k];
+            uint32_t q = hi ? (v >> 4) : (v & 0x0f);
+            if (T == 13 && ((tile[q5_qh(r, l >> 4) + (l & 15)] >> (2 * j + hi)) & 1)) q += 16;
+            o[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+        }
+    } else if (T == 14) {
+        // src/Dequant.jl:558-601: d * sc * q, left to right; two 16-groups per thread
+        const float d = h2f_bytes(tile + q6_d(r));
+        for (int gi = 0; gi < 2; gi++) {
+            const int g = 2 * sub + gi;  // group of 16 = element e/16
+            const int n = g >> 3, qq = (g >> 1) & 3, b = g & 1, a = qq & 1;
+            const float ds = __fmul_rn(d, (float)(int8_t)tile[q6_sc(r) + g]);
+            for (int e = 0; e < 16; e++) {
+                const int l = 16 * b + e, t = (l >> 2) & 3, jj = l & 3;
+                const int k = 4 * n + 2 * a + b;  // raw ql offset 16k + 4t + jj
+                const uint8_t lb = tile[q6_ql(k >> 2, r, t) + 4 * (k & 3) + jj];
+                const uint32_t lo = qq < 2 ? (lb & 0x0f) : (lb >> 4);
+                const int kh = 2 * n + b;         // raw qh offset 16kh + 4t + jj
+                const uint8_t hb = tile[q6_qh(r, t) + 4 * kh + jj];
+                const int q = (int)(lo | (((hb >> (2 * qq)) & 3) << 4)) - 32;
+                o[16 * gi + e] = __fmul_rn(ds, (float)q);
+            }
+        }
+    } else {
+        // Q8_0, src/Dequant.jl:304-321; block `sub` of the unit
+        const int64_t blk = 8 * u + sub;
+        if (blk >= nb_raw) return;
+        const float d = h2f_bytes(tile + q8_d(r) + 2 * sub);
+        for (int l = 0; l < 32; l++) {
+            const int t = l >> 3, k = l & 7;
+            const int8_t q = (int8_t)tile[q8_qs(sub >> 1, r, t) + 8 * (sub & 1) + k];
+            o[l] = __fmul_rn(d, (float)q);
+        }
     }
-}
-
-// Q8_0 (src/Dequant.jl:304-321), one thread per block
-__global__ void dequant_q80_kernel(const int8_t *__restrict__ qs, const uint16_t *__restrict__ dd,
-                                   float *__restrict__ out, int64_t nblk) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= nblk) return;
-    float d = h2f(dd[i]);
-    for (int j = 0; j < 32; j++) out[i * 32 + j] = __fmul_rn(d, (float)qs[i * 32 + j]);
 }
 
 cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s) {
-    int threads = 256;
-    int64_t nblk = t.rows * t.nb;
-    if (nblk == 0) return cudaSuccess;
-    if (t.type == 12 || t.type == 13) {
-        int64_t n = nblk * 8;
-        unsigned grid = (unsigned)((n + threads - 1) / threads);
-        if (t.type == 12) dequant_qk_kernel<false><<<grid, threads, 0, s>>>(t.data, out, n);
-        else dequant_qk_kernel<true><<<grid, threads, 0, s>>>(t.data, out, n);
-    } else if (t.type == 14) {
-        int64_t n = nblk * 16;
-        unsigned grid = (unsigned)((n + threads - 1) / threads);
-        dequant_q6k_kernel<<<grid, threads, 0, s>>>(t.data + t.off_ql, t.data + t.off_qh,
-                                                    (const int8_t *)(t.data + t.off_sc),
-                                                    (const uint16_t *)(t.data + t.off_d), out, n);
-    } else if (t.type == 8) {
-        unsigned grid = (unsigned)((nblk + threads - 1) / threads);
-        dequant_q80_kernel<<<grid, threads, 0, s>>>((const int8_t *)(t.data + t.off_ql),
-                                                    (const uint16_t *)(t.data + t.off_d), out,
-                                                    nblk);
-    } else {
-        return cudaErrorInvalidValue;
+    const int64_t n = t.rows * t.nu * 8;
+    if (n == 0) return cudaSuccess;
+    const int threads = 128;
+    const unsigned grid = (unsigned)((n + threads - 1) / threads);
+    switch (t.type) {
+    case 12: dequant_kernel<12><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
+    case 13: dequant_kernel<13><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
+    case 14: dequant_kernel<14><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
+    case 8: dequant_kernel<8><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
+    default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
