@@ -93,6 +93,10 @@ int ifr_dequant(ifr_ctx *ctx, const ifr_tensor *t, float *dev_out);
 int ifr_qgemm(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
               float *Y_dev);
 
+/* host-side quantizer (f32 rows -> GGUF blocks of `type`), the library's own
+ * encoder (the reference has none); multithreaded, no device needed */
+int ifr_quantize(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
+
 /* --- acceptance ------------------------------------------------------------
  * Sampled verification (fixed semantics of src/SpeculativeDecoding.jl:37-104):
  *   target  [batch][gamma+1][vocab] f32 logits (dev)
@@ -111,6 +115,48 @@ int ifr_accept(ifr_ctx *ctx, const float *target, const float *draft,
 int ifr_accept_greedy(ifr_ctx *ctx, const float *target, const int32_t *draft_tokens,
                       int batch, int gamma, int vocab, int32_t *accept_count,
                       int32_t *out_tokens);
+
+/* --- model and speculative-decoding state ---------------------------------
+ * A Qwen3.5-hybrid GGUF (general.architecture "qwen35": GatedDeltaNet layers
+ * where blk.N.ssm_a exists, full-attention layers elsewhere, SwiGLU MLPs,
+ * tied or separate lm_head; src/LoaderCPU.jl:265-694 of the reference) plus
+ * an optional MTP draft head (mtp.fc.weight, mtp.pre_fc_norm_embedding.weight,
+ * mtp.pre_fc_norm_hidden.weight, mtp.norm.weight, mtp.blk.0.* attention layer). */
+typedef struct ifr_model ifr_model;
+typedef struct ifr_state ifr_state;
+typedef struct {
+    int32_t hidden, n_layers, n_head, n_kv_head, head_dim, rotary_dim, ffn, vocab;
+    int32_t ssm_heads, ssm_head_dim, conv_kernel, context_length, n_attention_layers, has_mtp;
+    float rope_theta, rms_eps;
+    int64_t weight_bytes;   /* quantized bytes of the decoder layers + lm_head */
+} ifr_model_info;
+
+/* load all weights to the context's device (synchronous) */
+int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out);
+int ifr_model_free(ifr_model *m);
+int ifr_model_get_info(const ifr_model *m, ifr_model_info *info);
+
+/* KV caches, SSM/conv states and rollback buffers for max_ctx positions */
+int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out);
+int ifr_state_free(ifr_state *s);
+int ifr_state_reset(ifr_state *s);
+/* prefill a prompt (host tokens), emit the first greedy token (synchronous);
+ * forward_cpu!(prompt) then softmax_sample at temperature 0
+ * (src/ModelCPU.jl:1325-1336) */
+int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token);
+/* one greedy speculative step, asynchronous on the context stream:
+ * draft gamma tokens with the MTP head (or take `drafts`, gamma host tokens),
+ * verify [last, drafts] in one gamma+1-column forward, accept the longest
+ * prefix matching the target argmax (src/ModelCPU.jl:2099-2115), emit the
+ * accepted drafts plus the target's next token, and roll the SSM/conv/KV
+ * state back to the accepted prefix.  gamma = 0 is plain greedy decoding. */
+int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts);
+/* synchronous read of the emitted tokens and of
+ * scalars[4] = {position, last accept count, steps, last token} */
+int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars);
+/* synchronous read of the last forward: logits [n][vocab] (verify columns),
+ * final-normed hidden [n][hidden], the n tokens fed; any pointer may be NULL */
+int ifr_state_last_verify(ifr_state *s, float *logits, float *hidden, int32_t *tokens, int *n_cols);
 
 /* --- legacy shims: the reference's C symbols, identical signatures --------
  * src/kernels/quant_kernels.c:602-697, bound by src/QuantizedKernels.jl:90-145.

@@ -32,6 +32,16 @@ def row_bytes(qtype, cols):
     return cols // be * bb
 
 
+def quantize(qtype, x):
+    """f32 rows (numpy [rows, cols]) -> GGUF block bytes, the library's host encoder"""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(rows * row_bytes(qtype, cols), dtype=np.uint8)
+    check(load().ifr_quantize(qtype, x.ctypes.data_as(ctypes.c_void_p), rows, cols,
+                              out.ctypes.data_as(ctypes.c_void_p)))
+    return out
+
+
 def _ptr(t):
     """device pointer of a torch tensor (or None)"""
     return None if t is None else ctypes.c_void_p(t.data_ptr())

@@ -35,8 +35,19 @@ SIGNATURES = {
                              ctypes.POINTER(_i64)]),
     "ifr_dequant": (_i, [_vp, _vp, _vp]),
     "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "ifr_quantize": (_i, [_i, _vp, _i64, _i64, _vp]),
     "ifr_accept": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
     "ifr_accept_greedy": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "ifr_model_load_gguf": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "ifr_model_free": (_i, [_vp]),
+    "ifr_model_get_info": (_i, [_vp, _vp]),
+    "ifr_state_create": (_i, [_vp, _i, ctypes.POINTER(_vp)]),
+    "ifr_state_free": (_i, [_vp]),
+    "ifr_state_reset": (_i, [_vp]),
+    "ifr_prefill": (_i, [_vp, _vp, _i, _vp]),
+    "ifr_spec_step": (_i, [_vp, _i, _vp]),
+    "ifr_state_read": (_i, [_vp, _vp, _i, _vp, _vp]),
+    "ifr_state_last_verify": (_i, [_vp, _vp, _vp, _vp, _vp]),
     "q4_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),
     "q5_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),
     "q6_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),

@@ -9,11 +9,10 @@
 #include <mutex>
 #include <string>
 
-namespace {
+static thread_local std::string g_err;
 
-thread_local std::string g_err;
-
-int fail(int code, const char *fmt, ...) {
+// shared with engine.cu (hidden symbols of the library)
+int ifr_fail(int code, const char *fmt, ...) {
     char buf[512];
     va_list ap;
     va_start(ap, fmt);
@@ -23,10 +22,15 @@ int fail(int code, const char *fmt, ...) {
     return code;
 }
 
-int cuda_fail(cudaError_t e, const char *what) {
-    return fail(e == cudaErrorMemoryAllocation ? IFR_ERR_NOMEM : IFR_ERR_CUDA, "%s: %s (%s)", what,
-                cudaGetErrorString(e), cudaGetErrorName(e));
+int ifr_cuda_fail(cudaError_t e, const char *what) {
+    return ifr_fail(e == cudaErrorMemoryAllocation ? IFR_ERR_NOMEM : IFR_ERR_CUDA, "%s: %s (%s)", what,
+                    cudaGetErrorString(e), cudaGetErrorName(e));
 }
+
+namespace {
+
+#define fail ifr_fail
+#define cuda_fail ifr_cuda_fail
 
 #define IFR_CHECK_CUDA(expr, what)                  \
     do {                                            \
@@ -107,6 +111,19 @@ int make_tensor(int type, int64_t rows, int64_t cols, int device, ifr_tensor **o
 }
 
 }  // namespace
+
+int ifr_ctx_device(const ifr_ctx *c) { return c->device; }
+cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c) { return c->stream; }
+
+// GGUF bytes on the host -> device M-tile tensor (caller owns q->data)
+int ifr_upload_raw(ifr_ctx *c, int type, const void *host, int64_t rows, int64_t cols, ifr::QTensor *out) {
+    ifr_tensor *t = nullptr;
+    int rc = ifr_weights_upload(c, type, host, rows, cols, &t);
+    if (rc) return rc;
+    *out = t->q;
+    delete t;  // the device buffer now belongs to the caller
+    return IFR_OK;
+}
 
 extern "C" {
 
@@ -256,10 +273,18 @@ int ifr_qgemm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float 
     DeviceGuard g(c->device);
     for (int n0 = 0; n0 < ncols; n0 += IFR_MAX_VERIFY_COLS) {
         int n = ncols - n0 < IFR_MAX_VERIFY_COLS ? ncols - n0 : IFR_MAX_VERIFY_COLS;
-        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, c->stream),
+        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, false, W->q.rows, c->stream),
                        "qgemm launch");
     }
     return IFR_OK;
+}
+
+int ifr_quantize(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out) {
+    if (!x || !out) return fail(IFR_ERR_ARG, "NULL argument");
+    if (!valid_type(type)) return fail(IFR_ERR_ARG, "unsupported weight type %d", type);
+    if (rows < 0 || cols < 1 || ifr::raw_row_bytes(type, cols) == 0)
+        return fail(IFR_ERR_ARG, "cols=%lld is not a multiple of the block size", (long long)cols);
+    return ifr::quantize_host(type, x, rows, cols, out) == 0 ? IFR_OK : fail(IFR_ERR_ARG, "quantize failed");
 }
 
 int ifr_accept(ifr_ctx *c, const float *target, const float *draft, const int32_t *draft_tokens,

@@ -27,11 +27,15 @@ int64_t device_bytes(int type, int64_t rows, int64_t cols);
 
 // raw GGUF bytes on the device -> device layout (dst distinct from src)
 cudaError_t repack(const QTensor &t, const uint8_t *raw, cudaStream_t s);
-// bit-exact dequantization
+// bit-exact dequantization (all rows, or the rows listed in idx)
 cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s);
+cudaError_t dequant_rows(const QTensor &t, const int32_t *idx, int64_t nrows, float *out, cudaStream_t s);
 
 // Y[ncols][rows] = W * X[ncols][cols], ncols <= 8 per call; X 16-byte aligned
-cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, cudaStream_t s);
+cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                        cudaStream_t s);
+// host encoder (encode.cpp): 0 on success
+int quantize_host(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
 // device-side error flag set by bounded waits that ran out (read and cleared)
 cudaError_t read_device_error(int *flag, cudaStream_t s);
 

@@ -1,0 +1,855 @@
+// Verify-step engine: GGUF model loading, generation state and the
+// speculative-decoding step (MTP draft -> K+1-column verify -> greedy accept
+// -> commit), all enqueued on the context's stream.
+//
+// Reference: Inferno.jl src/GGUF.jl:119-165 (file format), src/LoaderCPU.jl
+// (tensor names :471-694, config keys :439-469), src/ModelCPU.jl:976-1020
+// (forward), :2099-2115 (greedy verify), src/SpeculativeDecoding.jl (loop).
+#include "../../include/inferno_b200.h"
+#include "common.cuh"
+#include "model.cuh"
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <string>
+#include <vector>
+
+// error reporting shared with api.cu
+int ifr_fail(int code, const char *fmt, ...);
+int ifr_cuda_fail(cudaError_t e, const char *what);
+int ifr_ctx_device(const ifr_ctx *c);
+cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
+int ifr_upload_raw(ifr_ctx *c, int type, const void *host, int64_t rows, int64_t cols, ifr::QTensor *out);
+
+#define ECHECK(expr, what)                                  \
+    do {                                                    \
+        cudaError_t _e = (expr);                            \
+        if (_e != cudaSuccess) return ifr_cuda_fail(_e, what); \
+    } while (0)
+
+namespace {
+
+// ------------------------------------------------------------------ GGUF ----
+struct GTensor {
+    std::vector<uint64_t> dims;
+    uint32_t type = 0;
+    uint64_t offset = 0;
+    int64_t nel() const {
+        int64_t n = 1;
+        for (auto d : dims) n *= (int64_t)d;
+        return n;
+    }
+};
+
+struct Gguf {
+    int fd = -1;
+    uint8_t *map = nullptr;
+    size_t size = 0;
+    uint64_t data_off = 0;
+    std::map<std::string, double> num;
+    std::map<std::string, std::string> str;
+    std::map<std::string, GTensor> t;
+
+    ~Gguf() {
+        if (map) munmap(map, size);
+        if (fd >= 0) close(fd);
+    }
+
+    bool open_file(const char *path, std::string &err) {
+        fd = ::open(path, O_RDONLY);
+        if (fd < 0) { err = std::string("cannot open ") + path; return false; }
+        struct stat st;
+        if (fstat(fd, &st) != 0) { err = "fstat failed"; return false; }
+        size = (size_t)st.st_size;
+        map = (uint8_t *)mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+        if (map == MAP_FAILED) { map = nullptr; err = "mmap failed"; return false; }
+        size_t p = 0;
+        auto need = [&](size_t n) { return p + n <= size; };
+        auto rd = [&](void *dst, size_t n) -> bool {
+            if (!need(n)) return false;
+            memcpy(dst, map + p, n);
+            p += n;
+            return true;
+        };
+        auto rd_str = [&](std::string &s) -> bool {
+            uint64_t n;
+            if (!rd(&n, 8) || n > (1u << 20) || !need(n)) return false;  // GGUF.jl:96-99
+            s.assign((const char *)map + p, n);
+            p += n;
+            return true;
+        };
+        const size_t scal[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+        std::function<bool(uint32_t, const std::string &, bool)> rd_val;
+        rd_val = [&](uint32_t ty, const std::string &key, bool keep) -> bool {
+            if (ty == 8) {
+                std::string s;
+                if (!rd_str(s)) return false;
+                if (keep) str[key] = s;
+                return true;
+            }
+            if (ty == 9) {
+                uint32_t at;
+                uint64_t n;
+                if (!rd(&at, 4) || !rd(&n, 8)) return false;
+                for (uint64_t i = 0; i < n; i++)
+                    if (!rd_val(at, key, false)) return false;
+                return true;
+            }
+            if (ty > 12) return false;
+            uint8_t b[8] = {0};
+            if (!rd(b, scal[ty])) return false;
+            double v = 0;
+            switch (ty) {
+            case 0: v = *(uint8_t *)b; break;
+            case 1: v = *(int8_t *)b; break;
+            case 2: v = *(uint16_t *)b; break;
+            case 3: v = *(int16_t *)b; break;
+            case 4: v = *(uint32_t *)b; break;
+            case 5: v = *(int32_t *)b; break;
+            case 6: v = *(float *)b; break;
+            case 7: v = b[0] ? 1 : 0; break;
+            case 10: v = (double)*(uint64_t *)b; break;
+            case 11: v = (double)*(int64_t *)b; break;
+            case 12: v = *(double *)b; break;
+            }
+            if (keep) num[key] = v;
+            return true;
+        };
+        uint32_t magic, version;
+        uint64_t nt, nkv;
+        if (!rd(&magic, 4) || magic != 0x46554747u) { err = "Not a valid GGUF file"; return false; }
+        if (!rd(&version, 4) || !rd(&nt, 8) || !rd(&nkv, 8)) { err = "truncated header"; return false; }
+        for (uint64_t i = 0; i < nkv; i++) {
+            std::string k;
+            uint32_t ty;
+            if (!rd_str(k) || !rd(&ty, 4) || !rd_val(ty, k, true)) { err = "bad metadata"; return false; }
+        }
+        for (uint64_t i = 0; i < nt; i++) {
+            std::string name;
+            GTensor g;
+            uint32_t nd;
+            if (!rd_str(name) || !rd(&nd, 4) || nd > 4) { err = "bad tensor info"; return false; }
+            g.dims.resize(nd);
+            for (uint32_t d = 0; d < nd; d++)
+                if (!rd(&g.dims[d], 8)) { err = "bad tensor info"; return false; }
+            if (!rd(&g.type, 4) || !rd(&g.offset, 8)) { err = "bad tensor info"; return false; }
+            t[name] = g;
+        }
+        const uint64_t align = num.count("general.alignment") ? (uint64_t)num["general.alignment"] : 32;
+        data_off = (p + align - 1) / align * align;  // GGUF.jl:152-156
+        return true;
+    }
+    const uint8_t *data(const GTensor &g) const { return map + data_off + g.offset; }
+    bool has(const std::string &n) const { return t.count(n) != 0; }
+};
+
+int64_t tensor_bytes(uint32_t type, int64_t nel) {
+    switch (type) {
+    case 0: return nel * 4;
+    case 1: return nel * 2;
+    case 8: return nel / 32 * 34;
+    case 12: return nel / 256 * 144;
+    case 13: return nel / 256 * 176;
+    case 14: return nel / 256 * 210;
+    }
+    return -1;
+}
+
+float h2f_host(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ff, f;
+    if (e == 0) {
+        if (m == 0) f = sign;
+        else {
+            int sh = 0;
+            while (!(m & 0x400)) { m <<= 1; sh++; }
+            f = sign | ((uint32_t)(113 - sh) << 23) | ((m & 0x3ff) << 13);
+        }
+    } else if (e == 0x1f) f = sign | 0x7f800000u | (m << 13);
+    else f = sign | ((e + 112) << 23) | (m << 13);
+    float r;
+    memcpy(&r, &f, 4);
+    return r;
+}
+
+}  // namespace
+
+// A projection: one quantized matrix, or same-K parts of different types whose
+// outputs land in consecutive row ranges of one output vector.
+struct Proj {
+    std::vector<ifr::QTensor> parts;
+    int64_t rows = 0, cols = 0;
+};
+
+struct DevLayer {
+    bool ssm = false;
+    float *attn_norm = nullptr, *post_norm = nullptr;
+    Proj proj, out, gate_up, down;
+    float *conv_w = nullptr, *ab_w = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;
+    float *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct ifr_model {
+    ifr_ctx *ctx = nullptr;
+    ifr_model_info info{};
+    int conv_channels = 0, inner = 0;
+    std::vector<DevLayer> layers;
+    DevLayer mtp_layer;
+    bool has_mtp = false;
+    Proj embed, lm_head;
+    float *final_norm = nullptr, *mtp_norm_e = nullptr, *mtp_norm_h = nullptr, *mtp_norm = nullptr;
+    Proj mtp_fc;
+    std::vector<void *> dev_allocs;
+    ~ifr_model() {
+        for (void *p : dev_allocs) cudaFree(p);
+    }
+};
+
+namespace {
+
+constexpr int kNMax = 8;
+
+int upload_f32(ifr_model *m, const Gguf &g, const std::string &name, int64_t expect, float **out) {
+    auto it = g.t.find(name);
+    if (it == g.t.end()) return ifr_fail(IFR_ERR_ARG, "tensor %s missing", name.c_str());
+    const GTensor &t = it->second;
+    if (expect >= 0 && t.nel() != expect)
+        return ifr_fail(IFR_ERR_ARG, "tensor %s has %lld elements, expected %lld", name.c_str(), (long long)t.nel(),
+                        (long long)expect);
+    std::vector<float> host((size_t)t.nel());
+    if (t.type == 0) memcpy(host.data(), g.data(t), host.size() * 4);
+    else if (t.type == 1) {
+        const uint16_t *h = (const uint16_t *)g.data(t);
+        for (size_t i = 0; i < host.size(); i++) host[i] = h2f_host(h[i]);
+    } else return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: type %u where F32/F16 is expected", name.c_str(), t.type);
+    void *d = nullptr;
+    ECHECK(cudaMalloc(&d, host.size() * 4), "cudaMalloc(f32 tensor)");
+    m->dev_allocs.push_back(d);
+    ECHECK(cudaMemcpy(d, host.data(), host.size() * 4, cudaMemcpyHostToDevice), "H2D f32 tensor");
+    *out = (float *)d;
+    return IFR_OK;
+}
+
+// concatenated f32 rows of several [rows][cols] tensors
+int upload_f32_cat(ifr_model *m, const Gguf &g, const std::vector<std::string> &names, float **out) {
+    std::vector<float> host;
+    for (auto &n : names) {
+        auto it = g.t.find(n);
+        if (it == g.t.end()) return ifr_fail(IFR_ERR_ARG, "tensor %s missing", n.c_str());
+        const GTensor &t = it->second;
+        const size_t off = host.size();
+        host.resize(off + (size_t)t.nel());
+        if (t.type == 0) memcpy(host.data() + off, g.data(t), (size_t)t.nel() * 4);
+        else if (t.type == 1) {
+            const uint16_t *h = (const uint16_t *)g.data(t);
+            for (int64_t i = 0; i < t.nel(); i++) host[off + i] = h2f_host(h[i]);
+        } else return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: type %u where F32/F16 is expected", n.c_str(), t.type);
+    }
+    void *d = nullptr;
+    ECHECK(cudaMalloc(&d, host.size() * 4), "cudaMalloc(f32 tensor)");
+    m->dev_allocs.push_back(d);
+    ECHECK(cudaMemcpy(d, host.data(), host.size() * 4, cudaMemcpyHostToDevice), "H2D f32 tensor");
+    *out = (float *)d;
+    return IFR_OK;
+}
+
+// quantized matrices with the same inner dim, stacked along rows; parts of the
+// same type are merged into one device tensor (one GEMV launch)
+int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &names, Proj *p) {
+    p->parts.clear();
+    p->rows = 0;
+    p->cols = -1;
+    size_t i = 0;
+    while (i < names.size()) {
+        auto it = g.t.find(names[i]);
+        if (it == g.t.end()) return ifr_fail(IFR_ERR_ARG, "tensor %s missing", names[i].c_str());
+        const GTensor &t0 = it->second;
+        if (t0.dims.size() != 2) return ifr_fail(IFR_ERR_ARG, "tensor %s is not a matrix", names[i].c_str());
+        const int64_t cols = (int64_t)t0.dims[0];
+        if (p->cols >= 0 && cols != p->cols) return ifr_fail(IFR_ERR_ARG, "tensor %s: inner dim mismatch", names[i].c_str());
+        p->cols = cols;
+        std::vector<uint8_t> raw;
+        int64_t rows = 0;
+        size_t j = i;
+        for (; j < names.size(); j++) {
+            auto jt = g.t.find(names[j]);
+            if (jt == g.t.end()) return ifr_fail(IFR_ERR_ARG, "tensor %s missing", names[j].c_str());
+            const GTensor &tj = jt->second;
+            if (tj.type != t0.type || tj.dims.size() != 2 || (int64_t)tj.dims[0] != cols) break;
+            const int64_t nb = tensor_bytes(tj.type, tj.nel());
+            if (nb < 0) return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: unsupported type %u", names[j].c_str(), tj.type);
+            raw.insert(raw.end(), g.data(tj), g.data(tj) + nb);
+            rows += (int64_t)tj.dims[1];
+        }
+        ifr::QTensor q{};
+        int rc = ifr_upload_raw(m->ctx, (int)t0.type, raw.data(), rows, cols, &q);
+        if (rc) return rc;
+        m->dev_allocs.push_back(q.data);
+        p->parts.push_back(q);
+        p->rows += rows;
+        i = j;
+    }
+    return IFR_OK;
+}
+
+int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L) {
+    const ifr_model_info &c = m->info;
+    int rc;
+    L.ssm = g.has(pre + "ssm_a");
+    if ((rc = upload_f32(m, g, pre + "attn_norm.weight", c.hidden, &L.attn_norm))) return rc;
+    if ((rc = upload_f32(m, g, pre + "post_attention_norm.weight", c.hidden, &L.post_norm))) return rc;
+    if (L.ssm) {
+        if ((rc = upload_proj(m, g, {pre + "attn_qkv.weight", pre + "attn_gate.weight"}, &L.proj))) return rc;
+        if ((rc = upload_proj(m, g, {pre + "ssm_out.weight"}, &L.out))) return rc;
+        if ((rc = upload_f32(m, g, pre + "ssm_conv1d.weight", (int64_t)m->conv_channels * c.conv_kernel, &L.conv_w))) return rc;
+        if ((rc = upload_f32_cat(m, g, {pre + "ssm_alpha.weight", pre + "ssm_beta.weight"}, &L.ab_w))) return rc;
+        if ((rc = upload_f32(m, g, pre + "ssm_a", c.ssm_heads, &L.ssm_a))) return rc;
+        if ((rc = upload_f32(m, g, pre + "ssm_dt.bias", c.ssm_heads, &L.dt_bias))) return rc;
+        if ((rc = upload_f32(m, g, pre + "ssm_norm.weight", c.ssm_head_dim, &L.ssm_norm))) return rc;
+        if (L.proj.rows != m->conv_channels + m->inner || L.out.cols != m->inner)
+            return ifr_fail(IFR_ERR_ARG, "%s: SSM projection shapes do not match the config", pre.c_str());
+    } else {
+        if ((rc = upload_proj(m, g, {pre + "attn_q.weight", pre + "attn_k.weight", pre + "attn_v.weight"}, &L.proj))) return rc;
+        if ((rc = upload_proj(m, g, {pre + "attn_output.weight"}, &L.out))) return rc;
+        if ((rc = upload_f32(m, g, pre + "attn_q_norm.weight", c.head_dim, &L.q_norm))) return rc;
+        if ((rc = upload_f32(m, g, pre + "attn_k_norm.weight", c.head_dim, &L.k_norm))) return rc;
+        if (L.proj.rows != (int64_t)(2 * c.n_head + 2 * c.n_kv_head) * c.head_dim)
+            return ifr_fail(IFR_ERR_ARG, "%s: attention projection shapes do not match the config", pre.c_str());
+    }
+    if ((rc = upload_proj(m, g, {pre + "ffn_gate.weight", pre + "ffn_up.weight"}, &L.gate_up))) return rc;
+    if ((rc = upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down))) return rc;
+    return IFR_OK;
+}
+
+int64_t proj_bytes(const Proj &p) {
+    int64_t b = 0;
+    for (auto &q : p.parts) b += ifr::raw_row_bytes(q.type, q.cols) * q.rows;
+    return b;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- state --------
+struct ifr_state {
+    ifr_model *m = nullptr;
+    int max_ctx = 0, log_cap = 0;
+    std::vector<void *> allocs;
+    ifr::EngineScalars *sc = nullptr;   // device
+    int32_t *vtok = nullptr, *acc = nullptr, *outtok = nullptr, *log = nullptr, *mtp_pos = nullptr;
+    int32_t *h_tok = nullptr;           // pinned staging
+    float *x, *xn, *proj, *y, *gu, *hmid, *hid, *logits;
+    float *mtp_h, *mtp_e, *mtp_cat, *mtp_x, *mtp_xn;
+    float *rope_cos, *rope_sin;
+    std::vector<float *> S, hist, rq, rkv;      // per layer (SSM) else null
+    std::vector<float *> kc, vc;                // per layer (attention) else null
+    float *mtp_kc = nullptr, *mtp_vc = nullptr;
+    void *acc_scratch = nullptr;
+    int last_n = 0;
+    ~ifr_state() {
+        for (void *p : allocs) cudaFree(p);
+        if (h_tok) cudaFreeHost(h_tok);
+    }
+};
+
+namespace {
+
+template <class T>
+int dalloc(ifr_state *s, T **p, size_t n) {
+    void *d = nullptr;
+    ECHECK(cudaMalloc(&d, n * sizeof(T) + 16), "cudaMalloc(state)");
+    ECHECK(cudaMemset(d, 0, n * sizeof(T) + 16), "cudaMemset(state)");
+    s->allocs.push_back(d);
+    *p = (T *)d;
+    return IFR_OK;
+}
+
+int gemv(const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st) {
+    int64_t r0 = 0;
+    for (auto &q : p.parts) {
+        ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, p.rows, st), "qgemm");
+        r0 += q.rows;
+    }
+    return IFR_OK;
+}
+
+// one decoder layer (attention or SSM) on n columns of s->x
+int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, float *vc, const int32_t *pos,
+                  cudaStream_t st) {
+    ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    const int d = c.hidden;
+    int rc;
+    ifr::rmsnorm(s->x, L.attn_norm, s->xn, n, d, c.rms_eps, d, d, st);
+    if ((rc = gemv(L.proj, s->xn, n, s->proj, false, st))) return rc;
+    if (L.ssm) {
+        ifr::SsmArgs a{};
+        a.proj = s->proj;
+        a.ldp = L.proj.rows;
+        a.xn = s->xn;
+        a.d = d;
+        a.conv_w = L.conv_w;
+        a.ab_w = L.ab_w;
+        a.ssm_a = L.ssm_a;
+        a.dt_bias = L.dt_bias;
+        a.norm_w = L.ssm_norm;
+        a.S = s->S[li];
+        a.hist = s->hist[li];
+        a.rq = s->rq[li];
+        a.rkv = s->rkv[li];
+        a.a_prev = &s->sc->a_prev;
+        a.y = s->y;
+        a.ldy = m->inner;
+        a.N = n;
+        a.H = c.ssm_heads;
+        a.C = m->conv_channels;
+        a.K = c.conv_kernel;
+        a.eps = c.rms_eps;
+        ECHECK(ifr::ssm_step(a, c.ssm_head_dim, st), "ssm_step");
+    } else {
+        ifr::AttnArgs a{};
+        a.qkv = s->proj;
+        a.ldq = L.proj.rows;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.kc = kc;
+        a.vc = vc;
+        a.pos = pos;
+        a.rope_cos = s->rope_cos;
+        a.rope_sin = s->rope_sin;
+        a.out = s->y;
+        a.ldo = (int64_t)c.n_head * c.head_dim;
+        a.N = n;
+        a.nh = c.n_head;
+        a.nkv = c.n_kv_head;
+        a.hd = c.head_dim;
+        a.rotary_dim = c.rotary_dim;
+        a.eps = c.rms_eps;
+        ECHECK(ifr::attn_step(a, st), "attn_step");
+    }
+    if ((rc = gemv(L.out, s->y, n, s->x, true, st))) return rc;
+    ifr::rmsnorm(s->x, L.post_norm, s->xn, n, d, c.rms_eps, d, d, st);
+    if ((rc = gemv(L.gate_up, s->xn, n, s->gu, false, st))) return rc;
+    ifr::swiglu(s->gu, s->hmid, n, c.ffn, st);
+    return gemv(L.down, s->hmid, n, s->x, true, st);
+}
+
+// target forward of the n tokens in s->vtok at positions pos.. (device);
+// final-normed hidden of every column in s->hid; logits of columns
+// [logit_from, n) in s->logits (none if logit_from >= n)
+int target_forward(ifr_state *s, int n, int logit_from, cudaStream_t st) {
+    ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    ECHECK(ifr::dequant_rows(m->embed.parts[0], s->vtok, n, s->x, st), "embedding");
+    for (int li = 0; li < c.n_layers; li++) {
+        int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, st);
+        if (rc) return rc;
+    }
+    ifr::rmsnorm(s->x, m->final_norm, s->hid, n, c.hidden, c.rms_eps, c.hidden, c.hidden, st);
+    if (logit_from < n) {
+        int rc = gemv(m->lm_head, s->hid + (int64_t)logit_from * c.hidden, n - logit_from, s->logits, false, st);
+        if (rc) return rc;
+    }
+    s->last_n = n;
+    return IFR_OK;
+}
+
+__global__ void set_pos_kernel(int32_t *dst, const ifr::EngineScalars *sc, int add) { *dst = sc->pos + add; }
+__global__ void prefill_finish_kernel(ifr::EngineScalars *sc, const int32_t *tok, const float *hid, float *mtp_h,
+                                      int d, int32_t *log, int log_cap) {
+    if (threadIdx.x == 0) {
+        sc->last_token = *tok;
+        if (sc->n_log < log_cap) log[sc->n_log++] = *tok;
+    }
+    for (int i = threadIdx.x; i < d; i += blockDim.x) mtp_h[i] = hid[i];
+}
+
+// MTP draft of gamma tokens into s->vtok[1..gamma]
+int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
+    ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    const int d = c.hidden;
+    for (int j = 1; j <= gamma; j++) {
+        const int32_t *tok = j == 1 ? &s->sc->last_token : s->vtok + (j - 1);
+        const float *hin = j == 1 ? s->mtp_h : s->mtp_x;
+        ECHECK(ifr::dequant_rows(m->embed.parts[0], tok, 1, s->mtp_e, st), "mtp embedding");
+        ifr::rmsnorm(s->mtp_e, m->mtp_norm_e, s->mtp_cat, 1, d, c.rms_eps, d, d, st);
+        ifr::rmsnorm(hin, m->mtp_norm_h, s->mtp_cat + d, 1, d, c.rms_eps, d, d, st);
+        int rc = gemv(m->mtp_fc, s->mtp_cat, 1, s->x, false, st);
+        if (rc) return rc;
+        set_pos_kernel<<<1, 1, 0, st>>>(s->mtp_pos, s->sc, j - 1);
+        if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, st))) return rc;
+        ECHECK(cudaMemcpyAsync(s->mtp_x, s->x, (size_t)d * 4, cudaMemcpyDeviceToDevice, st), "mtp hidden");
+        ifr::rmsnorm(s->x, m->mtp_norm, s->mtp_xn, 1, d, c.rms_eps, d, d, st);
+        if ((rc = gemv(m->lm_head, s->mtp_xn, 1, s->logits, false, st))) return rc;
+        ECHECK(ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st), "draft argmax");
+        ifr::set_token(s->vtok + j, s->outtok, st);
+    }
+    return IFR_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- C ABI --------
+extern "C" {
+
+int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out) {
+    if (!ctx || !path || !out) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    *out = nullptr;
+    int dev = ifr_ctx_device(ctx), prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev);
+    Gguf g;
+    std::string err;
+    if (!g.open_file(path, err)) {
+        cudaSetDevice(prev);
+        return ifr_fail(IFR_ERR_ARG, "%s: %s", path, err.c_str());
+    }
+    ifr_model *m = new ifr_model();
+    m->ctx = ctx;
+    // get_config (LoaderCPU.jl:439-469): "{arch}.key", then "key", then the default
+    const std::string arch = g.str.count("general.architecture") ? g.str["general.architecture"] : "qwen";
+    auto md = [&](const char *k, double def) {
+        std::string a = arch + "." + k;
+        if (g.num.count(a)) return g.num[a];
+        if (g.num.count(k)) return g.num[k];
+        return def;
+    };
+    ifr_model_info &c = m->info;
+    c.hidden = (int)md("embedding_length", 1024);
+    c.ffn = (int)md("feed_forward_length", 3584);
+    c.n_layers = (int)md("block_count", 24);
+    c.n_head = (int)md("attention.head_count", 8);
+    c.n_kv_head = (int)md("attention.head_count_kv", 2);
+    c.head_dim = (int)md("attention.key_length", 256);
+    c.rms_eps = (float)md("attention.layer_norm_rms_epsilon", 1e-6);
+    c.rope_theta = (float)md("rope.freq_base", 10000000.0);
+    c.context_length = (int)md("context_length", 4096);
+    c.conv_kernel = (int)md("ssm.conv_kernel", 4);
+    c.rotary_dim = (int)std::lround(c.head_dim * (float)md("rope.partial_rotary_factor", 0.25));  // LoaderCPU.jl:421
+    int rc = IFR_OK;
+    auto te = g.t.find("token_embd.weight");
+    if (te == g.t.end() || te->second.dims.size() != 2) rc = ifr_fail(IFR_ERR_ARG, "token_embd.weight missing");
+    if (!rc) {
+        c.vocab = (int)te->second.dims[1];  // actual vocab from the embedding (LoaderCPU.jl:321-322)
+        if ((int)te->second.dims[0] != c.hidden) rc = ifr_fail(IFR_ERR_ARG, "embedding width != embedding_length");
+    }
+    // SSM dims from the first SSM layer (LoaderCPU.jl:549-567)
+    for (int i = 0; !rc && i < c.n_layers; i++) {
+        const std::string pre = "blk." + std::to_string(i) + ".";
+        if (!g.has(pre + "ssm_a")) continue;
+        const int heads = (int)g.t[pre + "ssm_a"].nel();
+        const int inner = (int)g.t[pre + "attn_gate.weight"].dims[1];
+        const int C = (int)g.t[pre + "attn_qkv.weight"].dims[1];
+        c.ssm_heads = heads;
+        c.ssm_head_dim = inner / heads;
+        m->inner = inner;
+        m->conv_channels = C;
+        if ((C - inner) / (2 * heads) != c.ssm_head_dim)
+            rc = ifr_fail(IFR_ERR_UNSUPPORTED, "SSM head k dim != v dim is not supported");
+        break;
+    }
+    if (!rc && m->inner && c.ssm_head_dim != 128 && c.ssm_head_dim != 64)
+        rc = ifr_fail(IFR_ERR_UNSUPPORTED, "SSM head dim %d (supported: 64, 128)", c.ssm_head_dim);
+    if (!rc && c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
+        rc = ifr_fail(IFR_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128, 256)", c.head_dim);
+    if (!rc) rc = upload_proj(m, g, {"token_embd.weight"}, &m->embed);
+    if (!rc) {
+        if (g.has("output.weight")) rc = upload_proj(m, g, {"output.weight"}, &m->lm_head);
+        else m->lm_head = m->embed;  // tied (LoaderCPU.jl:411-417)
+    }
+    if (!rc && m->embed.parts.size() != 1) rc = ifr_fail(IFR_ERR_ARG, "bad embedding");
+    if (!rc) rc = upload_f32(m, g, "output_norm.weight", c.hidden, &m->final_norm);
+    m->layers.resize(c.n_layers);
+    for (int i = 0; !rc && i < c.n_layers; i++) {
+        rc = load_layer(m, g, "blk." + std::to_string(i) + ".", m->layers[i]);
+        if (!rc && !m->layers[i].ssm) c.n_attention_layers++;
+    }
+    if (!rc && g.has("mtp.fc.weight")) {
+        m->has_mtp = true;
+        rc = upload_proj(m, g, {"mtp.fc.weight"}, &m->mtp_fc);
+        if (!rc) rc = upload_f32(m, g, "mtp.pre_fc_norm_embedding.weight", c.hidden, &m->mtp_norm_e);
+        if (!rc) rc = upload_f32(m, g, "mtp.pre_fc_norm_hidden.weight", c.hidden, &m->mtp_norm_h);
+        if (!rc) rc = upload_f32(m, g, "mtp.norm.weight", c.hidden, &m->mtp_norm);
+        if (!rc) rc = load_layer(m, g, "mtp.blk.0.", m->mtp_layer);
+        if (!rc && m->mtp_layer.ssm) rc = ifr_fail(IFR_ERR_UNSUPPORTED, "the MTP layer must be an attention layer");
+    }
+    if (!rc) {
+        c.has_mtp = m->has_mtp ? 1 : 0;
+        int64_t wb = proj_bytes(m->lm_head);
+        for (auto &L : m->layers) wb += proj_bytes(L.proj) + proj_bytes(L.out) + proj_bytes(L.gate_up) + proj_bytes(L.down);
+        c.weight_bytes = wb;
+    }
+    cudaSetDevice(prev);
+    if (rc) {
+        delete m;
+        return rc;
+    }
+    *out = m;
+    return IFR_OK;
+}
+
+int ifr_model_free(ifr_model *m) {
+    if (!m) return IFR_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(m->ctx));
+    delete m;
+    cudaSetDevice(prev);
+    return IFR_OK;
+}
+
+int ifr_model_get_info(const ifr_model *m, ifr_model_info *info) {
+    if (!m || !info) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    *info = m->info;
+    return IFR_OK;
+}
+
+int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
+    if (!m || !out) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    const ifr_model_info &c = m->info;
+    if (max_ctx < 1 || max_ctx > c.context_length)
+        return ifr_fail(IFR_ERR_ARG, "max_ctx %d outside 1..context_length (%d)", max_ctx, c.context_length);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(m->ctx));
+    ifr_state *s = new ifr_state();
+    s->m = m;
+    s->max_ctx = max_ctx;
+    s->log_cap = max_ctx + 16;
+    const int d = c.hidden, N = kNMax;
+    int64_t maxproj = (int64_t)(2 * c.n_head + 2 * c.n_kv_head) * c.head_dim;
+    if (m->conv_channels + m->inner > maxproj) maxproj = m->conv_channels + m->inner;
+    const int64_t ymax = std::max<int64_t>(m->inner, (int64_t)c.n_head * c.head_dim);
+    int rc = IFR_OK;
+    auto chk = [&](int r) { if (!rc) rc = r; };
+    chk(dalloc(s, &s->sc, 1));
+    chk(dalloc(s, &s->vtok, N));
+    chk(dalloc(s, &s->acc, 4));
+    chk(dalloc(s, &s->outtok, N + 1));
+    chk(dalloc(s, &s->mtp_pos, 4));
+    chk(dalloc(s, &s->log, s->log_cap));
+    chk(dalloc(s, &s->x, (size_t)N * d));
+    chk(dalloc(s, &s->xn, (size_t)N * d));
+    chk(dalloc(s, &s->proj, (size_t)N * maxproj));
+    chk(dalloc(s, &s->y, (size_t)N * ymax));
+    chk(dalloc(s, &s->gu, (size_t)N * 2 * c.ffn));
+    chk(dalloc(s, &s->hmid, (size_t)N * c.ffn));
+    chk(dalloc(s, &s->hid, (size_t)N * d));
+    chk(dalloc(s, &s->logits, (size_t)N * c.vocab));
+    chk(dalloc(s, &s->mtp_h, d));
+    chk(dalloc(s, &s->mtp_e, d));
+    chk(dalloc(s, &s->mtp_cat, 2 * d));
+    chk(dalloc(s, &s->mtp_x, d));
+    chk(dalloc(s, &s->mtp_xn, d));
+    const int half = c.rotary_dim / 2;
+    chk(dalloc(s, &s->rope_cos, (size_t)max_ctx * half));
+    chk(dalloc(s, &s->rope_sin, (size_t)max_ctx * half));
+    s->S.assign(c.n_layers, nullptr);
+    s->hist.assign(c.n_layers, nullptr);
+    s->rq.assign(c.n_layers, nullptr);
+    s->rkv.assign(c.n_layers, nullptr);
+    s->kc.assign(c.n_layers, nullptr);
+    s->vc.assign(c.n_layers, nullptr);
+    const size_t kvn = (size_t)max_ctx * c.n_kv_head * c.head_dim;
+    for (int i = 0; !rc && i < c.n_layers; i++) {
+        if (m->layers[i].ssm) {
+            const int hd = c.ssm_head_dim;
+            chk(dalloc(s, &s->S[i], (size_t)c.ssm_heads * hd * hd));
+            chk(dalloc(s, &s->hist[i], (size_t)(c.conv_kernel - 1) * m->conv_channels));
+            chk(dalloc(s, &s->rq[i], (size_t)N * m->conv_channels));
+            chk(dalloc(s, &s->rkv[i], (size_t)c.ssm_heads * N * (2 * hd + 2)));
+        } else {
+            chk(dalloc(s, &s->kc[i], kvn));
+            chk(dalloc(s, &s->vc[i], kvn));
+        }
+    }
+    if (m->has_mtp) {
+        chk(dalloc(s, &s->mtp_kc, kvn));
+        chk(dalloc(s, &s->mtp_vc, kvn));
+    }
+    const int64_t accb = ifr::accept_greedy_scratch_bytes(1, kNMax, c.vocab);
+    if (!rc) {
+        void *p = nullptr;
+        cudaError_t e = cudaMalloc(&p, accb);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "cudaMalloc(accept scratch)");
+        else { s->allocs.push_back(p); s->acc_scratch = p; }
+    }
+    if (!rc && cudaMallocHost((void **)&s->h_tok, sizeof(int32_t) * 64) != cudaSuccess)
+        rc = ifr_fail(IFR_ERR_NOMEM, "cudaMallocHost failed");
+    if (!rc) {
+        // RoPE tables as the reference builds them (ModelCPU.jl:136-154):
+        // inv_freq = Float32(1/theta^(2(i-1)/rd)) in f64; angle = inv_freq * pos in f32
+        std::vector<float> cs((size_t)max_ctx * half), sn((size_t)max_ctx * half);
+        for (int i = 0; i < half; i++) {
+            const float inv = (float)(1.0 / std::pow((double)c.rope_theta, (double)(2 * i) / (double)c.rotary_dim));
+            for (int p = 0; p < max_ctx; p++) {
+                const float ang = inv * (float)p;
+                cs[(size_t)p * half + i] = std::cos(ang);
+                sn[(size_t)p * half + i] = std::sin(ang);
+            }
+        }
+        if (cudaMemcpy(s->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = ifr_fail(IFR_ERR_CUDA, "H2D rope tables");
+    }
+    if (!rc) {
+        ifr::EngineScalars init{};
+        init.a_prev = -1;
+        if (cudaMemcpy(s->sc, &init, sizeof init, cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = ifr_fail(IFR_ERR_CUDA, "H2D scalars");
+    }
+    cudaSetDevice(prev);
+    if (rc) {
+        delete s;
+        return rc;
+    }
+    *out = s;
+    return IFR_OK;
+}
+
+int ifr_state_free(ifr_state *s) {
+    if (!s) return IFR_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    cudaStreamSynchronize(ifr_ctx_stream_of(s->m->ctx));
+    delete s;
+    cudaSetDevice(prev);
+    return IFR_OK;
+}
+
+int ifr_state_reset(ifr_state *s) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    const ifr_model_info &c = s->m->info;
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    ifr::EngineScalars init{};
+    init.a_prev = -1;
+    ECHECK(cudaMemcpyAsync(s->sc, &init, sizeof init, cudaMemcpyHostToDevice, st), "reset scalars");
+    for (int i = 0; i < c.n_layers; i++)
+        if (s->S[i]) {
+            const int hd = c.ssm_head_dim;
+            ECHECK(cudaMemsetAsync(s->S[i], 0, (size_t)c.ssm_heads * hd * hd * 4, st), "reset state");
+            ECHECK(cudaMemsetAsync(s->hist[i], 0, (size_t)(c.conv_kernel - 1) * s->m->conv_channels * 4, st), "reset conv");
+        }
+    ECHECK(cudaStreamSynchronize(st), "reset");
+    return IFR_OK;
+}
+
+int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token) {
+    if (!s || !tokens || n < 1) return ifr_fail(IFR_ERR_ARG, "invalid prefill arguments");
+    const ifr_model_info &c = s->m->info;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= c.vocab) return ifr_fail(IFR_ERR_ARG, "token %d out of range", tokens[i]);
+    if (n + kNMax > s->max_ctx) return ifr_fail(IFR_ERR_ARG, "prompt of %d tokens does not fit max_ctx=%d", n, s->max_ctx);
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    int rc = IFR_OK;
+    for (int i0 = 0; !rc && i0 < n; i0 += kNMax) {
+        const int k = std::min(kNMax, n - i0);
+        memcpy(s->h_tok, tokens + i0, sizeof(int32_t) * k);
+        cudaError_t e = cudaMemcpyAsync(s->vtok, s->h_tok, sizeof(int32_t) * k, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "H2D prompt"); break; }
+        const bool last = i0 + k == n;
+        rc = target_forward(s, k, last ? k - 1 : k, st);
+        if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, st);
+        if (!rc && last) {
+            e = ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
+            if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "argmax"); break; }
+            prefill_finish_kernel<<<1, 256, 0, st>>>(s->sc, s->outtok, s->hid + (int64_t)(k - 1) * c.hidden,
+                                                     s->mtp_h, c.hidden, s->log, s->log_cap);
+        }
+        // the prompt tokens buffer is reused by the next chunk
+        if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = ifr_cuda_fail(cudaGetLastError(), "prefill");
+    }
+    if (!rc && first_token) {
+        cudaError_t e = cudaMemcpy(first_token, s->outtok, sizeof(int32_t), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "D2H first token");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
+    if (gamma > 0 && !drafts && !s->m->has_mtp) return ifr_fail(IFR_ERR_ARG, "no drafts given and the model has no MTP head");
+    const ifr_model_info &c = s->m->info;
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    int rc = IFR_OK;
+    if (gamma > 0) {
+        if (drafts) {
+            for (int i = 0; i < gamma; i++)
+                if (drafts[i] < 0 || drafts[i] >= c.vocab) { cudaSetDevice(prev); return ifr_fail(IFR_ERR_ARG, "draft token out of range"); }
+            cudaError_t e = cudaStreamSynchronize(st);  // staging buffer reuse
+            if (e == cudaSuccess) {
+                memcpy(s->h_tok, drafts, sizeof(int32_t) * gamma);
+                e = cudaMemcpyAsync(s->vtok + 1, s->h_tok, sizeof(int32_t) * gamma, cudaMemcpyHostToDevice, st);
+            }
+            if (e != cudaSuccess) rc = ifr_cuda_fail(e, "H2D drafts");
+        } else {
+            rc = mtp_draft(s, gamma, st);
+        }
+    }
+    if (!rc) {
+        ifr::set_token(s->vtok, &s->sc->last_token, st);
+        rc = target_forward(s, gamma + 1, 0, st);
+    }
+    if (!rc) {
+        cudaError_t e = ifr::accept_greedy(s->logits, s->vtok + 1, 1, gamma, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "accept_greedy");
+    }
+    if (!rc) ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, st);
+    if (!rc) {
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "spec step launch");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    ECHECK(cudaStreamSynchronize(st), "sync");
+    ifr::EngineScalars h{};
+    ECHECK(cudaMemcpy(&h, s->sc, sizeof h, cudaMemcpyDeviceToHost), "D2H scalars");
+    if (n_tokens) *n_tokens = h.n_log;
+    if (tokens && max_tokens > 0 && h.n_log > 0)
+        ECHECK(cudaMemcpy(tokens, s->log, sizeof(int32_t) * std::min(max_tokens, h.n_log), cudaMemcpyDeviceToHost), "D2H log");
+    if (scalars) {
+        scalars[0] = h.pos;
+        scalars[1] = h.last_accept;
+        scalars[2] = h.steps;
+        scalars[3] = h.last_token;
+    }
+    return IFR_OK;
+}
+
+int ifr_state_last_verify(ifr_state *s, float *logits, float *hidden, int32_t *tokens, int *n_cols) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    const ifr_model_info &c = s->m->info;
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    ECHECK(cudaStreamSynchronize(st), "sync");
+    const int n = s->last_n;
+    if (n_cols) *n_cols = n;
+    if (logits) ECHECK(cudaMemcpy(logits, s->logits, sizeof(float) * n * c.vocab, cudaMemcpyDeviceToHost), "D2H logits");
+    if (hidden) ECHECK(cudaMemcpy(hidden, s->hid, sizeof(float) * n * c.hidden, cudaMemcpyDeviceToHost), "D2H hidden");
+    if (tokens) ECHECK(cudaMemcpy(tokens, s->vtok, sizeof(int32_t) * n, cudaMemcpyDeviceToHost), "D2H tokens");
+    return IFR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,61 @@
+// Internal interface of the layer kernels (model.cu) used by the engine.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ifr {
+
+// device-resident scalars of one generation state (read by kernels, so a
+// verify step needs no host round trip)
+struct EngineScalars {
+    int32_t pos;          // committed tokens in the caches = position of the next token
+    int32_t a_prev;       // accepted drafts of the last call (-1: nothing to replay)
+    int32_t last_token;   // emitted, not yet fed to the target
+    int32_t last_accept;  // accept count of the last verify
+    int32_t n_log;        // tokens in the emitted-token log
+    int32_t steps;        // verify steps committed
+    int32_t pad[2];
+};
+
+struct SsmArgs {
+    const float *proj;   // [N][ldp]: conv inputs q|k|v (C) then z (inner)
+    int64_t ldp;
+    const float *xn;     // [N][d] normalised layer input (alpha/beta projections)
+    int d;
+    const float *conv_w; // [C][K]
+    const float *ab_w;   // [2H][d]: alpha rows then beta rows
+    const float *ssm_a, *dt_bias, *norm_w;
+    float *S;            // [H][HD][HD] committed state
+    float *hist;         // [K-1][C] committed conv inputs
+    float *rq;           // [8][C] conv inputs of the last call's tokens
+    float *rkv;          // [H][8][2HD+2] k, v, decay, beta of the last call's tokens
+    const int32_t *a_prev;
+    float *y;            // [N][ldy]
+    int64_t ldy;
+    int N, H, C, K;
+    float eps;
+};
+
+struct AttnArgs {
+    const float *qkv;    // [N][ldq]: per head [q; gate] (2 nh hd), then k (nkv hd), then v
+    int64_t ldq;
+    const float *q_norm, *k_norm;
+    float *kc, *vc;      // [max_ctx][nkv][hd]
+    const int32_t *pos;
+    const float *rope_cos, *rope_sin;  // [max_ctx][rotary_dim/2]
+    float *out;          // [N][ldo]
+    int64_t ldo;
+    int N, nh, nkv, hd, rotary_dim;
+    float eps;
+};
+
+void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float eps, int64_t ldx, int64_t ldo,
+             cudaStream_t s);
+void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s);
+cudaError_t ssm_step(const SsmArgs &a, int head_dim, cudaStream_t s);
+cudaError_t attn_step(const AttnArgs &a, cudaStream_t s);
+void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,
+            float *mtp_h, int d, int32_t *log, int log_cap, cudaStream_t s);
+void set_token(int32_t *dst, const int32_t *src, cudaStream_t s);
+
+}  // namespace ifr

@@ -402,6 +402,8 @@ struct GemvArgs {
     float *Y;          // [ncols][M]
     int UW, S;         // unit-warps per pass, ring stages
     int sweep_rg;      // row groups per sweep (their sums fit the shared accumulator)
+    int accumulate;    // 1: Y += W X (residual), 0: Y = W X
+    int64_t ldy;       // Y[col * ldy + row]
 };
 
 // Work order of one CTA: its contiguous range of row groups, cut into sweeps;
@@ -537,7 +539,10 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         const int64_t row0 = (int64_t)sw * MTG * 16;
         for (int i = tid; i < sw_rows * a.ncols; i += kThreads) {
             const int col = i / sw_rows, r = i % sw_rows;
-            if (row0 + r < a.M && !dead) a.Y[(int64_t)col * a.M + row0 + r] = acc[r * 8 + col];
+            if (row0 + r < a.M && !dead) {
+                float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
+                *y = a.accumulate ? *y + acc[r * 8 + col] : acc[r * 8 + col];
+            }
         }
         consumer_bar();
     }
@@ -558,7 +563,8 @@ static int num_sms() {
 }
 
 template <int FMT, int NT>
-static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, cudaStream_t s) {
+static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                          cudaStream_t s) {
     constexpr int MTB = mtile_bytes(FMT);
     constexpr int STAGE = 16 * MTB;
     constexpr int kSmemMax = 227 * 1024;
@@ -584,19 +590,20 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, ncols, Y, UW, S, sweep_rg};
+    GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, ncols, Y, UW, S, sweep_rg, accumulate ? 1 : 0, ldy};
     qgemv_kernel<FMT, NT><<<grid, kThreads, smem, s>>>(a);
     return cudaGetLastError();
 }
 
-cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, cudaStream_t s) {
+cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                        cudaStream_t s) {
     if (ncols < 1 || ncols > 8) return cudaErrorInvalidValue;
     const bool two = ncols > 4;
     switch (T.type) {
-    case 12: return two ? launch<12, 2>(T, X, ncols, Y, s) : launch<12, 1>(T, X, ncols, Y, s);
-    case 13: return two ? launch<13, 2>(T, X, ncols, Y, s) : launch<13, 1>(T, X, ncols, Y, s);
-    case 14: return two ? launch<14, 2>(T, X, ncols, Y, s) : launch<14, 1>(T, X, ncols, Y, s);
-    case 8: return two ? launch<8, 2>(T, X, ncols, Y, s) : launch<8, 1>(T, X, ncols, Y, s);
+    case 12: return two ? launch<12, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<12, 1>(T, X, ncols, Y, accumulate, ldy, s);
+    case 13: return two ? launch<13, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<13, 1>(T, X, ncols, Y, accumulate, ldy, s);
+    case 14: return two ? launch<14, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<14, 1>(T, X, ncols, Y, accumulate, ldy, s);
+    case 8: return two ? launch<8, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<8, 1>(T, X, ncols, Y, accumulate, ldy, s);
     }
     return cudaErrorInvalidValue;
 }

@@ -109,16 +109,24 @@ IFR_DEV void scale_min_k(int j, const uint8_t *s, uint32_t &sc, uint32_t &m) {
 IFR_DEV float h2f_bytes(const uint8_t *p) { return h2f((uint16_t)(p[0] | (p[1] << 8))); }
 
 // one thread per (row, unit, 32-element sub-group); writes out[row][u*256 + ...]
+// (idx: optional row indices, e.g. token ids of an embedding gather; clamped
+// to the tensor's rows; output row i holds source row idx[i])
 template <int T>
 __global__ void dequant_kernel(const uint8_t *__restrict__ w, float *__restrict__ out, int64_t rows,
-                               int64_t cols, int64_t nu, int64_t nb_raw) {
+                               int64_t cols, int64_t nu, int64_t nb_raw, const int32_t *__restrict__ idx,
+                               int64_t src_rows) {
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= rows * nu * 8) return;
     const int sub = (int)(i & 7);
-    const int64_t u = (i >> 3) % nu, row = (i >> 3) / nu;
+    const int64_t u = (i >> 3) % nu, orow = (i >> 3) / nu;
+    int64_t row = orow;
+    if (idx) {
+        row = idx[orow];
+        row = row < 0 ? 0 : (row >= src_rows ? src_rows - 1 : row);
+    }
     const int r = (int)(row & 15);
     const uint8_t *tile = w + ((row >> 4) * nu + u) * mtile_bytes(T);
-    float *o = out + row * cols + u * 256 + 32 * sub;
+    float *o = out + orow * cols + u * 256 + 32 * sub;
     if (T == 12 || T == 13) {
         // src/Dequant.jl:325-375 (Q4_K), :379-441 (Q5_K)
         const uint8_t *hdr = tile + qk_hdr(r);
@@ -166,19 +174,21 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ w, float *__restrict_
     }
 }
 
-cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s) {
-    const int64_t n = t.rows * t.nu * 8;
+cudaError_t dequant_rows(const QTensor &t, const int32_t *idx, int64_t nrows, float *out, cudaStream_t s) {
+    const int64_t n = nrows * t.nu * 8;
     if (n == 0) return cudaSuccess;
     const int threads = 128;
     const unsigned grid = (unsigned)((n + threads - 1) / threads);
     switch (t.type) {
-    case 12: dequant_kernel<12><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
-    case 13: dequant_kernel<13><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
-    case 14: dequant_kernel<14><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
-    case 8: dequant_kernel<8><<<grid, threads, 0, s>>>(t.data, out, t.rows, t.cols, t.nu, t.nb); break;
+    case 12: dequant_kernel<12><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
+    case 13: dequant_kernel<13><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
+    case 14: dequant_kernel<14><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
+    case 8: dequant_kernel<8><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
+
+cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s) { return dequant_rows(t, nullptr, t.rows, out, s); }
 
 }  // namespace ifr

@@ -1,0 +1,98 @@
+"""Model and generation-state wrappers over the C ABI (ifr_model / ifr_state)."""
+import ctypes
+
+import numpy as np
+
+from ._lib import check, load
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "hidden", "n_layers", "n_head", "n_kv_head", "head_dim", "rotary_dim", "ffn", "vocab",
+        "ssm_heads", "ssm_head_dim", "conv_kernel", "context_length", "n_attention_layers", "has_mtp")] + [
+        ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("weight_bytes", ctypes.c_int64)]
+
+
+class Model:
+    """A GGUF model resident on the context's device (load_model_cpu analogue,
+    src/LoaderCPU.jl:265-437)."""
+
+    def __init__(self, ctx, path):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        check(load().ifr_model_load_gguf(ctx.handle, path.encode(), ctypes.byref(h)))
+        self.handle = h
+        info = ModelInfo()
+        check(load().ifr_model_get_info(self.handle, ctypes.byref(info)))
+        self.info = info
+
+    def free(self):
+        if getattr(self, "handle", None):
+            load().ifr_model_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class State:
+    """KV caches, SSM states and the emitted-token log of one sequence."""
+
+    def __init__(self, model, max_ctx):
+        self.model = model
+        h = ctypes.c_void_p()
+        check(load().ifr_state_create(model.handle, int(max_ctx), ctypes.byref(h)))
+        self.handle = h
+        self.max_ctx = max_ctx
+
+    def free(self):
+        if getattr(self, "handle", None):
+            load().ifr_state_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def reset(self):
+        check(load().ifr_state_reset(self.handle))
+
+    def prefill(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        first = ctypes.c_int32()
+        check(load().ifr_prefill(self.handle, t.ctypes.data_as(ctypes.c_void_p), len(t), ctypes.byref(first)))
+        return first.value
+
+    def spec_step(self, gamma, drafts=None):
+        """asynchronous: MTP draft (or given drafts) -> verify -> accept -> commit"""
+        d = None
+        if drafts is not None:
+            d = np.ascontiguousarray(drafts, dtype=np.int32)
+            assert len(d) == gamma
+        check(load().ifr_spec_step(self.handle, int(gamma), d.ctypes.data_as(ctypes.c_void_p) if d is not None else None))
+
+    def read(self):
+        """(emitted tokens, position, last accept count, steps)"""
+        n = ctypes.c_int()
+        sc = (ctypes.c_int32 * 4)()
+        buf = np.empty(self.max_ctx + 16, dtype=np.int32)
+        check(load().ifr_state_read(self.handle, buf.ctypes.data_as(ctypes.c_void_p), len(buf), ctypes.byref(n), sc))
+        return buf[:n.value].copy(), sc[0], sc[1], sc[2]
+
+    def last_verify(self):
+        """(logits [n][vocab], hidden [n][hidden], tokens [n]) of the last forward"""
+        info = self.model.info
+        n = ctypes.c_int()
+        check(load().ifr_state_last_verify(self.handle, None, None, None, ctypes.byref(n)))
+        lg = np.empty((n.value, info.vocab), np.float32)
+        hd = np.empty((n.value, info.hidden), np.float32)
+        tk = np.empty(n.value, np.int32)
+        check(load().ifr_state_last_verify(self.handle, lg.ctypes.data_as(ctypes.c_void_p),
+                                           hd.ctypes.data_as(ctypes.c_void_p),
+                                           tk.ctypes.data_as(ctypes.c_void_p), ctypes.byref(n)))
+        return lg, hd, tk

@@ -1,0 +1,144 @@
+"""Seeded synthetic Qwen3.5-hybrid GGUF models (no checkpoints are available).
+
+Presets follow the benchmark configurations:
+  tiny  hidden 1024, 24 layers (attention every 4th), 8 q / 2 kv heads x 256,
+        partial RoPE 25%, SSM 16 heads x 128 (inner 2048, conv kernel 4),
+        FFN 3584, vocab 151936; Q4_K matmuls, Q6_K tied embedding / lm_head,
+        F32 norms; one-layer MTP draft head
+  9b    hidden 4096, 32 layers, 16 q / 4 kv heads x 256, SSM 32 heads x 128,
+        FFN 12288, vocab 151936; Q4_K matmuls, Q6_K ffn_down and lm_head
+  mini  a small model of the same structure for fast tests
+Weights are N(0, 0.02) (the layer norms, which GGUF stores as 1 + w, are
+1 + N(0, 0.02); ssm_a = -exp(N(0, 0.5)); conv1d N(0, 0.5)), quantized with the
+library's own encoder.  Tensor names and metadata keys are those the
+reference's loader reads (src/LoaderCPU.jl:439-694).
+"""
+import os
+import tempfile
+
+import numpy as np
+
+from . import gguf as G
+
+PRESETS = {
+    "tiny": dict(hidden=1024, n_layers=24, n_head=8, n_kv_head=2, head_dim=256, rope_frac=0.25,
+                 ffn=3584, vocab=151936, ssm_heads=16, ssm_head_dim=128, conv_kernel=4,
+                 attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=True,
+                 context=4096),
+    "9b": dict(hidden=4096, n_layers=32, n_head=16, n_kv_head=4, head_dim=256, rope_frac=0.25,
+               ffn=12288, vocab=151936, ssm_heads=32, ssm_head_dim=128, conv_kernel=4,
+               attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q6_K, emb=G.GGML_Q6_K, mtp=True,
+               context=8192),
+    "mini": dict(hidden=256, n_layers=4, n_head=4, n_kv_head=2, head_dim=64, rope_frac=0.25,
+                 ffn=512, vocab=4096, ssm_heads=4, ssm_head_dim=64, conv_kernel=4,
+                 attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=True,
+                 context=1024),
+}
+
+
+def _quant(qtype, x):
+    from . import quantize
+    return quantize(qtype, x)
+
+
+def build(path, preset="tiny", seed=0, **overrides):
+    """Write the seeded model to `path` (GGUF v3)."""
+    cfg = dict(PRESETS[preset])
+    cfg.update(overrides)
+    d, L = cfg["hidden"], cfg["n_layers"]
+    nh, nkv, hd = cfg["n_head"], cfg["n_kv_head"], cfg["head_dim"]
+    H, sd = cfg["ssm_heads"], cfg["ssm_head_dim"]
+    inner = H * sd
+    C = inner + 2 * H * sd
+    K = cfg["conv_kernel"]
+    ffn, V = cfg["ffn"], cfg["vocab"]
+    root = np.random.default_rng(seed)
+    w = G.GGUFWriter(path)
+    arch = "qwen35"
+    w.add("general.architecture", arch)
+    w.add("general.name", f"inferno-b200 synthetic {preset} seed {seed}")
+    for k, v in [("embedding_length", d), ("feed_forward_length", ffn), ("block_count", L),
+                 ("attention.head_count", nh), ("attention.head_count_kv", nkv),
+                 ("attention.key_length", hd), ("attention.value_length", hd),
+                 ("context_length", cfg["context"]), ("full_attention_interval", cfg["attn_every"]),
+                 ("ssm.inner_size", inner), ("ssm.state_size", sd), ("ssm.group_count", H),
+                 ("ssm.time_step_rank", H), ("ssm.conv_kernel", K)]:
+        w.add(f"{arch}.{k}", int(v))
+    w.add(f"{arch}.attention.layer_norm_rms_epsilon", 1e-6)
+    w.add(f"{arch}.rope.freq_base", 10000000.0)
+    w.add(f"{arch}.rope.partial_rotary_factor", float(cfg["rope_frac"]))
+
+    def rng():
+        return np.random.default_rng(root.integers(1 << 62))
+
+    def mat(name, rows, cols, qtype, std=0.02):
+        x = rng().standard_normal((rows, cols), dtype=np.float32) * np.float32(std)
+        w.add_tensor(name, [cols, rows], qtype, _quant(qtype, x))
+
+    def f32(name, dims, values):
+        w.add_tensor(name, dims, G.GGML_F32, np.ascontiguousarray(values, dtype=np.float32))
+
+    def norm(name, n):
+        f32(name, [n], 1.0 + 0.02 * rng().standard_normal(n, dtype=np.float32))
+
+    def attn_layer(pre):
+        mat(pre + "attn_q.weight", 2 * nh * hd, d, cfg["mat"])
+        mat(pre + "attn_k.weight", nkv * hd, d, cfg["mat"])
+        mat(pre + "attn_v.weight", nkv * hd, d, cfg["mat"])
+        mat(pre + "attn_output.weight", d, nh * hd, cfg["mat"])
+        norm(pre + "attn_q_norm.weight", hd)
+        norm(pre + "attn_k_norm.weight", hd)
+
+    def mlp(pre):
+        mat(pre + "ffn_gate.weight", ffn, d, cfg["mat"])
+        mat(pre + "ffn_up.weight", ffn, d, cfg["mat"])
+        mat(pre + "ffn_down.weight", d, ffn, cfg["down"])
+
+    mat("token_embd.weight", V, d, cfg["emb"])
+    norm("output_norm.weight", d)
+    for i in range(L):
+        pre = f"blk.{i}."
+        norm(pre + "attn_norm.weight", d)
+        norm(pre + "post_attention_norm.weight", d)
+        if (i + 1) % cfg["attn_every"] == 0:
+            attn_layer(pre)
+        else:
+            mat(pre + "attn_qkv.weight", C, d, cfg["mat"])
+            mat(pre + "attn_gate.weight", inner, d, cfg["mat"])
+            mat(pre + "ssm_out.weight", d, inner, cfg["mat"])
+            f32(pre + "ssm_conv1d.weight", [K, C], 0.5 * rng().standard_normal((C, K), dtype=np.float32))
+            f32(pre + "ssm_alpha.weight", [d, H], 0.02 * rng().standard_normal((H, d), dtype=np.float32))
+            f32(pre + "ssm_beta.weight", [d, H], 0.02 * rng().standard_normal((H, d), dtype=np.float32))
+            f32(pre + "ssm_a", [H], -np.exp(0.5 * rng().standard_normal(H)).astype(np.float32))
+            f32(pre + "ssm_dt.bias", [H], 0.02 * rng().standard_normal(H, dtype=np.float32))
+            norm(pre + "ssm_norm.weight", sd)
+        mlp(pre)
+    if cfg["mtp"]:
+        mat("mtp.fc.weight", d, 2 * d, cfg["mat"])
+        norm("mtp.pre_fc_norm_embedding.weight", d)
+        norm("mtp.pre_fc_norm_hidden.weight", d)
+        norm("mtp.norm.weight", d)
+        pre = "mtp.blk.0."
+        norm(pre + "attn_norm.weight", d)
+        norm(pre + "post_attention_norm.weight", d)
+        attn_layer(pre)
+        mlp(pre)
+    w.write()
+    return path
+
+
+def cached(preset="tiny", seed=0, directory=None):
+    """Path of the seeded model, built on first use (per machine)."""
+    directory = directory or os.path.join(tempfile.gettempdir(), "inferno_b200_models")
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{preset}_seed{seed}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".{os.getpid()}.tmp"
+        build(tmp, preset, seed)
+        os.replace(tmp, path)
+    return path
+
+
+def prompt(vocab, n=128, seed=0):
+    """seeded uniform prompt token ids"""
+    return np.random.default_rng(seed + 1_000_003).integers(0, vocab, n).astype(np.int32)

@@ -1,1 +1,461 @@
-/* model forward oracle: filled in below */
+/*
+ * Qwen3.5-hybrid forward pass, token by token, on dequantized f32 weights.
+ * TEST INFRASTRUCTURE ONLY (see oracle.h).
+ *
+ * Restates the reference's CPU path (Inferno.jl, src/ModelCPU.jl):
+ *   rmsnorm_cpu!            :111-123  out = x * (1/sqrt(ss/n + eps)) * w
+ *   rmsnorm_rotary!         :188-232  per-head RMSNorm, then half-split RoPE
+ *                                     on the first rotary_dim dims (pairs i, i+half)
+ *   RotaryEmbeddingCPU      :136-154  inv_freq = 1/theta^(2(i-1)/rd) in f64 -> f32,
+ *                                     angle = inv_freq * pos (f32), 0-based pos
+ *   GatedDeltaNetCPU        :566-731  conv ring + SiLU, L2-normalised q (x 1/sqrt(dk))
+ *                                     and k, f64 gates, delta rule, per-head norm,
+ *                                     y * silu(z), ssm_out
+ *   FullAttentionCPU        :787-887  per-head interleaved [q; gate], Q/K norm + RoPE,
+ *                                     KV cache, GQA flash attention (FlashAttention.jl
+ *                                     :19-84, 64-key blocks, online softmax), sigmoid gate
+ *   mlp_forward             :482-508  down(silu(gate x) * up x)
+ *   DecoderLayerCPU         :901-922  x += op(norm(x)); x += mlp(norm(x))
+ *   forward_cpu!            :976-1020 embedding column, layers, final norm, lm_head
+ * The embedding is tied (lm_head = token_embd rows, LoaderCPU.jl:411-417).
+ * The MTP draft head (mtp_forward!, :2031-2048) gains one attention decoder
+ * layer between fc and the final norm; its input hidden is the final-normed
+ * hidden of the last verified token for the first draft, then the layer
+ * output of the previous draft.
+ * Matrix-vector products accumulate in f32 in index order.
+ */
+#define _GNU_SOURCE
+#include "oracle.h"
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+typedef struct {
+    int ssm;
+    float *attn_norm, *post_norm;
+    /* ssm */
+    float *in_proj, *gate_proj, *ssm_out, *conv_w, *alpha_w, *beta_w, *ssm_a, *dt_bias, *ssm_norm;
+    float *conv_state, *h;                  /* [C][K], [heads][vd][kd] */
+    /* attention */
+    float *wq, *wk, *wv, *wo, *q_norm, *k_norm;
+    float *kc, *vc;                         /* [max_ctx][n_kv][hd] */
+    /* mlp */
+    float *ffn_gate, *ffn_up, *ffn_down;
+} or_layer;
+
+struct or_model {
+    or_model_config c;
+    or_layer *layers;
+    or_layer mtp_layer;
+    float *embed;        /* [vocab][d] dequantized */
+    float *final_norm;
+    float *mtp_fc, *mtp_norm_e, *mtp_norm_h, *mtp_norm;
+    float *cos_cache, *sin_cache;   /* [max_ctx][half] */
+    int conv_channels, inner, qk;
+};
+
+static void *xcalloc(size_t n, size_t s) { void *p = calloc(n, s); if (!p) abort(); return p; }
+
+or_model *or_model_new(const or_model_config *c) {
+    or_model *m = (or_model *)xcalloc(1, sizeof(or_model));
+    m->c = *c;
+    m->inner = c->ssm_heads * c->ssm_head_dim;
+    m->qk = c->ssm_heads * c->ssm_head_dim;
+    m->conv_channels = m->inner + 2 * m->qk;
+    m->layers = (or_layer *)xcalloc(c->n_layers, sizeof(or_layer));
+    int half = c->rotary_dim / 2;
+    m->cos_cache = (float *)xcalloc((size_t)c->max_ctx * half, 4);
+    m->sin_cache = (float *)xcalloc((size_t)c->max_ctx * half, 4);
+    for (int i = 0; i < half; i++) {
+        /* 1.0 / (theta ^ (2(i-1)/rd)) in Float64, stored as Float32 (ModelCPU.jl:139) */
+        float inv = (float)(1.0 / pow((double)c->rope_theta, (double)(2 * i) / (double)c->rotary_dim));
+        for (int p = 0; p < c->max_ctx; p++) {
+            float ang = inv * (float)p;
+            m->cos_cache[(size_t)p * half + i] = cosf(ang);
+            m->sin_cache[(size_t)p * half + i] = sinf(ang);
+        }
+    }
+    return m;
+}
+
+static void free_layer(or_layer *L) {
+    float **f[] = {&L->attn_norm, &L->post_norm, &L->in_proj, &L->gate_proj, &L->ssm_out, &L->conv_w,
+                   &L->alpha_w, &L->beta_w, &L->ssm_a, &L->dt_bias, &L->ssm_norm, &L->conv_state, &L->h,
+                   &L->wq, &L->wk, &L->wv, &L->wo, &L->q_norm, &L->k_norm, &L->kc, &L->vc,
+                   &L->ffn_gate, &L->ffn_up, &L->ffn_down};
+    for (size_t i = 0; i < sizeof f / sizeof f[0]; i++) { free(*f[i]); *f[i] = NULL; }
+}
+
+void or_model_free(or_model *m) {
+    if (!m) return;
+    for (int i = 0; i < m->c.n_layers; i++) free_layer(&m->layers[i]);
+    free_layer(&m->mtp_layer);
+    free(m->layers);
+    free(m->embed); free(m->final_norm); free(m->mtp_fc); free(m->mtp_norm_e); free(m->mtp_norm_h);
+    free(m->mtp_norm); free(m->cos_cache); free(m->sin_cache);
+    free(m);
+}
+
+/* tensor slots, addressed by (layer, kind); layer -1 = global, -2 = MTP layer */
+static float **slot(or_model *m, int layer, int kind) {
+    or_layer *L = layer >= 0 ? &m->layers[layer] : (layer == -2 ? &m->mtp_layer : NULL);
+    if (!L) {
+        switch (kind) {
+        case OR_T_EMBED: return &m->embed;
+        case OR_T_FINAL_NORM: return &m->final_norm;
+        case OR_T_MTP_FC: return &m->mtp_fc;
+        case OR_T_MTP_NORM_E: return &m->mtp_norm_e;
+        case OR_T_MTP_NORM_H: return &m->mtp_norm_h;
+        case OR_T_MTP_NORM: return &m->mtp_norm;
+        }
+        return NULL;
+    }
+    switch (kind) {
+    case OR_T_ATTN_NORM: return &L->attn_norm;
+    case OR_T_POST_NORM: return &L->post_norm;
+    case OR_T_IN_PROJ: return &L->in_proj;
+    case OR_T_GATE_PROJ: return &L->gate_proj;
+    case OR_T_SSM_OUT: return &L->ssm_out;
+    case OR_T_CONV: return &L->conv_w;
+    case OR_T_ALPHA: return &L->alpha_w;
+    case OR_T_BETA: return &L->beta_w;
+    case OR_T_SSM_A: return &L->ssm_a;
+    case OR_T_DT_BIAS: return &L->dt_bias;
+    case OR_T_SSM_NORM: return &L->ssm_norm;
+    case OR_T_WQ: return &L->wq;
+    case OR_T_WK: return &L->wk;
+    case OR_T_WV: return &L->wv;
+    case OR_T_WO: return &L->wo;
+    case OR_T_Q_NORM: return &L->q_norm;
+    case OR_T_K_NORM: return &L->k_norm;
+    case OR_T_FFN_GATE: return &L->ffn_gate;
+    case OR_T_FFN_UP: return &L->ffn_up;
+    case OR_T_FFN_DOWN: return &L->ffn_down;
+    }
+    return NULL;
+}
+
+/* raw GGUF bytes of `type` with n elements -> f32 slot (dequantized) */
+int or_model_set(or_model *m, int layer, int kind, int type, const void *data, int64_t n) {
+    float **s = slot(m, layer, kind);
+    if (!s) return -1;
+    free(*s);
+    *s = (float *)malloc((size_t)n * 4);
+    if (!*s) return -2;
+    if (or_dequantize(type, (const uint8_t *)data, n, *s)) return -1;
+    if (layer != -1 && kind == OR_T_SSM_A) {
+        or_layer *L = layer >= 0 ? &m->layers[layer] : &m->mtp_layer;
+        L->ssm = 1;
+    }
+    return 0;
+}
+
+static void alloc_state(or_model *m, or_layer *L) {
+    const or_model_config *c = &m->c;
+    if (L->ssm) {
+        if (!L->conv_state) L->conv_state = (float *)xcalloc((size_t)m->conv_channels * c->conv_kernel, 4);
+        if (!L->h) L->h = (float *)xcalloc((size_t)c->ssm_heads * c->ssm_head_dim * c->ssm_head_dim, 4);
+    } else {
+        size_t kv = (size_t)c->max_ctx * c->n_kv_head * c->head_dim;
+        if (!L->kc) L->kc = (float *)xcalloc(kv, 4);
+        if (!L->vc) L->vc = (float *)xcalloc(kv, 4);
+    }
+}
+
+void or_model_reset(or_model *m) {
+    for (int i = 0; i < m->c.n_layers; i++) {
+        or_layer *L = &m->layers[i];
+        alloc_state(m, L);
+        if (L->ssm) {
+            memset(L->conv_state, 0, (size_t)m->conv_channels * m->c.conv_kernel * 4);
+            memset(L->h, 0, (size_t)m->c.ssm_heads * m->c.ssm_head_dim * m->c.ssm_head_dim * 4);
+        }
+    }
+    if (m->mtp_fc) alloc_state(m, &m->mtp_layer);
+}
+
+/* ---------------- building blocks ---------------- */
+
+static void rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    float scale = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = 0; i < n; i++) out[i] = x[i] * scale * w[i];
+}
+
+/* rows split over threads; every row keeps its own index-order sum */
+typedef struct { float *y; const float *W, *x; int r0, r1, cols; } mv_job;
+static void *mv_run(void *p) {
+    mv_job *j = (mv_job *)p;
+    for (int r = j->r0; r < j->r1; r++) {
+        const float *w = j->W + (size_t)r * j->cols;
+        float acc = 0.f;
+        for (int k = 0; k < j->cols; k++) acc += w[k] * j->x[k];
+        j->y[r] = acc;
+    }
+    return NULL;
+}
+static void matvec(float *y, const float *W, const float *x, int rows, int cols) {
+    int nt = (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (nt > 32) nt = 32;
+    if (nt < 1 || (size_t)rows * cols < (1u << 18)) nt = 1;
+    mv_job jobs[32];
+    pthread_t th[32];
+    for (int i = 0; i < nt; i++) {
+        jobs[i] = (mv_job){y, W, x, (int)((int64_t)rows * i / nt), (int)((int64_t)rows * (i + 1) / nt), cols};
+        if (nt > 1) pthread_create(&th[i], NULL, mv_run, &jobs[i]);
+        else mv_run(&jobs[i]);
+    }
+    if (nt > 1)
+        for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
+}
+
+static inline float silu(float g) { return g / (1.0f + expf(-g)); }
+
+/* GatedDeltaNetCPU (ModelCPU.jl:566-731) */
+static void ssm_forward(or_model *m, or_layer *L, const float *x, float *out) {
+    const or_model_config *c = &m->c;
+    const int C = m->conv_channels, K = c->conv_kernel, H = c->ssm_heads, dk = c->ssm_head_dim,
+              dv = c->ssm_head_dim, inner = m->inner, d = c->hidden;
+    float *qkv = (float *)malloc(C * 4), *z = (float *)malloc(inner * 4), *xc = (float *)malloc(C * 4);
+    float *al = (float *)malloc(H * 4), *be = (float *)malloc(H * 4), *y = (float *)malloc(inner * 4);
+    float *qn = (float *)malloc(dk * 4), *kn = (float *)malloc(dk * 4), *sk = (float *)malloc(dv * 4);
+    matvec(qkv, L->in_proj, x, C, d);
+    matvec(z, L->gate_proj, x, inner, d);
+    for (int j = 0; j < K - 1; j++)
+        for (int i = 0; i < C; i++) L->conv_state[(size_t)i * K + j] = L->conv_state[(size_t)i * K + j + 1];
+    for (int i = 0; i < C; i++) L->conv_state[(size_t)i * K + K - 1] = qkv[i];
+    for (int ch = 0; ch < C; ch++) {
+        float v = 0.f;
+        for (int k = 0; k < K; k++) v += L->conv_state[(size_t)ch * K + k] * L->conv_w[(size_t)ch * K + k];
+        xc[ch] = v / (1.0f + expf(-v));
+    }
+    matvec(al, L->alpha_w, x, H, d);
+    matvec(be, L->beta_w, x, H, d);
+    const float eps = 1e-6f, scale = 1.0f / sqrtf((float)dk);
+    for (int h = 0; h < H; h++) {
+        int g = h % H;  /* num_k_heads == num_v_heads */
+        const float *qg = xc + g * dk, *kg = xc + m->qk + g * dk, *vg = xc + 2 * m->qk + h * dv;
+        float qs = 0.f, ks = 0.f;
+        for (int i = 0; i < dk; i++) { qs += qg[i] * qg[i]; ks += kg[i] * kg[i]; }
+        float qnv = 1.0f / (sqrtf(qs) + eps) * scale, knv = 1.0f / (sqrtf(ks) + eps);
+        for (int i = 0; i < dk; i++) { qn[i] = qg[i] * qnv; kn[i] = kg[i] * knv; }
+        double av = (double)al[h] + (double)L->dt_bias[h];
+        av = av < -20.0 ? -20.0 : (av > 20.0 ? 20.0 : av);
+        double sp = log(1.0 + exp(av));
+        float decay = (float)((double)L->ssm_a[h] * sp);
+        float dta = expf(decay);
+        double bv = (double)be[h];
+        bv = bv < -20.0 ? -20.0 : (bv > 20.0 ? 20.0 : bv);
+        float bg = (float)(1.0 / (1.0 + exp(-bv)));
+        float *S = L->h + (size_t)h * dv * dk;    /* S[i][j], i = v index */
+        for (int i = 0; i < dv * dk; i++) S[i] *= dta;
+        for (int i = 0; i < dv; i++) {
+            float s = 0.f;
+            for (int j = 0; j < dk; j++) s += S[(size_t)i * dk + j] * kn[j];
+            sk[i] = s;
+        }
+        for (int i = 0; i < dv; i++) {
+            float di = bg * (vg[i] - sk[i]);
+            for (int j = 0; j < dk; j++) S[(size_t)i * dk + j] += di * kn[j];
+        }
+        for (int i = 0; i < dv; i++) {
+            float s = 0.f;
+            for (int j = 0; j < dk; j++) s += S[(size_t)i * dk + j] * qn[j];
+            y[h * dv + i] = s;
+        }
+    }
+    for (int h = 0; h < H; h++) rmsnorm(y + h * dv, y + h * dv, L->ssm_norm, dv, c->rms_eps);
+    for (int i = 0; i < inner; i++) y[i] = y[i] * z[i] * (1.0f / (1.0f + expf(-z[i])));
+    matvec(out, L->ssm_out, y, d, inner);
+    free(qkv); free(z); free(xc); free(al); free(be); free(y); free(qn); free(kn); free(sk);
+}
+
+static void rmsnorm_rope(or_model *m, float *x, int nheads, int hd, const float *w, int pos) {
+    int half = m->c.rotary_dim / 2;
+    const float *cs = m->cos_cache + (size_t)pos * half, *sn = m->sin_cache + (size_t)pos * half;
+    for (int h = 0; h < nheads; h++) {
+        float *v = x + h * hd;
+        float ss = 0.f;
+        for (int i = 0; i < hd; i++) ss += v[i] * v[i];
+        float inv = 1.0f / sqrtf(ss / (float)hd + m->c.rms_eps);
+        for (int i = 0; i < hd; i++) v[i] = v[i] * inv * w[i];
+        for (int i = 0; i < half; i++) {
+            float x1 = v[i], x2 = v[i + half];
+            v[i] = x1 * cs[i] - x2 * sn[i];
+            v[i + half] = x1 * sn[i] + x2 * cs[i];
+        }
+    }
+}
+
+/* flash_attention_cpu! (FlashAttention.jl:19-84) for one query */
+static void flash_attn(float *out, const float *q, const float *kc, const float *vc, int kvh, int nkv,
+                       int seq, float scale, int hd) {
+    float scores[64];
+    float mx = -INFINITY, l = 0.f;
+    for (int d = 0; d < hd; d++) out[d] = 0.f;
+    for (int j = 0; j < seq; j += 64) {
+        int je = j + 64 < seq ? j + 64 : seq, bl = je - j;
+        float mn = mx;
+        for (int n = 0; n < bl; n++) {
+            const float *k = kc + ((size_t)(j + n) * nkv + kvh) * hd;
+            float s = 0.f;
+            for (int d = 0; d < hd; d++) s += q[d] * k[d];
+            float sc = s * scale;
+            scores[n] = sc;
+            if (sc > mn) mn = sc;
+        }
+        float sf = expf(mx - mn);
+        if (mn > mx) {
+            for (int d = 0; d < hd; d++) out[d] *= sf;
+            l *= sf;
+        }
+        for (int n = 0; n < bl; n++) {
+            const float *v = vc + ((size_t)(j + n) * nkv + kvh) * hd;
+            float p = expf(scores[n] - mn);
+            l += p;
+            for (int d = 0; d < hd; d++) out[d] += p * v[d];
+        }
+        mx = mn;
+    }
+    float il = 1.0f / l;
+    for (int d = 0; d < hd; d++) out[d] *= il;
+}
+
+/* FullAttentionCPU (ModelCPU.jl:787-887) */
+static void attn_forward(or_model *m, or_layer *L, const float *x, int pos, float *out) {
+    const or_model_config *c = &m->c;
+    const int nh = c->n_head, nkv = c->n_kv_head, hd = c->head_dim, d = c->hidden;
+    float *qg = (float *)malloc((size_t)2 * nh * hd * 4), *k = (float *)malloc((size_t)nkv * hd * 4);
+    float *v = (float *)malloc((size_t)nkv * hd * 4), *q = (float *)malloc((size_t)nh * hd * 4);
+    float *gate = (float *)malloc((size_t)nh * hd * 4), *o = (float *)malloc((size_t)nh * hd * 4);
+    matvec(qg, L->wq, x, 2 * nh * hd, d);
+    matvec(k, L->wk, x, nkv * hd, d);
+    matvec(v, L->wv, x, nkv * hd, d);
+    for (int h = 0; h < nh; h++)
+        for (int i = 0; i < hd; i++) {
+            q[h * hd + i] = qg[(size_t)h * 2 * hd + i];
+            gate[h * hd + i] = qg[(size_t)h * 2 * hd + hd + i];
+        }
+    rmsnorm_rope(m, q, nh, hd, L->q_norm, pos);
+    rmsnorm_rope(m, k, nkv, hd, L->k_norm, pos);
+    memcpy(L->kc + (size_t)pos * nkv * hd, k, (size_t)nkv * hd * 4);
+    memcpy(L->vc + (size_t)pos * nkv * hd, v, (size_t)nkv * hd * 4);
+    const int ratio = nh / nkv;
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int h = 0; h < nh; h++) flash_attn(o + h * hd, q + h * hd, L->kc, L->vc, h / ratio, nkv, pos + 1, scale, hd);
+    for (int i = 0; i < nh * hd; i++) o[i] *= 1.0f / (1.0f + expf(-gate[i]));
+    matvec(out, L->wo, o, d, nh * hd);
+    free(qg); free(k); free(v); free(q); free(gate); free(o);
+}
+
+static void mlp_forward(or_model *m, or_layer *L, const float *x, float *out) {
+    const int f = m->c.ffn, d = m->c.hidden;
+    float *g = (float *)malloc(f * 4), *u = (float *)malloc(f * 4);
+    matvec(g, L->ffn_gate, x, f, d);
+    for (int i = 0; i < f; i++) g[i] = g[i] / (1.0f + expf(-g[i]));
+    matvec(u, L->ffn_up, x, f, d);
+    for (int i = 0; i < f; i++) g[i] = g[i] * u[i];
+    matvec(out, L->ffn_down, g, d, f);
+    free(g); free(u);
+}
+
+static void decoder_layer(or_model *m, or_layer *L, float *x, int pos) {
+    const int d = m->c.hidden;
+    float *xn = (float *)malloc(d * 4), *r = (float *)malloc(d * 4);
+    rmsnorm(xn, x, L->attn_norm, d, m->c.rms_eps);
+    if (L->ssm) ssm_forward(m, L, xn, r);
+    else attn_forward(m, L, xn, pos, r);
+    for (int i = 0; i < d; i++) x[i] += r[i];
+    rmsnorm(xn, x, L->post_norm, d, m->c.rms_eps);
+    mlp_forward(m, L, xn, r);
+    for (int i = 0; i < d; i++) x[i] += r[i];
+    free(xn); free(r);
+}
+
+/* one token of forward_cpu!: logits (vocab) and the final-normed hidden (d) */
+int or_forward_token(or_model *m, int token, int pos, float *logits, float *hidden) {
+    const or_model_config *c = &m->c;
+    if (token < 0 || token >= c->vocab || pos < 0 || pos >= c->max_ctx) return -1;
+    const int d = c->hidden;
+    float *x = (float *)malloc(d * 4), *xn = (float *)malloc(d * 4);
+    memcpy(x, m->embed + (size_t)token * d, d * 4);
+    for (int i = 0; i < c->n_layers; i++) decoder_layer(m, &m->layers[i], x, pos);
+    rmsnorm(xn, x, m->final_norm, d, c->rms_eps);
+    if (hidden) memcpy(hidden, xn, d * 4);
+    if (logits) matvec(logits, m->embed, xn, c->vocab, d);
+    free(x); free(xn);
+    return 0;
+}
+
+/* one MTP draft step: token embedding + hidden -> logits (vocab), next hidden (d) */
+int or_mtp_step(or_model *m, int token, const float *hidden, int pos, float *logits, float *hidden_out) {
+    const or_model_config *c = &m->c;
+    if (!m->mtp_fc || token < 0 || token >= c->vocab || pos < 0 || pos >= c->max_ctx) return -1;
+    const int d = c->hidden;
+    float *cat = (float *)malloc(2 * d * 4), *x = (float *)malloc(d * 4), *xn = (float *)malloc(d * 4);
+    rmsnorm(cat, m->embed + (size_t)token * d, m->mtp_norm_e, d, c->rms_eps);
+    rmsnorm(cat + d, hidden, m->mtp_norm_h, d, c->rms_eps);
+    matvec(x, m->mtp_fc, cat, d, 2 * d);
+    decoder_layer(m, &m->mtp_layer, x, pos);
+    if (hidden_out) memcpy(hidden_out, x, d * 4);
+    rmsnorm(xn, x, m->mtp_norm, d, c->rms_eps);
+    if (logits) matvec(logits, m->embed, xn, c->vocab, d);
+    free(cat); free(x); free(xn);
+    return 0;
+}
+
+/* state snapshot: SSM/conv states and the KV caches of all layers (incl. MTP) */
+struct or_snapshot { float **bufs; size_t *sizes; int n; };
+
+static int collect(or_model *m, float ***ptrs, size_t **sizes) {
+    const or_model_config *c = &m->c;
+    int n = 0, cap = 2 * (c->n_layers + 1);
+    *ptrs = (float **)xcalloc(cap, sizeof(float *));
+    *sizes = (size_t *)xcalloc(cap, sizeof(size_t));
+    for (int i = -1; i < c->n_layers; i++) {
+        or_layer *L = i < 0 ? &m->mtp_layer : &m->layers[i];
+        if (i < 0 && !m->mtp_fc) continue;
+        if (L->ssm) {
+            (*ptrs)[n] = L->conv_state; (*sizes)[n++] = (size_t)m->conv_channels * c->conv_kernel;
+            (*ptrs)[n] = L->h; (*sizes)[n++] = (size_t)c->ssm_heads * c->ssm_head_dim * c->ssm_head_dim;
+        } else {
+            size_t kv = (size_t)c->max_ctx * c->n_kv_head * c->head_dim;
+            (*ptrs)[n] = L->kc; (*sizes)[n++] = kv;
+            (*ptrs)[n] = L->vc; (*sizes)[n++] = kv;
+        }
+    }
+    return n;
+}
+
+or_snapshot *or_snapshot_take(or_model *m) {
+    or_snapshot *s = (or_snapshot *)xcalloc(1, sizeof(or_snapshot));
+    float **p;
+    s->n = collect(m, &p, &s->sizes);
+    s->bufs = (float **)xcalloc(s->n, sizeof(float *));
+    for (int i = 0; i < s->n; i++) {
+        s->bufs[i] = (float *)malloc(s->sizes[i] * 4);
+        memcpy(s->bufs[i], p[i], s->sizes[i] * 4);
+    }
+    free(p);
+    return s;
+}
+
+void or_snapshot_restore(or_model *m, const or_snapshot *s) {
+    float **p;
+    size_t *sz;
+    int n = collect(m, &p, &sz);
+    for (int i = 0; i < n && i < s->n; i++) memcpy(p[i], s->bufs[i], s->sizes[i] * 4);
+    free(p);
+    free(sz);
+}
+
+void or_snapshot_free(or_snapshot *s) {
+    if (!s) return;
+    for (int i = 0; i < s->n; i++) free(s->bufs[i]);
+    free(s->bufs);
+    free(s->sizes);
+    free(s);
+}

@@ -61,6 +61,31 @@ int   or_accept_greedy(const float *target, const int32_t *draft_tokens, int bat
                        int gamma, int vocab, int32_t *accept_count, int32_t *out_tokens);
 int   or_argmax(const float *row, int n);
 
+/* ---- model forward (model.c) ---- */
+typedef struct {
+    int32_t hidden, n_layers, n_head, n_kv_head, head_dim, rotary_dim, ffn, vocab;
+    int32_t ssm_heads, ssm_head_dim, conv_kernel, max_ctx;
+    float rope_theta, rms_eps;
+} or_model_config;
+typedef struct or_model or_model;
+typedef struct or_snapshot or_snapshot;
+enum {
+    OR_T_EMBED = 0, OR_T_FINAL_NORM, OR_T_MTP_FC, OR_T_MTP_NORM_E, OR_T_MTP_NORM_H, OR_T_MTP_NORM,
+    OR_T_ATTN_NORM = 10, OR_T_POST_NORM, OR_T_IN_PROJ, OR_T_GATE_PROJ, OR_T_SSM_OUT, OR_T_CONV,
+    OR_T_ALPHA, OR_T_BETA, OR_T_SSM_A, OR_T_DT_BIAS, OR_T_SSM_NORM, OR_T_WQ, OR_T_WK, OR_T_WV,
+    OR_T_WO, OR_T_Q_NORM, OR_T_K_NORM, OR_T_FFN_GATE, OR_T_FFN_UP, OR_T_FFN_DOWN
+};
+or_model *or_model_new(const or_model_config *c);
+void or_model_free(or_model *m);
+/* layer >= 0: decoder layer; -1: global tensors; -2: the MTP decoder layer */
+int  or_model_set(or_model *m, int layer, int kind, int type, const void *data, int64_t n);
+void or_model_reset(or_model *m);
+int  or_forward_token(or_model *m, int token, int pos, float *logits, float *hidden);
+int  or_mtp_step(or_model *m, int token, const float *hidden, int pos, float *logits, float *hidden_out);
+or_snapshot *or_snapshot_take(or_model *m);
+void or_snapshot_restore(or_model *m, const or_snapshot *s);
+void or_snapshot_free(or_snapshot *s);
+
 #define OR_ACCEPT_CHUNK 2048   /* elements per statistics chunk */
 #define OR_ACCEPT_THREADS 256  /* lanes per chunk in the canonical reduction */
 

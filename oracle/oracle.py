@@ -182,3 +182,168 @@ def norm_rel(a, b):
     den = np.linalg.norm(b, axis=1)
     den[den == 0] = 1.0
     return np.linalg.norm(a - b, axis=1) / den
+
+
+# ---------------------------------------------------------------- model ----
+
+class _Cfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("hidden", "n_layers", "n_head", "n_kv_head", "head_dim",
+                                              "rotary_dim", "ffn", "vocab", "ssm_heads", "ssm_head_dim",
+                                              "conv_kernel", "max_ctx")] + [
+        ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+
+_KIND = {"attn_norm.weight": 10, "post_attention_norm.weight": 11, "attn_qkv.weight": 12,
+         "attn_gate.weight": 13, "ssm_out.weight": 14, "ssm_conv1d.weight": 15, "ssm_alpha.weight": 16,
+         "ssm_beta.weight": 17, "ssm_a": 18, "ssm_dt.bias": 19, "ssm_norm.weight": 20,
+         "attn_q.weight": 21, "attn_k.weight": 22, "attn_v.weight": 23, "attn_output.weight": 24,
+         "attn_q_norm.weight": 25, "attn_k_norm.weight": 26, "ffn_gate.weight": 27, "ffn_up.weight": 28,
+         "ffn_down.weight": 29}
+_GLOBAL = {"token_embd.weight": 0, "output_norm.weight": 1, "mtp.fc.weight": 2,
+           "mtp.pre_fc_norm_embedding.weight": 3, "mtp.pre_fc_norm_hidden.weight": 4, "mtp.norm.weight": 5}
+
+
+def _model_lib():
+    L = lib()
+    if not hasattr(L, "_model_init"):
+        L.or_model_new.restype = ctypes.c_void_p
+        L.or_model_new.argtypes = [ctypes.POINTER(_Cfg)]
+        L.or_model_free.argtypes = [ctypes.c_void_p]
+        L.or_model_set.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                   ctypes.c_int64]
+        L.or_model_reset.argtypes = [ctypes.c_void_p]
+        L.or_forward_token.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _fp, _fp]
+        L.or_mtp_step.argtypes = [ctypes.c_void_p, ctypes.c_int, _fp, ctypes.c_int, _fp, _fp]
+        L.or_snapshot_take.restype = ctypes.c_void_p
+        L.or_snapshot_take.argtypes = [ctypes.c_void_p]
+        L.or_snapshot_restore.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.or_snapshot_free.argtypes = [ctypes.c_void_p]
+        L._model_init = True
+    return L
+
+
+class OracleModel:
+    """forward_cpu! restated in C (model.c), loaded from a GGUF file read with
+    the package's GGUF reader."""
+
+    def __init__(self, gguf_file, max_ctx):
+        f = gguf_file
+        md = f.metadata
+        arch = md.get("general.architecture", "qwen")
+        g = lambda k, dflt: md.get(f"{arch}.{k}", md.get(k, dflt))  # noqa: E731
+        emb = f.tensors["token_embd.weight"]
+        self.hidden, self.vocab = int(emb.dims[0]), int(emb.dims[1])
+        hd = int(g("attention.key_length", 256))
+        ssm_heads, ssm_hd = 0, 0
+        for i in range(int(g("block_count", 24))):
+            if f"blk.{i}.ssm_a" in f.tensors:
+                ssm_heads = f.tensors[f"blk.{i}.ssm_a"].n_elements
+                ssm_hd = int(f.tensors[f"blk.{i}.attn_gate.weight"].dims[1]) // ssm_heads
+                break
+        self.cfg = _Cfg(self.hidden, int(g("block_count", 24)), int(g("attention.head_count", 8)),
+                        int(g("attention.head_count_kv", 2)), hd,
+                        int(round(hd * float(g("rope.partial_rotary_factor", 0.25)))),
+                        int(g("feed_forward_length", 3584)), self.vocab, ssm_heads, ssm_hd,
+                        int(g("ssm.conv_kernel", 4)), int(max_ctx),
+                        float(g("rope.freq_base", 1e7)), float(g("attention.layer_norm_rms_epsilon", 1e-6)))
+        L = _model_lib()
+        self.L = L
+        self.h = L.or_model_new(ctypes.byref(self.cfg))
+        for name, ti in f.tensors.items():
+            if name in _GLOBAL:
+                layer, kind = -1, _GLOBAL[name]
+            elif name.startswith("blk."):
+                _, idx, rest = name.split(".", 2)
+                layer, kind = int(idx), _KIND[rest]
+            elif name.startswith("mtp.blk.0."):
+                layer, kind = -2, _KIND[name[len("mtp.blk.0."):]]
+            else:
+                continue
+            raw = np.ascontiguousarray(f.raw(name))
+            assert L.or_model_set(self.h, layer, kind, ti.type, raw.ctypes.data, ti.n_elements) == 0, name
+        self.has_mtp = "mtp.fc.weight" in f.tensors
+        L.or_model_reset(self.h)
+
+    def close(self):
+        if self.h:
+            self.L.or_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        self.L.or_model_reset(self.h)
+
+    def forward_token(self, token, pos):
+        lg = np.empty(self.vocab, np.float32)
+        hd = np.empty(self.hidden, np.float32)
+        assert self.L.or_forward_token(self.h, int(token), int(pos), _p(lg, _fp), _p(hd, _fp)) == 0
+        return lg, hd
+
+    def mtp_step(self, token, hidden, pos):
+        lg = np.empty(self.vocab, np.float32)
+        ho = np.empty(self.hidden, np.float32)
+        hi = np.ascontiguousarray(hidden, np.float32)
+        assert self.L.or_mtp_step(self.h, int(token), _p(hi, _fp), int(pos), _p(lg, _fp), _p(ho, _fp)) == 0
+        return lg, ho
+
+    def spec_decode(self, prompt, n_steps, gamma, drafts=None):
+        """Greedy speculative decoding with the engine's protocol: MTP drafts
+        (first from the hidden of the last accepted column, then from the MTP
+        layer output), one verify over [last, drafts], longest matching prefix,
+        the target's token at the first mismatch, state rolled back to the
+        accepted prefix.  drafts: optional callable(step) -> gamma tokens."""
+        L = self.L
+        self.reset()
+        for i, t in enumerate(prompt):
+            lg, hid = self.forward_token(t, i)
+        last = int(np.argmax(lg))
+        out, pos, h = [last], len(prompt), hid
+        steps = []
+        for s in range(n_steps):
+            if drafts is None:
+                ds, hin = [], h
+                for j in range(1, gamma + 1):
+                    tok = last if j == 1 else ds[-1]
+                    dl, hin = self.mtp_step(tok, hin, pos + j - 1)
+                    ds.append(int(np.argmax(dl)))
+            else:
+                ds = [int(x) for x in drafts(s)]
+            snap = L.or_snapshot_take(self.h)
+            cols = [last] + ds
+            lgs, hs = [], []
+            for t, tok in enumerate(cols):
+                lg, hd = self.forward_token(tok, pos + t)
+                lgs.append(lg)
+                hs.append(hd)
+            acc = 0
+            while acc < gamma and int(np.argmax(lgs[acc])) == ds[acc]:
+                acc += 1
+            y = int(np.argmax(lgs[acc]))
+            L.or_snapshot_restore(self.h, snap)
+            L.or_snapshot_free(snap)
+            for t in range(acc + 1):
+                self.forward_token(cols[t], pos + t)
+            out += ds[:acc] + [y]
+            steps.append(dict(drafts=ds, logits=np.stack(lgs), hidden=np.stack(hs), acc=acc, pos=pos))
+            pos += acc + 1
+            h = hs[acc]
+            last = y
+        return out, steps
+
+    def greedy(self, prompt, n_tokens):
+        """plain greedy decoding (generate_stream_cpu at temperature 0)"""
+        self.reset()
+        for i, t in enumerate(prompt):
+            lg, _ = self.forward_token(t, i)
+        out = [int(np.argmax(lg))]
+        pos = len(prompt)
+        while len(out) < n_tokens:
+            lg, _ = self.forward_token(out[-1], pos)
+            pos += 1
+            out.append(int(np.argmax(lg)))
+        return out

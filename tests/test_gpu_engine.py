@@ -1,0 +1,135 @@
+"""GPU parity of the speculative-decoding verify engine against the CPU oracle
+(forward_cpu! + MTP head restated in C): draft tokens, verify-column logits,
+accept counts and emitted tokens, through the C ABI."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-4  # norm-relative per verify column (f32 accumulation both sides)
+
+
+@pytest.fixture(scope="module")
+def mini(pkg, O, ctx):
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model
+    path = synth.cached("mini", seed=1)
+    model = Model(ctx, path)
+    om = O.OracleModel(gguf.GGUFFile(path), 512)
+    return model, om, synth.prompt(model.info.vocab, 24, seed=1)
+
+
+def _state(model, n=512):
+    from inferno_b200.engine import State
+    return State(model, n)
+
+
+def test_model_info(mini):
+    model, om, _ = mini
+    i = model.info
+    assert (i.hidden, i.n_layers, i.n_head, i.n_kv_head, i.head_dim, i.rotary_dim) == (256, 4, 4, 2, 64, 16)
+    assert (i.ssm_heads, i.ssm_head_dim, i.vocab, i.n_attention_layers, i.has_mtp) == (4, 64, 4096, 1, 1)
+
+
+def test_spec_decode_mtp_matches_oracle(O, mini):
+    model, om, prompt = mini
+    G, steps = 4, 6
+    st = _state(model)
+    first = st.prefill(prompt)
+    out_o, ref = om.spec_decode(prompt, steps, G)
+    assert first == out_o[0]
+    for s in range(steps):
+        st.spec_step(G)
+        lg, hd, tk = st.last_verify()
+        r = ref[s]
+        assert list(tk[1:]) == r["drafts"], (s, tk, r["drafts"])
+        err = O.norm_rel(lg, r["logits"])
+        assert err.max() < LOGIT_TOL, (s, err)
+        assert O.norm_rel(hd, r["hidden"]).max() < LOGIT_TOL
+        toks, pos, acc, nst = st.read()
+        assert acc == r["acc"] and nst == s + 1 and pos == r["pos"] + acc + 1
+    toks, *_ = st.read()
+    assert list(toks) == out_o
+
+
+def test_forced_drafts_full_partial_and_rejected(O, mini):
+    """drafts from the greedy continuation: all accepted, then one wrong in the
+    middle, then a wrong first draft (rollback of SSM, conv and KV state)"""
+    model, om, prompt = mini
+    G = 4
+    greedy = om.greedy(prompt, 40)
+    plans = []
+
+    def drafts_for(emitted, kind):
+        n = len(emitted)
+        d = list(greedy[n:n + G])
+        if kind == 1:
+            d[2] = (d[2] + 1) % model.info.vocab
+        if kind == 2:
+            d[0] = (d[0] + 1) % model.info.vocab
+        return d
+
+    kinds = [0, 1, 2, 0, 1]
+    st = _state(model)
+    emitted = [st.prefill(prompt)]
+    for k in kinds:
+        d = drafts_for(emitted, k)
+        plans.append(d)
+        st.spec_step(G, d)
+        toks, pos, acc, _ = st.read()
+        emitted = list(toks)
+        assert acc == {0: G, 1: 2, 2: 0}[k]
+    assert emitted == greedy[:len(emitted)]
+    out_o, ref = om.spec_decode(prompt, len(kinds), G, drafts=lambda s: plans[s])
+    assert emitted == out_o
+    lg, _, _ = st.last_verify()
+    assert O.norm_rel(lg, ref[-1]["logits"]).max() < LOGIT_TOL
+
+
+def test_gamma_zero_is_greedy(O, mini):
+    model, om, prompt = mini
+    st = _state(model)
+    st.prefill(prompt)
+    for _ in range(15):
+        st.spec_step(0)
+    toks, pos, acc, _ = st.read()
+    assert list(toks) == om.greedy(prompt, 16)
+    assert pos == len(prompt) + 15
+
+
+def test_state_reset_and_errors(pkg, mini):
+    model, om, prompt = mini
+    st = _state(model, 64)
+    a = st.prefill(prompt)
+    st.reset()
+    b = st.prefill(prompt)
+    assert a == b
+    with pytest.raises(pkg.IfrError, match="gamma"):
+        st.spec_step(9)
+    with pytest.raises(pkg.IfrError, match="out of range"):
+        st.spec_step(2, [0, model.info.vocab])
+    with pytest.raises(pkg.IfrError, match="max_ctx"):
+        st.prefill(np.zeros(60, np.int32))
+
+
+def test_config1_tiny_model_matches_oracle(O, pkg, ctx):
+    """BASELINE config 1 shapes (tiny Qwen3.5 hybrid, Q4_K / Q6_K, 128-token
+    prompt): prefill + two MTP spec steps, logits and tokens vs the oracle"""
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model, State
+    path = synth.cached("tiny", seed=0)
+    model = Model(ctx, path)
+    om = O.OracleModel(gguf.GGUFFile(path), 300)
+    prompt = synth.prompt(model.info.vocab, 128, seed=0)
+    st = State(model, 300)
+    first = st.prefill(prompt)
+    out_o, ref = om.spec_decode(prompt, 2, 4)
+    assert first == out_o[0]
+    for s in range(2):
+        st.spec_step(4)
+        lg, _, tk = st.last_verify()
+        assert list(tk[1:]) == ref[s]["drafts"]
+        assert O.norm_rel(lg, ref[s]["logits"]).max() < LOGIT_TOL
+    toks, *_ = st.read()
+    assert list(toks) == out_o
+    del om
