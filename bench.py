@@ -1,7 +1,17 @@
 """Benchmark of the B200 verify path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload sweep]
-    python bench.py --impl reference ...      # the reference's CPU kernels
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload spec|sweep]
+    python bench.py --impl reference ...      # the reference's CPU path
+
+Workload "spec" (default, BASELINE config 1 and its headline metric): greedy
+speculative decoding of the seeded tiny Qwen3.5-shape hybrid (hidden 1024, 24
+layers, Q4_K matmuls, Q6_K tied embedding/lm_head, one-layer MTP draft head)
+after a 128-token seeded prompt; one step = MTP draft of 4 tokens + one
+5-column verify forward + greedy acceptance + state rollback, replayed as a
+CUDA graph.  value = emitted tokens per second (all ranks).  `roofline` is the
+verify's dequant-GEMV launches (all decoder-layer GEMVs + the lm_head of one
+step), timed per launch with CUDA events inside a timed run.  Every step reads
+~967 MB of weights (verify 411 MB + 4 drafts x 139 MB), far above L2.
 
 Workload "sweep": one step = one verify dequant-GEMV at
 N=5 columns (draft length 4 + 1) over each of the 16 seeded weights
@@ -116,32 +126,31 @@ def barrier(ws):
         dist.barrier()
 
 
-def make_weights(O, qt, M, K, rng):
-    """seeded N(0, 0.02) weights in `qt`: a 2048-row encoded pool tiled to M rows"""
-    rb = O.row_bytes(qt, K)
+def make_weights(pkg, qt, M, K, rng):
+    """seeded N(0, 0.02) weights in `qt` (the library's encoder): a 2048-row
+    pool tiled to M rows"""
+    rb = pkg.row_bytes(qt, K)
     pool_rows = min(M, 2048)
-    pool = O.quantize(qt, rng.normal(0, 0.02, (pool_rows, K)).astype(np.float32)).reshape(pool_rows, rb)
+    pool = pkg.quantize(qt, rng.normal(0, 0.02, (pool_rows, K)).astype(np.float32)).reshape(pool_rows, rb)
     idx = np.arange(M) % pool_rows
     return pool[idx].ravel()
 
 
 # ------------------------------------------------------------------ ours ----
 
-def run_ours(args):
+def run_sweep(args):
     import torch
     import __graft_entry__ as ge
     ws, rank, local = dist_init()
     torch.cuda.set_device(local)
     pkg = ge.load_package()
     pkg.load()
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O  # noqa: E402  (encoder for the synthetic weights only)
     ctx = pkg.Context(local)
     rng = np.random.default_rng(1234)
     Ws, Xs, Ys, byts = [], [], [], []
     for qt, name in FORMATS:
         for (M, K) in SHAPES:
-            q = make_weights(O, qt, M, K, rng)
+            q = make_weights(pkg, qt, M, K, rng)
             W = ctx.upload(qt, q, M, K)
             Ws.append(W)
             Xs.append(torch.from_numpy(rng.normal(0, 1, (NCOLS, K)).astype(np.float32)).cuda())
@@ -204,7 +213,9 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(O, args)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O  # the CPU baseline leg only
+        cpu = cpu_baseline(O, pkg, args)
     if rank == 0:
         peak, peak_kind = measured_peaks()
         big_bytes = byts[big_i]
@@ -250,14 +261,14 @@ def run_ours(args):
 
 # --------------------------------------------------------- CPU reference ----
 
-def ref_sample(O, rng, seconds_budget):
+def ref_sample(O, pkg, rng, seconds_budget):
     """Bounded sample of the sweep for the CPU: 4096x4096 and 12288x4096 of
     every format, N=5 columns each as 5 single-column calls (how the
     reference's forward_cpu! runs the verify tokens)."""
     items = []
     for qt, name in FORMATS:
         for (M, K) in SHAPES[:2]:
-            items.append((qt, name, M, K, make_weights(O, qt, M, K, rng),
+            items.append((qt, name, M, K, make_weights(pkg, qt, M, K, rng),
                           rng.normal(0, 1, (NCOLS, K)).astype(np.float32)))
     return items
 
@@ -272,14 +283,14 @@ def time_ref_sample(O, items):
     return nbytes, time.perf_counter() - t
 
 
-def cpu_baseline(O, args):
+def cpu_baseline(O, pkg, args):
     if not O.ref_available():
         return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference",
                 "sample": "oracle/_ref/libquant_ref.so missing"}
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     rng = np.random.default_rng(99)
-    items = ref_sample(O, rng, 20)
+    items = ref_sample(O, pkg, rng, 20)
     time_ref_sample(O, items)  # warm-up
     nb, dt = time_ref_sample(O, items)
     return {"value": round(nb / dt / 1e9, 3), "unit": "GB/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
@@ -289,20 +300,22 @@ def cpu_baseline(O, args):
                       "single-threaded in the reference", "seconds": round(dt, 2)}
 
 
-def run_reference(args):
+def run_reference_sweep(args):
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
     if not O.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libquant_ref.so not built"}))
         return
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     rng = np.random.default_rng(99)
-    items = ref_sample(O, rng, 20)
+    items = ref_sample(O, pkg, rng, 20)
     for _ in range(args.warmup):
         time_ref_sample(O, items)
     tot_b, tot_t = 0, 0.0
@@ -324,6 +337,200 @@ def run_reference(args):
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
+# ------------------------------------------------------- spec workload ----
+
+SPEC_PRESET, SPEC_SEED, SPEC_PROMPT = "tiny", 0, 128
+
+
+def spec_bytes_per_step(info, gamma):
+    """algorithmic weight bytes one spec step reads: the verify (decoder layers
+    + lm_head) and, per draft, the MTP fc + layer + lm_head"""
+    # fc (hidden x 2 hidden) + one attention layer, same formats as the target
+    d, hd = info.hidden, info.head_dim
+    mtp_rows_k = [(d, 2 * d), ((2 * info.n_head + 2 * info.n_kv_head) * hd, d), (d, info.n_head * hd),
+                  (2 * info.ffn, d), (d, info.ffn)]
+    mtp = sum(r * k for r, k in mtp_rows_k) * 144 // 256
+    lm = info.vocab * d * 210 // 256
+    return info.weight_bytes + gamma * (mtp + lm)
+
+
+def run_spec(args):
+    import torch
+    import __graft_entry__ as ge
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    pkg = ge.load_package()
+    pkg.load()
+    from inferno_b200 import synth
+    from inferno_b200.engine import Model, State
+    G = args.gamma
+    ctx = pkg.Context(local, torch_stream=False)  # own stream: capturable
+    path = synth.cached(SPEC_PRESET, SPEC_SEED)
+    model = Model(ctx, path)
+    info = model.info
+    prompt = synth.prompt(info.vocab, SPEC_PROMPT, SPEC_SEED)
+    max_ctx = SPEC_PROMPT + (args.warmup + 2 * args.steps + 8) * (G + 1) + 16
+    st = State(model, max_ctx)
+    st.prefill(prompt)
+    st.spec_step(G)  # eager step: every kernel initialised before capture
+    st.capture(G, 1)
+    import ctypes
+    sp = ctypes.c_void_p()
+    pkg.check(pkg.load().ifr_ctx_get_stream(ctx.handle, ctypes.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value)
+    for _ in range(args.warmup):
+        st.launch()
+    ctx.sync()
+    n0 = len(st.read()[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            st.launch()
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    toks, pos, acc, nsteps = st.read()
+    emitted = len(toks) - n0
+    barrier(ws)
+    ms_max = max_over_ranks(ms, ws)
+    # per-launch timing of the same steps (event nodes captured in the graph)
+    st.profile(True)
+    st.capture(G, 1)
+    for _ in range(args.steps):
+        st.launch()
+    prof, _ = st.profile_read()
+    st.profile(False)
+    l0 = st.profile_read()[1]
+    st.spec_step(G)
+    launches_per_step = st.profile_read()[1] - l0
+    verify = [prof["layer_gemv"], prof["lm_head"]]
+    v_ms = sum(p["ms"] for p in verify) / args.steps
+    v_bytes = sum(p["bytes"] for p in verify) / args.steps
+    allg = [prof[k] for k in ("layer_gemv", "lm_head", "draft_gemv", "draft_lm_head")]
+    g_ms = sum(p["ms"] for p in allg) / args.steps
+    g_bytes = sum(p["bytes"] for p in allg) / args.steps
+    # end to end: one request through the public API with host buffers:
+    # prompt H2D + prefill, then per step ifr_spec_step + D2H of the emitted tokens
+    st2 = State(model, max_ctx)
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.sync()
+    ee0.record(stream)
+    st2.prefill(prompt)
+    d2h = 0
+    for _ in range(args.steps):
+        st2.spec_step(G)
+        t2 = st2.read()[0]
+        d2h += t2.nbytes
+    ee1.record(stream)
+    ee1.synchronize()
+    e2e_ms = max_over_ranks(ee0.elapsed_time(ee1), ws)
+    e2e_tokens = len(st2.read()[0])
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = spec_cpu_baseline(path, prompt, G, steps=3)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        step_bytes = spec_bytes_per_step(info, G)
+        value = emitted * ws / (ms_max * 1e-3)
+        achieved = v_bytes / (v_ms * 1e-3) / 1e9
+        per_cat = {k: dict(ms_per_step=round(p["ms"] / args.steps, 4),
+                           GBps=round(p["bytes"] / (p["ms"] * 1e-3) / 1e9, 1) if p["ms"] else None,
+                           launches_per_step=p["count"] // max(1, args.steps))
+                   for k, p in prof.items()}
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tokens/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q4_k/q6_k weights, f32 activations (fp16 hi+lo split on tensor cores), f32 accumulate",
+            "data": "synthetic: seeded random-init Qwen3.5-shape hybrid GGUF (N(0,0.02) weights, the library's encoder), seeded uniform 128-token prompt",
+            "config": {"workload": "greedy spec-decode, BASELINE config 1 (tiny Qwen3.5-shape hybrid)",
+                       "model": "hidden 1024, 24 layers (18 GatedDeltaNet + 6 attention), 8q/2kv x 256, FFN 3584, vocab 151936, 1-layer MTP head",
+                       "gamma": G, "verify_columns": G + 1, "prompt": SPEC_PROMPT, "batch": 1,
+                       "tokens_emitted_timed": emitted, "accept_rate": round((emitted / args.steps - 1) / G, 4),
+                       "weight_bytes_per_step": step_bytes,
+                       "l2": "inputs larger than L2: %.0f MB of weights read per step" % (step_bytes / 1e6),
+                       "parallelism": f"replicas x{ws}", "graph": "one CUDA graph per spec step"},
+            "step_hbm_GBps": round(step_bytes / (ms_max / args.steps * 1e-3) / 1e9, 1),
+            "roofline": {"bound": "hbm", "kernel": "verify dequant-GEMV (24 layers x 4 GEMVs + Q6_K lm_head, N=5)",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "algorithmic_bytes_per_launch": int(v_bytes), "launch_ms": round(v_ms, 4),
+                         "all_gemv_GBps": round(g_bytes / (g_ms * 1e-3) / 1e9, 1), "per_category": per_cat},
+            "e2e": {"value": round(e2e_tokens / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(prompt.nbytes / args.steps), "d2h_bytes_per_step": int(d2h / args.steps),
+                    "note": "one request: H2D prompt + prefill + steps x (ifr_spec_step + D2H of the emitted tokens)"},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _oracle_spec(path, prompt, gamma, steps, warmup=0):
+    """tokens/s of `steps` oracle spec steps after the prefill and `warmup` steps"""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O  # CPU baseline / reference arm only
+    import __graft_entry__ as ge
+    ge.load_package()
+    from inferno_b200 import gguf
+    om = O.OracleModel(gguf.GGUFFile(path), len(prompt) + (steps + warmup + 2) * (gamma + 1) + 8)
+    _, rec = om.spec_decode(prompt, warmup + steps, gamma)
+    timed = rec[warmup:]
+    dt = sum(r["seconds"] for r in timed)
+    tokens = sum(r["acc"] + 1 for r in timed)
+    return tokens / dt, dt, None
+
+
+def spec_cpu_baseline(path, prompt, gamma, steps=3):
+    cores = os.cpu_count() or 1
+    tps, dt, _ = _oracle_spec(path, prompt, gamma, steps)
+    return {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"C restatement of forward_cpu! + MTP head + the fixed spec-decode loop (oracle/model.c, "
+                      f"f32 dequantized weights, {cores} threads over matvec rows): {steps} spec steps "
+                      f"(gamma {gamma}) after the 128-token prefill, {dt:.1f} s"}
+
+
+def run_reference_spec(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import __graft_entry__ as ge
+    ge.load_package()
+    from inferno_b200 import synth
+    path = synth.cached(SPEC_PRESET, SPEC_SEED)
+    from inferno_b200 import gguf
+    V = int(gguf.GGUFFile(path).tensors["token_embd.weight"].dims[1])
+    prompt = synth.prompt(V, SPEC_PROMPT, SPEC_SEED)
+    steps = max(1, min(args.steps, 4))
+    tps, dt, _ = _oracle_spec(path, prompt, args.gamma, steps, warmup=1)
+    cores = os.cpu_count() or 1
+    sample = (f"reference CPU path restated in C (oracle/model.c: forward_cpu! + MTP head + fixed greedy spec-decode "
+              f"loop, {cores} threads): {steps} spec steps, gamma {args.gamma}, after a 128-token prefill")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tokens/s", "n_gpus": ws,
+        "steps": steps, "warmup": 1, "ms_per_step": round(dt / steps * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantized weights)", "data": "synthetic",
+        "config": {"workload": "greedy spec-decode, BASELINE config 1 (tiny Qwen3.5-shape hybrid), CPU sample",
+                   "gamma": args.gamma},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -331,15 +538,18 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sweep", choices=["sweep"])
+    ap.add_argument("--workload", default="spec", choices=["spec", "sweep"])
+    ap.add_argument("--gamma", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
-        run_reference(args)
+    if args.workload == "spec":
+        (run_reference_spec if args.impl == "reference" else run_spec)(args)
+    elif args.impl == "reference":
+        run_reference_sweep(args)
     else:
-        run_ours(args)
+        run_sweep(args)
 
 
 if __name__ == "__main__":

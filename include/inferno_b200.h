@@ -151,6 +151,19 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
  * accepted drafts plus the target's next token, and roll the SSM/conv/KV
  * state back to the accepted prefix.  gamma = 0 is plain greedy decoding. */
 int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts);
+/* capture `steps` consecutive MTP spec steps (gamma drafts each) into one
+ * CUDA graph on the context stream (which must not be the legacy default
+ * stream); ifr_spec_graph_launch replays it asynchronously.  Run one eager
+ * ifr_spec_step first so that every kernel is initialised before capture. */
+int ifr_spec_graph(ifr_state *s, int gamma, int steps);
+int ifr_spec_graph_launch(ifr_state *s);
+/* per-launch CUDA-event timing of the state's work (0 = off, default), and
+ * its totals per category since enabling: 0 verify lm_head, 1 draft lm_head,
+ * 2 decoder-layer GEMVs, 3 draft GEMVs, 4 SSM steps, 5 attention steps
+ * (ms[8], algorithmic weight bytes[8], timed launches[8]); launches = kernel
+ * launches enqueued by the state so far */
+int ifr_state_profile(ifr_state *s, int enable);
+int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count, int64_t *launches);
 /* synchronous read of the emitted tokens and of
  * scalars[4] = {position, last accept count, steps, last token} */
 int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars);

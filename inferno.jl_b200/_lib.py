@@ -46,6 +46,10 @@ SIGNATURES = {
     "ifr_state_reset": (_i, [_vp]),
     "ifr_prefill": (_i, [_vp, _vp, _i, _vp]),
     "ifr_spec_step": (_i, [_vp, _i, _vp]),
+    "ifr_spec_graph": (_i, [_vp, _i, _i]),
+    "ifr_spec_graph_launch": (_i, [_vp]),
+    "ifr_state_profile": (_i, [_vp, _i]),
+    "ifr_state_profile_read": (_i, [_vp, _vp, _vp, _vp, _vp]),
     "ifr_state_read": (_i, [_vp, _vp, _i, _vp, _vp]),
     "ifr_state_last_verify": (_i, [_vp, _vp, _vp, _vp, _vp]),
     "q4_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),

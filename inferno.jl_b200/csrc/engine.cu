@@ -330,6 +330,8 @@ int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L)
     return IFR_OK;
 }
 
+}  // namespace
+namespace {
 int64_t proj_bytes(const Proj &p) {
     int64_t b = 0;
     for (auto &q : p.parts) b += ifr::raw_row_bytes(q.type, q.cols) * q.rows;
@@ -354,7 +356,21 @@ struct ifr_state {
     float *mtp_kc = nullptr, *mtp_vc = nullptr;
     void *acc_scratch = nullptr;
     int last_n = 0;
+    // kernel launches enqueued (for the benchmark's launch count)
+    int64_t launches = 0;
+    // optional per-category CUDA-event timing of the launches
+    bool prof = false;
+    std::vector<cudaEvent_t> ev_pool;
+    struct Rec { int ev0, cat; int64_t bytes; };
+    std::vector<Rec> recs;
+    int ev_next = 0;
+    // a captured CUDA graph of consecutive spec steps
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
     ~ifr_state() {
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        if (graph) cudaGraphDestroy(graph);
+        for (auto e : ev_pool) cudaEventDestroy(e);
         for (void *p : allocs) cudaFree(p);
         if (h_tok) cudaFreeHost(h_tok);
     }
@@ -372,25 +388,56 @@ int dalloc(ifr_state *s, T **p, size_t n) {
     return IFR_OK;
 }
 
-int gemv(const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st) {
+// categories of timed launches (ifr_state_profile_read)
+enum { CAT_LM_HEAD = 0, CAT_DRAFT_LM_HEAD, CAT_LAYER_GEMV, CAT_DRAFT_GEMV, CAT_SSM, CAT_ATTN, CAT_NCAT = 8 };
+
+struct ProfScope {
+    ifr_state *s;
+    cudaStream_t st;
+    int ev0 = -1;
+    ProfScope(ifr_state *s_, int cat, int64_t bytes, cudaStream_t st_) : s(s_), st(st_) {
+        if (!s || !s->prof) return;
+        while ((int)s->ev_pool.size() < s->ev_next + 2) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return;
+            s->ev_pool.push_back(e);
+        }
+        ev0 = s->ev_next;
+        s->ev_next += 2;
+        cudaEventRecord(s->ev_pool[ev0], st);
+        s->recs.push_back({ev0, cat, bytes});
+    }
+    ~ProfScope() {
+        if (ev0 >= 0) cudaEventRecord(s->ev_pool[ev0 + 1], st);
+    }
+};
+
+int64_t proj_bytes(const Proj &p);
+
+int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st) {
+    ProfScope ps(s, cat, proj_bytes(p), st);
     int64_t r0 = 0;
     for (auto &q : p.parts) {
         ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, p.rows, st), "qgemm");
         r0 += q.rows;
+        if (s) s->launches++;
     }
     return IFR_OK;
 }
 
 // one decoder layer (attention or SSM) on n columns of s->x
 int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, float *vc, const int32_t *pos,
-                  cudaStream_t st) {
+                  bool draft, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
     const int d = c.hidden;
+    const int gcat = draft ? CAT_DRAFT_GEMV : CAT_LAYER_GEMV;
     int rc;
     ifr::rmsnorm(s->x, L.attn_norm, s->xn, n, d, c.rms_eps, d, d, st);
-    if ((rc = gemv(L.proj, s->xn, n, s->proj, false, st))) return rc;
+    s->launches += 4;  // two norms, the SSM/attention step, SwiGLU
+    if ((rc = gemv(s, gcat, L.proj, s->xn, n, s->proj, false, st))) return rc;
     if (L.ssm) {
+        ProfScope ps(s, CAT_SSM, 0, st);
         ifr::SsmArgs a{};
         a.proj = s->proj;
         a.ldp = L.proj.rows;
@@ -415,6 +462,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.eps = c.rms_eps;
         ECHECK(ifr::ssm_step(a, c.ssm_head_dim, st), "ssm_step");
     } else {
+        ProfScope ps(s, CAT_ATTN, 0, st);
         ifr::AttnArgs a{};
         a.qkv = s->proj;
         a.ldq = L.proj.rows;
@@ -435,11 +483,11 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.eps = c.rms_eps;
         ECHECK(ifr::attn_step(a, st), "attn_step");
     }
-    if ((rc = gemv(L.out, s->y, n, s->x, true, st))) return rc;
+    if ((rc = gemv(s, gcat, L.out, s->y, n, s->x, true, st))) return rc;
     ifr::rmsnorm(s->x, L.post_norm, s->xn, n, d, c.rms_eps, d, d, st);
-    if ((rc = gemv(L.gate_up, s->xn, n, s->gu, false, st))) return rc;
+    if ((rc = gemv(s, gcat, L.gate_up, s->xn, n, s->gu, false, st))) return rc;
     ifr::swiglu(s->gu, s->hmid, n, c.ffn, st);
-    return gemv(L.down, s->hmid, n, s->x, true, st);
+    return gemv(s, gcat, L.down, s->hmid, n, s->x, true, st);
 }
 
 // target forward of the n tokens in s->vtok at positions pos.. (device);
@@ -449,13 +497,15 @@ int target_forward(ifr_state *s, int n, int logit_from, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
     ECHECK(ifr::dequant_rows(m->embed.parts[0], s->vtok, n, s->x, st), "embedding");
+    s->launches += 2;  // embedding, final norm
     for (int li = 0; li < c.n_layers; li++) {
-        int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, st);
+        int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, false, st);
         if (rc) return rc;
     }
     ifr::rmsnorm(s->x, m->final_norm, s->hid, n, c.hidden, c.rms_eps, c.hidden, c.hidden, st);
     if (logit_from < n) {
-        int rc = gemv(m->lm_head, s->hid + (int64_t)logit_from * c.hidden, n - logit_from, s->logits, false, st);
+        int rc = gemv(s, CAT_LM_HEAD, m->lm_head, s->hid + (int64_t)logit_from * c.hidden, n - logit_from,
+                      s->logits, false, st);
         if (rc) return rc;
     }
     s->last_n = n;
@@ -483,15 +533,16 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
         ECHECK(ifr::dequant_rows(m->embed.parts[0], tok, 1, s->mtp_e, st), "mtp embedding");
         ifr::rmsnorm(s->mtp_e, m->mtp_norm_e, s->mtp_cat, 1, d, c.rms_eps, d, d, st);
         ifr::rmsnorm(hin, m->mtp_norm_h, s->mtp_cat + d, 1, d, c.rms_eps, d, d, st);
-        int rc = gemv(m->mtp_fc, s->mtp_cat, 1, s->x, false, st);
+        int rc = gemv(s, CAT_DRAFT_GEMV, m->mtp_fc, s->mtp_cat, 1, s->x, false, st);
         if (rc) return rc;
         set_pos_kernel<<<1, 1, 0, st>>>(s->mtp_pos, s->sc, j - 1);
-        if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, st))) return rc;
+        if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, true, st))) return rc;
         ECHECK(cudaMemcpyAsync(s->mtp_x, s->x, (size_t)d * 4, cudaMemcpyDeviceToDevice, st), "mtp hidden");
         ifr::rmsnorm(s->x, m->mtp_norm, s->mtp_xn, 1, d, c.rms_eps, d, d, st);
-        if ((rc = gemv(m->lm_head, s->mtp_xn, 1, s->logits, false, st))) return rc;
+        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->mtp_xn, 1, s->logits, false, st))) return rc;
         ECHECK(ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st), "draft argmax");
         ifr::set_token(s->vtok + j, s->outtok, st);
+        s->launches += 9;  // embedding, 3 norms, set_pos, 2 argmax, set_token, (copy)
     }
     return IFR_OK;
 }
@@ -780,6 +831,31 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
     return rc;
 }
 
+}  // extern "C"
+
+namespace {
+// the device work of one spec step (capturable): MTP drafts (or drafts
+// already in vtok[1..gamma]), verify, greedy accept, commit
+int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st) {
+    const ifr_model_info &c = s->m->info;
+    int rc = IFR_OK;
+    if (gamma > 0 && mtp) rc = mtp_draft(s, gamma, st);
+    if (!rc) {
+        ifr::set_token(s->vtok, &s->sc->last_token, st);
+        rc = target_forward(s, gamma + 1, 0, st);
+    }
+    if (!rc) {
+        cudaError_t e = ifr::accept_greedy(s->logits, s->vtok + 1, 1, gamma, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "accept_greedy");
+    }
+    if (!rc) ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, st);
+    s->launches += 4;  // set_token, 2 accept, commit
+    return rc;
+}
+}  // namespace
+
+extern "C" {
+
 int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts) {
     if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
     if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
@@ -790,35 +866,88 @@ int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts) {
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(s->m->ctx));
     int rc = IFR_OK;
-    if (gamma > 0) {
-        if (drafts) {
-            for (int i = 0; i < gamma; i++)
-                if (drafts[i] < 0 || drafts[i] >= c.vocab) { cudaSetDevice(prev); return ifr_fail(IFR_ERR_ARG, "draft token out of range"); }
-            cudaError_t e = cudaStreamSynchronize(st);  // staging buffer reuse
-            if (e == cudaSuccess) {
-                memcpy(s->h_tok, drafts, sizeof(int32_t) * gamma);
-                e = cudaMemcpyAsync(s->vtok + 1, s->h_tok, sizeof(int32_t) * gamma, cudaMemcpyHostToDevice, st);
-            }
-            if (e != cudaSuccess) rc = ifr_cuda_fail(e, "H2D drafts");
-        } else {
-            rc = mtp_draft(s, gamma, st);
+    if (gamma > 0 && drafts) {
+        for (int i = 0; i < gamma; i++)
+            if (drafts[i] < 0 || drafts[i] >= c.vocab) { cudaSetDevice(prev); return ifr_fail(IFR_ERR_ARG, "draft token out of range"); }
+        cudaError_t e = cudaStreamSynchronize(st);  // staging buffer reuse
+        if (e == cudaSuccess) {
+            memcpy(s->h_tok, drafts, sizeof(int32_t) * gamma);
+            e = cudaMemcpyAsync(s->vtok + 1, s->h_tok, sizeof(int32_t) * gamma, cudaMemcpyHostToDevice, st);
         }
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "H2D drafts");
+        if (!rc) rc = spec_step_device(s, gamma, false, st);
+    } else {
+        rc = spec_step_device(s, gamma, true, st);
     }
-    if (!rc) {
-        ifr::set_token(s->vtok, &s->sc->last_token, st);
-        rc = target_forward(s, gamma + 1, 0, st);
-    }
-    if (!rc) {
-        cudaError_t e = ifr::accept_greedy(s->logits, s->vtok + 1, 1, gamma, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
-        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "accept_greedy");
-    }
-    if (!rc) ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, st);
     if (!rc) {
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "spec step launch");
     }
     cudaSetDevice(prev);
     return rc;
+}
+
+int ifr_spec_graph(ifr_state *s, int gamma, int steps) {
+    if (!s || steps < 1) return ifr_fail(IFR_ERR_ARG, "invalid graph arguments");
+    if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
+    if (gamma > 0 && !s->m->has_mtp) return ifr_fail(IFR_ERR_ARG, "the model has no MTP head");
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    if (st == nullptr) return ifr_fail(IFR_ERR_ARG, "the context stream is the legacy default stream, which cannot be captured");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    if (s->graph_exec) { cudaGraphExecDestroy(s->graph_exec); s->graph_exec = nullptr; }
+    if (s->graph) { cudaGraphDestroy(s->graph); s->graph = nullptr; }
+    int rc = IFR_OK;
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) rc = ifr_cuda_fail(e, "begin capture");
+    for (int i = 0; !rc && i < steps; i++) rc = spec_step_device(s, gamma, true, st);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(st, &g);
+    if (!rc && e != cudaSuccess) rc = ifr_cuda_fail(e, "end capture");
+    if (!rc) {
+        s->graph = g;
+        e = cudaGraphInstantiate(&s->graph_exec, g, 0);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "graph instantiate");
+    } else if (g) {
+        cudaGraphDestroy(g);
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int ifr_spec_graph_launch(ifr_state *s) {
+    if (!s || !s->graph_exec) return ifr_fail(IFR_ERR_ARG, "no captured graph (call ifr_spec_graph first)");
+    ECHECK(cudaGraphLaunch(s->graph_exec, ifr_ctx_stream_of(s->m->ctx)), "graph launch");
+    return IFR_OK;
+}
+
+int ifr_state_profile(ifr_state *s, int enable) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    s->prof = enable != 0;
+    s->recs.clear();
+    s->ev_next = 0;
+    return IFR_OK;
+}
+
+int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count, int64_t *launches) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    ECHECK(cudaStreamSynchronize(ifr_ctx_stream_of(s->m->ctx)), "sync");
+    for (int k = 0; k < CAT_NCAT; k++) {
+        if (ms) ms[k] = 0;
+        if (bytes) bytes[k] = 0;
+        if (count) count[k] = 0;
+    }
+    for (auto &r : s->recs) {
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, s->ev_pool[r.ev0], s->ev_pool[r.ev0 + 1]) != cudaSuccess) continue;
+        if (ms) ms[r.cat] += t;
+        if (bytes) bytes[r.cat] += r.bytes;
+        if (count) count[r.cat] += 1;
+    }
+    if (launches) *launches = s->launches;
+    return IFR_OK;
 }
 
 int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars) {

@@ -76,6 +76,27 @@ class State:
             assert len(d) == gamma
         check(load().ifr_spec_step(self.handle, int(gamma), d.ctypes.data_as(ctypes.c_void_p) if d is not None else None))
 
+    def capture(self, gamma, steps):
+        """capture `steps` MTP spec steps into a CUDA graph (context stream must be capturable)"""
+        check(load().ifr_spec_graph(self.handle, int(gamma), int(steps)))
+
+    def launch(self):
+        check(load().ifr_spec_graph_launch(self.handle))
+
+    def profile(self, enable=True):
+        check(load().ifr_state_profile(self.handle, 1 if enable else 0))
+
+    CATEGORIES = ("lm_head", "draft_lm_head", "layer_gemv", "draft_gemv", "ssm", "attention")
+
+    def profile_read(self):
+        ms = (ctypes.c_double * 8)()
+        by = (ctypes.c_int64 * 8)()
+        ct = (ctypes.c_int * 8)()
+        nl = ctypes.c_int64()
+        check(load().ifr_state_profile_read(self.handle, ms, by, ct, ctypes.byref(nl)))
+        out = {c: dict(ms=ms[i], bytes=by[i], count=ct[i]) for i, c in enumerate(self.CATEGORIES)}
+        return out, nl.value
+
     def read(self):
         """(emitted tokens, position, last accept count, steps)"""
         n = ctypes.c_int()

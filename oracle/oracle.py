@@ -304,7 +304,9 @@ class OracleModel:
         last = int(np.argmax(lg))
         out, pos, h = [last], len(prompt), hid
         steps = []
+        import time as _time
         for s in range(n_steps):
+            t_step = _time.perf_counter()
             if drafts is None:
                 ds, hin = [], h
                 for j in range(1, gamma + 1):
@@ -329,7 +331,8 @@ class OracleModel:
             for t in range(acc + 1):
                 self.forward_token(cols[t], pos + t)
             out += ds[:acc] + [y]
-            steps.append(dict(drafts=ds, logits=np.stack(lgs), hidden=np.stack(hs), acc=acc, pos=pos))
+            steps.append(dict(drafts=ds, logits=np.stack(lgs), hidden=np.stack(hs), acc=acc, pos=pos,
+                              seconds=_time.perf_counter() - t_step))
             pos += acc + 1
             h = hs[acc]
             last = y
