@@ -164,6 +164,11 @@ int ifr_spec_graph_launch(ifr_state *s);
  * launches enqueued by the state so far */
 int ifr_state_profile(ifr_state *s, int enable);
 int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count, int64_t *launches);
+/* enqueue only the dequant-GEMV launches of one verify forward (every
+ * decoder-layer projection + the lm_head) on ncols columns of scratch
+ * activations, back to back (capturable): a measurement of the verify GEMVs
+ * alone.  Scratch buffers only; the committed state is not touched. */
+int ifr_gemv_pass(ifr_state *s, int ncols);
 /* synchronous read of the emitted tokens and of
  * scalars[4] = {position, last accept count, steps, last token} */
 int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars);

@@ -50,6 +50,7 @@ SIGNATURES = {
     "ifr_spec_graph_launch": (_i, [_vp]),
     "ifr_state_profile": (_i, [_vp, _i]),
     "ifr_state_profile_read": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    "ifr_gemv_pass": (_i, [_vp, _i]),
     "ifr_state_read": (_i, [_vp, _vp, _i, _vp, _vp]),
     "ifr_state_last_verify": (_i, [_vp, _vp, _vp, _vp, _vp]),
     "q4_k_gemv": (None, [_vp, _vp, _vp, _vp, _i, _i]),

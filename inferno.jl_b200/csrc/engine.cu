@@ -939,15 +939,39 @@ int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count,
         if (bytes) bytes[k] = 0;
         if (count) count[k] = 0;
     }
+    int failed = 0;
     for (auto &r : s->recs) {
         float t = 0.f;
-        if (cudaEventElapsedTime(&t, s->ev_pool[r.ev0], s->ev_pool[r.ev0 + 1]) != cudaSuccess) continue;
+        if (cudaEventElapsedTime(&t, s->ev_pool[r.ev0], s->ev_pool[r.ev0 + 1]) != cudaSuccess) {
+            failed++;
+            continue;
+        }
         if (ms) ms[r.cat] += t;
         if (bytes) bytes[r.cat] += r.bytes;
         if (count) count[r.cat] += 1;
     }
+    cudaGetLastError();  // a failed elapsed-time query must not surface in a later launch check
     if (launches) *launches = s->launches;
+    if (failed) return ifr_fail(IFR_ERR_UNSUPPORTED, "%d timings unavailable (events recorded inside a CUDA graph cannot be timed); profile eagerly", failed);
     return IFR_OK;
+}
+
+int ifr_gemv_pass(ifr_state *s, int ncols) {
+    if (!s || ncols < 1 || ncols > kNMax) return ifr_fail(IFR_ERR_ARG, "ncols must be in 1..%d", kNMax);
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    int rc = IFR_OK;
+    for (auto &L : s->m->layers) {
+        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.proj, s->xn, ncols, s->proj, false, st);
+        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.out, s->y, ncols, s->gu, false, st);
+        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->gu, false, st);
+        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.down, s->hmid, ncols, s->hid, false, st);
+    }
+    if (!rc) rc = gemv(s, CAT_LM_HEAD, s->m->lm_head, s->hid, ncols, s->logits, false, st);
+    cudaSetDevice(prev);
+    return rc;
 }
 
 int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars) {

@@ -97,6 +97,10 @@ class State:
         out = {c: dict(ms=ms[i], bytes=by[i], count=ct[i]) for i, c in enumerate(self.CATEGORIES)}
         return out, nl.value
 
+    def gemv_pass(self, ncols):
+        """enqueue the verify's dequant-GEMV launches alone (scratch activations)"""
+        check(load().ifr_gemv_pass(self.handle, int(ncols)))
+
     def read(self):
         """(emitted tokens, position, last accept count, steps)"""
         n = ctypes.c_int()
