@@ -110,6 +110,23 @@ int ifr_accept(ifr_ctx *ctx, const float *target, const float *draft,
                const int32_t *draft_tokens, const float *uniforms, int batch,
                int gamma, int vocab, float temperature, int32_t *accept_count,
                int32_t *out_tokens, int32_t *draft_out);
+/* ifr_accept without any device allocation (no counterpart in the reference):
+ * same arguments and bit-identical results, with the scratch in a fixed
+ * 1 MiB array per device inside the library instead of the context's
+ * cudaMalloc'd buffer.  For callers that must not allocate device memory at
+ * call time: a host whose own pool (e.g. CUDA.jl's) already holds the free
+ * HBM, or a serving loop that cannot take the device-wide synchronization
+ * cudaMalloc/cudaFree may cause.  Sizes whose scratch
+ * (2 * batch * (2 * gamma + 1) * ceil(vocab / 2048) floats plus small terms)
+ * exceeds 1 MiB fail with IFR_ERR_ARG.  The first call on a device does a
+ * one-time set-up (module load, symbol lookup): make it once before stream
+ * capture or timed work.  The array is shared by all callers on the device:
+ * calls that can overlap (other streams or contexts on that device) race and
+ * must be ordered by the caller. */
+int ifr_accept_noalloc(ifr_ctx *ctx, const float *target, const float *draft,
+                       const int32_t *draft_tokens, const float *uniforms, int batch,
+                       int gamma, int vocab, float temperature, int32_t *accept_count,
+                       int32_t *out_tokens, int32_t *draft_out);
 /* greedy verification (src/ModelCPU.jl:2099-2115): accept while
  * argmax(target[i]) == draft[i], then emit the target argmax */
 int ifr_accept_greedy(ifr_ctx *ctx, const float *target, const int32_t *draft_tokens,

@@ -469,3 +469,81 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
 }
 
 }  // namespace ifr
+
+// ------------------------------------------------ allocation-free entry ------
+// ifr_accept_noalloc: the sampled verification of ifr_accept with its scratch
+// in a file-scope device array instead of the context's cudaMalloc'd buffer.
+// Every scratch word is written by an earlier launch of the same call before
+// it is read (chunk_stats -> cmax/csum, row_decide -> rstat/xdraft/okflag,
+// finish -> rchunk), so nothing has to start at zero.  The one array per
+// device is shared by every caller on that device: calls whose launches can
+// overlap (different streams or contexts on one device) race on it and must
+// be ordered by the caller.
+#include "../../include/inferno_b200.h"
+
+#include <mutex>
+
+int ifr_fail(int code, const char *fmt, ...);
+int ifr_cuda_fail(cudaError_t e, const char *what);
+int ifr_ctx_device(const ifr_ctx *c);
+cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
+
+namespace {
+
+constexpr int64_t kNoAllocScratch = (int64_t)1 << 20;  // 1 MiB per device
+static __device__ __align__(256) unsigned char g_accept_scratch[kNoAllocScratch];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices];
+
+// set-up, once per device, with that device current: the array's address
+int noalloc_scratch(int dev, void **out) {
+    if (dev < 0 || dev >= kMaxDevices) return ifr_fail(IFR_ERR_ARG, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_accept_scratch);
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+        if (e != cudaSuccess) return ifr_cuda_fail(e, "cudaGetSymbolAddress(accept scratch)");
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return IFR_OK;
+}
+
+}  // namespace
+
+extern "C" int ifr_accept_noalloc(ifr_ctx *c, const float *target, const float *draft,
+                                  const int32_t *draft_tokens, const float *uniforms, int batch,
+                                  int gamma, int vocab, float temperature, int32_t *accept_count,
+                                  int32_t *out_tokens, int32_t *draft_out) {
+    if (!c || !target || !draft || !uniforms || !accept_count || !out_tokens)
+        return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    if (batch < 1 || gamma < 1 || gamma > 64 || vocab < 1)
+        return ifr_fail(IFR_ERR_ARG, "invalid sizes batch=%d gamma=%d vocab=%d", batch, gamma, vocab);
+    if (!(temperature > 0.f) || !(temperature < 1e30f))
+        return ifr_fail(IFR_ERR_ARG, "temperature must be finite and > 0 (got %g)", (double)temperature);
+    const int64_t need = ifr::accept_scratch_bytes(batch, gamma, vocab);
+    if (need > kNoAllocScratch)
+        return ifr_fail(IFR_ERR_ARG,
+                        "ifr_accept_noalloc: batch=%d gamma=%d vocab=%d needs %lld scratch bytes, above its "
+                        "fixed %lld (use ifr_accept)",
+                        batch, gamma, vocab, (long long)need, (long long)kNoAllocScratch);
+    const int dev = ifr_ctx_device(c);
+    void *scratch = nullptr;
+    int rc = noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+    cudaError_t e = ifr::accept_sampled(target, draft, draft_tokens, uniforms, batch, gamma, vocab,
+                                        temperature, accept_count, out_tokens, draft_out, scratch,
+                                        ifr_ctx_stream_of(c));
+    if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    if (e != cudaSuccess) return ifr_cuda_fail(e, "accept_noalloc launch");
+    return IFR_OK;
+}
