@@ -9,9 +9,9 @@ layers, Q4_K matmuls, Q6_K tied embedding/lm_head, one-layer MTP draft head)
 after a 128-token seeded prompt; one step = MTP draft of 4 tokens + one
 5-column verify forward + greedy acceptance + state rollback, replayed as a
 CUDA graph.  value = emitted tokens per second (all ranks).  `roofline` is the
-verify's dequant-GEMV launches (all decoder-layer GEMVs + the lm_head of one
-step), timed per launch with CUDA events inside a timed run.  Every step reads
-~967 MB of weights (verify 411 MB + 4 drafts x 139 MB), far above L2.
+verify's 97 dequant-GEMV launches (all decoder-layer GEMVs + the lm_head of
+one step) captured back to back in a CUDA graph and timed with CUDA events.
+Every step reads ~964 MB of weights (verify 407 MB + 4 drafts), far above L2.
 
 Workload "sweep": one step = one verify dequant-GEMV at
 N=5 columns (draft length 4 + 1) over each of the 16 seeded weights
@@ -20,8 +20,13 @@ weights resident in HBM (2.3 GB per step, larger than the 126 MB L2, so
 every step streams them from DRAM).  value = quantized weight bytes streamed
 per second (all ranks); `roofline` is the largest launch (Q4_K 151936x4096).
 
-Multi-GPU: every rank runs the same sweep on its own GPU (replicas, no
-collective); value sums the ranks' bytes over the max-over-ranks time.
+Multi-GPU: every rank runs the same workload on its own GPU (replicas, no
+collective); value sums the ranks' units over the max-over-ranks time.
+
+Profiling cases (no JSON line; the launches of interest are bracketed by
+cudaProfilerStart/Stop for `ncu --profile-from-start off`):
+    python bench.py --profile spec        # 2 graph-replayed spec steps, config 1
+    python bench.py --profile qgemv --qtype Q4_K --shape 65536x4096 --ncols 5
 """
 import argparse
 import json
@@ -547,6 +552,52 @@ def run_reference_spec(args):
 
 
 
+def run_profile(args):
+    """small cases for ncu: only the launches between profiler start/stop count"""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    pkg.load()
+    torch.cuda.set_device(0)
+    if args.profile == "spec":
+        from inferno_b200 import synth
+        from inferno_b200.engine import Model, State
+        ctx = pkg.Context(0, torch_stream=False)
+        model = Model(ctx, synth.cached(SPEC_PRESET, SPEC_SEED))
+        prompt = synth.prompt(model.info.vocab, SPEC_PROMPT, SPEC_SEED)
+        st = State(model, SPEC_PROMPT + 64)
+        st.prefill(prompt)
+        st.spec_step(args.gamma)
+        st.capture(args.gamma, 1)
+        for _ in range(3):
+            st.launch()
+        ctx.sync()
+        torch.cuda.profiler.start()
+        for _ in range(2):
+            st.launch()
+        ctx.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profile": "spec", "launches_per_step": _launches(st)}))
+        return
+    qt = {"Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q8_0": 8}[args.qtype]
+    M, K = (int(v) for v in args.shape.split("x"))
+    rng = np.random.default_rng(7)
+    ctx = pkg.Context(0)
+    t = ctx.upload(qt, make_weights(pkg, qt, M, K, rng), M, K)
+    X = torch.from_numpy(rng.normal(0, 1, (args.ncols, K)).astype(np.float32)).cuda()
+    Y = torch.empty(args.ncols, M, device="cuda")
+    for _ in range(3):
+        ctx.qgemm(t, X, Y)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(3):
+        ctx.qgemm(t, X, Y)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profile": "qgemv", "qtype": args.qtype, "shape": [M, K], "ncols": args.ncols,
+                      "weight_bytes": int(M * K * BPW[qt])}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -556,7 +607,14 @@ def main():
     ap.add_argument("--workload", default="spec", choices=["spec", "sweep"])
     ap.add_argument("--gamma", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["spec", "qgemv"], help="small case for ncu (no JSON line)")
+    ap.add_argument("--qtype", default="Q4_K")
+    ap.add_argument("--shape", default="65536x4096")
+    ap.add_argument("--ncols", type=int, default=5)
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.workload == "spec":

@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "model.cuh"
 
+#include <cooperative_groups.h>
 #include <math_constants.h>
 
 namespace ifr {
@@ -68,8 +69,8 @@ void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s) {
 }
 
 // -------------------------------------------------------- GatedDeltaNet -----
-// One CTA per head.  GatedDeltaNetCPU (ModelCPU.jl:566-731) for the N new
-// tokens, preceded by the replay of the previous call's committed tokens:
+// GatedDeltaNetCPU (ModelCPU.jl:566-731) for the N new tokens, preceded by
+// the replay of the previous call's committed tokens:
 //   * conv ring (:576-599): window = committed history (K-1 tokens) + new tokens
 //   * q, k L2-normalised with 1/(sqrt(ss) + 1e-6), q also x 1/sqrt(dk) (:638-651)
 //   * decay = exp(f32(ssm_a * softplus(clamp(alpha + dt_bias, +-20)))),
@@ -80,23 +81,44 @@ void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s) {
 // new tokens' conv inputs and (k, v, decay, beta); the next call first
 // replays the first a_prev+1 of them (a_prev = accepted drafts of the last
 // verify) and writes that committed state back before computing new outputs.
+//
+// Grid (kSsmSplit, H), one cluster of kSsmSplit CTAs per head.  The rows of S
+// (value dims) are independent given k and q, so CTA `rank` owns rows
+// r0 .. r0 + RPC of S, the conv channels of v rows r0.. and of q, k dims r0..;
+// the head's q and k are gathered from the cluster's shared memory, and the
+// per-head RMSNorm sums the CTAs' partial sums of squares in rank order.
+// Each conv channel's history is read and written by its owner only; the
+// replay record is read by every CTA before the first cluster barrier and
+// rewritten after it.
+constexpr int kSsmSplit = 8;
+
 template <int HD>
-__global__ void __launch_bounds__(256) ssm_step_kernel(SsmArgs a) {
-    constexpr int TPR = 256 / HD;   // threads per state row
-    constexpr int CPT = HD / TPR;   // state columns per thread
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_step_kernel(SsmArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    constexpr int RPC = HD / kSsmSplit;  // state rows (and q, k dims) per CTA
+    constexpr int TPR = 256 / RPC;       // threads per state row
+    constexpr int CPT = HD / TPR;        // state columns per thread (interleaved by TPR)
+    constexpr int REC = 2 * HD + 2;      // replay record floats per token
+    const int rank = (int)cluster.block_rank();
+    const int h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int N = a.N, K = a.K, C = a.C, qk = a.H * HD;
-    __shared__ float xc[3][kMaxN][HD];        // conv outputs q, k, v of the new tokens
-    __shared__ float rk[kMaxN][HD], rv[kMaxN][HD];
+    const int r0 = rank * RPC;
+    __shared__ float cq[kMaxN][RPC], ck[kMaxN][RPC], cv[kMaxN][RPC];  // own conv outputs
+    __shared__ __align__(16) float xq[kMaxN][HD];
+    __shared__ __align__(16) float xk[kMaxN][HD];
+    __shared__ __align__(16) float rk[kMaxN][HD];
+    __shared__ float rv[kMaxN][RPC];
     __shared__ float rdec[kMaxN], rbeta[kMaxN], ndec[kMaxN], nbeta[kMaxN];
     __shared__ float ab[2][kMaxN];
-    __shared__ float ys[kMaxN][HD];
-    __shared__ float red[8];
+    __shared__ float ys[kMaxN][RPC];
+    __shared__ float ssq[kMaxN];
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
 
-    // 1. conv window: committed history and new tokens, per owned channel
-    for (int lc = tid; lc < 3 * HD; lc += 256) {
-        const int part = lc / HD, ch = part * qk + h * HD + lc % HD;
+    // 1. conv of the owned channels: committed history + replayed + new tokens
+    for (int lc = tid; lc < 3 * RPC; lc += 256) {
+        const int part = lc / RPC, i = lc % RPC;
+        const int ch = part * qk + h * HD + r0 + i;
         float seq[3 + kMaxN + kMaxN];  // old history (K-1) + replayed + new
         int n = 0;
         for (int j = 0; j < K - 1; j++) seq[n++] = a.hist[(int64_t)j * C + ch];
@@ -113,7 +135,10 @@ __global__ void __launch_bounds__(256) ssm_step_kernel(SsmArgs a) {
         for (int t = 0; t < N; t++) {
             float acc = 0.f;
             for (int k = 0; k < K; k++) acc += seq[base + t + k] * w[k];
-            xc[part][t][lc % HD] = acc / (1.0f + expf(-acc));
+            const float o = acc / (1.0f + expf(-acc));
+            if (part == 0) cq[t][i] = o;
+            else if (part == 1) ck[t][i] = o;
+            else cv[t][i] = o;
         }
     }
     // 2. alpha / beta projections of the new tokens (ssm_alpha/beta . x)
@@ -126,32 +151,38 @@ __global__ void __launch_bounds__(256) ssm_step_kernel(SsmArgs a) {
         s = warp_sum(s);
         if (lane == 0) ab[which][t] = s;
     }
-    // saved replay data of the previous call (read before it is overwritten)
-    float *rkv = a.rkv + (int64_t)h * kMaxN * (2 * HD + 2);
-    for (int i = tid; i < r * (2 * HD + 2); i += 256) {
-        const int j = i / (2 * HD + 2), c = i % (2 * HD + 2);
-        const float v = rkv[i];
-        if (c < HD) rk[j][c] = v;
-        else if (c < 2 * HD) rv[j][c - HD] = v;
-        else if (c == 2 * HD) rdec[j] = v;
-        else rbeta[j] = v;
+    // 3. the previous call's replay record: k (all dims), own v rows, decay, beta
+    float *rec = a.rkv + (int64_t)h * kMaxN * REC;
+    for (int i = tid; i < r * HD; i += 256) rk[i / HD][i % HD] = rec[(i / HD) * REC + i % HD];
+    for (int i = tid; i < r * RPC; i += 256) rv[i / RPC][i % RPC] = rec[(i / RPC) * REC + HD + r0 + i % RPC];
+    if (tid < r) {
+        rdec[tid] = rec[tid * REC + 2 * HD];
+        rbeta[tid] = rec[tid * REC + 2 * HD + 1];
+    }
+    cluster.sync();  // conv slices visible to the cluster; old record read by all
+    // 4. the head's q and k, gathered from the owners
+    for (int i = tid; i < N * HD; i += 256) {
+        const int t = i / HD, c = i % HD, src = c / RPC, ci = c % RPC;
+        xq[t][c] = cluster.map_shared_rank(&cq[0][0], src)[t * RPC + ci];
+        xk[t][c] = cluster.map_shared_rank(&ck[0][0], src)[t * RPC + ci];
     }
     __syncthreads();
-    // 3. L2 norms of q, k per new token (warp t), gates in f64
+    // 5. L2 norms of q, k per new token (warp t), gates in f64
     if (warp < N) {
         const int t = warp;
         float qs = 0.f, ks = 0.f;
         for (int i = lane; i < HD; i += 32) {
-            qs += xc[0][t][i] * xc[0][t][i];
-            ks += xc[1][t][i] * xc[1][t][i];
+            qs += xq[t][i] * xq[t][i];
+            ks += xk[t][i] * xk[t][i];
         }
         qs = warp_sum(qs);
         ks = warp_sum(ks);
         const float scale = 1.0f / sqrtf((float)HD);
         const float qn = 1.0f / (sqrtf(qs) + 1e-6f) * scale, kn = 1.0f / (sqrtf(ks) + 1e-6f);
+        __syncwarp();
         for (int i = lane; i < HD; i += 32) {
-            xc[0][t][i] *= qn;
-            xc[1][t][i] *= kn;
+            xq[t][i] *= qn;
+            xk[t][i] *= kn;
         }
         if (lane == 0) {
             double av = (double)ab[0][t] + (double)a.dt_bias[h];
@@ -165,113 +196,150 @@ __global__ void __launch_bounds__(256) ssm_step_kernel(SsmArgs a) {
         }
     }
     __syncthreads();
-    // save this call's replay data
-    for (int i = tid; i < N * (2 * HD + 2); i += 256) {
-        const int t = i / (2 * HD + 2), c = i % (2 * HD + 2);
-        rkv[i] = c < HD ? xc[1][t][c] : (c < 2 * HD ? xc[2][t][c - HD] : (c == 2 * HD ? ndec[t] : nbeta[t]));
+    // 6. this call's replay record (rank 0: k, decay, beta; every CTA: its v rows)
+    if (rank == 0) {
+        for (int i = tid; i < N * HD; i += 256) rec[(i / HD) * REC + i % HD] = xk[i / HD][i % HD];
+        if (tid < N) {
+            rec[tid * REC + 2 * HD] = ndec[tid];
+            rec[tid * REC + 2 * HD + 1] = nbeta[tid];
+        }
     }
-    // 4. the state: row = tid / TPR, columns c0 .. c0 + CPT
-    const int row = tid / TPR, c0 = (tid % TPR) * CPT;
-    float *Sp = a.S + ((int64_t)h * HD + row) * HD + c0;
+    for (int i = tid; i < N * RPC; i += 256) rec[(i / RPC) * REC + HD + r0 + i % RPC] = cv[i / RPC][i % RPC];
+    // 7. the state rows: row r0 + tid / TPR, columns lc + TPR * e
+    const int row = tid / TPR, lc = tid % TPR;
+    float *Sp = a.S + ((int64_t)h * HD + r0 + row) * HD + lc;
     float s[CPT];
 #pragma unroll
-    for (int c = 0; c < CPT; c += 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(Sp + c);
-        s[c] = v.x; s[c + 1] = v.y; s[c + 2] = v.z; s[c + 3] = v.w;
-    }
+    for (int e = 0; e < CPT; e++) s[e] = Sp[TPR * e];
     auto update = [&](const float *kv, float dec, float beta, float vrow) {
         float sk = 0.f;
 #pragma unroll
-        for (int c = 0; c < CPT; c++) {
-            s[c] *= dec;
-            sk += s[c] * kv[c0 + c];
+        for (int e = 0; e < CPT; e++) {
+            s[e] *= dec;
+            sk += s[e] * kv[lc + TPR * e];
         }
 #pragma unroll
         for (int o = 1; o < TPR; o <<= 1) sk += __shfl_xor_sync(0xffffffffu, sk, o);
         const float dd = beta * (vrow - sk);
 #pragma unroll
-        for (int c = 0; c < CPT; c++) s[c] += dd * kv[c0 + c];
+        for (int e = 0; e < CPT; e++) s[e] += dd * kv[lc + TPR * e];
     };
     for (int j = 0; j < r; j++) update(rk[j], rdec[j], rbeta[j], rv[j][row]);
 #pragma unroll
-    for (int c = 0; c < CPT; c += 4) *reinterpret_cast<float4 *>(Sp + c) = make_float4(s[c], s[c + 1], s[c + 2], s[c + 3]);
+    for (int e = 0; e < CPT; e++) Sp[TPR * e] = s[e];
     for (int t = 0; t < N; t++) {
-        update(xc[1][t], ndec[t], nbeta[t], xc[2][t][row]);
+        update(xk[t], ndec[t], nbeta[t], cv[t][row]);
         float y = 0.f;
 #pragma unroll
-        for (int c = 0; c < CPT; c++) y += s[c] * xc[0][t][c0 + c];
+        for (int e = 0; e < CPT; e++) y += s[e] * xq[t][lc + TPR * e];
 #pragma unroll
         for (int o = 1; o < TPR; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
-        if (tid % TPR == 0) ys[t][row] = y;
+        if (lc == 0) ys[t][row] = y;
     }
     __syncthreads();
-    // 5. per-head RMSNorm, gate with silu(z)
-    for (int t = 0; t < N; t++) {
-        float ss = 0.f;
-        for (int i = tid; i < HD; i += 256) ss += ys[t][i] * ys[t][i];
-        ss = block_sum256(ss, red);
-        const float scale = 1.0f / sqrtf(ss / (float)HD + a.eps);
-        for (int i = tid; i < HD; i += 256) {
-            const float z = a.proj[(int64_t)t * a.ldp + C + h * HD + i];
-            const float yn = ys[t][i] * scale * a.norm_w[i];
-            a.y[(int64_t)t * a.ldy + h * HD + i] = yn * z * (1.0f / (1.0f + expf(-z)));
-        }
+    // 8. per-head RMSNorm (partial sums of squares, summed over the cluster in
+    //    rank order), gate with silu(z)
+    if (warp < N) {
+        const float v = lane < RPC ? ys[warp][lane] * ys[warp][lane] : 0.f;
+        const float t2 = warp_sum(v);
+        if (lane == 0) ssq[warp] = t2;
     }
+    cluster.sync();
+    for (int i = tid; i < N * RPC; i += 256) {
+        const int t = i / RPC, c = i % RPC;
+        float ss = 0.f;
+        for (int q = 0; q < kSsmSplit; q++) ss += cluster.map_shared_rank(&ssq[0], q)[t];
+        const float scale = 1.0f / sqrtf(ss / (float)HD + a.eps);
+        const float z = a.proj[(int64_t)t * a.ldp + C + h * HD + r0 + c];
+        const float yn = ys[t][c] * scale * a.norm_w[r0 + c];
+        a.y[(int64_t)t * a.ldy + h * HD + r0 + c] = yn * z * (1.0f / (1.0f + expf(-z)));
+    }
+    cluster.sync();  // peers may still read this CTA's shared memory
 }
 
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4) return cudaErrorInvalidValue;
-    if (head_dim == 128) ssm_step_kernel<128><<<a.H, 256, 0, s>>>(a);
-    else if (head_dim == 64) ssm_step_kernel<64><<<a.H, 256, 0, s>>>(a);
+    const dim3 grid(kSsmSplit, a.H);
+    if (head_dim == 128) ssm_step_kernel<128><<<grid, 256, 0, s>>>(a);
+    else if (head_dim == 64) ssm_step_kernel<64><<<grid, 256, 0, s>>>(a);
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 
 // ----------------------------------------------------------- attention ------
-// One CTA per query head.  FullAttentionCPU (ModelCPU.jl:787-887): per-head
-// [q; gate] rows, RMSNorm + half-split partial RoPE of q and k
+// FullAttentionCPU (ModelCPU.jl:787-887) for N new tokens of one sequence:
+// per-head [q; gate] rows, RMSNorm + half-split partial RoPE of q and k
 // (rmsnorm_rotary!, :188-232), K/V written at the token positions, GQA
-// attention with scale 1/sqrt(hd) over keys 0..pos+t (online softmax in
-// chunks of 64 keys), output x sigmoid(gate).  Every CTA of a KV group
-// normalises the group's new keys itself; the first one writes the cache.
+// attention with scale 1/sqrt(hd) over keys 0..pos+t, output x sigmoid(gate).
+//
+// Grid (kAttnSplit, n_head), one cluster of kAttnSplit CTAs per query head:
+// CTA `rank` takes a contiguous slice of the keys (flash-decoding split) and
+// runs an online softmax over it in chunks of 64 keys (FlashAttention.jl:19-84
+// uses the same chunking over all keys); the partial (max, sum, P.V) of the
+// slices are combined through distributed shared memory, each CTA finishing
+// HD / kAttnSplit output dims.  Every CTA normalises the new keys itself and
+// reads them from shared memory; one CTA per KV head writes them to the cache
+// (no CTA reads the new positions from the cache, so there is no race).
+constexpr int kAttnSplit = 8;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(256) attn_step_kernel(AttnArgs a) {
-    constexpr int DPT = (HD + 255) / 256;  // dims per thread
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_step_kernel(AttnArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    constexpr int G = 256 / HD;   // key groups of the P.V product
+    constexpr int DL = HD / 32;   // dims per lane in the score dot products
+    constexpr int DS = HD / kAttnSplit;
+    const int rank = (int)cluster.block_rank();
+    const int h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int N = a.N, ratio = a.nh / a.nkv, kvh = h / ratio;
     const int p0 = *a.pos;
-    __shared__ float q[kMaxN][HD], kn[kMaxN][HD], vn[kMaxN][HD], gt[kMaxN][HD];
+    const int nkeys = p0 + N;
+    const int per = (nkeys + kAttnSplit - 1) / kAttnSplit;
+    const int lo = min(nkeys, rank * per), hi = min(nkeys, lo + per);
+    __shared__ __align__(16) float q[kMaxN][HD];
+    __shared__ __align__(16) float kn[kMaxN][HD];
+    __shared__ __align__(16) float vn[kMaxN][HD];
+    __shared__ __align__(16) float po[kMaxN][HD];  // this slice's P.V (unnormalised)
     __shared__ float sc[kMaxN][64];
-    __shared__ float red[8];
+    __shared__ float ms[kMaxN], ls[kMaxN], fs[kMaxN];
     const int half = a.rotary_dim / 2;
-    // load
+
+    // 1. q of this head, new k and v of its KV head; RMSNorm + RoPE (warp t = token t)
     for (int i = tid; i < N * HD; i += 256) {
         const int t = i / HD, d = i % HD;
         const float *row = a.qkv + (int64_t)t * a.ldq;
         q[t][d] = row[(int64_t)h * 2 * HD + d];
-        gt[t][d] = row[(int64_t)h * 2 * HD + HD + d];
         kn[t][d] = row[(int64_t)a.nh * 2 * HD + kvh * HD + d];
         vn[t][d] = row[(int64_t)a.nh * 2 * HD + a.nkv * HD + kvh * HD + d];
     }
+    if (tid < kMaxN) {
+        ms[tid] = -CUDART_INF_F;
+        ls[tid] = 0.f;
+    }
     __syncthreads();
-    // RMSNorm + RoPE of q and k, token by token
-    for (int t = 0; t < N; t++) {
+    if (warp < N) {
+        const int t = warp;
         float sq = 0.f, sk = 0.f;
-        for (int d = tid; d < HD; d += 256) {
+        for (int d = lane; d < HD; d += 32) {
             sq += q[t][d] * q[t][d];
             sk += kn[t][d] * kn[t][d];
         }
-        sq = block_sum256(sq, red);
-        sk = block_sum256(sk, red);
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
         const float iq = 1.0f / sqrtf(sq / (float)HD + a.eps), ik = 1.0f / sqrtf(sk / (float)HD + a.eps);
-        __syncthreads();
-        for (int d = tid; d < HD; d += 256) {
+        for (int d = lane; d < HD; d += 32) {
             q[t][d] = q[t][d] * iq * a.q_norm[d];
             kn[t][d] = kn[t][d] * ik * a.k_norm[d];
         }
-        __syncthreads();
+        __syncwarp();
         const float *cs = a.rope_cos + (int64_t)(p0 + t) * half, *sn = a.rope_sin + (int64_t)(p0 + t) * half;
-        for (int i = tid; i < half; i += 256) {
+        for (int i = lane; i < half; i += 32) {
             const float c = cs[i], s_ = sn[i];
             float x1 = q[t][i], x2 = q[t][i + half];
             q[t][i] = x1 * c - x2 * s_;
@@ -281,9 +349,9 @@ __global__ void __launch_bounds__(256) attn_step_kernel(AttnArgs a) {
             kn[t][i] = x1 * c - x2 * s_;
             kn[t][i + half] = x1 * s_ + x2 * c;
         }
-        __syncthreads();
     }
-    if (h % ratio == 0) {
+    __syncthreads();
+    if (rank == 0 && h % ratio == 0) {
         for (int i = tid; i < N * HD; i += 256) {
             const int t = i / HD, d = i % HD;
             const int64_t o = ((int64_t)(p0 + t) * a.nkv + kvh) * HD + d;
@@ -291,86 +359,103 @@ __global__ void __launch_bounds__(256) attn_step_kernel(AttnArgs a) {
             a.vc[o] = vn[t][d];
         }
     }
-    // attention, online softmax over chunks of 64 keys
+
+    // 2. keys lo..hi: scores, online softmax, P.V, in chunks of 64
     const float scale = 1.0f / sqrtf((float)HD);
-    float o_[kMaxN][DPT];
-    float m[kMaxN], l[kMaxN];
+    const int d = tid % HD, g = tid / HD;
+    float o[kMaxN];
 #pragma unroll
-    for (int t = 0; t < kMaxN; t++) {
-        m[t] = -CUDART_INF_F;
-        l[t] = 0.f;
-#pragma unroll
-        for (int e = 0; e < DPT; e++) o_[t][e] = 0.f;
-    }
-    const int nkeys = p0 + N;
-    for (int j0 = 0; j0 < nkeys; j0 += 64) {
-        const int nj = min(64, nkeys - j0);
-        __syncthreads();
+    for (int t = 0; t < kMaxN; t++) o[t] = 0.f;
+    for (int j0 = lo; j0 < hi; j0 += 64) {
+        const int nj = min(64, hi - j0);
         for (int jj = warp; jj < nj; jj += 8) {
             const int j = j0 + jj;
             const float *kp = j < p0 ? a.kc + ((int64_t)j * a.nkv + kvh) * HD : kn[j - p0];
-            float part[kMaxN];
+            float kd[DL];
 #pragma unroll
-            for (int t = 0; t < kMaxN; t++) part[t] = 0.f;
-            for (int d = lane; d < HD; d += 32) {
-                const float kd = kp[d];
-#pragma unroll
-                for (int t = 0; t < kMaxN; t++)
-                    if (t < N) part[t] += q[t][d] * kd;
-            }
+            for (int e = 0; e < DL; e++) kd[e] = kp[lane + 32 * e];
 #pragma unroll
             for (int t = 0; t < kMaxN; t++) {
                 if (t < N) {
-                    const float v = warp_sum(part[t]);
-                    if (lane == 0) sc[t][jj] = (j <= p0 + t) ? v * scale : -CUDART_INF_F;
+                    float part = 0.f;
+#pragma unroll
+                    for (int e = 0; e < DL; e++) part += q[t][lane + 32 * e] * kd[e];
+                    part = warp_sum(part);
+                    if (lane == 0) sc[t][jj] = (j <= p0 + t) ? part * scale : -CUDART_INF_F;
                 }
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int t = 0; t < kMaxN; t++) {
-            if (t >= N) break;
-            float cm = -CUDART_INF_F;
-            for (int jj = 0; jj < nj; jj++) cm = fmaxf(cm, sc[t][jj]);
-            const float mn = fmaxf(m[t], cm);
-            if (mn == -CUDART_INF_F) continue;
-            const float f = expf(m[t] - mn);
-            l[t] *= f;
-#pragma unroll
-            for (int e = 0; e < DPT; e++) o_[t][e] *= f;
-            for (int jj = 0; jj < nj; jj++) {
-                const float p = expf(sc[t][jj] - mn);
-                l[t] += p;
-                const int j = j0 + jj;
-                const float *vp = j < p0 ? a.vc + ((int64_t)j * a.nkv + kvh) * HD : vn[j - p0];
-#pragma unroll
-                for (int e = 0; e < DPT; e++) {
-                    const int d = tid + 256 * e;
-                    if (d < HD) o_[t][e] += p * vp[d];
-                }
+        if (warp < N) {
+            const int t = warp;
+            const float s0 = lane < nj ? sc[t][lane] : -CUDART_INF_F;
+            const float s1 = lane + 32 < nj ? sc[t][lane + 32] : -CUDART_INF_F;
+            const float mo = ms[t], mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
+            float f = 1.f, e0 = 0.f, e1 = 0.f;
+            if (mn != -CUDART_INF_F) {
+                f = expf(mo - mn);
+                e0 = expf(s0 - mn);
+                e1 = expf(s1 - mn);
             }
-            m[t] = mn;
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < kMaxN; t++) {
-        if (t >= N) break;
-#pragma unroll
-        for (int e = 0; e < DPT; e++) {
-            const int d = tid + 256 * e;
-            if (d < HD) {
-                const float g = 1.0f / (1.0f + expf(-gt[t][d]));
-                a.out[(int64_t)t * a.ldo + (int64_t)h * HD + d] = o_[t][e] / l[t] * g;
+            if (lane < nj) sc[t][lane] = e0;
+            if (lane + 32 < nj) sc[t][lane + 32] = e1;
+            const float ps = warp_sum(e0 + e1);
+            if (lane == 0) {
+                ls[t] = ls[t] * f + ps;
+                ms[t] = mn;
+                fs[t] = f;
             }
         }
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++)
+            if (t < N) o[t] *= fs[t];
+#pragma unroll 4
+        for (int jj = g; jj < nj; jj += G) {
+            const int j = j0 + jj;
+            const float vd = j < p0 ? a.vc[((int64_t)j * a.nkv + kvh) * HD + d] : vn[j - p0][d];
+#pragma unroll
+            for (int t = 0; t < kMaxN; t++)
+                if (t < N) o[t] += sc[t][jj] * vd;
+        }
+        __syncthreads();  // sc and fs are rewritten by the next chunk
     }
+    // the key groups' partials, summed in group order
+    for (int gg = 0; gg < G; gg++) {
+        if (g == gg) {
+#pragma unroll
+            for (int t = 0; t < kMaxN; t++)
+                if (t < N) po[t][d] = gg == 0 ? o[t] : po[t][d] + o[t];
+        }
+        __syncthreads();
+    }
+
+    // 3. combine the slices (distributed shared memory); this CTA: dims rank*DS ..
+    cluster.sync();
+    for (int i = tid; i < N * DS; i += 256) {
+        const int t = i / DS, dd = rank * DS + i % DS;
+        float M = -CUDART_INF_F;
+        for (int r = 0; r < kAttnSplit; r++) M = fmaxf(M, cluster.map_shared_rank(&ms[0], r)[t]);
+        float L = 0.f, O = 0.f;
+        for (int r = 0; r < kAttnSplit; r++) {
+            const float mr = cluster.map_shared_rank(&ms[0], r)[t];
+            if (mr == -CUDART_INF_F) continue;
+            const float w = expf(mr - M);
+            L += cluster.map_shared_rank(&ls[0], r)[t] * w;
+            O += cluster.map_shared_rank(&po[0][0], r)[t * HD + dd] * w;
+        }
+        const float gv = a.qkv[(int64_t)t * a.ldq + (int64_t)h * 2 * HD + HD + dd];
+        a.out[(int64_t)t * a.ldo + (int64_t)h * HD + dd] = O / L * (1.0f / (1.0f + expf(-gv)));
+    }
+    cluster.sync();  // peers may still read this CTA's shared memory
 }
 
 cudaError_t attn_step(const AttnArgs &a, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.nh % a.nkv) return cudaErrorInvalidValue;
-    if (a.hd == 256) attn_step_kernel<256><<<a.nh, 256, 0, s>>>(a);
-    else if (a.hd == 128) attn_step_kernel<128><<<a.nh, 256, 0, s>>>(a);
-    else if (a.hd == 64) attn_step_kernel<64><<<a.nh, 256, 0, s>>>(a);
+    const dim3 grid(kAttnSplit, a.nh);
+    if (a.hd == 256) attn_step_kernel<256><<<grid, 256, 0, s>>>(a);
+    else if (a.hd == 128) attn_step_kernel<128><<<grid, 256, 0, s>>>(a);
+    else if (a.hd == 64) attn_step_kernel<64><<<grid, 256, 0, s>>>(a);
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
