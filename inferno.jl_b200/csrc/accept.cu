@@ -401,6 +401,8 @@ __global__ void __launch_bounds__(kNL) chunk_argmax_kernel(const float *__restri
     __shared__ float sv[kNL];
     __shared__ int si[kNL];
     const int c = blockIdx.x, r = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
     const float *row = target + (int64_t)r * V;
     float x[8];
     const int n = load8(row, V, c, x);
@@ -434,6 +436,8 @@ __global__ void greedy_finish_kernel(const float *__restrict__ vmax, const int32
                                      const int32_t *__restrict__ draft_tokens, int G, int nch,
                                      int32_t *__restrict__ accept_count, int32_t *__restrict__ out_tokens) {
     const int b = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x != 0) return;
     int32_t *ot = out_tokens + (int64_t)b * (G + 1);
     for (int i = 0; i <= G; i++) ot[i] = -1;
@@ -463,9 +467,10 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
     const int nch = (V + kCH - 1) / kCH;
     float *vmax = (float *)scratch;
     int32_t *imax = (int32_t *)((char *)scratch + (int64_t)B * (G + 1) * nch * 4);
-    chunk_argmax_kernel<<<dim3(nch, B * (G + 1)), kNL, 0, s>>>(target, V, nch, vmax, imax);
-    greedy_finish_kernel<<<B, 32, 0, s>>>(vmax, imax, draft_tokens, G, nch, accept_count, out_tokens);
-    return cudaGetLastError();
+    cudaError_t e = launch_k(chunk_argmax_kernel, dim3(nch, B * (G + 1)), dim3(kNL), 0, s, target, V, nch, vmax, imax);
+    if (e != cudaSuccess) return e;
+    return launch_k(greedy_finish_kernel, dim3(B), dim3(32), 0, s, (const float *)vmax, (const int32_t *)imax,
+                    draft_tokens, G, nch, accept_count, out_tokens);
 }
 
 }  // namespace ifr

@@ -112,6 +112,16 @@ int make_tensor(int type, int64_t rows, int64_t cols, int device, ifr_tensor **o
 
 }  // namespace
 
+namespace ifr {
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("IFR_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+}  // namespace ifr
+
 int ifr_ctx_device(const ifr_ctx *c) { return c->device; }
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c) { return c->stream; }
 

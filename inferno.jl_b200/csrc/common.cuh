@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define IFR_DEV __device__ __forceinline__
 
 namespace ifr {
@@ -102,5 +104,34 @@ IFR_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 IFR_DEV uint4 ldg_nc4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 IFR_DEV uint2 ldg_nc2(const void *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+
+// ---- programmatic dependent launch ------------------------------------------
+// Every kernel of the decode step is launched with programmatic stream
+// serialization: the next kernel may start (prologue, weight prefetch) while
+// this one runs.  Rules each kernel follows: nothing written to global memory
+// and nothing read that an earlier kernel produces before pdl_wait(), which
+// returns once all prerequisite grids have completed and their writes are
+// visible (and is a no-op for a normal launch).  Because every kernel waits,
+// completion is transitive along the stream.
+IFR_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+IFR_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+bool pdl_enabled();  // IFR_PDL=0 in the environment turns it off (api.cu)
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace ifr

@@ -512,9 +512,15 @@ int target_forward(ifr_state *s, int n, int logit_from, cudaStream_t st) {
     return IFR_OK;
 }
 
-__global__ void set_pos_kernel(int32_t *dst, const ifr::EngineScalars *sc, int add) { *dst = sc->pos + add; }
+__global__ void set_pos_kernel(int32_t *dst, const ifr::EngineScalars *sc, int add) {
+    ifr::pdl_trigger();
+    ifr::pdl_wait();
+    *dst = sc->pos + add;
+}
 __global__ void prefill_finish_kernel(ifr::EngineScalars *sc, const int32_t *tok, const float *hid, float *mtp_h,
                                       int d, int32_t *log, int log_cap) {
+    ifr::pdl_trigger();
+    ifr::pdl_wait();
     if (threadIdx.x == 0) {
         sc->last_token = *tok;
         if (sc->n_log < log_cap) log[sc->n_log++] = *tok;
@@ -529,15 +535,16 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
     const int d = c.hidden;
     for (int j = 1; j <= gamma; j++) {
         const int32_t *tok = j == 1 ? &s->sc->last_token : s->vtok + (j - 1);
-        const float *hin = j == 1 ? s->mtp_h : s->mtp_x;
+        // the previous draft's layer output stays in s->x until the fc GEMV below
+        // overwrites it, after this step's norms have read it
+        const float *hin = j == 1 ? s->mtp_h : s->x;
         ECHECK(ifr::dequant_rows(m->embed.parts[0], tok, 1, s->mtp_e, st), "mtp embedding");
         ifr::rmsnorm(s->mtp_e, m->mtp_norm_e, s->mtp_cat, 1, d, c.rms_eps, d, d, st);
         ifr::rmsnorm(hin, m->mtp_norm_h, s->mtp_cat + d, 1, d, c.rms_eps, d, d, st);
         int rc = gemv(s, CAT_DRAFT_GEMV, m->mtp_fc, s->mtp_cat, 1, s->x, false, st);
         if (rc) return rc;
-        set_pos_kernel<<<1, 1, 0, st>>>(s->mtp_pos, s->sc, j - 1);
+        ECHECK(ifr::launch_k(set_pos_kernel, dim3(1), dim3(1), 0, st, s->mtp_pos, (const ifr::EngineScalars *)s->sc, j - 1), "set_pos");
         if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, true, st))) return rc;
-        ECHECK(cudaMemcpyAsync(s->mtp_x, s->x, (size_t)d * 4, cudaMemcpyDeviceToDevice, st), "mtp hidden");
         ifr::rmsnorm(s->x, m->mtp_norm, s->mtp_xn, 1, d, c.rms_eps, d, d, st);
         if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->mtp_xn, 1, s->logits, false, st))) return rc;
         ECHECK(ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st), "draft argmax");
@@ -817,8 +824,10 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
         if (!rc && last) {
             e = ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
             if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "argmax"); break; }
-            prefill_finish_kernel<<<1, 256, 0, st>>>(s->sc, s->outtok, s->hid + (int64_t)(k - 1) * c.hidden,
-                                                     s->mtp_h, c.hidden, s->log, s->log_cap);
+            e = ifr::launch_k(prefill_finish_kernel, dim3(1), dim3(256), 0, st, s->sc, (const int32_t *)s->outtok,
+                              (const float *)(s->hid + (int64_t)(k - 1) * c.hidden), s->mtp_h, (int)c.hidden, s->log,
+                              (int)s->log_cap);
+            if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prefill finish"); break; }
         }
         // the prompt tokens buffer is reused by the next chunk
         if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = ifr_cuda_fail(cudaGetLastError(), "prefill");

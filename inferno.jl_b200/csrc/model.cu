@@ -37,6 +37,8 @@ __device__ __forceinline__ float block_sum256(float v, float *red) {
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                                       float *out, int n, float eps, int64_t ldx, int64_t ldo) {
     __shared__ float red[8];
+    pdl_trigger();
+    pdl_wait();
     const float *xr = x + blockIdx.x * ldx;
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += 256) ss += xr[i] * xr[i];
@@ -48,13 +50,15 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
 
 void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float eps, int64_t ldx, int64_t ldo,
              cudaStream_t s) {
-    rmsnorm_kernel<<<rows, 256, 0, s>>>(x, w, out, n, eps, ldx, ldo);
+    launch_k(rmsnorm_kernel, dim3(rows), dim3(256), 0, s, x, w, out, n, eps, ldx, ldo);
 }
 
 // ------------------------------------------------------------- SwiGLU -------
 // mlp_forward (ModelCPU.jl:482-508): h = silu(g) * u with g, u from one GEMV
 // whose output rows are [gate (ffn) | up (ffn)]
 __global__ void swiglu_kernel(const float *__restrict__ gu, float *__restrict__ h, int n, int ffn) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= (int64_t)n * ffn) return;
     const int64_t t = i / ffn, j = i % ffn;
@@ -65,7 +69,7 @@ __global__ void swiglu_kernel(const float *__restrict__ gu, float *__restrict__ 
 
 void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s) {
     const int64_t tot = (int64_t)n * ffn;
-    swiglu_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(gu, h, n, ffn);
+    launch_k(swiglu_kernel, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, s, gu, h, n, ffn);
 }
 
 // -------------------------------------------------------- GatedDeltaNet -----
@@ -113,6 +117,8 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     __shared__ float ab[2][kMaxN];
     __shared__ float ys[kMaxN][RPC];
     __shared__ float ssq[kMaxN];
+    pdl_trigger();
+    pdl_wait();
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
 
     // 1. conv of the owned channels: committed history + replayed + new tokens
@@ -260,10 +266,9 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4) return cudaErrorInvalidValue;
     const dim3 grid(kSsmSplit, a.H);
-    if (head_dim == 128) ssm_step_kernel<128><<<grid, 256, 0, s>>>(a);
-    else if (head_dim == 64) ssm_step_kernel<64><<<grid, 256, 0, s>>>(a);
-    else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (head_dim == 128) return launch_k(ssm_step_kernel<128>, grid, dim3(256), 0, s, a);
+    if (head_dim == 64) return launch_k(ssm_step_kernel<64>, grid, dim3(256), 0, s, a);
+    return cudaErrorInvalidValue;
 }
 
 // ----------------------------------------------------------- attention ------
@@ -298,6 +303,8 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     const int rank = (int)cluster.block_rank();
     const int h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int N = a.N, ratio = a.nh / a.nkv, kvh = h / ratio;
+    pdl_trigger();
+    pdl_wait();
     const int p0 = *a.pos;
     const int nkeys = p0 + N;
     const int per = (nkeys + kAttnSplit - 1) / kAttnSplit;
@@ -453,11 +460,10 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
 cudaError_t attn_step(const AttnArgs &a, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.nh % a.nkv) return cudaErrorInvalidValue;
     const dim3 grid(kAttnSplit, a.nh);
-    if (a.hd == 256) attn_step_kernel<256><<<grid, 256, 0, s>>>(a);
-    else if (a.hd == 128) attn_step_kernel<128><<<grid, 256, 0, s>>>(a);
-    else if (a.hd == 64) attn_step_kernel<64><<<grid, 256, 0, s>>>(a);
-    else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (a.hd == 256) return launch_k(attn_step_kernel<256>, grid, dim3(256), 0, s, a);
+    if (a.hd == 128) return launch_k(attn_step_kernel<128>, grid, dim3(256), 0, s, a);
+    if (a.hd == 64) return launch_k(attn_step_kernel<64>, grid, dim3(256), 0, s, a);
+    return cudaErrorInvalidValue;
 }
 
 // ------------------------------------------------------------- commit -------
@@ -469,6 +475,8 @@ cudaError_t attn_step(const AttnArgs &a, cudaStream_t s) {
 __global__ void commit_kernel(EngineScalars *sc, const int32_t *acc_dev, const int32_t *out_tok, int n,
                               int all, const float *hid, float *mtp_h, int d, int32_t *log, int log_cap) {
     __shared__ int acc_s;
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x == 0) {
         const int acc = all ? n - 1 : *acc_dev;
         acc_s = acc;
@@ -489,11 +497,17 @@ __global__ void commit_kernel(EngineScalars *sc, const int32_t *acc_dev, const i
 
 void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,
             float *mtp_h, int d, int32_t *log, int log_cap, cudaStream_t s) {
-    commit_kernel<<<1, 256, 0, s>>>(sc, acc, out_tok, n, all ? 1 : 0, hid, mtp_h, d, log, log_cap);
+    launch_k(commit_kernel, dim3(1), dim3(256), 0, s, sc, acc, out_tok, n, all ? 1 : 0, hid, mtp_h, d, log, log_cap);
 }
 
 // copy a device scalar token into a slot of the verify token vector
-__global__ void set_token_kernel(int32_t *dst, const int32_t *src) { *dst = *src; }
-void set_token(int32_t *dst, const int32_t *src, cudaStream_t s) { set_token_kernel<<<1, 1, 0, s>>>(dst, src); }
+__global__ void set_token_kernel(int32_t *dst, const int32_t *src) {
+    pdl_trigger();
+    pdl_wait();
+    *dst = *src;
+}
+void set_token(int32_t *dst, const int32_t *src, cudaStream_t s) {
+    launch_k(set_token_kernel, dim3(1), dim3(1), 0, s, dst, src);
+}
 
 }  // namespace ifr

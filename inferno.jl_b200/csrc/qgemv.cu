@@ -17,8 +17,8 @@
 //     accumulators; the Q4_K/Q5_K "min" term is one m16n8k8 against
 //     per-sub-block activation sums.
 //
-// Data movement (one persistent CTA per SM, 8 consumer warps + 1 producer warp):
-//   * the producer streams weight stages (16 M-tiles = one row group x the
+// Data movement (one persistent CTA per SM, 8 warps):
+//   * thread 0 streams weight stages (16 M-tiles = one row group x the
 //     units of one K pass) global -> shared with cp.async.bulk into a ring of
 //     S stages guarded by mbarriers, keeping ~S x 37..70 KB in flight per SM;
 //   * consumer warp w owns one unit of the pass (w % UW) and two M-tiles of
@@ -466,11 +466,15 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     o.passes = (a.nu + UW - 1) / UW;
     const int total = o.total();
 
+    pdl_trigger();
+    // the weights are constant: their first stages stream in before the
+    // previous kernel (producer of X, reader/writer of Y) has finished
     if (tid == 0) {
         for (int s = 0; s < a.S; s++) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB>(a, o, q, ring, full);
     }
+    pdl_wait();
     __syncthreads();
 
     const int ui = warp % UW, mp = warp / UW;
@@ -591,8 +595,7 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
         attr_set = true;
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, ncols, Y, UW, S, sweep_rg, accumulate ? 1 : 0, ldy};
-    qgemv_kernel<FMT, NT><<<grid, kThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_k(qgemv_kernel<FMT, NT>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
 }
 
 cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,

@@ -115,6 +115,8 @@ template <int T>
 __global__ void dequant_kernel(const uint8_t *__restrict__ w, float *__restrict__ out, int64_t rows,
                                int64_t cols, int64_t nu, int64_t nb_raw, const int32_t *__restrict__ idx,
                                int64_t src_rows) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= rows * nu * 8) return;
     const int sub = (int)(i & 7);
@@ -180,13 +182,12 @@ cudaError_t dequant_rows(const QTensor &t, const int32_t *idx, int64_t nrows, fl
     const int threads = 128;
     const unsigned grid = (unsigned)((n + threads - 1) / threads);
     switch (t.type) {
-    case 12: dequant_kernel<12><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
-    case 13: dequant_kernel<13><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
-    case 14: dequant_kernel<14><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
-    case 8: dequant_kernel<8><<<grid, threads, 0, s>>>(t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows); break;
+    case 12: return launch_k(dequant_kernel<12>, dim3(grid), dim3(threads), 0, s, (const uint8_t *)t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows);
+    case 13: return launch_k(dequant_kernel<13>, dim3(grid), dim3(threads), 0, s, (const uint8_t *)t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows);
+    case 14: return launch_k(dequant_kernel<14>, dim3(grid), dim3(threads), 0, s, (const uint8_t *)t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows);
+    case 8: return launch_k(dequant_kernel<8>, dim3(grid), dim3(threads), 0, s, (const uint8_t *)t.data, out, nrows, t.cols, t.nu, t.nb, idx, t.rows);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s) { return dequant_rows(t, nullptr, t.rows, out, s); }
