@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -48,6 +49,8 @@ struct ifr_ctx {
     cudaStream_t stream = nullptr;
     void *scratch = nullptr;
     size_t scratch_cap = 0;
+    std::atomic<int> refs{0};      // live models built on this context
+    std::atomic<bool> closing{false};
 };
 
 struct ifr_tensor {
@@ -123,6 +126,18 @@ bool pdl_enabled() {
 }  // namespace ifr
 
 int ifr_ctx_device(const ifr_ctx *c) { return c->device; }
+static void ctx_destroy_now(ifr_ctx *c) {
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->scratch) cudaFree(c->scratch);
+    if (c->own) cudaStreamDestroy(c->own);
+    delete c;
+}
+
+void ifr_ctx_retain(ifr_ctx *c) { c->refs++; }
+void ifr_ctx_release(ifr_ctx *c) {
+    if (--c->refs == 0 && c->closing) ctx_destroy_now(c);
+}
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c) { return c->stream; }
 
 // GGUF bytes on the host -> device M-tile tensor (caller owns q->data)
@@ -165,13 +180,12 @@ int ifr_ctx_create(int device, ifr_ctx **out) {
     return IFR_OK;
 }
 
+// a context outlives the models built on it: destroying it while models are
+// alive only marks it, and the last ifr_model_free completes the destruction
 int ifr_ctx_destroy(ifr_ctx *c) {
     if (!c) return IFR_OK;
-    DeviceGuard g(c->device);
-    cudaStreamSynchronize(c->stream);
-    if (c->scratch) cudaFree(c->scratch);
-    if (c->own) cudaStreamDestroy(c->own);
-    delete c;
+    c->closing = true;
+    if (c->refs.load() == 0) ctx_destroy_now(c);
     return IFR_OK;
 }
 

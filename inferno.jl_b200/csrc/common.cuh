@@ -33,9 +33,17 @@ cudaError_t repack(const QTensor &t, const uint8_t *raw, cudaStream_t s);
 cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s);
 cudaError_t dequant_rows(const QTensor &t, const int32_t *idx, int64_t nrows, float *out, cudaStream_t s);
 
-// Y[ncols][rows] = W * X[ncols][cols], ncols <= 8 per call; X 16-byte aligned
+// activation transform applied by the GEMV while it reads X
+struct XForm {
+    int kind = 0;              // 0: none; 1: RMSNorm x * (1/sqrt(mean x^2 + eps)) * w; 2: SwiGLU
+                               // silu(X[c][k]) * X[c][K + k] (X holds [gate | up] per column)
+    const float *w = nullptr;  // RMSNorm weights [cols]
+    float eps = 0.f;
+    int64_t ldx = 0;           // column stride of X in floats (0: the matrix's cols)
+};
+// Y[ncols][rows] (+)= W * f(X), ncols <= 8 per call; X 16-byte aligned, ldx a multiple of 4
 cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
-                        cudaStream_t s);
+                        cudaStream_t s, const XForm &xf = XForm());
 // host encoder (encode.cpp): 0 on success
 int quantize_host(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
 // device-side error flag set by bounded waits that ran out (read and cleared)
@@ -89,6 +97,16 @@ IFR_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A(16x16 f16) * B(16x8 f16), f32 (C = 0)
+IFR_DEV void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                        uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
 // D = A(16x8 f16) * B(8x8 f16) + C, f32 accumulate

@@ -27,6 +27,8 @@
 int ifr_fail(int code, const char *fmt, ...);
 int ifr_cuda_fail(cudaError_t e, const char *what);
 int ifr_ctx_device(const ifr_ctx *c);
+void ifr_ctx_retain(ifr_ctx *c);
+void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
 int ifr_upload_raw(ifr_ctx *c, int type, const void *host, int64_t rows, int64_t cols, ifr::QTensor *out);
 
@@ -651,6 +653,7 @@ int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out) {
         delete m;
         return rc;
     }
+    ifr_ctx_retain(ctx);
     *out = m;
     return IFR_OK;
 }
@@ -659,9 +662,11 @@ int ifr_model_free(ifr_model *m) {
     if (!m) return IFR_OK;
     int prev = 0;
     cudaGetDevice(&prev);
-    cudaSetDevice(ifr_ctx_device(m->ctx));
+    ifr_ctx *c = m->ctx;
+    cudaSetDevice(ifr_ctx_device(c));
     delete m;
     cudaSetDevice(prev);
+    ifr_ctx_release(c);
     return IFR_OK;
 }
 

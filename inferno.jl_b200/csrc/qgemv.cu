@@ -95,89 +95,147 @@ IFR_DEV int unit_exp(float m) {
     const int e = 14 - ex;
     return e < -100 ? -100 : (e > 100 ? 100 : e);
 }
-IFR_DEV uint32_t hi_lo_h2(float v) {  // (hi, lo) with v = hi + lo exactly up to f32 rounding of lo
-    const __half h = __float2half_rn(v);
-    const __half l = __float2half_rn(v - __half2float(h));
-    return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
-}
+
+struct GemvArgs {
+    const uint8_t *W;  // M-tiles
+    int64_t M, K;
+    int nrb, nu;       // row blocks of 16, units of 256
+    const float *X;    // column c at X + c * ldx
+    int64_t ldx;
+    int ncols;
+    float *Y;          // [ncols][M]
+    int UW, S;         // unit-warps per pass, ring stages
+    int sweep_rg;      // row groups per sweep (their sums fit the shared accumulator)
+    int accumulate;    // 1: Y += W X (residual), 0: Y = W X
+    int64_t ldy;       // Y[col * ldy + row]
+    int xf;            // activation transform: 0 none, 1 RMSNorm(xw, eps), 2 SwiGLU
+    const float *xw;   // RMSNorm weights [K]
+    float eps;
+};
 
 // ---- B fragments of one unit, built in registers ------------------------------
-// Lane L holds column 4*nt + L/8 as holder j = L%8 (tiles.cuh holder maps):
-// 32 scaled values as (hi, lo) pairs; fragments are gathered by shuffles.
-template <int FMT, int NT>
+// Lane (g, t) feeds B column g of every step: activation column 4 nt + g/2,
+// its fp16 high part (g even) or low part (g odd), for the elements
+// 64t .. 64t+63 of the unit (tiles.cuh).  The two lanes of a pair (g, g^1)
+// load 32 elements each, split them into (hi, lo) and swap halves by one
+// shuffle per register.  Activations are scaled by a power of two per unit
+// (exact) so that hi + lo carries ~22 bits; es undoes it on the f32 sums.
+template <int NT>
 struct BFrag {
-    uint32_t b[16][NT][2];  // per step: (k 2t,2t+1), (k 2t+8,2t+9) halves for B column g
-    uint32_t m[NT];         // min-MMA B fragment (Q4_K/Q5_K)
+    uint32_t b[16][NT][2];  // per step: slots (0,1), (2,3)
+    uint32_t m[NT];         // min-MMA B fragment: sub-block sums (Q4_K/Q5_K)
     float es[NT];           // 2^-e of the unit for C column 4*nt + t
 };
 
-template <int FMT, int NT>
-IFR_DEV void build_b(const float *__restrict__ X, int64_t K, int ncols, int64_t u, int lane,
-                     BFrag<FMT, NT> &F) {
-    const int g = lane >> 2, t = lane & 3, j = lane & 7;
+IFR_DEV uint32_t cvt_h2(float hi_half, float lo_half) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_half), "f"(lo_half));
+    return r;
+}
+IFR_DEV float h2_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
+IFR_DEV float h2_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
+
+// one activation with the transform applied (ragged K: the rare scalar path)
+template <int XF>
+__device__ __noinline__ float load_x1(const GemvArgs &a, const float *xc, float iv, int64_t k) {
+    if (k >= a.K) return 0.f;
+    float x = __ldg(xc + k);
+    if (XF == 1) x = x * iv * __ldg(a.xw + k);
+    if (XF == 2) x = x / (1.0f + expf(-x)) * __ldg(xc + a.K + k);
+    return x;
+}
+
+// 8 runs of 4 activations of column col at k0 + i * step (transform XF
+// applied; 0 beyond K or for absent columns)
+template <int XF>
+IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, int step, bool has,
+                      float (&v)[32]) {
+    const float *xc = a.X + (int64_t)col * a.ldx;
+    const float iv = XF == 1 && has ? inv[col] : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int64_t k = k0 + (int64_t)step * i;
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has && k + 3 < a.K) {
+            q = __ldg(reinterpret_cast<const float4 *>(xc + k));
+            if (XF == 1) {
+                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.xw + k));
+                q.x = q.x * iv * w.x;
+                q.y = q.y * iv * w.y;
+                q.z = q.z * iv * w.z;
+                q.w = q.w * iv * w.w;
+            } else if (XF == 2) {
+                const float4 u = __ldg(reinterpret_cast<const float4 *>(xc + a.K + k));
+                q.x = q.x / (1.0f + expf(-q.x)) * u.x;
+                q.y = q.y / (1.0f + expf(-q.y)) * u.y;
+                q.z = q.z / (1.0f + expf(-q.z)) * u.z;
+                q.w = q.w / (1.0f + expf(-q.w)) * u.w;
+            }
+        } else if (has) {
+            q = make_float4(load_x1<XF>(a, xc, iv, k), load_x1<XF>(a, xc, iv, k + 1),
+                            load_x1<XF>(a, xc, iv, k + 2), load_x1<XF>(a, xc, iv, k + 3));
+        }
+        v[4 * i] = q.x;
+        v[4 * i + 1] = q.y;
+        v[4 * i + 2] = q.z;
+        v[4 * i + 3] = q.w;
+    }
+}
+
+template <int FMT, int NT, int XF>
+IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, BFrag<NT> &F) {
+    const int g = lane >> 2, t = lane & 3, part = g & 1;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        const int col = 4 * nt + (lane >> 3);
+        const int col = 4 * nt + (g >> 1);
+        // this lane's steps 8 part .. 8 part + 7 (elem() of tiles.cuh)
+        constexpr bool kq = FMT == 12 || FMT == 13;
         float v[32];
-        const float *xc = X + (int64_t)col * K + u * 256;
-        const bool has = col < ncols;
+        load_x32<XF>(a, inv, col, kq ? u * 256 + 64 * t + 32 * part : u * 256 + 128 * part + 4 * t, kq ? 4 : 16,
+                 col < a.ncols, v);
+        float mx = 0.f;
 #pragma unroll
-        for (int r4 = 0; r4 < 8; r4++) {
-            const int e = elem_of_holder(FMT, j, 4 * r4);
-            const int64_t k = u * 256 + e;
-            if (has && k + 3 < K) {
-                const float4 q = __ldg(reinterpret_cast<const float4 *>(xc + e));
-                v[4 * r4] = q.x; v[4 * r4 + 1] = q.y; v[4 * r4 + 2] = q.z; v[4 * r4 + 3] = q.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 4; i++) v[4 * r4 + i] = (has && k + i < K) ? __ldg(xc + e + i) : 0.f;
-            }
-        }
-        float m = 0.f;
-#pragma unroll
-        for (int r = 0; r < 32; r++) m = fmaxf(m, fabsf(v[r]));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        const int ex = unit_exp(m);
+        for (int r = 0; r < 32; r++) mx = fmaxf(mx, fabsf(v[r]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const int ex = unit_exp(mx);
         const float scl = pow2i(ex);
         F.es[nt] = __shfl_sync(0xffffffffu, pow2i(-ex), 8 * t);
-        uint32_t H[32];
+        float S = 0.f;
+        uint32_t keep[8][2], send[8][2];
 #pragma unroll
-        for (int r = 0; r < 32; r++) {
-            v[r] *= scl;  // exact
-            H[r] = hi_lo_h2(v[r]);
-        }
-        const int src_base = 8 * (g >> 1), part = g & 1;
+        for (int i = 0; i < 8; i++) {
+            float x[4];
 #pragma unroll
-        for (int s = 0; s < 16; s++) {
-            uint32_t hv[4];
-#pragma unroll
-            for (int slot = 0; slot < 4; slot++) {
-                const int src = src_base + holder_of(FMT, elem_of(FMT, s, t, slot));
-                const uint32_t w = __shfl_sync(0xffffffffu, H[slot_reg(FMT, s, slot)], src);
-                hv[slot] = part ? (w >> 16) : (w & 0xffffu);
+            for (int j = 0; j < 4; j++) {
+                x[j] = v[4 * i + j] * scl;  // exact
+                S += x[j];
             }
-            F.b[s][nt][0] = hv[0] | (hv[1] << 16);
-            F.b[s][nt][1] = hv[2] | (hv[3] << 16);
+            const uint32_t h01 = cvt_h2(x[1], x[0]), h23 = cvt_h2(x[3], x[2]);
+            const uint32_t l01 = cvt_h2(x[1] - h2_hi(h01), x[0] - h2_lo(h01));
+            const uint32_t l23 = cvt_h2(x[3] - h2_hi(h23), x[2] - h2_lo(h23));
+            keep[i][0] = part ? l01 : h01;
+            keep[i][1] = part ? l23 : h23;
+            send[i][0] = part ? h01 : l01;
+            send[i][1] = part ? h23 : l23;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t r = __shfl_xor_sync(0xffffffffu, send[i][h], 4);
+                F.b[i][nt][h] = part ? r : keep[i][h];
+                F.b[8 + i][nt][h] = part ? keep[i][h] : r;
+            }
         }
         if (FMT == 12 || FMT == 13) {
-            // sub-block sums: holder j has elements of sub-blocks j/2 (r < 16) and 4 + j/2
-            float p0 = 0.f, p1 = 0.f;
-#pragma unroll
-            for (int r = 0; r < 16; r++) { p0 += v[r]; p1 += v[16 + r]; }
-            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
-            uint32_t hm[2];
-#pragma unroll
-            for (int kr = 0; kr < 2; kr++) {
-                const int src = src_base + 4 * (t >> 1) + 2 * kr;
-                const float a = __shfl_sync(0xffffffffu, p0, src);
-                const float b = __shfl_sync(0xffffffffu, p1, src);
-                const uint32_t w = hi_lo_h2(((t & 1) ? b : a) * 0.03125f);
-                hm[kr] = part ? (w >> 16) : (w & 0xffffu);
-            }
-            F.m[nt] = hm[0] | (hm[1] << 16);
+            // sums of sub-blocks 2t (part 0) and 2t+1 (part 1), x 2^-5 to stay in fp16 range
+            const float Sm = S * 0.03125f;
+            const uint32_t hs = cvt_h2(0.f, Sm);
+            const uint32_t ls = cvt_h2(0.f, Sm - h2_lo(hs));
+            const uint32_t r = __shfl_xor_sync(0xffffffffu, part ? hs : ls, 4) & 0xffffu;
+            F.m[nt] = part ? (r | (ls << 16)) : ((hs & 0xffffu) | (r << 16));
         }
     }
 }
@@ -190,92 +248,84 @@ IFR_DEV uint32_t bcast_byte_h2(uint32_t word, int byte) {
 IFR_DEV uint32_t bytes01_h2(uint32_t word) {
     return hsub2_u(__byte_perm(word, 0u, 0x4140u) | 0x64006400u, 0x64006400u);
 }
+constexpr uint32_t kMagic = 0x64006400u;     // (1024, 1024)
 constexpr uint32_t kNegH1024 = 0xE400E400u;  // (-1024, -1024)
 constexpr uint32_t kH1_16 = 0x2C002C00u;     // (1/16, 1/16)
 constexpr uint32_t kNegH64 = 0xD400D400u;    // (-64, -64)
 
+// Q4_K / Q5_K constants of one row for lane quad t: sub-blocks 2t (low
+// nibbles, steps 0-7) and 2t+1 (high nibbles, steps 8-15)
 struct QKRow {
-    uint32_t klo[2], nlo[2], khi[2], nhi[2];
-    uint32_t mA;
+    uint32_t klo, nlo, khi, nhi;  // A = q*sc: lo as fma(1024+q, sc, -1024 sc); hi from 1024+16q
+    uint32_t mA;                  // (m_2t, m_2t+1) for the min MMA
     float d, dm32;
 };
 
-// scales of the four sub-blocks lane quad t reads (2p, 2p+1, 4+2p, 5+2p)
 IFR_DEV void qk_row_consts(const uint4 &h, int t, QKRow &R) {
-    const int p = t >> 1;
-    const uint32_t A = h.y >> (16 * p), B = h.z >> (16 * p), C = h.w >> (16 * p);
-    const uint32_t sc_a = A & 0x3F3Fu, m_a = B & 0x3F3Fu;
-    const uint32_t sc_b = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
-    const uint32_t m_b = ((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-        const uint32_t scw = c ? sc_b : sc_a;
-        const uint32_t s_lo = bcast_byte_h2(scw, 0), s_hi = bcast_byte_h2(scw, 1);
-        R.klo[c] = s_lo;
-        R.nlo[c] = hmul2_u(s_lo, kNegH1024);
-        R.khi[c] = hmul2_u(s_hi, kH1_16);
-        R.nhi[c] = hmul2_u(s_hi, kNegH64);
-    }
-    R.mA = bytes01_h2((t & 1) ? m_b : m_a);
+    const int tt = t & 1;
+    const uint32_t A = h.y >> (16 * tt), B = h.z >> (16 * tt), C = h.w >> (16 * tt);
+    const bool upper = t >= 2;  // sub-blocks 4..7 use the split 6-bit encoding (src/Dequant.jl:345-362)
+    const uint32_t sc = upper ? ((C & 0x0F0Fu) | ((A >> 2) & 0x3030u)) : (A & 0x3F3Fu);
+    const uint32_t m = upper ? (((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u)) : (B & 0x3F3Fu);
+    const uint32_t s_lo = bcast_byte_h2(sc, 0), s_hi = bcast_byte_h2(sc, 1);
+    R.klo = s_lo;
+    R.nlo = hmul2_u(s_lo, kNegH1024);
+    R.khi = hmul2_u(s_hi, kH1_16);
+    R.nhi = hmul2_u(s_hi, kNegH64);
+    R.mA = bytes01_h2(m);
     R.d = h2f((uint16_t)(h.x & 0xffffu));
     R.dm32 = h2f((uint16_t)(h.x >> 16)) * 32.0f;
 }
 
+// bit b of each 16-bit half of w moved to bit `to` (compile-time shifts)
+template <int B, int TO>
+IFR_DEV uint32_t bits_to(uint32_t w) { return TO >= B ? (w << (TO - B)) : (w >> (B - TO)); }
+
 // ---- one M-tile (16 rows x 256 columns) from shared memory --------------------
 template <int FMT, int NT>
-IFR_DEV void mtile_qk(const uint8_t *tile, int lane, const BFrag<FMT, NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_qk(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
     constexpr bool Q5 = FMT == 13;
     const int g = lane >> 2, t = lane & 3;
     const uint4 h0 = lds128(tile + qk_hdr(g)), h1 = lds128(tile + qk_hdr(g + 8));
-    uint4 q0[2], q1[2], qh0 = {}, qh1 = {};
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-        q0[c] = lds128(tile + qk_qs(Q5, c, g, t));
-        q1[c] = lds128(tile + qk_qs(Q5, c, g + 8, t));
-    }
-    if (Q5) {
-        qh0 = lds128(tile + q5_qh(g, t & 1));
-        qh1 = lds128(tile + q5_qh(g + 8, t & 1));
-    }
+    const uint4 q00 = lds128(tile + qk_qs(Q5, 0, g, t)), q01 = lds128(tile + qk_qs(Q5, 1, g, t));
+    const uint4 q10 = lds128(tile + qk_qs(Q5, 0, g + 8, t)), q11 = lds128(tile + qk_qs(Q5, 1, g + 8, t));
+    uint4 hb = {};
+    if (Q5) hb = lds128(tile + q5_qh(g, t));
     QKRow R0, R1;
     qk_row_consts(h0, t, R0);
     qk_row_consts(h1, t, R1);
-    // two accumulator sets (even / odd words) halve the MMA dependency chains
-    float csc[2][NT][4], cm[NT][4];
+    float c[2][NT][4], cm[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) csc[0][nt][i] = csc[1][nt][i] = cm[nt][i] = 0.f;
+        for (int i = 0; i < 4; i++) c[0][nt][i] = c[1][nt][i] = cm[nt][i] = 0.f;
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
-        const int j4 = 2 * c + (t >> 1);
+    for (int w = 0; w < 8; w++) {
+        const uint32_t W0 = u4w(w < 4 ? q00 : q01, w & 3), W1 = u4w(w < 4 ? q10 : q11, w & 3);
+        const uint32_t W0s = W0 >> 8, W1s = W1 >> 8;
+        uint32_t lo01_0 = lop_and_or(W0, 0x000F000Fu, kMagic), lo23_0 = lop_and_or(W0s, 0x000F000Fu, kMagic);
+        uint32_t hi01_0 = lop_and_or(W0, 0x00F000F0u, kMagic), hi23_0 = lop_and_or(W0s, 0x00F000F0u, kMagic);
+        uint32_t lo01_1 = lop_and_or(W1, 0x000F000Fu, kMagic), lo23_1 = lop_and_or(W1s, 0x000F000Fu, kMagic);
+        uint32_t hi01_1 = lop_and_or(W1, 0x00F000F0u, kMagic), hi23_1 = lop_and_or(W1s, 0x00F000F0u, kMagic);
+        if (Q5) {
+            // fifth bit: step w (low nibble) -> bit 4 (+16), step w+8 (high nibble) -> bit 8 (x16)
+            lo01_0 |= bits_to<0, 4>(hb.x >> w) & 0x00100010u;
+            lo23_0 |= bits_to<0, 4>(hb.y >> w) & 0x00100010u;
+            lo01_1 |= bits_to<0, 4>(hb.z >> w) & 0x00100010u;
+            lo23_1 |= bits_to<0, 4>(hb.w >> w) & 0x00100010u;
+            hi01_0 |= bits_to<0, 8>(hb.x >> (w + 8)) & 0x01000100u;
+            hi23_0 |= bits_to<0, 8>(hb.y >> (w + 8)) & 0x01000100u;
+            hi01_1 |= bits_to<0, 8>(hb.z >> (w + 8)) & 0x01000100u;
+            hi23_1 |= bits_to<0, 8>(hb.w >> (w + 8)) & 0x01000100u;
+        }
+        const uint32_t a0 = hfma2_u(lo01_0, R0.klo, R0.nlo), a1 = hfma2_u(lo01_1, R1.klo, R1.nlo);
+        const uint32_t a2 = hfma2_u(lo23_0, R0.klo, R0.nlo), a3 = hfma2_u(lo23_1, R1.klo, R1.nlo);
+        const uint32_t b0 = hfma2_u(hi01_0, R0.khi, R0.nhi), b1 = hfma2_u(hi01_1, R1.khi, R1.nhi);
+        const uint32_t b2 = hfma2_u(hi23_0, R0.khi, R0.nhi), b3 = hfma2_u(hi23_1, R1.khi, R1.nhi);
 #pragma unroll
-        for (int w = 0; w < 4; w++) {
-            const uint32_t W0 = u4w(q0[c], w), W1 = u4w(q1[c], w);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const uint32_t s0 = h ? (W0 >> 8) : W0, s1 = h ? (W1 >> 8) : W1;
-                uint32_t lo0 = lop_and_or(s0, 0x000F000Fu, 0x64006400u);
-                uint32_t hi0 = lop_and_or(s0, 0x00F000F0u, 0x64006400u);
-                uint32_t lo1 = lop_and_or(s1, 0x000F000Fu, 0x64006400u);
-                uint32_t hi1 = lop_and_or(s1, 0x00F000F0u, 0x64006400u);
-                if (Q5) {
-                    const uint32_t H0 = u4w(qh0, w) >> (8 * h + 2 * j4);
-                    const uint32_t H1 = u4w(qh1, w) >> (8 * h + 2 * j4);
-                    lo0 |= (H0 << 4) & 0x00100010u;
-                    hi0 |= (H0 << 7) & 0x01000100u;
-                    lo1 |= (H1 << 4) & 0x00100010u;
-                    hi1 |= (H1 << 7) & 0x01000100u;
-                }
-                const uint32_t a0 = hfma2_u(lo0, R0.klo[c], R0.nlo[c]);
-                const uint32_t a1 = hfma2_u(lo1, R1.klo[c], R1.nlo[c]);
-                const uint32_t a2 = hfma2_u(hi0, R0.khi[c], R0.nhi[c]);
-                const uint32_t a3 = hfma2_u(hi1, R1.khi[c], R1.nhi[c]);
-                const int s = 8 * c + 2 * w + h;
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++)
-                    mma16816(csc[w & 1][nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
-            }
+        for (int nt = 0; nt < NT; nt++) {
+            mma16816(c[0][nt], a0, a1, a2, a3, F.b[w][nt][0], F.b[w][nt][1]);
+            mma16816(c[1][nt], b0, b1, b2, b3, F.b[w + 8][nt][0], F.b[w + 8][nt][1]);
         }
     }
 #pragma unroll
@@ -284,24 +334,25 @@ IFR_DEV void mtile_qk(const uint8_t *tile, int lane, const BFrag<FMT, NT> &F, fl
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const float d = i < 2 ? R0.d : R1.d, dm = i < 2 ? R0.dm32 : R1.dm32;
-            tot[nt][i] = fmaf(F.es[nt], d * (csc[0][nt][i] + csc[1][nt][i]) - dm * cm[nt][i], tot[nt][i]);
+            tot[nt][i] = fmaf(F.es[nt], d * (c[0][nt][i] + c[1][nt][i]) - dm * cm[nt][i], tot[nt][i]);
         }
     }
 }
 
+// Q6_K: step s = scale group s.  A = q - 32: low-nibble steps (1024 + q) - 1056,
+// high-nibble steps (1024 + 16 q) / 16 - 96; the int8 group scale multiplies
+// each step's f32 MMA result
 template <int NT>
-IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<14, NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const float d0 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g)));
     const float d1 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g + 8)));
     const uint4 sc0 = lds128(tile + q6_sc(g)), sc1 = lds128(tile + q6_sc(g + 8));
-    uint4 l0[2], l1[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        l0[h] = lds128(tile + q6_ql(h, g, t));
-        l1[h] = lds128(tile + q6_ql(h, g + 8, t));
-    }
+    const uint4 l00 = lds128(tile + q6_ql(0, g, t)), l01 = lds128(tile + q6_ql(1, g, t));
+    const uint4 l10 = lds128(tile + q6_ql(0, g + 8, t)), l11 = lds128(tile + q6_ql(1, g + 8, t));
     const uint4 hq0 = lds128(tile + q6_qh(g, t)), hq1 = lds128(tile + q6_qh(g + 8, t));
+    constexpr uint32_t k1056 = 0x64206420u;   // (1056, 1056)
+    constexpr uint32_t kNeg96 = 0xD600D600u;  // (-96, -96)
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
@@ -309,25 +360,27 @@ IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<14, NT> &F, fl
         for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
 #pragma unroll
     for (int s = 0; s < 16; s++) {
-        const int n = s >> 3, qq = (s >> 1) & 3, b = s & 1;
-        const int kw = 4 * n + 2 * (qq & 1) + b, kh = 2 * n + b;
-        const uint32_t WA0 = u4w(l0[kw >> 2], kw & 3), WA1 = u4w(l1[kw >> 2], kw & 3);
-        const uint32_t H0 = u4w(hq0, kh), H1 = u4w(hq1, kh);
-        const int ns = qq >= 2 ? 4 : 0, hs = 2 * qq;
-        const uint32_t x02_0 = ((WA0 >> ns) & 0x000F000Fu) | (((H0 >> hs) << 4) & 0x00300030u);
-        const uint32_t x13_0 = ((WA0 >> (ns + 8)) & 0x000F000Fu) | (((H0 >> (hs + 8)) << 4) & 0x00300030u);
-        const uint32_t x02_1 = ((WA1 >> ns) & 0x000F000Fu) | (((H1 >> hs) << 4) & 0x00300030u);
-        const uint32_t x13_1 = ((WA1 >> (ns + 8)) & 0x000F000Fu) | (((H1 >> (hs + 8)) << 4) & 0x00300030u);
-        const uint32_t a0 = hsub2_u(x02_0 | 0x64006400u, 0x64206420u);
-        const uint32_t a1 = hsub2_u(x02_1 | 0x64006400u, 0x64206420u);
-        const uint32_t a2 = hsub2_u(x13_0 | 0x64006400u, 0x64206420u);
-        const uint32_t a3 = hsub2_u(x13_1 | 0x64006400u, 0x64206420u);
+        const int lw = q6_lo_word(s), hw = q6_hi_word(s), qq = (s >> 1) & 3;
+        const uint32_t W0 = u4w(lw < 4 ? l00 : l01, lw & 3), W1 = u4w(lw < 4 ? l10 : l11, lw & 3);
+        const uint32_t H0 = u4w(hq0, hw) >> (2 * qq), H1 = u4w(hq1, hw) >> (2 * qq);
+        uint32_t a0, a1, a2, a3;
+        if (((s >> 2) & 1) == 0) {
+            a0 = hsub2_u(lop_and_or(W0, 0x000F000Fu, kMagic) | ((H0 << 4) & 0x00300030u), k1056);
+            a1 = hsub2_u(lop_and_or(W1, 0x000F000Fu, kMagic) | ((H1 << 4) & 0x00300030u), k1056);
+            a2 = hsub2_u(lop_and_or(W0 >> 8, 0x000F000Fu, kMagic) | ((H0 >> 4) & 0x00300030u), k1056);
+            a3 = hsub2_u(lop_and_or(W1 >> 8, 0x000F000Fu, kMagic) | ((H1 >> 4) & 0x00300030u), k1056);
+        } else {
+            a0 = hfma2_u(lop_and_or(W0, 0x00F000F0u, kMagic) | ((H0 << 8) & 0x03000300u), kH1_16, kNeg96);
+            a1 = hfma2_u(lop_and_or(W1, 0x00F000F0u, kMagic) | ((H1 << 8) & 0x03000300u), kH1_16, kNeg96);
+            a2 = hfma2_u(lop_and_or(W0 >> 8, 0x00F000F0u, kMagic) | (H0 & 0x03000300u), kH1_16, kNeg96);
+            a3 = hfma2_u(lop_and_or(W1 >> 8, 0x00F000F0u, kMagic) | (H1 & 0x03000300u), kH1_16, kNeg96);
+        }
         const float f0 = (float)(int8_t)(u4w(sc0, s >> 2) >> (8 * (s & 3)));
         const float f1 = (float)(int8_t)(u4w(sc1, s >> 2) >> (8 * (s & 3)));
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(c, a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+            float c[4];
+            mma16816_z(c, a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
             acc[nt][0] = fmaf(f0, c[0], acc[nt][0]);
             acc[nt][1] = fmaf(f0, c[1], acc[nt][1]);
             acc[nt][2] = fmaf(f1, c[2], acc[nt][2]);
@@ -343,10 +396,13 @@ IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<14, NT> &F, fl
     }
 }
 
+// Q8_0: steps 2b, 2b+1 = block b; int8 -> fp16 as ((x ^ 0x80) | 0x6400) - 1152,
+// the block scale multiplies the f32 MMA result of its two steps
 template <int NT>
-IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<8, NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const uint4 dd0 = lds128(tile + q8_d(g)), dd1 = lds128(tile + q8_d(g + 8));
+    constexpr uint32_t k1152 = 0x64806480u;
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
@@ -357,27 +413,24 @@ IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<8, NT> &F, flo
         const uint4 p0 = lds128(tile + q8_qs(q, g, t)), p1 = lds128(tile + q8_qs(q, g + 8, t));
 #pragma unroll
         for (int bb = 0; bb < 2; bb++) {
-            const int bl = 2 * q + bb;
-            const float db0 = h2f((uint16_t)(u4w(dd0, bl >> 1) >> (16 * (bl & 1))));
-            const float db1 = h2f((uint16_t)(u4w(dd1, bl >> 1) >> (16 * (bl & 1))));
+            const int blk = 2 * q + bb;
             float c[NT][4];
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                for (int i = 0; i < 4; i++) c[nt][i] = 0.f;
-#pragma unroll
             for (int h = 0; h < 2; h++) {
-                const uint32_t W0 = bb ? (h ? p0.w : p0.z) : (h ? p0.y : p0.x);
-                const uint32_t W1 = bb ? (h ? p1.w : p1.z) : (h ? p1.y : p1.x);
-                // int8 -> f16: (b ^ 0x80) | 0x6400 = 1152 + q, minus 1152
-                const uint32_t a0 = hsub2_u(((W0 & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                const uint32_t a1 = hsub2_u(((W1 & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                const uint32_t a2 = hsub2_u((((W0 >> 8) & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                const uint32_t a3 = hsub2_u((((W1 >> 8) & 0x00FF00FFu) ^ 0x00800080u) | 0x64006400u, 0x64806480u);
-                const int s = 2 * bl + h;
+                const int s = 2 * blk + h;
+                const uint32_t W0 = u4w(p0, 2 * bb + h) ^ 0x80808080u, W1 = u4w(p1, 2 * bb + h) ^ 0x80808080u;
+                const uint32_t a0 = hsub2_u(lop_and_or(W0, 0x00FF00FFu, kMagic), k1152);
+                const uint32_t a1 = hsub2_u(lop_and_or(W1, 0x00FF00FFu, kMagic), k1152);
+                const uint32_t a2 = hsub2_u(lop_and_or(W0 >> 8, 0x00FF00FFu, kMagic), k1152);
+                const uint32_t a3 = hsub2_u(lop_and_or(W1 >> 8, 0x00FF00FFu, kMagic), k1152);
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++) mma16816(c[nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+                for (int nt = 0; nt < NT; nt++) {
+                    if (h == 0) mma16816_z(c[nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+                    else mma16816(c[nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+                }
             }
+            const float db0 = h2f((uint16_t)(u4w(dd0, blk >> 1) >> (16 * (blk & 1))));
+            const float db1 = h2f((uint16_t)(u4w(dd1, blk >> 1) >> (16 * (blk & 1))));
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 acc[nt][0] = fmaf(db0, c[nt][0], acc[nt][0]);
@@ -392,19 +445,6 @@ IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<8, NT> &F, flo
 #pragma unroll
         for (int i = 0; i < 4; i++) tot[nt][i] = fmaf(F.es[nt], acc[nt][i], tot[nt][i]);
 }
-
-struct GemvArgs {
-    const uint8_t *W;  // M-tiles
-    int64_t M, K;
-    int nrb, nu;       // row blocks of 16, units of 256
-    const float *X;    // [ncols][K]
-    int ncols;
-    float *Y;          // [ncols][M]
-    int UW, S;         // unit-warps per pass, ring stages
-    int sweep_rg;      // row groups per sweep (their sums fit the shared accumulator)
-    int accumulate;    // 1: Y += W X (residual), 0: Y = W X
-    int64_t ldy;       // Y[col * ldy + row]
-};
 
 // Work order of one CTA: its contiguous range of row groups, cut into sweeps;
 // per sweep all K passes; per pass the sweep's row groups (one stage each).
@@ -446,7 +486,7 @@ IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring
     }
 }
 
-template <int FMT, int NT>
+template <int FMT, int NT, int XF>
 __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int MTB = mtile_bytes(FMT);
@@ -475,10 +515,41 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB>(a, o, q, ring, full);
     }
     pdl_wait();
+    // RMSNorm of the input columns: 1 / sqrt(sum x^2 / K + eps) per column
+    // (rmsnorm_cpu!, ModelCPU.jl:111-123), applied while building B
+    __shared__ float inv_s[8];
+    __shared__ float part_s[kConsumers][8];
+    if (XF == 1) {
+        float ss[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) ss[c] = 0.f;
+        for (int64_t k = 4 * tid; k < a.K; k += 4 * kThreads) {
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                if (c < a.ncols) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(a.X + c * a.ldx + k));
+                    ss[c] += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+                }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            float v = ss[c];
+#pragma unroll
+            for (int o2 = 16; o2; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
+            if (lane == 0) part_s[warp][c] = v;
+        }
+        __syncthreads();
+        if (tid < 8) {
+            float v = 0.f;
+            for (int w = 0; w < kConsumers; w++) v += part_s[w][tid];
+            inv_s[tid] = 1.0f / sqrtf(v / (float)a.K + a.eps);
+        }
+    }
     __syncthreads();
 
     const int ui = warp % UW, mp = warp / UW;
-    BFrag<FMT, NT> F;
+    BFrag<NT> F;
     int it = 0;
     bool dead = false;
     for (int sw = o.rg_lo; sw < o.rg_hi; sw += o.sweep_rg) {
@@ -488,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         for (int p = 0; p < o.passes; p++) {
             const int64_t u = (int64_t)p * UW + ui;
             const bool active = u < a.nu;
-            if (active) build_b<FMT, NT>(a.X, a.K, a.ncols, u, lane, F);
+            if (active) build_b<FMT, NT, XF>(a, inv_s, u, lane, F);
             for (int rg = sw; rg < sw_hi; rg++, it++) {
                 const int s = it % a.S;
                 if (!dead && !mbar_wait(full + s, (uint32_t)(it / a.S) & 1)) dead = true;
@@ -566,12 +637,12 @@ static int num_sms() {
     return n;
 }
 
-template <int FMT, int NT>
+template <int FMT, int NT, int XF>
 static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
-                          cudaStream_t s) {
+                          cudaStream_t s, const XForm &xf) {
     constexpr int MTB = mtile_bytes(FMT);
     constexpr int STAGE = 16 * MTB;
-    constexpr int kSmemMax = 227 * 1024;
+    constexpr int kSmemMax = 226 * 1024;  // dynamic; 1 KB of the 227 KB per block stays for static shared memory
     int UW = 1;
     while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
     const int MTG = 16 / UW;
@@ -579,34 +650,52 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     const int64_t nrg = (T.nrb + MTG - 1) / MTG;
     const int grid = (int)(nrg < num_sms() ? nrg : num_sms());
     // ring stages first (2..5), then the shared accumulator gets the rest
+    const int64_t per_cta = (nrg + grid - 1) / grid;
+    const int64_t stages_per_cta = per_cta * ((T.nu + UW - 1) / UW);
     int S = (kSmemMax - 128 - red - 16 * 1024) / STAGE;
     S = S < 2 ? 2 : (S > 5 ? 5 : S);
+    if (S > stages_per_cta) S = (int)stages_per_cta;  // small matrices: request only what is used
     const int acc_bytes_avail = kSmemMax - 128 - S * STAGE - red;
     const int rg_bytes = MTG * 16 * 8 * 4;
-    const int64_t per_cta = (nrg + grid - 1) / grid;
     int sweep_rg = acc_bytes_avail / rg_bytes;
     if (sweep_rg < 1) return cudaErrorInvalidConfiguration;
     if (sweep_rg > per_cta) sweep_rg = (int)per_cta;
     const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, ncols, Y, UW, S, sweep_rg, accumulate ? 1 : 0, ldy};
-    return launch_k(qgemv_kernel<FMT, NT>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
+    GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
+               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps};
+    return launch_k(qgemv_kernel<FMT, NT, XF>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
+}
+
+template <int FMT>
+static cudaError_t launch_fmt(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                              cudaStream_t s, const XForm &xf) {
+    const bool two = ncols > 4;
+    switch (xf.kind) {
+    case 0: return two ? launch<FMT, 2, 0>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 1: return two ? launch<FMT, 2, 1>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 1>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 2: return two ? launch<FMT, 2, 2>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 2>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    }
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
-                        cudaStream_t s) {
+                        cudaStream_t s, const XForm &xf) {
     if (ncols < 1 || ncols > 8) return cudaErrorInvalidValue;
-    const bool two = ncols > 4;
+    if (xf.kind < 0 || xf.kind > 2 || (xf.kind == 1 && !xf.w)) return cudaErrorInvalidValue;
     switch (T.type) {
-    case 12: return two ? launch<12, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<12, 1>(T, X, ncols, Y, accumulate, ldy, s);
-    case 13: return two ? launch<13, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<13, 1>(T, X, ncols, Y, accumulate, ldy, s);
-    case 14: return two ? launch<14, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<14, 1>(T, X, ncols, Y, accumulate, ldy, s);
-    case 8: return two ? launch<8, 2>(T, X, ncols, Y, accumulate, ldy, s) : launch<8, 1>(T, X, ncols, Y, accumulate, ldy, s);
+    case 12: return launch_fmt<12>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 13: return launch_fmt<13>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 14: return launch_fmt<14>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 8: return launch_fmt<8>(T, X, ncols, Y, accumulate, ldy, s, xf);
     }
     return cudaErrorInvalidValue;
 }

@@ -25,8 +25,8 @@ int64_t device_bytes(int type, int64_t rows, int64_t cols) {
 }
 
 // ---------------------------------------------------------------- repack ----
-// one thread per (row, unit): scatter that row's bytes of the unit into its
-// M-tile; padding rows and missing Q8_0 blocks become zeros.
+// one thread per (row, unit): that row's bits of the unit go to their M-tile
+// places (tiles.cuh); padding rows and missing Q8_0 blocks become zeros.
 template <int T>
 __global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ dst, int64_t rows,
                               int64_t nrb, int64_t nu, int64_t nb_raw) {
@@ -38,31 +38,33 @@ __global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restri
     const bool pad = row >= rows;
     const int BB = raw_block_bytes(T);
     if (T == 12 || T == 13) {
+        constexpr bool q5 = T == 13;
         const uint8_t *b = raw + (row * nb_raw + u) * BB;
-        const int qs0 = T == 13 ? 48 : 16;
+        const int qs0 = q5 ? 48 : 16;
         for (int k = 0; k < 16; k++) tile[qk_hdr(r) + k] = pad ? 0 : b[k];
-        if (T == 13)
-            for (int h = 0; h < 2; h++)
-                for (int k = 0; k < 16; k++) tile[q5_qh(r, h) + k] = pad ? 0 : b[16 + 16 * h + k];
-        for (int c = 0; c < 2; c++)
-            for (int t = 0; t < 4; t++)
-                for (int k = 0; k < 16; k++)
-                    tile[qk_qs(T == 13, c, r, t) + k] = pad ? 0 : b[qs0 + 64 * c + 16 * t + k];
+        for (int q = 0; q < 128; q++) tile[qk_qs_byte(q5, r, q)] = pad ? 0 : b[qs0 + q];
+        if (q5) {
+            for (int t = 0; t < 4; t++) {
+                uint8_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int j = 0; j < 64; j++) {
+                    const int e = 64 * t + j;
+                    const int bit = pad ? 0 : (b[16 + (e & 31)] >> (e >> 5)) & 1;
+                    const int off = q5_bit_byte(r, e) - (q5_qh(r & 7, t) + 8 * (r >> 3));
+                    w[off] |= (uint8_t)(bit << q5_bit_shift(e));
+                }
+                for (int k = 0; k < 8; k++) tile[q5_qh(r & 7, t) + 8 * (r >> 3) + k] = w[k];
+            }
+        }
     } else if (T == 14) {
+        // ql and qh bytes are permuted whole: low-nibble elements carry their
+        // high-nibble partner (e + 64), qq = 0 elements the other three 2-bit fields
         const uint8_t *b = raw + (row * nb_raw + u) * BB;
         tile[q6_d(r)] = pad ? 0 : b[208];
         tile[q6_d(r) + 1] = pad ? 0 : b[209];
         for (int k = 0; k < 16; k++) tile[q6_sc(r) + k] = pad ? 0 : b[192 + k];
-        for (int t = 0; t < 4; t++) {
-            for (int h = 0; h < 2; h++)
-                for (int q = 0; q < 16; q++) {
-                    const int k = 4 * h + (q >> 2), j = q & 3;
-                    tile[q6_ql(h, r, t) + q] = pad ? 0 : b[16 * k + 4 * t + j];
-                }
-            for (int q = 0; q < 16; q++) {
-                const int k = q >> 2, j = q & 3;
-                tile[q6_qh(r, t) + q] = pad ? 0 : b[128 + 16 * k + 4 * t + j];
-            }
+        for (int e = 0; e < 256; e++) {
+            if (q6_lo_shift(e) == 0) tile[q6_lo_byte(r, e)] = pad ? 0 : b[q6_raw_lo_byte(e)];
+            if (q6_hi_shift(e) == 0) tile[q6_hi_byte(r, e)] = pad ? 0 : b[q6_raw_hi_byte(e)];
         }
     } else {  // Q8_0: unit u = raw blocks 8u .. 8u+7
         for (int bl = 0; bl < 8; bl++) {
@@ -71,9 +73,7 @@ __global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restri
             const uint8_t *b = raw + (row * nb_raw + rb) * BB;
             tile[q8_d(r) + 2 * bl] = miss ? 0 : b[0];
             tile[q8_d(r) + 2 * bl + 1] = miss ? 0 : b[1];
-            for (int t = 0; t < 4; t++)
-                for (int o = 0; o < 8; o++)
-                    tile[q8_qs(bl >> 1, r, t) + 8 * (bl & 1) + o] = miss ? 0 : b[2 + 8 * t + o];
+            for (int p = 0; p < 32; p++) tile[q8_qs_byte(r, 32 * bl + p)] = miss ? 0 : b[2 + p];
         }
     }
 }
@@ -130,49 +130,38 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ w, float *__restrict_
     const uint8_t *tile = w + ((row >> 4) * nu + u) * mtile_bytes(T);
     float *o = out + orow * cols + u * 256 + 32 * sub;
     if (T == 12 || T == 13) {
-        // src/Dequant.jl:325-375 (Q4_K), :379-441 (Q5_K)
+        // src/Dequant.jl:325-375 (Q4_K), :379-441 (Q5_K): element e = 32 sub + l is
+        // nibble (e % 64 >= 32) of raw qs byte 32 (e / 64) + e % 32
+        constexpr bool q5 = T == 13;
         const uint8_t *hdr = tile + qk_hdr(r);
         const float d = h2f_bytes(hdr), dmin = h2f_bytes(hdr + 2);
         uint32_t sc, m;
         scale_min_k(sub, hdr + 4, sc, m);
         const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
-        const int j = sub >> 1, hi = sub & 1;
+        const int hi = sub & 1;
         for (int l = 0; l < 32; l++) {
-            const int byte = 32 * j + l;  // raw qs byte index
-            const int c = byte >> 6, t = (byte >> 4) & 3, k = byte & 15;
-            const uint8_t v = tile[qk_qs(T == 13, c, r, t) + k];
+            const int e = 32 * sub + l;
+            const uint8_t v = tile[qk_qs_byte(q5, r, 32 * (e >> 6) + (e & 31))];
             uint32_t q = hi ? (v >> 4) : (v & 0x0f);
-            if (T == 13 && ((tile[q5_qh(r, l >> 4) + (l & 15)] >> (2 * j + hi)) & 1)) q += 16;
+            if (q5 && ((tile[q5_bit_byte(r, e)] >> q5_bit_shift(e)) & 1)) q += 16;
             o[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
         }
     } else if (T == 14) {
-        // src/Dequant.jl:558-601: d * sc * q, left to right; two 16-groups per thread
+        // src/Dequant.jl:558-601: (d * sc[e / 16]) * (q - 32)
         const float d = h2f_bytes(tile + q6_d(r));
-        for (int gi = 0; gi < 2; gi++) {
-            const int g = 2 * sub + gi;  // group of 16 = element e/16
-            const int n = g >> 3, qq = (g >> 1) & 3, b = g & 1, a = qq & 1;
-            const float ds = __fmul_rn(d, (float)(int8_t)tile[q6_sc(r) + g]);
-            for (int e = 0; e < 16; e++) {
-                const int l = 16 * b + e, t = (l >> 2) & 3, jj = l & 3;
-                const int k = 4 * n + 2 * a + b;  // raw ql offset 16k + 4t + jj
-                const uint8_t lb = tile[q6_ql(k >> 2, r, t) + 4 * (k & 3) + jj];
-                const uint32_t lo = qq < 2 ? (lb & 0x0f) : (lb >> 4);
-                const int kh = 2 * n + b;         // raw qh offset 16kh + 4t + jj
-                const uint8_t hb = tile[q6_qh(r, t) + 4 * kh + jj];
-                const int q = (int)(lo | (((hb >> (2 * qq)) & 3) << 4)) - 32;
-                o[16 * gi + e] = __fmul_rn(ds, (float)q);
-            }
+        for (int l = 0; l < 32; l++) {
+            const int e = 32 * sub + l;
+            const float ds = __fmul_rn(d, (float)(int8_t)tile[q6_sc(r) + (e >> 4)]);
+            const int l4 = (tile[q6_lo_byte(r, e)] >> q6_lo_shift(e)) & 15;
+            const int h2 = (tile[q6_hi_byte(r, e)] >> q6_hi_shift(e)) & 3;
+            o[l] = __fmul_rn(ds, (float)((l4 | (h2 << 4)) - 32));
         }
     } else {
         // Q8_0, src/Dequant.jl:304-321; block `sub` of the unit
         const int64_t blk = 8 * u + sub;
         if (blk >= nb_raw) return;
         const float d = h2f_bytes(tile + q8_d(r) + 2 * sub);
-        for (int l = 0; l < 32; l++) {
-            const int t = l >> 3, k = l & 7;
-            const int8_t q = (int8_t)tile[q8_qs(sub >> 1, r, t) + 8 * (sub & 1) + k];
-            o[l] = __fmul_rn(d, (float)q);
-        }
+        for (int l = 0; l < 32; l++) o[l] = __fmul_rn(d, (float)(int8_t)tile[q8_qs_byte(r, 32 * sub + l)]);
     }
 }
 

@@ -12,75 +12,94 @@ CHECKER = r"""
 #include "tiles.cuh"
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 using namespace ifr;
 static int fails = 0;
 #define CHECK(c) do { if (!(c)) { std::printf("FAIL %s line %d\n", #c, __LINE__); fails++; } } while (0)
 
+// bit coverage of one M-tile
+static int cov[4352 * 8];
+static void mark_bits(int byte, int bit0, int nbits) { for (int i = 0; i < nbits; i++) cov[byte * 8 + bit0 + i]++; }
+static void mark_bytes(int byte, int n) { for (int i = 0; i < n; i++) mark_bits(byte + i, 0, 8); }
+static int pos_of_slot(int slot) { return wperm(slot); }  // stored position the GEMV unpack reads
+
 int main() {
+    // the MMA element map covers the unit once
+    int seen[256]; std::memset(seen, 0, sizeof seen);
+    for (int T : {12, 14}) {
+        std::memset(seen, 0, sizeof seen);
+        for (int s = 0; s < 16; s++) for (int t = 0; t < 4; t++) for (int sl = 0; sl < 4; sl++) seen[elem(T, s, t, sl)]++;
+        for (int e = 0; e < 256; e++) CHECK(seen[e] == 1);
+    }
+    for (int i = 0; i < 4; i++) CHECK(wperm(wperm(i)) == i);
+
     const int types[4] = {12, 13, 14, 8};
     for (int ti = 0; ti < 4; ti++) {
-        int T = types[ti];
-        // element map: every (s, t, slot) hits each element of the unit once
-        int seen[256]; std::memset(seen, 0, sizeof seen);
-        for (int s = 0; s < 16; s++) for (int t = 0; t < 4; t++) for (int sl = 0; sl < 4; sl++) {
-            int e = elem_of(T, s, t, sl);
-            CHECK(e >= 0 && e < 256);
-            seen[e]++;
-            // holder register is independent of t and given by slot_reg
-            CHECK(hreg_of(T, e) == slot_reg(T, s, sl));
-            // four t's of one (s, slot) live in distinct holders
-            for (int t2 = 0; t2 < t; t2++) CHECK(holder_of(T, elem_of(T, s, t2, sl)) != holder_of(T, e));
-        }
-        for (int e = 0; e < 256; e++) CHECK(seen[e] == 1);
-        // holder bijection
-        for (int j = 0; j < 8; j++) for (int r = 0; r < 32; r++) {
-            int e = elem_of_holder(T, j, r);
-            CHECK(e >= 0 && e < 256 && holder_of(T, e) == j && hreg_of(T, e) == r);
-        }
-        // holders load runs of 4 (or 16) consecutive elements, 16-byte aligned
-        for (int j = 0; j < 8; j++) for (int r = 0; r < 32; r += 4) {
-            int e = elem_of_holder(T, j, r);
-            CHECK(e % 4 == 0);
-            for (int i = 1; i < 4; i++) CHECK(elem_of_holder(T, j, r + i) == e + i);
-        }
-    }
-    // Q4_K / Q5_K: lane quad t reads sub-blocks 2p,2p+1 (c=0) and 4+2p,5+2p (c=1)
-    for (int s = 0; s < 16; s++) for (int t = 0; t < 4; t++) for (int sl = 0; sl < 4; sl++) {
-        int e = elem_qk(s, t, sl), c = s >> 3, p = t >> 1;
-        int sub = e >> 5;
-        CHECK(sub == 2 * (2 * c + p) + ((sl & 2) ? 1 : 0));
-        // the byte holding e in the raw block sits in lane t's qs piece of chunk c
-        int lq = e & 31, j4 = e >> 6;  // raw qs byte = 32*j4 + l
-        int byte = 32 * j4 + lq;
-        CHECK(byte >= 64 * c + 16 * t && byte < 64 * c + 16 * t + 16);
-    }
-    // min-MMA sub-blocks: the 4 lane quads x 2 k-rows cover sub-blocks 0..7 once
-    int ms[8] = {0};
-    for (int t = 0; t < 4; t++) for (int kr = 0; kr < 2; kr++) ms[minsub_qk(t, kr)]++;
-    for (int i = 0; i < 8; i++) CHECK(ms[i] == 1);
-    // M-tile byte maps: pieces cover the tile exactly once
-    const int T2[4] = {12, 13, 14, 8};
-    for (int ti = 0; ti < 4; ti++) {
-        int T = T2[ti], nb = mtile_bytes(T);
-        static int cov[8192]; std::memset(cov, 0, sizeof cov);
-        auto mark = [&](int off, int n) { for (int i = 0; i < n; i++) cov[off + i]++; };
+        const int T = types[ti], nb = mtile_bytes(T);
+        CHECK(nb == 16 * (T == 8 ? 8 * 34 : raw_block_bytes(T)));
+        std::memset(cov, 0, sizeof cov);
         for (int r = 0; r < 16; r++) {
             if (T == 12 || T == 13) {
-                mark(qk_hdr(r), 16);
-                if (T == 13) for (int h = 0; h < 2; h++) mark(q5_qh(r, h), 16);
-                for (int c = 0; c < 2; c++) for (int t = 0; t < 4; t++) mark(qk_qs(T == 13, c, r, t), 16);
+                const bool q5 = T == 13;
+                mark_bytes(qk_hdr(r), 16);
+                for (int q = 0; q < 128; q++) mark_bytes(qk_qs_byte(q5, r, q), 1);
+                if (q5) for (int e = 0; e < 256; e++) mark_bits(q5_bit_byte(r, e), q5_bit_shift(e), 1);
             } else if (T == 14) {
-                mark(q6_d(r), 2); mark(q6_sc(r), 16);
-                for (int h = 0; h < 2; h++) for (int t = 0; t < 4; t++) mark(q6_ql(h, r, t), 16);
-                for (int t = 0; t < 4; t++) mark(q6_qh(r, t), 16);
+                mark_bytes(q6_d(r), 2);
+                mark_bytes(q6_sc(r), 16);
+                for (int e = 0; e < 256; e++) {
+                    mark_bits(q6_lo_byte(r, e), q6_lo_shift(e), 4);
+                    mark_bits(q6_hi_byte(r, e), q6_hi_shift(e), 2);
+                }
             } else {
-                mark(q8_d(r), 16);
-                for (int q = 0; q < 4; q++) for (int t = 0; t < 4; t++) mark(q8_qs(q, r, t), 16);
+                mark_bytes(q8_d(r), 16);
+                for (int e = 0; e < 256; e++) mark_bytes(q8_qs_byte(r, e), 1);
             }
         }
-        for (int i = 0; i < nb; i++) CHECK(cov[i] == 1);
-        CHECK(nb == 16 * (T == 8 ? 8 * 34 : raw_block_bytes(T)));
-        CHECK(nb % 16 == 0);
+        for (int i = 0; i < nb * 8; i++) CHECK(cov[i] == 1);
+    }
+
+    // what the GEMV reads for (step s, lane quad t, slot) of row r is element elem(type, s, t, slot)
+    for (int r = 0; r < 16; r++) for (int s = 0; s < 16; s++) for (int t = 0; t < 4; t++) for (int sl = 0; sl < 4; sl++) {
+        // Q4_K / Q5_K: word s % 8 of lane t's qs stream, nibble s >= 8, stored position of the slot
+        const int e = elem(12, s, t, sl), w = s & 7;
+        for (int q5 = 0; q5 < 2; q5++) {
+            const int rawq = 32 * (e >> 6) + (e & 31);
+            CHECK(qk_qs_byte(q5, r, rawq) == qk_qs(q5, w >> 2, r, t) + 4 * (w & 3) + pos_of_slot(sl));
+            CHECK(((e & 63) >= 32) == (s >= 8));
+            CHECK((e >> 5) == 2 * t + (s >= 8));  // sub-block of the lane's scale
+        }
+        // Q5_K bit: word (slot >> 1), bit s (+16 for odd slots), rows g / g+8 in bytes 0-7 / 8-15
+        CHECK(q5_bit_byte(r, e) * 8 + q5_bit_shift(e) ==
+              (q5_qh(r & 7, t) + 8 * (r >> 3) + 4 * (sl >> 1)) * 8 + ((sl & 1) ? 16 : 0) + s);
+        // Q6_K: ql word q6_lo_word(s) (high nibble for steps with bit 2 set), qh word
+        // q6_hi_word(s) at bits 2 ((s >> 1) & 3) of the slot's byte; scale = step
+        const int e6 = elem(14, s, t, sl);
+        const int lw = q6_lo_word(s);
+        CHECK(q6_lo_byte(r, e6) == q6_ql(lw >> 2, r, t) + 4 * (lw & 3) + pos_of_slot(sl));
+        CHECK(q6_lo_shift(e6) == (((s >> 2) & 1) ? 4 : 0));
+        CHECK(q6_hi_byte(r, e6) == q6_qh(r, t) + 4 * q6_hi_word(s) + pos_of_slot(sl));
+        CHECK(q6_hi_shift(e6) == 2 * ((s >> 1) & 3));
+        CHECK((e6 >> 4) == s);
+        // Q8_0: word s of the 64-byte stream, block s / 2
+        const int e8 = elem(8, s, t, sl);
+        CHECK(q8_qs_byte(r, e8) == q8_qs(s >> 2, r, t) + 4 * (s & 3) + pos_of_slot(sl));
+        CHECK((e8 >> 5) == (s >> 1));
+    }
+    // raw Q6_K parts: every (byte, bits) of ql / qh used once over the block
+    std::memset(cov, 0, sizeof cov);
+    for (int e = 0; e < 256; e++) {
+        mark_bits(q6_raw_lo_byte(e), q6_raw_lo_shift(e), 4);
+        mark_bits(q6_raw_hi_byte(e), q6_raw_hi_shift(e), 2);
+    }
+    for (int i = 0; i < 192 * 8; i++) CHECK(cov[i] == 1);
+    // 16-byte pieces of one (p, row) across the 32 lanes of a warp are consecutive
+    for (int g = 0; g < 8; g++) for (int t = 0; t < 4; t++) {
+        CHECK(qk_qs(false, 1, g, t) == qk_qs(false, 1, 0, 0) + 16 * (4 * g + t));
+        CHECK(q6_ql(0, g, t) == q6_ql(0, 0, 0) + 16 * (4 * g + t));
+        CHECK(q6_qh(g, t) == q6_qh(0, 0) + 16 * (4 * g + t));
+        CHECK(q8_qs(2, g, t) == q8_qs(2, 0, 0) + 16 * (4 * g + t));
+        CHECK(q5_qh(g, t) == q5_qh(0, 0) + 16 * (4 * g + t));
     }
     std::printf(fails ? "FAILED %d\n" : "OK\n", fails);
     return fails != 0;
