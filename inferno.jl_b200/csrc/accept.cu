@@ -457,6 +457,84 @@ __global__ void greedy_finish_kernel(const float *__restrict__ vmax, const int32
     accept_count[b] = acc;
 }
 
+// One launch for both steps: every CTA writes its chunk's (max, argmax),
+// then counts itself done on its sequence's counter; the CTA that finishes
+// last (the classic fenced-counter reduction, nothing waits) reads all
+// chunks in chunk order, decides, and returns the counter to zero for the
+// next launch.
+__global__ void __launch_bounds__(kNL) greedy_fused_kernel(const float *__restrict__ target, int V, int nch, int G,
+                                                           const int32_t *__restrict__ draft_tokens,
+                                                           float *vmax, int32_t *imax, unsigned *counter,
+                                                           int32_t *__restrict__ accept_count,
+                                                           int32_t *__restrict__ out_tokens) {
+    __shared__ float sv[kNL];
+    __shared__ int si[kNL];
+    __shared__ bool last;
+    const int c = blockIdx.x, r = blockIdx.y, b = r / (G + 1);
+    pdl_trigger();
+    pdl_wait();
+    const float *row = target + (int64_t)r * V;
+    float x[8];
+    const int n = load8(row, V, c, x);
+    float bv = -CUDART_INF_F;
+    int bi = INT_MAX;
+#pragma unroll
+    for (int q = 0; q < kPER; q++)
+        if (q < n && (x[q] > bv || bi == INT_MAX)) { bv = x[q]; bi = c * kCH + kPER * threadIdx.x + q; }
+    sv[threadIdx.x] = bv;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int off = kNL / 2; off; off >>= 1) {
+        if (threadIdx.x < off) {
+            float ov = sv[threadIdx.x + off];
+            int oi = si[threadIdx.x + off];
+            if (oi != INT_MAX && (si[threadIdx.x] == INT_MAX || ov > sv[threadIdx.x] ||
+                                  (ov == sv[threadIdx.x] && oi < si[threadIdx.x]))) {
+                sv[threadIdx.x] = ov;
+                si[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        vmax[(int64_t)r * nch + c] = sv[0];
+        imax[(int64_t)r * nch + c] = si[0];
+        __threadfence();
+        const unsigned done = atomicAdd(counter + b, 1u);
+        last = done == (unsigned)(nch * (G + 1) - 1);
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    int32_t *ot = out_tokens + (int64_t)b * (G + 1);
+    for (int i = 0; i <= G; i++) ot[i] = -1;
+    int acc = 0;
+    for (int i = 0; i <= G; i++) {
+        const int64_t rr = (int64_t)b * (G + 1) + i;
+        float best = __ldcg(vmax + rr * nch);
+        int arg = __ldcg(imax + rr * nch);
+        for (int cc = 1; cc < nch; cc++) {
+            const float v = __ldcg(vmax + rr * nch + cc);
+            if (v > best) { best = v; arg = __ldcg(imax + rr * nch + cc); }
+        }
+        ot[i] = arg;
+        if (i == G || arg != draft_tokens[b * G + i]) break;
+        acc++;
+    }
+    accept_count[b] = acc;
+    counter[b] = 0u;
+}
+
+cudaError_t accept_greedy_fused(const float *target, const int32_t *draft_tokens, int B, int G, int V,
+                                int32_t *accept_count, int32_t *out_tokens, void *scratch, unsigned *counter,
+                                cudaStream_t s) {
+    const int nch = (V + kCH - 1) / kCH;
+    float *vmax = (float *)scratch;
+    int32_t *imax = (int32_t *)((char *)scratch + (int64_t)B * (G + 1) * nch * 4);
+    return launch_k(greedy_fused_kernel, dim3(nch, B * (G + 1)), dim3(kNL), 0, s, target, V, nch, G, draft_tokens,
+                    vmax, imax, counter, accept_count, out_tokens);
+}
+
 int64_t accept_greedy_scratch_bytes(int B, int G, int V) {
     const int64_t nch = (V + kCH - 1) / kCH;
     return (int64_t)B * (G + 1) * nch * 8 + 256;

@@ -40,6 +40,9 @@ struct XForm {
     const float *w = nullptr;  // RMSNorm weights [cols]
     float eps = 0.f;
     int64_t ldx = 0;           // column stride of X in floats (0: the matrix's cols)
+    int ep = 0;                // 1: the rows are 16-row blocks of gate and up interleaved
+                               // (gate 0-15, up 0-15, gate 16-31, ...); Y gets silu(gate) * up,
+                               // rows/2 rows (not with accumulate)
 };
 // Y[ncols][rows] (+)= W * f(X), ncols <= 8 per call; X 16-byte aligned, ldx a multiple of 4
 cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
@@ -58,6 +61,11 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
                           int vocab, int32_t *accept_count, int32_t *out_tokens, void *scratch,
                           cudaStream_t s);
 int64_t accept_greedy_scratch_bytes(int batch, int gamma, int vocab);
+// the same in one launch; counter: one zero-initialised unsigned per sequence,
+// left at zero (not shared by launches that can overlap)
+cudaError_t accept_greedy_fused(const float *target, const int32_t *draft_tokens, int batch, int gamma, int vocab,
+                                int32_t *accept_count, int32_t *out_tokens, void *scratch, unsigned *counter,
+                                cudaStream_t s);
 
 }  // namespace ifr
 

@@ -8,6 +8,7 @@
 #include "../../include/inferno_b200.h"
 #include "common.cuh"
 #include "model.cuh"
+#include "dequant.cuh"
 
 #include <fcntl.h>
 #include <sys/mman.h>
@@ -190,6 +191,7 @@ float h2f_host(uint16_t h) {
 struct Proj {
     std::vector<ifr::QTensor> parts;
     int64_t rows = 0, cols = 0;
+    bool glu = false;  // gate/up 16-row blocks interleaved in one tensor (SwiGLU epilogue)
 };
 
 struct DevLayer {
@@ -303,6 +305,37 @@ int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &nam
     return IFR_OK;
 }
 
+// ffn_gate and ffn_up as one tensor with their 16-row blocks interleaved, so
+// that the GEMV can form silu(gate) * up in its epilogue; falls back to the
+// plain stack when the two differ in type or shape
+int upload_gate_up(ifr_model *m, const Gguf &g, const std::string &gate, const std::string &up, Proj *p) {
+    auto gi = g.t.find(gate), ui = g.t.find(up);
+    if (gi == g.t.end() || ui == g.t.end()) return upload_proj(m, g, {gate, up}, p);
+    const GTensor &tg = gi->second, &tu = ui->second;
+    if (tg.type != tu.type || tg.dims.size() != 2 || tu.dims.size() != 2 || tg.dims[0] != tu.dims[0] ||
+        tg.dims[1] != tu.dims[1] || tg.dims[1] % 16)
+        return upload_proj(m, g, {gate, up}, p);
+    const int64_t cols = (int64_t)tg.dims[0], rows = (int64_t)tg.dims[1];
+    const int64_t nb = tensor_bytes(tg.type, tg.nel());
+    if (nb < 0) return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: unsupported type %u", gate.c_str(), tg.type);
+    const int64_t rb = nb / rows;
+    std::vector<uint8_t> raw((size_t)nb * 2);
+    const uint8_t *pg = g.data(tg), *pu = g.data(tu);
+    for (int64_t b = 0; b < rows / 16; b++) {
+        memcpy(raw.data() + (2 * b) * 16 * rb, pg + b * 16 * rb, (size_t)(16 * rb));
+        memcpy(raw.data() + (2 * b + 1) * 16 * rb, pu + b * 16 * rb, (size_t)(16 * rb));
+    }
+    ifr::QTensor q{};
+    int rc = ifr_upload_raw(m->ctx, (int)tg.type, raw.data(), 2 * rows, cols, &q);
+    if (rc) return rc;
+    m->dev_allocs.push_back(q.data);
+    p->parts.assign(1, q);
+    p->rows = 2 * rows;
+    p->cols = cols;
+    p->glu = true;
+    return IFR_OK;
+}
+
 int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L) {
     const ifr_model_info &c = m->info;
     int rc;
@@ -327,7 +360,7 @@ int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L)
         if (L.proj.rows != (int64_t)(2 * c.n_head + 2 * c.n_kv_head) * c.head_dim)
             return ifr_fail(IFR_ERR_ARG, "%s: attention projection shapes do not match the config", pre.c_str());
     }
-    if ((rc = upload_proj(m, g, {pre + "ffn_gate.weight", pre + "ffn_up.weight"}, &L.gate_up))) return rc;
+    if ((rc = upload_gate_up(m, g, pre + "ffn_gate.weight", pre + "ffn_up.weight", &L.gate_up))) return rc;
     if ((rc = upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down))) return rc;
     return IFR_OK;
 }
@@ -351,7 +384,8 @@ struct ifr_state {
     int32_t *vtok = nullptr, *acc = nullptr, *outtok = nullptr, *log = nullptr, *mtp_pos = nullptr;
     int32_t *h_tok = nullptr;           // pinned staging
     float *x, *xn, *proj, *y, *gu, *hmid, *hid, *logits;
-    float *mtp_h, *mtp_e, *mtp_cat, *mtp_x, *mtp_xn;
+    float *mtp_h, *mtp_cat;
+    unsigned *gcount = nullptr;         // fused argmax/accept: per-launch completion counter (returns to 0)
     float *rope_cos, *rope_sin;
     std::vector<float *> S, hist, rq, rkv;      // per layer (SSM) else null
     std::vector<float *> kc, vc;                // per layer (attention) else null
@@ -416,11 +450,13 @@ struct ProfScope {
 
 int64_t proj_bytes(const Proj &p);
 
-int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st) {
+int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st,
+         const ifr::XForm &xf = ifr::XForm()) {
     ProfScope ps(s, cat, proj_bytes(p), st);
     int64_t r0 = 0;
+    const int64_t ldy = xf.ep ? p.rows / 2 : p.rows;
     for (auto &q : p.parts) {
-        ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, p.rows, st), "qgemm");
+        ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, ldy, st, xf), "qgemm");
         r0 += q.rows;
         if (s) s->launches++;
     }
@@ -435,8 +471,10 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     const int d = c.hidden;
     const int gcat = draft ? CAT_DRAFT_GEMV : CAT_LAYER_GEMV;
     int rc;
+    // RMSNorm kernels feed the input GEMVs (fusing the norm into every GEMV CTA
+    // costs each of them a full reduction over the input, more than the launch)
     ifr::rmsnorm(s->x, L.attn_norm, s->xn, n, d, c.rms_eps, d, d, st);
-    s->launches += 4;  // two norms, the SSM/attention step, SwiGLU
+    s->launches += 3;  // two norms, the SSM / attention step
     if ((rc = gemv(s, gcat, L.proj, s->xn, n, s->proj, false, st))) return rc;
     if (L.ssm) {
         ProfScope ps(s, CAT_SSM, 0, st);
@@ -487,18 +525,126 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     }
     if ((rc = gemv(s, gcat, L.out, s->y, n, s->x, true, st))) return rc;
     ifr::rmsnorm(s->x, L.post_norm, s->xn, n, d, c.rms_eps, d, d, st);
+    if (L.gate_up.glu) {
+        // silu(gate) * up formed in the gate/up GEMV's epilogue
+        ifr::XForm glu;
+        glu.ep = 1;
+        if ((rc = gemv(s, gcat, L.gate_up, s->xn, n, s->hmid, false, st, glu))) return rc;
+        return gemv(s, gcat, L.down, s->hmid, n, s->x, true, st);
+    }
     if ((rc = gemv(s, gcat, L.gate_up, s->xn, n, s->gu, false, st))) return rc;
-    ifr::swiglu(s->gu, s->hmid, n, c.ffn, st);
-    return gemv(s, gcat, L.down, s->hmid, n, s->x, true, st);
+    // silu(gate) * up formed while the down GEMV reads [gate | up]
+    ifr::XForm swiglu;
+    swiglu.kind = 2;
+    swiglu.ldx = 2 * (int64_t)c.ffn;
+    return gemv(s, gcat, L.down, s->gu, n, s->x, true, st, swiglu);
+}
+
+// embedding rows of the n verify tokens: token 0 from the state's last
+// emitted token when `first` is set (and written to vtok[0]), the others from
+// vtok; one thread per 32-element group (get_embedding, ModelCPU.jl:1005-1007)
+template <int T>
+__global__ void embed_kernel(const uint8_t *__restrict__ w, int64_t nu, int64_t nb_raw, int64_t rows, int64_t cols,
+                             int32_t *vtok, const int32_t *first, int n, float *__restrict__ out) {
+    ifr::pdl_trigger();
+    ifr::pdl_wait();
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n * nu * 8) return;
+    const int sub = (int)(i & 7);
+    const int64_t u = (i >> 3) % nu;
+    const int t = (int)((i >> 3) / nu);
+    int64_t tok = (t == 0 && first) ? *first : vtok[t];
+    if (i == 0 && first) vtok[0] = (int32_t)tok;
+    tok = tok < 0 ? 0 : (tok >= rows ? rows - 1 : tok);
+    ifr::dequant_group<T>(w, nu, nb_raw, tok, u, sub, out + t * cols + u * 256 + 32 * sub);
+}
+
+__device__ float block_sum_256(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+    for (int w = 0; w < 8; w++) r += red[w];
+    return r;
+}
+
+// MTP input of one draft (mtp_forward!, ModelCPU.jl:2031-2051):
+// cat = [RMSNorm(embed(tok), norm_e); RMSNorm(h, norm_h)], and the draft's
+// position pos + add for the MTP attention layer
+template <int T>
+__global__ void __launch_bounds__(256) mtp_prep_kernel(const uint8_t *__restrict__ w, int64_t nu, int64_t nb_raw,
+                                                       int64_t rows, const int32_t *tok, const float *h,
+                                                       const float *__restrict__ we, const float *__restrict__ wh,
+                                                       float eps, int d, float *__restrict__ cat, int32_t *pos_out,
+                                                       const ifr::EngineScalars *sc, int add) {
+    extern __shared__ float e_s[];  // nu * 256 floats
+    __shared__ float red[8];
+    ifr::pdl_trigger();
+    ifr::pdl_wait();
+    int64_t t = *tok;
+    t = t < 0 ? 0 : (t >= rows ? rows - 1 : t);
+    for (int gi = threadIdx.x; gi < nu * 8; gi += 256) ifr::dequant_group<T>(w, nu, nb_raw, t, gi >> 3, gi & 7, e_s + 32 * gi);
+    __syncthreads();
+    float se = 0.f, sh = 0.f;
+    for (int i = threadIdx.x; i < d; i += 256) {
+        se += e_s[i] * e_s[i];
+        sh += h[i] * h[i];
+    }
+    se = block_sum_256(se, red);
+    sh = block_sum_256(sh, red);
+    const float ie = 1.0f / sqrtf(se / (float)d + eps), ih = 1.0f / sqrtf(sh / (float)d + eps);
+    for (int i = threadIdx.x; i < d; i += 256) {
+        cat[i] = e_s[i] * ie * we[i];
+        cat[d + i] = h[i] * ih * wh[i];
+    }
+    if (threadIdx.x == 0) *pos_out = sc->pos + add;
+}
+
+template <int T>
+cudaError_t launch_embed_t(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int n, float *out, cudaStream_t st) {
+    const int64_t tot = (int64_t)n * e.nu * 8;
+    return ifr::launch_k(embed_kernel<T>, dim3((unsigned)((tot + 127) / 128)), dim3(128), 0, st, (const uint8_t *)e.data,
+                         (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, (int64_t)e.cols, vtok, first, n, out);
+}
+cudaError_t launch_embed(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int n, float *out, cudaStream_t st) {
+    switch (e.type) {
+    case 12: return launch_embed_t<12>(e, vtok, first, n, out, st);
+    case 13: return launch_embed_t<13>(e, vtok, first, n, out, st);
+    case 14: return launch_embed_t<14>(e, vtok, first, n, out, st);
+    case 8: return launch_embed_t<8>(e, vtok, first, n, out, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int T>
+cudaError_t launch_mtp_prep_t(const ifr::QTensor &e, const int32_t *tok, const float *h, const float *we,
+                              const float *wh, float eps, int d, float *cat, int32_t *pos_out,
+                              const ifr::EngineScalars *sc, int add, cudaStream_t st) {
+    return ifr::launch_k(mtp_prep_kernel<T>, dim3(1), dim3(256), (size_t)e.nu * 256 * 4, st, (const uint8_t *)e.data,
+                         (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, tok, h, we, wh, eps, d, cat, pos_out, sc, add);
+}
+cudaError_t launch_mtp_prep(const ifr::QTensor &e, const int32_t *tok, const float *h, const float *we,
+                            const float *wh, float eps, int d, float *cat, int32_t *pos_out,
+                            const ifr::EngineScalars *sc, int add, cudaStream_t st) {
+    switch (e.type) {
+    case 12: return launch_mtp_prep_t<12>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
+    case 13: return launch_mtp_prep_t<13>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
+    case 14: return launch_mtp_prep_t<14>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
+    case 8: return launch_mtp_prep_t<8>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
+    }
+    return cudaErrorInvalidValue;
 }
 
 // target forward of the n tokens in s->vtok at positions pos.. (device);
 // final-normed hidden of every column in s->hid; logits of columns
 // [logit_from, n) in s->logits (none if logit_from >= n)
-int target_forward(ifr_state *s, int n, int logit_from, cudaStream_t st) {
+int target_forward(ifr_state *s, int n, int logit_from, bool first_from_state, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
-    ECHECK(ifr::dequant_rows(m->embed.parts[0], s->vtok, n, s->x, st), "embedding");
+    ECHECK(launch_embed(m->embed.parts[0], s->vtok, first_from_state ? &s->sc->last_token : nullptr, n, s->x, st),
+           "embedding");
     s->launches += 2;  // embedding, final norm
     for (int li = 0; li < c.n_layers; li++) {
         int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, false, st);
@@ -535,23 +681,27 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
     const int d = c.hidden;
+    ifr::XForm norm_out;  // the MTP head's final norm, applied inside the lm_head GEMV
+    norm_out.kind = 1;
+    norm_out.w = m->mtp_norm;
+    norm_out.eps = c.rms_eps;
     for (int j = 1; j <= gamma; j++) {
         const int32_t *tok = j == 1 ? &s->sc->last_token : s->vtok + (j - 1);
         // the previous draft's layer output stays in s->x until the fc GEMV below
-        // overwrites it, after this step's norms have read it
+        // overwrites it, after the prep kernel has read it
         const float *hin = j == 1 ? s->mtp_h : s->x;
-        ECHECK(ifr::dequant_rows(m->embed.parts[0], tok, 1, s->mtp_e, st), "mtp embedding");
-        ifr::rmsnorm(s->mtp_e, m->mtp_norm_e, s->mtp_cat, 1, d, c.rms_eps, d, d, st);
-        ifr::rmsnorm(hin, m->mtp_norm_h, s->mtp_cat + d, 1, d, c.rms_eps, d, d, st);
+        ECHECK(launch_mtp_prep(m->embed.parts[0], tok, hin, m->mtp_norm_e, m->mtp_norm_h, c.rms_eps, d, s->mtp_cat,
+                               s->mtp_pos, s->sc, j - 1, st),
+               "mtp prep");
         int rc = gemv(s, CAT_DRAFT_GEMV, m->mtp_fc, s->mtp_cat, 1, s->x, false, st);
         if (rc) return rc;
-        ECHECK(ifr::launch_k(set_pos_kernel, dim3(1), dim3(1), 0, st, s->mtp_pos, (const ifr::EngineScalars *)s->sc, j - 1), "set_pos");
         if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, true, st))) return rc;
-        ifr::rmsnorm(s->x, m->mtp_norm, s->mtp_xn, 1, d, c.rms_eps, d, d, st);
-        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->mtp_xn, 1, s->logits, false, st))) return rc;
-        ECHECK(ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st), "draft argmax");
-        ifr::set_token(s->vtok + j, s->outtok, st);
-        s->launches += 9;  // embedding, 3 norms, set_pos, 2 argmax, set_token, (copy)
+        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->x, 1, s->logits, false, st, norm_out))) return rc;
+        // greedy draft token straight into the verify tokens
+        ECHECK(ifr::accept_greedy_fused(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->vtok + j, s->acc_scratch,
+                                        s->gcount, st),
+               "draft argmax");
+        s->launches += 2;  // prep, argmax
     }
     return IFR_OK;
 }
@@ -709,10 +859,8 @@ int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
     chk(dalloc(s, &s->hid, (size_t)N * d));
     chk(dalloc(s, &s->logits, (size_t)N * c.vocab));
     chk(dalloc(s, &s->mtp_h, d));
-    chk(dalloc(s, &s->mtp_e, d));
     chk(dalloc(s, &s->mtp_cat, 2 * d));
-    chk(dalloc(s, &s->mtp_x, d));
-    chk(dalloc(s, &s->mtp_xn, d));
+    chk(dalloc(s, &s->gcount, 4));
     const int half = c.rotary_dim / 2;
     chk(dalloc(s, &s->rope_cos, (size_t)max_ctx * half));
     chk(dalloc(s, &s->rope_sin, (size_t)max_ctx * half));
@@ -824,10 +972,11 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
         cudaError_t e = cudaMemcpyAsync(s->vtok, s->h_tok, sizeof(int32_t) * k, cudaMemcpyHostToDevice, st);
         if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "H2D prompt"); break; }
         const bool last = i0 + k == n;
-        rc = target_forward(s, k, last ? k - 1 : k, st);
+        rc = target_forward(s, k, last ? k - 1 : k, false, st);
         if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, st);
         if (!rc && last) {
-            e = ifr::accept_greedy(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
+            e = ifr::accept_greedy_fused(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch,
+                                         s->gcount, st);
             if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "argmax"); break; }
             e = ifr::launch_k(prefill_finish_kernel, dim3(1), dim3(256), 0, st, s->sc, (const int32_t *)s->outtok,
                               (const float *)(s->hid + (int64_t)(k - 1) * c.hidden), s->mtp_h, (int)c.hidden, s->log,
@@ -854,16 +1003,14 @@ int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st) {
     const ifr_model_info &c = s->m->info;
     int rc = IFR_OK;
     if (gamma > 0 && mtp) rc = mtp_draft(s, gamma, st);
+    if (!rc) rc = target_forward(s, gamma + 1, 0, true, st);
     if (!rc) {
-        ifr::set_token(s->vtok, &s->sc->last_token, st);
-        rc = target_forward(s, gamma + 1, 0, st);
-    }
-    if (!rc) {
-        cudaError_t e = ifr::accept_greedy(s->logits, s->vtok + 1, 1, gamma, c.vocab, s->acc, s->outtok, s->acc_scratch, st);
+        cudaError_t e = ifr::accept_greedy_fused(s->logits, s->vtok + 1, 1, gamma, c.vocab, s->acc, s->outtok,
+                                                 s->acc_scratch, s->gcount, st);
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "accept_greedy");
     }
     if (!rc) ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, st);
-    s->launches += 4;  // set_token, 2 accept, commit
+    s->launches += 2;  // accept, commit
     return rc;
 }
 }  // namespace
@@ -977,11 +1124,29 @@ int ifr_gemv_pass(ifr_state *s, int ncols) {
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(s->m->ctx));
     int rc = IFR_OK;
+    const ifr_model_info &c = s->m->info;
+    ifr::XForm norm;
+    norm.kind = 1;
+    norm.eps = c.rms_eps;
+    ifr::XForm swiglu;
+    swiglu.kind = 2;
+    swiglu.ldx = 2 * (int64_t)c.ffn;
+    // the verify's GEMVs with their fused input transforms; outputs go to
+    // buffers a spec step rewrites before it reads them (proj, gu, hid): the
+    // caches, SSM states and residual stream are not changed
     for (auto &L : s->m->layers) {
         if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.proj, s->xn, ncols, s->proj, false, st);
-        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.out, s->y, ncols, s->gu, false, st);
-        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->gu, false, st);
-        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.down, s->hmid, ncols, s->hid, false, st);
+        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.out, s->y, ncols, s->hid, false, st);
+        norm.w = L.post_norm;
+        if (L.gate_up.glu) {
+            ifr::XForm glu;
+            glu.ep = 1;
+            if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->hmid, false, st, glu);
+            if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.down, s->hmid, ncols, s->hid, false, st);
+        } else {
+            if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->gu, false, st);
+            if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.down, s->gu, ncols, s->hid, false, st, swiglu);
+        }
     }
     if (!rc) rc = gemv(s, CAT_LM_HEAD, s->m->lm_head, s->hid, ncols, s->logits, false, st);
     cudaSetDevice(prev);

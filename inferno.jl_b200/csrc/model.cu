@@ -117,45 +117,84 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     __shared__ float ab[2][kMaxN];
     __shared__ float ys[kMaxN][RPC];
     __shared__ float ssq[kMaxN];
+    __shared__ float red_n[8][2 * kMaxN];
     pdl_trigger();
     pdl_wait();
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
 
-    // 1. conv of the owned channels: committed history + replayed + new tokens
+    // 1. conv of the owned channels over the window: committed history (K-1),
+    //    replayed tokens (r), new tokens (N).  Element i of the window is read
+    //    straight from where it lives, so all loads are independent.
+    auto win = [&](int i, int ch) -> const float * {
+        if (i < K - 1) return a.hist + (int64_t)i * C + ch;
+        if (i < K - 1 + r) return a.rq + (int64_t)(i - K + 1) * C + ch;
+        return a.proj + (int64_t)(i - K + 1 - r) * a.ldp + ch;
+    };
     for (int lc = tid; lc < 3 * RPC; lc += 256) {
         const int part = lc / RPC, i = lc % RPC;
         const int ch = part * qk + h * HD + r0 + i;
-        float seq[3 + kMaxN + kMaxN];  // old history (K-1) + replayed + new
-        int n = 0;
-        for (int j = 0; j < K - 1; j++) seq[n++] = a.hist[(int64_t)j * C + ch];
-        for (int j = 0; j < r; j++) seq[n++] = a.rq[(int64_t)j * C + ch];
-        // new committed history = last K-1 of (history + replayed)
-        for (int j = 0; j < K - 1; j++) a.hist[(int64_t)j * C + ch] = seq[n - (K - 1) + j];
-        const int base = n - (K - 1);
-        for (int t = 0; t < N; t++) {
-            const float v = a.proj[(int64_t)t * a.ldp + ch];
-            seq[n + t] = v;
-            a.rq[(int64_t)t * C + ch] = v;  // saved for the next call's replay
+        float w[4], tap[kMaxN][4], nh[3], pv[kMaxN];
+#pragma unroll
+        for (int k = 0; k < 4; k++) w[k] = k < K ? a.conv_w[(int64_t)ch * K + k] : 0.f;
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) {
+            pv[t] = t < N ? a.proj[(int64_t)t * a.ldp + ch] : 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) tap[t][k] = (t < N && k < K) ? *win(r + t + k, ch) : 0.f;
         }
-        const float *w = a.conv_w + (int64_t)ch * K;
-        for (int t = 0; t < N; t++) {
-            float acc = 0.f;
-            for (int k = 0; k < K; k++) acc += seq[base + t + k] * w[k];
-            const float o = acc / (1.0f + expf(-acc));
-            if (part == 0) cq[t][i] = o;
-            else if (part == 1) ck[t][i] = o;
-            else cv[t][i] = o;
+        // new committed history = last K-1 of (history + replayed)
+#pragma unroll
+        for (int j = 0; j < 3; j++) nh[j] = j < K - 1 ? *win(r + j, ch) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            if (j < K - 1) a.hist[(int64_t)j * C + ch] = nh[j];
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) {
+            if (t < N) {
+                a.rq[(int64_t)t * C + ch] = pv[t];  // saved for the next call's replay
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    if (k < K) acc += tap[t][k] * w[k];
+                const float o = acc / (1.0f + expf(-acc));
+                if (part == 0) cq[t][i] = o;
+                else if (part == 1) ck[t][i] = o;
+                else cv[t][i] = o;
+            }
         }
     }
-    // 2. alpha / beta projections of the new tokens (ssm_alpha/beta . x)
-    for (int item = warp; item < 2 * N; item += 8) {
-        const int which = item / N, t = item % N;
-        const float *w = a.ab_w + (int64_t)(which * a.H + h) * a.d;
-        const float *x = a.xn + (int64_t)t * a.d;
-        float s = 0.f;
-        for (int i = lane; i < a.d; i += 32) s += w[i] * x[i];
-        s = warp_sum(s);
-        if (lane == 0) ab[which][t] = s;
+    // 2. alpha / beta projections of the new tokens (ssm_alpha/beta . xn),
+    //    block-wide with all loads independent
+    {
+        float pa[kMaxN], pb[kMaxN];
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = 0.f;
+        const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
+        for (int i = tid; i < a.d; i += 256) {
+            const float al = wa[i], be = wb[i];
+#pragma unroll
+            for (int t = 0; t < kMaxN; t++)
+                if (t < N) {
+                    const float xn = a.xn[(int64_t)t * a.d + i];
+                    pa[t] += al * xn;
+                    pb[t] += be * xn;
+                }
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) {
+            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]);
+            if (lane == 0) {
+                red_n[warp][t] = va;
+                red_n[warp][kMaxN + t] = vb;
+            }
+        }
+        __syncthreads();
+        if (tid < 2 * N) {
+            const int which = tid / N, t = tid % N;
+            float v = 0.f;
+            for (int w8 = 0; w8 < 8; w8++) v += red_n[w8][which * kMaxN + t];
+            ab[which][t] = v;
+        }
     }
     // 3. the previous call's replay record: k (all dims), own v rows, decay, beta
     float *rec = a.rkv + (int64_t)h * kMaxN * REC;

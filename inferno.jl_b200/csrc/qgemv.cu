@@ -111,6 +111,7 @@ struct GemvArgs {
     int xf;            // activation transform: 0 none, 1 RMSNorm(xw, eps), 2 SwiGLU
     const float *xw;   // RMSNorm weights [K]
     float eps;
+    int ep;            // 1: SwiGLU epilogue over interleaved gate/up 16-row blocks
 };
 
 // ---- B fragments of one unit, built in registers ------------------------------
@@ -612,11 +613,26 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         }
         // the sweep's rows are final: write Y (coalesced over rows)
         const int64_t row0 = (int64_t)sw * MTG * 16;
-        for (int i = tid; i < sw_rows * a.ncols; i += kThreads) {
-            const int col = i / sw_rows, r = i % sw_rows;
-            if (row0 + r < a.M && !dead) {
-                float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
-                *y = a.accumulate ? *y + acc[r * 8 + col] : acc[r * 8 + col];
+        if (a.ep) {
+            // mlp_forward (ModelCPU.jl:482-508): h = silu(gate) * up; a sweep holds whole
+            // gate/up block pairs (MTG is even), local rows 32p.. gate, 32p+16.. up
+            const int half_rows = sw_rows / 2;
+            const int64_t j0 = row0 / 2;
+            for (int i = tid; i < half_rows * a.ncols; i += kThreads) {
+                const int col = i / half_rows, rr = i % half_rows;
+                const int gr = (rr >> 4) * 32 + (rr & 15);
+                if (j0 + rr < a.M / 2 && !dead) {
+                    const float gv = acc[gr * 8 + col], uv = acc[(gr + 16) * 8 + col];
+                    a.Y[(int64_t)col * a.ldy + j0 + rr] = gv / (1.0f + expf(-gv)) * uv;
+                }
+            }
+        } else {
+            for (int i = tid; i < sw_rows * a.ncols; i += kThreads) {
+                const int col = i / sw_rows, r = i % sw_rows;
+                if (row0 + r < a.M && !dead) {
+                    float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
+                    *y = a.accumulate ? *y + acc[r * 8 + col] : acc[r * 8 + col];
+                }
             }
         }
         consumer_bar();
@@ -671,7 +687,7 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
         attr_set = true;
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
-               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps};
+               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
     return launch_k(qgemv_kernel<FMT, NT, XF>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
 }
 
@@ -691,6 +707,7 @@ cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, b
                         cudaStream_t s, const XForm &xf) {
     if (ncols < 1 || ncols > 8) return cudaErrorInvalidValue;
     if (xf.kind < 0 || xf.kind > 2 || (xf.kind == 1 && !xf.w)) return cudaErrorInvalidValue;
+    if (xf.ep && (accumulate || T.rows % 32)) return cudaErrorInvalidValue;
     switch (T.type) {
     case 12: return launch_fmt<12>(T, X, ncols, Y, accumulate, ldy, s, xf);
     case 13: return launch_fmt<13>(T, X, ncols, Y, accumulate, ldy, s, xf);

@@ -6,6 +6,7 @@
 // form there), hence the explicit __fmul_rn/__fsub_rn.
 #include "common.cuh"
 #include "tiles.cuh"
+#include "dequant.cuh"
 
 namespace ifr {
 
@@ -95,19 +96,6 @@ cudaError_t repack(const QTensor &t, const uint8_t *raw, cudaStream_t s) {
 
 // --------------------------------------------------------------- dequant ----
 
-// src/Dequant.jl:345-362
-IFR_DEV void scale_min_k(int j, const uint8_t *s, uint32_t &sc, uint32_t &m) {
-    if (j < 4) {
-        sc = s[j] & 63;
-        m = s[j + 4] & 63;
-    } else {
-        sc = (s[j + 4] & 0x0f) | ((s[j - 4] >> 6) << 4);
-        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-    }
-}
-
-IFR_DEV float h2f_bytes(const uint8_t *p) { return h2f((uint16_t)(p[0] | (p[1] << 8))); }
-
 // one thread per (row, unit, 32-element sub-group); writes out[row][u*256 + ...]
 // (idx: optional row indices, e.g. token ids of an embedding gather; clamped
 // to the tensor's rows; output row i holds source row idx[i])
@@ -126,43 +114,7 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ w, float *__restrict_
         row = idx[orow];
         row = row < 0 ? 0 : (row >= src_rows ? src_rows - 1 : row);
     }
-    const int r = (int)(row & 15);
-    const uint8_t *tile = w + ((row >> 4) * nu + u) * mtile_bytes(T);
-    float *o = out + orow * cols + u * 256 + 32 * sub;
-    if (T == 12 || T == 13) {
-        // src/Dequant.jl:325-375 (Q4_K), :379-441 (Q5_K): element e = 32 sub + l is
-        // nibble (e % 64 >= 32) of raw qs byte 32 (e / 64) + e % 32
-        constexpr bool q5 = T == 13;
-        const uint8_t *hdr = tile + qk_hdr(r);
-        const float d = h2f_bytes(hdr), dmin = h2f_bytes(hdr + 2);
-        uint32_t sc, m;
-        scale_min_k(sub, hdr + 4, sc, m);
-        const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
-        const int hi = sub & 1;
-        for (int l = 0; l < 32; l++) {
-            const int e = 32 * sub + l;
-            const uint8_t v = tile[qk_qs_byte(q5, r, 32 * (e >> 6) + (e & 31))];
-            uint32_t q = hi ? (v >> 4) : (v & 0x0f);
-            if (q5 && ((tile[q5_bit_byte(r, e)] >> q5_bit_shift(e)) & 1)) q += 16;
-            o[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
-        }
-    } else if (T == 14) {
-        // src/Dequant.jl:558-601: (d * sc[e / 16]) * (q - 32)
-        const float d = h2f_bytes(tile + q6_d(r));
-        for (int l = 0; l < 32; l++) {
-            const int e = 32 * sub + l;
-            const float ds = __fmul_rn(d, (float)(int8_t)tile[q6_sc(r) + (e >> 4)]);
-            const int l4 = (tile[q6_lo_byte(r, e)] >> q6_lo_shift(e)) & 15;
-            const int h2 = (tile[q6_hi_byte(r, e)] >> q6_hi_shift(e)) & 3;
-            o[l] = __fmul_rn(ds, (float)((l4 | (h2 << 4)) - 32));
-        }
-    } else {
-        // Q8_0, src/Dequant.jl:304-321; block `sub` of the unit
-        const int64_t blk = 8 * u + sub;
-        if (blk >= nb_raw) return;
-        const float d = h2f_bytes(tile + q8_d(r) + 2 * sub);
-        for (int l = 0; l < 32; l++) o[l] = __fmul_rn(d, (float)(int8_t)tile[q8_qs_byte(r, 32 * sub + l)]);
-    }
+    dequant_group<T>(w, nu, nb_raw, row, u, sub, out + orow * cols + u * 256 + 32 * sub);
 }
 
 cudaError_t dequant_rows(const QTensor &t, const int32_t *idx, int64_t nrows, float *out, cudaStream_t s) {
