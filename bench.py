@@ -370,6 +370,7 @@ def run_spec(args):
     from inferno_b200.engine import Model, State
     G = args.gamma
     ctx = pkg.Context(local, torch_stream=False)  # own stream: capturable
+    ctx.set_activation(args.act)
     path = synth.cached(SPEC_PRESET, SPEC_SEED)
     model = Model(ctx, path)
     info = model.info
@@ -607,6 +608,8 @@ def main():
     ap.add_argument("--workload", default="spec", choices=["spec", "sweep"])
     ap.add_argument("--gamma", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--act", type=int, default=0, choices=[0, 1],
+                    help="K-quant GEMV activations: 0 = exact f32 (default), 1 = Q8_K (the reference's kernels)")
     ap.add_argument("--profile", choices=["spec", "qgemv"], help="small case for ncu (no JSON line)")
     ap.add_argument("--qtype", default="Q4_K")
     ap.add_argument("--shape", default="65536x4096")

@@ -63,6 +63,21 @@ int ifr_ctx_get_stream(ifr_ctx *ctx, void **cuda_stream);
  * (batch, gamma, vocab) so later calls allocate nothing (e.g. before CUDA
  * graph capture).  ifr_qgemm needs no scratch. */
 int ifr_ctx_reserve_accept(ifr_ctx *ctx, int batch, int gamma, int vocab);
+/* Activations of the K-quant (Q4_K/Q5_K/Q6_K) GEMVs:
+ *   IFR_ACT_EXACT (default)  f32 activations, split exactly into fp16 hi + lo
+ *                            on the fp16 tensor cores: the exact product with
+ *                            the dequantized weights, up to f32 summation;
+ *   IFR_ACT_Q8K              each 256-block of a column quantized as the
+ *                            reference's quantize_row_q8_K (src/kernels/
+ *                            quant_kernels.c:166-194; d = amax/127, roundf(x/d))
+ *                            and multiplied exactly on the integer tensor
+ *                            cores: the results of the reference's q4_k_gemv
+ *                            .. q6_k_gemv up to f32 summation order.
+ * Q8_0 GEMVs always use exact f32 activations (the reference's q8_0_gemv).
+ * The mode applies to ifr_qgemm and to the model engine of this context. */
+#define IFR_ACT_EXACT 0
+#define IFR_ACT_Q8K 1
+int ifr_ctx_set_activation(ifr_ctx *ctx, int mode);
 /* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
  * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);
@@ -85,11 +100,12 @@ int ifr_tensor_info(const ifr_tensor *t, int *type, int64_t *rows, int64_t *cols
 int ifr_dequant(ifr_ctx *ctx, const ifr_tensor *t, float *dev_out);
 
 /* Y = W * X for ncols verify columns (any ncols >= 1; passes of 8).
- * X must be 16-byte aligned.
- * f32 activations, exact fp16 hi/lo split on the tensor cores, f32
- * accumulation.  Replaces q4_k_gemv/q5_k_gemv/q6_k_gemv/q8_0_gemv
- * (src/kernels/quant_kernels.c:602-697), called once per column by the
- * reference (src/ModelCPU.jl:285-379). */
+ * X must be 16-byte aligned.  K-quants: int8 activations in the context's
+ * activation mode (ifr_ctx_set_activation) on the integer tensor cores, exact
+ * integer sub-block sums, f32 scaling and accumulation; Q8_0: f32 activations
+ * split exactly into fp16 hi + lo on the fp16 tensor cores.  Replaces
+ * q4_k_gemv/q5_k_gemv/q6_k_gemv/q8_0_gemv (src/kernels/quant_kernels.c:602-697),
+ * called once per column by the reference (src/ModelCPU.jl:285-379). */
 int ifr_qgemm(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
               float *Y_dev);
 

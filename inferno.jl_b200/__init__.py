@@ -101,6 +101,13 @@ class Context:
         except Exception:
             pass
 
+    ACT_EXACT, ACT_Q8K = 0, 1
+
+    def set_activation(self, mode):
+        """K-quant GEMV activations: ACT_EXACT (default, exact f32) or ACT_Q8K
+        (Q8_K-quantised, the reference's kernels)"""
+        check(load().ifr_ctx_set_activation(self.handle, int(mode)))
+
     def set_stream(self, stream):
         check(load().ifr_ctx_set_stream(self.handle, ctypes.c_void_p(stream.cuda_stream)))
 

@@ -37,6 +37,7 @@ SIGNATURES = {
     "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
     "ifr_quantize": (_i, [_i, _vp, _i64, _i64, _vp]),
     "ifr_accept": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
+    "ifr_ctx_set_activation": (_i, [_vp, _i]),
     "ifr_accept_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
     "ifr_accept_greedy": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "ifr_model_load_gguf": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),

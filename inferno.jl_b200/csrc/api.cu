@@ -49,6 +49,7 @@ struct ifr_ctx {
     cudaStream_t stream = nullptr;
     void *scratch = nullptr;
     size_t scratch_cap = 0;
+    int act = IFR_ACT_EXACT;       // K-quant activation mode of the GEMVs
     std::atomic<int> refs{0};      // live models built on this context
     std::atomic<bool> closing{false};
 };
@@ -126,6 +127,7 @@ bool pdl_enabled() {
 }  // namespace ifr
 
 int ifr_ctx_device(const ifr_ctx *c) { return c->device; }
+int ifr_ctx_activation(const ifr_ctx *c) { return c->act; }
 static void ctx_destroy_now(ifr_ctx *c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
@@ -186,6 +188,14 @@ int ifr_ctx_destroy(ifr_ctx *c) {
     if (!c) return IFR_OK;
     c->closing = true;
     if (c->refs.load() == 0) ctx_destroy_now(c);
+    return IFR_OK;
+}
+
+int ifr_ctx_set_activation(ifr_ctx *c, int mode) {
+    if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
+    if (mode != IFR_ACT_EXACT && mode != IFR_ACT_Q8K)
+        return fail(IFR_ERR_ARG, "activation mode must be IFR_ACT_EXACT (0) or IFR_ACT_Q8K (1), got %d", mode);
+    c->act = mode;
     return IFR_OK;
 }
 
@@ -297,7 +307,10 @@ int ifr_qgemm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float 
     DeviceGuard g(c->device);
     for (int n0 = 0; n0 < ncols; n0 += IFR_MAX_VERIFY_COLS) {
         int n = ncols - n0 < IFR_MAX_VERIFY_COLS ? ncols - n0 : IFR_MAX_VERIFY_COLS;
-        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, false, W->q.rows, c->stream),
+        ifr::XForm xf;
+        xf.act = c->act;
+        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, false,
+                                        W->q.rows, c->stream, xf),
                        "qgemm launch");
     }
     return IFR_OK;
@@ -366,6 +379,7 @@ int legacy_gemv(int type, const uint8_t *weight, const float *x, float *out, int
     if (!g_legacy_ctx) {
         int rc = ifr_ctx_create(0, &g_legacy_ctx);
         if (rc) return rc;
+        g_legacy_ctx->act = IFR_ACT_Q8K;  // the reference kernels' own activation rounding
     }
     ifr_ctx *c = g_legacy_ctx;
     DeviceGuard g(c->device);

@@ -40,6 +40,8 @@ struct XForm {
     const float *w = nullptr;  // RMSNorm weights [cols]
     float eps = 0.f;
     int64_t ldx = 0;           // column stride of X in floats (0: the matrix's cols)
+    int act = 0;               // K-quant activations: 0 = exact f32 (fp16 hi + lo),
+                               // 1 = Q8_K (the reference's kernels, integer tensor cores)
     int ep = 0;                // 1: the rows are 16-row blocks of gate and up interleaved
                                // (gate 0-15, up 0-15, gate 16-31, ...); Y gets silu(gate) * up,
                                // rows/2 rows (not with accumulate)
@@ -115,6 +117,25 @@ IFR_DEV void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, ui
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// D = A(16x32 s8) * B(32x8 s8), s32 (C = 0)
+IFR_DEV void imma16832_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                         uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// D = A(16x16 s8) * B(16x8 s8), s32 (C = 0)
+IFR_DEV void imma16816_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 
 // D = A(16x8 f16) * B(8x8 f16) + C, f32 accumulate

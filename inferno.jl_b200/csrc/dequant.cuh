@@ -30,7 +30,7 @@ IFR_DEV void dequant_group(const uint8_t *__restrict__ w, int64_t nu, int64_t nb
     const uint8_t *tile = w + ((row >> 4) * nu + u) * mtile_bytes(T);
     if (T == 12 || T == 13) {
         // src/Dequant.jl:325-375 (Q4_K), :379-441 (Q5_K): element e = 32 sub + l is
-        // nibble (e % 64 >= 32) of raw qs byte 32 (e / 64) + e % 32
+        // nibble (e % 64 >= 32) of raw qs byte 32 (e / 64) + e % 32, Q5_K bit sub of qh byte l
         constexpr bool q5 = T == 13;
         const uint8_t *hdr = tile + qk_hdr(r);
         const float d = h2f_bytes(hdr), dmin = h2f_bytes(hdr + 2);
@@ -42,7 +42,7 @@ IFR_DEV void dequant_group(const uint8_t *__restrict__ w, int64_t nu, int64_t nb
             const int e = 32 * sub + l;
             const uint8_t v = tile[qk_qs_byte(q5, r, 32 * (e >> 6) + (e & 31))];
             uint32_t q = hi ? (v >> 4) : (v & 0x0f);
-            if (q5 && ((tile[q5_bit_byte(r, e)] >> q5_bit_shift(e)) & 1)) q += 16;
+            if (q5 && ((tile[q5_qh_byte(r, l)] >> sub) & 1)) q += 16;
             o[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
         }
     } else if (T == 14) {
@@ -51,8 +51,8 @@ IFR_DEV void dequant_group(const uint8_t *__restrict__ w, int64_t nu, int64_t nb
         for (int l = 0; l < 32; l++) {
             const int e = 32 * sub + l;
             const float ds = __fmul_rn(d, (float)(int8_t)tile[q6_sc(r) + (e >> 4)]);
-            const int l4 = (tile[q6_lo_byte(r, e)] >> q6_lo_shift(e)) & 15;
-            const int h2 = (tile[q6_hi_byte(r, e)] >> q6_hi_shift(e)) & 3;
+            const int l4 = (tile[q6_ql_byte(r, q6_raw_lo_byte(e))] >> q6_raw_lo_shift(e)) & 15;
+            const int h2 = (tile[q6_qh_byte(r, q6_raw_hi_byte(e) - 128)] >> q6_raw_hi_shift(e)) & 3;
             o[l] = __fmul_rn(ds, (float)((l4 | (h2 << 4)) - 32));
         }
     } else {

@@ -28,6 +28,7 @@
 int ifr_fail(int code, const char *fmt, ...);
 int ifr_cuda_fail(cudaError_t e, const char *what);
 int ifr_ctx_device(const ifr_ctx *c);
+int ifr_ctx_activation(const ifr_ctx *c);
 void ifr_ctx_retain(ifr_ctx *c);
 void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
@@ -204,6 +205,8 @@ struct DevLayer {
 
 struct ifr_model {
     ifr_ctx *ctx = nullptr;
+    int states = 0;          // live states built on this model
+    bool closing = false;    // ifr_model_free called while states were alive
     ifr_model_info info{};
     int conv_channels = 0, inner = 0;
     std::vector<DevLayer> layers;
@@ -455,8 +458,10 @@ int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, 
     ProfScope ps(s, cat, proj_bytes(p), st);
     int64_t r0 = 0;
     const int64_t ldy = xf.ep ? p.rows / 2 : p.rows;
+    ifr::XForm f = xf;
+    f.act = ifr_ctx_activation(s->m->ctx);
     for (auto &q : p.parts) {
-        ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, ldy, st, xf), "qgemm");
+        ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, ldy, st, f), "qgemm");
         r0 += q.rows;
         if (s) s->launches++;
     }
@@ -808,8 +813,7 @@ int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out) {
     return IFR_OK;
 }
 
-int ifr_model_free(ifr_model *m) {
-    if (!m) return IFR_OK;
+static int model_destroy(ifr_model *m) {
     int prev = 0;
     cudaGetDevice(&prev);
     ifr_ctx *c = m->ctx;
@@ -818,6 +822,14 @@ int ifr_model_free(ifr_model *m) {
     cudaSetDevice(prev);
     ifr_ctx_release(c);
     return IFR_OK;
+}
+
+// a model outlives the states built on it: freeing it while states are alive
+// only marks it, and the last ifr_state_free completes the destruction
+int ifr_model_free(ifr_model *m) {
+    if (!m) return IFR_OK;
+    m->closing = true;
+    return m->states == 0 ? model_destroy(m) : IFR_OK;
 }
 
 int ifr_model_get_info(const ifr_model *m, ifr_model_info *info) {
@@ -923,6 +935,7 @@ int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
         delete s;
         return rc;
     }
+    m->states++;
     *out = s;
     return IFR_OK;
 }
@@ -933,8 +946,10 @@ int ifr_state_free(ifr_state *s) {
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(s->m->ctx));
     cudaStreamSynchronize(ifr_ctx_stream_of(s->m->ctx));
+    ifr_model *m = s->m;
     delete s;
     cudaSetDevice(prev);
+    if (--m->states == 0 && m->closing) return model_destroy(m);
     return IFR_OK;
 }
 

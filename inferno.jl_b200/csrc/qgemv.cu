@@ -31,6 +31,8 @@
 #include "common.cuh"
 #include "tiles.cuh"
 
+#include <type_traits>
+
 namespace ifr {
 
 __device__ int g_dev_error = 0;
@@ -114,17 +116,18 @@ struct GemvArgs {
     int ep;            // 1: SwiGLU epilogue over interleaved gate/up 16-row blocks
 };
 
-// ---- B fragments of one unit, built in registers ------------------------------
+// ---- exact f32 activations on the fp16 tensor cores ----------------------------
 // Lane (g, t) feeds B column g of every step: activation column 4 nt + g/2,
 // its fp16 high part (g even) or low part (g odd), for the elements
-// 64t .. 64t+63 of the unit (tiles.cuh).  The two lanes of a pair (g, g^1)
-// load 32 elements each, split them into (hi, lo) and swap halves by one
-// shuffle per register.  Activations are scaled by a power of two per unit
-// (exact) so that hi + lo carries ~22 bits; es undoes it on the f32 sums.
+// 16 s + 4t + {0..3} of step s (tiles.cuh), slots (0, 1) = elements (0, 2) and
+// slots (2, 3) = elements (1, 3).  The two lanes of a pair (g, g^1) load half
+// the steps each, split them into (hi, lo) and swap halves by one shuffle per
+// register.  Activations are scaled by a power of two per unit (exact) so that
+// hi + lo carries ~22 bits; es undoes it on the f32 sums.
 template <int NT>
 struct BFrag {
     uint32_t b[16][NT][2];  // per step: slots (0,1), (2,3)
-    uint32_t m[NT];         // min-MMA B fragment: sub-block sums (Q4_K/Q5_K)
+    uint32_t m[NT];         // Q4_K/Q5_K min MMA: sums of sub-blocks 2t, 2t+1 (x 2^-5)
     float es[NT];           // 2^-e of the unit for C column 4*nt + t
 };
 
@@ -149,8 +152,7 @@ __device__ __noinline__ float load_x1(const GemvArgs &a, const float *xc, float 
 // 8 runs of 4 activations of column col at k0 + i * step (transform XF
 // applied; 0 beyond K or for absent columns)
 template <int XF>
-IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, int step, bool has,
-                      float (&v)[32]) {
+IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, int step, bool has, float *v) {
     const float *xc = a.X + (int64_t)col * a.ldx;
     const float iv = XF == 1 && has ? inv[col] : 0.f;
 #pragma unroll
@@ -189,11 +191,9 @@ IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, B
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int col = 4 * nt + (g >> 1);
-        // this lane's steps 8 part .. 8 part + 7 (elem() of tiles.cuh)
-        constexpr bool kq = FMT == 12 || FMT == 13;
+        // this lane's steps 8 part .. 8 part + 7 (elem_s() of tiles.cuh)
         float v[32];
-        load_x32<XF>(a, inv, col, kq ? u * 256 + 64 * t + 32 * part : u * 256 + 128 * part + 4 * t, kq ? 4 : 16,
-                 col < a.ncols, v);
+        load_x32<XF>(a, inv, col, u * 256 + 128 * part + 4 * t, 16, col < a.ncols, v);
         float mx = 0.f;
 #pragma unroll
         for (int r = 0; r < 32; r++) mx = fmaxf(mx, fabsf(v[r]));
@@ -203,23 +203,23 @@ IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, B
         const int ex = unit_exp(mx);
         const float scl = pow2i(ex);
         F.es[nt] = __shfl_sync(0xffffffffu, pow2i(-ex), 8 * t);
-        float S = 0.f;
         uint32_t keep[8][2], send[8][2];
+        float cs[4] = {0.f, 0.f, 0.f, 0.f};  // this lane's part of chunks 4 part .. 4 part + 3
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             float x[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 x[j] = v[4 * i + j] * scl;  // exact
-                S += x[j];
+                cs[i >> 1] += x[j];
             }
-            const uint32_t h01 = cvt_h2(x[1], x[0]), h23 = cvt_h2(x[3], x[2]);
-            const uint32_t l01 = cvt_h2(x[1] - h2_hi(h01), x[0] - h2_lo(h01));
-            const uint32_t l23 = cvt_h2(x[3] - h2_hi(h23), x[2] - h2_lo(h23));
-            keep[i][0] = part ? l01 : h01;
-            keep[i][1] = part ? l23 : h23;
-            send[i][0] = part ? h01 : l01;
-            send[i][1] = part ? h23 : l23;
+            const uint32_t h02 = cvt_h2(x[2], x[0]), h13 = cvt_h2(x[3], x[1]);
+            const uint32_t l02 = cvt_h2(x[2] - h2_hi(h02), x[0] - h2_lo(h02));
+            const uint32_t l13 = cvt_h2(x[3] - h2_hi(h13), x[1] - h2_lo(h13));
+            keep[i][0] = part ? l02 : h02;
+            keep[i][1] = part ? l13 : h13;
+            send[i][0] = part ? h02 : l02;
+            send[i][1] = part ? h13 : l13;
         }
 #pragma unroll
         for (int i = 0; i < 8; i++) {
@@ -231,120 +231,138 @@ IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, B
             }
         }
         if (FMT == 12 || FMT == 13) {
-            // sums of sub-blocks 2t (part 0) and 2t+1 (part 1), x 2^-5 to stay in fp16 range
-            const float Sm = S * 0.03125f;
-            const uint32_t hs = cvt_h2(0.f, Sm);
-            const uint32_t ls = cvt_h2(0.f, Sm - h2_lo(hs));
-            const uint32_t r = __shfl_xor_sync(0xffffffffu, part ? hs : ls, 4) & 0xffffu;
-            F.m[nt] = part ? (r | (ls << 16)) : ((hs & 0xffffu) | (r << 16));
+            // sub-block (= chunk) sums of column col: over the lane quad, then the partner
+            // lane's four chunks; lane (g, t) takes chunks 2t, 2t+1, its hi or lo part
+            float S[8];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float v2 = cs[k];
+                v2 += __shfl_xor_sync(0xffffffffu, v2, 1);
+                v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
+                const float o = __shfl_xor_sync(0xffffffffu, v2, 4);
+                S[k] = part ? o : v2;
+                S[4 + k] = part ? v2 : o;
+            }
+            float sa = S[0], sb = S[1];
+#pragma unroll
+            for (int k = 1; k < 4; k++)
+                if (t == k) {
+                    sa = S[2 * k];
+                    sb = S[2 * k + 1];
+                }
+            sa *= 0.03125f;  // x 2^-5 keeps the sums in fp16 range
+            sb *= 0.03125f;
+            const uint32_t hs = cvt_h2(sb, sa);
+            const uint32_t ls = cvt_h2(sb - h2_hi(hs), sa - h2_lo(hs));
+            F.m[nt] = part ? ls : hs;
         }
     }
 }
 
-// ---- fp16 constants from a byte ---------------------------------------------
+constexpr uint32_t kMagic = 0x64006400u;  // (1024, 1024)
+
+// fp16 constants from a byte
 IFR_DEV uint32_t bcast_byte_h2(uint32_t word, int byte) {
     const uint32_t sel = (uint32_t)byte | (4u << 4) | ((uint32_t)byte << 8) | (4u << 12);
-    return hsub2_u(__byte_perm(word, 0u, sel) | 0x64006400u, 0x64006400u);
+    return hsub2_u(__byte_perm(word, 0u, sel) | kMagic, kMagic);
 }
 IFR_DEV uint32_t bytes01_h2(uint32_t word) {
-    return hsub2_u(__byte_perm(word, 0u, 0x4140u) | 0x64006400u, 0x64006400u);
+    return hsub2_u(__byte_perm(word, 0u, 0x4140u) | kMagic, kMagic);
 }
-constexpr uint32_t kMagic = 0x64006400u;     // (1024, 1024)
 constexpr uint32_t kNegH1024 = 0xE400E400u;  // (-1024, -1024)
 constexpr uint32_t kH1_16 = 0x2C002C00u;     // (1/16, 1/16)
 constexpr uint32_t kNegH64 = 0xD400D400u;    // (-64, -64)
 
-// Q4_K / Q5_K constants of one row for lane quad t: sub-blocks 2t (low
-// nibbles, steps 0-7) and 2t+1 (high nibbles, steps 8-15)
-struct QKRow {
-    uint32_t klo, nlo, khi, nhi;  // A = q*sc: lo as fma(1024+q, sc, -1024 sc); hi from 1024+16q
-    uint32_t mA;                  // (m_2t, m_2t+1) for the min MMA
-    float d, dm32;
-};
-
-IFR_DEV void qk_row_consts(const uint4 &h, int t, QKRow &R) {
-    const int tt = t & 1;
-    const uint32_t A = h.y >> (16 * tt), B = h.z >> (16 * tt), C = h.w >> (16 * tt);
-    const bool upper = t >= 2;  // sub-blocks 4..7 use the split 6-bit encoding (src/Dequant.jl:345-362)
-    const uint32_t sc = upper ? ((C & 0x0F0Fu) | ((A >> 2) & 0x3030u)) : (A & 0x3F3Fu);
-    const uint32_t m = upper ? (((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u)) : (B & 0x3F3Fu);
-    const uint32_t s_lo = bcast_byte_h2(sc, 0), s_hi = bcast_byte_h2(sc, 1);
-    R.klo = s_lo;
-    R.nlo = hmul2_u(s_lo, kNegH1024);
-    R.khi = hmul2_u(s_hi, kH1_16);
-    R.nhi = hmul2_u(s_hi, kNegH64);
-    R.mA = bytes01_h2(m);
-    R.d = h2f((uint16_t)(h.x & 0xffffu));
-    R.dm32 = h2f((uint16_t)(h.x >> 16)) * 32.0f;
+// 6-bit scales and mins of the 8 sub-blocks of a Q4_K/Q5_K header
+// (src/Dequant.jl:345-362), one byte each: words [0] = sub-blocks 0-3, [1] = 4-7
+IFR_DEV void qk_scales(const uint4 &h, uint32_t (&sc)[2], uint32_t (&mn)[2]) {
+    sc[0] = h.y & 0x3f3f3f3fu;
+    mn[0] = h.z & 0x3f3f3f3fu;
+    sc[1] = (h.w & 0x0f0f0f0fu) | (((h.y >> 6) & 0x03030303u) << 4);
+    mn[1] = ((h.w >> 4) & 0x0f0f0f0fu) | (((h.z >> 6) & 0x03030303u) << 4);
 }
 
-// bit b of each 16-bit half of w moved to bit `to` (compile-time shifts)
-template <int B, int TO>
-IFR_DEV uint32_t bits_to(uint32_t w) { return TO >= B ? (w << (TO - B)) : (w >> (B - TO)); }
-
-// ---- one M-tile (16 rows x 256 columns) from shared memory --------------------
-template <int FMT, int NT>
-IFR_DEV void mtile_qk(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
-    constexpr bool Q5 = FMT == 13;
+// Q4_K / Q5_K with exact activations: A = q * sc in fp16 (exact: sc*q <= 63*31 <
+// 2048), low-nibble chunks as fma(1024+q, sc, -1024 sc), high-nibble chunks as
+// fma(1024+16q, sc/16, -64 sc); one qs word serves the steps of chunks 2p, 2p+1
+template <bool Q5, int NT>
+IFR_DEV void mtile_qk_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const uint4 h0 = lds128(tile + qk_hdr(g)), h1 = lds128(tile + qk_hdr(g + 8));
     const uint4 q00 = lds128(tile + qk_qs(Q5, 0, g, t)), q01 = lds128(tile + qk_qs(Q5, 1, g, t));
     const uint4 q10 = lds128(tile + qk_qs(Q5, 0, g + 8, t)), q11 = lds128(tile + qk_qs(Q5, 1, g + 8, t));
     uint4 hb = {};
     if (Q5) hb = lds128(tile + q5_qh(g, t));
-    QKRow R0, R1;
-    qk_row_consts(h0, t, R0);
-    qk_row_consts(h1, t, R1);
+    uint32_t sc0[2], mn0[2], sc1[2], mn1[2];
+    qk_scales(h0, sc0, mn0);
+    qk_scales(h1, sc1, mn1);
+    // min MMA A fragment: (m_2t, m_2t+1) of rows g and g+8
+    const uint32_t mA0 = bytes01_h2(mn0[t >> 1] >> (16 * (t & 1)));
+    const uint32_t mA1 = bytes01_h2(mn1[t >> 1] >> (16 * (t & 1)));
     float c[2][NT][4], cm[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
         for (int i = 0; i < 4; i++) c[0][nt][i] = c[1][nt][i] = cm[nt][i] = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; w++) {
-        const uint32_t W0 = u4w(w < 4 ? q00 : q01, w & 3), W1 = u4w(w < 4 ? q10 : q11, w & 3);
-        const uint32_t W0s = W0 >> 8, W1s = W1 >> 8;
-        uint32_t lo01_0 = lop_and_or(W0, 0x000F000Fu, kMagic), lo23_0 = lop_and_or(W0s, 0x000F000Fu, kMagic);
-        uint32_t hi01_0 = lop_and_or(W0, 0x00F000F0u, kMagic), hi23_0 = lop_and_or(W0s, 0x00F000F0u, kMagic);
-        uint32_t lo01_1 = lop_and_or(W1, 0x000F000Fu, kMagic), lo23_1 = lop_and_or(W1s, 0x000F000Fu, kMagic);
-        uint32_t hi01_1 = lop_and_or(W1, 0x00F000F0u, kMagic), hi23_1 = lop_and_or(W1s, 0x00F000F0u, kMagic);
-        if (Q5) {
-            // fifth bit: step w (low nibble) -> bit 4 (+16), step w+8 (high nibble) -> bit 8 (x16)
-            lo01_0 |= bits_to<0, 4>(hb.x >> w) & 0x00100010u;
-            lo23_0 |= bits_to<0, 4>(hb.y >> w) & 0x00100010u;
-            lo01_1 |= bits_to<0, 4>(hb.z >> w) & 0x00100010u;
-            lo23_1 |= bits_to<0, 4>(hb.w >> w) & 0x00100010u;
-            hi01_0 |= bits_to<0, 8>(hb.x >> (w + 8)) & 0x01000100u;
-            hi23_0 |= bits_to<0, 8>(hb.y >> (w + 8)) & 0x01000100u;
-            hi01_1 |= bits_to<0, 8>(hb.z >> (w + 8)) & 0x01000100u;
-            hi23_1 |= bits_to<0, 8>(hb.w >> (w + 8)) & 0x01000100u;
-        }
-        const uint32_t a0 = hfma2_u(lo01_0, R0.klo, R0.nlo), a1 = hfma2_u(lo01_1, R1.klo, R1.nlo);
-        const uint32_t a2 = hfma2_u(lo23_0, R0.klo, R0.nlo), a3 = hfma2_u(lo23_1, R1.klo, R1.nlo);
-        const uint32_t b0 = hfma2_u(hi01_0, R0.khi, R0.nhi), b1 = hfma2_u(hi01_1, R1.khi, R1.nhi);
-        const uint32_t b2 = hfma2_u(hi23_0, R0.khi, R0.nhi), b3 = hfma2_u(hi23_1, R1.khi, R1.nhi);
+    for (int p = 0; p < 4; p++) {
+        const int cl = 2 * p, chh = 2 * p + 1;
+        const uint32_t kl0 = bcast_byte_h2(sc0[cl >> 2], cl & 3), kl1 = bcast_byte_h2(sc1[cl >> 2], cl & 3);
+        const uint32_t nl0 = hmul2_u(kl0, kNegH1024), nl1 = hmul2_u(kl1, kNegH1024);
+        const uint32_t sh0 = bcast_byte_h2(sc0[chh >> 2], chh & 3), sh1 = bcast_byte_h2(sc1[chh >> 2], chh & 3);
+        const uint32_t kh0 = hmul2_u(sh0, kH1_16), kh1 = hmul2_u(sh1, kH1_16);
+        const uint32_t nh0 = hmul2_u(sh0, kNegH64), nh1 = hmul2_u(sh1, kNegH64);
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            mma16816(c[0][nt], a0, a1, a2, a3, F.b[w][nt][0], F.b[w][nt][1]);
-            mma16816(c[1][nt], b0, b1, b2, b3, F.b[w + 8][nt][0], F.b[w + 8][nt][1]);
+        for (int h = 0; h < 2; h++) {
+            const uint4 Q0 = (p >> 1) ? q01 : q00, Q1 = (p >> 1) ? q11 : q10;
+            const uint32_t W0 = u4w(Q0, 2 * (p & 1) + h), W1 = u4w(Q1, 2 * (p & 1) + h);
+            const uint32_t W0s = W0 >> 8, W1s = W1 >> 8;
+            uint32_t lo02_0 = lop_and_or(W0, 0x000F000Fu, kMagic), lo13_0 = lop_and_or(W0s, 0x000F000Fu, kMagic);
+            uint32_t hi02_0 = lop_and_or(W0, 0x00F000F0u, kMagic), hi13_0 = lop_and_or(W0s, 0x00F000F0u, kMagic);
+            uint32_t lo02_1 = lop_and_or(W1, 0x000F000Fu, kMagic), lo13_1 = lop_and_or(W1s, 0x000F000Fu, kMagic);
+            uint32_t hi02_1 = lop_and_or(W1, 0x00F000F0u, kMagic), hi13_1 = lop_and_or(W1s, 0x00F000F0u, kMagic);
+            if (Q5) {
+                // fifth bit: bit c of qh byte j; low nibble -> +16 (bit 4), high nibble -> +256 (bit 8)
+                const uint32_t H0 = h ? hb.y : hb.x, H1 = h ? hb.w : hb.z;
+                lo02_0 |= ((H0 >> cl) & 0x00010001u) << 4;
+                lo13_0 |= ((H0 >> (8 + cl)) & 0x00010001u) << 4;
+                lo02_1 |= ((H1 >> cl) & 0x00010001u) << 4;
+                lo13_1 |= ((H1 >> (8 + cl)) & 0x00010001u) << 4;
+                hi02_0 |= ((H0 >> chh) & 0x00010001u) << 8;
+                hi13_0 |= ((H0 >> (8 + chh)) & 0x00010001u) << 8;
+                hi02_1 |= ((H1 >> chh) & 0x00010001u) << 8;
+                hi13_1 |= ((H1 >> (8 + chh)) & 0x00010001u) << 8;
+            }
+            const uint32_t a0 = hfma2_u(lo02_0, kl0, nl0), a1 = hfma2_u(lo02_1, kl1, nl1);
+            const uint32_t a2 = hfma2_u(lo13_0, kl0, nl0), a3 = hfma2_u(lo13_1, kl1, nl1);
+            const uint32_t b0 = hfma2_u(hi02_0, kh0, nh0), b1 = hfma2_u(hi02_1, kh1, nh1);
+            const uint32_t b2 = hfma2_u(hi13_0, kh0, nh0), b3 = hfma2_u(hi13_1, kh1, nh1);
+            const int sl = 2 * cl + h, shs = 2 * chh + h;
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                mma16816(c[0][nt], a0, a1, a2, a3, F.b[sl][nt][0], F.b[sl][nt][1]);
+                mma16816(c[1][nt], b0, b1, b2, b3, F.b[shs][nt][0], F.b[shs][nt][1]);
+            }
         }
     }
+    const float d0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16)) * 32.0f;
+    const float d1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16)) * 32.0f;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        mma1688(cm[nt], R0.mA, R1.mA, F.m[nt]);
+        mma1688(cm[nt], mA0, mA1, F.m[nt]);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const float d = i < 2 ? R0.d : R1.d, dm = i < 2 ? R0.dm32 : R1.dm32;
+            const float d = i < 2 ? d0 : d1, dm = i < 2 ? dm0 : dm1;
             tot[nt][i] = fmaf(F.es[nt], d * (c[0][nt][i] + c[1][nt][i]) - dm * cm[nt][i], tot[nt][i]);
         }
     }
 }
 
-// Q6_K: step s = scale group s.  A = q - 32: low-nibble steps (1024 + q) - 1056,
-// high-nibble steps (1024 + 16 q) / 16 - 96; the int8 group scale multiplies
-// each step's f32 MMA result
+// Q6_K with exact activations: step s = scale group s; A = q - 32 as
+// (1024 + q) - 1056 (low nibbles) or (1024 + 16 q) / 16 - 96 (high nibbles); the
+// int8 group scale multiplies each step's f32 MMA result
 template <int NT>
-IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_q6_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const float d0 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g)));
     const float d1 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g + 8)));
@@ -360,32 +378,36 @@ IFR_DEV void mtile_q6k(const uint8_t *tile, int lane, const BFrag<NT> &F, float 
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
 #pragma unroll
-    for (int s = 0; s < 16; s++) {
-        const int lw = q6_lo_word(s), hw = q6_hi_word(s), qq = (s >> 1) & 3;
-        const uint32_t W0 = u4w(lw < 4 ? l00 : l01, lw & 3), W1 = u4w(lw < 4 ? l10 : l11, lw & 3);
-        const uint32_t H0 = u4w(hq0, hw) >> (2 * qq), H1 = u4w(hq1, hw) >> (2 * qq);
-        uint32_t a0, a1, a2, a3;
-        if (((s >> 2) & 1) == 0) {
-            a0 = hsub2_u(lop_and_or(W0, 0x000F000Fu, kMagic) | ((H0 << 4) & 0x00300030u), k1056);
-            a1 = hsub2_u(lop_and_or(W1, 0x000F000Fu, kMagic) | ((H1 << 4) & 0x00300030u), k1056);
-            a2 = hsub2_u(lop_and_or(W0 >> 8, 0x000F000Fu, kMagic) | ((H0 >> 4) & 0x00300030u), k1056);
-            a3 = hsub2_u(lop_and_or(W1 >> 8, 0x000F000Fu, kMagic) | ((H1 >> 4) & 0x00300030u), k1056);
-        } else {
-            a0 = hfma2_u(lop_and_or(W0, 0x00F000F0u, kMagic) | ((H0 << 8) & 0x03000300u), kH1_16, kNeg96);
-            a1 = hfma2_u(lop_and_or(W1, 0x00F000F0u, kMagic) | ((H1 << 8) & 0x03000300u), kH1_16, kNeg96);
-            a2 = hfma2_u(lop_and_or(W0 >> 8, 0x00F000F0u, kMagic) | (H0 & 0x03000300u), kH1_16, kNeg96);
-            a3 = hfma2_u(lop_and_or(W1 >> 8, 0x00F000F0u, kMagic) | (H1 & 0x03000300u), kH1_16, kNeg96);
-        }
-        const float f0 = (float)(int8_t)(u4w(sc0, s >> 2) >> (8 * (s & 3)));
-        const float f1 = (float)(int8_t)(u4w(sc1, s >> 2) >> (8 * (s & 3)));
+    for (int c = 0; c < 8; c++) {
+        const int n = c >> 2, qq = c & 3;
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            float c[4];
-            mma16816_z(c, a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
-            acc[nt][0] = fmaf(f0, c[0], acc[nt][0]);
-            acc[nt][1] = fmaf(f0, c[1], acc[nt][1]);
-            acc[nt][2] = fmaf(f1, c[2], acc[nt][2]);
-            acc[nt][3] = fmaf(f1, c[3], acc[nt][3]);
+        for (int h = 0; h < 2; h++) {
+            const int s = 2 * c + h;
+            const uint32_t W0 = u4w(n ? l01 : l00, 2 * (qq & 1) + h), W1 = u4w(n ? l11 : l10, 2 * (qq & 1) + h);
+            const uint32_t H0 = u4w(hq0, 2 * n + h) >> (2 * qq), H1 = u4w(hq1, 2 * n + h) >> (2 * qq);
+            uint32_t a0, a1, a2, a3;
+            if ((qq >> 1) == 0) {
+                a0 = hsub2_u(lop_and_or(W0, 0x000F000Fu, kMagic) | ((H0 << 4) & 0x00300030u), k1056);
+                a1 = hsub2_u(lop_and_or(W1, 0x000F000Fu, kMagic) | ((H1 << 4) & 0x00300030u), k1056);
+                a2 = hsub2_u(lop_and_or(W0 >> 8, 0x000F000Fu, kMagic) | ((H0 >> 4) & 0x00300030u), k1056);
+                a3 = hsub2_u(lop_and_or(W1 >> 8, 0x000F000Fu, kMagic) | ((H1 >> 4) & 0x00300030u), k1056);
+            } else {
+                a0 = hfma2_u(lop_and_or(W0, 0x00F000F0u, kMagic) | ((H0 << 8) & 0x03000300u), kH1_16, kNeg96);
+                a1 = hfma2_u(lop_and_or(W1, 0x00F000F0u, kMagic) | ((H1 << 8) & 0x03000300u), kH1_16, kNeg96);
+                a2 = hfma2_u(lop_and_or(W0 >> 8, 0x00F000F0u, kMagic) | (H0 & 0x03000300u), kH1_16, kNeg96);
+                a3 = hfma2_u(lop_and_or(W1 >> 8, 0x00F000F0u, kMagic) | (H1 & 0x03000300u), kH1_16, kNeg96);
+            }
+            const float f0 = (float)(int8_t)(u4w(sc0, s >> 2) >> (8 * (s & 3)));
+            const float f1 = (float)(int8_t)(u4w(sc1, s >> 2) >> (8 * (s & 3)));
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                float cc[4];
+                mma16816_z(cc, a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+                acc[nt][0] = fmaf(f0, cc[0], acc[nt][0]);
+                acc[nt][1] = fmaf(f0, cc[1], acc[nt][1]);
+                acc[nt][2] = fmaf(f1, cc[2], acc[nt][2]);
+                acc[nt][3] = fmaf(f1, cc[3], acc[nt][3]);
+            }
         }
     }
 #pragma unroll
@@ -447,6 +469,154 @@ IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<NT> &F, float 
         for (int i = 0; i < 4; i++) tot[nt][i] = fmaf(F.es[nt], acc[nt][i], tot[nt][i]);
 }
 
+// ---- K-quants with Q8_K activations on the integer tensor cores ---------------
+// quantize_row_q8_K (src/kernels/quant_kernels.c:166-194) per 256-element unit
+// of each column: d = amax / 127, q = roundf(x * (1/d)), in correctly rounded
+// f32, then exact integer sub-block sums: the reference's own kernels.
+// Lane (g, t) builds the B fragments of column g (the C fragment's lanes
+// (g', t) read columns 2t, 2t+1, whose scales and sub-block sums are fetched
+// by shuffles).
+struct BFragI8 {
+    uint32_t b[8][2];  // chunk c: int8 of k-slots 4t..4t+3 and 16+4t..16+4t+3, column g
+    int s8[2][8];      // sum of the 32 int8 of chunk c, columns 2t and 2t+1 (Q4_K/Q5_K mins)
+    float d8[2];       // Q8_K scales of columns 2t and 2t+1
+};
+
+IFR_DEV uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
+    return (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+           ((uint32_t)(q3 & 0xff) << 24);
+}
+
+template <int FMT, int XF>
+IFR_DEV void build_b_i8(const GemvArgs &a, const float *inv, int64_t u, int lane, BFragI8 &F) {
+    const int g = lane >> 2, t = lane & 3;
+    const bool has = g < a.ncols;
+    // elements 32c + 16h + 4t + {0..3} for run i = 2c + h: k0 + 16 i
+    float v[64];
+    float *v0 = v, *v1 = v + 32;
+    load_x32<XF>(a, inv, g, u * 256 + 4 * t, 16, has, v0);
+    load_x32<XF>(a, inv, g, u * 256 + 128 + 4 * t, 16, has, v1);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i++) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    int csum[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        int q[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) q[j] = (int)roundf(__fmul_rn(v[8 * c + j], id));
+        F.b[c][0] = pack4_s8(q[0], q[1], q[2], q[3]);
+        F.b[c][1] = pack4_s8(q[4], q[5], q[6], q[7]);
+        csum[c] = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+    }
+    F.d8[0] = __shfl_sync(0xffffffffu, d, 8 * t);
+    F.d8[1] = __shfl_sync(0xffffffffu, d, 8 * t + 4);
+    if (FMT == 12 || FMT == 13) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            int sc = csum[c];
+            sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+            sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+            F.s8[0][c] = __shfl_sync(0xffffffffu, sc, 8 * t);
+            F.s8[1][c] = __shfl_sync(0xffffffffu, sc, 8 * t + 4);
+        }
+    }
+}
+
+IFR_DEV int byte_of(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
+
+// Q4_K / Q5_K x Q8_K (vec_dot_q4_K_q8_K / q5_K, quant_kernels.c:204-435): per
+// unit and output, the exact integer sums S = sum_c sc_c (q . q8)_c and
+// M = sum_c m_c bsum_c, then d8 * d * S - d8 * dmin * M in f32
+template <bool Q5>
+IFR_DEV void mtile_qk_i8(const uint8_t *tile, int lane, const BFragI8 &F, float (&tot)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint4 h0 = lds128(tile + qk_hdr(g)), h1 = lds128(tile + qk_hdr(g + 8));
+    const uint4 q00 = lds128(tile + qk_qs(Q5, 0, g, t)), q01 = lds128(tile + qk_qs(Q5, 1, g, t));
+    const uint4 q10 = lds128(tile + qk_qs(Q5, 0, g + 8, t)), q11 = lds128(tile + qk_qs(Q5, 1, g + 8, t));
+    uint4 hb = {};
+    if (Q5) hb = lds128(tile + q5_qh(g, t));
+    uint32_t sc[2][2], mn[2][2];
+    qk_scales(h0, sc[0], mn[0]);
+    qk_scales(h1, sc[1], mn[1]);
+    int S[4] = {0, 0, 0, 0}, M[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const int p = c >> 1, sh = 4 * (c & 1), wi = 2 * (p & 1);
+        const uint4 Q0 = (p >> 1) ? q01 : q00, Q1 = (p >> 1) ? q11 : q10;
+        uint32_t a0 = (u4w(Q0, wi) >> sh) & 0x0f0f0f0fu, a2 = (u4w(Q0, wi + 1) >> sh) & 0x0f0f0f0fu;
+        uint32_t a1 = (u4w(Q1, wi) >> sh) & 0x0f0f0f0fu, a3 = (u4w(Q1, wi + 1) >> sh) & 0x0f0f0f0fu;
+        if (Q5) {
+            a0 |= ((hb.x >> c) & 0x01010101u) << 4;
+            a2 |= ((hb.y >> c) & 0x01010101u) << 4;
+            a1 |= ((hb.z >> c) & 0x01010101u) << 4;
+            a3 |= ((hb.w >> c) & 0x01010101u) << 4;
+        }
+        int cc[4];
+        imma16832_z(cc, a0, a1, a2, a3, F.b[c][0], F.b[c][1]);
+        const int s0 = byte_of(sc[0][c >> 2], c & 3), s1 = byte_of(sc[1][c >> 2], c & 3);
+        const int m0 = byte_of(mn[0][c >> 2], c & 3), m1 = byte_of(mn[1][c >> 2], c & 3);
+        S[0] += s0 * cc[0];
+        S[1] += s0 * cc[1];
+        S[2] += s1 * cc[2];
+        S[3] += s1 * cc[3];
+        M[0] += m0 * F.s8[0][c];
+        M[1] += m0 * F.s8[1][c];
+        M[2] += m1 * F.s8[0][c];
+        M[3] += m1 * F.s8[1][c];
+    }
+    const float d0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16));
+    const float d1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16));
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float d8 = F.d8[i & 1];
+        tot[i] += (d8 * (i < 2 ? d0 : d1)) * (float)S[i] - (d8 * (i < 2 ? dm0 : dm1)) * (float)M[i];
+    }
+}
+
+// Q6_K x Q8_K (vec_dot_q6_K_q8_K, quant_kernels.c:440-...): S = sum_j sc_j
+// ((q6 - 32) . q8)_j over the 16 groups, then d8 * d * S; one k16 MMA per group
+IFR_DEV void mtile_q6_i8(const uint8_t *tile, int lane, const BFragI8 &F, float (&tot)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const float d0 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g)));
+    const float d1 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g + 8)));
+    const uint4 sc0 = lds128(tile + q6_sc(g)), sc1 = lds128(tile + q6_sc(g + 8));
+    const uint4 l00 = lds128(tile + q6_ql(0, g, t)), l01 = lds128(tile + q6_ql(1, g, t));
+    const uint4 l10 = lds128(tile + q6_ql(0, g + 8, t)), l11 = lds128(tile + q6_ql(1, g + 8, t));
+    const uint4 hq0 = lds128(tile + q6_qh(g, t)), hq1 = lds128(tile + q6_qh(g + 8, t));
+    int S[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const int n = c >> 2, qq = c & 3;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t w0 = u4w(n ? l01 : l00, 2 * (qq & 1) + h), w1 = u4w(n ? l11 : l10, 2 * (qq & 1) + h);
+            const uint32_t x0 = ((w0 >> (4 * (qq >> 1))) & 0x0f0f0f0fu) |
+                                (((u4w(hq0, 2 * n + h) >> (2 * qq)) & 0x03030303u) << 4);
+            const uint32_t x1 = ((w1 >> (4 * (qq >> 1))) & 0x0f0f0f0fu) |
+                                (((u4w(hq1, 2 * n + h) >> (2 * qq)) & 0x03030303u) << 4);
+            // bytewise q - 32 without borrows between bytes
+            const uint32_t a0 = ((x0 | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
+            const uint32_t a1 = ((x1 | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
+            int cc[4];
+            imma16816_z(cc, a0, a1, F.b[c][h]);
+            const int j = 2 * c + h;
+            const int f0 = (int)(int8_t)byte_of(u4w(sc0, j >> 2), j & 3);
+            const int f1 = (int)(int8_t)byte_of(u4w(sc1, j >> 2), j & 3);
+            S[0] += f0 * cc[0];
+            S[1] += f0 * cc[1];
+            S[2] += f1 * cc[2];
+            S[3] += f1 * cc[3];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) tot[i] += (F.d8[i & 1] * (i < 2 ? d0 : d1)) * (float)S[i];
+}
+
 // Work order of one CTA: its contiguous range of row groups, cut into sweeps;
 // per sweep all K passes; per pass the sweep's row groups (one stage each).
 // Partial sums of a sweep live in shared memory, so no K pass touches global
@@ -470,10 +640,10 @@ struct Order {
 };
 
 // Issue the bulk copies of stage q into its ring slot (one thread).
-template <int MTB>
+template <int MTB, int MPW>
 IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring, uint64_t *full) {
-    constexpr int STAGE = 16 * MTB;
-    const int UW = a.UW, MTG = 16 / UW;
+    constexpr int STAGE = 8 * MPW * MTB;
+    const int UW = a.UW, MTG = 8 * MPW / UW;
     int p, rg;
     o.at(q, p, rg);
     const int s = q % a.S;
@@ -487,13 +657,17 @@ IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring
     }
 }
 
-template <int FMT, int NT, int XF>
+// MPW: M-tiles per warp per stage (a stage is 8 * MPW M-tiles = MTG row
+// blocks x UW units); 1 halves each warp's serial work for small matrices
+// ACT: K-quant activations, 0 exact f32 (fp16 tensor cores), 1 Q8_K (integer
+// tensor cores, the reference's kernels); Q8_0 is always exact
+template <int FMT, int NT, int XF, int MPW, int ACT>
 __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int MTB = mtile_bytes(FMT);
-    constexpr int STAGE = 16 * MTB;   // MTG * UW M-tiles
-    constexpr int NRED = 2 * NT * 4;  // floats per lane per warp in the reduction
-    const int UW = a.UW, MTG = 16 / UW;
+    constexpr int STAGE = 8 * MPW * MTB;  // MTG * UW M-tiles
+    constexpr int NRED = MPW * NT * 4;    // floats per lane per warp in the reduction
+    const int UW = a.UW, MTG = 8 * MPW / UW;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
     float *red = reinterpret_cast<float *>(ring + (size_t)a.S * STAGE);
@@ -513,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     if (tid == 0) {
         for (int s = 0; s < a.S; s++) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB>(a, o, q, ring, full);
+        for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB, MPW>(a, o, q, ring, full);
     }
     pdl_wait();
     // RMSNorm of the input columns: 1 / sqrt(sum x^2 / K + eps) per column
@@ -550,7 +724,8 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     __syncthreads();
 
     const int ui = warp % UW, mp = warp / UW;
-    BFrag<NT> F;
+    constexpr bool kI8 = FMT != 8 && ACT == 1;
+    std::conditional_t<kI8, BFragI8, BFrag<NT>> F;
     int it = 0;
     bool dead = false;
     for (int sw = o.rg_lo; sw < o.rg_hi; sw += o.sweep_rg) {
@@ -560,13 +735,16 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         for (int p = 0; p < o.passes; p++) {
             const int64_t u = (int64_t)p * UW + ui;
             const bool active = u < a.nu;
-            if (active) build_b<FMT, NT, XF>(a, inv_s, u, lane, F);
+            if (active) {
+                if constexpr (kI8) build_b_i8<FMT, XF>(a, inv_s, u, lane, F);
+                else build_b<FMT, NT, XF>(a, inv_s, u, lane, F);
+            }
             for (int rg = sw; rg < sw_hi; rg++, it++) {
                 const int s = it % a.S;
                 if (!dead && !mbar_wait(full + s, (uint32_t)(it / a.S) & 1)) dead = true;
-                float tot[2][NT][4];
+                float tot[MPW][NT][4];
 #pragma unroll
-                for (int mm = 0; mm < 2; mm++)
+                for (int mm = 0; mm < MPW; mm++)
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
@@ -574,37 +752,47 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
                 if (active && !dead) {
                     const uint8_t *st = ring + (size_t)s * STAGE;
 #pragma unroll
-                    for (int mm = 0; mm < 2; mm++) {
-                        const int m = 2 * mp + mm;
+                    for (int mm = 0; mm < MPW; mm++) {
+                        const int m = MPW * mp + mm;
                         if (rg * MTG + m < a.nrb) {
                             const uint8_t *tile = st + (size_t)(m * UW + ui) * MTB;
-                            if constexpr (FMT == 14) mtile_q6k<NT>(tile, lane, F, tot[mm]);
-                            else if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot[mm]);
-                            else mtile_qk<FMT, NT>(tile, lane, F, tot[mm]);
+                            if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot[mm]);
+                            else if constexpr (kI8 && FMT == 14) mtile_q6_i8(tile, lane, F, tot[mm][0]);
+                            else if constexpr (kI8) mtile_qk_i8<FMT == 13>(tile, lane, F, tot[mm][0]);
+                            else if constexpr (FMT == 14) mtile_q6_h<NT>(tile, lane, F, tot[mm]);
+                            else mtile_qk_h<FMT == 13, NT>(tile, lane, F, tot[mm]);
                         }
                     }
                 }
 #pragma unroll
-                for (int mm = 0; mm < 2; mm++)
+                for (int mm = 0; mm < MPW; mm++)
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                         for (int i = 0; i < 4; i++)
-                            red[((warp * 2 + mm) * NT * 4 + nt * 4 + i) * 32 + lane] = tot[mm][nt][i];
+                            red[((warp * MPW + mm) * NT * 4 + nt * 4 + i) * 32 + lane] = tot[mm][nt][i];
                 consumer_bar();  // slot s fully read; partials visible
-                if (tid == 0 && !dead && it + a.S < total) issue_stage<MTB>(a, o, it + a.S, ring, full);
+                if (tid == 0 && !dead && it + a.S < total) issue_stage<MTB, MPW>(a, o, it + a.S, ring, full);
                 // each thread owns outputs (m, row, col) = o, o + 256, ... in every pass
                 const int base = (rg - sw) * MTG * 16;
                 for (int oi = tid; oi < MTG * 128; oi += kThreads) {
                     const int col = oi & 7, r16 = (oi >> 3) & 15, m = oi >> 7;
-                    const int nt = col >> 2;
-                    if (nt >= NT) continue;
-                    const int mmp = m >> 1, mm = m & 1, half = r16 >> 3;
-                    const int ln = 4 * (r16 & 7) + (col & 3);
+                    const int mmp = m / MPW, mm = m % MPW, half = r16 >> 3;
                     float v = 0.f;
-                    for (int q = 0; q < UW; q++) {
-                        const float *pp = red + (((mmp * UW + q) * 2 + mm) * NT * 4 + nt * 4 + 2 * half) * 32 + ln;
-                        v += pp[0] + pp[32];
+                    if constexpr (!kI8) {
+                        // C columns 2t, 2t+1 of n-tile nt are the hi and lo parts of column 4 nt + t
+                        const int nt = col >> 2;
+                        if (nt >= NT) continue;
+                        const int ln = 4 * (r16 & 7) + (col & 3);
+                        for (int q = 0; q < UW; q++) {
+                            const float *pp = red + (((mmp * UW + q) * MPW + mm) * NT * 4 + nt * 4 + 2 * half) * 32 + ln;
+                            v += pp[0] + pp[32];
+                        }
+                    } else {
+                        // C columns 2t, 2t+1 are activation columns 2t, 2t+1
+                        const int ln = 4 * (r16 & 7) + (col >> 1);
+                        for (int q = 0; q < UW; q++)
+                            v += red[(((mmp * UW + q) * MPW + mm) * NT * 4 + 2 * half + (col & 1)) * 32 + ln];
                     }
                     acc[(base + m * 16 + r16) * 8 + col] += v;
                 }
@@ -653,16 +841,14 @@ static int num_sms() {
     return n;
 }
 
-template <int FMT, int NT, int XF>
-static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
-                          cudaStream_t s, const XForm &xf) {
+template <int FMT, int NT, int XF, int MPW, int ACT>
+static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                              cudaStream_t s, const XForm &xf, int UW) {
     constexpr int MTB = mtile_bytes(FMT);
-    constexpr int STAGE = 16 * MTB;
+    constexpr int STAGE = 8 * MPW * MTB;
     constexpr int kSmemMax = 226 * 1024;  // dynamic; 1 KB of the 227 KB per block stays for static shared memory
-    int UW = 1;
-    while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
-    const int MTG = 16 / UW;
-    const int red = kConsumers * (2 * NT * 4) * 32 * 4;
+    const int MTG = 8 * MPW / UW;
+    const int red = kConsumers * (MPW * NT * 4) * 32 * 4;
     const int64_t nrg = (T.nrb + MTG - 1) / MTG;
     const int grid = (int)(nrg < num_sms() ? nrg : num_sms());
     // ring stages first (2..5), then the shared accumulator gets the rest
@@ -679,26 +865,49 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF>, cudaFuncAttributePreferredSharedMemoryCarveout,
+        e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
                sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
-    return launch_k(qgemv_kernel<FMT, NT, XF>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
+    return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
+}
+
+// Work split: UW warps share each row block's units; two M-tiles per warp and
+// stage unless that leaves fewer than half the SMs busy, then one (twice the
+// CTAs, half the serial work per warp).
+template <int FMT, int NT, int XF, int ACT>
+static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                          cudaStream_t s, const XForm &xf) {
+    int UW = 1;
+    while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
+    const int64_t nrg2 = (T.nrb + 16 / UW - 1) / (16 / UW);
+    if (UW == 8 && 2 * nrg2 < num_sms() && !xf.ep)
+        return launch_mpw<FMT, NT, XF, 1, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
+    return launch_mpw<FMT, NT, XF, 2, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
+}
+
+template <int FMT, int NT, int XF>
+static cudaError_t launch_act(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                              cudaStream_t s, const XForm &xf) {
+    if constexpr (FMT == 8) return launch<FMT, NT, XF, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    else if (xf.act == 1) return launch<FMT, 1, XF, 1>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    else return launch<FMT, NT, XF, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
 }
 
 template <int FMT>
 static cudaError_t launch_fmt(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                               cudaStream_t s, const XForm &xf) {
-    const bool two = ncols > 4;
+    const bool two = ncols > 4 && (FMT == 8 || xf.act == 0);  // Q8_K: all 8 columns in one n-tile
     switch (xf.kind) {
-    case 0: return two ? launch<FMT, 2, 0>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
-    case 1: return two ? launch<FMT, 2, 1>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 1>(T, X, ncols, Y, accumulate, ldy, s, xf);
-    case 2: return two ? launch<FMT, 2, 2>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 2>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 0: return two ? launch_act<FMT, 2, 0>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch_act<FMT, 1, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 1: return two ? launch_act<FMT, 2, 1>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch_act<FMT, 1, 1>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 2: return two ? launch_act<FMT, 2, 2>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch_act<FMT, 1, 2>(T, X, ncols, Y, accumulate, ldy, s, xf);
     }
     return cudaErrorInvalidValue;
 }
@@ -708,6 +917,7 @@ cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, b
     if (ncols < 1 || ncols > 8) return cudaErrorInvalidValue;
     if (xf.kind < 0 || xf.kind > 2 || (xf.kind == 1 && !xf.w)) return cudaErrorInvalidValue;
     if (xf.ep && (accumulate || T.rows % 32)) return cudaErrorInvalidValue;
+    if (xf.act != 0 && xf.act != 1) return cudaErrorInvalidValue;
     switch (T.type) {
     case 12: return launch_fmt<12>(T, X, ncols, Y, accumulate, ldy, s, xf);
     case 13: return launch_fmt<13>(T, X, ncols, Y, accumulate, ldy, s, xf);

@@ -44,29 +44,15 @@ __global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restri
         const int qs0 = q5 ? 48 : 16;
         for (int k = 0; k < 16; k++) tile[qk_hdr(r) + k] = pad ? 0 : b[k];
         for (int q = 0; q < 128; q++) tile[qk_qs_byte(q5, r, q)] = pad ? 0 : b[qs0 + q];
-        if (q5) {
-            for (int t = 0; t < 4; t++) {
-                uint8_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                for (int j = 0; j < 64; j++) {
-                    const int e = 64 * t + j;
-                    const int bit = pad ? 0 : (b[16 + (e & 31)] >> (e >> 5)) & 1;
-                    const int off = q5_bit_byte(r, e) - (q5_qh(r & 7, t) + 8 * (r >> 3));
-                    w[off] |= (uint8_t)(bit << q5_bit_shift(e));
-                }
-                for (int k = 0; k < 8; k++) tile[q5_qh(r & 7, t) + 8 * (r >> 3) + k] = w[k];
-            }
-        }
+        if (q5)
+            for (int l = 0; l < 32; l++) tile[q5_qh_byte(r, l)] = pad ? 0 : b[16 + l];
     } else if (T == 14) {
-        // ql and qh bytes are permuted whole: low-nibble elements carry their
-        // high-nibble partner (e + 64), qq = 0 elements the other three 2-bit fields
         const uint8_t *b = raw + (row * nb_raw + u) * BB;
         tile[q6_d(r)] = pad ? 0 : b[208];
         tile[q6_d(r) + 1] = pad ? 0 : b[209];
         for (int k = 0; k < 16; k++) tile[q6_sc(r) + k] = pad ? 0 : b[192 + k];
-        for (int e = 0; e < 256; e++) {
-            if (q6_lo_shift(e) == 0) tile[q6_lo_byte(r, e)] = pad ? 0 : b[q6_raw_lo_byte(e)];
-            if (q6_hi_shift(e) == 0) tile[q6_hi_byte(r, e)] = pad ? 0 : b[q6_raw_hi_byte(e)];
-        }
+        for (int q = 0; q < 128; q++) tile[q6_ql_byte(r, q)] = pad ? 0 : b[q];
+        for (int h = 0; h < 64; h++) tile[q6_qh_byte(r, h)] = pad ? 0 : b[128 + h];
     } else {  // Q8_0: unit u = raw blocks 8u .. 8u+7
         for (int bl = 0; bl < 8; bl++) {
             const int64_t rb = 8 * u + bl;

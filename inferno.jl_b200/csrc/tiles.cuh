@@ -9,24 +9,20 @@
 // padding, nothing added), so traffic equals the algorithmic bytes; rows
 // beyond M (to a multiple of 16) and Q8_0 blocks beyond K are zero-filled.
 //
-// Tensor-core mapping.  The GEMV multiplies one M-tile by the activations with
-// 16 steps of mma.m16n8k16.  In step s, MMA lane quad t (t = lane % 4) holds
-// the k-slots {2t, 2t+1, 2t+8, 2t+9} ("slots" 0..3); slot `slot` of step s is
-// unit element elem(type, s, t, slot):
-//   Q4_K / Q5_K   64 t + 4 s + slot   lane quad t owns the contiguous elements
-//                                     64t .. 64t+63 = sub-blocks 2t (steps 0-7)
-//                                     and 2t+1 (steps 8-15); their 6-bit scales
-//                                     are folded into the fp16 weights, so a
-//                                     step may mix sub-blocks
-//   Q6_K / Q8_0   16 s + 4 t + slot   step s is one Q6_K scale group of 16 (and
-//                                     steps 2b, 2b+1 one Q8_0 block): their
-//                                     scales multiply the f32 MMA results
-// Each lane's weight bits are stored as a contiguous "stream" in 16-byte
+// Tensor-core mapping.  In 16-element step s of a unit (s = 2c + h: half h of
+// 32-element chunk c), MMA lane quad t (t = lane % 4) holds the elements
+// 16 s + 4t + {0..3}, the 4 bytes of one 4-byte word of its stream:
+//   * exact f32 activations (fp16 hi + lo on mma.m16n8k16.f16): bytes (0, 2)
+//     are k-slots (2t, 2t+1) and bytes (1, 3) are k-slots (2t+8, 2t+9), which
+//     is what the fp16 magic-number unpack (w & 0x000F000F) | 0x64006400 and
+//     the same on (w >> 8) produce;
+//   * Q8_K activations (mma.m16n8k32.s8, K-quants): chunk c is one k32 step,
+//     its two words are k-slots 4t..4t+3 and 16+4t..16+4t+3 (Q6_K: two k16
+//     steps, one per 16-element scale group).
+// A K-quant sub-block (32 elements) is one chunk, so one scale per step.  The
+// weight bytes a lane needs are stored as a contiguous "stream" in 16-byte
 // pieces placed so that a warp reads them with conflict-free 16-byte
-// shared-memory loads, and inside every 4-byte word the bytes are ordered
-// (b0, b2, b1, b3): the fp16 magic-number unpack (w & 0x000F000F) | 0x64006400
-// then yields slots (0, 1) from the bytes at positions 0 and 2, and the same
-// on (w >> 8) yields slots (2, 3).
+// shared-memory loads; bytes keep their raw order inside each word.
 #pragma once
 #include <stdint.h>
 
@@ -48,67 +44,55 @@ IFR_HD int raw_block_bytes(int type) {
     return type == 12 ? 144 : type == 13 ? 176 : type == 14 ? 210 : type == 8 ? 34 : 0;
 }
 
-IFR_HD int elem(int type, int s, int t, int slot) {
-    return (type == 12 || type == 13) ? 64 * t + 4 * s + slot : 16 * s + 4 * t + slot;
-}
-// byte order inside a stored 4-byte word (self-inverse): raw i <-> position wperm(i)
-IFR_HD int wperm(int i) { return i == 1 ? 2 : (i == 2 ? 1 : i); }
-// position of byte i (0..15) of a lane stream inside its 16-byte piece
-IFR_HD int piece_byte(int i) { return (i & 12) + wperm(i & 3); }
+// K-quants: element of chunk c, lane quad t, slot j (0..7; j >= 4 is the +16 half)
+IFR_HD int elem_k(int c, int t, int j) { return 32 * c + 4 * t + (j & 3) + ((j & 4) ? 16 : 0); }
+// element of step s, lane quad t, byte j of its word (all formats)
+IFR_HD int elem_s(int s, int t, int j) { return 16 * s + 4 * t + j; }
+// the lane word (0..1) and byte of element e within its 32-element chunk:
+// word h = (e % 32) / 16, byte (e % 4); lane t = (e % 16) / 4
+IFR_HD int k_lane(int e) { return (e >> 2) & 3; }
+IFR_HD int k_half(int e) { return (e >> 4) & 1; }
 
 // ---- Q4_K / Q5_K --------------------------------------------------------------
 //   header of row r (raw bytes 0..15: d, dmin, 12 scale bytes)       16 r
-//   Q5_K qh bit-words of rows g and g+8 for lane quad t              256 + (4g+t)*16
-//        (8 bytes per row: word 0 = slots 0 | 1 << 16, word 1 = slots 2 | 3 << 16,
-//         bit s of each half = step s)
-//   qs piece (p, r, t): raw qs bytes 32t + 16p .. +16, word-permuted   QS0 + ((16p+r)*4+t)*16
-// Raw qs byte 32t + w holds element 64t + w (low nibble, step w/4) and
-// 64t + 32 + w (high nibble, step 8 + w/4).
+//   Q5_K qh words of rows g and g+8 for lane quad t                 256 + (4g+t)*16
+//        row g: raw qh bytes 4t..4t+3, 16+4t..16+4t+3; then row g+8 (bit c = chunk c)
+//   qs piece (q, r, t): raw qs bytes 32p + 4t.., 32p + 16 + 4t.. for p = 2q, 2q+1
+//                                                                   QS0 + ((16q+r)*4+t)*16
+// Raw qs byte 32p + l holds element 64p + l (low nibble, chunk 2p) and
+// 64p + 32 + l (high nibble, chunk 2p+1).
 IFR_HD int qk_hdr(int r) { return 16 * r; }
 IFR_HD int q5_qh(int g, int t) { return 256 + (4 * g + t) * 16; }
-IFR_HD int qk_qs(bool q5, int p, int r, int t) { return (q5 ? 768 : 256) + ((16 * p + r) * 4 + t) * 16; }
-IFR_HD int qk_qs_byte(bool q5, int r, int q) {  // raw qs byte q (0..127) of row r
-    return qk_qs(q5, (q & 31) >> 4, r, q >> 5) + piece_byte(q & 15);
+IFR_HD int qk_qs(bool q5, int q, int r, int t) { return (q5 ? 768 : 256) + ((16 * q + r) * 4 + t) * 16; }
+IFR_HD int qk_qs_byte(bool q5, int r, int qb) {  // raw qs byte qb (0..127) of row r
+    const int p = qb >> 5, l = qb & 31;
+    return qk_qs(q5, p >> 1, r, k_lane(l)) + 8 * (p & 1) + 4 * k_half(l) + (l & 3);
 }
-// Q5_K high bit of element e of row r: tile byte, and the bit inside it
-IFR_HD int q5_bit_byte(int r, int e) {
-    const int t = e >> 6, j = e & 63, s = j >> 2, slot = j & 3;
-    const int b = ((slot & 1) ? 16 : 0) + s;
-    return q5_qh(r & 7, t) + 8 * (r >> 3) + 4 * (slot >> 1) + (b >> 3);
-}
-IFR_HD int q5_bit_shift(int e) {
-    const int j = e & 63, s = j >> 2, slot = j & 3;
-    return (((slot & 1) ? 16 : 0) + s) & 7;
+IFR_HD int q5_qh_byte(int r, int l) {  // raw qh byte l (0..31) of row r
+    return q5_qh(r & 7, k_lane(l)) + 8 * (r >> 3) + 4 * k_half(l) + (l & 3);
 }
 
 // ---- Q6_K -----------------------------------------------------------------------
 //   d of row r                                   2 r
-//   16 int8 group scales of row r (raw order)     32 + 16 r   (step s uses scale s)
-//   ql piece (p, r, t)                            288 + ((16p+r)*4+t)*16
-//        lane stream word w (0..7) = raw ql bytes of elements 16 s + 4t + {0..3}
-//        for s = (w & 3) + 8 (w >> 2): low nibbles = step s, high nibbles = step s + 4
+//   16 int8 group scales of row r (raw order)     32 + 16 r
+//   ql piece (n, r, t)                            288 + ((16n+r)*4+t)*16
+//        words: raw ql bytes 64n + 32h1 + 16h + 4t .. +4 for (h1, h) = (0,0), (0,1), (1,0), (1,1)
 //   qh piece (r, t)                               2336 + (4r+t)*16
-//        word j (0..3) = raw qh bytes 32 (j/2) + 16 (j%2) + 4t + {0..3}: bits 2qq of
-//        step 8 (j/2) + 2 qq + j%2
-// Element e of the raw block: 6-bit q = ql nibble | qh 2 bits << 4, value
-// d * sc[e/16] * (q - 32) (src/Dequant.jl:558-601).
+//        words: raw qh bytes 32n + 16h + 4t .. +4 for (n, h) = (0,0), (0,1), (1,0), (1,1)
+// Element e = 128n + 32qq + l of the raw block: 6-bit q = (ql[64n + 32(qq%2) + l]
+// >> 4(qq/2)) & 15 | ((qh[32n + l] >> 2qq) & 3) << 4, value d * sc[e/16] * (q - 32)
+// (src/Dequant.jl:558-601).  Chunk c = 4n + qq.
 IFR_HD int q6_d(int r) { return 2 * r; }
 IFR_HD int q6_sc(int r) { return 32 + 16 * r; }
-IFR_HD int q6_ql(int p, int r, int t) { return 288 + ((16 * p + r) * 4 + t) * 16; }
+IFR_HD int q6_ql(int n, int r, int t) { return 288 + ((16 * n + r) * 4 + t) * 16; }
 IFR_HD int q6_qh(int r, int t) { return 2336 + (4 * r + t) * 16; }
-// ql word of step s and its nibble; qh word of step s and its bit pair
-IFR_HD int q6_lo_word(int s) { return (s & 3) + 4 * (s >> 3); }
-IFR_HD int q6_lo_shift(int e) { return ((e >> 6) & 1) ? 4 : 0; }
-IFR_HD int q6_hi_word(int s) { return 2 * (s >> 3) + (s & 1); }
-IFR_HD int q6_hi_shift(int e) { return 2 * ((e >> 5) & 3); }
-IFR_HD int q6_lo_byte(int r, int e) {
-    const int s = e >> 4, t = (e >> 2) & 3, slot = e & 3;
-    const int i = 4 * q6_lo_word(s) + wperm(slot);
-    return q6_ql(i >> 4, r, t) + (i & 15);
+IFR_HD int q6_ql_byte(int r, int qb) {  // raw ql byte qb (0..127)
+    const int n = qb >> 6, h1 = (qb >> 5) & 1, l = qb & 31;
+    return q6_ql(n, r, k_lane(l)) + 8 * h1 + 4 * k_half(l) + (l & 3);
 }
-IFR_HD int q6_hi_byte(int r, int e) {
-    const int s = e >> 4, t = (e >> 2) & 3, slot = e & 3;
-    return q6_qh(r, t) + 4 * q6_hi_word(s) + wperm(slot);
+IFR_HD int q6_qh_byte(int r, int hb) {  // raw qh byte hb (0..63)
+    const int n = hb >> 5, l = hb & 31;
+    return q6_qh(r, k_lane(l)) + 8 * n + 4 * k_half(l) + (l & 3);
 }
 // raw Q6_K block: the two parts of element e (ql at 0, qh at 128, sc at 192, d at 208)
 IFR_HD int q6_raw_lo_byte(int e) { return 64 * (e >> 7) + 32 * ((e >> 5) & 1) + (e & 31); }
@@ -119,12 +103,12 @@ IFR_HD int q6_raw_hi_shift(int e) { return 2 * ((e >> 5) & 3); }
 // ---- Q8_0 (unit = 8 blocks) --------------------------------------------------------
 //   d of the 8 blocks of row r (raw order)         16 r
 //   qs piece (q, r, t): lane stream words 4q .. 4q+3, word s = block s/2 bytes
-//        16 (s%2) + 4t .. +4 (elements 16 s + 4t + {0..3}), word-permuted
+//        16 (s%2) + 4t .. +4 (elements 16 s + 4t + {0..3})
 IFR_HD int q8_d(int r) { return 16 * r; }
 IFR_HD int q8_qs(int q, int r, int t) { return 256 + ((16 * q + r) * 4 + t) * 16; }
 IFR_HD int q8_qs_byte(int r, int e) {
-    const int s = e >> 4, t = (e >> 2) & 3, slot = e & 3;
-    return q8_qs(s >> 2, r, t) + 4 * (s & 3) + wperm(slot);
+    const int s = e >> 4, t = (e >> 2) & 3;
+    return q8_qs(s >> 2, r, t) + 4 * (s & 3) + (e & 3);
 }
 
 }  // namespace ifr

@@ -22,7 +22,12 @@
  * layer between fc and the final norm; its input hidden is the final-normed
  * hidden of the last verified token for the first draft, then the layer
  * output of the previous draft.
- * Matrix-vector products accumulate in f32 in index order.
+ * Matrix-vector products accumulate in f32 in index order (activation mode
+ * 0, default: the GPU engine's exact f32 activations).  In mode 1 those with
+ * K-quant weights (Q4_K/Q5_K/Q6_K) follow the reference's quantized kernels:
+ * the activation vector is quantized to Q8_K first (quantize_row_q8_K,
+ * src/kernels/quant_kernels.c:166-194, then q4_k_gemv .. q6_k_gemv :602-650)
+ * and the products are summed per 256 block in double.
  */
 #define _GNU_SOURCE
 #include "oracle.h"
@@ -54,6 +59,9 @@ struct or_model {
     float *mtp_fc, *mtp_norm_e, *mtp_norm_h, *mtp_norm;
     float *cos_cache, *sin_cache;   /* [max_ctx][half] */
     int conv_channels, inner, qk;
+    const float *kq[1024];          /* weight slots holding K-quant matrices */
+    int nkq;
+    int act;                        /* K-quant activation mode: 0 exact f32, 1 Q8_K */
 };
 
 static void *xcalloc(size_t n, size_t s) { void *p = calloc(n, s); if (!p) abort(); return p; }
@@ -65,6 +73,7 @@ or_model *or_model_new(const or_model_config *c) {
     m->qk = c->ssm_heads * c->ssm_head_dim;
     m->conv_channels = m->inner + 2 * m->qk;
     m->layers = (or_layer *)xcalloc(c->n_layers, sizeof(or_layer));
+    m->act = 0;
     int half = c->rotary_dim / 2;
     m->cos_cache = (float *)xcalloc((size_t)c->max_ctx * half, 4);
     m->sin_cache = (float *)xcalloc((size_t)c->max_ctx * half, 4);
@@ -141,10 +150,13 @@ static float **slot(or_model *m, int layer, int kind) {
 int or_model_set(or_model *m, int layer, int kind, int type, const void *data, int64_t n) {
     float **s = slot(m, layer, kind);
     if (!s) return -1;
+    for (int i = 0; i < m->nkq; i++)
+        if (m->kq[i] == *s) m->kq[i] = m->kq[--m->nkq];
     free(*s);
     *s = (float *)malloc((size_t)n * 4);
     if (!*s) return -2;
     if (or_dequantize(type, (const uint8_t *)data, n, *s)) return -1;
+    if ((type == OR_Q4_K || type == OR_Q5_K || type == OR_Q6_K) && m->nkq < 1024) m->kq[m->nkq++] = *s;
     if (layer != -1 && kind == OR_T_SSM_A) {
         or_layer *L = layer >= 0 ? &m->layers[layer] : &m->mtp_layer;
         L->ssm = 1;
@@ -212,6 +224,51 @@ static void matvec(float *y, const float *W, const float *x, int rows, int cols)
         for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
 }
 
+/* K-quant weights with Q8_K activations, per-block sums in double */
+typedef struct { float *y; const float *W; const float *d1; const int8_t *q1; int r0, r1, cols; } mq_job;
+static void *mq_run(void *p) {
+    mq_job *j = (mq_job *)p;
+    const int nb = j->cols / 256;
+    for (int r = j->r0; r < j->r1; r++) {
+        const float *w = j->W + (size_t)r * j->cols;
+        double acc = 0.0;
+        for (int b = 0; b < nb; b++) {
+            double s1 = 0.0;
+            for (int k = 0; k < 256; k++) s1 += (double)w[256 * b + k] * (double)j->q1[256 * b + k];
+            acc += (double)j->d1[b] * s1;
+        }
+        j->y[r] = (float)acc;
+    }
+    return NULL;
+}
+static void matvec_w(or_model *m, float *y, const float *W, const float *x, int rows, int cols) {
+    int kq = 0;
+    for (int i = 0; i < m->nkq; i++) kq |= m->kq[i] == W;
+    if (!kq || cols % 256 || m->act == 0) {
+        matvec(y, W, x, rows, cols);
+        return;
+    }
+    float *d1 = (float *)xcalloc((size_t)cols / 256, 4);
+    int8_t *q1 = (int8_t *)xcalloc((size_t)cols, 1);
+    or_quantize_q8k(x, cols, d1, q1);
+    int nt = (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (nt > 32) nt = 32;
+    if (nt < 1 || (size_t)rows * cols < (1u << 18)) nt = 1;
+    mq_job jobs[32];
+    pthread_t th[32];
+    for (int i = 0; i < nt; i++) {
+        jobs[i] = (mq_job){y, W, d1, q1, (int)((int64_t)rows * i / nt), (int)((int64_t)rows * (i + 1) / nt), cols};
+        if (nt > 1) pthread_create(&th[i], NULL, mq_run, &jobs[i]);
+        else mq_run(&jobs[i]);
+    }
+    if (nt > 1)
+        for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
+    free(d1);
+    free(q1);
+}
+
+void or_model_set_activation(or_model *m, int mode) { m->act = mode; }
+
 static inline float silu(float g) { return g / (1.0f + expf(-g)); }
 
 /* GatedDeltaNetCPU (ModelCPU.jl:566-731) */
@@ -222,8 +279,8 @@ static void ssm_forward(or_model *m, or_layer *L, const float *x, float *out) {
     float *qkv = (float *)malloc(C * 4), *z = (float *)malloc(inner * 4), *xc = (float *)malloc(C * 4);
     float *al = (float *)malloc(H * 4), *be = (float *)malloc(H * 4), *y = (float *)malloc(inner * 4);
     float *qn = (float *)malloc(dk * 4), *kn = (float *)malloc(dk * 4), *sk = (float *)malloc(dv * 4);
-    matvec(qkv, L->in_proj, x, C, d);
-    matvec(z, L->gate_proj, x, inner, d);
+    matvec_w(m, qkv, L->in_proj, x, C, d);
+    matvec_w(m, z, L->gate_proj, x, inner, d);
     for (int j = 0; j < K - 1; j++)
         for (int i = 0; i < C; i++) L->conv_state[(size_t)i * K + j] = L->conv_state[(size_t)i * K + j + 1];
     for (int i = 0; i < C; i++) L->conv_state[(size_t)i * K + K - 1] = qkv[i];
@@ -232,8 +289,8 @@ static void ssm_forward(or_model *m, or_layer *L, const float *x, float *out) {
         for (int k = 0; k < K; k++) v += L->conv_state[(size_t)ch * K + k] * L->conv_w[(size_t)ch * K + k];
         xc[ch] = v / (1.0f + expf(-v));
     }
-    matvec(al, L->alpha_w, x, H, d);
-    matvec(be, L->beta_w, x, H, d);
+    matvec_w(m, al, L->alpha_w, x, H, d);
+    matvec_w(m, be, L->beta_w, x, H, d);
     const float eps = 1e-6f, scale = 1.0f / sqrtf((float)dk);
     for (int h = 0; h < H; h++) {
         int g = h % H;  /* num_k_heads == num_v_heads */
@@ -269,7 +326,7 @@ static void ssm_forward(or_model *m, or_layer *L, const float *x, float *out) {
     }
     for (int h = 0; h < H; h++) rmsnorm(y + h * dv, y + h * dv, L->ssm_norm, dv, c->rms_eps);
     for (int i = 0; i < inner; i++) y[i] = y[i] * z[i] * (1.0f / (1.0f + expf(-z[i])));
-    matvec(out, L->ssm_out, y, d, inner);
+    matvec_w(m, out, L->ssm_out, y, d, inner);
     free(qkv); free(z); free(xc); free(al); free(be); free(y); free(qn); free(kn); free(sk);
 }
 
@@ -331,9 +388,9 @@ static void attn_forward(or_model *m, or_layer *L, const float *x, int pos, floa
     float *qg = (float *)malloc((size_t)2 * nh * hd * 4), *k = (float *)malloc((size_t)nkv * hd * 4);
     float *v = (float *)malloc((size_t)nkv * hd * 4), *q = (float *)malloc((size_t)nh * hd * 4);
     float *gate = (float *)malloc((size_t)nh * hd * 4), *o = (float *)malloc((size_t)nh * hd * 4);
-    matvec(qg, L->wq, x, 2 * nh * hd, d);
-    matvec(k, L->wk, x, nkv * hd, d);
-    matvec(v, L->wv, x, nkv * hd, d);
+    matvec_w(m, qg, L->wq, x, 2 * nh * hd, d);
+    matvec_w(m, k, L->wk, x, nkv * hd, d);
+    matvec_w(m, v, L->wv, x, nkv * hd, d);
     for (int h = 0; h < nh; h++)
         for (int i = 0; i < hd; i++) {
             q[h * hd + i] = qg[(size_t)h * 2 * hd + i];
@@ -347,18 +404,18 @@ static void attn_forward(or_model *m, or_layer *L, const float *x, int pos, floa
     const float scale = 1.0f / sqrtf((float)hd);
     for (int h = 0; h < nh; h++) flash_attn(o + h * hd, q + h * hd, L->kc, L->vc, h / ratio, nkv, pos + 1, scale, hd);
     for (int i = 0; i < nh * hd; i++) o[i] *= 1.0f / (1.0f + expf(-gate[i]));
-    matvec(out, L->wo, o, d, nh * hd);
+    matvec_w(m, out, L->wo, o, d, nh * hd);
     free(qg); free(k); free(v); free(q); free(gate); free(o);
 }
 
 static void mlp_forward(or_model *m, or_layer *L, const float *x, float *out) {
     const int f = m->c.ffn, d = m->c.hidden;
     float *g = (float *)malloc(f * 4), *u = (float *)malloc(f * 4);
-    matvec(g, L->ffn_gate, x, f, d);
+    matvec_w(m, g, L->ffn_gate, x, f, d);
     for (int i = 0; i < f; i++) g[i] = g[i] / (1.0f + expf(-g[i]));
-    matvec(u, L->ffn_up, x, f, d);
+    matvec_w(m, u, L->ffn_up, x, f, d);
     for (int i = 0; i < f; i++) g[i] = g[i] * u[i];
-    matvec(out, L->ffn_down, g, d, f);
+    matvec_w(m, out, L->ffn_down, g, d, f);
     free(g); free(u);
 }
 
@@ -385,7 +442,7 @@ int or_forward_token(or_model *m, int token, int pos, float *logits, float *hidd
     for (int i = 0; i < c->n_layers; i++) decoder_layer(m, &m->layers[i], x, pos);
     rmsnorm(xn, x, m->final_norm, d, c->rms_eps);
     if (hidden) memcpy(hidden, xn, d * 4);
-    if (logits) matvec(logits, m->embed, xn, c->vocab, d);
+    if (logits) matvec_w(m, logits, m->embed, xn, c->vocab, d);
     free(x); free(xn);
     return 0;
 }
@@ -398,11 +455,11 @@ int or_mtp_step(or_model *m, int token, const float *hidden, int pos, float *log
     float *cat = (float *)malloc(2 * d * 4), *x = (float *)malloc(d * 4), *xn = (float *)malloc(d * 4);
     rmsnorm(cat, m->embed + (size_t)token * d, m->mtp_norm_e, d, c->rms_eps);
     rmsnorm(cat + d, hidden, m->mtp_norm_h, d, c->rms_eps);
-    matvec(x, m->mtp_fc, cat, d, 2 * d);
+    matvec_w(m, x, m->mtp_fc, cat, d, 2 * d);
     decoder_layer(m, &m->mtp_layer, x, pos);
     if (hidden_out) memcpy(hidden_out, x, d * 4);
     rmsnorm(xn, x, m->mtp_norm, d, c->rms_eps);
-    if (logits) matvec(logits, m->embed, xn, c->vocab, d);
+    if (logits) matvec_w(m, logits, m->embed, xn, c->vocab, d);
     free(cat); free(x); free(xn);
     return 0;
 }

@@ -41,8 +41,13 @@ int or_quantize(int type, const float *x, int64_t rows, int64_t cols, uint8_t *o
 int or_dequantize(int type, const uint8_t *blocks, int64_t n, float *out);
 
 /* Y[n][r] = sum_k W[r][k] * X[n][k]; W quantized rows x cols, X ncols x cols.
+ * or_gemm_q8k quantizes each activation column to Q8_K first (the reference's
+ * quantized kernels, K-quant weights only) and then accumulates in double,
  * or_gemm_f64 accumulates the dequantized f32 weights in double ("truth"),
  * or_gemm_f32 accumulates in float, index order (the reference's fallback). */
+void or_quantize_q8k(const float *x, int64_t k, float *d, int8_t *q);
+int or_gemm_q8k(int type, const uint8_t *W, int64_t rows, int64_t cols,
+                const float *X, int ncols, double *Y);
 int or_gemm_f64(int type, const uint8_t *W, int64_t rows, int64_t cols,
                 const float *X, int ncols, double *Y);
 int or_gemm_f32(int type, const uint8_t *W, int64_t rows, int64_t cols,
@@ -79,6 +84,7 @@ or_model *or_model_new(const or_model_config *c);
 void or_model_free(or_model *m);
 /* layer >= 0: decoder layer; -1: global tensors; -2: the MTP decoder layer */
 int  or_model_set(or_model *m, int layer, int kind, int type, const void *data, int64_t n);
+void or_model_set_activation(or_model *m, int mode);  /* 0 exact f32 (default), 1 Q8_K */
 void or_model_reset(or_model *m);
 int  or_forward_token(or_model *m, int token, int pos, float *logits, float *hidden);
 int  or_mtp_step(or_model *m, int token, const float *hidden, int pos, float *logits, float *hidden_out);

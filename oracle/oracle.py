@@ -48,6 +48,9 @@ def lib():
         L.or_quantize.argtypes = [ctypes.c_int, _fp, i64, i64, _u8p]
         L.or_dequantize.argtypes = [ctypes.c_int, _u8p, i64, _fp]
         L.or_gemm_f64.argtypes = [ctypes.c_int, _u8p, i64, i64, _fp, ctypes.c_int, _dp]
+        L.or_gemm_q8k.argtypes = [ctypes.c_int, _u8p, i64, i64, _fp, ctypes.c_int, _dp]
+        L.or_quantize_q8k.argtypes = [_fp, i64, _fp, ctypes.POINTER(ctypes.c_int8)]
+        L.or_quantize_q8k.restype = None
         L.or_gemm_f32.argtypes = [ctypes.c_int, _u8p, i64, i64, _fp, ctypes.c_int, _fp]
         L.or_exp.restype = ctypes.c_float
         L.or_exp.argtypes = [ctypes.c_float]
@@ -112,6 +115,33 @@ def gemm_f64(qtype, W, rows, cols, X):
     return Y
 
 
+def gemm_q8k(qtype, W, rows, cols, X):
+    """K-quant weights against Q8_K-quantised activations, f64 sums"""
+    X = np.ascontiguousarray(X, dtype=np.float32).reshape(-1, cols)
+    Y = np.empty((X.shape[0], rows), dtype=np.float64)
+    assert lib().or_gemm_q8k(qtype, _p(np.ascontiguousarray(W), _u8p), rows, cols,
+                             _p(X, _fp), X.shape[0], _p(Y, _dp)) == 0
+    return Y
+
+
+def gemm_ref(qtype, W, rows, cols, X, act=0):
+    """the GPU GEMV's semantics: exact f32 activations (act 0, default), or for
+    the K-quants Q8_K activations (act 1, the reference's q4_k_gemv ..
+    q6_k_gemv); Q8_0 always exact (the reference's q8_0_gemv)"""
+    if qtype == 8 or act == 0:
+        return gemm_f64(qtype, W, rows, cols, X)
+    return gemm_q8k(qtype, W, rows, cols, X)
+
+
+def quantize_q8k(x):
+    """quantize_row_q8_K restated: (d per 256 block, int8 values)"""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    d = np.empty(len(x) // 256, np.float32)
+    q = np.empty(len(x), np.int8)
+    lib().or_quantize_q8k(_p(x, _fp), len(x), _p(d, _fp), q.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)))
+    return d, q
+
+
 def gemm_f32(qtype, W, rows, cols, X):
     X = np.ascontiguousarray(X, dtype=np.float32).reshape(-1, cols)
     Y = np.empty((X.shape[0], rows), dtype=np.float32)
@@ -133,6 +163,22 @@ def ref_gemv(qtype, W, rows, cols, x):
         fn = {Q4_K: R.q4_k_gemv, Q5_K: R.q5_k_gemv, Q6_K: R.q6_k_gemv}[qtype]
         fn(_p(W, _u8p), _p(x, _fp), _p(out, _fp), _p(scratch, _u8p), cols, rows)
     return out
+
+
+def ref_quantize_q8k(x):
+    """quantize_row_q8_K of the reference (oracle/_ref): (d per block, int8),
+    or None when oracle/_ref is not built"""
+    if not os.path.exists(REF_PATH):
+        return None
+    R = ref()
+    R.quantize_row_q8_K.argtypes = [_fp, _u8p, ctypes.c_int64]
+    R.quantize_row_q8_K.restype = None
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    nb = len(x) // 256
+    buf = np.empty(nb * 292, np.uint8)  # block_q8_K: f32 d, int8 qs[256], int16 bsums[16]
+    R.quantize_row_q8_K(_p(x, _fp), _p(buf, _u8p), len(x))
+    blocks = buf.reshape(nb, 292)
+    return blocks[:, :4].copy().view(np.float32).ravel(), blocks[:, 4:260].copy().view(np.int8).ravel()
 
 
 def exp(x):
@@ -212,6 +258,8 @@ def _model_lib():
         L.or_model_set.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                    ctypes.c_int64]
         L.or_model_reset.argtypes = [ctypes.c_void_p]
+        L.or_model_set_activation.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.or_model_set_activation.restype = None
         L.or_forward_token.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _fp, _fp]
         L.or_mtp_step.argtypes = [ctypes.c_void_p, ctypes.c_int, _fp, ctypes.c_int, _fp, _fp]
         L.or_snapshot_take.restype = ctypes.c_void_p

@@ -335,6 +335,53 @@ int or_gemm_f64(int type, const uint8_t *W, int64_t rows, int64_t cols,
     return 0;
 }
 
+/* quantize_row_q8_K (src/kernels/quant_kernels.c:166-194): per block of 256,
+ * d = amax / 127, q = roundf(x * (1/d)) (0 when amax is 0), f32 throughout */
+void or_quantize_q8k(const float *x, int64_t k, float *d, int8_t *q) {
+    for (int64_t b = 0; b < k / QK_K; b++) {
+        const float *s = x + QK_K * b;
+        float amax = 0.f;
+        for (int j = 0; j < QK_K; j++) {
+            const float a = fabsf(s[j]);
+            if (a > amax) amax = a;
+        }
+        const float dd = amax / 127.0f;
+        const float id = dd != 0.f ? 1.0f / dd : 0.f;
+        d[b] = dd;
+        for (int j = 0; j < QK_K; j++) q[QK_K * b + j] = (int8_t)roundf(s[j] * id);
+    }
+}
+
+/* The reference's quantized matvec (q4_k_gemv .. q6_k_gemv, quant_kernels.c:602-650):
+ * activations quantized to Q8_K, then sum_b d8_b * sum_{k in b} w[k] q8[k], here in
+ * double over the dequantized weights ("truth" for the quantized activations). */
+int or_gemm_q8k(int type, const uint8_t *W, int64_t rows, int64_t cols,
+                const float *X, int ncols, double *Y) {
+    int64_t rb = or_row_bytes(type, cols);
+    if (rb == 0 || cols % QK_K || type == OR_Q8_0) return -1;
+    const int64_t nb = cols / QK_K;
+    float *w = (float *)malloc((size_t)cols * sizeof(float));
+    float *d8 = (float *)malloc((size_t)nb * ncols * sizeof(float));
+    int8_t *q8 = (int8_t *)malloc((size_t)cols * ncols);
+    if (!w || !d8 || !q8) { free(w); free(d8); free(q8); return -2; }
+    for (int n = 0; n < ncols; n++) or_quantize_q8k(X + (int64_t)n * cols, cols, d8 + nb * n, q8 + cols * n);
+    for (int64_t r = 0; r < rows; r++) {
+        if (or_dequantize(type, W + r * rb, cols, w)) { free(w); free(d8); free(q8); return -1; }
+        for (int n = 0; n < ncols; n++) {
+            const int8_t *q = q8 + cols * n;
+            double acc = 0.0;
+            for (int64_t b = 0; b < nb; b++) {
+                double s = 0.0;
+                for (int j = 0; j < QK_K; j++) s += (double)w[QK_K * b + j] * (double)q[QK_K * b + j];
+                acc += (double)d8[nb * n + b] * s;
+            }
+            Y[(int64_t)n * rows + r] = acc;
+        }
+    }
+    free(w); free(d8); free(q8);
+    return 0;
+}
+
 int or_gemm_f32(int type, const uint8_t *W, int64_t rows, int64_t cols,
                 const float *X, int ncols, float *Y) {
     int64_t rb = or_row_bytes(type, cols);
