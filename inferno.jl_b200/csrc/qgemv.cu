@@ -878,17 +878,14 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
 }
 
-// Work split: UW warps share each row block's units; two M-tiles per warp and
-// stage unless that leaves fewer than half the SMs busy, then one (twice the
-// CTAs, half the serial work per warp).
+// Work split: UW warps share each row block's units, two M-tiles per warp and
+// stage.  (One M-tile per warp doubles the CTAs of small matrices, but measured
+// over a whole decode step it is slower: more kernel variants in flight.)
 template <int FMT, int NT, int XF, int ACT>
 static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                           cudaStream_t s, const XForm &xf) {
     int UW = 1;
     while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
-    const int64_t nrg2 = (T.nrb + 16 / UW - 1) / (16 / UW);
-    if (UW == 8 && 2 * nrg2 < num_sms() && !xf.ep)
-        return launch_mpw<FMT, NT, XF, 1, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
     return launch_mpw<FMT, NT, XF, 2, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
 }
 
