@@ -100,14 +100,26 @@ int ifr_tensor_info(const ifr_tensor *t, int *type, int64_t *rows, int64_t *cols
 int ifr_dequant(ifr_ctx *ctx, const ifr_tensor *t, float *dev_out);
 
 /* Y = W * X for ncols verify columns (any ncols >= 1; passes of 8).
- * X must be 16-byte aligned.  K-quants: int8 activations in the context's
- * activation mode (ifr_ctx_set_activation) on the integer tensor cores, exact
- * integer sub-block sums, f32 scaling and accumulation; Q8_0: f32 activations
- * split exactly into fp16 hi + lo on the fp16 tensor cores.  Replaces
- * q4_k_gemv/q5_k_gemv/q6_k_gemv/q8_0_gemv (src/kernels/quant_kernels.c:602-697),
- * called once per column by the reference (src/ModelCPU.jl:285-379). */
+ * X [ncols][cols] and Y [ncols][rows] f32 on the device, X 16-byte aligned.
+ * K-quants use the context's activation mode (ifr_ctx_set_activation): exact
+ * f32 products by default, or the reference's Q8_K quantized activations;
+ * Q8_0 always exact.  f32 accumulation.  Replaces q4_k_gemv/q5_k_gemv/
+ * q6_k_gemv/q8_0_gemv (src/kernels/quant_kernels.c:602-697), which the
+ * reference calls once per column (src/ModelCPU.jl:285-379). */
 int ifr_qgemm(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
               float *Y_dev);
+
+/* Y = W * X for many columns at once (batched verify across requests, prompt
+ * chunks) on the tcgen05 tensor cores: every weight is its exact dequantized
+ * value rounded to fp16, every activation column is scaled by a power of two
+ * and rounded to fp16, products are summed in f32 (relative error of each
+ * product <= 2^-10).  Same arguments as ifr_qgemm; uses the context's scratch
+ * (allocated on first use, or by ifr_ctx_reserve_dense).  Replaces the same
+ * per-column calls as ifr_qgemm, once ncols makes the contraction dense. */
+int ifr_qgemm_dense(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
+                    float *Y_dev);
+/* pre-size the scratch of ifr_qgemm_dense for W and up to ncols columns */
+int ifr_ctx_reserve_dense(ifr_ctx *ctx, const ifr_tensor *W, int ncols);
 
 /* host-side quantizer (f32 rows -> GGUF blocks of `type`), the library's own
  * encoder (the reference has none); multithreaded, no device needed */

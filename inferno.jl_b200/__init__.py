@@ -153,6 +153,17 @@ class Context:
         check(load().ifr_qgemm(self.handle, W.handle, _ptr(X), n, _ptr(out)))
         return out
 
+    def qgemm_dense(self, W, X, out=None):
+        """X [ncols, cols] f32 (device) -> Y [ncols, rows] on the tensor cores
+        (fp16 operands, f32 accumulation)"""
+        torch = self.torch
+        assert X.dtype == torch.float32 and X.is_contiguous() and X.shape[-1] == W.cols
+        n = X.numel() // W.cols
+        if out is None:
+            out = torch.empty(n, W.rows, dtype=torch.float32, device=X.device)
+        check(load().ifr_qgemm_dense(self.handle, W.handle, _ptr(X), n, _ptr(out)))
+        return out
+
     def accept(self, target, draft, uniforms, temperature, draft_tokens=None):
         """sampled verification; returns (accept_count, out_tokens, draft_tokens)"""
         torch = self.torch

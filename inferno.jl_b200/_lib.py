@@ -35,6 +35,8 @@ SIGNATURES = {
                              ctypes.POINTER(_i64)]),
     "ifr_dequant": (_i, [_vp, _vp, _vp]),
     "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "ifr_qgemm_dense": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "ifr_ctx_reserve_dense": (_i, [_vp, _vp, _i]),
     "ifr_quantize": (_i, [_i, _vp, _i64, _i64, _vp]),
     "ifr_accept": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
     "ifr_ctx_set_activation": (_i, [_vp, _i]),

@@ -316,6 +316,29 @@ int ifr_qgemm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float 
     return IFR_OK;
 }
 
+int ifr_ctx_reserve_dense(ifr_ctx *c, const ifr_tensor *W, int ncols) {
+    if (!c || !W) return fail(IFR_ERR_ARG, "NULL argument");
+    if (ncols < 1) return fail(IFR_ERR_ARG, "ncols must be >= 1 (got %d)", ncols);
+    const int64_t need = ifr::qgemm_dense_scratch_bytes(W->q, ncols);
+    if (need < 0) return fail(IFR_ERR_ARG, "no dense plan for this tensor and ncols=%d", ncols);
+    DeviceGuard g(c->device);
+    return ensure_scratch(c, (size_t)need);
+}
+
+int ifr_qgemm_dense(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float *Y) {
+    if (!c || !W || !X || !Y) return fail(IFR_ERR_ARG, "NULL argument");
+    if (ncols < 1) return fail(IFR_ERR_ARG, "ncols must be >= 1 (got %d)", ncols);
+    if (W->device != c->device) return fail(IFR_ERR_ARG, "tensor lives on device %d, context on %d", W->device, c->device);
+    if (((uintptr_t)X & 15) || ((uintptr_t)Y & 3)) return fail(IFR_ERR_ARG, "X must be 16-byte and Y 4-byte aligned");
+    int rc = ifr_ctx_reserve_dense(c, W, ncols);
+    if (rc) return rc;
+    DeviceGuard g(c->device);
+    IFR_CHECK_CUDA(ifr::qgemm_dense(W->q, X, ncols, Y, false, W->q.rows, c->stream, ifr::XForm(), c->scratch,
+                                    (int64_t)c->scratch_cap),
+                   "qgemm_dense launch");
+    return IFR_OK;
+}
+
 int ifr_quantize(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out) {
     if (!x || !out) return fail(IFR_ERR_ARG, "NULL argument");
     if (!valid_type(type)) return fail(IFR_ERR_ARG, "unsupported weight type %d", type);

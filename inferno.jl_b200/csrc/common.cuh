@@ -49,6 +49,13 @@ struct XForm {
 // Y[ncols][rows] (+)= W * f(X), ncols <= 8 per call; X 16-byte aligned, ldx a multiple of 4
 cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                         cudaStream_t s, const XForm &xf = XForm());
+// Dense path for many columns (qmma.cu): tcgen05 tensor cores, fp16 operands
+// (weights = exact dequantized values rounded to fp16; activations scaled by a
+// power of two per column), f32 accumulation.  scratch >= qgemm_dense_scratch_bytes.
+cudaError_t qgemm_dense(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                        cudaStream_t s, const XForm &xf, void *scratch, int64_t scratch_bytes);
+int64_t qgemm_dense_scratch_bytes(const QTensor &t, int ncols);  // -1: unsupported
+cudaError_t read_mma_error(int *flag, cudaStream_t s);
 // host encoder (encode.cpp): 0 on success
 int quantize_host(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
 // device-side error flag set by bounded waits that ran out (read and cleared)

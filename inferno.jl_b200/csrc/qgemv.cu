@@ -929,6 +929,9 @@ cudaError_t read_device_error(int *flag, cudaStream_t s) {
     cudaError_t e = cudaMemcpyFromSymbolAsync(flag, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    int f2 = 0;
+    if (e == cudaSuccess) e = read_mma_error(&f2, s);
+    if (f2) *flag = 1;
     return e;
 }
 
