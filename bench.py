@@ -587,15 +587,16 @@ def run_profile(args):
     t = ctx.upload(qt, make_weights(pkg, qt, M, K, rng), M, K)
     X = torch.from_numpy(rng.normal(0, 1, (args.ncols, K)).astype(np.float32)).cuda()
     Y = torch.empty(args.ncols, M, device="cuda")
+    run = ctx.qgemm_dense if args.profile == "dense" else ctx.qgemm
     for _ in range(3):
-        ctx.qgemm(t, X, Y)
+        run(t, X, Y)
     torch.cuda.synchronize()
     torch.cuda.profiler.start()
     for _ in range(3):
-        ctx.qgemm(t, X, Y)
+        run(t, X, Y)
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
-    print(json.dumps({"profile": "qgemv", "qtype": args.qtype, "shape": [M, K], "ncols": args.ncols,
+    print(json.dumps({"profile": args.profile, "qtype": args.qtype, "shape": [M, K], "ncols": args.ncols,
                       "weight_bytes": int(M * K * BPW[qt])}))
 
 
@@ -610,7 +611,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--act", type=int, default=0, choices=[0, 1],
                     help="K-quant GEMV activations: 0 = exact f32 (default), 1 = Q8_K (the reference's kernels)")
-    ap.add_argument("--profile", choices=["spec", "qgemv"], help="small case for ncu (no JSON line)")
+    ap.add_argument("--profile", choices=["spec", "qgemv", "dense"], help="small case for ncu (no JSON line)")
     ap.add_argument("--qtype", default="Q4_K")
     ap.add_argument("--shape", default="65536x4096")
     ap.add_argument("--ncols", type=int, default=5)

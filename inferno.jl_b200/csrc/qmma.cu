@@ -4,20 +4,24 @@
 // Q6_K / Q8_0 (M-tile layout, tiles.cuh).  The N <= 8 verify GEMV (qgemv.cu)
 // is HBM-bound; here the contraction is dense enough for the tensor cores.
 //
-// Precision (stated; this is not the exact path): every weight is its exact
-// dequantized value (src/Dequant.jl:304-601) rounded once to fp16; every
-// activation column is scaled by a power of two (max |x| -> [2^13, 2^14)) and
-// rounded to fp16; products are summed in f32 in tensor memory.
+// Precision (stated; this is not the exact path): weights are formed in fp16
+// from their exact integer quants - Q4_K/Q5_K fma(q, fp16(d sc), -fp16(dmin m)),
+// Q6_K (q - 32) fp16(d sc), Q8_0 q d, each rounded once - and every activation
+// column is scaled by a power of two (max |x| -> [2^13, 2^14)) and rounded to
+// fp16; products are summed in f32 in tensor memory.
 //
-// One CTA computes 128 output rows x one tile of up to 256 columns over a
-// range of K units (split-K over blockIdx.y when rows alone give too few CTAs):
-//   warp 0     producer: cp.async.bulk of the raw M-tiles of each 256-column
-//              unit (ring of 2) and of the packed fp16 activations of each
-//              64-column K stage (ring of ST), completion on mbarriers;
-//   warp 1     allocates the accumulator in tensor memory; one thread issues
-//              tcgen05.mma (M = 128, N = npad, K = 16) four times per stage and
-//              tcgen05.commit, which frees the stage when the MMAs are done;
-//   warps 2-9  dequantize each stage's 128 x 64 weights into the canonical
+// One CTA computes 128 output rows x a tile of up to 512 columns (MMA chunks
+// of <= 256) over a range of K units (split-K over blockIdx.y when the rows
+// alone give too few CTAs):
+//   warp 0     weight producer: cp.async.bulk of the raw M-tiles of each
+//              256-column unit into a ring of 2-3 slots (no dependency on the
+//              previous kernel, so it runs ahead from the first cycle);
+//   warp 1     allocates the accumulators in tensor memory; one thread issues
+//              tcgen05.mma (M = 128, N = chunk, K = 16) per chunk, four K steps
+//              per stage, and tcgen05.commit, which frees the stage;
+//   warp 2     activation producer: cp.async.bulk of the packed fp16
+//              activations of each 64-wide K stage (ring of ST);
+//   warps 3-18 dequantize each stage's 128 x 64 weights into the canonical
 //              K-major (no swizzle) shared-memory layout of the MMA, then read
 //              the f32 accumulators back (tcgen05.ld) and write Y or the split
 //              partials.
@@ -32,19 +36,24 @@
 #include "common.cuh"
 #include "tiles.cuh"
 
+#include <type_traits>
+
 namespace ifr {
 
 __device__ int g_mma_error = 0;
 
 namespace {
 
-constexpr int kDqWarps = 8;
+constexpr int kDqWarps = 16;
 constexpr int kDqThreads = 32 * kDqWarps;
-constexpr int kMmaThreads = 64 + kDqThreads;
+constexpr int kMmaThreads = 96 + kDqThreads;  // producer, MMA, activation producer, dequant warps
+constexpr int kMaxRaw = 3;                    // raw weight ring slots (units)
+constexpr int kMaxStages = 4;                 // operand stages (64-wide K)
 constexpr int kBM = 128;                 // rows per CTA (8 row blocks)
-constexpr int kBK = 64;                  // K per stage (4 MMAs of K = 16)
-constexpr int kRawSlots = 2;
-constexpr int kAStage = kBM * kBK * 2;   // fp16 A tile, 16 KB
+// A tile: 8 K-chunks of 128 rows x 16 bytes; chunks 2112 bytes apart (2048 + 64)
+// so that the two halves of a warp's 64-bit stores hit disjoint banks
+constexpr int kALbo = 2112;
+constexpr int kAStage = 7 * kALbo + kBM * 16 + 64;  // 16896 bytes
 constexpr int kMaxSmem = 232448;         // 227 KB per block
 constexpr long long kMmaWait = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -145,7 +154,6 @@ IFR_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 IFR_DEV uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 IFR_DEV uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
 IFR_DEV uint32_t wsel(const uint4 &v, int w) { return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w; }
-IFR_DEV int byte_at(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
 IFR_DEV uint32_t pack_h2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -155,97 +163,187 @@ IFR_DEV uint32_t pack_h2(float lo, float hi) {
 // ---- dequantization of one piece ------------------------------------------------
 // A piece is (M-tile row r, lane quad t) of one 64-element K stage p of a unit:
 // the 16 elements 64 p + 16 w + 4 t + b (run w = 0..3, b = 0..3), exactly the
-// bytes the M-tile keeps together for t (tiles.cuh).  v[4 w + b] gets the
-// exact f32 value of src/Dequant.jl (separately rounded products).
-template <bool Q5>
-IFR_DEV void piece_qk(const uint8_t *tile, int r, int t, int p, float (&v)[16]) {
-    const uint4 h = lds128(tile + qk_hdr(r));
-    const float d = h2f((uint16_t)(h.x & 0xffffu)), dmin = h2f((uint16_t)(h.x >> 16));
-    // 6-bit scales and mins (src/Dequant.jl:345-362), byte j of word j / 4
-    const uint32_t sc0 = h.y & 0x3f3f3f3fu, mn0 = h.z & 0x3f3f3f3fu;
-    const uint32_t sc1 = (h.w & 0x0f0f0f0fu) | (((h.y >> 6) & 0x03030303u) << 4);
-    const uint32_t mn1 = ((h.w >> 4) & 0x0f0f0f0fu) | (((h.z >> 6) & 0x03030303u) << 4);
-    const int cl = 2 * p, ch = 2 * p + 1;  // sub-blocks of the low and high nibbles
-    const float dl = __fmul_rn(d, (float)byte_at(cl < 4 ? sc0 : sc1, cl & 3));
-    const float ml = __fmul_rn(dmin, (float)byte_at(cl < 4 ? mn0 : mn1, cl & 3));
-    const float dh = __fmul_rn(d, (float)byte_at(ch < 4 ? sc0 : sc1, ch & 3));
-    const float mh = __fmul_rn(dmin, (float)byte_at(ch < 4 ? mn0 : mn1, ch & 3));
-    // raw qs bytes 32 p + 16 hh + 4 t + b (hh = 0, 1): low nibble element 64 p + 16 hh + 4 t + b,
-    // high nibble element 64 p + 32 + 16 hh + 4 t + b
-    const uint2 q = lds64(tile + qk_qs(Q5, p >> 1, r, t) + 8 * (p & 1));
-    uint2 qh = make_uint2(0u, 0u);
-    if (Q5) qh = lds64(tile + q5_qh(r & 7, t) + 8 * (r >> 3));
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-        const uint32_t W = hh ? q.y : q.x, H = hh ? qh.y : qh.x;
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-            int lo = (int)((W >> (8 * b)) & 15u), hi = (int)((W >> (8 * b + 4)) & 15u);
-            if (Q5) {
-                lo += (int)((H >> (8 * b + cl)) & 1u) << 4;
-                hi += (int)((H >> (8 * b + ch)) & 1u) << 4;
-            }
-            v[4 * hh + b] = __fsub_rn(__fmul_rn(dl, (float)lo), ml);
-            v[8 + 4 * hh + b] = __fsub_rn(__fmul_rn(dh, (float)hi), mh);
-        }
-    }
+// bytes the M-tile keeps together for t (tiles.cuh).  out[2 w], out[2 w + 1]
+// hold run w as fp16 pairs (b = 0, 2) and (b = 1, 3): the MMA's K slots of
+// every group of four hold the elements (0, 2, 1, 3), and the activations are
+// packed in the same order.  Arithmetic in fp16 from exact integers
+// (magic-number unpack): Q4_K/Q5_K fma(q, fp16(d sc), -fp16(dmin m)), Q6_K
+// (q - 32) fp16(d sc), Q8_0 q d, each rounded once.
+constexpr uint32_t kMagic = 0x64006400u;  // (1024, 1024)
+
+IFR_DEV uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+IFR_DEV uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+IFR_DEV uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+IFR_DEV uint32_t and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));
+    return r;
 }
 
-// Q6_K (src/Dequant.jl:558-601): element e = 64 p + 32 j + 16 hh + 4 t + b is raw
-// ql byte 64 (p / 2) + 32 j + 16 hh + 4 t + b >> 4 (p % 2), raw qh byte
-// 32 (p / 2) + 16 hh + 4 t + b >> (4 (p % 2) + 2 j), scale group 4 p + 2 j + hh
-IFR_DEV void piece_q6(const uint8_t *tile, int r, int t, int p, float (&v)[16]) {
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(r)));
-    const uint4 sc = lds128(tile + q6_sc(r));
-    const uint4 ql = lds128(tile + q6_ql(p >> 1, r, t));
-    const uint2 qh = lds64(tile + q6_qh(r, t) + 8 * (p >> 1));
-    const int sl = 4 * (p & 1);
+// fp16 pair (lo, hi) of bytes a and b of w (0 <= byte <= 255 exactly)
+IFR_DEV uint32_t byte_pair_h2(uint32_t w, uint32_t sel) { return hsub2(__byte_perm(w, 0u, sel) | kMagic, kMagic); }
+constexpr uint32_t kSelB01 = 0x4140u, kSelB23 = 0x4342u;   // bytes (0, 1), (2, 3) into the two halves
+IFR_DEV uint32_t dup_lo(uint32_t h2) { return __byte_perm(h2, 0u, 0x1010u); }
+IFR_DEV uint32_t dup_hi(uint32_t h2) { return __byte_perm(h2, 0u, 0x3232u); }
+
+// Per-thread dequantizer of one piece (M-tile row r, lane quad t) across the
+// four stages p = 0..3 of a unit: unit() decodes the block header once,
+// stage(p) produces the 16 fp16 weights of stage p.
+template <bool Q5>
+struct DeqK {
+    const uint8_t *tile;
+    int r, t;
+    uint32_t dsc[4], nmn[4];  // (sub-blocks 2p, 2p+1): fp16(d sc), -fp16(dmin m)
+    uint2 qh;
+    uint4 qs;                 // qs piece of stages 2q, 2q+1
+    IFR_DEV void unit(const uint8_t *tl, int r_, int t_) {
+        tile = tl;
+        r = r_;
+        t = t_;
+        const uint4 h = lds128(tile + qk_hdr(r));
+        const uint32_t dd = (h.x & 0xffffu) * 0x10001u, dm = (h.x >> 16) * 0x10001u;
+        // 6-bit scales and mins (src/Dequant.jl:345-362), byte j of word j / 4
+        const uint32_t sc0 = h.y & 0x3f3f3f3fu, mn0 = h.z & 0x3f3f3f3fu;
+        const uint32_t sc1 = (h.w & 0x0f0f0f0fu) | (((h.y >> 6) & 0x03030303u) << 4);
+        const uint32_t mn1 = ((h.w >> 4) & 0x0f0f0f0fu) | (((h.z >> 6) & 0x03030303u) << 4);
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
+        for (int p = 0; p < 4; p++) {
+            const uint32_t sel = (p & 1) ? kSelB23 : kSelB01;
+            dsc[p] = hmul2(byte_pair_h2(p < 2 ? sc0 : sc1, sel), dd);
+            nmn[p] = hmul2(byte_pair_h2(p < 2 ? mn0 : mn1, sel), dm) ^ 0x80008000u;
+        }
+        if (Q5) qh = lds64(tile + q5_qh(r & 7, t) + 8 * (r >> 3));
+    }
+    // raw qs bytes 32 p + 16 hh + 4 t + b: low nibble element 64 p + 16 hh + 4 t + b,
+    // high nibble element 64 p + 32 + 16 hh + 4 t + b
+    IFR_DEV void stage(int p, uint32_t (&o)[8]) {
+        if ((p & 1) == 0) qs = lds128(tile + qk_qs(Q5, p >> 1, r, t));
+        const uint32_t dl = dup_lo(dsc[p]), dh = dup_hi(dsc[p]), ml = dup_lo(nmn[p]), mh = dup_hi(nmn[p]);
+        const int cl = 2 * p, ch = 2 * p + 1;
 #pragma unroll
         for (int hh = 0; hh < 2; hh++) {
-            const uint32_t L = wsel(ql, 2 * j + hh), H = hh ? qh.y : qh.x;
-            const int g = 4 * p + 2 * j + hh;
-            const float ds = __fmul_rn(d, (float)(int8_t)byte_at(wsel(sc, g >> 2), g & 3));
+            const uint32_t W = (p & 1) ? (hh ? qs.w : qs.z) : (hh ? qs.y : qs.x);
+            uint32_t l02 = and_or(W, 0x000F000Fu, kMagic), l13 = and_or(W >> 8, 0x000F000Fu, kMagic);
+            uint32_t h02 = and_or(W >> 4, 0x000F000Fu, kMagic), h13 = and_or(W >> 12, 0x000F000Fu, kMagic);
+            if (Q5) {
+                // fifth bit: bit (sub-block) of qh byte b -> +16
+                const uint32_t H = hh ? qh.y : qh.x;
+                l02 |= ((H >> cl) & 0x00010001u) << 4;
+                l13 |= ((H >> (8 + cl)) & 0x00010001u) << 4;
+                h02 |= ((H >> ch) & 0x00010001u) << 4;
+                h13 |= ((H >> (8 + ch)) & 0x00010001u) << 4;
+            }
+            o[2 * hh] = hfma2(hsub2(l02, kMagic), dl, ml);
+            o[2 * hh + 1] = hfma2(hsub2(l13, kMagic), dl, ml);
+            o[4 + 2 * hh] = hfma2(hsub2(h02, kMagic), dh, mh);
+            o[4 + 2 * hh + 1] = hfma2(hsub2(h13, kMagic), dh, mh);
+        }
+    }
+};
+
+// Q6_K (src/Dequant.jl:558-601): element 64 p + 32 j + 16 hh + 4 t + b is raw ql
+// byte 64 (p / 2) + 32 j + 16 hh + 4 t + b >> 4 (p % 2), raw qh byte
+// 32 (p / 2) + 16 hh + 4 t + b >> (4 (p % 2) + 2 j), scale group 4 p + 2 j + hh
+struct DeqQ6 {
+    const uint8_t *tile;
+    int r, t;
+    uint32_t ds[8];  // (groups 2i, 2i+1): fp16(d sc)
+    uint4 qh, ql;
+    IFR_DEV void unit(const uint8_t *tl, int r_, int t_) {
+        tile = tl;
+        r = r_;
+        t = t_;
+        const uint32_t dd = (uint32_t)(*reinterpret_cast<const uint16_t *>(tile + q6_d(r))) * 0x10001u;
+        const uint4 sc = lds128(tile + q6_sc(r));
+        constexpr uint32_t k1152 = 0x64806480u;  // (1024 + 128) x 2: int8 + 128 -> int8
 #pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const int q = (int)((L >> (8 * b + sl)) & 15u) | ((int)((H >> (8 * b + sl + 2 * j)) & 3u) << 4);
-                v[4 * (2 * j + hh) + b] = __fmul_rn(ds, (float)(q - 32));
+        for (int i = 0; i < 8; i++) {
+            const uint32_t b = (__byte_perm(wsel(sc, i >> 1), 0u, (i & 1) ? kSelB23 : kSelB01) ^ 0x00800080u) | kMagic;
+            ds[i] = hmul2(hsub2(b, k1152), dd);
+        }
+        qh = lds128(tile + q6_qh(r, t));
+    }
+    IFR_DEV void stage(int p, uint32_t (&o)[8]) {
+        constexpr uint32_t k1056 = 0x64206420u;  // (1024 + 32) x 2
+        if ((p & 1) == 0) ql = lds128(tile + q6_ql(p >> 1, r, t));
+        const int sl = 4 * (p & 1), n = p >> 1;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const uint32_t L = wsel(ql, 2 * j + hh) >> sl, H = wsel(qh, 2 * n + hh) >> (sl + 2 * j);
+                const uint32_t d2 = hh ? dup_hi(ds[2 * p + j]) : dup_lo(ds[2 * p + j]);
+                const uint32_t q02 = and_or(L, 0x000F000Fu, kMagic) | ((H << 4) & 0x00300030u);
+                const uint32_t q13 = and_or(L >> 8, 0x000F000Fu, kMagic) | ((H >> 4) & 0x00300030u);
+                o[2 * (2 * j + hh)] = hmul2(hsub2(q02, k1056), d2);
+                o[2 * (2 * j + hh) + 1] = hmul2(hsub2(q13, k1056), d2);
             }
         }
     }
-}
+};
 
 // Q8_0 (src/Dequant.jl:304-321): element 64 p + 16 w + 4 t + b of the unit is
 // byte b of word w of piece (p, r, t), block 2 p + w / 2
-IFR_DEV void piece_q8(const uint8_t *tile, int r, int t, int p, float (&v)[16]) {
-    const uint4 q = lds128(tile + q8_qs(p, r, t));
-    const uint32_t dd = *reinterpret_cast<const uint32_t *>(tile + q8_d(r) + 4 * p);  // blocks 2p, 2p+1
-    const float d0 = h2f((uint16_t)(dd & 0xffffu)), d1 = h2f((uint16_t)(dd >> 16));
-#pragma unroll
-    for (int w = 0; w < 4; w++) {
-        const uint32_t W = wsel(q, w);
-#pragma unroll
-        for (int b = 0; b < 4; b++) v[4 * w + b] = __fmul_rn(w < 2 ? d0 : d1, (float)(int8_t)byte_at(W, b));
+struct DeqQ8 {
+    const uint8_t *tile;
+    int r, t;
+    uint4 dd;  // block scales, blocks (2p, 2p+1) in word p
+    IFR_DEV void unit(const uint8_t *tl, int r_, int t_) {
+        tile = tl;
+        r = r_;
+        t = t_;
+        dd = lds128(tile + q8_d(r));
     }
-}
+    IFR_DEV void stage(int p, uint32_t (&o)[8]) {
+        constexpr uint32_t k1152 = 0x64806480u;  // (1024 + 128) x 2
+        const uint4 q = lds128(tile + q8_qs(p, r, t));
+        const uint32_t d0 = dup_lo(wsel(dd, p)), d1 = dup_hi(wsel(dd, p));
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const uint32_t W = wsel(q, w) ^ 0x80808080u;  // int8 + 128
+            o[2 * w] = hmul2(hsub2(and_or(W, 0x00FF00FFu, kMagic), k1152), w < 2 ? d0 : d1);
+            o[2 * w + 1] = hmul2(hsub2(and_or(W >> 8, 0x00FF00FFu, kMagic), k1152), w < 2 ? d0 : d1);
+        }
+    }
+};
 
 template <int FMT>
-IFR_DEV void dequant_piece(const uint8_t *tile, int r, int t, int p, float (&v)[16]) {
-    if constexpr (FMT == 12) piece_qk<false>(tile, r, t, p, v);
-    else if constexpr (FMT == 13) piece_qk<true>(tile, r, t, p, v);
-    else if constexpr (FMT == 14) piece_q6(tile, r, t, p, v);
-    else piece_q8(tile, r, t, p, v);
-}
+using Deq = std::conditional_t<FMT == 12, DeqK<false>,
+                               std::conditional_t<FMT == 13, DeqK<true>, std::conditional_t<FMT == 14, DeqQ6, DeqQ8>>>;
 
 }  // namespace
+
+// position in a ring of n slots: slot, and how often the ring has wrapped
+struct Ring {
+    int n, slot = 0, round = 0;
+    IFR_DEV void next() {
+        if (++slot == n) {
+            slot = 0;
+            ++round;
+        }
+    }
+    IFR_DEV uint32_t full_par() const { return (uint32_t)round & 1; }         // data of this round landed
+    IFR_DEV uint32_t empty_par() const { return (uint32_t)(round - 1) & 1; }  // previous round consumed
+};
 
 struct MmaArgs {
     const uint8_t *W;      // M-tiles
     int nrb, nu;           // row blocks of 16, units of 256
     const uint16_t *Xp;    // packed fp16 activations [ntiles][nu * 4][8][npad][8]
     const float *xinv;     // [ntiles * npad] 2^-e of each column
-    int ncols, npad, ntiles, splits, ST;
+    int ncols, npad, ntiles, nch, splits, RS, ST;
     float *Y;
     int64_t ldy, M;
     int accumulate, ep;
@@ -257,17 +355,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr int MTB = mtile_bytes(FMT);
     constexpr int RAW = 8 * MTB;
-    const int ST = a.ST, npad = a.npad;
+    const int RS = a.RS, ST = a.ST, npad = a.npad;
     uint64_t *raw_full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *raw_empty = raw_full + kRawSlots;
-    uint64_t *a_full = raw_empty + kRawSlots;
-    uint64_t *b_full = a_full + 4;
-    uint64_t *ab_empty = b_full + 4;
-    uint64_t *acc_full = ab_empty + 4;
+    uint64_t *raw_empty = raw_full + kMaxRaw;
+    uint64_t *a_full = raw_empty + kMaxRaw;
+    uint64_t *b_full = a_full + kMaxStages;
+    uint64_t *ab_empty = b_full + kMaxStages;
+    uint64_t *acc_full = ab_empty + kMaxStages;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *dead = reinterpret_cast<volatile int *>(tmem_holder + 1);
     uint8_t *raw = smem + 1024;
-    const int raw_bytes = (kRawSlots * RAW + 1023) & ~1023;
+    const int raw_bytes = (RS * RAW + 1023) & ~1023;
     const int bstage = npad * 128;
     const int stage_bytes = (kAStage + bstage + 1023) & ~1023;
     uint8_t *stages = raw + raw_bytes;
@@ -278,11 +376,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     const int nmt = min(8, a.nrb - rb0);
     const int u0 = (int)((int64_t)z * a.nu / a.splits), u1 = (int)((int64_t)(z + 1) * a.nu / a.splits);
     const int nunits = u1 - u0, nst = 4 * nunits;
-    const uint32_t tcols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
+    const uint32_t tcols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : npad <= 256 ? 256 : 512;
 
     pdl_trigger();
     if (tid == 0) {
-        for (int i = 0; i < kRawSlots; i++) {
+        for (int i = 0; i < RS; i++) {
             mb_init(raw_full + i, 1);
             mb_init(raw_empty + i, kDqThreads);
         }
@@ -302,106 +400,113 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     const uint32_t tmem = *tmem_holder;
 
     if (warp == 0) {
-        // ---------------- producer ----------------
+        // ---------------- weight producer (constant data: no dependency wait) ----------------
         if (lane == 0) {
-            int raw_uses[kRawSlots] = {0, 0}, b_uses[4] = {0, 0, 0, 0};
-            for (int i = 0; i < nunits && !*dead; i++) {
-                const int rs = i % kRawSlots;
-                if (i >= kRawSlots && !mb_wait(raw_empty + rs, (uint32_t)((i / kRawSlots) - 1) & 1, dead)) break;
+            Ring rr{RS};
+            const uint8_t *src = a.W + ((int64_t)rb0 * a.nu + u0) * MTB;
+            const int64_t rb_stride = (int64_t)a.nu * MTB;
+            int issued = 0;
+            for (int i = 0; i < nunits && !*dead; i++, rr.next(), src += MTB) {
+                if (rr.round > 0 && !mb_wait(raw_empty + rr.slot, rr.empty_par(), dead)) break;
                 fence_async_smem();
-                mb_expect_tx(raw_full + rs, (uint32_t)(nmt * MTB));
-                for (int m = 0; m < nmt; m++)
-                    bulk_copy(raw + rs * RAW + m * MTB, a.W + ((int64_t)(rb0 + m) * a.nu + u0 + i) * MTB, MTB,
-                              raw_full + rs);
-                raw_uses[rs]++;
-                // the weights are constant; the activations come from the previous kernel
-                if (i == 0) pdl_wait();
-                for (int j = 0; j < 4; j++) {
-                    const int q = 4 * i + j, st = q % ST;
-                    if (q >= ST && !mb_wait(ab_empty + st, (uint32_t)((q / ST) - 1) & 1, dead)) break;
-                    uint8_t *B = stages + st * stage_bytes + kAStage;
-                    mb_expect_tx(b_full + st, (uint32_t)bstage);
-                    const uint16_t *src = a.Xp + ((int64_t)nt * a.nu * 4 + 4 * (u0 + i) + j) * (int64_t)npad * 64;
-                    bulk_copy(B, src, (uint32_t)bstage, b_full + st);
-                    b_uses[st]++;
-                }
+                mb_expect_tx(raw_full + rr.slot, (uint32_t)(nmt * MTB));
+                uint8_t *dst = raw + rr.slot * RAW;
+                for (int m = 0; m < nmt; m++) bulk_copy(dst + m * MTB, src + m * rb_stride, MTB, raw_full + rr.slot);
+                issued = i + 1;
             }
-            if (nunits == 0) pdl_wait();
             // no copy may land after the CTA exits: a slot is reissued only after its
-            // previous contents were consumed, so only its last use can be in flight
-            for (int rs = 0; rs < kRawSlots; rs++)
-                if (raw_uses[rs] > 0) mb_drain(raw_full + rs, (uint32_t)(raw_uses[rs] - 1) & 1);
-            for (int st = 0; st < ST; st++)
-                if (b_uses[st] > 0) mb_drain(b_full + st, (uint32_t)(b_uses[st] - 1) & 1);
+            // previous contents were consumed, so only the last RS issues can be in flight
+            for (int k = 0; k < RS && k < issued; k++) {
+                const int i = issued - 1 - k;
+                mb_drain(raw_full + i % RS, (uint32_t)(i / RS) & 1);
+            }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = mma_idesc(npad);
-            for (int q = 0; q < nst; q++) {
-                const int st = q % ST;
-                const uint32_t par = (uint32_t)(q / ST) & 1;
-                if (!mb_wait(a_full + st, par, dead) || !mb_wait(b_full + st, par, dead)) break;
+            const int cw = npad / a.nch;
+            const uint32_t idesc = mma_idesc(cw);
+            const uint32_t s0 = su32(stages);
+            const uint64_t da = smem_desc(s0, kALbo, 128), db = smem_desc(s0 + kAStage, npad * 16, 128);
+            Ring ab{ST};
+            for (int q = 0; q < nst; q++, ab.next()) {
+                if (!mb_wait(a_full + ab.slot, ab.full_par(), dead) || !mb_wait(b_full + ab.slot, ab.full_par(), dead))
+                    break;
                 tc_fence_after();
-                const uint32_t A = su32(stages + st * stage_bytes), B = A + kAStage;
+                const uint32_t so = (uint32_t)(ab.slot * stage_bytes) >> 4;  // descriptor start fields advance in 16 B
 #pragma unroll
                 for (int s = 0; s < 4; s++)
-                    mma_f16(tmem, smem_desc(A + s * 2 * (kBM * 16), kBM * 16, 128),
-                            smem_desc(B + s * 2 * (npad * 16), npad * 16, 128), idesc, (q | s) != 0);
-                mma_commit(ab_empty + st);
+                    for (int c = 0; c < a.nch; c++)
+                        mma_f16(tmem + (uint32_t)(c * cw), da + so + (s * 2 * kALbo >> 4),
+                                db + so + (uint32_t)((s * 2 * npad + c * cw) * 16 >> 4), idesc, (q | s) != 0);
+                mma_commit(ab_empty + ab.slot);
             }
             mma_commit(acc_full);
             mb_drain(acc_full, 0);  // every MMA has completed before TMEM is released
         }
         __syncwarp();
+    } else if (warp == 2) {
+        // ---------------- activation producer ----------------
+        if (lane == 0) {
+            pdl_wait();  // the activations come from the previous kernel
+            Ring ab{ST};
+            const uint16_t *src = a.Xp + ((int64_t)nt * a.nu * 4 + 4 * u0) * (int64_t)npad * 64;
+            int issued = 0;
+            for (int q = 0; q < nst && !*dead; q++, ab.next(), src += npad * 64) {
+                if (ab.round > 0 && !mb_wait(ab_empty + ab.slot, ab.empty_par(), dead)) break;
+                mb_expect_tx(b_full + ab.slot, (uint32_t)bstage);
+                bulk_copy(stages + ab.slot * stage_bytes + kAStage, src, (uint32_t)bstage, b_full + ab.slot);
+                issued = q + 1;
+            }
+            for (int k = 0; k < ST && k < issued; k++) {
+                const int q = issued - 1 - k;
+                mb_drain(b_full + q % ST, (uint32_t)(q / ST) & 1);
+            }
+        }
     } else {
         // ---------------- dequant, then epilogue ----------------
         pdl_wait();
-        const int dt = tid - 64;
-        for (int i = 0; i < nunits && !*dead; i++) {
-            const int rs = i % kRawSlots;
-            if (!mb_wait(raw_full + rs, (uint32_t)(i / kRawSlots) & 1, dead)) break;
-            const uint8_t *slot = raw + rs * RAW;
+        // one piece per thread: M-tile m, row r, lane quad t, the same in every stage
+        const int P = tid - 96;
+        const int m = P >> 6, r = (P >> 2) & 15, t = P & 3;
+        const int off = (t >> 1) * kALbo + (16 * m + r) * 16 + (t & 1) * 8;  // run w adds 2 w kALbo
+        const bool has_rows = m < nmt;
+        Deq<FMT> dq;
+        Ring rr{RS}, ab{ST};
+        for (int i = 0; i < nunits && !*dead; i++, rr.next()) {
+            if (!mb_wait(raw_full + rr.slot, rr.full_par(), dead)) break;
+            if (has_rows) dq.unit(raw + rr.slot * RAW + m * MTB, r, t);
             bool ok = true;
-            for (int j = 0; j < 4; j++) {
-                const int q = 4 * i + j, st = q % ST;
-                if (q >= ST && !mb_wait(ab_empty + st, (uint32_t)((q / ST) - 1) & 1, dead)) {
+#pragma unroll
+            for (int j = 0; j < 4; j++, ab.next()) {
+                if (ab.round > 0 && !mb_wait(ab_empty + ab.slot, ab.empty_par(), dead)) {
                     ok = false;
                     break;
                 }
-                uint8_t *A = stages + st * stage_bytes;
+                uint8_t *A = stages + ab.slot * stage_bytes + off;
+                uint32_t o[8];
+                if (has_rows) {
+                    dq.stage(j, o);
+                } else {
 #pragma unroll
-                for (int pc = 0; pc < 512 / kDqThreads; pc++) {
-                    const int P = pc * kDqThreads + dt;
-                    const int m = P >> 6, r = (P >> 2) & 15, t = P & 3;
-                    float v[16];
-                    if (m < nmt) {
-                        dequant_piece<FMT>(slot + m * MTB, r, t, j, v);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; e++) v[e] = 0.f;
-                    }
-                    const int rr = 16 * m + r;
-#pragma unroll
-                    for (int w = 0; w < 4; w++) {
-                        uint8_t *dst = A + (2 * w + (t >> 1)) * (kBM * 16) + rr * 16 + (t & 1) * 8;
-                        *reinterpret_cast<uint2 *>(dst) =
-                            make_uint2(pack_h2(v[4 * w], v[4 * w + 1]), pack_h2(v[4 * w + 2], v[4 * w + 3]));
-                    }
+                    for (int e = 0; e < 8; e++) o[e] = 0u;
                 }
+#pragma unroll
+                for (int w = 0; w < 4; w++)
+                    *reinterpret_cast<uint2 *>(A + 2 * w * kALbo) = make_uint2(o[2 * w], o[2 * w + 1]);
                 fence_async_smem();
-                mb_arrive(a_full + st);
+                mb_arrive(a_full + ab.slot);
             }
             if (!ok) break;
-            mb_arrive(raw_empty + rs);
+            mb_arrive(raw_empty + rr.slot);
         }
-        // epilogue: TMEM lane quarter (warp % 4) = rows 32 (warp % 4) ..; the two warps
-        // of a quarter take alternate 16-column chunks
+        // epilogue: TMEM lane quarter (warp % 4) = rows 32 (warp % 4) ..; the four warps
+        // of a quarter take every fourth 16-column chunk
         const bool have = __all_sync(0xffffffffu, mb_wait(acc_full, 0, dead));
         tc_fence_after();
-        const int quarter = warp & 3, chalf = (warp - 2) >> 2;
+        const int quarter = warp & 3, cgrp = (warp - 3) >> 2;
         const int64_t row = (int64_t)rb0 * 16 + 32 * quarter + lane;
-        for (int c0 = 16 * chalf; c0 < npad; c0 += 32) {
+        for (int c0 = 16 * cgrp; c0 < npad; c0 += 64) {
             uint32_t rv[16];
             tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, rv);
             if (!have) continue;
@@ -410,7 +515,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
                 const int col = nt * npad + c0 + c;
                 const float val = col < a.ncols ? __uint_as_float(rv[c]) * a.xinv[col] : 0.f;
                 if (a.splits > 1) {
-                    if (col < a.ncols && row < (int64_t)a.nrb * 16) a.ws[((int64_t)z * a.ncols + col) * ((int64_t)a.nrb * 16) + row] = val;
+                    if (col < a.ncols && row < (int64_t)a.nrb * 16)
+                        a.ws[((int64_t)z * a.ncols + col) * ((int64_t)a.nrb * 16) + row] = val;
                 } else if (a.ep) {
                     // rows 32 P + (0..15) gate, 32 P + 16 + (0..15) up -> output 16 P + (0..15)
                     const float up = __shfl_down_sync(0xffffffffu, val, 16);
@@ -433,8 +539,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
 }
 
 // pack the columns of one n-tile to fp16 in the per-stage operand layout,
-// scaled by 2^e per column (max |x| 2^e in [2^13, 2^14)); the activation
-// transform of the GEMV (RMSNorm, SwiGLU) is applied on the way
+// scaled by 2^e per column (max |x| 2^e in [2^13, 2^14)), the K slots of each
+// group of four holding the elements (0, 2, 1, 3) like the weights; the
+// activation transform of the GEMV (RMSNorm, SwiGLU) is applied on the way
 template <int XF>
 __global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ X, int64_t ldx, int64_t K, int ncols,
                                                      int npad, int nu, const float *__restrict__ xw, float eps,
@@ -443,8 +550,7 @@ __global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ X
     __shared__ float bc;
     pdl_trigger();
     pdl_wait();
-    const int slot = blockIdx.x, tile = slot / npad, n = slot % npad;
-    const int col = slot;  // tiles hold consecutive columns
+    const int col = blockIdx.x, tile = col / npad, n = col % npad;  // tiles hold consecutive columns
     const int tid = threadIdx.x;
     const int64_t nchunks = (int64_t)nu * 32;  // 8-element chunks of the padded K
     const bool has = col < ncols;
@@ -491,14 +597,14 @@ __global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ X
         e = e < -100 ? -100 : (e > 100 ? 100 : e);
     }
     const float scl = __int_as_float((e + 127) << 23);
-    if (tid == 0) xinv[slot] = has ? __int_as_float((127 - e) << 23) : 0.f;
+    if (tid == 0) xinv[col] = has ? __int_as_float((127 - e) << 23) : 0.f;
     for (int64_t c = tid; c < nchunks; c += 256) {
-        const int64_t kst = c >> 3, ch = c & 7;
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) w[i] = pack_h2(value(8 * c + 2 * i) * scl, value(8 * c + 2 * i + 1) * scl);
-        uint16_t *dst = Xp + ((((int64_t)tile * nu * 4 + kst) * 8 + ch) * npad + n) * 8;
-        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        const int64_t kst = c >> 3, ch = c & 7, k0 = 8 * c;
+        const uint4 w = make_uint4(pack_h2(value(k0) * scl, value(k0 + 2) * scl),
+                                   pack_h2(value(k0 + 1) * scl, value(k0 + 3) * scl),
+                                   pack_h2(value(k0 + 4) * scl, value(k0 + 6) * scl),
+                                   pack_h2(value(k0 + 5) * scl, value(k0 + 7) * scl));
+        *reinterpret_cast<uint4 *>(Xp + ((((int64_t)tile * nu * 4 + kst) * 8 + ch) * npad + n) * 8) = w;
     }
 }
 
@@ -542,30 +648,49 @@ int sm_count() {
 }
 
 struct Plan {
-    int ntiles, npad, splits, ST, rtiles, smem;
+    int ntiles, npad, nch, splits, RS, ST, rtiles, smem;
     int64_t xp_bytes, xinv_bytes, ws_bytes;
 };
 
+// columns per CTA up to 512 (one weight dequant serves all of them), in MMA
+// chunks of <= 256; split-K minimises waves x units per CTA
 bool make_plan(const QTensor &T, int ncols, Plan &p) {
     if (ncols < 1) return false;
-    p.ntiles = (ncols + 255) / 256;
-    const int per = (ncols + p.ntiles - 1) / p.ntiles;
-    p.npad = (per + 15) / 16 * 16;
-    p.rtiles = (int)((T.nrb + 7) / 8);
-    const int base = p.rtiles * p.ntiles;
-    p.splits = 1;
-    if (base < sm_count()) {
-        const int want = (sm_count() + base - 1) / base;
-        p.splits = (int)(want < T.nu ? want : T.nu);
-        if (p.splits < 1) p.splits = 1;
+    const int raw1 = 8 * mtile_bytes(T.type);
+    bool ok = false;
+    for (int cap = 512; cap >= 256 && !ok; cap -= 256) {
+        p.ntiles = (ncols + cap - 1) / cap;
+        const int per = (ncols + p.ntiles - 1) / p.ntiles;
+        p.nch = (per + 255) / 256;
+        const int cw = ((per + p.nch - 1) / p.nch + 15) / 16 * 16;
+        p.npad = cw * p.nch;
+        const int stage = (kAStage + p.npad * 128 + 1023) & ~1023;
+        for (p.RS = kMaxRaw; p.RS >= 2 && !ok; p.RS--) {
+            const int raw = (p.RS * raw1 + 1023) & ~1023;
+            int st = (kMaxSmem - 2048 - raw) / stage;  // 1 KB barriers, 1 KB slack
+            if (st > kMaxStages) st = kMaxStages;
+            if (st >= 2 && (st >= 3 || p.RS == 2)) {
+                p.ST = st;
+                p.smem = 1024 + raw + st * stage;
+                ok = true;
+            }
+        }
+        if (ok) p.RS++;  // undo the loop's final decrement
     }
-    const int raw = (kRawSlots * 8 * mtile_bytes(T.type) + 1023) & ~1023;
-    const int stage = (kAStage + p.npad * 128 + 1023) & ~1023;
-    int st = (kMaxSmem - 1024 - 1024 - raw) / stage;  // 1 KB barriers, 1 KB static/alignment slack
-    if (st > 4) st = 4;
-    if (st < 2) return false;
-    p.ST = st;
-    p.smem = 1024 + raw + st * stage;
+    if (!ok) return false;
+    p.rtiles = (int)((T.nrb + 7) / 8);
+    const int base = p.rtiles * p.ntiles, nsm = sm_count();
+    p.splits = 1;
+    int64_t best = -1;
+    for (int s = 1; s <= T.nu && s <= 64; s++) {
+        // a CTA costs its units plus ~2 units of start-up (first weights, TMEM, epilogue)
+        const int64_t waves = ((int64_t)base * s + nsm - 1) / nsm;
+        const int64_t cost = waves * ((T.nu + s - 1) / s + 2);
+        if (best < 0 || cost < best) {
+            best = cost;
+            p.splits = s;
+        }
+    }
     p.xp_bytes = (int64_t)p.ntiles * p.npad * T.nu * 256 * 2;
     p.xinv_bytes = ((int64_t)p.ntiles * p.npad * 4 + 255) / 256 * 256;
     p.ws_bytes = p.splits > 1 ? (int64_t)p.splits * ncols * T.nrb * 16 * 4 : 0;
@@ -612,7 +737,7 @@ cudaError_t qgemm_dense(const QTensor &T, const float *X, int ncols, float *Y, b
     default: e = launch_k(pack_x_kernel<2>, pg, dim3(256), 0, s, X, ldx, (int64_t)T.cols, ncols, p.npad, (int)T.nu, xf.w, xf.eps, Xp, xinv); break;
     }
     if (e != cudaSuccess) return e;
-    MmaArgs a{T.data, (int)T.nrb, (int)T.nu, Xp, xinv, ncols, p.npad, p.ntiles, p.splits, p.ST,
+    MmaArgs a{T.data, (int)T.nrb, (int)T.nu, Xp, xinv, ncols, p.npad, p.ntiles, p.nch, p.splits, p.RS, p.ST,
               Y, ldy, T.rows, accumulate ? 1 : 0, xf.ep, ws};
     switch (T.type) {
     case 12: e = launch_qmma<12>(a, p, s); break;

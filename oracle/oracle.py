@@ -221,6 +221,57 @@ def accept_greedy(target, draft_tokens):
     return acc, out
 
 
+def _kq_scales(s):
+    """6-bit sub-block scales and mins of Q4_K/Q5_K headers (src/Dequant.jl:345-362)"""
+    s = s.astype(np.int64)
+    sc = np.empty((s.shape[0], 8), np.int64)
+    m = np.empty((s.shape[0], 8), np.int64)
+    for j in range(4):
+        sc[:, j] = s[:, j] & 63
+        m[:, j] = s[:, j + 4] & 63
+    for j in range(4, 8):
+        sc[:, j] = (s[:, j + 4] & 0x0F) | ((s[:, j - 4] >> 6) << 4)
+        m[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+    return sc, m
+
+
+def dense_fp16_weights(qtype, blocks, rows, cols):
+    """The fp16 weights of the dense tensor-core GEMM (ifr_qgemm_dense), formed
+    from the exact integer quants of the GGUF blocks: Q4_K/Q5_K
+    fp16(q * fp16(d sc) - fp16(dmin m)), Q6_K fp16((q - 32) fp16(d sc)),
+    Q8_0 fp16(q d), each a single rounding of the exact value (f64 here)."""
+    be, bb = BLOCK[qtype]
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, bb)
+    nb = b.shape[0]
+    f16 = lambda a: a.copy().view(np.float16).astype(np.float64)  # noqa: E731
+    e = np.arange(be)
+    if qtype in (Q4_K, Q5_K):
+        d = f16(b[:, 0:2])
+        dmin = f16(b[:, 2:4])
+        sc, m = _kq_scales(b[:, 4:16])
+        qs = b[:, 48:176] if qtype == Q5_K else b[:, 16:144]
+        l = e % 32
+        q = (qs[:, 32 * (e // 64) + l].astype(np.int64) >> (4 * ((e % 64) >= 32))) & 15
+        j = e // 32
+        if qtype == Q5_K:
+            q = q + 16 * ((b[:, 16 + l].astype(np.int64) >> j) & 1)
+        d1 = (d * sc).astype(np.float16).astype(np.float64)[:, j]
+        m1 = (dmin * m).astype(np.float16).astype(np.float64)[:, j]
+        w = q * d1 - m1
+    elif qtype == Q6_K:
+        d = f16(b[:, 208:210])
+        sc = b[:, 192:208].view(np.int8).astype(np.float64)
+        n, qq, l = e // 128, (e % 128) // 32, e % 32
+        lo = (b[:, 64 * n + 32 * (qq % 2) + l].astype(np.int64) >> (4 * (qq // 2))) & 15
+        hi = (b[:, 128 + 32 * n + l].astype(np.int64) >> (2 * qq)) & 3
+        ds = (d * sc).astype(np.float16).astype(np.float64)[:, e // 16]
+        w = ((lo | (hi << 4)) - 32) * ds
+    else:
+        d = f16(b[:, 0:2])
+        w = b[:, 2:34].view(np.int8).astype(np.float64) * d
+    return w.astype(np.float16).reshape(rows, cols)
+
+
 def norm_rel(a, b):
     """||a-b|| / ||b|| per leading row (the GEMV/logits parity metric)."""
     a = np.asarray(a, dtype=np.float64).reshape(-1, np.shape(b)[-1])

@@ -2,9 +2,11 @@
 fp16 operands, f32 accumulation in tensor memory) through the C ABI.
 
 Two references per case:
-  * the stated arithmetic in f64: fp16(exact dequantized W) x fp16(X 2^e) 2^-e
-    (e per column: max|x| 2^e in [2^13, 2^14)); only the f32 summation order
-    differs, so the tolerance is tight (DENSE_TOL);
+  * the stated arithmetic in f64: the oracle's fp16 weights of the dense path
+    (oracle.dense_fp16_weights: each weight one rounding from its exact
+    integer quant) times fp16(X 2^e) 2^-e (e per column: max|x| 2^e in
+    [2^13, 2^14)); only the f32 summation order differs, so the tolerance is
+    tight (DENSE_TOL);
   * the exact product of the oracle (f64), within the fp16 rounding of both
     operands (EXACT_TOL).
 """
@@ -20,8 +22,7 @@ EXACT_TOL = 3e-3   # norm-relative per column vs the exact f64 product
 
 
 def fp16_model(O, qt, q, M, K, X):
-    W = O.dequantize(qt, q, M * K).reshape(M, K).astype(np.float32)
-    W16 = W.astype(np.float16).astype(np.float64)
+    W16 = O.dense_fp16_weights(qt, q, M, K).astype(np.float64)
     amax = np.abs(X).max(axis=1)
     e = np.zeros(len(X), dtype=np.int64)
     nz = amax > 0
@@ -35,7 +36,7 @@ def fp16_model(O, qt, q, M, K, X):
 # (M, K, N): one tile; ragged rows; split-K with partial sums; two column tiles;
 # the largest column tile; a column count that is not a multiple of 16
 CASES = [(256, 512, 16), (300, 768, 40), (1000, 1024, 9), (512, 2048, 160), (136, 1024, 300),
-         (128, 1024, 256), (2048, 4096, 64)]
+         (128, 1024, 256), (2048, 4096, 64), (384, 1024, 512), (256, 512, 700)]
 
 
 @pytest.mark.parametrize("qt", FORMATS)
