@@ -53,7 +53,8 @@ constexpr int kBM = 128;                 // rows per CTA (8 row blocks)
 // A tile: 8 K-chunks of 128 rows x 16 bytes; chunks 2112 bytes apart (2048 + 64)
 // so that the two halves of a warp's 64-bit stores hit disjoint banks
 constexpr int kALbo = 2112;
-constexpr int kAStage = 7 * kALbo + kBM * 16 + 64;  // 16896 bytes
+// A tile of a stage of KS x 64 K: 8 KS chunks
+IFR_HD int a_stage_bytes(int ks) { return (8 * ks - 1) * kALbo + kBM * 16 + 64; }
 constexpr int kMaxSmem = 232448;         // 227 KB per block
 constexpr long long kMmaWait = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -350,7 +351,9 @@ struct MmaArgs {
     float *ws;             // split partials [splits][ncols][nrb * 16] (splits > 1)
 };
 
-template <int FMT>
+// KS: 64-wide K sub-stages per pipeline stage (2 when the column tile is <= 256,
+// so that one tcgen05.commit covers at least eight MMAs)
+template <int FMT, int KS>
 __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr int MTB = mtile_bytes(FMT);
@@ -366,7 +369,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     volatile int *dead = reinterpret_cast<volatile int *>(tmem_holder + 1);
     uint8_t *raw = smem + 1024;
     const int raw_bytes = (RS * RAW + 1023) & ~1023;
-    const int bstage = npad * 128;
+    constexpr int kAStage = a_stage_bytes(KS);
+    const int bstage = npad * 128 * KS;
     const int stage_bytes = (kAStage + bstage + 1023) & ~1023;
     uint8_t *stages = raw + raw_bytes;
 
@@ -375,7 +379,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     const int rb0 = rt * 8;
     const int nmt = min(8, a.nrb - rb0);
     const int u0 = (int)((int64_t)z * a.nu / a.splits), u1 = (int)((int64_t)(z + 1) * a.nu / a.splits);
-    const int nunits = u1 - u0, nst = 4 * nunits;
+    const int nunits = u1 - u0, nst = 4 / KS * nunits;
     const uint32_t tcols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : npad <= 256 ? 256 : 512;
 
     pdl_trigger();
@@ -435,7 +439,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
                 tc_fence_after();
                 const uint32_t so = (uint32_t)(ab.slot * stage_bytes) >> 4;  // descriptor start fields advance in 16 B
 #pragma unroll
-                for (int s = 0; s < 4; s++)
+                for (int s = 0; s < 4 * KS; s++)
                     for (int c = 0; c < a.nch; c++)
                         mma_f16(tmem + (uint32_t)(c * cw), da + so + (s * 2 * kALbo >> 4),
                                 db + so + (uint32_t)((s * 2 * npad + c * cw) * 16 >> 4), idesc, (q | s) != 0);
@@ -452,7 +456,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
             Ring ab{ST};
             const uint16_t *src = a.Xp + ((int64_t)nt * a.nu * 4 + 4 * u0) * (int64_t)npad * 64;
             int issued = 0;
-            for (int q = 0; q < nst && !*dead; q++, ab.next(), src += npad * 64) {
+            for (int q = 0; q < nst && !*dead; q++, ab.next(), src += npad * 64 * KS) {
                 if (ab.round > 0 && !mb_wait(ab_empty + ab.slot, ab.empty_par(), dead)) break;
                 mb_expect_tx(b_full + ab.slot, (uint32_t)bstage);
                 bulk_copy(stages + ab.slot * stage_bytes + kAStage, src, (uint32_t)bstage, b_full + ab.slot);
@@ -478,22 +482,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
             if (has_rows) dq.unit(raw + rr.slot * RAW + m * MTB, r, t);
             bool ok = true;
 #pragma unroll
-            for (int j = 0; j < 4; j++, ab.next()) {
+            for (int j = 0; j < 4 / KS; j++, ab.next()) {
                 if (ab.round > 0 && !mb_wait(ab_empty + ab.slot, ab.empty_par(), dead)) {
                     ok = false;
                     break;
                 }
                 uint8_t *A = stages + ab.slot * stage_bytes + off;
-                uint32_t o[8];
-                if (has_rows) {
-                    dq.stage(j, o);
-                } else {
 #pragma unroll
-                    for (int e = 0; e < 8; e++) o[e] = 0u;
+                for (int ss = 0; ss < KS; ss++) {
+                    uint32_t o[8];
+                    if (has_rows) {
+                        dq.stage(KS * j + ss, o);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; e++) o[e] = 0u;
+                    }
+#pragma unroll
+                    for (int w = 0; w < 4; w++)
+                        *reinterpret_cast<uint2 *>(A + (8 * ss + 2 * w) * kALbo) = make_uint2(o[2 * w], o[2 * w + 1]);
                 }
-#pragma unroll
-                for (int w = 0; w < 4; w++)
-                    *reinterpret_cast<uint2 *>(A + 2 * w * kALbo) = make_uint2(o[2 * w], o[2 * w + 1]);
                 fence_async_smem();
                 mb_arrive(a_full + ab.slot);
             }
@@ -648,12 +655,13 @@ int sm_count() {
 }
 
 struct Plan {
-    int ntiles, npad, nch, splits, RS, ST, rtiles, smem;
+    int ntiles, npad, nch, ks, splits, RS, ST, rtiles, smem;
     int64_t xp_bytes, xinv_bytes, ws_bytes;
 };
 
 // columns per CTA up to 512 (one weight dequant serves all of them), in MMA
-// chunks of <= 256; split-K minimises waves x units per CTA
+// chunks of <= 256; 128-wide K stages for tiles of <= 256 columns; split-K
+// minimises waves x (units + start-up) per CTA
 bool make_plan(const QTensor &T, int ncols, Plan &p) {
     if (ncols < 1) return false;
     const int raw1 = 8 * mtile_bytes(T.type);
@@ -664,18 +672,21 @@ bool make_plan(const QTensor &T, int ncols, Plan &p) {
         p.nch = (per + 255) / 256;
         const int cw = ((per + p.nch - 1) / p.nch + 15) / 16 * 16;
         p.npad = cw * p.nch;
-        const int stage = (kAStage + p.npad * 128 + 1023) & ~1023;
-        for (p.RS = kMaxRaw; p.RS >= 2 && !ok; p.RS--) {
-            const int raw = (p.RS * raw1 + 1023) & ~1023;
-            int st = (kMaxSmem - 2048 - raw) / stage;  // 1 KB barriers, 1 KB slack
-            if (st > kMaxStages) st = kMaxStages;
-            if (st >= 2 && (st >= 3 || p.RS == 2)) {
-                p.ST = st;
-                p.smem = 1024 + raw + st * stage;
-                ok = true;
+        for (p.ks = p.npad <= 256 ? 2 : 1; p.ks >= 1 && !ok; p.ks--) {
+            const int stage = (a_stage_bytes(p.ks) + p.npad * 128 * p.ks + 1023) & ~1023;
+            for (p.RS = kMaxRaw; p.RS >= 2 && !ok; p.RS--) {
+                const int raw = (p.RS * raw1 + 1023) & ~1023;
+                int st = (kMaxSmem - 2048 - raw) / stage;  // 1 KB barriers, 1 KB slack
+                if (st > kMaxStages) st = kMaxStages;
+                if (st >= 2 && (st >= 3 || p.RS == 2)) {
+                    p.ST = st;
+                    p.smem = 1024 + raw + st * stage;
+                    ok = true;
+                }
             }
+            if (ok) p.RS++;  // undo the loops' final decrements
         }
-        if (ok) p.RS++;  // undo the loop's final decrement
+        if (ok) p.ks++;
     }
     if (!ok) return false;
     p.rtiles = (int)((T.nrb + 7) / 8);
@@ -697,16 +708,21 @@ bool make_plan(const QTensor &T, int ncols, Plan &p) {
     return true;
 }
 
-template <int FMT>
-cudaError_t launch_qmma(const MmaArgs &a, const Plan &p, cudaStream_t s) {
+template <int FMT, int KS>
+cudaError_t launch_qmma_ks(const MmaArgs &a, const Plan &p, cudaStream_t s) {
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(qmma_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(qmma_kernel<FMT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kMaxSmem - 1024);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return launch_k(qmma_kernel<FMT>, dim3(p.rtiles * p.ntiles, p.splits), dim3(kMmaThreads), (size_t)p.smem, s, a);
+    return launch_k(qmma_kernel<FMT, KS>, dim3(p.rtiles * p.ntiles, p.splits), dim3(kMmaThreads), (size_t)p.smem, s,
+                    a);
+}
+template <int FMT>
+cudaError_t launch_qmma(const MmaArgs &a, const Plan &p, cudaStream_t s) {
+    return p.ks == 2 ? launch_qmma_ks<FMT, 2>(a, p, s) : launch_qmma_ks<FMT, 1>(a, p, s);
 }
 
 }  // namespace
