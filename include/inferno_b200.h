@@ -41,6 +41,8 @@ extern "C" {
 #define IFR_TYPE_Q6_K 14
 
 #define IFR_MAX_VERIFY_COLS 8  /* columns per pass of the small-N kernel */
+#define IFR_MAX_BATCH 256      /* requests per batched state */
+#define IFR_DENSE_MIN_COLS_DEFAULT 24  /* engine GEMMs of >= this many columns use ifr_qgemm_dense's path */
 
 typedef struct ifr_ctx ifr_ctx;
 typedef struct ifr_tensor ifr_tensor;
@@ -78,6 +80,12 @@ int ifr_ctx_reserve_accept(ifr_ctx *ctx, int batch, int gamma, int vocab);
 #define IFR_ACT_EXACT 0
 #define IFR_ACT_Q8K 1
 int ifr_ctx_set_activation(ifr_ctx *ctx, int mode);
+/* The model engine computes a projection over n columns (requests x verify
+ * tokens) with the exact small-N kernel in passes of 8 columns while
+ * n < ncols, and with the dense tensor-core path of ifr_qgemm_dense (fp16
+ * operands, f32 accumulation) from ncols columns on.  Default
+ * IFR_DENSE_MIN_COLS_DEFAULT; a state of one request never reaches it. */
+int ifr_ctx_set_dense_min_cols(ifr_ctx *ctx, int ncols);
 /* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
  * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);
@@ -183,12 +191,20 @@ int ifr_model_get_info(const ifr_model *m, ifr_model_info *info);
 
 /* KV caches, SSM/conv states and rollback buffers for max_ctx positions */
 int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out);
+/* the same for `batch` independent requests that advance together: every
+ * call below then works on all of them at once (prompts, drafts and reads
+ * per request as documented).  No counterpart in the reference, which
+ * serves one sequence at a time (src/SpeculativeDecoding.jl:106-172). */
+int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out);
 int ifr_state_free(ifr_state *s);
 int ifr_state_reset(ifr_state *s);
 /* prefill a prompt (host tokens), emit the first greedy token (synchronous);
  * forward_cpu!(prompt) then softmax_sample at temperature 0
  * (src/ModelCPU.jl:1325-1336) */
 int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token);
+/* batched state: tokens [batch][n] (every request's prompt has n tokens),
+ * first_tokens [batch] (may be NULL) */
+int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first_tokens);
 /* one greedy speculative step, asynchronous on the context stream:
  * draft gamma tokens with the MTP head (or take `drafts`, gamma host tokens),
  * verify [last, drafts] in one gamma+1-column forward, accept the longest
@@ -196,6 +212,7 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
  * accepted drafts plus the target's next token, and roll the SSM/conv/KV
  * state back to the accepted prefix.  gamma = 0 is plain greedy decoding. */
 int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts);
+/* (batched state: drafts [batch][gamma]) */
 /* capture `steps` consecutive MTP spec steps (gamma drafts each) into one
  * CUDA graph on the context stream (which must not be the legacy default
  * stream); ifr_spec_graph_launch replays it asynchronously.  Run one eager
@@ -217,8 +234,12 @@ int ifr_gemv_pass(ifr_state *s, int ncols);
 /* synchronous read of the emitted tokens and of
  * scalars[4] = {position, last accept count, steps, last token} */
 int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars);
-/* synchronous read of the last forward: logits [n][vocab] (verify columns),
- * final-normed hidden [n][hidden], the n tokens fed; any pointer may be NULL */
+/* the same for request b of a batched state (ifr_state_read reads request 0) */
+int ifr_state_read_request(ifr_state *s, int b, int32_t *tokens, int max_tokens, int *n_tokens,
+                           int32_t *scalars);
+/* synchronous read of the last forward: logits [batch * n][vocab] (verify
+ * columns, request-major), final-normed hidden [batch * n][hidden], the
+ * tokens fed [batch][n]; any pointer may be NULL */
 int ifr_state_last_verify(ifr_state *s, float *logits, float *hidden, int32_t *tokens, int *n_cols);
 
 /* --- legacy shims: the reference's C symbols, identical signatures --------

@@ -108,6 +108,10 @@ class Context:
         (Q8_K-quantised, the reference's kernels)"""
         check(load().ifr_ctx_set_activation(self.handle, int(mode)))
 
+    def set_dense_min_cols(self, ncols):
+        """engine projections of >= ncols columns use the dense tensor-core path"""
+        check(load().ifr_ctx_set_dense_min_cols(self.handle, int(ncols)))
+
     def set_stream(self, stream):
         check(load().ifr_ctx_set_stream(self.handle, ctypes.c_void_p(stream.cuda_stream)))
 

@@ -35,6 +35,10 @@ SIGNATURES = {
                              ctypes.POINTER(_i64)]),
     "ifr_dequant": (_i, [_vp, _vp, _vp]),
     "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "ifr_ctx_set_dense_min_cols": (_i, [_vp, _i]),
+    "ifr_state_read_request": (_i, [_vp, _i, _vp, _i, _vp, _vp]),
+    "ifr_prefill_batch": (_i, [_vp, _vp, _i, _vp]),
+    "ifr_state_create_batch": (_i, [_vp, _i, _i, ctypes.POINTER(_vp)]),
     "ifr_qgemm_dense": (_i, [_vp, _vp, _vp, _i, _vp]),
     "ifr_ctx_reserve_dense": (_i, [_vp, _vp, _i]),
     "ifr_quantize": (_i, [_i, _vp, _i64, _i64, _vp]),

@@ -463,10 +463,10 @@ __global__ void greedy_finish_kernel(const float *__restrict__ vmax, const int32
 // chunks in chunk order, decides, and returns the counter to zero for the
 // next launch.
 __global__ void __launch_bounds__(kNL) greedy_fused_kernel(const float *__restrict__ target, int V, int nch, int G,
-                                                           const int32_t *__restrict__ draft_tokens,
+                                                           const int32_t *__restrict__ draft_tokens, int draft_ld,
                                                            float *vmax, int32_t *imax, unsigned *counter,
                                                            int32_t *__restrict__ accept_count,
-                                                           int32_t *__restrict__ out_tokens) {
+                                                           int32_t *__restrict__ out_tokens, int out_ld) {
     __shared__ float sv[kNL];
     __shared__ int si[kNL];
     __shared__ bool last;
@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(kNL) greedy_fused_kernel(const float *__restri
     __syncthreads();
     if (!last || threadIdx.x != 0) return;
     __threadfence();
-    int32_t *ot = out_tokens + (int64_t)b * (G + 1);
+    int32_t *ot = out_tokens + (int64_t)b * out_ld;
     for (int i = 0; i <= G; i++) ot[i] = -1;
     int acc = 0;
     for (int i = 0; i <= G; i++) {
@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(kNL) greedy_fused_kernel(const float *__restri
             if (v > best) { best = v; arg = __ldcg(imax + rr * nch + cc); }
         }
         ot[i] = arg;
-        if (i == G || arg != draft_tokens[b * G + i]) break;
+        if (i == G || arg != draft_tokens[(int64_t)b * draft_ld + i]) break;
         acc++;
     }
     accept_count[b] = acc;
@@ -527,12 +527,13 @@ __global__ void __launch_bounds__(kNL) greedy_fused_kernel(const float *__restri
 
 cudaError_t accept_greedy_fused(const float *target, const int32_t *draft_tokens, int B, int G, int V,
                                 int32_t *accept_count, int32_t *out_tokens, void *scratch, unsigned *counter,
-                                cudaStream_t s) {
+                                cudaStream_t s, int draft_ld, int out_ld) {
     const int nch = (V + kCH - 1) / kCH;
     float *vmax = (float *)scratch;
     int32_t *imax = (int32_t *)((char *)scratch + (int64_t)B * (G + 1) * nch * 4);
     return launch_k(greedy_fused_kernel, dim3(nch, B * (G + 1)), dim3(kNL), 0, s, target, V, nch, G, draft_tokens,
-                    vmax, imax, counter, accept_count, out_tokens);
+                    draft_ld > 0 ? draft_ld : G, vmax, imax, counter, accept_count, out_tokens,
+                    out_ld > 0 ? out_ld : G + 1);
 }
 
 int64_t accept_greedy_scratch_bytes(int B, int G, int V) {

@@ -71,10 +71,12 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
                           cudaStream_t s);
 int64_t accept_greedy_scratch_bytes(int batch, int gamma, int vocab);
 // the same in one launch; counter: one zero-initialised unsigned per sequence,
-// left at zero (not shared by launches that can overlap)
+// left at zero (not shared by launches that can overlap); draft b's tokens at
+// draft_tokens + b * draft_ld, its outputs at out_tokens + b * out_ld
+// (0: gamma and gamma + 1)
 cudaError_t accept_greedy_fused(const float *target, const int32_t *draft_tokens, int batch, int gamma, int vocab,
                                 int32_t *accept_count, int32_t *out_tokens, void *scratch, unsigned *counter,
-                                cudaStream_t s);
+                                cudaStream_t s, int draft_ld = 0, int out_ld = 0);
 
 }  // namespace ifr
 

@@ -29,6 +29,7 @@ int ifr_fail(int code, const char *fmt, ...);
 int ifr_cuda_fail(cudaError_t e, const char *what);
 int ifr_ctx_device(const ifr_ctx *c);
 int ifr_ctx_activation(const ifr_ctx *c);
+int ifr_ctx_dense_min(const ifr_ctx *c);
 void ifr_ctx_retain(ifr_ctx *c);
 void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
@@ -379,8 +380,12 @@ int64_t proj_bytes(const Proj &p) {
 }  // namespace
 
 // ------------------------------------------------------------- state --------
+// B requests share the model and advance together; request b's verify tokens
+// are vtok[b * kNMax ..], its scalars sc[b], its caches offset by b per-request
+// strides; a call with n tokens per request uses activation columns b * n + t.
 struct ifr_state {
     ifr_model *m = nullptr;
+    int B = 1;
     int max_ctx = 0, log_cap = 0;
     std::vector<void *> allocs;
     ifr::EngineScalars *sc = nullptr;   // device
@@ -394,6 +399,8 @@ struct ifr_state {
     std::vector<float *> kc, vc;                // per layer (attention) else null
     float *mtp_kc = nullptr, *mtp_vc = nullptr;
     void *acc_scratch = nullptr;
+    void *dense = nullptr;              // scratch of the dense tensor-core GEMMs
+    int64_t dense_bytes = 0;
     int last_n = 0;
     // kernel launches enqueued (for the benchmark's launch count)
     int64_t launches = 0;
@@ -453,6 +460,8 @@ struct ProfScope {
 
 int64_t proj_bytes(const Proj &p);
 
+// Y (+)= W X over n columns: the exact small-N kernel in passes of 8 columns,
+// or the dense tensor-core kernel once n reaches the context's threshold
 int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st,
          const ifr::XForm &xf = ifr::XForm()) {
     ProfScope ps(s, cat, proj_bytes(p), st);
@@ -460,27 +469,40 @@ int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, 
     const int64_t ldy = xf.ep ? p.rows / 2 : p.rows;
     ifr::XForm f = xf;
     f.act = ifr_ctx_activation(s->m->ctx);
+    const bool dense = n >= ifr_ctx_dense_min(s->m->ctx) && s->dense;
     for (auto &q : p.parts) {
-        ECHECK(ifr::qgemm_small(q, X, n, Y + r0, accumulate, ldy, st, f), "qgemm");
+        if (dense) {
+            ECHECK(ifr::qgemm_dense(q, X, n, Y + r0, accumulate, ldy, st, f, s->dense, s->dense_bytes), "qgemm_dense");
+            s->launches += 2;
+        } else {
+            const int64_t ldx = f.ldx > 0 ? f.ldx : q.cols;
+            for (int c0 = 0; c0 < n; c0 += kNMax) {
+                const int k = std::min(kNMax, n - c0);
+                ECHECK(ifr::qgemm_small(q, X + c0 * ldx, k, Y + r0 + c0 * ldy, accumulate, ldy, st, f), "qgemm");
+                s->launches++;
+            }
+        }
         r0 += q.rows;
-        if (s) s->launches++;
     }
     return IFR_OK;
 }
 
 // one decoder layer (attention or SSM) on n columns of s->x
+// n tokens per request, s->B requests (columns b * n + t); pos of request b at
+// pos + b * pos_ld; kc / vc of request b at + b * kv_ld
 int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, float *vc, const int32_t *pos,
-                  bool draft, cudaStream_t st) {
+                  int pos_ld, int64_t kv_ld, bool draft, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
     const int d = c.hidden;
+    const int B = s->B, nc = B * n;
     const int gcat = draft ? CAT_DRAFT_GEMV : CAT_LAYER_GEMV;
     int rc;
     // RMSNorm kernels feed the input GEMVs (fusing the norm into every GEMV CTA
     // costs each of them a full reduction over the input, more than the launch)
-    ifr::rmsnorm(s->x, L.attn_norm, s->xn, n, d, c.rms_eps, d, d, st);
+    ifr::rmsnorm(s->x, L.attn_norm, s->xn, nc, d, c.rms_eps, d, d, st);
     s->launches += 3;  // two norms, the SSM / attention step
-    if ((rc = gemv(s, gcat, L.proj, s->xn, n, s->proj, false, st))) return rc;
+    if ((rc = gemv(s, gcat, L.proj, s->xn, nc, s->proj, false, st))) return rc;
     if (L.ssm) {
         ProfScope ps(s, CAT_SSM, 0, st);
         ifr::SsmArgs a{};
@@ -505,7 +527,13 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.C = m->conv_channels;
         a.K = c.conv_kernel;
         a.eps = c.rms_eps;
-        ECHECK(ifr::ssm_step(a, c.ssm_head_dim, st), "ssm_step");
+        const int64_t hd = c.ssm_head_dim;
+        a.b_S = (int64_t)c.ssm_heads * hd * hd;
+        a.b_hist = (int64_t)(c.conv_kernel - 1) * m->conv_channels;
+        a.b_rq = (int64_t)kNMax * m->conv_channels;
+        a.b_rkv = (int64_t)c.ssm_heads * kNMax * (2 * hd + 2);
+        a.b_prev = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
+        ECHECK(ifr::ssm_step(a, c.ssm_head_dim, B, st), "ssm_step");
     } else {
         ProfScope ps(s, CAT_ATTN, 0, st);
         ifr::AttnArgs a{};
@@ -526,42 +554,47 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.hd = c.head_dim;
         a.rotary_dim = c.rotary_dim;
         a.eps = c.rms_eps;
-        ECHECK(ifr::attn_step(a, st), "attn_step");
+        a.b_kv = kv_ld;
+        a.b_pos = pos_ld;
+        ECHECK(ifr::attn_step(a, B, st), "attn_step");
     }
-    if ((rc = gemv(s, gcat, L.out, s->y, n, s->x, true, st))) return rc;
-    ifr::rmsnorm(s->x, L.post_norm, s->xn, n, d, c.rms_eps, d, d, st);
+    if ((rc = gemv(s, gcat, L.out, s->y, nc, s->x, true, st))) return rc;
+    ifr::rmsnorm(s->x, L.post_norm, s->xn, nc, d, c.rms_eps, d, d, st);
     if (L.gate_up.glu) {
         // silu(gate) * up formed in the gate/up GEMV's epilogue
         ifr::XForm glu;
         glu.ep = 1;
-        if ((rc = gemv(s, gcat, L.gate_up, s->xn, n, s->hmid, false, st, glu))) return rc;
-        return gemv(s, gcat, L.down, s->hmid, n, s->x, true, st);
+        if ((rc = gemv(s, gcat, L.gate_up, s->xn, nc, s->hmid, false, st, glu))) return rc;
+        return gemv(s, gcat, L.down, s->hmid, nc, s->x, true, st);
     }
-    if ((rc = gemv(s, gcat, L.gate_up, s->xn, n, s->gu, false, st))) return rc;
+    if ((rc = gemv(s, gcat, L.gate_up, s->xn, nc, s->gu, false, st))) return rc;
     // silu(gate) * up formed while the down GEMV reads [gate | up]
     ifr::XForm swiglu;
     swiglu.kind = 2;
     swiglu.ldx = 2 * (int64_t)c.ffn;
-    return gemv(s, gcat, L.down, s->gu, n, s->x, true, st, swiglu);
+    return gemv(s, gcat, L.down, s->gu, nc, s->x, true, st, swiglu);
 }
 
-// embedding rows of the n verify tokens: token 0 from the state's last
-// emitted token when `first` is set (and written to vtok[0]), the others from
-// vtok; one thread per 32-element group (get_embedding, ModelCPU.jl:1005-1007)
+// embedding rows of the n verify tokens of each of B requests (row b * n + t):
+// token 0 of request b from its last emitted token (first + b * first_ld) when
+// `first` is set (and written to its vtok[0]), the others from vtok[b * kNMax + t];
+// one thread per 32-element group (get_embedding, ModelCPU.jl:1005-1007)
 template <int T>
 __global__ void embed_kernel(const uint8_t *__restrict__ w, int64_t nu, int64_t nb_raw, int64_t rows, int64_t cols,
-                             int32_t *vtok, const int32_t *first, int n, float *__restrict__ out) {
+                             int32_t *vtok, const int32_t *first, int first_ld, int n, int B,
+                             float *__restrict__ out) {
     ifr::pdl_trigger();
     ifr::pdl_wait();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= (int64_t)n * nu * 8) return;
+    if (i >= (int64_t)B * n * nu * 8) return;
     const int sub = (int)(i & 7);
     const int64_t u = (i >> 3) % nu;
-    const int t = (int)((i >> 3) / nu);
-    int64_t tok = (t == 0 && first) ? *first : vtok[t];
-    if (i == 0 && first) vtok[0] = (int32_t)tok;
+    const int tg = (int)((i >> 3) / nu), b = tg / n, t = tg % n;
+    int32_t *vt = vtok + (int64_t)b * kNMax;
+    int64_t tok = (t == 0 && first) ? first[(int64_t)b * first_ld] : vt[t];
+    if (t == 0 && u == 0 && sub == 0 && first) vt[0] = (int32_t)tok;
     tok = tok < 0 ? 0 : (tok >= rows ? rows - 1 : tok);
-    ifr::dequant_group<T>(w, nu, nb_raw, tok, u, sub, out + t * cols + u * 256 + 32 * sub);
+    ifr::dequant_group<T>(w, nu, nb_raw, tok, u, sub, out + (int64_t)tg * cols + u * 256 + 32 * sub);
 }
 
 __device__ float block_sum_256(float v, float *red) {
@@ -575,12 +608,12 @@ __device__ float block_sum_256(float v, float *red) {
     return r;
 }
 
-// MTP input of one draft (mtp_forward!, ModelCPU.jl:2031-2051):
-// cat = [RMSNorm(embed(tok), norm_e); RMSNorm(h, norm_h)], and the draft's
-// position pos + add for the MTP attention layer
+// MTP input of one draft (mtp_forward!, ModelCPU.jl:2031-2051), request
+// b = blockIdx.x: cat = [RMSNorm(embed(tok), norm_e); RMSNorm(h, norm_h)], and
+// the draft's position pos + add for the MTP attention layer
 template <int T>
 __global__ void __launch_bounds__(256) mtp_prep_kernel(const uint8_t *__restrict__ w, int64_t nu, int64_t nb_raw,
-                                                       int64_t rows, const int32_t *tok, const float *h,
+                                                       int64_t rows, const int32_t *tok, int tok_ld, const float *h,
                                                        const float *__restrict__ we, const float *__restrict__ wh,
                                                        float eps, int d, float *__restrict__ cat, int32_t *pos_out,
                                                        const ifr::EngineScalars *sc, int add) {
@@ -588,6 +621,12 @@ __global__ void __launch_bounds__(256) mtp_prep_kernel(const uint8_t *__restrict
     __shared__ float red[8];
     ifr::pdl_trigger();
     ifr::pdl_wait();
+    const int b = blockIdx.x;
+    tok += (int64_t)b * tok_ld;
+    h += (int64_t)b * d;
+    cat += (int64_t)b * 2 * d;
+    pos_out += b;
+    sc += b;
     int64_t t = *tok;
     t = t < 0 ? 0 : (t >= rows ? rows - 1 : t);
     for (int gi = threadIdx.x; gi < nu * 8; gi += 256) ifr::dequant_group<T>(w, nu, nb_raw, t, gi >> 3, gi & 7, e_s + 32 * gi);
@@ -608,57 +647,64 @@ __global__ void __launch_bounds__(256) mtp_prep_kernel(const uint8_t *__restrict
 }
 
 template <int T>
-cudaError_t launch_embed_t(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int n, float *out, cudaStream_t st) {
-    const int64_t tot = (int64_t)n * e.nu * 8;
+cudaError_t launch_embed_t(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int first_ld, int n, int B,
+                           float *out, cudaStream_t st) {
+    const int64_t tot = (int64_t)B * n * e.nu * 8;
     return ifr::launch_k(embed_kernel<T>, dim3((unsigned)((tot + 127) / 128)), dim3(128), 0, st, (const uint8_t *)e.data,
-                         (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, (int64_t)e.cols, vtok, first, n, out);
+                         (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, (int64_t)e.cols, vtok, first, first_ld, n, B,
+                         out);
 }
-cudaError_t launch_embed(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int n, float *out, cudaStream_t st) {
+cudaError_t launch_embed(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int first_ld, int n, int B,
+                         float *out, cudaStream_t st) {
     switch (e.type) {
-    case 12: return launch_embed_t<12>(e, vtok, first, n, out, st);
-    case 13: return launch_embed_t<13>(e, vtok, first, n, out, st);
-    case 14: return launch_embed_t<14>(e, vtok, first, n, out, st);
-    case 8: return launch_embed_t<8>(e, vtok, first, n, out, st);
+    case 12: return launch_embed_t<12>(e, vtok, first, first_ld, n, B, out, st);
+    case 13: return launch_embed_t<13>(e, vtok, first, first_ld, n, B, out, st);
+    case 14: return launch_embed_t<14>(e, vtok, first, first_ld, n, B, out, st);
+    case 8: return launch_embed_t<8>(e, vtok, first, first_ld, n, B, out, st);
     }
     return cudaErrorInvalidValue;
 }
 
 template <int T>
-cudaError_t launch_mtp_prep_t(const ifr::QTensor &e, const int32_t *tok, const float *h, const float *we,
+cudaError_t launch_mtp_prep_t(const ifr::QTensor &e, const int32_t *tok, int tok_ld, const float *h, const float *we,
                               const float *wh, float eps, int d, float *cat, int32_t *pos_out,
-                              const ifr::EngineScalars *sc, int add, cudaStream_t st) {
-    return ifr::launch_k(mtp_prep_kernel<T>, dim3(1), dim3(256), (size_t)e.nu * 256 * 4, st, (const uint8_t *)e.data,
-                         (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, tok, h, we, wh, eps, d, cat, pos_out, sc, add);
+                              const ifr::EngineScalars *sc, int add, int B, cudaStream_t st) {
+    return ifr::launch_k(mtp_prep_kernel<T>, dim3(B), dim3(256), (size_t)e.nu * 256 * 4, st, (const uint8_t *)e.data,
+                         (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, tok, tok_ld, h, we, wh, eps, d, cat, pos_out,
+                         sc, add);
 }
-cudaError_t launch_mtp_prep(const ifr::QTensor &e, const int32_t *tok, const float *h, const float *we,
+cudaError_t launch_mtp_prep(const ifr::QTensor &e, const int32_t *tok, int tok_ld, const float *h, const float *we,
                             const float *wh, float eps, int d, float *cat, int32_t *pos_out,
-                            const ifr::EngineScalars *sc, int add, cudaStream_t st) {
+                            const ifr::EngineScalars *sc, int add, int B, cudaStream_t st) {
     switch (e.type) {
-    case 12: return launch_mtp_prep_t<12>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
-    case 13: return launch_mtp_prep_t<13>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
-    case 14: return launch_mtp_prep_t<14>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
-    case 8: return launch_mtp_prep_t<8>(e, tok, h, we, wh, eps, d, cat, pos_out, sc, add, st);
+    case 12: return launch_mtp_prep_t<12>(e, tok, tok_ld, h, we, wh, eps, d, cat, pos_out, sc, add, B, st);
+    case 13: return launch_mtp_prep_t<13>(e, tok, tok_ld, h, we, wh, eps, d, cat, pos_out, sc, add, B, st);
+    case 14: return launch_mtp_prep_t<14>(e, tok, tok_ld, h, we, wh, eps, d, cat, pos_out, sc, add, B, st);
+    case 8: return launch_mtp_prep_t<8>(e, tok, tok_ld, h, we, wh, eps, d, cat, pos_out, sc, add, B, st);
     }
     return cudaErrorInvalidValue;
 }
 
-// target forward of the n tokens in s->vtok at positions pos.. (device);
-// final-normed hidden of every column in s->hid; logits of columns
-// [logit_from, n) in s->logits (none if logit_from >= n)
-int target_forward(ifr_state *s, int n, int logit_from, bool first_from_state, cudaStream_t st) {
+// target forward of the n tokens per request in vtok (request b: vtok[b *
+// kNMax ..], positions sc[b].pos ..; device); final-normed hidden of every
+// column in s->hid; logits of every column in s->logits when `logits` is set
+int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
-    ECHECK(launch_embed(m->embed.parts[0], s->vtok, first_from_state ? &s->sc->last_token : nullptr, n, s->x, st),
+    const int B = s->B, nc = B * n;
+    const int sc_ld = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
+    ECHECK(launch_embed(m->embed.parts[0], s->vtok, first_from_state ? &s->sc->last_token : nullptr, sc_ld, n, B,
+                        s->x, st),
            "embedding");
     s->launches += 2;  // embedding, final norm
+    const int64_t kv_ld = (int64_t)s->max_ctx * c.n_kv_head * c.head_dim;
     for (int li = 0; li < c.n_layers; li++) {
-        int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, false, st);
+        int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, sc_ld, kv_ld, false, st);
         if (rc) return rc;
     }
-    ifr::rmsnorm(s->x, m->final_norm, s->hid, n, c.hidden, c.rms_eps, c.hidden, c.hidden, st);
-    if (logit_from < n) {
-        int rc = gemv(s, CAT_LM_HEAD, m->lm_head, s->hid + (int64_t)logit_from * c.hidden, n - logit_from,
-                      s->logits, false, st);
+    ifr::rmsnorm(s->x, m->final_norm, s->hid, nc, c.hidden, c.rms_eps, c.hidden, c.hidden, st);
+    if (logits) {
+        int rc = gemv(s, CAT_LM_HEAD, m->lm_head, s->hid, nc, s->logits, false, st);
         if (rc) return rc;
     }
     s->last_n = n;
@@ -670,10 +716,18 @@ __global__ void set_pos_kernel(int32_t *dst, const ifr::EngineScalars *sc, int a
     ifr::pdl_wait();
     *dst = sc->pos + add;
 }
+// after the prompt's last token (one column per request, b = blockIdx.x):
+// its greedy token is emitted and fed next, its hidden feeds the MTP head
 __global__ void prefill_finish_kernel(ifr::EngineScalars *sc, const int32_t *tok, const float *hid, float *mtp_h,
                                       int d, int32_t *log, int log_cap) {
     ifr::pdl_trigger();
     ifr::pdl_wait();
+    const int b = blockIdx.x;
+    sc += b;
+    tok += b;
+    hid += (int64_t)b * d;
+    mtp_h += (int64_t)b * d;
+    log += (int64_t)b * log_cap;
     if (threadIdx.x == 0) {
         sc->last_token = *tok;
         if (sc->n_log < log_cap) log[sc->n_log++] = *tok;
@@ -681,30 +735,34 @@ __global__ void prefill_finish_kernel(ifr::EngineScalars *sc, const int32_t *tok
     for (int i = threadIdx.x; i < d; i += blockDim.x) mtp_h[i] = hid[i];
 }
 
-// MTP draft of gamma tokens into s->vtok[1..gamma]
+// MTP draft of gamma tokens into vtok[b * kNMax + 1 .. gamma] of every request
 int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
-    const int d = c.hidden;
+    const int d = c.hidden, B = s->B;
+    const int sc_ld = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
+    const int64_t kv_ld = (int64_t)s->max_ctx * c.n_kv_head * c.head_dim;
     ifr::XForm norm_out;  // the MTP head's final norm, applied inside the lm_head GEMV
     norm_out.kind = 1;
     norm_out.w = m->mtp_norm;
     norm_out.eps = c.rms_eps;
     for (int j = 1; j <= gamma; j++) {
         const int32_t *tok = j == 1 ? &s->sc->last_token : s->vtok + (j - 1);
+        const int tok_ld = j == 1 ? sc_ld : kNMax;
         // the previous draft's layer output stays in s->x until the fc GEMV below
         // overwrites it, after the prep kernel has read it
         const float *hin = j == 1 ? s->mtp_h : s->x;
-        ECHECK(launch_mtp_prep(m->embed.parts[0], tok, hin, m->mtp_norm_e, m->mtp_norm_h, c.rms_eps, d, s->mtp_cat,
-                               s->mtp_pos, s->sc, j - 1, st),
+        ECHECK(launch_mtp_prep(m->embed.parts[0], tok, tok_ld, hin, m->mtp_norm_e, m->mtp_norm_h, c.rms_eps, d,
+                               s->mtp_cat, s->mtp_pos, s->sc, j - 1, B, st),
                "mtp prep");
-        int rc = gemv(s, CAT_DRAFT_GEMV, m->mtp_fc, s->mtp_cat, 1, s->x, false, st);
+        int rc = gemv(s, CAT_DRAFT_GEMV, m->mtp_fc, s->mtp_cat, B, s->x, false, st);
         if (rc) return rc;
-        if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, true, st))) return rc;
-        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->x, 1, s->logits, false, st, norm_out))) return rc;
+        if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, 1, kv_ld, true, st)))
+            return rc;
+        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->x, B, s->logits, false, st, norm_out))) return rc;
         // greedy draft token straight into the verify tokens
-        ECHECK(ifr::accept_greedy_fused(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->vtok + j, s->acc_scratch,
-                                        s->gcount, st),
+        ECHECK(ifr::accept_greedy_fused(s->logits, nullptr, B, 0, c.vocab, s->acc, s->vtok + j, s->acc_scratch,
+                                        s->gcount, st, 1, kNMax),
                "draft argmax");
         s->launches += 2;  // prep, argmax
     }
@@ -838,30 +896,34 @@ int ifr_model_get_info(const ifr_model *m, ifr_model_info *info) {
     return IFR_OK;
 }
 
-int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
+int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) { return ifr_state_create_batch(m, max_ctx, 1, out); }
+
+int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out) {
     if (!m || !out) return ifr_fail(IFR_ERR_ARG, "NULL argument");
     const ifr_model_info &c = m->info;
     if (max_ctx < 1 || max_ctx > c.context_length)
         return ifr_fail(IFR_ERR_ARG, "max_ctx %d outside 1..context_length (%d)", max_ctx, c.context_length);
+    if (batch < 1 || batch > IFR_MAX_BATCH) return ifr_fail(IFR_ERR_ARG, "batch %d outside 1..%d", batch, IFR_MAX_BATCH);
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(m->ctx));
     ifr_state *s = new ifr_state();
     s->m = m;
+    s->B = batch;
     s->max_ctx = max_ctx;
     s->log_cap = max_ctx + 16;
-    const int d = c.hidden, N = kNMax;
+    const int d = c.hidden, N = kNMax * batch, B = batch;
     int64_t maxproj = (int64_t)(2 * c.n_head + 2 * c.n_kv_head) * c.head_dim;
     if (m->conv_channels + m->inner > maxproj) maxproj = m->conv_channels + m->inner;
     const int64_t ymax = std::max<int64_t>(m->inner, (int64_t)c.n_head * c.head_dim);
     int rc = IFR_OK;
     auto chk = [&](int r) { if (!rc) rc = r; };
-    chk(dalloc(s, &s->sc, 1));
+    chk(dalloc(s, &s->sc, B));
     chk(dalloc(s, &s->vtok, N));
-    chk(dalloc(s, &s->acc, 4));
-    chk(dalloc(s, &s->outtok, N + 1));
-    chk(dalloc(s, &s->mtp_pos, 4));
-    chk(dalloc(s, &s->log, s->log_cap));
+    chk(dalloc(s, &s->acc, B + 4));
+    chk(dalloc(s, &s->outtok, N + B));
+    chk(dalloc(s, &s->mtp_pos, B + 4));
+    chk(dalloc(s, &s->log, (size_t)B * s->log_cap));
     chk(dalloc(s, &s->x, (size_t)N * d));
     chk(dalloc(s, &s->xn, (size_t)N * d));
     chk(dalloc(s, &s->proj, (size_t)N * maxproj));
@@ -870,9 +932,9 @@ int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
     chk(dalloc(s, &s->hmid, (size_t)N * c.ffn));
     chk(dalloc(s, &s->hid, (size_t)N * d));
     chk(dalloc(s, &s->logits, (size_t)N * c.vocab));
-    chk(dalloc(s, &s->mtp_h, d));
-    chk(dalloc(s, &s->mtp_cat, 2 * d));
-    chk(dalloc(s, &s->gcount, 4));
+    chk(dalloc(s, &s->mtp_h, (size_t)B * d));
+    chk(dalloc(s, &s->mtp_cat, (size_t)B * 2 * d));
+    chk(dalloc(s, &s->gcount, B + 4));
     const int half = c.rotary_dim / 2;
     chk(dalloc(s, &s->rope_cos, (size_t)max_ctx * half));
     chk(dalloc(s, &s->rope_sin, (size_t)max_ctx * half));
@@ -882,12 +944,12 @@ int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
     s->rkv.assign(c.n_layers, nullptr);
     s->kc.assign(c.n_layers, nullptr);
     s->vc.assign(c.n_layers, nullptr);
-    const size_t kvn = (size_t)max_ctx * c.n_kv_head * c.head_dim;
+    const size_t kvn = (size_t)B * max_ctx * c.n_kv_head * c.head_dim;
     for (int i = 0; !rc && i < c.n_layers; i++) {
         if (m->layers[i].ssm) {
             const int hd = c.ssm_head_dim;
-            chk(dalloc(s, &s->S[i], (size_t)c.ssm_heads * hd * hd));
-            chk(dalloc(s, &s->hist[i], (size_t)(c.conv_kernel - 1) * m->conv_channels));
+            chk(dalloc(s, &s->S[i], (size_t)B * c.ssm_heads * hd * hd));
+            chk(dalloc(s, &s->hist[i], (size_t)B * (c.conv_kernel - 1) * m->conv_channels));
             chk(dalloc(s, &s->rq[i], (size_t)N * m->conv_channels));
             chk(dalloc(s, &s->rkv[i], (size_t)c.ssm_heads * N * (2 * hd + 2)));
         } else {
@@ -899,14 +961,39 @@ int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
         chk(dalloc(s, &s->mtp_kc, kvn));
         chk(dalloc(s, &s->mtp_vc, kvn));
     }
-    const int64_t accb = ifr::accept_greedy_scratch_bytes(1, kNMax, c.vocab);
+    const int64_t accb = ifr::accept_greedy_scratch_bytes(B, kNMax, c.vocab);
     if (!rc) {
         void *p = nullptr;
         cudaError_t e = cudaMalloc(&p, accb);
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "cudaMalloc(accept scratch)");
         else { s->allocs.push_back(p); s->acc_scratch = p; }
     }
-    if (!rc && cudaMallocHost((void **)&s->h_tok, sizeof(int32_t) * 64) != cudaSuccess)
+    if (!rc && N > kNMax) {
+        // dense tensor-core GEMMs of up to B * kNMax columns: the largest plan of all projections
+        int64_t need = 0;
+        auto plan = [&](const Proj &p) {
+            for (auto &q : p.parts) need = std::max(need, ifr::qgemm_dense_scratch_bytes(q, N));
+        };
+        for (auto &L : m->layers) {
+            plan(L.proj);
+            plan(L.out);
+            plan(L.gate_up);
+            plan(L.down);
+        }
+        plan(m->lm_head);
+        if (m->has_mtp) {
+            plan(m->mtp_fc);
+            plan(m->mtp_layer.proj);
+            plan(m->mtp_layer.out);
+            plan(m->mtp_layer.gate_up);
+            plan(m->mtp_layer.down);
+        }
+        void *p = nullptr;
+        cudaError_t e = cudaMalloc(&p, need);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "cudaMalloc(dense scratch)");
+        else { s->allocs.push_back(p); s->dense = p; s->dense_bytes = need; }
+    }
+    if (!rc && cudaMallocHost((void **)&s->h_tok, sizeof(int32_t) * (N + 64)) != cudaSuccess)
         rc = ifr_fail(IFR_ERR_NOMEM, "cudaMallocHost failed");
     if (!rc) {
         // RoPE tables as the reference builds them (ModelCPU.jl:136-154):
@@ -927,7 +1014,8 @@ int ifr_state_create(ifr_model *m, int max_ctx, ifr_state **out) {
     if (!rc) {
         ifr::EngineScalars init{};
         init.a_prev = -1;
-        if (cudaMemcpy(s->sc, &init, sizeof init, cudaMemcpyHostToDevice) != cudaSuccess)
+        std::vector<ifr::EngineScalars> all(B, init);
+        if (cudaMemcpy(s->sc, all.data(), sizeof(init) * B, cudaMemcpyHostToDevice) != cudaSuccess)
             rc = ifr_fail(IFR_ERR_CUDA, "H2D scalars");
     }
     cudaSetDevice(prev);
@@ -959,21 +1047,33 @@ int ifr_state_reset(ifr_state *s) {
     cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
     ifr::EngineScalars init{};
     init.a_prev = -1;
-    ECHECK(cudaMemcpyAsync(s->sc, &init, sizeof init, cudaMemcpyHostToDevice, st), "reset scalars");
+    std::vector<ifr::EngineScalars> all(s->B, init);
+    ECHECK(cudaStreamSynchronize(st), "reset");
+    ECHECK(cudaMemcpy(s->sc, all.data(), sizeof(init) * s->B, cudaMemcpyHostToDevice), "reset scalars");
     for (int i = 0; i < c.n_layers; i++)
         if (s->S[i]) {
             const int hd = c.ssm_head_dim;
-            ECHECK(cudaMemsetAsync(s->S[i], 0, (size_t)c.ssm_heads * hd * hd * 4, st), "reset state");
-            ECHECK(cudaMemsetAsync(s->hist[i], 0, (size_t)(c.conv_kernel - 1) * s->m->conv_channels * 4, st), "reset conv");
+            ECHECK(cudaMemsetAsync(s->S[i], 0, (size_t)s->B * c.ssm_heads * hd * hd * 4, st), "reset state");
+            ECHECK(cudaMemsetAsync(s->hist[i], 0, (size_t)s->B * (c.conv_kernel - 1) * s->m->conv_channels * 4, st),
+                   "reset conv");
         }
     ECHECK(cudaStreamSynchronize(st), "reset");
     return IFR_OK;
 }
 
 int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (s->B != 1) return ifr_fail(IFR_ERR_ARG, "batched state: use ifr_prefill_batch");
+    return ifr_prefill_batch(s, tokens, n, first_token);
+}
+
+// every request's prompt (n tokens each, row-major [batch][n]) in chunks of up
+// to kNMax tokens per request; the last token alone, with logits
+int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first_tokens) {
     if (!s || !tokens || n < 1) return ifr_fail(IFR_ERR_ARG, "invalid prefill arguments");
     const ifr_model_info &c = s->m->info;
-    for (int i = 0; i < n; i++)
+    const int B = s->B;
+    for (int64_t i = 0; i < (int64_t)B * n; i++)
         if (tokens[i] < 0 || tokens[i] >= c.vocab) return ifr_fail(IFR_ERR_ARG, "token %d out of range", tokens[i]);
     if (n + kNMax > s->max_ctx) return ifr_fail(IFR_ERR_ARG, "prompt of %d tokens does not fit max_ctx=%d", n, s->max_ctx);
     cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
@@ -981,28 +1081,28 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(s->m->ctx));
     int rc = IFR_OK;
-    for (int i0 = 0; !rc && i0 < n; i0 += kNMax) {
-        const int k = std::min(kNMax, n - i0);
-        memcpy(s->h_tok, tokens + i0, sizeof(int32_t) * k);
-        cudaError_t e = cudaMemcpyAsync(s->vtok, s->h_tok, sizeof(int32_t) * k, cudaMemcpyHostToDevice, st);
+    for (int i0 = 0; !rc && i0 < n;) {
+        const bool last = i0 == n - 1;
+        const int k = last ? 1 : std::min(kNMax, n - 1 - i0);
+        for (int b = 0; b < B; b++) memcpy(s->h_tok + (int64_t)b * kNMax, tokens + (int64_t)b * n + i0, sizeof(int32_t) * k);
+        cudaError_t e = cudaMemcpyAsync(s->vtok, s->h_tok, sizeof(int32_t) * kNMax * B, cudaMemcpyHostToDevice, st);
         if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "H2D prompt"); break; }
-        const bool last = i0 + k == n;
-        rc = target_forward(s, k, last ? k - 1 : k, false, st);
-        if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, st);
+        rc = target_forward(s, k, last, false, st);
+        if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, B, st);
         if (!rc && last) {
-            e = ifr::accept_greedy_fused(s->logits, nullptr, 1, 0, c.vocab, s->acc, s->outtok, s->acc_scratch,
+            e = ifr::accept_greedy_fused(s->logits, nullptr, B, 0, c.vocab, s->acc, s->outtok, s->acc_scratch,
                                          s->gcount, st);
             if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "argmax"); break; }
-            e = ifr::launch_k(prefill_finish_kernel, dim3(1), dim3(256), 0, st, s->sc, (const int32_t *)s->outtok,
-                              (const float *)(s->hid + (int64_t)(k - 1) * c.hidden), s->mtp_h, (int)c.hidden, s->log,
-                              (int)s->log_cap);
+            e = ifr::launch_k(prefill_finish_kernel, dim3(B), dim3(256), 0, st, s->sc, (const int32_t *)s->outtok,
+                              (const float *)s->hid, s->mtp_h, (int)c.hidden, s->log, (int)s->log_cap);
             if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prefill finish"); break; }
         }
         // the prompt tokens buffer is reused by the next chunk
         if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = ifr_cuda_fail(cudaGetLastError(), "prefill");
+        i0 += k;
     }
-    if (!rc && first_token) {
-        cudaError_t e = cudaMemcpy(first_token, s->outtok, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (!rc && first_tokens) {
+        cudaError_t e = cudaMemcpy(first_tokens, s->outtok, sizeof(int32_t) * B, cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "D2H first token");
     }
     cudaSetDevice(prev);
@@ -1013,18 +1113,20 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
 
 namespace {
 // the device work of one spec step (capturable): MTP drafts (or drafts
-// already in vtok[1..gamma]), verify, greedy accept, commit
+// already in vtok[b * kNMax + 1 .. gamma]), verify, greedy accept, commit
 int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st) {
     const ifr_model_info &c = s->m->info;
+    const int B = s->B;
     int rc = IFR_OK;
     if (gamma > 0 && mtp) rc = mtp_draft(s, gamma, st);
-    if (!rc) rc = target_forward(s, gamma + 1, 0, true, st);
+    if (!rc) rc = target_forward(s, gamma + 1, true, true, st);
     if (!rc) {
-        cudaError_t e = ifr::accept_greedy_fused(s->logits, s->vtok + 1, 1, gamma, c.vocab, s->acc, s->outtok,
-                                                 s->acc_scratch, s->gcount, st);
+        cudaError_t e = ifr::accept_greedy_fused(s->logits, s->vtok + 1, B, gamma, c.vocab, s->acc, s->outtok,
+                                                 s->acc_scratch, s->gcount, st, kNMax, gamma + 1);
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "accept_greedy");
     }
-    if (!rc) ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, st);
+    if (!rc)
+        ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, B, st);
     s->launches += 2;  // accept, commit
     return rc;
 }
@@ -1037,18 +1139,22 @@ int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts) {
     if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
     if (gamma > 0 && !drafts && !s->m->has_mtp) return ifr_fail(IFR_ERR_ARG, "no drafts given and the model has no MTP head");
     const ifr_model_info &c = s->m->info;
+    const int B = s->B;
     cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(s->m->ctx));
     int rc = IFR_OK;
     if (gamma > 0 && drafts) {
-        for (int i = 0; i < gamma; i++)
+        for (int64_t i = 0; i < (int64_t)B * gamma; i++)
             if (drafts[i] < 0 || drafts[i] >= c.vocab) { cudaSetDevice(prev); return ifr_fail(IFR_ERR_ARG, "draft token out of range"); }
         cudaError_t e = cudaStreamSynchronize(st);  // staging buffer reuse
         if (e == cudaSuccess) {
-            memcpy(s->h_tok, drafts, sizeof(int32_t) * gamma);
-            e = cudaMemcpyAsync(s->vtok + 1, s->h_tok, sizeof(int32_t) * gamma, cudaMemcpyHostToDevice, st);
+            // drafts [batch][gamma] into vtok[b * kNMax + 1 ..]; slot 0 is set on the device
+            for (int b = 0; b < B; b++) memcpy(s->h_tok + (int64_t)b * kNMax + 1, drafts + (int64_t)b * gamma, sizeof(int32_t) * gamma);
+            for (int b = 0; b < B && e == cudaSuccess; b++)
+                e = cudaMemcpyAsync(s->vtok + (int64_t)b * kNMax + 1, s->h_tok + (int64_t)b * kNMax + 1,
+                                    sizeof(int32_t) * gamma, cudaMemcpyHostToDevice, st);
         }
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "H2D drafts");
         if (!rc) rc = spec_step_device(s, gamma, false, st);
@@ -1133,7 +1239,7 @@ int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count,
 }
 
 int ifr_gemv_pass(ifr_state *s, int ncols) {
-    if (!s || ncols < 1 || ncols > kNMax) return ifr_fail(IFR_ERR_ARG, "ncols must be in 1..%d", kNMax);
+    if (!s || ncols < 1 || ncols > kNMax * s->B) return ifr_fail(IFR_ERR_ARG, "ncols must be in 1..%d", kNMax * s->B);
     cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
     int prev = 0;
     cudaGetDevice(&prev);
@@ -1169,14 +1275,21 @@ int ifr_gemv_pass(ifr_state *s, int ncols) {
 }
 
 int ifr_state_read(ifr_state *s, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars) {
+    return ifr_state_read_request(s, 0, tokens, max_tokens, n_tokens, scalars);
+}
+
+int ifr_state_read_request(ifr_state *s, int b, int32_t *tokens, int max_tokens, int *n_tokens, int32_t *scalars) {
     if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (b < 0 || b >= s->B) return ifr_fail(IFR_ERR_ARG, "request %d outside 0..%d", b, s->B - 1);
     cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
     ECHECK(cudaStreamSynchronize(st), "sync");
     ifr::EngineScalars h{};
-    ECHECK(cudaMemcpy(&h, s->sc, sizeof h, cudaMemcpyDeviceToHost), "D2H scalars");
+    ECHECK(cudaMemcpy(&h, s->sc + b, sizeof h, cudaMemcpyDeviceToHost), "D2H scalars");
     if (n_tokens) *n_tokens = h.n_log;
     if (tokens && max_tokens > 0 && h.n_log > 0)
-        ECHECK(cudaMemcpy(tokens, s->log, sizeof(int32_t) * std::min(max_tokens, h.n_log), cudaMemcpyDeviceToHost), "D2H log");
+        ECHECK(cudaMemcpy(tokens, s->log + (int64_t)b * s->log_cap, sizeof(int32_t) * std::min(max_tokens, h.n_log),
+                          cudaMemcpyDeviceToHost),
+               "D2H log");
     if (scalars) {
         scalars[0] = h.pos;
         scalars[1] = h.last_accept;
@@ -1191,11 +1304,16 @@ int ifr_state_last_verify(ifr_state *s, float *logits, float *hidden, int32_t *t
     const ifr_model_info &c = s->m->info;
     cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
     ECHECK(cudaStreamSynchronize(st), "sync");
-    const int n = s->last_n;
+    const int n = s->last_n, B = s->B;
     if (n_cols) *n_cols = n;
-    if (logits) ECHECK(cudaMemcpy(logits, s->logits, sizeof(float) * n * c.vocab, cudaMemcpyDeviceToHost), "D2H logits");
-    if (hidden) ECHECK(cudaMemcpy(hidden, s->hid, sizeof(float) * n * c.hidden, cudaMemcpyDeviceToHost), "D2H hidden");
-    if (tokens) ECHECK(cudaMemcpy(tokens, s->vtok, sizeof(int32_t) * n, cudaMemcpyDeviceToHost), "D2H tokens");
+    if (logits)
+        ECHECK(cudaMemcpy(logits, s->logits, sizeof(float) * B * n * c.vocab, cudaMemcpyDeviceToHost), "D2H logits");
+    if (hidden)
+        ECHECK(cudaMemcpy(hidden, s->hid, sizeof(float) * B * n * c.hidden, cudaMemcpyDeviceToHost), "D2H hidden");
+    for (int b = 0; tokens && b < B; b++)
+        ECHECK(cudaMemcpy(tokens + (int64_t)b * n, s->vtok + (int64_t)b * kNMax, sizeof(int32_t) * n,
+                          cudaMemcpyDeviceToHost),
+               "D2H tokens");
     return IFR_OK;
 }
 

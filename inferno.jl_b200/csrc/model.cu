@@ -1,4 +1,5 @@
-// Layer kernels of the Qwen3.5-hybrid verify step (N <= 8 tokens per call).
+// Layer kernels of the Qwen3.5-hybrid verify step (N <= 8 tokens per request
+// and call; batched calls put the requests on blockIdx.z).
 //
 // Reference semantics: src/ModelCPU.jl of Inferno.jl (line numbers below).
 // All arithmetic is f32 except the SSM gates, which the reference evaluates in
@@ -98,6 +99,7 @@ constexpr int kSsmSplit = 8;
 
 template <int HD>
 __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_step_kernel(SsmArgs a) {
+    // (a is a by-value copy: the per-request offsets below are local)
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     constexpr int RPC = HD / kSsmSplit;  // state rows (and q, k dims) per CTA
@@ -120,6 +122,17 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     __shared__ float red_n[8][2 * kMaxN];
     pdl_trigger();
     pdl_wait();
+    {  // request blockIdx.z of a batched call
+        const int64_t b = blockIdx.z;
+        a.proj += b * a.N * a.ldp;
+        a.xn += b * a.N * a.d;
+        a.y += b * a.N * a.ldy;
+        a.S += b * a.b_S;
+        a.hist += b * a.b_hist;
+        a.rq += b * a.b_rq;
+        a.rkv += b * a.b_rkv;
+        a.a_prev += b * a.b_prev;
+    }
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
 
     // 1. conv of the owned channels over the window: committed history (K-1),
@@ -302,9 +315,9 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     cluster.sync();  // peers may still read this CTA's shared memory
 }
 
-cudaError_t ssm_step(const SsmArgs &a, int head_dim, cudaStream_t s) {
-    if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4) return cudaErrorInvalidValue;
-    const dim3 grid(kSsmSplit, a.H);
+cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s) {
+    if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4 || batch < 1) return cudaErrorInvalidValue;
+    const dim3 grid(kSsmSplit, a.H, batch);
     if (head_dim == 128) return launch_k(ssm_step_kernel<128>, grid, dim3(256), 0, s, a);
     if (head_dim == 64) return launch_k(ssm_step_kernel<64>, grid, dim3(256), 0, s, a);
     return cudaErrorInvalidValue;
@@ -344,6 +357,14 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     const int N = a.N, ratio = a.nh / a.nkv, kvh = h / ratio;
     pdl_trigger();
     pdl_wait();
+    {  // request blockIdx.z of a batched call
+        const int64_t b = blockIdx.z;
+        a.qkv += b * a.N * a.ldq;
+        a.out += b * a.N * a.ldo;
+        a.kc += b * a.b_kv;
+        a.vc += b * a.b_kv;
+        a.pos += b * a.b_pos;
+    }
     const int p0 = *a.pos;
     const int nkeys = p0 + N;
     const int per = (nkeys + kAttnSplit - 1) / kAttnSplit;
@@ -496,9 +517,9 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     cluster.sync();  // peers may still read this CTA's shared memory
 }
 
-cudaError_t attn_step(const AttnArgs &a, cudaStream_t s) {
-    if (a.N < 1 || a.N > kMaxN || a.nh % a.nkv) return cudaErrorInvalidValue;
-    const dim3 grid(kAttnSplit, a.nh);
+cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s) {
+    if (a.N < 1 || a.N > kMaxN || a.nh % a.nkv || batch < 1) return cudaErrorInvalidValue;
+    const dim3 grid(kAttnSplit, a.nh, batch);
     if (a.hd == 256) return launch_k(attn_step_kernel<256>, grid, dim3(256), 0, s, a);
     if (a.hd == 128) return launch_k(attn_step_kernel<128>, grid, dim3(256), 0, s, a);
     if (a.hd == 64) return launch_k(attn_step_kernel<64>, grid, dim3(256), 0, s, a);
@@ -516,6 +537,15 @@ __global__ void commit_kernel(EngineScalars *sc, const int32_t *acc_dev, const i
     __shared__ int acc_s;
     pdl_trigger();
     pdl_wait();
+    {  // request blockIdx.x
+        const int b = blockIdx.x;
+        sc += b;
+        acc_dev += b;
+        out_tok += (int64_t)b * n;
+        if (hid) hid += (int64_t)b * n * d;
+        if (mtp_h) mtp_h += (int64_t)b * d;
+        log += (int64_t)b * log_cap;
+    }
     if (threadIdx.x == 0) {
         const int acc = all ? n - 1 : *acc_dev;
         acc_s = acc;
@@ -535,8 +565,9 @@ __global__ void commit_kernel(EngineScalars *sc, const int32_t *acc_dev, const i
 }
 
 void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,
-            float *mtp_h, int d, int32_t *log, int log_cap, cudaStream_t s) {
-    launch_k(commit_kernel, dim3(1), dim3(256), 0, s, sc, acc, out_tok, n, all ? 1 : 0, hid, mtp_h, d, log, log_cap);
+            float *mtp_h, int d, int32_t *log, int log_cap, int batch, cudaStream_t s) {
+    launch_k(commit_kernel, dim3(batch), dim3(256), 0, s, sc, acc, out_tok, n, all ? 1 : 0, hid, mtp_h, d, log,
+             log_cap);
 }
 
 // copy a device scalar token into a slot of the verify token vector

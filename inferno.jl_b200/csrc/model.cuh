@@ -17,6 +17,9 @@ struct EngineScalars {
     int32_t pad[2];
 };
 
+// Batched calls: blockIdx.z = request b; per-request data is offset by b
+// times the b_* strides (elements), and a request's N columns of proj, xn and
+// y start at column b * N.
 struct SsmArgs {
     const float *proj;   // [N][ldp]: conv inputs q|k|v (C) then z (inner)
     int64_t ldp;
@@ -34,6 +37,8 @@ struct SsmArgs {
     int64_t ldy;
     int N, H, C, K;
     float eps;
+    int64_t b_S = 0, b_hist = 0, b_rq = 0, b_rkv = 0;  // per-request strides
+    int b_prev = 0;                                    // stride of a_prev (int32)
 };
 
 struct AttnArgs {
@@ -47,15 +52,19 @@ struct AttnArgs {
     int64_t ldo;
     int N, nh, nkv, hd, rotary_dim;
     float eps;
+    int64_t b_kv = 0;    // per-request stride of kc / vc
+    int b_pos = 0;       // stride of pos (int32)
 };
 
 void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float eps, int64_t ldx, int64_t ldo,
              cudaStream_t s);
 void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s);
-cudaError_t ssm_step(const SsmArgs &a, int head_dim, cudaStream_t s);
-cudaError_t attn_step(const AttnArgs &a, cudaStream_t s);
+cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s);
+cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s);
+// per request b (grid of `batch` CTAs): sc + b, acc + b, out_tok + b * n,
+// hid + b * n * d, mtp_h + b * d, log + b * log_cap
 void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,
-            float *mtp_h, int d, int32_t *log, int log_cap, cudaStream_t s);
+            float *mtp_h, int d, int32_t *log, int log_cap, int batch, cudaStream_t s);
 void set_token(int32_t *dst, const int32_t *src, cudaStream_t s);
 
 }  // namespace ifr

@@ -39,14 +39,19 @@ class Model:
 
 
 class State:
-    """KV caches, SSM states and the emitted-token log of one sequence."""
+    """KV caches, SSM states and the emitted-token logs of `batch` sequences
+    that advance together (one sequence by default)."""
 
-    def __init__(self, model, max_ctx):
+    def __init__(self, model, max_ctx, batch=1):
         self.model = model
         h = ctypes.c_void_p()
-        check(load().ifr_state_create(model.handle, int(max_ctx), ctypes.byref(h)))
+        if batch == 1:
+            check(load().ifr_state_create(model.handle, int(max_ctx), ctypes.byref(h)))
+        else:
+            check(load().ifr_state_create_batch(model.handle, int(max_ctx), int(batch), ctypes.byref(h)))
         self.handle = h
         self.max_ctx = max_ctx
+        self.batch = batch
 
     def free(self):
         if getattr(self, "handle", None):
@@ -63,17 +68,24 @@ class State:
         check(load().ifr_state_reset(self.handle))
 
     def prefill(self, tokens):
+        """tokens [n] (one sequence) or [batch][n]; returns the first greedy token(s)"""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
-        first = ctypes.c_int32()
-        check(load().ifr_prefill(self.handle, t.ctypes.data_as(ctypes.c_void_p), len(t), ctypes.byref(first)))
-        return first.value
+        if self.batch == 1 and t.ndim == 1:
+            first = ctypes.c_int32()
+            check(load().ifr_prefill(self.handle, t.ctypes.data_as(ctypes.c_void_p), len(t), ctypes.byref(first)))
+            return first.value
+        t = t.reshape(self.batch, -1)
+        first = np.empty(self.batch, np.int32)
+        check(load().ifr_prefill_batch(self.handle, t.ctypes.data_as(ctypes.c_void_p), t.shape[1],
+                                       first.ctypes.data_as(ctypes.c_void_p)))
+        return first
 
     def spec_step(self, gamma, drafts=None):
         """asynchronous: MTP draft (or given drafts) -> verify -> accept -> commit"""
         d = None
         if drafts is not None:
             d = np.ascontiguousarray(drafts, dtype=np.int32)
-            assert len(d) == gamma
+            assert d.size == gamma * self.batch
         check(load().ifr_spec_step(self.handle, int(gamma), d.ctypes.data_as(ctypes.c_void_p) if d is not None else None))
 
     def capture(self, gamma, steps):
@@ -101,22 +113,25 @@ class State:
         """enqueue the verify's dequant-GEMV launches alone (scratch activations)"""
         check(load().ifr_gemv_pass(self.handle, int(ncols)))
 
-    def read(self):
-        """(emitted tokens, position, last accept count, steps)"""
+    def read(self, b=0):
+        """(emitted tokens, position, last accept count, steps) of request b"""
         n = ctypes.c_int()
         sc = (ctypes.c_int32 * 4)()
         buf = np.empty(self.max_ctx + 16, dtype=np.int32)
-        check(load().ifr_state_read(self.handle, buf.ctypes.data_as(ctypes.c_void_p), len(buf), ctypes.byref(n), sc))
+        check(load().ifr_state_read_request(self.handle, int(b), buf.ctypes.data_as(ctypes.c_void_p), len(buf),
+                                            ctypes.byref(n), sc))
         return buf[:n.value].copy(), sc[0], sc[1], sc[2]
 
     def last_verify(self):
-        """(logits [n][vocab], hidden [n][hidden], tokens [n]) of the last forward"""
+        """(logits [batch * n][vocab], hidden [batch * n][hidden], tokens [batch * n])
+        of the last forward, request-major"""
         info = self.model.info
         n = ctypes.c_int()
         check(load().ifr_state_last_verify(self.handle, None, None, None, ctypes.byref(n)))
-        lg = np.empty((n.value, info.vocab), np.float32)
-        hd = np.empty((n.value, info.hidden), np.float32)
-        tk = np.empty(n.value, np.int32)
+        rows = n.value * self.batch
+        lg = np.empty((rows, info.vocab), np.float32)
+        hd = np.empty((rows, info.hidden), np.float32)
+        tk = np.empty(rows, np.int32)
         check(load().ifr_state_last_verify(self.handle, lg.ctypes.data_as(ctypes.c_void_p),
                                            hd.ctypes.data_as(ctypes.c_void_p),
                                            tk.ctypes.data_as(ctypes.c_void_p), ctypes.byref(n)))

@@ -10,7 +10,9 @@ Presets follow the benchmark configurations:
   mini  a small model of the same structure for fast tests
 Weights are N(0, 0.02) (the layer norms, which GGUF stores as 1 + w, are
 1 + N(0, 0.02); ssm_a = -exp(N(0, 0.5)); conv1d N(0, 0.5)), quantized with the
-library's own encoder.  Tensor names and metadata keys are those the
+library's own encoder.  Presets with `row_pool` (9b) draw that many rows per
+matrix and repeat them down the matrix, so that the 5 GB model is built in
+seconds; the bytes per weight and the kernels' work are unchanged.  Tensor names and metadata keys are those the
 reference's loader reads (src/LoaderCPU.jl:439-694).
 """
 import os
@@ -28,7 +30,7 @@ PRESETS = {
     "9b": dict(hidden=4096, n_layers=32, n_head=16, n_kv_head=4, head_dim=256, rope_frac=0.25,
                ffn=12288, vocab=151936, ssm_heads=32, ssm_head_dim=128, conv_kernel=4,
                attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q6_K, emb=G.GGML_Q6_K, mtp=True,
-               context=8192),
+               context=8192, row_pool=1024),
     "mini": dict(hidden=256, n_layers=4, n_head=4, n_kv_head=2, head_dim=64, rope_frac=0.25,
                  ffn=512, vocab=4096, ssm_heads=4, ssm_head_dim=64, conv_kernel=4,
                  attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=True,
@@ -71,9 +73,15 @@ def build(path, preset="tiny", seed=0, **overrides):
     def rng():
         return np.random.default_rng(root.integers(1 << 62))
 
+    pool = cfg.get("row_pool", 0)
+
     def mat(name, rows, cols, qtype, std=0.02):
-        x = rng().standard_normal((rows, cols), dtype=np.float32) * np.float32(std)
-        w.add_tensor(name, [cols, rows], qtype, _quant(qtype, x))
+        n = min(rows, pool) if pool else rows
+        x = rng().standard_normal((n, cols), dtype=np.float32) * np.float32(std)
+        q = _quant(qtype, x)
+        if n < rows:  # quantization is row-wise: repeat the quantized rows
+            q = np.tile(q.reshape(n, -1), ((rows + n - 1) // n, 1))[:rows].ravel()
+        w.add_tensor(name, [cols, rows], qtype, q)
 
     def f32(name, dims, values):
         w.add_tensor(name, dims, G.GGML_F32, np.ascontiguousarray(values, dtype=np.float32))

@@ -1,0 +1,113 @@
+"""GPU parity of the batched engine (ifr_state_create_batch: several requests
+advancing together) against the CPU oracle run on each request's prompt alone,
+through the C ABI.
+
+  * exact path (every projection on the small-N kernel): the same bar as the
+    one-request engine - drafts, accept counts and emitted tokens equal,
+    verify logits within LOGIT_TOL;
+  * dense path (projections of many columns on the tcgen05 kernel, fp16
+    operands): verify logits within DENSE_TOL of the oracle, the north star's
+    bound for reduced-precision accumulation, with forced drafts so both sides
+    see the same tokens.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-4   # exact path, f32 accumulation on both sides
+DENSE_TOL = 1e-2   # dense path: fp16 operands, f32 accumulation
+
+
+@pytest.fixture(scope="module")
+def mini(pkg, O, ctx):
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model
+    path = synth.cached("mini", seed=1)
+    model = Model(ctx, path)
+    om = O.OracleModel(gguf.GGUFFile(path), 512)
+    return model, om
+
+
+def _prompts(vocab, B, n):
+    from inferno_b200 import synth
+    return np.stack([synth.prompt(vocab, n, seed=100 + b) for b in range(B)])
+
+
+@pytest.mark.parametrize("B,G,dense_min", [(2, 3, None), (3, 4, 10**6), (5, 2, 10**6)])
+def test_batch_exact_matches_oracle(O, ctx, mini, B, G, dense_min):
+    from inferno_b200.engine import State
+    model, om = mini
+    V = model.info.vocab
+    steps = 5
+    prompts = _prompts(V, B, 21)
+    ref = [om.spec_decode(list(p), steps, G) for p in prompts]
+    if dense_min:
+        ctx.set_dense_min_cols(dense_min)
+    try:
+        st = State(model, 512, batch=B)
+        firsts = st.prefill(prompts)
+        assert [int(f) for f in firsts] == [r[0][0] for r in ref]
+        for s in range(steps):
+            st.spec_step(G)
+            lg, hd, tk = st.last_verify()
+            lg = lg.reshape(B, G + 1, V)
+            hd = hd.reshape(B, G + 1, -1)
+            tk = tk.reshape(B, G + 1)
+            for b in range(B):
+                r = ref[b][1][s]
+                assert list(tk[b, 1:]) == r["drafts"], (b, s)
+                assert O.norm_rel(lg[b], r["logits"]).max() < LOGIT_TOL, (b, s)
+                assert O.norm_rel(hd[b], r["hidden"]).max() < LOGIT_TOL, (b, s)
+                _, pos, acc, nst = st.read(b)
+                assert acc == r["acc"] and nst == s + 1 and pos == r["pos"] + acc + 1, (b, s)
+        for b in range(B):
+            toks, *_ = st.read(b)
+            assert list(toks) == ref[b][0], b
+        st.free()
+    finally:
+        ctx.set_dense_min_cols(24)
+
+
+def test_batch_dense_logits_within_tolerance(O, ctx, mini):
+    """prefill (B x 8 columns per chunk) and a verify of B x 5 columns on the
+    dense tensor-core path; drafts forced to the oracle's greedy continuation"""
+    from inferno_b200.engine import State
+    model, om = mini
+    V = model.info.vocab
+    B, G = 6, 4
+    prompts = _prompts(V, B, 30)
+    greedy = [om.greedy(list(p), G + 2) for p in prompts]
+    ctx.set_dense_min_cols(8)
+    try:
+        st = State(model, 512, batch=B)
+        firsts = st.prefill(prompts)
+        assert [int(f) for f in firsts] == [g[0] for g in greedy]
+        drafts = np.array([g[1:G + 1] for g in greedy], np.int32)
+        st.spec_step(G, drafts)
+        lg, _, tk = st.last_verify()
+        lg = lg.reshape(B, G + 1, V)
+        for b, p in enumerate(prompts):
+            # oracle logits of the same columns: prompt, then [first, drafts]
+            om.reset()
+            for i, t in enumerate(p):
+                om.forward_token(int(t), i)
+            cols = greedy[b][:G + 1]
+            ref = np.stack([om.forward_token(t, len(p) + j)[0] for j, t in enumerate(cols)])
+            assert list(tk.reshape(B, G + 1)[b]) == cols
+            err = O.norm_rel(lg[b], ref)
+            assert err.max() < DENSE_TOL, (b, err)
+        _, pos, acc, _ = st.read(0)
+        assert acc == G  # the forced drafts are the greedy continuation
+        st.free()
+    finally:
+        ctx.set_dense_min_cols(24)
+
+
+def test_batch_argument_errors(pkg, mini):
+    from inferno_b200._lib import load
+    import ctypes
+    model, _ = mini
+    h = ctypes.c_void_p()
+    assert load().ifr_state_create_batch(model.handle, 512, 0, ctypes.byref(h)) != 0
+    assert load().ifr_state_create_batch(model.handle, 512, 10**6, ctypes.byref(h)) != 0
