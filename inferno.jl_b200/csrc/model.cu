@@ -116,7 +116,7 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     __shared__ __align__(16) float rk[kMaxN][HD];
     __shared__ float rv[kMaxN][RPC];
     __shared__ float rdec[kMaxN], rbeta[kMaxN], ndec[kMaxN], nbeta[kMaxN];
-    __shared__ float ab[2][kMaxN];
+    __shared__ float ab[2][kMaxN], ab_part[2][kMaxN];
     __shared__ float ys[kMaxN][RPC];
     __shared__ float ssq[kMaxN];
     __shared__ float red_n[8][2 * kMaxN];
@@ -176,14 +176,17 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
             }
         }
     }
-    // 2. alpha / beta projections of the new tokens (ssm_alpha/beta . xn),
-    //    block-wide with all loads independent
+    // 2. alpha / beta projections of the new tokens (ssm_alpha/beta . xn): CTA
+    //    `rank` sums its d / kSsmSplit slice, the partials are added across the
+    //    cluster in rank order after the next cluster barrier (step 5)
     {
         float pa[kMaxN], pb[kMaxN];
 #pragma unroll
         for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = 0.f;
         const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
-        for (int i = tid; i < a.d; i += 256) {
+        const int per = (a.d + kSsmSplit - 1) / kSsmSplit;
+        const int i0 = rank * per, i1 = min(a.d, i0 + per);
+        for (int i = i0 + tid; i < i1; i += 256) {
             const float al = wa[i], be = wb[i];
 #pragma unroll
             for (int t = 0; t < kMaxN; t++)
@@ -206,7 +209,7 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
             const int which = tid / N, t = tid % N;
             float v = 0.f;
             for (int w8 = 0; w8 < 8; w8++) v += red_n[w8][which * kMaxN + t];
-            ab[which][t] = v;
+            ab_part[which][t] = v;
         }
     }
     // 3. the previous call's replay record: k (all dims), own v rows, decay, beta
@@ -218,11 +221,18 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
         rbeta[tid] = rec[tid * REC + 2 * HD + 1];
     }
     cluster.sync();  // conv slices visible to the cluster; old record read by all
-    // 4. the head's q and k, gathered from the owners
+    // 4. the head's q and k, gathered from the owners; alpha / beta summed over
+    //    the cluster's slices
     for (int i = tid; i < N * HD; i += 256) {
         const int t = i / HD, c = i % HD, src = c / RPC, ci = c % RPC;
         xq[t][c] = cluster.map_shared_rank(&cq[0][0], src)[t * RPC + ci];
         xk[t][c] = cluster.map_shared_rank(&ck[0][0], src)[t * RPC + ci];
+    }
+    if (tid < 2 * N) {
+        const int which = tid / N, t = tid % N;
+        float v = 0.f;
+        for (int q = 0; q < kSsmSplit; q++) v += cluster.map_shared_rank(&ab_part[0][0], q)[which * kMaxN + t];
+        ab[which][t] = v;
     }
     __syncthreads();
     // 5. L2 norms of q, k per new token (warp t), gates in f64
@@ -517,8 +527,249 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     cluster.sync();  // peers may still read this CTA's shared memory
 }
 
+// Batched variant: one cluster of kAttnSplit CTAs per (KV head, request) covers
+// all `ratio` query heads of the group, so every cached key and value is read
+// once (not once per query head).  Rows r = hh * N + t (query head hh of the
+// group, token t).  Keys of the CTA's slice are staged in chunks of kGrpKeys
+// in shared memory (K rows padded by four floats: 16-byte loads without bank
+// conflicts); thread (key jj, row group w) scores rows w, w + 8, ..., one warp
+// per row updates the online softmax, and thread d accumulates P.V for dims d
+// (+ 256) of every row.
+constexpr int kGrpKeys = 32;
+constexpr int kGrpRows = 32;  // ratio * N
+
+template <int HD>
+struct GrpSmem {
+    static constexpr int KS = HD + 4;  // 16-byte rows; key jj starts 4 jj banks further
+    // floats: q[R][HD] | kn[N][HD] | vn[N][HD] | Ks[kGrpKeys][KS] | Vs[kGrpKeys][HD] | sc[R][kGrpKeys] | ms, ls, fs [R]
+    static __host__ __device__ int bytes(int R, int N) {
+        return 4 * (R * HD + 2 * N * HD + kGrpKeys * KS + kGrpKeys * HD + R * kGrpKeys + 3 * R);
+    }
+};
+
+template <int HD>
+__global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    constexpr int KS = GrpSmem<HD>::KS;
+    constexpr int DS = HD / kAttnSplit;
+    constexpr int RPT = (kGrpRows * HD + 255) / 256;  // P.V outputs per thread (upper bound)
+    extern __shared__ __align__(16) float gs[];
+    const int rank = (int)cluster.block_rank();
+    const int g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int N = a.N, ratio = a.nh / a.nkv, R = ratio * N;
+    float *q = gs, *kn = q + R * HD, *vn = kn + N * HD, *Ks = vn + N * HD, *Vs = Ks + kGrpKeys * KS;
+    float *sc = Vs + kGrpKeys * HD, *ms = sc + R * kGrpKeys, *ls = ms + R, *fs = ls + R;
+    float *po = Ks;  // after the key loop: this slice's P.V [R][HD] (fits: R * HD <= Ks + Vs)
+    pdl_trigger();
+    pdl_wait();
+    {  // request blockIdx.z
+        const int64_t b = blockIdx.z;
+        a.qkv += b * a.N * a.ldq;
+        a.out += b * a.N * a.ldo;
+        a.kc += b * a.b_kv;
+        a.vc += b * a.b_kv;
+        a.pos += b * a.b_pos;
+    }
+    const int p0 = *a.pos;
+    const int nkeys = p0 + N;
+    const int per = (nkeys + kAttnSplit - 1) / kAttnSplit;
+    const int lo = min(nkeys, rank * per), hi = min(nkeys, lo + per);
+    const int half = a.rotary_dim / 2;
+
+    // 1. the group's q rows, the new k and v; RMSNorm + RoPE (warp per row)
+    for (int i = tid; i < R * HD; i += 256) {
+        const int r = i / HD, d = i % HD, hh = r / N, t = r % N;
+        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(g * ratio + hh) * 2 * HD + d];
+    }
+    for (int i = tid; i < N * HD; i += 256) {
+        const int t = i / HD, d = i % HD;
+        const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * 2 * HD;
+        kn[i] = row[g * HD + d];
+        vn[i] = row[a.nkv * HD + g * HD + d];
+    }
+    if (tid < R) {
+        ms[tid] = -CUDART_INF_F;
+        ls[tid] = 0.f;
+    }
+    __syncthreads();
+    for (int rr = warp; rr < R + N; rr += 8) {
+        const bool isq = rr < R;
+        float *x = isq ? q + rr * HD : kn + (rr - R) * HD;
+        const float *w = isq ? a.q_norm : a.k_norm;
+        const int t = isq ? rr % N : rr - R;
+        float ss = 0.f;
+        for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
+        ss = warp_sum(ss);
+        const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+        for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv * w[d];
+        __syncwarp();
+        const float *cs = a.rope_cos + (int64_t)(p0 + t) * half, *sn = a.rope_sin + (int64_t)(p0 + t) * half;
+        for (int i = lane; i < half; i += 32) {
+            const float c = cs[i], s_ = sn[i];
+            const float x1 = x[i], x2 = x[i + half];
+            x[i] = x1 * c - x2 * s_;
+            x[i + half] = x1 * s_ + x2 * c;
+        }
+    }
+    __syncthreads();
+    if (rank == 0) {
+        for (int i = tid; i < N * HD; i += 256) {
+            const int t = i / HD, d = i % HD;
+            const int64_t o = ((int64_t)(p0 + t) * a.nkv + g) * HD + d;
+            a.kc[o] = kn[i];
+            a.vc[o] = vn[i];
+        }
+    }
+
+    // 2. keys lo..hi in chunks: scores, online softmax, P.V
+    const float scale = 1.0f / sqrtf((float)HD);
+    float o[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; k++) o[k] = 0.f;
+    for (int j0 = lo; j0 < hi; j0 += kGrpKeys) {
+        const int nj = min(kGrpKeys, hi - j0);
+        {
+            // the chunk's K and V rows, 16 bytes per load, every load of a thread in flight at once
+            constexpr int NL = kGrpKeys * HD / 4 / 256;
+            float4 kv[NL], vv[NL];
+#pragma unroll
+            for (int l = 0; l < NL; l++) {
+                const int i = tid + 256 * l, jj = i / (HD / 4), d = 4 * (i % (HD / 4)), j = j0 + jj;
+                kv[l] = vv[l] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (jj < nj && j < p0) {
+                    const int64_t o = ((int64_t)j * a.nkv + g) * HD + d;
+                    kv[l] = *reinterpret_cast<const float4 *>(a.kc + o);
+                    vv[l] = *reinterpret_cast<const float4 *>(a.vc + o);
+                } else if (jj < nj) {
+                    kv[l] = *reinterpret_cast<const float4 *>(kn + (j - p0) * HD + d);
+                    vv[l] = *reinterpret_cast<const float4 *>(vn + (j - p0) * HD + d);
+                }
+            }
+#pragma unroll
+            for (int l = 0; l < NL; l++) {
+                const int i = tid + 256 * l, jj = i / (HD / 4), d = 4 * (i % (HD / 4));
+                *reinterpret_cast<float4 *>(Ks + jj * KS + d) = kv[l];
+                *reinterpret_cast<float4 *>(Vs + jj * HD + d) = vv[l];
+            }
+        }
+        __syncthreads();
+        {
+            // thread (jj = lane, row group = warp): K row jj read once, q rows broadcast
+            const int jj = lane, j = j0 + jj;
+            constexpr int RG = kGrpRows / 8;
+            float acc[RG];
+#pragma unroll
+            for (int k = 0; k < RG; k++) acc[k] = 0.f;
+            const float4 *kr = reinterpret_cast<const float4 *>(Ks + jj * KS);
+#pragma unroll 4
+            for (int d4 = 0; d4 < HD / 4; d4++) {
+                const float4 kv = kr[d4];
+#pragma unroll
+                for (int k = 0; k < RG; k++) {
+                    const int r = warp + 8 * k;
+                    if (r < R) {
+                        const float4 qv = reinterpret_cast<const float4 *>(q + r * HD)[d4];
+                        acc[k] += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < RG; k++) {
+                const int r = warp + 8 * k;
+                if (r < R) sc[r * kGrpKeys + jj] = (jj < nj && j <= p0 + r % N) ? acc[k] * scale : -CUDART_INF_F;
+            }
+        }
+        __syncthreads();
+        for (int r = warp; r < R; r += 8) {
+            const float sv = lane < kGrpKeys ? sc[r * kGrpKeys + lane] : -CUDART_INF_F;
+            const float mo = ms[r], mn = fmaxf(mo, warp_max(sv));
+            float f = 1.f, e = 0.f;
+            if (mn != -CUDART_INF_F) {
+                f = expf(mo - mn);
+                e = expf(sv - mn);
+            }
+            if (lane < kGrpKeys) sc[r * kGrpKeys + lane] = e;
+            const float ps = warp_sum(e);
+            if (lane == 0) {
+                ls[r] = ls[r] * f + ps;
+                ms[r] = mn;
+                fs[r] = f;
+            }
+        }
+        __syncthreads();
+        // thread: dim d = (tid + 256 k) % HD of row (tid + 256 k) / HD; V loaded once per key
+#pragma unroll
+        for (int k = 0; k < RPT; k++) {
+            const int i = tid + 256 * k;
+            if (i < R * HD) o[k] *= fs[i / HD];
+        }
+        // four keys per step: the rows' probabilities as one 16-byte load each (the
+        // chunk's tail keys have probability 0 and zeroed V rows)
+        for (int jj = 0; jj < nj; jj += 4) {
+            const int d = tid % HD;
+            const float v0 = Vs[jj * HD + d], v1 = Vs[(jj + 1) * HD + d];
+            const float v2 = Vs[(jj + 2) * HD + d], v3 = Vs[(jj + 3) * HD + d];
+#pragma unroll
+            for (int k = 0; k < RPT; k++) {
+                const int i = tid + 256 * k;
+                if (i < R * HD) {
+                    const float4 p = *reinterpret_cast<const float4 *>(sc + (i / HD) * kGrpKeys + jj);
+                    o[k] += p.x * v0 + p.y * v1 + p.z * v2 + p.w * v3;
+                }
+            }
+        }
+        __syncthreads();  // Ks, Vs, sc and fs are rewritten by the next chunk
+    }
+#pragma unroll
+    for (int k = 0; k < RPT; k++) {
+        const int i = tid + 256 * k;
+        if (i < R * HD) po[i] = o[k];
+    }
+
+    // 3. combine the slices (distributed shared memory); this CTA: dims rank*DS ..
+    cluster.sync();
+    for (int i = tid; i < R * DS; i += 256) {
+        const int r = i / DS, dd = rank * DS + i % DS, hh = r / N, t = r % N;
+        float M = -CUDART_INF_F;
+        for (int k = 0; k < kAttnSplit; k++) M = fmaxf(M, cluster.map_shared_rank(ms, k)[r]);
+        float L = 0.f, O = 0.f;
+        for (int k = 0; k < kAttnSplit; k++) {
+            const float mr = cluster.map_shared_rank(ms, k)[r];
+            if (mr == -CUDART_INF_F) continue;
+            const float w = expf(mr - M);
+            L += cluster.map_shared_rank(ls, k)[r] * w;
+            O += cluster.map_shared_rank(po, k)[r * HD + dd] * w;
+        }
+        const int h = g * ratio + hh;
+        const float gv = a.qkv[(int64_t)t * a.ldq + (int64_t)h * 2 * HD + HD + dd];
+        a.out[(int64_t)t * a.ldo + (int64_t)h * HD + dd] = O / L * (1.0f / (1.0f + expf(-gv)));
+    }
+    cluster.sync();  // peers may still read this CTA's shared memory
+}
+
+template <int HD>
+static cudaError_t launch_group(const AttnArgs &a, int batch, cudaStream_t s) {
+    const int R = a.nh / a.nkv * a.N;
+    const int smem = GrpSmem<HD>::bytes(R, a.N);
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(attn_group_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             GrpSmem<HD>::bytes(kGrpRows, kMaxN));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    return launch_k(attn_group_kernel<HD>, dim3(kAttnSplit, a.nkv, batch), dim3(256), (size_t)smem, s, a);
+}
+
 cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.nh % a.nkv || batch < 1) return cudaErrorInvalidValue;
+    // many requests: group the query heads of each KV head (KV read once)
+    if (batch > 1 && (a.nh / a.nkv) * a.N <= kGrpRows) {
+        if (a.hd == 256) return launch_group<256>(a, batch, s);
+        if (a.hd == 128) return launch_group<128>(a, batch, s);
+        if (a.hd == 64) return launch_group<64>(a, batch, s);
+    }
     const dim3 grid(kAttnSplit, a.nh, batch);
     if (a.hd == 256) return launch_k(attn_step_kernel<256>, grid, dim3(256), 0, s, a);
     if (a.hd == 128) return launch_k(attn_step_kernel<128>, grid, dim3(256), 0, s, a);
