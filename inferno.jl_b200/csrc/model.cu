@@ -325,8 +325,217 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     cluster.sync();  // peers may still read this CTA's shared memory
 }
 
+// Batched variant: one CTA of 4 HD threads per (head, request), no cluster.
+// Same arithmetic as ssm_step_kernel: thread (row = tid / 4, lc = tid % 4) owns
+// columns lc + 4 e of state row `row`; thread c < 3 HD owns conv channel c of
+// the head (q, k, v); the alpha/beta projections are summed block-wide.
+template <int HD>
+__global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
+    constexpr int NT = 4 * HD;
+    constexpr int CPT = HD / 4;        // state columns per thread
+    constexpr int REC = 2 * HD + 2;
+    constexpr int NW = NT / 32;
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int N = a.N, K = a.K, C = a.C, qk = a.H * HD;
+    __shared__ __align__(16) float xq[kMaxN][HD];
+    __shared__ __align__(16) float xk[kMaxN][HD];
+    __shared__ __align__(16) float cv[kMaxN][HD];
+    __shared__ __align__(16) float rk[kMaxN][HD];
+    __shared__ float rv[kMaxN][HD];
+    __shared__ float ys[kMaxN][HD];
+    __shared__ float rdec[kMaxN], rbeta[kMaxN], ndec[kMaxN], nbeta[kMaxN];
+    __shared__ float ab[2][kMaxN], ssq[kMaxN];
+    __shared__ float red_n[NW][2 * kMaxN];
+    pdl_trigger();
+    pdl_wait();
+    {  // request blockIdx.y
+        const int64_t b = blockIdx.y;
+        a.proj += b * a.N * a.ldp;
+        a.xn += b * a.N * a.d;
+        a.y += b * a.N * a.ldy;
+        a.S += b * a.b_S;
+        a.hist += b * a.b_hist;
+        a.rq += b * a.b_rq;
+        a.rkv += b * a.b_rkv;
+        a.a_prev += b * a.b_prev;
+    }
+    const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
+    // 1. conv of the head's channels (ssm_step_kernel step 1)
+    auto win = [&](int i, int ch) -> const float * {
+        if (i < K - 1) return a.hist + (int64_t)i * C + ch;
+        if (i < K - 1 + r) return a.rq + (int64_t)(i - K + 1) * C + ch;
+        return a.proj + (int64_t)(i - K + 1 - r) * a.ldp + ch;
+    };
+    if (tid < 3 * HD) {
+        const int part = tid / HD, i = tid % HD;
+        const int ch = part * qk + h * HD + i;
+        float w[4], tap[kMaxN][4], nh[3], pv[kMaxN];
+#pragma unroll
+        for (int k = 0; k < 4; k++) w[k] = k < K ? a.conv_w[(int64_t)ch * K + k] : 0.f;
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) {
+            pv[t] = t < N ? a.proj[(int64_t)t * a.ldp + ch] : 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) tap[t][k] = (t < N && k < K) ? *win(r + t + k, ch) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 3; j++) nh[j] = j < K - 1 ? *win(r + j, ch) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            if (j < K - 1) a.hist[(int64_t)j * C + ch] = nh[j];
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) {
+            if (t < N) {
+                a.rq[(int64_t)t * C + ch] = pv[t];
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    if (k < K) acc += tap[t][k] * w[k];
+                const float o = acc / (1.0f + expf(-acc));
+                if (part == 0) xq[t][i] = o;
+                else if (part == 1) xk[t][i] = o;
+                else cv[t][i] = o;
+            }
+        }
+    }
+    // 2. alpha / beta projections of the new tokens, block-wide
+    {
+        float pa[kMaxN], pb[kMaxN];
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = 0.f;
+        const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
+        for (int i = tid; i < a.d; i += NT) {
+            const float al = wa[i], be = wb[i];
+#pragma unroll
+            for (int t = 0; t < kMaxN; t++)
+                if (t < N) {
+                    const float xn = a.xn[(int64_t)t * a.d + i];
+                    pa[t] += al * xn;
+                    pb[t] += be * xn;
+                }
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxN; t++) {
+            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]);
+            if (lane == 0) {
+                red_n[warp][t] = va;
+                red_n[warp][kMaxN + t] = vb;
+            }
+        }
+    }
+    // 3. the previous call's replay record
+    float *rec = a.rkv + (int64_t)h * kMaxN * REC;
+    for (int i = tid; i < r * HD; i += NT) {
+        rk[i / HD][i % HD] = rec[(i / HD) * REC + i % HD];
+        rv[i / HD][i % HD] = rec[(i / HD) * REC + HD + i % HD];
+    }
+    if (tid < r) {
+        rdec[tid] = rec[tid * REC + 2 * HD];
+        rbeta[tid] = rec[tid * REC + 2 * HD + 1];
+    }
+    __syncthreads();
+    if (tid < 2 * N) {
+        const int which = tid / N, t = tid % N;
+        float v = 0.f;
+        for (int w8 = 0; w8 < NW; w8++) v += red_n[w8][which * kMaxN + t];
+        ab[which][t] = v;
+    }
+    __syncthreads();
+    // 4. L2 norms of q, k (warp t), gates in f64
+    if (warp < N) {
+        const int t = warp;
+        float qs = 0.f, ks = 0.f;
+        for (int i = lane; i < HD; i += 32) {
+            qs += xq[t][i] * xq[t][i];
+            ks += xk[t][i] * xk[t][i];
+        }
+        qs = warp_sum(qs);
+        ks = warp_sum(ks);
+        const float scale = 1.0f / sqrtf((float)HD);
+        const float qn = 1.0f / (sqrtf(qs) + 1e-6f) * scale, kn = 1.0f / (sqrtf(ks) + 1e-6f);
+        __syncwarp();
+        for (int i = lane; i < HD; i += 32) {
+            xq[t][i] *= qn;
+            xk[t][i] *= kn;
+        }
+        if (lane == 0) {
+            double av = (double)ab[0][t] + (double)a.dt_bias[h];
+            av = av < -20.0 ? -20.0 : (av > 20.0 ? 20.0 : av);
+            const double sp = log(1.0 + exp(av));
+            const float dec = (float)((double)a.ssm_a[h] * sp);
+            ndec[t] = expf(dec);
+            double bv = (double)ab[1][t];
+            bv = bv < -20.0 ? -20.0 : (bv > 20.0 ? 20.0 : bv);
+            nbeta[t] = (float)(1.0 / (1.0 + exp(-bv)));
+        }
+    }
+    __syncthreads();
+    // 5. this call's replay record (the old one was read in step 3)
+    for (int i = tid; i < N * HD; i += NT) {
+        rec[(i / HD) * REC + i % HD] = xk[i / HD][i % HD];
+        rec[(i / HD) * REC + HD + i % HD] = cv[i / HD][i % HD];
+    }
+    if (tid < N) {
+        rec[tid * REC + 2 * HD] = ndec[tid];
+        rec[tid * REC + 2 * HD + 1] = nbeta[tid];
+    }
+    // 6. the state rows: row tid / 4, columns lc + 4 e
+    const int row = tid >> 2, lc = tid & 3;
+    float *Sp = a.S + ((int64_t)h * HD + row) * HD + lc;
+    float sv[CPT];
+#pragma unroll
+    for (int e = 0; e < CPT; e++) sv[e] = Sp[4 * e];
+    auto update = [&](const float *kv, float dec, float beta, float vrow) {
+        float sk = 0.f;
+#pragma unroll
+        for (int e = 0; e < CPT; e++) {
+            sv[e] *= dec;
+            sk += sv[e] * kv[lc + 4 * e];
+        }
+        sk += __shfl_xor_sync(0xffffffffu, sk, 1);
+        sk += __shfl_xor_sync(0xffffffffu, sk, 2);
+        const float dd = beta * (vrow - sk);
+#pragma unroll
+        for (int e = 0; e < CPT; e++) sv[e] += dd * kv[lc + 4 * e];
+    };
+    for (int j = 0; j < r; j++) update(rk[j], rdec[j], rbeta[j], rv[j][row]);
+#pragma unroll
+    for (int e = 0; e < CPT; e++) Sp[4 * e] = sv[e];
+    for (int t = 0; t < N; t++) {
+        update(xk[t], ndec[t], nbeta[t], cv[t][row]);
+        float yv = 0.f;
+#pragma unroll
+        for (int e = 0; e < CPT; e++) yv += sv[e] * xq[t][lc + 4 * e];
+        yv += __shfl_xor_sync(0xffffffffu, yv, 1);
+        yv += __shfl_xor_sync(0xffffffffu, yv, 2);
+        if (lc == 0) ys[t][row] = yv;
+    }
+    __syncthreads();
+    // 7. per-head RMSNorm and the silu(z) gate
+    if (warp < N) {
+        float v = 0.f;
+        for (int i = lane; i < HD; i += 32) v += ys[warp][i] * ys[warp][i];
+        v = warp_sum(v);
+        if (lane == 0) ssq[warp] = v;
+    }
+    __syncthreads();
+    for (int i = tid; i < N * HD; i += NT) {
+        const int t = i / HD, c = i % HD;
+        const float scale = 1.0f / sqrtf(ssq[t] / (float)HD + a.eps);
+        const float z = a.proj[(int64_t)t * a.ldp + C + h * HD + c];
+        const float yn = ys[t][c] * scale * a.norm_w[c];
+        a.y[(int64_t)t * a.ldy + h * HD + c] = yn * z * (1.0f / (1.0f + expf(-z)));
+    }
+}
+
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4 || batch < 1) return cudaErrorInvalidValue;
+    if (batch > 1) {
+        const dim3 grid(a.H, batch);
+        if (head_dim == 128) return launch_k(ssm_batch_kernel<128>, grid, dim3(512), 0, s, a);
+        if (head_dim == 64) return launch_k(ssm_batch_kernel<64>, grid, dim3(256), 0, s, a);
+        return cudaErrorInvalidValue;
+    }
     const dim3 grid(kSsmSplit, a.H, batch);
     if (head_dim == 128) return launch_k(ssm_step_kernel<128>, grid, dim3(256), 0, s, a);
     if (head_dim == 64) return launch_k(ssm_step_kernel<64>, grid, dim3(256), 0, s, a);
