@@ -26,7 +26,13 @@ collective); value sums the ranks' units over the max-over-ranks time.
 Profiling cases (no JSON line; the launches of interest are bracketed by
 cudaProfilerStart/Stop for `ncu --profile-from-start off`):
     python bench.py --profile spec        # 2 graph-replayed spec steps, config 1
-    python bench.py --profile qgemv --qtype Q4_K --shape 65536x4096 --ncols 5
+    python bench.py --profile qgemv --qtype Q4_K --shape 65536x4096 --ncols 5 [--act 1]
+    python bench.py --profile dense --qtype Q4_K --shape 4096x4096 --ncols 320
+    python bench.py --profile batch       # 1 graph-replayed step of the batch workload
+
+Workload "batch": the ~9B-shape hybrid, 64 requests with
+2048-token seeded prompts (split over the ranks), one step = MTP drafts +
+one verify of 64 x 5 columns + acceptance, as a CUDA graph.
 """
 import argparse
 import json
@@ -46,6 +52,11 @@ SHAPES = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
 FORMATS = [(12, "Q4_K"), (13, "Q5_K"), (14, "Q6_K"), (8, "Q8_0")]
 NCOLS = 5
 BPW = {12: 144 / 256, 13: 176 / 256, 14: 210 / 256, 8: 34 / 32}
+# arithmetic of the K-quant GEMVs per activation mode (--act); Q8_0 is always exact
+ACT_DTYPE = {
+    0: "q4_k/q6_k weights x f32 activations, exact products (fp16 hi+lo split on the tensor cores), f32 accumulate",
+    1: "q4_k/q6_k weights x Q8_K activations (the reference's quantize_row_q8_K), exact int32 sub-block sums on the integer tensor cores, f32 scaling",
+}
 
 
 def measured_peaks():
@@ -151,6 +162,7 @@ def run_sweep(args):
     pkg = ge.load_package()
     pkg.load()
     ctx = pkg.Context(local)
+    ctx.set_activation(args.act)
     rng = np.random.default_rng(1234)
     Ws, Xs, Ys, byts = [], [], [], []
     for qt, name in FORMATS:
@@ -237,9 +249,9 @@ def run_sweep(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "q4_k/q5_k/q6_k/q8_0 weights, f32 activations (fp16 hi+lo split), f32 accumulate",
+            "dtype": ACT_DTYPE[args.act].replace("q4_k/q6_k", "q4_k/q5_k/q6_k/q8_0"),
             "data": "synthetic: seeded N(0,0.02) weights encoded by the repo's own K-quant encoder, N(0,1) activations",
-            "config": {"workload": "verify GEMV sweep (BASELINE config 2)", "ncols": NCOLS,
+            "config": {"workload": "verify GEMV sweep (BASELINE config 2)", "ncols": NCOLS, "activations": ["exact f32", "Q8_K"][args.act],
                        "shapes": [f"{m}x{k}" for m, k in SHAPES], "formats": [n for _, n in FORMATS],
                        "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2: %.2f GB of weights per step" % (step_bytes / 1e9),
@@ -464,11 +476,12 @@ def run_spec(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "q4_k/q6_k weights, f32 activations (fp16 hi+lo split on tensor cores), f32 accumulate",
+            "dtype": ACT_DTYPE[args.act],
             "data": "synthetic: seeded random-init Qwen3.5-shape hybrid GGUF (N(0,0.02) weights, the library's encoder), seeded uniform 128-token prompt",
             "config": {"workload": "greedy spec-decode, BASELINE config 1 (tiny Qwen3.5-shape hybrid)",
                        "model": "hidden 1024, 24 layers (18 GatedDeltaNet + 6 attention), 8q/2kv x 256, FFN 3584, vocab 151936, 1-layer MTP head",
                        "gamma": G, "verify_columns": G + 1, "prompt": SPEC_PROMPT, "batch": 1,
+                       "activations": ["exact f32", "Q8_K"][args.act],
                        "tokens_emitted_timed": emitted, "accept_rate": round((emitted / args.steps - 1) / G, 4),
                        "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2: %.0f MB of weights read per step" % (step_bytes / 1e6),
@@ -720,6 +733,26 @@ def run_profile(args):
         torch.cuda.profiler.stop()
         print(json.dumps({"profile": "spec", "launches_per_step": _launches(st)}))
         return
+    if args.profile == "batch":
+        from inferno_b200 import synth
+        from inferno_b200.engine import Model, State
+        ctx = pkg.Context(0, torch_stream=False)
+        model = Model(ctx, synth.cached(BATCH_PRESET, BATCH_SEED))
+        B, P = args.batch, args.prompt
+        prompts = np.stack([synth.prompt(model.info.vocab, P, BATCH_SEED + 1000 + b) for b in range(B)])
+        st = State(model, P + 64, batch=B)
+        st.prefill(prompts)
+        st.spec_step(args.gamma)
+        st.capture(args.gamma, 1)
+        for _ in range(2):
+            st.launch()
+        ctx.sync()
+        torch.cuda.profiler.start()
+        st.launch()
+        ctx.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profile": "batch", "requests": B, "prompt": P}))
+        return
     qt = {"Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q8_0": 8}[args.qtype]
     M, K = (int(v) for v in args.shape.split("x"))
     rng = np.random.default_rng(7)
@@ -727,6 +760,7 @@ def run_profile(args):
     t = ctx.upload(qt, make_weights(pkg, qt, M, K, rng), M, K)
     X = torch.from_numpy(rng.normal(0, 1, (args.ncols, K)).astype(np.float32)).cuda()
     Y = torch.empty(args.ncols, M, device="cuda")
+    ctx.set_activation(args.act)
     run = ctx.qgemm_dense if args.profile == "dense" else ctx.qgemm
     for _ in range(3):
         run(t, X, Y)
@@ -753,7 +787,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--act", type=int, default=0, choices=[0, 1],
                     help="K-quant GEMV activations: 0 = exact f32 (default), 1 = Q8_K (the reference's kernels)")
-    ap.add_argument("--profile", choices=["spec", "qgemv", "dense"], help="small case for ncu (no JSON line)")
+    ap.add_argument("--profile", choices=["spec", "qgemv", "dense", "batch"], help="small case for ncu (no JSON line)")
     ap.add_argument("--qtype", default="Q4_K")
     ap.add_argument("--shape", default="65536x4096")
     ap.add_argument("--ncols", type=int, default=5)
