@@ -186,6 +186,30 @@ typedef struct {
 
 /* load all weights to the context's device (synchronous) */
 int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out);
+
+/* --- tensor parallelism (config 5): one process or thread per GPU ---------
+ * A communicator (NCCL over NVLink, bound at run time) for `world` ranks;
+ * rank 0 creates the unique id and the host hands it to every rank.  The
+ * reference has no multi-GPU path; this replaces its single-process
+ * forward_cpu! for models too large or too slow for one GPU. */
+#define IFR_COMM_ID_BYTES 128
+typedef struct ifr_comm ifr_comm;
+int ifr_comm_available(void);                 /* 1 if libnccl.so.2 could be bound */
+int ifr_comm_unique_id(uint8_t *id_out);      /* IFR_COMM_ID_BYTES bytes */
+int ifr_comm_create(ifr_ctx *ctx, int rank, int world, const uint8_t *id, ifr_comm **out);
+int ifr_comm_destroy(ifr_comm *comm);
+/* load this rank's shard of an attention-only model: query/key/value heads,
+ * gate/up rows (256-column units) and lm_head vocabulary rows split across the
+ * ranks (column parallel), attention-output and down projections split along
+ * their inner dimension (row parallel, one sum all-reduce of the residual
+ * after each); norms and the embedding are replicated.  Greedy acceptance
+ * takes the argmax over all ranks' vocabulary shards.  comm == NULL is
+ * ifr_model_load_gguf.  The communicator must outlive the model. */
+int ifr_model_load_gguf_tp(ifr_ctx *ctx, const char *path, ifr_comm *comm, ifr_model **out);
+/* this rank's share: shard[8] = {rank, world, query heads, KV heads, FFN
+ * columns, FFN offset, lm_head vocabulary rows, vocabulary offset}.  The
+ * logits of ifr_state_last_verify are the rank's vocabulary rows. */
+int ifr_model_get_shard(const ifr_model *m, int32_t *shard);
 int ifr_model_free(ifr_model *m);
 int ifr_model_get_info(const ifr_model *m, ifr_model_info *info);
 

@@ -47,6 +47,12 @@ SIGNATURES = {
     "ifr_accept_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
     "ifr_accept_greedy": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "ifr_model_load_gguf": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "ifr_model_load_gguf_tp": (_i, [_vp, ctypes.c_char_p, _vp, ctypes.POINTER(_vp)]),
+    "ifr_comm_available": (_i, []),
+    "ifr_model_get_shard": (_i, [_vp, _vp]),
+    "ifr_comm_unique_id": (_i, [_vp]),
+    "ifr_comm_create": (_i, [_vp, _i, _i, _vp, ctypes.POINTER(_vp)]),
+    "ifr_comm_destroy": (_i, [_vp]),
     "ifr_model_free": (_i, [_vp]),
     "ifr_model_get_info": (_i, [_vp, _vp]),
     "ifr_state_create": (_i, [_vp, _i, ctypes.POINTER(_vp)]),

@@ -13,12 +13,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libinferno_b200.so")
-SOURCES = ["api.cu", "quant.cu", "qgemv.cu", "qmma.cu", "accept.cu", "model.cu", "engine.cu", "encode.cpp"]
+SOURCES = ["api.cu", "quant.cu", "qgemv.cu", "qmma.cu", "accept.cu", "model.cu", "engine.cu", "comm.cpp", "encode.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
-    "--shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+    "--shared", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-ldl",
     "-Xptxas", "-warn-spills",
     "-I", os.path.join(ROOT, "include"),
 ]

@@ -631,3 +631,84 @@ extern "C" int ifr_accept_noalloc(ifr_ctx *c, const float *target, const float *
     if (e != cudaSuccess) return ifr_cuda_fail(e, "accept_noalloc launch");
     return IFR_OK;
 }
+
+// ---- greedy acceptance over a vocabulary split across tensor-parallel ranks ----
+namespace ifr {
+
+// per row: (max, off + argmax) over V logits, the lowest index among equal
+// maxima (the rule of greedy_fused_kernel); cand[row] = {value, index bits}
+__global__ void __launch_bounds__(256) row_argmax_kernel(const float *__restrict__ x, int64_t V, int off,
+                                                         float2 *__restrict__ cand) {
+    __shared__ float sv[256];
+    __shared__ int si[256];
+    pdl_trigger();
+    pdl_wait();
+    const float *row = x + (int64_t)blockIdx.x * V;
+    float bv = -CUDART_INF_F;
+    int bi = INT_MAX;
+    for (int64_t j = threadIdx.x; j < V; j += 256) {
+        const float v = row[j];
+        if (v > bv || bi == INT_MAX) {
+            bv = v;
+            bi = (int)j;
+        }
+    }
+    sv[threadIdx.x] = bv;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int o = 128; o; o >>= 1) {
+        if (threadIdx.x < o) {
+            const float ov = sv[threadIdx.x + o];
+            const int oi = si[threadIdx.x + o];
+            if (oi != INT_MAX && (si[threadIdx.x] == INT_MAX || ov > sv[threadIdx.x] ||
+                                  (ov == sv[threadIdx.x] && oi < si[threadIdx.x]))) {
+                sv[threadIdx.x] = ov;
+                si[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) cand[blockIdx.x] = make_float2(sv[0], __int_as_float(si[0] + off));
+}
+
+// one thread per sequence: the rows' argmax over the W ranks' candidates
+// ([W][rows], ranks in vocabulary order), then the longest matching draft
+// prefix (mtp_verify_step!, src/ModelCPU.jl:2099-2115)
+__global__ void tp_accept_kernel(const float2 *__restrict__ cand, int W, int rows, const int32_t *drafts,
+                                 int draft_ld, int B, int G, int32_t *acc, int32_t *out, int out_ld) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    int32_t *ot = out + (int64_t)b * out_ld;
+    for (int i = 0; i <= G; i++) ot[i] = -1;
+    int a = 0;
+    for (int i = 0; i <= G; i++) {
+        const int r = b * (G + 1) + i;
+        float best = cand[r].x;
+        int arg = __float_as_int(cand[r].y);
+        for (int w = 1; w < W; w++) {
+            const float2 c = cand[(int64_t)w * rows + r];
+            if (c.x > best) {
+                best = c.x;
+                arg = __float_as_int(c.y);
+            }
+        }
+        ot[i] = arg;
+        if (i == G || arg != drafts[(int64_t)b * draft_ld + i]) break;
+        a++;
+    }
+    acc[b] = a;
+}
+
+cudaError_t row_argmax(const float *x, int rows, int64_t V, int off, float *cand, cudaStream_t s) {
+    return launch_k(row_argmax_kernel, dim3(rows), dim3(256), 0, s, x, V, off, reinterpret_cast<float2 *>(cand));
+}
+
+cudaError_t tp_accept(const float *cand, int W, int rows, const int32_t *drafts, int draft_ld, int B, int G,
+                      int32_t *acc, int32_t *out, int out_ld, cudaStream_t s) {
+    return launch_k(tp_accept_kernel, dim3((B + 127) / 128), dim3(128), 0, s, reinterpret_cast<const float2 *>(cand),
+                    W, rows, drafts, draft_ld, B, G, acc, out, out_ld);
+}
+
+}  // namespace ifr

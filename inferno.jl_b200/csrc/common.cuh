@@ -70,6 +70,12 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
                           int vocab, int32_t *accept_count, int32_t *out_tokens, void *scratch,
                           cudaStream_t s);
 int64_t accept_greedy_scratch_bytes(int batch, int gamma, int vocab);
+// tensor-parallel greedy acceptance: per-row (max, off + argmax) of a vocabulary
+// shard into cand[rows][2]; then, over all ranks' candidates cand[W][rows][2],
+// the argmax per row and the longest matching draft prefix per sequence
+cudaError_t row_argmax(const float *x, int rows, int64_t V, int off, float *cand, cudaStream_t s);
+cudaError_t tp_accept(const float *cand, int W, int rows, const int32_t *drafts, int draft_ld, int B, int G,
+                      int32_t *acc, int32_t *out, int out_ld, cudaStream_t s);
 // the same in one launch; counter: one zero-initialised unsigned per sequence,
 // left at zero (not shared by launches that can overlap); draft b's tokens at
 // draft_tokens + b * draft_ld, its outputs at out_tokens + b * out_ld

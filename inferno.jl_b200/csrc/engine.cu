@@ -6,6 +6,7 @@
 // (tensor names :471-694, config keys :439-469), src/ModelCPU.jl:976-1020
 // (forward), :2099-2115 (greedy verify), src/SpeculativeDecoding.jl (loop).
 #include "../../include/inferno_b200.h"
+#include "comm.h"
 #include "common.cuh"
 #include "model.cuh"
 #include "dequant.cuh"
@@ -216,6 +217,10 @@ struct ifr_model {
     Proj embed, lm_head;
     float *final_norm = nullptr, *mtp_norm_e = nullptr, *mtp_norm_h = nullptr, *mtp_norm = nullptr;
     Proj mtp_fc;
+    // tensor parallelism: this rank's query / KV heads, FFN width and lm_head rows
+    ifr_comm *comm = nullptr;
+    int tp_rank = 0, tp_world = 1;
+    int nh = 0, nkv = 0, ffn = 0, ffn_off = 0, vocab = 0, vocab_off = 0;
     std::vector<void *> dev_allocs;
     ~ifr_model() {
         for (void *p : dev_allocs) cudaFree(p);
@@ -270,9 +275,37 @@ int upload_f32_cat(ifr_model *m, const Gguf &g, const std::vector<std::string> &
     return IFR_OK;
 }
 
+// a row range and an inner-dimension range of a quantized matrix (whole by default)
+struct Slice {
+    int64_t r0 = 0, r1 = -1, k0 = 0, k1 = -1;
+};
+
+// raw GGUF bytes of rows [r0, r1) x columns [k0, k1) (k at block boundaries)
+int slice_raw(const Gguf &g, const std::string &name, const GTensor &t, const Slice &sl, std::vector<uint8_t> &out,
+              int64_t &rows, int64_t &cols) {
+    const int64_t C = (int64_t)t.dims[0], R = (int64_t)t.dims[1];
+    const int64_t r0 = sl.r0, r1 = sl.r1 < 0 ? R : sl.r1, k0 = sl.k0, k1 = sl.k1 < 0 ? C : sl.k1;
+    const int64_t be = t.type == 8 ? 32 : 256, rb = tensor_bytes(t.type, C);
+    if (rb <= 0) return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: unsupported type %u", name.c_str(), t.type);
+    if (r0 < 0 || r1 > R || r0 >= r1 || k0 < 0 || k1 > C || k0 >= k1 || k0 % be || k1 % be)
+        return ifr_fail(IFR_ERR_ARG, "tensor %s: slice rows %lld..%lld cols %lld..%lld does not fit %lldx%lld blocks of %lld",
+                        name.c_str(), (long long)r0, (long long)r1, (long long)k0, (long long)k1, (long long)R,
+                        (long long)C, (long long)be);
+    const int64_t bb = rb / (C / be);  // bytes per block
+    const int64_t off = k0 / be * bb, len = (k1 - k0) / be * bb;
+    out.resize((size_t)((r1 - r0) * len));
+    const uint8_t *src = g.data(t);
+    for (int64_t r = r0; r < r1; r++) memcpy(out.data() + (r - r0) * len, src + r * rb + off, (size_t)len);
+    rows = r1 - r0;
+    cols = k1 - k0;
+    return IFR_OK;
+}
+
 // quantized matrices with the same inner dim, stacked along rows; parts of the
-// same type are merged into one device tensor (one GEMV launch)
-int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &names, Proj *p) {
+// same type are merged into one device tensor (one GEMV launch); `slices`
+// (optional, one per name) take a shard of each matrix
+int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &names, Proj *p,
+                const std::vector<Slice> &slices = {}) {
     p->parts.clear();
     p->rows = 0;
     p->cols = -1;
@@ -282,7 +315,8 @@ int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &nam
         if (it == g.t.end()) return ifr_fail(IFR_ERR_ARG, "tensor %s missing", names[i].c_str());
         const GTensor &t0 = it->second;
         if (t0.dims.size() != 2) return ifr_fail(IFR_ERR_ARG, "tensor %s is not a matrix", names[i].c_str());
-        const int64_t cols = (int64_t)t0.dims[0];
+        const Slice s0 = i < slices.size() ? slices[i] : Slice();
+        const int64_t cols = (s0.k1 < 0 ? (int64_t)t0.dims[0] : s0.k1) - s0.k0;
         if (p->cols >= 0 && cols != p->cols) return ifr_fail(IFR_ERR_ARG, "tensor %s: inner dim mismatch", names[i].c_str());
         p->cols = cols;
         std::vector<uint8_t> raw;
@@ -292,11 +326,15 @@ int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &nam
             auto jt = g.t.find(names[j]);
             if (jt == g.t.end()) return ifr_fail(IFR_ERR_ARG, "tensor %s missing", names[j].c_str());
             const GTensor &tj = jt->second;
-            if (tj.type != t0.type || tj.dims.size() != 2 || (int64_t)tj.dims[0] != cols) break;
-            const int64_t nb = tensor_bytes(tj.type, tj.nel());
-            if (nb < 0) return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: unsupported type %u", names[j].c_str(), tj.type);
-            raw.insert(raw.end(), g.data(tj), g.data(tj) + nb);
-            rows += (int64_t)tj.dims[1];
+            const Slice sj = j < slices.size() ? slices[j] : Slice();
+            const int64_t cj = (sj.k1 < 0 ? (int64_t)tj.dims[0] : sj.k1) - sj.k0;
+            if (tj.type != t0.type || tj.dims.size() != 2 || cj != cols) break;
+            std::vector<uint8_t> part;
+            int64_t pr = 0, pc = 0;
+            int rc = slice_raw(g, names[j], tj, sj, part, pr, pc);
+            if (rc) return rc;
+            raw.insert(raw.end(), part.begin(), part.end());
+            rows += pr;
         }
         ifr::QTensor q{};
         int rc = ifr_upload_raw(m->ctx, (int)t0.type, raw.data(), rows, cols, &q);
@@ -312,25 +350,30 @@ int upload_proj(ifr_model *m, const Gguf &g, const std::vector<std::string> &nam
 // ffn_gate and ffn_up as one tensor with their 16-row blocks interleaved, so
 // that the GEMV can form silu(gate) * up in its epilogue; falls back to the
 // plain stack when the two differ in type or shape
-int upload_gate_up(ifr_model *m, const Gguf &g, const std::string &gate, const std::string &up, Proj *p) {
+int upload_gate_up(ifr_model *m, const Gguf &g, const std::string &gate, const std::string &up, Proj *p,
+                   const Slice &sl = Slice()) {
     auto gi = g.t.find(gate), ui = g.t.find(up);
-    if (gi == g.t.end() || ui == g.t.end()) return upload_proj(m, g, {gate, up}, p);
+    if (gi == g.t.end() || ui == g.t.end()) return upload_proj(m, g, {gate, up}, p, {sl, sl});
     const GTensor &tg = gi->second, &tu = ui->second;
+    const int64_t r0 = sl.r0, r1 = sl.r1 < 0 ? (int64_t)tg.dims[1] : sl.r1;
     if (tg.type != tu.type || tg.dims.size() != 2 || tu.dims.size() != 2 || tg.dims[0] != tu.dims[0] ||
-        tg.dims[1] != tu.dims[1] || tg.dims[1] % 16)
-        return upload_proj(m, g, {gate, up}, p);
-    const int64_t cols = (int64_t)tg.dims[0], rows = (int64_t)tg.dims[1];
-    const int64_t nb = tensor_bytes(tg.type, tg.nel());
-    if (nb < 0) return ifr_fail(IFR_ERR_UNSUPPORTED, "tensor %s: unsupported type %u", gate.c_str(), tg.type);
+        tg.dims[1] != tu.dims[1] || (r1 - r0) % 16 || sl.k0 != 0 || sl.k1 >= 0)
+        return upload_proj(m, g, {gate, up}, p, {sl, sl});
+    std::vector<uint8_t> sg, su;
+    int64_t rows = 0, cols = 0;
+    int rc = slice_raw(g, gate, tg, sl, sg, rows, cols);
+    if (!rc) rc = slice_raw(g, up, tu, sl, su, rows, cols);
+    if (rc) return rc;
+    const int64_t nb = (int64_t)sg.size();
     const int64_t rb = nb / rows;
     std::vector<uint8_t> raw((size_t)nb * 2);
-    const uint8_t *pg = g.data(tg), *pu = g.data(tu);
+    const uint8_t *pg = sg.data(), *pu = su.data();
     for (int64_t b = 0; b < rows / 16; b++) {
         memcpy(raw.data() + (2 * b) * 16 * rb, pg + b * 16 * rb, (size_t)(16 * rb));
         memcpy(raw.data() + (2 * b + 1) * 16 * rb, pu + b * 16 * rb, (size_t)(16 * rb));
     }
     ifr::QTensor q{};
-    int rc = ifr_upload_raw(m->ctx, (int)tg.type, raw.data(), 2 * rows, cols, &q);
+    rc = ifr_upload_raw(m->ctx, (int)tg.type, raw.data(), 2 * rows, cols, &q);
     if (rc) return rc;
     m->dev_allocs.push_back(q.data);
     p->parts.assign(1, q);
@@ -357,15 +400,31 @@ int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L)
         if (L.proj.rows != m->conv_channels + m->inner || L.out.cols != m->inner)
             return ifr_fail(IFR_ERR_ARG, "%s: SSM projection shapes do not match the config", pre.c_str());
     } else {
-        if ((rc = upload_proj(m, g, {pre + "attn_q.weight", pre + "attn_k.weight", pre + "attn_v.weight"}, &L.proj))) return rc;
-        if ((rc = upload_proj(m, g, {pre + "attn_output.weight"}, &L.out))) return rc;
+        // this rank's heads: q rows [q; gate] per head, k / v rows per KV head, the
+        // output projection's inner range of those heads (the whole model for one rank)
+        const int64_t hd = c.head_dim, h0 = (int64_t)m->tp_rank * m->nh, kv0 = (int64_t)m->tp_rank * m->nkv;
+        Slice sq, sk, so;
+        sq.r0 = h0 * 2 * hd;
+        sq.r1 = (h0 + m->nh) * 2 * hd;
+        sk.r0 = kv0 * hd;
+        sk.r1 = (kv0 + m->nkv) * hd;
+        so.k0 = h0 * hd;
+        so.k1 = (h0 + m->nh) * hd;
+        if ((rc = upload_proj(m, g, {pre + "attn_q.weight", pre + "attn_k.weight", pre + "attn_v.weight"}, &L.proj,
+                              {sq, sk, sk})))
+            return rc;
+        if ((rc = upload_proj(m, g, {pre + "attn_output.weight"}, &L.out, {so}))) return rc;
         if ((rc = upload_f32(m, g, pre + "attn_q_norm.weight", c.head_dim, &L.q_norm))) return rc;
         if ((rc = upload_f32(m, g, pre + "attn_k_norm.weight", c.head_dim, &L.k_norm))) return rc;
-        if (L.proj.rows != (int64_t)(2 * c.n_head + 2 * c.n_kv_head) * c.head_dim)
+        if (L.proj.rows != (int64_t)(2 * m->nh + 2 * m->nkv) * c.head_dim)
             return ifr_fail(IFR_ERR_ARG, "%s: attention projection shapes do not match the config", pre.c_str());
     }
-    if ((rc = upload_gate_up(m, g, pre + "ffn_gate.weight", pre + "ffn_up.weight", &L.gate_up))) return rc;
-    if ((rc = upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down))) return rc;
+    // this rank's FFN units: gate / up rows and the down projection's inner range
+    Slice sf, sd;
+    sf.r0 = sd.k0 = m->ffn_off;
+    sf.r1 = sd.k1 = m->ffn_off + m->ffn;
+    if ((rc = upload_gate_up(m, g, pre + "ffn_gate.weight", pre + "ffn_up.weight", &L.gate_up, sf))) return rc;
+    if ((rc = upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down, {sd}))) return rc;
     return IFR_OK;
 }
 
@@ -393,6 +452,7 @@ struct ifr_state {
     int32_t *h_tok = nullptr;           // pinned staging
     float *x, *xn, *proj, *y, *gu, *hmid, *hid, *logits;
     float *mtp_h, *mtp_cat;
+    float *cand = nullptr;              // tensor parallel: per-row (max, argmax) of every rank
     unsigned *gcount = nullptr;         // fused argmax/accept: per-launch completion counter (returns to 0)
     float *rope_cos, *rope_sin;
     std::vector<float *> S, hist, rq, rkv;      // per layer (SSM) else null
@@ -547,10 +607,10 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.rope_cos = s->rope_cos;
         a.rope_sin = s->rope_sin;
         a.out = s->y;
-        a.ldo = (int64_t)c.n_head * c.head_dim;
+        a.ldo = (int64_t)m->nh * c.head_dim;
         a.N = n;
-        a.nh = c.n_head;
-        a.nkv = c.n_kv_head;
+        a.nh = m->nh;
+        a.nkv = m->nkv;
         a.hd = c.head_dim;
         a.rotary_dim = c.rotary_dim;
         a.eps = c.rms_eps;
@@ -558,21 +618,26 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.b_pos = pos_ld;
         ECHECK(ifr::attn_step(a, B, st), "attn_step");
     }
-    if ((rc = gemv(s, gcat, L.out, s->y, nc, s->x, true, st))) return rc;
+    // row-parallel projections: rank 0 adds its partial to the residual, the
+    // others write theirs, and one sum all-reduce leaves x + sum on every rank
+    if ((rc = gemv(s, gcat, L.out, s->y, nc, s->x, m->tp_rank == 0, st))) return rc;
+    if ((rc = comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st))) return rc;
     ifr::rmsnorm(s->x, L.post_norm, s->xn, nc, d, c.rms_eps, d, d, st);
     if (L.gate_up.glu) {
         // silu(gate) * up formed in the gate/up GEMV's epilogue
         ifr::XForm glu;
         glu.ep = 1;
         if ((rc = gemv(s, gcat, L.gate_up, s->xn, nc, s->hmid, false, st, glu))) return rc;
-        return gemv(s, gcat, L.down, s->hmid, nc, s->x, true, st);
+        if ((rc = gemv(s, gcat, L.down, s->hmid, nc, s->x, m->tp_rank == 0, st))) return rc;
+        return comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st);
     }
     if ((rc = gemv(s, gcat, L.gate_up, s->xn, nc, s->gu, false, st))) return rc;
     // silu(gate) * up formed while the down GEMV reads [gate | up]
     ifr::XForm swiglu;
     swiglu.kind = 2;
-    swiglu.ldx = 2 * (int64_t)c.ffn;
-    return gemv(s, gcat, L.down, s->gu, nc, s->x, true, st, swiglu);
+    swiglu.ldx = 2 * (int64_t)m->ffn;
+    if ((rc = gemv(s, gcat, L.down, s->gu, nc, s->x, m->tp_rank == 0, st, swiglu))) return rc;
+    return comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st);
 }
 
 // embedding rows of the n verify tokens of each of B requests (row b * n + t):
@@ -685,6 +750,27 @@ cudaError_t launch_mtp_prep(const ifr::QTensor &e, const int32_t *tok, int tok_l
     return cudaErrorInvalidValue;
 }
 
+// greedy acceptance of G drafts per sequence over B x (G+1) logits rows (the
+// argmax over all ranks' vocabulary shards under tensor parallelism)
+int greedy_accept(ifr_state *s, const int32_t *drafts, int draft_ld, int B, int G, int32_t *out, int out_ld,
+                  cudaStream_t st) {
+    ifr_model *m = s->m;
+    if (!m->comm) {
+        ECHECK(ifr::accept_greedy_fused(s->logits, drafts, B, G, m->vocab, s->acc, out, s->acc_scratch, s->gcount, st,
+                                        draft_ld, out_ld),
+               "greedy accept");
+        return IFR_OK;
+    }
+    const int rows = B * (G + 1), W = m->tp_world;
+    float *mine = s->cand + (size_t)2 * rows * W;  // this rank's candidates, past the gathered block
+    ECHECK(ifr::row_argmax(s->logits, rows, m->vocab, m->vocab_off, mine, st), "row argmax");
+    int rc = comm_allgather_bytes(m->comm, mine, s->cand, (size_t)rows * 8, st);
+    if (rc) return rc;
+    ECHECK(ifr::tp_accept(s->cand, W, rows, drafts, draft_ld, B, G, s->acc, out, out_ld, st), "tp accept");
+    s->launches += 2;
+    return IFR_OK;
+}
+
 // target forward of the n tokens per request in vtok (request b: vtok[b *
 // kNMax ..], positions sc[b].pos ..; device); final-normed hidden of every
 // column in s->hid; logits of every column in s->logits when `logits` is set
@@ -697,7 +783,7 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
                         s->x, st),
            "embedding");
     s->launches += 2;  // embedding, final norm
-    const int64_t kv_ld = (int64_t)s->max_ctx * c.n_kv_head * c.head_dim;
+    const int64_t kv_ld = (int64_t)s->max_ctx * m->nkv * c.head_dim;
     for (int li = 0; li < c.n_layers; li++) {
         int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, sc_ld, kv_ld, false, st);
         if (rc) return rc;
@@ -741,7 +827,7 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
     const ifr_model_info &c = m->info;
     const int d = c.hidden, B = s->B;
     const int sc_ld = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
-    const int64_t kv_ld = (int64_t)s->max_ctx * c.n_kv_head * c.head_dim;
+    const int64_t kv_ld = (int64_t)s->max_ctx * m->nkv * c.head_dim;
     ifr::XForm norm_out;  // the MTP head's final norm, applied inside the lm_head GEMV
     norm_out.kind = 1;
     norm_out.w = m->mtp_norm;
@@ -775,6 +861,10 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
 extern "C" {
 
 int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out) {
+    return ifr_model_load_gguf_tp(ctx, path, nullptr, out);
+}
+
+int ifr_model_load_gguf_tp(ifr_ctx *ctx, const char *path, ifr_comm *comm, ifr_model **out) {
     if (!ctx || !path || !out) return ifr_fail(IFR_ERR_ARG, "NULL argument");
     *out = nullptr;
     int dev = ifr_ctx_device(ctx), prev = 0;
@@ -834,10 +924,44 @@ int ifr_model_load_gguf(ifr_ctx *ctx, const char *path, ifr_model **out) {
         rc = ifr_fail(IFR_ERR_UNSUPPORTED, "SSM head dim %d (supported: 64, 128)", c.ssm_head_dim);
     if (!rc && c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
         rc = ifr_fail(IFR_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128, 256)", c.head_dim);
+    // this rank's share (the whole model for one rank)
+    m->comm = comm;
+    m->tp_rank = comm_rank(comm);
+    m->tp_world = comm_world(comm);
+    const int W = m->tp_world, r = m->tp_rank;
+    if (!rc && (c.n_head % W || c.n_kv_head % W))
+        rc = ifr_fail(IFR_ERR_ARG, "%d query / %d KV heads do not split over %d ranks", c.n_head, c.n_kv_head, W);
+    if (!rc && W > 1 && m->inner)
+        rc = ifr_fail(IFR_ERR_UNSUPPORTED, "tensor parallelism covers attention-only models (this one has SSM layers)");
+    if (!rc && W > 1 && g.has("mtp.fc.weight"))
+        rc = ifr_fail(IFR_ERR_UNSUPPORTED, "tensor parallelism with an MTP head is not supported (use a draft model)");
+    if (!rc && W > 1 && (c.n_head / W * c.head_dim) % 256)
+        rc = ifr_fail(IFR_ERR_ARG, "per-rank attention width %d is not a multiple of 256", c.n_head / W * c.head_dim);
+    if (!rc && W > 1 && c.ffn % 256) rc = ifr_fail(IFR_ERR_ARG, "FFN width %d is not a multiple of 256", c.ffn);
+    if (!rc) {
+        m->nh = c.n_head / W;
+        m->nkv = c.n_kv_head / W;
+        const int nuf = c.ffn / (W > 1 ? 256 : 1);  // FFN units (256 columns) split as evenly as possible
+        const int u0 = (int)((int64_t)r * nuf / W), u1 = (int)((int64_t)(r + 1) * nuf / W);
+        const int unit = W > 1 ? 256 : 1;
+        m->ffn_off = u0 * unit;
+        m->ffn = (u1 - u0) * unit;
+        m->vocab_off = (int)((int64_t)r * c.vocab / W);
+        m->vocab = (int)((int64_t)(r + 1) * c.vocab / W) - m->vocab_off;
+    }
     if (!rc) rc = upload_proj(m, g, {"token_embd.weight"}, &m->embed);
     if (!rc) {
-        if (g.has("output.weight")) rc = upload_proj(m, g, {"output.weight"}, &m->lm_head);
-        else m->lm_head = m->embed;  // tied (LoaderCPU.jl:411-417)
+        const std::string lm = g.has("output.weight") ? "output.weight" : "token_embd.weight";
+        if (W > 1) {
+            Slice sv;
+            sv.r0 = m->vocab_off;
+            sv.r1 = m->vocab_off + m->vocab;
+            rc = upload_proj(m, g, {lm}, &m->lm_head, {sv});
+        } else if (g.has("output.weight")) {
+            rc = upload_proj(m, g, {"output.weight"}, &m->lm_head);
+        } else {
+            m->lm_head = m->embed;  // tied (LoaderCPU.jl:411-417)
+        }
     }
     if (!rc && m->embed.parts.size() != 1) rc = ifr_fail(IFR_ERR_ARG, "bad embedding");
     if (!rc) rc = upload_f32(m, g, "output_norm.weight", c.hidden, &m->final_norm);
@@ -890,6 +1014,13 @@ int ifr_model_free(ifr_model *m) {
     return m->states == 0 ? model_destroy(m) : IFR_OK;
 }
 
+int ifr_model_get_shard(const ifr_model *m, int32_t *sh) {
+    if (!m || !sh) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    const int32_t v[8] = {m->tp_rank, m->tp_world, m->nh, m->nkv, m->ffn, m->ffn_off, m->vocab, m->vocab_off};
+    memcpy(sh, v, sizeof v);
+    return IFR_OK;
+}
+
 int ifr_model_get_info(const ifr_model *m, ifr_model_info *info) {
     if (!m || !info) return ifr_fail(IFR_ERR_ARG, "NULL argument");
     *info = m->info;
@@ -913,9 +1044,9 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     s->max_ctx = max_ctx;
     s->log_cap = max_ctx + 16;
     const int d = c.hidden, N = kNMax * batch, B = batch;
-    int64_t maxproj = (int64_t)(2 * c.n_head + 2 * c.n_kv_head) * c.head_dim;
+    int64_t maxproj = (int64_t)(2 * m->nh + 2 * m->nkv) * c.head_dim;
     if (m->conv_channels + m->inner > maxproj) maxproj = m->conv_channels + m->inner;
-    const int64_t ymax = std::max<int64_t>(m->inner, (int64_t)c.n_head * c.head_dim);
+    const int64_t ymax = std::max<int64_t>(m->inner, (int64_t)m->nh * c.head_dim);
     int rc = IFR_OK;
     auto chk = [&](int r) { if (!rc) rc = r; };
     chk(dalloc(s, &s->sc, B));
@@ -928,10 +1059,11 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     chk(dalloc(s, &s->xn, (size_t)N * d));
     chk(dalloc(s, &s->proj, (size_t)N * maxproj));
     chk(dalloc(s, &s->y, (size_t)N * ymax));
-    chk(dalloc(s, &s->gu, (size_t)N * 2 * c.ffn));
-    chk(dalloc(s, &s->hmid, (size_t)N * c.ffn));
+    chk(dalloc(s, &s->gu, (size_t)N * 2 * m->ffn));
+    chk(dalloc(s, &s->hmid, (size_t)N * m->ffn));
     chk(dalloc(s, &s->hid, (size_t)N * d));
-    chk(dalloc(s, &s->logits, (size_t)N * c.vocab));
+    chk(dalloc(s, &s->logits, (size_t)N * m->vocab));
+    chk(dalloc(s, &s->cand, (size_t)2 * N * (m->tp_world + 1)));
     chk(dalloc(s, &s->mtp_h, (size_t)B * d));
     chk(dalloc(s, &s->mtp_cat, (size_t)B * 2 * d));
     chk(dalloc(s, &s->gcount, B + 4));
@@ -944,7 +1076,7 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     s->rkv.assign(c.n_layers, nullptr);
     s->kc.assign(c.n_layers, nullptr);
     s->vc.assign(c.n_layers, nullptr);
-    const size_t kvn = (size_t)B * max_ctx * c.n_kv_head * c.head_dim;
+    const size_t kvn = (size_t)B * max_ctx * m->nkv * c.head_dim;
     for (int i = 0; !rc && i < c.n_layers; i++) {
         if (m->layers[i].ssm) {
             const int hd = c.ssm_head_dim;
@@ -961,7 +1093,7 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
         chk(dalloc(s, &s->mtp_kc, kvn));
         chk(dalloc(s, &s->mtp_vc, kvn));
     }
-    const int64_t accb = ifr::accept_greedy_scratch_bytes(B, kNMax, c.vocab);
+    const int64_t accb = ifr::accept_greedy_scratch_bytes(B, kNMax, m->vocab);
     if (!rc) {
         void *p = nullptr;
         cudaError_t e = cudaMalloc(&p, accb);
@@ -1090,9 +1222,8 @@ int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first
         rc = target_forward(s, k, last, false, st);
         if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, B, st);
         if (!rc && last) {
-            e = ifr::accept_greedy_fused(s->logits, nullptr, B, 0, c.vocab, s->acc, s->outtok, s->acc_scratch,
-                                         s->gcount, st);
-            if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "argmax"); break; }
+            rc = greedy_accept(s, nullptr, 0, B, 0, s->outtok, 1, st);
+            if (rc) break;
             e = ifr::launch_k(prefill_finish_kernel, dim3(B), dim3(256), 0, st, s->sc, (const int32_t *)s->outtok,
                               (const float *)s->hid, s->mtp_h, (int)c.hidden, s->log, (int)s->log_cap);
             if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prefill finish"); break; }
@@ -1121,9 +1252,7 @@ int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st) {
     if (gamma > 0 && mtp) rc = mtp_draft(s, gamma, st);
     if (!rc) rc = target_forward(s, gamma + 1, true, true, st);
     if (!rc) {
-        cudaError_t e = ifr::accept_greedy_fused(s->logits, s->vtok + 1, B, gamma, c.vocab, s->acc, s->outtok,
-                                                 s->acc_scratch, s->gcount, st, kNMax, gamma + 1);
-        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "accept_greedy");
+        rc = greedy_accept(s, s->vtok + 1, kNMax, B, gamma, s->outtok, gamma + 1, st);
     }
     if (!rc)
         ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, B, st);
@@ -1251,7 +1380,7 @@ int ifr_gemv_pass(ifr_state *s, int ncols) {
     norm.eps = c.rms_eps;
     ifr::XForm swiglu;
     swiglu.kind = 2;
-    swiglu.ldx = 2 * (int64_t)c.ffn;
+    swiglu.ldx = 2 * (int64_t)s->m->ffn;
     // the verify's GEMVs with their fused input transforms; outputs go to
     // buffers a spec step rewrites before it reads them (proj, gu, hid): the
     // caches, SSM states and residual stream are not changed
@@ -1307,7 +1436,7 @@ int ifr_state_last_verify(ifr_state *s, float *logits, float *hidden, int32_t *t
     const int n = s->last_n, B = s->B;
     if (n_cols) *n_cols = n;
     if (logits)
-        ECHECK(cudaMemcpy(logits, s->logits, sizeof(float) * B * n * c.vocab, cudaMemcpyDeviceToHost), "D2H logits");
+        ECHECK(cudaMemcpy(logits, s->logits, sizeof(float) * B * n * s->m->vocab, cudaMemcpyDeviceToHost), "D2H logits");
     if (hidden)
         ECHECK(cudaMemcpy(hidden, s->hid, sizeof(float) * B * n * c.hidden, cudaMemcpyDeviceToHost), "D2H hidden");
     for (int b = 0; tokens && b < B; b++)

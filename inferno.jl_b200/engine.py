@@ -13,18 +13,56 @@ class ModelInfo(ctypes.Structure):
         ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("weight_bytes", ctypes.c_int64)]
 
 
+class Comm:
+    """Tensor-parallel communicator of one rank (NCCL, bound at run time).
+    unique_id() on rank 0; every rank passes the same bytes."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def available():
+        return bool(load().ifr_comm_available())
+
+    @staticmethod
+    def unique_id():
+        buf = (ctypes.c_uint8 * Comm.ID_BYTES)()
+        check(load().ifr_comm_unique_id(buf))
+        return bytes(buf)
+
+    def __init__(self, ctx, rank, world, uid=None):
+        self.ctx = ctx
+        self.rank, self.world = rank, world
+        h = ctypes.c_void_p()
+        idb = (ctypes.c_uint8 * Comm.ID_BYTES).from_buffer_copy(uid) if uid is not None else None
+        check(load().ifr_comm_create(ctx.handle, int(rank), int(world), idb, ctypes.byref(h)))
+        self.handle = h
+
+    def free(self):
+        if getattr(self, "handle", None):
+            load().ifr_comm_destroy(self.handle)
+            self.handle = None
+
+
 class Model:
     """A GGUF model resident on the context's device (load_model_cpu analogue,
-    src/LoaderCPU.jl:265-437)."""
+    src/LoaderCPU.jl:265-437); with a Comm, this rank's tensor-parallel shard."""
 
-    def __init__(self, ctx, path):
+    def __init__(self, ctx, path, comm=None):
         self.ctx = ctx
+        self.comm = comm
         h = ctypes.c_void_p()
-        check(load().ifr_model_load_gguf(ctx.handle, path.encode(), ctypes.byref(h)))
+        if comm is None:
+            check(load().ifr_model_load_gguf(ctx.handle, path.encode(), ctypes.byref(h)))
+        else:
+            check(load().ifr_model_load_gguf_tp(ctx.handle, path.encode(), comm.handle, ctypes.byref(h)))
         self.handle = h
         info = ModelInfo()
         check(load().ifr_model_get_info(self.handle, ctypes.byref(info)))
         self.info = info
+        sh = (ctypes.c_int32 * 8)()
+        check(load().ifr_model_get_shard(self.handle, sh))
+        (self.tp_rank, self.tp_world, self.n_head_local, self.n_kv_local, self.ffn_local, self.ffn_off,
+         self.vocab_local, self.vocab_off) = list(sh)
 
     def free(self):
         if getattr(self, "handle", None):
@@ -129,7 +167,7 @@ class State:
         n = ctypes.c_int()
         check(load().ifr_state_last_verify(self.handle, None, None, None, ctypes.byref(n)))
         rows = n.value * self.batch
-        lg = np.empty((rows, info.vocab), np.float32)
+        lg = np.empty((rows, self.model.vocab_local), np.float32)
         hd = np.empty((rows, info.hidden), np.float32)
         tk = np.empty(rows, np.int32)
         check(load().ifr_state_last_verify(self.handle, lg.ctypes.data_as(ctypes.c_void_p),

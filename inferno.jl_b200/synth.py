@@ -35,6 +35,22 @@ PRESETS = {
                  ffn=512, vocab=4096, ssm_heads=4, ssm_head_dim=64, conv_kernel=4,
                  attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=True,
                  context=1024),
+    # config 5: Gemma4 shapes (hidden 5376, 62 layers, 32 q / 16 kv x 128, FFN
+    # 21504, vocab 262144, Q4_K) built from the same Qwen-style attention blocks,
+    # and its Q8_0 draft model (hidden 1152, 26 layers); attention-only
+    "gemma": dict(hidden=5376, n_layers=62, n_head=32, n_kv_head=16, head_dim=128, rope_frac=0.25,
+                  ffn=21504, vocab=262144, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                  attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q4_K, mtp=False,
+                  context=8192, row_pool=1024),
+    "gemma_draft": dict(hidden=1152, n_layers=26, n_head=4, n_kv_head=1, head_dim=256, rope_frac=0.25,
+                        ffn=6912, vocab=262144, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                        attn_every=1, mat=G.GGML_Q8_0, down=G.GGML_Q8_0, emb=G.GGML_Q8_0, mtp=False,
+                        context=8192, row_pool=1024),
+    # attention-only test model whose heads and FFN units split over 2 ranks
+    "tp_mini": dict(hidden=256, n_layers=4, n_head=8, n_kv_head=4, head_dim=64, rope_frac=0.25,
+                    ffn=1024, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                    attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=False,
+                    context=1024),
 }
 
 
