@@ -243,6 +243,16 @@ int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts);
  * ifr_spec_step first so that every kernel is initialised before capture. */
 int ifr_spec_graph(ifr_state *s, int gamma, int steps);
 int ifr_spec_graph_launch(ifr_state *s);
+/* one greedy speculative step with a separate draft model (the draft ->
+ * verify -> accept loop of src/SpeculativeDecoding.jl:106-172 with the draft
+ * model's greedy tokens; the reference drafts with the same call shape):
+ * `draft` (an attention-only, unsharded model on the same context, prefilled
+ * with the same prompt) decodes gamma tokens, the target verifies them as in
+ * ifr_spec_step, and the draft follows the target's accepted prefix.
+ * Asynchronous; batch sizes must match.  ifr_spec_graph_draft captures
+ * `steps` such steps into the target state's graph (ifr_spec_graph_launch). */
+int ifr_spec_step_draft(ifr_state *target, ifr_state *draft, int gamma);
+int ifr_spec_graph_draft(ifr_state *target, ifr_state *draft, int gamma, int steps);
 /* per-launch CUDA-event timing of the state's work (0 = off, default), and
  * its totals per category since enabling: 0 verify lm_head, 1 draft lm_head,
  * 2 decoder-layer GEMVs, 3 draft GEMVs, 4 SSM steps, 5 attention steps

@@ -49,6 +49,8 @@ SIGNATURES = {
     "ifr_model_load_gguf": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "ifr_model_load_gguf_tp": (_i, [_vp, ctypes.c_char_p, _vp, ctypes.POINTER(_vp)]),
     "ifr_comm_available": (_i, []),
+    "ifr_spec_step_draft": (_i, [_vp, _vp, _i]),
+    "ifr_spec_graph_draft": (_i, [_vp, _vp, _i, _i]),
     "ifr_model_get_shard": (_i, [_vp, _vp]),
     "ifr_comm_unique_id": (_i, [_vp]),
     "ifr_comm_create": (_i, [_vp, _i, _i, _vp, ctypes.POINTER(_vp)]),

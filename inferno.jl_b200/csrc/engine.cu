@@ -1243,6 +1243,64 @@ int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first
 }  // extern "C"
 
 namespace {
+
+// draft-model steps: request b's token j of the target's verify tokens becomes
+// the draft state's next input
+__global__ void copy_token_kernel(int32_t *dst, const int32_t *src, int B) {
+    ifr::pdl_trigger();
+    ifr::pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) dst[(int64_t)b * kNMax] = src[(int64_t)b * kNMax];
+}
+// the draft state follows the target: its last token and position (positions
+// past the committed ones are overwritten by the next step; attention only)
+__global__ void draft_sync_kernel(ifr::EngineScalars *draft, const ifr::EngineScalars *target, int B) {
+    ifr::pdl_trigger();
+    ifr::pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) {
+        draft[b].last_token = target[b].last_token;
+        draft[b].pos = target[b].pos;
+        draft[b].a_prev = -1;
+    }
+}
+
+int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st);
+
+// one speculative step with a separate draft model (SpeculativeDecoding.jl's
+// draft -> verify -> accept loop with the draft model's greedy tokens): the
+// draft feeds [last, d1 .. d_gamma] (gamma + 1 single-token forwards, so that
+// its cache holds every token the target may commit), its argmaxes d1..d_gamma
+// go into the target's verify tokens; then verify, accept, commit, and the
+// draft is re-synced to the target's position and last token
+int draft_step_device(ifr_state *t, ifr_state *d, int gamma, cudaStream_t st) {
+    const int B = t->B;
+    const ifr_model_info &dc = d->m->info;
+    ECHECK(ifr::launch_k(draft_sync_kernel, dim3((B + 127) / 128), dim3(128), 0, st, d->sc,
+                         (const ifr::EngineScalars *)t->sc, B),
+           "draft sync");
+    for (int j = 1; j <= gamma + 1; j++) {
+        if (j > 1)
+            ECHECK(ifr::launch_k(copy_token_kernel, dim3((B + 127) / 128), dim3(128), 0, st, d->vtok,
+                                 (const int32_t *)(t->vtok + (j - 1)), B),
+                   "draft input");
+        int rc = target_forward(d, 1, j <= gamma, j == 1, st);
+        if (rc) return rc;
+        if (j <= gamma) {
+            rc = greedy_accept(d, nullptr, 0, B, 0, t->vtok + j, kNMax, st);
+            if (rc) return rc;
+        }
+        ifr::commit(d->sc, d->acc, d->outtok, 1, true, nullptr, nullptr, dc.hidden, d->log, d->log_cap, B, st);
+        d->launches += 2;
+    }
+    int rc = spec_step_device(t, gamma, false, st);
+    if (rc) return rc;
+    ECHECK(ifr::launch_k(draft_sync_kernel, dim3((B + 127) / 128), dim3(128), 0, st, d->sc,
+                         (const ifr::EngineScalars *)t->sc, B),
+           "draft sync");
+    return IFR_OK;
+}
+
 // the device work of one spec step (capturable): MTP drafts (or drafts
 // already in vtok[b * kNMax + 1 .. gamma]), verify, greedy accept, commit
 int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st) {
@@ -1293,6 +1351,62 @@ int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts) {
     if (!rc) {
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "spec step launch");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+namespace {
+int check_draft_pair(ifr_state *t, ifr_state *d, int gamma) {
+    if (!t || !d) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (gamma < 1 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 1..%d", kNMax - 1);
+    if (t->B != d->B) return ifr_fail(IFR_ERR_ARG, "target batch %d != draft batch %d", t->B, d->B);
+    if (t->m->ctx != d->m->ctx) return ifr_fail(IFR_ERR_ARG, "target and draft must share a context");
+    if (d->m->inner || d->m->comm) return ifr_fail(IFR_ERR_UNSUPPORTED, "the draft model must be attention-only and unsharded");
+    if (d->m->info.vocab != t->m->info.vocab) return ifr_fail(IFR_ERR_ARG, "draft and target vocabularies differ");
+    return IFR_OK;
+}
+}  // namespace
+
+int ifr_spec_step_draft(ifr_state *t, ifr_state *d, int gamma) {
+    int rc = check_draft_pair(t, d, gamma);
+    if (rc) return rc;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(t->m->ctx));
+    rc = draft_step_device(t, d, gamma, ifr_ctx_stream_of(t->m->ctx));
+    if (!rc) {
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "draft step launch");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int ifr_spec_graph_draft(ifr_state *t, ifr_state *d, int gamma, int steps) {
+    int rc = check_draft_pair(t, d, gamma);
+    if (rc) return rc;
+    if (steps < 1) return ifr_fail(IFR_ERR_ARG, "steps must be >= 1");
+    cudaStream_t st = ifr_ctx_stream_of(t->m->ctx);
+    if (st == nullptr) return ifr_fail(IFR_ERR_ARG, "the context stream is the legacy default stream, which cannot be captured");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(t->m->ctx));
+    if (t->graph_exec) { cudaGraphExecDestroy(t->graph_exec); t->graph_exec = nullptr; }
+    if (t->graph) { cudaGraphDestroy(t->graph); t->graph = nullptr; }
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) rc = ifr_cuda_fail(e, "begin capture");
+    for (int i = 0; !rc && i < steps; i++) rc = draft_step_device(t, d, gamma, st);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(st, &g);
+    if (!rc && e != cudaSuccess) rc = ifr_cuda_fail(e, "end capture");
+    if (!rc) {
+        t->graph = g;
+        e = cudaGraphInstantiate(&t->graph_exec, g, 0);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "graph instantiate");
+    } else if (g) {
+        cudaGraphDestroy(g);
     }
     cudaSetDevice(prev);
     return rc;

@@ -126,6 +126,14 @@ class State:
             assert d.size == gamma * self.batch
         check(load().ifr_spec_step(self.handle, int(gamma), d.ctypes.data_as(ctypes.c_void_p) if d is not None else None))
 
+    def spec_step_draft(self, draft, gamma):
+        """asynchronous: `draft` (a State of an attention-only draft model on the
+        same context) decodes gamma tokens -> verify -> accept -> commit"""
+        check(load().ifr_spec_step_draft(self.handle, draft.handle, int(gamma)))
+
+    def capture_draft(self, draft, gamma, steps):
+        check(load().ifr_spec_graph_draft(self.handle, draft.handle, int(gamma), int(steps)))
+
     def capture(self, gamma, steps):
         """capture `steps` MTP spec steps into a CUDA graph (context stream must be capturable)"""
         check(load().ifr_spec_graph(self.handle, int(gamma), int(steps)))

@@ -149,3 +149,39 @@ def _fixed(greedy, s, G, vocab):
     if s % 2:
         d[1] = (d[1] + 7) % vocab
     return d
+
+
+def test_draft_model_spec_decode_matches_oracle(O, pkg, ctx, tpm):
+    """ifr_spec_step_draft: a second (attention-only) model drafts greedily,
+    the target verifies; tokens and verify logits vs the oracle running the
+    same protocol with both models"""
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model, State
+    path, om = tpm
+    dpath = synth.cached("tp_mini", seed=2)
+    dm = O.OracleModel(gguf.GGUFFile(dpath), 512)
+    prompt = [int(t) for t in synth.prompt(om.vocab, 18, seed=5)]
+    G, steps = 3, 4
+    target, draft = Model(ctx, path), Model(ctx, dpath)
+    ts, ds = State(target, 256), State(draft, 256)
+    first = int(ts.prefill(np.array(prompt, np.int32)))
+    ds.prefill(np.array(prompt, np.int32))
+    plan = []
+
+    def drafts_at(out):
+        # the draft model's greedy continuation of prompt + emitted tokens
+        return [int(t) for t in dm.greedy(prompt + out, G)]
+    out = [first]
+    for s in range(steps):
+        plan.append(drafts_at(out))
+        out, _ = om.spec_decode(prompt, s + 1, G, drafts=lambda i: plan[i])
+    ref_out, ref = om.spec_decode(prompt, steps, G, drafts=lambda i: plan[i])
+    for s in range(steps):
+        ts.spec_step_draft(ds, G)
+        lg, _, tk = ts.last_verify()
+        assert list(tk[1:]) == plan[s], (s, tk, plan[s])
+        assert O.norm_rel(lg, ref[s]["logits"]).max() < LOGIT_TOL, s
+    toks, pos, acc, nst = ts.read()
+    assert [int(t) for t in toks] == ref_out
+    ts.free()
+    ds.free()
