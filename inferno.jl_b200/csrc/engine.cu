@@ -230,6 +230,8 @@ struct ifr_model {
 namespace {
 
 constexpr int kNMax = 8;
+// one request: split-KV attention from this cache length on (shorter caches use the cluster kernel)
+constexpr int kSplitMinCtx = 1024;
 
 int upload_f32(ifr_model *m, const Gguf &g, const std::string &name, int64_t expect, float **out) {
     auto it = g.t.find(name);
@@ -459,6 +461,7 @@ struct ifr_state {
     std::vector<float *> kc, vc;                // per layer (attention) else null
     float *mtp_kc = nullptr, *mtp_vc = nullptr;
     void *acc_scratch = nullptr;
+    float *attn_part = nullptr;         // split-KV attention: partial softmax states (null: cluster kernel)
     void *dense = nullptr;              // scratch of the dense tensor-core GEMMs
     int64_t dense_bytes = 0;
     int last_n = 0;
@@ -616,6 +619,10 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.eps = c.rms_eps;
         a.b_kv = kv_ld;
         a.b_pos = pos_ld;
+        if (s->attn_part) {
+            a.part = s->attn_part;
+            a.splits = ifr::attn_splits(m->nh, m->nkv, n, B, s->max_ctx);
+        }
         ECHECK(ifr::attn_step(a, B, st), "attn_step");
     }
     // row-parallel projections: rank 0 adds its partial to the residual, the
@@ -1089,6 +1096,11 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
             chk(dalloc(s, &s->vc[i], kvn));
         }
     }
+    // batches and long caches: split-KV attention (key slices spread over the
+    // GPU, partial softmax states merged by a second kernel); one request with
+    // a short cache keeps the single-launch cluster kernel
+    if (B > 1 || max_ctx >= kSplitMinCtx)
+        chk(dalloc(s, &s->attn_part, (size_t)ifr::attn_part_floats(m->nh, m->nkv, c.head_dim, B, max_ctx)));
     if (m->has_mtp) {
         chk(dalloc(s, &s->mtp_kc, kvn));
         chk(dalloc(s, &s->mtp_vc, kvn));
@@ -1189,6 +1201,13 @@ int ifr_state_reset(ifr_state *s) {
             ECHECK(cudaMemsetAsync(s->hist[i], 0, (size_t)s->B * (c.conv_kernel - 1) * s->m->conv_channels * 4, st),
                    "reset conv");
         }
+    // the MTP layer attends over positions that only its drafts write: they
+    // read as zeros until then, as after creation
+    if (s->mtp_kc) {
+        const size_t kvb = (size_t)s->B * s->max_ctx * s->m->nkv * c.head_dim * 4;
+        ECHECK(cudaMemsetAsync(s->mtp_kc, 0, kvb, st), "reset mtp cache");
+        ECHECK(cudaMemsetAsync(s->mtp_vc, 0, kvb, st), "reset mtp cache");
+    }
     ECHECK(cudaStreamSynchronize(st), "reset");
     return IFR_OK;
 }

@@ -7,6 +7,7 @@
 #include "common.cuh"
 #include "model.cuh"
 
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <math_constants.h>
 
@@ -736,16 +737,32 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     cluster.sync();  // peers may still read this CTA's shared memory
 }
 
-// Batched variant: one cluster of kAttnSplit CTAs per (KV head, request) covers
-// all `ratio` query heads of the group, so every cached key and value is read
-// once (not once per query head).  Rows r = hh * N + t (query head hh of the
-// group, token t).  Keys of the CTA's slice are staged in chunks of kGrpKeys
-// in shared memory (K rows padded by four floats: 16-byte loads without bank
-// conflicts); thread (key jj, row group w) scores rows w, w + 8, ..., one warp
-// per row updates the online softmax, and thread d accumulates P.V for dims d
-// (+ 256) of every row.
+// Split-KV (flash-decoding) attention, for batches and long caches: grid
+// (S, n_kv x row groups, B), no cluster.  CTA (s, y, b) takes keys
+// [s kps, (s + 1) kps) of request b - kps = attn_kps(nkeys, S), a multiple of
+// kGrpKeys sized from that request's own key count, so the live keys are
+// always spread evenly over the slices - for up to hg query heads of one KV
+// group (rows r = hh N + t, at most kGrpRows), so each row group reads every
+// cached key and value once, and the slice count grows with the cache length
+// (few KV heads or requests still fill the GPU).  Keys are staged in chunks of
+// kGrpKeys in shared memory (K rows padded by four floats: 16-byte loads
+// without bank conflicts); thread (key jj, row group w) scores rows w, w + 8,
+// ..., one warp per row updates the online softmax, and thread d accumulates
+// P.V for dims d (+ 256) of every row.  The slice's unnormalised (max, sum,
+// P.V) per row goes to scratch; attn_combine_kernel merges the slices with the
+// online-softmax rescaling and applies the output gate.
+//
+// Scratch per slice s (rows = B nh N, row id (b nh + h) N + t):
+// [max rows][sum rows][P.V rows x HD] at part + s rows (HD + 2).
 constexpr int kGrpKeys = 32;
-constexpr int kGrpRows = 32;  // ratio * N
+constexpr int kGrpRows = 32;      // hg * N
+constexpr int kSplitCtas = 8 * 148;  // target CTAs of one split launch
+constexpr int kMaxSplits = 256;
+
+__host__ __device__ __forceinline__ int attn_kps(int nkeys, int S) {
+    const int per = (nkeys + S - 1) / S;
+    return max(kGrpKeys, (per + kGrpKeys - 1) / kGrpKeys * kGrpKeys);
+}
 
 template <int HD>
 struct GrpSmem {
@@ -757,39 +774,32 @@ struct GrpSmem {
 };
 
 template <int HD>
-__global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
+__global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int S) {
     constexpr int KS = GrpSmem<HD>::KS;
-    constexpr int DS = HD / kAttnSplit;
     constexpr int RPT = (kGrpRows * HD + 255) / 256;  // P.V outputs per thread (upper bound)
     extern __shared__ __align__(16) float gs[];
-    const int rank = (int)cluster.block_rank();
-    const int g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int N = a.N, ratio = a.nh / a.nkv, R = ratio * N;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int N = a.N, ratio = a.nh / a.nkv, nrg = (ratio + hg - 1) / hg;
+    const int g = blockIdx.y / nrg, hb = blockIdx.y % nrg, h0 = g * ratio + hb * hg;
+    const int R = min(hg, ratio - hb * hg) * N;
+    const int sl = blockIdx.x, b = blockIdx.z;
     float *q = gs, *kn = q + R * HD, *vn = kn + N * HD, *Ks = vn + N * HD, *Vs = Ks + kGrpKeys * KS;
     float *sc = Vs + kGrpKeys * HD, *ms = sc + R * kGrpKeys, *ls = ms + R, *fs = ls + R;
-    float *po = Ks;  // after the key loop: this slice's P.V [R][HD] (fits: R * HD <= Ks + Vs)
     pdl_trigger();
     pdl_wait();
-    {  // request blockIdx.z
-        const int64_t b = blockIdx.z;
-        a.qkv += b * a.N * a.ldq;
-        a.out += b * a.N * a.ldo;
-        a.kc += b * a.b_kv;
-        a.vc += b * a.b_kv;
-        a.pos += b * a.b_pos;
-    }
-    const int p0 = *a.pos;
-    const int nkeys = p0 + N;
-    const int per = (nkeys + kAttnSplit - 1) / kAttnSplit;
-    const int lo = min(nkeys, rank * per), hi = min(nkeys, lo + per);
+    a.qkv += (int64_t)b * N * a.ldq;
+    a.kc += b * a.b_kv;
+    a.vc += b * a.b_kv;
+    const int p0 = a.pos[(int64_t)b * a.b_pos];
+    const int nkeys = p0 + N, kps = attn_kps(nkeys, S);
+    const int lo = sl * kps, hi = min(nkeys, lo + kps);
+    if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
     const int half = a.rotary_dim / 2;
 
-    // 1. the group's q rows, the new k and v; RMSNorm + RoPE (warp per row)
+    // 1. the row group's q rows, the new k and v; RMSNorm + RoPE (warp per row)
     for (int i = tid; i < R * HD; i += 256) {
         const int r = i / HD, d = i % HD, hh = r / N, t = r % N;
-        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(g * ratio + hh) * 2 * HD + d];
+        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * 2 * HD + d];
     }
     for (int i = tid; i < N * HD; i += 256) {
         const int t = i / HD, d = i % HD;
@@ -822,7 +832,8 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_g
         }
     }
     __syncthreads();
-    if (rank == 0) {
+    // one CTA per (KV head, request) writes the new keys; no CTA reads them from the cache
+    if (sl == 0 && hb == 0) {
         for (int i = tid; i < N * HD; i += 256) {
             const int t = i / HD, d = i % HD;
             const int64_t o = ((int64_t)(p0 + t) * a.nkv + g) * HD + d;
@@ -930,54 +941,123 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_g
         }
         __syncthreads();  // Ks, Vs, sc and fs are rewritten by the next chunk
     }
+
+    // 3. the slice's partial state
+    const int64_t rows = (int64_t)gridDim.z * a.nh * N;
+    float *pm = a.part + (int64_t)sl * rows * (HD + 2), *pl = pm + rows, *po = pl + rows;
+    const int64_t rid0 = ((int64_t)b * a.nh + h0) * N;  // row r of this CTA is row id rid0 + r
 #pragma unroll
     for (int k = 0; k < RPT; k++) {
         const int i = tid + 256 * k;
-        if (i < R * HD) po[i] = o[k];
+        if (i < R * HD) po[(rid0 + i / HD) * HD + i % HD] = o[k];
     }
+    if (tid < R) {
+        pm[rid0 + tid] = ms[tid];
+        pl[rid0 + tid] = ls[tid];
+    }
+}
 
-    // 3. combine the slices (distributed shared memory); this CTA: dims rank*DS ..
-    cluster.sync();
-    for (int i = tid; i < R * DS; i += 256) {
-        const int r = i / DS, dd = rank * DS + i % DS, hh = r / N, t = r % N;
-        float M = -CUDART_INF_F;
-        for (int k = 0; k < kAttnSplit; k++) M = fmaxf(M, cluster.map_shared_rank(ms, k)[r]);
-        float L = 0.f, O = 0.f;
-        for (int k = 0; k < kAttnSplit; k++) {
-            const float mr = cluster.map_shared_rank(ms, k)[r];
-            if (mr == -CUDART_INF_F) continue;
-            const float w = expf(mr - M);
-            L += cluster.map_shared_rank(ls, k)[r] * w;
-            O += cluster.map_shared_rank(po, k)[r * HD + dd] * w;
-        }
-        const int h = g * ratio + hh;
-        const float gv = a.qkv[(int64_t)t * a.ldq + (int64_t)h * 2 * HD + HD + dd];
-        a.out[(int64_t)t * a.ldo + (int64_t)h * HD + dd] = O / L * (1.0f / (1.0f + expf(-gv)));
+// Merges the key slices of one row (b, h, t) per CTA: M = max_s m_s,
+// L = sum_s l_s e^(m_s - M), O = sum_s o_s e^(m_s - M) (slice order), and
+// writes O / L x sigmoid(gate).  The slices' (m, l) and weights are formed in
+// parallel in shared memory; thread group q (256 / HD groups) sums P.V over
+// slices q, q + 256 / HD, ... with independent loads in flight, and the groups'
+// sums are added in group order.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch, int S) {
+    constexpr int NG = 256 / HD;
+    __shared__ float w[kMaxSplits], red[8], og[NG][HD];
+    pdl_trigger();
+    pdl_wait();
+    const int N = a.N, tid = threadIdx.x, d = tid % HD, q = tid / HD;
+    const int64_t rows = (int64_t)batch * a.nh * N, rid = blockIdx.x;
+    const int t = (int)(rid % N), h = (int)((rid / N) % a.nh), b = (int)(rid / ((int64_t)N * a.nh));
+    const int nkeys = a.pos[(int64_t)b * a.b_pos] + N, kps = attn_kps(nkeys, S);
+    const int ns = (nkeys + kps - 1) / kps;
+    const int64_t stride = rows * (HD + 2);
+    float mv = -CUDART_INF_F, lv = 0.f;
+    if (tid < ns) {
+        mv = a.part[tid * stride + rid];
+        lv = a.part[tid * stride + rows + rid];
     }
-    cluster.sync();  // peers may still read this CTA's shared memory
+    // block max of m (ns <= kMaxSplits <= 256)
+    float M = warp_max(mv);
+    if ((tid & 31) == 0) red[tid >> 5] = M;
+    __syncthreads();
+    M = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) M = fmaxf(M, red[i]);
+    const float wv = mv == -CUDART_INF_F ? 0.f : expf(mv - M);
+    if (tid < ns) w[tid] = wv;
+    const float L = block_sum256(lv * wv, red);  // synchronises: w visible
+    const float *po = a.part + 2 * rows + rid * HD + d;
+    float O = 0.f;
+    int sl = q;
+    for (; sl + 3 * NG < ns; sl += 4 * NG) {
+        const float o0 = po[sl * stride], o1 = po[(sl + NG) * stride];
+        const float o2 = po[(sl + 2 * NG) * stride], o3 = po[(sl + 3 * NG) * stride];
+        O += w[sl] * o0;
+        O += w[sl + NG] * o1;
+        O += w[sl + 2 * NG] * o2;
+        O += w[sl + 3 * NG] * o3;
+    }
+    for (; sl < ns; sl += NG) O += w[sl] * po[sl * stride];
+    if (NG > 1) {
+        og[q][d] = O;
+        __syncthreads();
+        if (q) return;
+        O = og[0][d];
+#pragma unroll
+        for (int g2 = 1; g2 < NG; g2++) O += og[g2][d];
+    }
+    const int64_t tok = (int64_t)b * N + t;
+    const float gv = a.qkv[tok * a.ldq + (int64_t)h * 2 * HD + HD + d];
+    a.out[tok * a.ldo + (int64_t)h * HD + d] = O / L * (1.0f / (1.0f + expf(-gv)));
+}
+
+static int split_heads(int ratio, int N) { return std::max(1, std::min(ratio, kGrpRows / N)); }
+
+int attn_splits(int nh, int nkv, int N, int batch, int max_ctx) {
+    const int ratio = nh / nkv, hg = split_heads(ratio, N), nrg = (ratio + hg - 1) / hg;
+    const int64_t ctas = (int64_t)nkv * nrg * batch;
+    int64_t S = (kSplitCtas + ctas - 1) / ctas;
+    S = std::min<int64_t>(S, (max_ctx + kGrpKeys - 1) / kGrpKeys);
+    S = std::min<int64_t>(S, kMaxSplits);
+    return (int)std::max<int64_t>(S, 1);
+}
+
+int64_t attn_part_floats(int nh, int nkv, int hd, int batch, int max_ctx) {
+    int S = 1;
+    for (int N = 1; N <= kMaxN; N++) S = std::max(S, attn_splits(nh, nkv, N, batch, max_ctx));
+    return (int64_t)S * batch * nh * kMaxN * (hd + 2);
 }
 
 template <int HD>
-static cudaError_t launch_group(const AttnArgs &a, int batch, cudaStream_t s) {
-    const int R = a.nh / a.nkv * a.N;
-    const int smem = GrpSmem<HD>::bytes(R, a.N);
+static cudaError_t launch_split(const AttnArgs &a, int batch, cudaStream_t s) {
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(attn_group_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(attn_part_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              GrpSmem<HD>::bytes(kGrpRows, kMaxN));
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return launch_k(attn_group_kernel<HD>, dim3(kAttnSplit, a.nkv, batch), dim3(256), (size_t)smem, s, a);
+    const int ratio = a.nh / a.nkv, hg = split_heads(ratio, a.N), nrg = (ratio + hg - 1) / hg;
+    const int R = std::min(hg, ratio) * a.N;
+    cudaError_t e = launch_k(attn_part_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
+                             (size_t)GrpSmem<HD>::bytes(R, a.N), s, a, hg, a.splits);
+    if (e != cudaSuccess) return e;
+    return launch_k(attn_combine_kernel<HD>, dim3((unsigned)(batch * a.nh * a.N)), dim3(256), 0, s, a, batch,
+                    a.splits);
 }
 
 cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.nh % a.nkv || batch < 1) return cudaErrorInvalidValue;
-    // many requests: group the query heads of each KV head (KV read once)
-    if (batch > 1 && (a.nh / a.nkv) * a.N <= kGrpRows) {
-        if (a.hd == 256) return launch_group<256>(a, batch, s);
-        if (a.hd == 128) return launch_group<128>(a, batch, s);
-        if (a.hd == 64) return launch_group<64>(a, batch, s);
+    if (a.splits > 0) {
+        if (!a.part || a.splits > kMaxSplits) return cudaErrorInvalidValue;
+        if (a.hd == 256) return launch_split<256>(a, batch, s);
+        if (a.hd == 128) return launch_split<128>(a, batch, s);
+        if (a.hd == 64) return launch_split<64>(a, batch, s);
+        return cudaErrorInvalidValue;
     }
     const dim3 grid(kAttnSplit, a.nh, batch);
     if (a.hd == 256) return launch_k(attn_step_kernel<256>, grid, dim3(256), 0, s, a);

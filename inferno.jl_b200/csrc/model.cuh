@@ -54,6 +54,10 @@ struct AttnArgs {
     float eps;
     int64_t b_kv = 0;    // per-request stride of kc / vc
     int b_pos = 0;       // stride of pos (int32)
+    // split-KV path (attn_splits > 0): key slices per row group and the
+    // scratch of their partial softmax states (attn_part_floats floats)
+    int splits = 0;
+    float *part = nullptr;
 };
 
 void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float eps, int64_t ldx, int64_t ldo,
@@ -61,6 +65,10 @@ void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float 
 void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s);
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s);
 cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s);
+// key slices of a split-KV call of N tokens per request, and the scratch
+// (floats) that every call on a state of `batch` requests and max_ctx fits in
+int attn_splits(int nh, int nkv, int N, int batch, int max_ctx);
+int64_t attn_part_floats(int nh, int nkv, int hd, int batch, int max_ctx);
 // per request b (grid of `batch` CTAs): sc + b, acc + b, out_tok + b * n,
 // hid + b * n * d, mtp_h + b * d, log + b * log_cap
 void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,

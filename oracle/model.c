@@ -185,7 +185,15 @@ void or_model_reset(or_model *m) {
             memset(L->h, 0, (size_t)m->c.ssm_heads * m->c.ssm_head_dim * m->c.ssm_head_dim * 4);
         }
     }
-    if (m->mtp_fc) alloc_state(m, &m->mtp_layer);
+    if (m->mtp_fc) {
+        /* the MTP layer attends over positions that only its drafts write:
+           zeros until then, as after allocation */
+        or_layer *L = &m->mtp_layer;
+        alloc_state(m, L);
+        const size_t kv = (size_t)m->c.max_ctx * m->c.n_kv_head * m->c.head_dim * 4;
+        memset(L->kc, 0, kv);
+        memset(L->vc, 0, kv);
+    }
 }
 
 /* ---------------- building blocks ---------------- */

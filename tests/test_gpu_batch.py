@@ -111,3 +111,37 @@ def test_batch_argument_errors(pkg, mini):
     h = ctypes.c_void_p()
     assert load().ifr_state_create_batch(model.handle, 512, 0, ctypes.byref(h)) != 0
     assert load().ifr_state_create_batch(model.handle, 512, 10**6, ctypes.byref(h)) != 0
+
+
+@pytest.mark.parametrize("B,P,max_ctx", [(1, 300, 1024), (3, 200, 512)])
+def test_split_kv_attention_matches_oracle(O, ctx, mini, B, P, max_ctx):
+    """split-KV attention (one request with a long cache, or a batch): the
+    keys of every request spread over several slices whose partial softmax
+    states are merged; the exact-path bar (tokens equal, logits 1e-4)"""
+    from inferno_b200.engine import State
+    model, om = mini
+    V = model.info.vocab
+    G, steps = 4, 3
+    prompts = _prompts(V, B, P)
+    ref = [om.spec_decode(list(p), steps, G) for p in prompts]
+    ctx.set_dense_min_cols(10**6)  # every projection on the exact small-N kernel
+    try:
+        st = State(model, max_ctx, batch=B)
+        firsts = st.prefill(prompts if B > 1 else prompts[0])
+        firsts = np.atleast_1d(firsts)
+        assert [int(f) for f in firsts] == [r[0][0] for r in ref]
+        for s in range(steps):
+            st.spec_step(G)
+            lg, _, tk = st.last_verify()
+            lg = lg.reshape(B, G + 1, V)
+            tk = tk.reshape(B, G + 1)
+            for b in range(B):
+                r = ref[b][1][s]
+                assert list(tk[b, 1:]) == r["drafts"], (b, s)
+                assert O.norm_rel(lg[b], r["logits"]).max() < LOGIT_TOL, (b, s)
+        for b in range(B):
+            toks, *_ = st.read(b)
+            assert list(toks) == ref[b][0], b
+        st.free()
+    finally:
+        ctx.set_dense_min_cols(24)
