@@ -117,6 +117,17 @@ int ifr_dequant(ifr_ctx *ctx, const ifr_tensor *t, float *dev_out);
 int ifr_qgemm(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
               float *Y_dev);
 
+/* Y = W * RMSNorm(X) for ncols columns: each column x normalised as
+ * x * (1 / sqrt(mean(x^2) + eps)) * norm_w (rmsnorm_cpu!, src/ModelCPU.jl:
+ * 111-123) and multiplied by W, in one launch per 8 columns.  With exact
+ * activations the norm is folded into the epilogue: W (x * norm_w) times the
+ * column's 1/rms, the sums of squares formed from the loads that feed the
+ * tensor cores.  norm_w [cols] f32 on the device, 16-byte aligned; other
+ * arguments as ifr_qgemm.  Replaces the reference's rmsnorm_cpu! followed by
+ * the per-column GEMV of src/ModelCPU.jl:285-379. */
+int ifr_qgemm_rmsnorm(ifr_ctx *ctx, const ifr_tensor *W, const float *X_dev, int ncols,
+                      const float *norm_w_dev, float eps, float *Y_dev);
+
 /* Y = W * X for many columns at once (batched verify across requests, prompt
  * chunks) on the tcgen05 tensor cores: every weight is its exact dequantized
  * value rounded to fp16, every activation column is scaled by a power of two

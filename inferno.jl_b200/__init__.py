@@ -157,6 +157,18 @@ class Context:
         check(load().ifr_qgemm(self.handle, W.handle, _ptr(X), n, _ptr(out)))
         return out
 
+    def qgemm_rmsnorm(self, W, X, norm_w, eps, out=None):
+        """X [ncols, cols] f32 (device) -> Y [ncols, rows] = W RMSNorm(X; norm_w, eps)"""
+        torch = self.torch
+        assert X.dtype == torch.float32 and X.is_contiguous() and X.shape[-1] == W.cols
+        assert norm_w.dtype == torch.float32 and norm_w.is_contiguous() and norm_w.numel() == W.cols
+        n = X.numel() // W.cols
+        if out is None:
+            out = torch.empty(n, W.rows, dtype=torch.float32, device=X.device)
+        check(load().ifr_qgemm_rmsnorm(self.handle, W.handle, _ptr(X), n, _ptr(norm_w), ctypes.c_float(eps),
+                                       _ptr(out)))
+        return out
+
     def qgemm_dense(self, W, X, out=None):
         """X [ncols, cols] f32 (device) -> Y [ncols, rows] on the tensor cores
         (fp16 operands, f32 accumulation)"""

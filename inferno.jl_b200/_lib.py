@@ -40,6 +40,7 @@ SIGNATURES = {
     "ifr_prefill_batch": (_i, [_vp, _vp, _i, _vp]),
     "ifr_state_create_batch": (_i, [_vp, _i, _i, ctypes.POINTER(_vp)]),
     "ifr_qgemm_dense": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "ifr_qgemm_rmsnorm": (_i, [_vp, _vp, _vp, _i, _vp, _f, _vp]),
     "ifr_ctx_reserve_dense": (_i, [_vp, _vp, _i]),
     "ifr_quantize": (_i, [_i, _vp, _i64, _i64, _vp]),
     "ifr_accept": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),

@@ -325,6 +325,29 @@ int ifr_qgemm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float 
     return IFR_OK;
 }
 
+int ifr_qgemm_rmsnorm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, const float *norm_w, float eps,
+                      float *Y) {
+    if (!c || !W || !X || !Y || !norm_w) return fail(IFR_ERR_ARG, "NULL argument");
+    if (ncols < 1) return fail(IFR_ERR_ARG, "ncols must be >= 1 (got %d)", ncols);
+    if (W->device != c->device) return fail(IFR_ERR_ARG, "tensor lives on device %d, context on %d", W->device, c->device);
+    if (((uintptr_t)X & 15) || ((uintptr_t)norm_w & 15) || ((uintptr_t)Y & 3))
+        return fail(IFR_ERR_ARG, "X and norm_w must be 16-byte and Y 4-byte aligned");
+    if (!(eps >= 0.f)) return fail(IFR_ERR_ARG, "eps must be >= 0");
+    DeviceGuard g(c->device);
+    for (int n0 = 0; n0 < ncols; n0 += IFR_MAX_VERIFY_COLS) {
+        int n = ncols - n0 < IFR_MAX_VERIFY_COLS ? ncols - n0 : IFR_MAX_VERIFY_COLS;
+        ifr::XForm xf;
+        xf.act = c->act;
+        xf.kind = 1;
+        xf.w = norm_w;
+        xf.eps = eps;
+        IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, false,
+                                        W->q.rows, c->stream, xf),
+                       "qgemm launch");
+    }
+    return IFR_OK;
+}
+
 int ifr_ctx_reserve_dense(ifr_ctx *c, const ifr_tensor *W, int ncols) {
     if (!c || !W) return fail(IFR_ERR_ARG, "NULL argument");
     if (ncols < 1) return fail(IFR_ERR_ARG, "ncols must be >= 1 (got %d)", ncols);

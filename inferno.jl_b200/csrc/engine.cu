@@ -561,17 +561,22 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     const int B = s->B, nc = B * n;
     const int gcat = draft ? CAT_DRAFT_GEMV : CAT_LAYER_GEMV;
     int rc;
-    // RMSNorm kernels feed the input GEMVs (fusing the norm into every GEMV CTA
-    // costs each of them a full reduction over the input, more than the launch)
-    ifr::rmsnorm(s->x, L.attn_norm, s->xn, nc, d, c.rms_eps, d, d, st);
-    s->launches += 3;  // two norms, the SSM / attention step
-    if ((rc = gemv(s, gcat, L.proj, s->xn, nc, s->proj, false, st))) return rc;
+    // the layer's two RMSNorms are applied inside their consumers: the input
+    // GEMVs (folded into the epilogue on the small-N kernel, in the packing
+    // kernel on the dense path) and the SSM's alpha / beta projections
+    ifr::XForm in_norm;
+    in_norm.kind = 1;
+    in_norm.w = L.attn_norm;
+    in_norm.eps = c.rms_eps;
+    s->launches += (L.ssm || !s->attn_part) ? 1 : 2;  // the SSM / attention step (split-KV: two kernels)
+    if ((rc = gemv(s, gcat, L.proj, s->x, nc, s->proj, false, st, in_norm))) return rc;
     if (L.ssm) {
         ProfScope ps(s, CAT_SSM, 0, st);
         ifr::SsmArgs a{};
         a.proj = s->proj;
         a.ldp = L.proj.rows;
-        a.xn = s->xn;
+        a.xn = s->x;
+        a.in_norm = L.attn_norm;
         a.d = d;
         a.conv_w = L.conv_w;
         a.ab_w = L.ab_w;
@@ -629,16 +634,17 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     // others write theirs, and one sum all-reduce leaves x + sum on every rank
     if ((rc = gemv(s, gcat, L.out, s->y, nc, s->x, m->tp_rank == 0, st))) return rc;
     if ((rc = comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st))) return rc;
-    ifr::rmsnorm(s->x, L.post_norm, s->xn, nc, d, c.rms_eps, d, d, st);
+    ifr::XForm post_norm = in_norm;
+    post_norm.w = L.post_norm;
     if (L.gate_up.glu) {
         // silu(gate) * up formed in the gate/up GEMV's epilogue
-        ifr::XForm glu;
+        ifr::XForm glu = post_norm;
         glu.ep = 1;
-        if ((rc = gemv(s, gcat, L.gate_up, s->xn, nc, s->hmid, false, st, glu))) return rc;
+        if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->hmid, false, st, glu))) return rc;
         if ((rc = gemv(s, gcat, L.down, s->hmid, nc, s->x, m->tp_rank == 0, st))) return rc;
         return comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st);
     }
-    if ((rc = gemv(s, gcat, L.gate_up, s->xn, nc, s->gu, false, st))) return rc;
+    if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->gu, false, st, post_norm))) return rc;
     // silu(gate) * up formed while the down GEMV reads [gate | up]
     ifr::XForm swiglu;
     swiglu.kind = 2;
@@ -1518,16 +1524,17 @@ int ifr_gemv_pass(ifr_state *s, int ncols) {
     // buffers a spec step rewrites before it reads them (proj, gu, hid): the
     // caches, SSM states and residual stream are not changed
     for (auto &L : s->m->layers) {
-        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.proj, s->xn, ncols, s->proj, false, st);
+        norm.w = L.attn_norm;
+        if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.proj, s->xn, ncols, s->proj, false, st, norm);
         if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.out, s->y, ncols, s->hid, false, st);
         norm.w = L.post_norm;
         if (L.gate_up.glu) {
-            ifr::XForm glu;
+            ifr::XForm glu = norm;
             glu.ep = 1;
             if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->hmid, false, st, glu);
             if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.down, s->hmid, ncols, s->hid, false, st);
         } else {
-            if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->gu, false, st);
+            if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.gate_up, s->xn, ncols, s->gu, false, st, norm);
             if (!rc) rc = gemv(s, CAT_LAYER_GEMV, L.down, s->gu, ncols, s->hid, false, st, swiglu);
         }
     }

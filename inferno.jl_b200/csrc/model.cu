@@ -117,10 +117,10 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     __shared__ __align__(16) float rk[kMaxN][HD];
     __shared__ float rv[kMaxN][RPC];
     __shared__ float rdec[kMaxN], rbeta[kMaxN], ndec[kMaxN], nbeta[kMaxN];
-    __shared__ float ab[2][kMaxN], ab_part[2][kMaxN];
+    __shared__ float ab[3][kMaxN], ab_part[3][kMaxN];
     __shared__ float ys[kMaxN][RPC];
     __shared__ float ssq[kMaxN];
-    __shared__ float red_n[8][2 * kMaxN];
+    __shared__ float red_n[8][3 * kMaxN];
     pdl_trigger();
     pdl_wait();
     {  // request blockIdx.z of a batched call
@@ -181,32 +181,34 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     //    `rank` sums its d / kSsmSplit slice, the partials are added across the
     //    cluster in rank order after the next cluster barrier (step 5)
     {
-        float pa[kMaxN], pb[kMaxN];
+        float pa[kMaxN], pb[kMaxN], ps[kMaxN];
 #pragma unroll
-        for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = 0.f;
+        for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = ps[t] = 0.f;
         const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
         const int per = (a.d + kSsmSplit - 1) / kSsmSplit;
         const int i0 = rank * per, i1 = min(a.d, i0 + per);
         for (int i = i0 + tid; i < i1; i += 256) {
-            const float al = wa[i], be = wb[i];
+            const float al = wa[i], be = wb[i], nw = a.in_norm ? a.in_norm[i] : 1.f;
 #pragma unroll
             for (int t = 0; t < kMaxN; t++)
                 if (t < N) {
-                    const float xn = a.xn[(int64_t)t * a.d + i];
+                    const float xv = a.xn[(int64_t)t * a.d + i], xn = xv * nw;
                     pa[t] += al * xn;
                     pb[t] += be * xn;
+                    ps[t] += xv * xv;
                 }
         }
 #pragma unroll
         for (int t = 0; t < kMaxN; t++) {
-            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]);
+            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]), vs = warp_sum(ps[t]);
             if (lane == 0) {
                 red_n[warp][t] = va;
                 red_n[warp][kMaxN + t] = vb;
+                red_n[warp][2 * kMaxN + t] = vs;
             }
         }
         __syncthreads();
-        if (tid < 2 * N) {
+        if (tid < 3 * N) {
             const int which = tid / N, t = tid % N;
             float v = 0.f;
             for (int w8 = 0; w8 < 8; w8++) v += red_n[w8][which * kMaxN + t];
@@ -229,11 +231,17 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
         xq[t][c] = cluster.map_shared_rank(&cq[0][0], src)[t * RPC + ci];
         xk[t][c] = cluster.map_shared_rank(&ck[0][0], src)[t * RPC + ci];
     }
-    if (tid < 2 * N) {
+    if (tid < 3 * N) {
         const int which = tid / N, t = tid % N;
         float v = 0.f;
         for (int q = 0; q < kSsmSplit; q++) v += cluster.map_shared_rank(&ab_part[0][0], q)[which * kMaxN + t];
         ab[which][t] = v;
+    }
+    __syncthreads();
+    if (a.in_norm && tid < N) {  // RMSNorm folded: the projections of x w, scaled by rms(x)^-1
+        const float iv = 1.0f / sqrtf(ab[2][tid] / (float)a.d + a.eps);
+        ab[0][tid] *= iv;
+        ab[1][tid] *= iv;
     }
     __syncthreads();
     // 5. L2 norms of q, k per new token (warp t), gates in f64
@@ -345,8 +353,8 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
     __shared__ float rv[kMaxN][HD];
     __shared__ float ys[kMaxN][HD];
     __shared__ float rdec[kMaxN], rbeta[kMaxN], ndec[kMaxN], nbeta[kMaxN];
-    __shared__ float ab[2][kMaxN], ssq[kMaxN];
-    __shared__ float red_n[NW][2 * kMaxN];
+    __shared__ float ab[3][kMaxN], ssq[kMaxN];
+    __shared__ float red_n[NW][3 * kMaxN];
     pdl_trigger();
     pdl_wait();
     {  // request blockIdx.y
@@ -401,26 +409,28 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
     }
     // 2. alpha / beta projections of the new tokens, block-wide
     {
-        float pa[kMaxN], pb[kMaxN];
+        float pa[kMaxN], pb[kMaxN], ps[kMaxN];
 #pragma unroll
-        for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = 0.f;
+        for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = ps[t] = 0.f;
         const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
         for (int i = tid; i < a.d; i += NT) {
-            const float al = wa[i], be = wb[i];
+            const float al = wa[i], be = wb[i], nw = a.in_norm ? a.in_norm[i] : 1.f;
 #pragma unroll
             for (int t = 0; t < kMaxN; t++)
                 if (t < N) {
-                    const float xn = a.xn[(int64_t)t * a.d + i];
+                    const float xv = a.xn[(int64_t)t * a.d + i], xn = xv * nw;
                     pa[t] += al * xn;
                     pb[t] += be * xn;
+                    ps[t] += xv * xv;
                 }
         }
 #pragma unroll
         for (int t = 0; t < kMaxN; t++) {
-            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]);
+            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]), vs = warp_sum(ps[t]);
             if (lane == 0) {
                 red_n[warp][t] = va;
                 red_n[warp][kMaxN + t] = vb;
+                red_n[warp][2 * kMaxN + t] = vs;
             }
         }
     }
@@ -435,11 +445,17 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
         rbeta[tid] = rec[tid * REC + 2 * HD + 1];
     }
     __syncthreads();
-    if (tid < 2 * N) {
+    if (tid < 3 * N) {
         const int which = tid / N, t = tid % N;
         float v = 0.f;
         for (int w8 = 0; w8 < NW; w8++) v += red_n[w8][which * kMaxN + t];
         ab[which][t] = v;
+    }
+    __syncthreads();
+    if (a.in_norm && tid < N) {  // RMSNorm folded: the projections of x w, scaled by rms(x)^-1
+        const float iv = 1.0f / sqrtf(ab[2][tid] / (float)a.d + a.eps);
+        ab[0][tid] *= iv;
+        ab[1][tid] *= iv;
     }
     __syncthreads();
     // 4. L2 norms of q, k (warp t), gates in f64

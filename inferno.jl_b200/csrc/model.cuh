@@ -23,8 +23,10 @@ struct EngineScalars {
 struct SsmArgs {
     const float *proj;   // [N][ldp]: conv inputs q|k|v (C) then z (inner)
     int64_t ldp;
-    const float *xn;     // [N][d] normalised layer input (alpha/beta projections)
+    const float *xn;     // [N][d] normalised layer input (alpha/beta projections), or
+                         // the raw input when in_norm is set
     int d;
+    const float *in_norm = nullptr;  // RMSNorm weights [d]: alpha/beta = rms(x)^-1 (ab_w . (x w))
     const float *conv_w; // [C][K]
     const float *ab_w;   // [2H][d]: alpha rows then beta rows
     const float *ssm_a, *dt_bias, *norm_w;

@@ -38,6 +38,7 @@ namespace ifr {
 __device__ int g_dev_error = 0;
 
 constexpr int kConsumers = 8;
+constexpr int kMaxFoldUnits = 512;  // folded RMSNorm: K up to 131072
 constexpr int kThreads = 32 * kConsumers;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -139,61 +140,100 @@ IFR_DEV uint32_t cvt_h2(float hi_half, float lo_half) {
 IFR_DEV float h2_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
 IFR_DEV float h2_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
 
-// one activation with the transform applied (ragged K: the rare scalar path)
-template <int XF>
-__device__ __noinline__ float load_x1(const GemvArgs &a, const float *xc, float iv, int64_t k) {
-    if (k >= a.K) return 0.f;
-    float x = __ldg(xc + k);
-    if (XF == 1) x = x * iv * __ldg(a.xw + k);
-    if (XF == 2) x = x / (1.0f + expf(-x)) * __ldg(xc + a.K + k);
-    return x;
-}
-
-// 8 runs of 4 activations of column col at k0 + i * step (transform XF
-// applied; 0 beyond K or for absent columns)
-template <int XF>
-IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, int step, bool has, float *v) {
-    const float *xc = a.X + (int64_t)col * a.ldx;
-    const float iv = XF == 1 && has ? inv[col] : 0.f;
+// 8 runs of 4 floats at p + k0 + i * step (0 beyond K or when !has).  No
+// value is used here, so every load of the 8 runs is in flight at once.
+IFR_DEV void ld_runs(const float *p, int64_t K, int64_t k0, int step, bool has, float4 (&r)[8]) {
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int64_t k = k0 + (int64_t)step * i;
-        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has && k + 3 < a.K) {
-            q = __ldg(reinterpret_cast<const float4 *>(xc + k));
-            if (XF == 1) {
-                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.xw + k));
-                q.x = q.x * iv * w.x;
-                q.y = q.y * iv * w.y;
-                q.z = q.z * iv * w.z;
-                q.w = q.w * iv * w.w;
-            } else if (XF == 2) {
-                const float4 u = __ldg(reinterpret_cast<const float4 *>(xc + a.K + k));
-                q.x = q.x / (1.0f + expf(-q.x)) * u.x;
-                q.y = q.y / (1.0f + expf(-q.y)) * u.y;
-                q.z = q.z / (1.0f + expf(-q.z)) * u.z;
-                q.w = q.w / (1.0f + expf(-q.w)) * u.w;
-            }
-        } else if (has) {
-            q = make_float4(load_x1<XF>(a, xc, iv, k), load_x1<XF>(a, xc, iv, k + 1),
-                            load_x1<XF>(a, xc, iv, k + 2), load_x1<XF>(a, xc, iv, k + 3));
+        r[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has && k + 3 < K) {
+            r[i] = __ldg(reinterpret_cast<const float4 *>(p + k));
+        } else if (has) {  // ragged K: the rare scalar path
+            if (k < K) r[i].x = __ldg(p + k);
+            if (k + 1 < K) r[i].y = __ldg(p + k + 1);
+            if (k + 2 < K) r[i].z = __ldg(p + k + 2);
+        }
+    }
+}
+
+// 8 runs of 4 activations of column col at k0 + i * step (transform XF
+// applied; 0 beyond K or for absent columns): all loads first, then the
+// arithmetic.  XF 3 (RMSNorm folded into the epilogue): x * w, and ss
+// accumulates the raw x^2
+template <int XF>
+IFR_DEV void xform_runs(const float4 (&xr)[8], const float4 (&wr)[8], float iv, float *v, float *ss) {
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float4 q = xr[i];
+        if (XF == 1) {
+            q.x = q.x * iv * wr[i].x;
+            q.y = q.y * iv * wr[i].y;
+            q.z = q.z * iv * wr[i].z;
+            q.w = q.w * iv * wr[i].w;
+        } else if (XF == 3) {
+            s2 += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+            q.x *= wr[i].x;
+            q.y *= wr[i].y;
+            q.z *= wr[i].z;
+            q.w *= wr[i].w;
+        } else if (XF == 2) {
+            q.x = q.x / (1.0f + expf(-q.x)) * wr[i].x;
+            q.y = q.y / (1.0f + expf(-q.y)) * wr[i].y;
+            q.z = q.z / (1.0f + expf(-q.z)) * wr[i].z;
+            q.w = q.w / (1.0f + expf(-q.w)) * wr[i].w;
         }
         v[4 * i] = q.x;
         v[4 * i + 1] = q.y;
         v[4 * i + 2] = q.z;
         v[4 * i + 3] = q.w;
     }
+    if (XF == 3) *ss += s2;
 }
 
+template <int XF>
+IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, int step, bool has, float *v,
+                      float *ss = nullptr) {
+    const float *xc = a.X + (int64_t)col * a.ldx;
+    float4 xr[8], wr[8];
+    ld_runs(xc, a.K, k0, step, has, xr);
+    if (XF == 1 || XF == 3) ld_runs(a.xw, a.K, k0, step, has, wr);
+    if (XF == 2) ld_runs(xc + a.K, a.K, k0, step, has, wr);  // up half of [gate | up]
+    xform_runs<XF>(xr, wr, XF == 1 && has ? inv[col] : 0.f, v, ss);
+}
+
+// ssq (XF 3, may be null): [unit][8] sums of x^2 of the unit's activations
 template <int FMT, int NT, int XF>
-IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, BFrag<NT> &F) {
+IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, BFrag<NT> &F, float *ssq) {
     const int g = lane >> 2, t = lane & 3, part = g & 1;
+    // this lane's steps 8 part .. 8 part + 7 (elem_s() of tiles.cuh): the same
+    // positions in every column; every column's loads (and the norm weights)
+    // in flight before the first is used (SwiGLU inputs: per column)
+    const int64_t k0 = u * 256 + 128 * part + 4 * t;
+    float4 xr[NT][8], wr[8];
+    if (XF != 2) {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int col = 4 * nt + (g >> 1);
+            ld_runs(a.X + (int64_t)col * a.ldx, a.K, k0, 16, col < a.ncols, xr[nt]);
+        }
+        if (XF == 1 || XF == 3) ld_runs(a.xw, a.K, k0, 16, true, wr);
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int col = 4 * nt + (g >> 1);
-        // this lane's steps 8 part .. 8 part + 7 (elem_s() of tiles.cuh)
         float v[32];
-        load_x32<XF>(a, inv, col, u * 256 + 128 * part + 4 * t, 16, col < a.ncols, v);
+        float ss = 0.f;
+        if (XF == 2) load_x32<XF>(a, inv, col, k0, 16, col < a.ncols, v, &ss);
+        else xform_runs<XF>(xr[nt], wr, XF == 1 && col < a.ncols ? inv[col] : 0.f, v, &ss);
+        if (XF == 3) {
+            // the unit's 256 elements of column col are spread over lanes 8c .. 8c + 7
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+            if (ssq && (lane & 7) == 0) ssq[u * 8 + col] = ss;
+        }
         float mx = 0.f;
 #pragma unroll
         for (int r = 0; r < 32; r++) mx = fmaxf(mx, fabsf(v[r]));
@@ -672,6 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     uint8_t *ring = smem + 128;
     float *red = reinterpret_cast<float *>(ring + (size_t)a.S * STAGE);
     float *acc = red + kConsumers * NRED * 32;  // [sweep_rg * MTG * 16 rows][8 cols]
+    float *ssq = acc + a.sweep_rg * MTG * 16 * 8;  // XF 3: [nu][8] sums of x^2 per unit and column
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nrg = (a.nrb + MTG - 1) / MTG;
     Order o;
@@ -737,7 +778,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
             const bool active = u < a.nu;
             if (active) {
                 if constexpr (kI8) build_b_i8<FMT, XF>(a, inv_s, u, lane, F);
-                else build_b<FMT, NT, XF>(a, inv_s, u, lane, F);
+                else build_b<FMT, NT, XF>(a, inv_s, u, lane, F, sw == o.rg_lo ? ssq : nullptr);
             }
             for (int rg = sw; rg < sw_hi; rg++, it++) {
                 const int s = it % a.S;
@@ -801,6 +842,20 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         }
         // the sweep's rows are final: write Y (coalesced over rows)
         const int64_t row0 = (int64_t)sw * MTG * 16;
+        // XF 3: W (x w) / rms(x) per column; the sums of squares in unit order
+        if (XF == 3) {
+            if (tid < 8) {
+                float v = 0.f;
+                if (tid < a.ncols)
+                    for (int uu = 0; uu < a.nu; uu++) v += ssq[uu * 8 + tid];
+                inv_s[tid] = tid < a.ncols ? 1.0f / sqrtf(v / (float)a.K + a.eps) : 0.f;
+            }
+            consumer_bar();
+        }
+        auto accv = [&](int r, int col) {
+            const float v = acc[r * 8 + col];
+            return XF == 3 ? v * inv_s[col] : v;
+        };
         if (a.ep) {
             // mlp_forward (ModelCPU.jl:482-508): h = silu(gate) * up; a sweep holds whole
             // gate/up block pairs (MTG is even), local rows 32p.. gate, 32p+16.. up
@@ -810,7 +865,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
                 const int col = i / half_rows, rr = i % half_rows;
                 const int gr = (rr >> 4) * 32 + (rr & 15);
                 if (j0 + rr < a.M / 2 && !dead) {
-                    const float gv = acc[gr * 8 + col], uv = acc[(gr + 16) * 8 + col];
+                    const float gv = accv(gr, col), uv = accv(gr + 16, col);
                     a.Y[(int64_t)col * a.ldy + j0 + rr] = gv / (1.0f + expf(-gv)) * uv;
                 }
             }
@@ -819,7 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
                 const int col = i / sw_rows, r = i % sw_rows;
                 if (row0 + r < a.M && !dead) {
                     float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
-                    *y = a.accumulate ? *y + acc[r * 8 + col] : acc[r * 8 + col];
+                    *y = a.accumulate ? *y + accv(r, col) : accv(r, col);
                 }
             }
         }
@@ -857,12 +912,13 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     int S = (kSmemMax - 128 - red - 16 * 1024) / STAGE;
     S = S < 2 ? 2 : (S > 5 ? 5 : S);
     if (S > stages_per_cta) S = (int)stages_per_cta;  // small matrices: request only what is used
-    const int acc_bytes_avail = kSmemMax - 128 - S * STAGE - red;
+    const int ssq_bytes = XF == 3 ? (int)T.nu * 8 * 4 : 0;
+    const int acc_bytes_avail = kSmemMax - 128 - S * STAGE - red - ssq_bytes;
     const int rg_bytes = MTG * 16 * 8 * 4;
     int sweep_rg = acc_bytes_avail / rg_bytes;
     if (sweep_rg < 1) return cudaErrorInvalidConfiguration;
     if (sweep_rg > per_cta) sweep_rg = (int)per_cta;
-    const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes;
+    const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes + ssq_bytes;
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT>,
@@ -901,9 +957,14 @@ template <int FMT>
 static cudaError_t launch_fmt(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                               cudaStream_t s, const XForm &xf) {
     const bool two = ncols > 4 && (FMT == 8 || xf.act == 0);  // Q8_K: all 8 columns in one n-tile
-    switch (xf.kind) {
+    // RMSNorm input with exact activations: folded into the epilogue (W (x w)
+    // / rms(x), the sums of squares formed from the loads that build B), so
+    // no CTA reduces the whole input before its first MMA
+    const bool fold = xf.kind == 1 && (FMT == 8 || xf.act == 0) && T.nu <= kMaxFoldUnits;
+    switch (fold ? 3 : xf.kind) {
     case 0: return two ? launch_act<FMT, 2, 0>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch_act<FMT, 1, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
     case 1: return two ? launch_act<FMT, 2, 1>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch_act<FMT, 1, 1>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    case 3: return two ? launch<FMT, 2, 3, 0>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch<FMT, 1, 3, 0>(T, X, ncols, Y, accumulate, ldy, s, xf);
     case 2: return two ? launch_act<FMT, 2, 2>(T, X, ncols, Y, accumulate, ldy, s, xf) : launch_act<FMT, 1, 2>(T, X, ncols, Y, accumulate, ldy, s, xf);
     }
     return cudaErrorInvalidValue;

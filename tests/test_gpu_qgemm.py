@@ -76,6 +76,47 @@ def test_qgemm_parity(O, ctx, qt, M, K, act):
         ctx.set_activation(0)
 
 
+def _rmsnorm(X, w, eps):
+    """rmsnorm_cpu! (src/ModelCPU.jl:111-123) per column, in f32"""
+    ss = np.einsum("ij,ij->i", X.astype(np.float64), X.astype(np.float64)).astype(np.float32)
+    scale = (np.float32(1.0) / np.sqrt(ss / np.float32(X.shape[1]) + np.float32(eps))).astype(np.float32)
+    return (X * scale[:, None] * w[None, :]).astype(np.float32)
+
+
+NORM_CASES = [(12, 256, 256), (12, 1000, 1024), (13, 130, 4096), (14, 300, 2048), (8, 256, 1024),
+              (8, 200, 1152), (8, 64, 800)]
+
+
+@pytest.mark.parametrize("act", [0, 1])
+@pytest.mark.parametrize("qt,M,K", NORM_CASES)
+def test_qgemm_rmsnorm_parity(O, ctx, qt, M, K, act):
+    """ifr_qgemm_rmsnorm = RMSNorm then GEMV: exact activations fold the norm
+    into the epilogue (the oracle normalises first, so only f32 rounding
+    differs: TOL); Q8_K activations quantize the normalised input like the
+    reference (a rare rounding flip of one Q8_K value moves a column by
+    ~1e-4: Q8K_TOL).  Ragged K (Q8_0, K = 800, 1152) takes the scalar loads."""
+    torch = _torch()
+    rng = np.random.default_rng(M + K * 3 + qt + act)
+    q = O.quantize(qt, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    W = ctx.upload(qt, q, M, K)
+    X = rng.normal(0, 1, (13, K)).astype(np.float32)
+    X[3] *= 40.0  # columns of very different scale
+    w = (1.0 + rng.normal(0, 0.2, K)).astype(np.float32)
+    eps = 1e-6
+    ref = O.gemm_ref(qt, q, M, K, _rmsnorm(X, w, eps), act=act if qt != 8 else 0)
+    Xd = torch.from_numpy(X).cuda()
+    wd = torch.from_numpy(w).cuda()
+    tol = TOL if act == 0 or qt == 8 else 1e-3
+    ctx.set_activation(act)
+    try:
+        for n in (1, 5, 8, 13):
+            Y = ctx.qgemm_rmsnorm(W, Xd[:n].contiguous(), wd, eps).cpu().numpy()
+            err = O.norm_rel(Y, ref[:n])
+            assert err.max() < 5 * tol, (NAMES[qt], M, K, n, act, err)
+    finally:
+        ctx.set_activation(0)
+
+
 @pytest.mark.parametrize("qt", FORMATS)
 def test_qgemm_matches_reference_c_kernel(O, ctx, qt):
     """in the reference's activation mode (Q8_K) the GPU GEMV reproduces the
