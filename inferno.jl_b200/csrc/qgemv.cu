@@ -37,9 +37,12 @@ namespace ifr {
 
 __device__ int g_dev_error = 0;
 
-constexpr int kConsumers = 8;
+// consumer warps per CTA: 8 with exact activations (fp16 hi/lo B fragments
+// of ~200 registers per thread), 16 with Q8_K activations (<= 128 registers:
+// twice the warps to hide the dependent-instruction latency)
+template <int ACT>
+__host__ __device__ constexpr int consumers() { return ACT == 1 ? 16 : 8; }
 constexpr int kMaxFoldUnits = 512;  // folded RMSNorm: K up to 131072
-constexpr int kThreads = 32 * kConsumers;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 IFR_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -516,15 +519,33 @@ IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<NT> &F, float 
 // Lane (g, t) builds the B fragments of column g (the C fragment's lanes
 // (g', t) read columns 2t, 2t+1, whose scales and sub-block sums are fetched
 // by shuffles).
-struct BFragI8 {
-    uint32_t b[8][2];  // chunk c: int8 of k-slots 4t..4t+3 and 16+4t..16+4t+3, column g
-    int s8[2][8];      // sum of the 32 int8 of chunk c, columns 2t and 2t+1 (Q4_K/Q5_K mins)
-    float d8[2];       // Q8_K scales of columns 2t and 2t+1
-};
-
 IFR_DEV uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
     return (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
            ((uint32_t)(q3 & 0xff) << 24);
+}
+
+struct BFragI8 {
+    uint32_t b[8][2];  // chunk c: int8 of k-slots 4t..4t+3 and 16+4t..16+4t+3, column g
+    // B of the correction MMA (k16): the block sums of column g as 7-bit limbs,
+    // [0] = sum & 127, [1] = sum >> 7 (k-slots 4t..4t+3); Q4_K/Q5_K: the 8
+    // chunk sums (mins term, lanes t < 2), Q6_K: the 16 group sums (the -32 offset)
+    uint32_t bc[2];
+    float d8[2];       // Q8_K scales of columns 2t and 2t+1
+};
+
+// byte k of w, zero- or sign-extended (one PRMT)
+IFR_DEV int ubyte(uint32_t w, int k) { return (int)__byte_perm(w, 0u, 0x4440u | (uint32_t)k); }
+IFR_DEV int sbyte(uint32_t w, int k) {
+    // selector nibbles: byte k, then three copies of its sign (msb of the nibble set)
+    const uint32_t x = 8u | (uint32_t)k, sel = (uint32_t)k | (x << 4) | (x << 8) | (x << 12);
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(w), "r"(0u), "r"(sel));
+    return (int)r;
+}
+// 4 sums as 7-bit limbs: lo bytes (v & 127) and hi bytes (v >> 7), v in [-2^14, 2^14)
+IFR_DEV void limbs4(int v0, int v1, int v2, int v3, uint32_t &lo, uint32_t &hi) {
+    lo = pack4_s8(v0 & 127, v1 & 127, v2 & 127, v3 & 127);
+    hi = pack4_s8(v0 >> 7, v1 >> 7, v2 >> 7, v3 >> 7);
 }
 
 template <int FMT, int XF>
@@ -543,7 +564,7 @@ IFR_DEV void build_b_i8(const GemvArgs &a, const float *inv, int64_t u, int lane
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-    int csum[8];
+    int hsum[16];  // this lane's 4 elements of each 16-element group 2c + h
 #pragma unroll
     for (int c = 0; c < 8; c++) {
         int q[8];
@@ -551,23 +572,42 @@ IFR_DEV void build_b_i8(const GemvArgs &a, const float *inv, int64_t u, int lane
         for (int j = 0; j < 8; j++) q[j] = (int)roundf(__fmul_rn(v[8 * c + j], id));
         F.b[c][0] = pack4_s8(q[0], q[1], q[2], q[3]);
         F.b[c][1] = pack4_s8(q[4], q[5], q[6], q[7]);
-        csum[c] = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+        hsum[2 * c] = q[0] + q[1] + q[2] + q[3];
+        hsum[2 * c + 1] = q[4] + q[5] + q[6] + q[7];
     }
     F.d8[0] = __shfl_sync(0xffffffffu, d, 8 * t);
     F.d8[1] = __shfl_sync(0xffffffffu, d, 8 * t + 4);
+    F.bc[0] = F.bc[1] = 0u;
     if (FMT == 12 || FMT == 13) {
+        // chunk sums of column g (over the quad); lane t < 2 holds chunks 4t .. 4t + 3
+        int cs[8];
 #pragma unroll
         for (int c = 0; c < 8; c++) {
-            int sc = csum[c];
-            sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-            sc += __shfl_xor_sync(0xffffffffu, sc, 2);
-            F.s8[0][c] = __shfl_sync(0xffffffffu, sc, 8 * t);
-            F.s8[1][c] = __shfl_sync(0xffffffffu, sc, 8 * t + 4);
+            int v2 = hsum[2 * c] + hsum[2 * c + 1];
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 1);
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
+            cs[c] = v2;
         }
+        if (t < 2) {
+            const bool hi = t == 1;
+            limbs4(hi ? cs[4] : cs[0], hi ? cs[5] : cs[1], hi ? cs[6] : cs[2], hi ? cs[7] : cs[3], F.bc[0], F.bc[1]);
+        }
+    } else if (FMT == 14) {
+        // group sums of column g (over the quad); lane t holds groups 4t .. 4t + 3
+        int gs[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            int v2 = hsum[j];
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 1);
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
+            gs[j] = v2;
+        }
+        int w4[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) w4[i] = t == 0 ? gs[i] : t == 1 ? gs[4 + i] : t == 2 ? gs[8 + i] : gs[12 + i];
+        limbs4(w4[0], w4[1], w4[2], w4[3], F.bc[0], F.bc[1]);
     }
 }
-
-IFR_DEV int byte_of(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
 
 // Q4_K / Q5_K x Q8_K (vec_dot_q4_K_q8_K / q5_K, quant_kernels.c:204-435): per
 // unit and output, the exact integer sums S = sum_c sc_c (q . q8)_c and
@@ -583,7 +623,7 @@ IFR_DEV void mtile_qk_i8(const uint8_t *tile, int lane, const BFragI8 &F, float 
     uint32_t sc[2][2], mn[2][2];
     qk_scales(h0, sc[0], mn[0]);
     qk_scales(h1, sc[1], mn[1]);
-    int S[4] = {0, 0, 0, 0}, M[4] = {0, 0, 0, 0};
+    int S[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 8; c++) {
         const int p = c >> 1, sh = 4 * (c & 1), wi = 2 * (p & 1);
@@ -598,17 +638,21 @@ IFR_DEV void mtile_qk_i8(const uint8_t *tile, int lane, const BFragI8 &F, float 
         }
         int cc[4];
         imma16832_z(cc, a0, a1, a2, a3, F.b[c][0], F.b[c][1]);
-        const int s0 = byte_of(sc[0][c >> 2], c & 3), s1 = byte_of(sc[1][c >> 2], c & 3);
-        const int m0 = byte_of(mn[0][c >> 2], c & 3), m1 = byte_of(mn[1][c >> 2], c & 3);
+        const int s0 = ubyte(sc[0][c >> 2], c & 3), s1 = ubyte(sc[1][c >> 2], c & 3);
         S[0] += s0 * cc[0];
         S[1] += s0 * cc[1];
         S[2] += s1 * cc[2];
         S[3] += s1 * cc[3];
-        M[0] += m0 * F.s8[0][c];
-        M[1] += m0 * F.s8[1][c];
-        M[2] += m1 * F.s8[0][c];
-        M[3] += m1 * F.s8[1][c];
     }
+    // mins M = sum_c m_c bsum_c on the integer tensor cores: A = the 6-bit mins
+    // (k-slot = chunk; lanes t < 2), B = the chunk sums' 7-bit limbs
+    const uint32_t ma0 = t == 0 ? mn[0][0] : (t == 1 ? mn[0][1] : 0u);
+    const uint32_t ma1 = t == 0 ? mn[1][0] : (t == 1 ? mn[1][1] : 0u);
+    int ml[4], mh[4], M[4];
+    imma16816_z(ml, ma0, ma1, F.bc[0]);
+    imma16816_z(mh, ma0, ma1, F.bc[1]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) M[i] = ml[i] + mh[i] * 128;
     const float d0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16));
     const float d1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16));
 #pragma unroll
@@ -635,26 +679,35 @@ IFR_DEV void mtile_q6_i8(const uint8_t *tile, int lane, const BFragI8 &F, float 
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const uint32_t w0 = u4w(n ? l01 : l00, 2 * (qq & 1) + h), w1 = u4w(n ? l11 : l10, 2 * (qq & 1) + h);
+            // unsigned 6-bit q (0..63); the -32 is applied once per unit below
             const uint32_t x0 = ((w0 >> (4 * (qq >> 1))) & 0x0f0f0f0fu) |
                                 (((u4w(hq0, 2 * n + h) >> (2 * qq)) & 0x03030303u) << 4);
             const uint32_t x1 = ((w1 >> (4 * (qq >> 1))) & 0x0f0f0f0fu) |
                                 (((u4w(hq1, 2 * n + h) >> (2 * qq)) & 0x03030303u) << 4);
-            // bytewise q - 32 without borrows between bytes
-            const uint32_t a0 = ((x0 | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
-            const uint32_t a1 = ((x1 | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
             int cc[4];
-            imma16816_z(cc, a0, a1, F.b[c][h]);
+            imma16816_z(cc, x0, x1, F.b[c][h]);
             const int j = 2 * c + h;
-            const int f0 = (int)(int8_t)byte_of(u4w(sc0, j >> 2), j & 3);
-            const int f1 = (int)(int8_t)byte_of(u4w(sc1, j >> 2), j & 3);
+            const int f0 = sbyte(u4w(sc0, j >> 2), j & 3);
+            const int f1 = sbyte(u4w(sc1, j >> 2), j & 3);
             S[0] += f0 * cc[0];
             S[1] += f0 * cc[1];
             S[2] += f1 * cc[2];
             S[3] += f1 * cc[3];
         }
     }
+    // sum_j sc_j ((q - 32) . q8)_j = sum_j sc_j (q . q8)_j - 32 sum_j sc_j bsum_j; the
+    // second sum on the integer tensor cores: A = the int8 group scales (k-slot =
+    // group), B = the group sums' 7-bit limbs
+    const uint32_t sa0 = t == 0 ? sc0.x : t == 1 ? sc0.y : t == 2 ? sc0.z : sc0.w;
+    const uint32_t sa1 = t == 0 ? sc1.x : t == 1 ? sc1.y : t == 2 ? sc1.z : sc1.w;
+    int cl[4], ch[4];
+    imma16816_z(cl, sa0, sa1, F.bc[0]);
+    imma16816_z(ch, sa0, sa1, F.bc[1]);
 #pragma unroll
-    for (int i = 0; i < 4; i++) tot[i] += (F.d8[i & 1] * (i < 2 ? d0 : d1)) * (float)S[i];
+    for (int i = 0; i < 4; i++) {
+        S[i] -= 32 * (cl[i] + ch[i] * 128);
+        tot[i] += (F.d8[i & 1] * (i < 2 ? d0 : d1)) * (float)S[i];
+    }
 }
 
 // Work order of one CTA: its contiguous range of row groups, cut into sweeps;
@@ -680,10 +733,10 @@ struct Order {
 };
 
 // Issue the bulk copies of stage q into its ring slot (one thread).
-template <int MTB, int MPW>
+template <int MTB, int MPW, int CW>
 IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring, uint64_t *full) {
-    constexpr int STAGE = 8 * MPW * MTB;
-    const int UW = a.UW, MTG = 8 * MPW / UW;
+    constexpr int STAGE = CW * MPW * MTB;
+    const int UW = a.UW, MTG = CW * MPW / UW;
     int p, rg;
     o.at(q, p, rg);
     const int s = q % a.S;
@@ -702,16 +755,19 @@ IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring
 // ACT: K-quant activations, 0 exact f32 (fp16 tensor cores), 1 Q8_K (integer
 // tensor cores, the reference's kernels); Q8_0 is always exact
 template <int FMT, int NT, int XF, int MPW, int ACT>
-__global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArgs a) {
+    constexpr int CW = consumers<ACT>(), NTH = 32 * CW;
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int MTB = mtile_bytes(FMT);
-    constexpr int STAGE = 8 * MPW * MTB;  // MTG * UW M-tiles
+    constexpr int STAGE = CW * MPW * MTB;  // MTG * UW M-tiles
     constexpr int NRED = MPW * NT * 4;    // floats per lane per warp in the reduction
-    const int UW = a.UW, MTG = 8 * MPW / UW;
+    const int UW = a.UW, MTG = CW * MPW / UW;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
     float *red = reinterpret_cast<float *>(ring + (size_t)a.S * STAGE);
-    float *acc = red + kConsumers * NRED * 32;  // [sweep_rg * MTG * 16 rows][8 cols]
+    // red: two buffers of per-warp partials, so consecutive stages alternate and
+    // one barrier per stage suffices
+    float *acc = red + 2 * CW * NRED * 32;  // [sweep_rg * MTG * 16 rows][8 cols]
     float *ssq = acc + a.sweep_rg * MTG * 16 * 8;  // XF 3: [nu][8] sums of x^2 per unit and column
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nrg = (a.nrb + MTG - 1) / MTG;
@@ -728,18 +784,18 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     if (tid == 0) {
         for (int s = 0; s < a.S; s++) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB, MPW>(a, o, q, ring, full);
+        for (int q = 0; q < min(a.S, total); q++) issue_stage<MTB, MPW, CW>(a, o, q, ring, full);
     }
     pdl_wait();
     // RMSNorm of the input columns: 1 / sqrt(sum x^2 / K + eps) per column
     // (rmsnorm_cpu!, ModelCPU.jl:111-123), applied while building B
     __shared__ float inv_s[8];
-    __shared__ float part_s[kConsumers][8];
+    __shared__ float part_s[CW][8];
     if (XF == 1) {
         float ss[8];
 #pragma unroll
         for (int c = 0; c < 8; c++) ss[c] = 0.f;
-        for (int64_t k = 4 * tid; k < a.K; k += 4 * kThreads) {
+        for (int64_t k = 4 * tid; k < a.K; k += 4 * NTH) {
 #pragma unroll
             for (int c = 0; c < 8; c++) {
                 if (c < a.ncols) {
@@ -758,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
         __syncthreads();
         if (tid < 8) {
             float v = 0.f;
-            for (int w = 0; w < kConsumers; w++) v += part_s[w][tid];
+            for (int w = 0; w < CW; w++) v += part_s[w][tid];
             inv_s[tid] = 1.0f / sqrtf(v / (float)a.K + a.eps);
         }
     }
@@ -772,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
     for (int sw = o.rg_lo; sw < o.rg_hi; sw += o.sweep_rg) {
         const int sw_hi = min(o.rg_hi, sw + o.sweep_rg);
         const int sw_rows = (sw_hi - sw) * MTG * 16;
-        for (int i = tid; i < sw_rows * 8; i += kThreads) acc[i] = 0.f;
+        for (int i = tid; i < sw_rows * 8; i += NTH) acc[i] = 0.f;
         for (int p = 0; p < o.passes; p++) {
             const int64_t u = (int64_t)p * UW + ui;
             const bool active = u < a.nu;
@@ -782,6 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
             }
             for (int rg = sw; rg < sw_hi; rg++, it++) {
                 const int s = it % a.S;
+                float *redb = red + (it & 1) * (CW * NRED * 32);
                 if (!dead && !mbar_wait(full + s, (uint32_t)(it / a.S) & 1)) dead = true;
                 float tot[MPW][NT][4];
 #pragma unroll
@@ -811,12 +868,12 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
                     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                         for (int i = 0; i < 4; i++)
-                            red[((warp * MPW + mm) * NT * 4 + nt * 4 + i) * 32 + lane] = tot[mm][nt][i];
-                consumer_bar();  // slot s fully read; partials visible
-                if (tid == 0 && !dead && it + a.S < total) issue_stage<MTB, MPW>(a, o, it + a.S, ring, full);
+                            redb[((warp * MPW + mm) * NT * 4 + nt * 4 + i) * 32 + lane] = tot[mm][nt][i];
+                consumer_bar();  // slot s fully read; partials visible; the other buffer's reads done
+                if (tid == 0 && !dead && it + a.S < total) issue_stage<MTB, MPW, CW>(a, o, it + a.S, ring, full);
                 // each thread owns outputs (m, row, col) = o, o + 256, ... in every pass
                 const int base = (rg - sw) * MTG * 16;
-                for (int oi = tid; oi < MTG * 128; oi += kThreads) {
+                for (int oi = tid; oi < MTG * 128; oi += NTH) {
                     const int col = oi & 7, r16 = (oi >> 3) & 15, m = oi >> 7;
                     const int mmp = m / MPW, mm = m % MPW, half = r16 >> 3;
                     float v = 0.f;
@@ -826,20 +883,20 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
                         if (nt >= NT) continue;
                         const int ln = 4 * (r16 & 7) + (col & 3);
                         for (int q = 0; q < UW; q++) {
-                            const float *pp = red + (((mmp * UW + q) * MPW + mm) * NT * 4 + nt * 4 + 2 * half) * 32 + ln;
+                            const float *pp = redb + (((mmp * UW + q) * MPW + mm) * NT * 4 + nt * 4 + 2 * half) * 32 + ln;
                             v += pp[0] + pp[32];
                         }
                     } else {
                         // C columns 2t, 2t+1 are activation columns 2t, 2t+1
                         const int ln = 4 * (r16 & 7) + (col >> 1);
                         for (int q = 0; q < UW; q++)
-                            v += red[(((mmp * UW + q) * MPW + mm) * NT * 4 + 2 * half + (col & 1)) * 32 + ln];
+                            v += redb[(((mmp * UW + q) * MPW + mm) * NT * 4 + 2 * half + (col & 1)) * 32 + ln];
                     }
                     acc[(base + m * 16 + r16) * 8 + col] += v;
                 }
-                consumer_bar();  // red reused by the next stage
             }
         }
+        consumer_bar();  // every stage's sums are in acc
         // the sweep's rows are final: write Y (coalesced over rows)
         const int64_t row0 = (int64_t)sw * MTG * 16;
         // XF 3: W (x w) / rms(x) per column; the sums of squares in unit order
@@ -861,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
             // gate/up block pairs (MTG is even), local rows 32p.. gate, 32p+16.. up
             const int half_rows = sw_rows / 2;
             const int64_t j0 = row0 / 2;
-            for (int i = tid; i < half_rows * a.ncols; i += kThreads) {
+            for (int i = tid; i < half_rows * a.ncols; i += NTH) {
                 const int col = i / half_rows, rr = i % half_rows;
                 const int gr = (rr >> 4) * 32 + (rr & 15);
                 if (j0 + rr < a.M / 2 && !dead) {
@@ -870,7 +927,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_kernel(GemvArgs a) {
                 }
             }
         } else {
-            for (int i = tid; i < sw_rows * a.ncols; i += kThreads) {
+            for (int i = tid; i < sw_rows * a.ncols; i += NTH) {
                 const int col = i / sw_rows, r = i % sw_rows;
                 if (row0 + r < a.M && !dead) {
                     float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
@@ -900,10 +957,11 @@ template <int FMT, int NT, int XF, int MPW, int ACT>
 static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                               cudaStream_t s, const XForm &xf, int UW) {
     constexpr int MTB = mtile_bytes(FMT);
-    constexpr int STAGE = 8 * MPW * MTB;
+    constexpr int CW = consumers<ACT>();
+    constexpr int STAGE = CW * MPW * MTB;
     constexpr int kSmemMax = 226 * 1024;  // dynamic; 1 KB of the 227 KB per block stays for static shared memory
-    const int MTG = 8 * MPW / UW;
-    const int red = kConsumers * (MPW * NT * 4) * 32 * 4;
+    const int MTG = CW * MPW / UW;
+    const int red = 2 * CW * (MPW * NT * 4) * 32 * 4;
     const int64_t nrg = (T.nrb + MTG - 1) / MTG;
     const int grid = (int)(nrg < num_sms() ? nrg : num_sms());
     // ring stages first (2..5), then the shared accumulator gets the rest
@@ -931,7 +989,7 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
                sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
-    return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(kThreads), (size_t)smem, s, a);
+    return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a);
 }
 
 // Work split: UW warps share each row block's units, two M-tiles per warp and
@@ -942,7 +1000,10 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
                           cudaStream_t s, const XForm &xf) {
     int UW = 1;
     while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
-    return launch_mpw<FMT, NT, XF, 2, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
+    // a stage: 8 warps x 2 M-tiles (exact activations), 16 warps x 2 (Q8_K
+    // activations; x 1 for Q6_K, whose larger tiles would leave one ring stage)
+    constexpr int MPW = ACT == 1 && mtile_bytes(FMT) > 2816 ? 1 : 2;
+    return launch_mpw<FMT, NT, XF, MPW, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
 }
 
 template <int FMT, int NT, int XF>
