@@ -372,6 +372,7 @@ def run_reference_sweep(args):
 # ------------------------------------------------------- spec workload ----
 
 SPEC_PRESET, SPEC_SEED, SPEC_PROMPT = "tiny", 0, 128
+SPEC_GEN = 128  # config 1: 128 greedy tokens per request
 
 
 def spec_bytes_per_step(info, gamma):
@@ -456,22 +457,29 @@ def run_spec(args):
     nl0 = _launches(st)
     st.spec_step(G)
     launches_per_step = _launches(st) - nl0
-    # end to end: one request through the public API with host buffers:
-    # prompt H2D + prefill, then per step ifr_spec_step + D2H of the emitted tokens
-    st2 = State(model, max_ctx)
+    # end to end: one config-1 request through the public C ABI with host
+    # buffers: the 128-token prompt H2D + ifr_prefill, then spec steps
+    # (ifr_spec_graph_launch of the state's captured step) each followed by
+    # ifr_state_read (sync + D2H of the emitted tokens and the scalars) until
+    # SPEC_GEN tokens have been emitted.  The state and its graph are set up
+    # before the timed region (capture runs no kernel).
+    st2 = State(model, SPEC_PROMPT + (SPEC_GEN + 2) * (G + 1) + 16)
+    st2.capture(G, 1)
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx.sync()
+    barrier(ws)
     ee0.record(stream)
     st2.prefill(prompt)
-    d2h = 0
-    for _ in range(args.steps):
-        st2.spec_step(G)
+    d2h, e2e_steps, t2 = 0, 0, st2.read()[0]
+    while len(t2) < SPEC_GEN:
+        st2.launch()
         t2 = st2.read()[0]
-        d2h += t2.nbytes
+        d2h += t2.nbytes + 16
+        e2e_steps += 1
     ee1.record(stream)
     ee1.synchronize()
     e2e_ms = max_over_ranks(ee0.elapsed_time(ee1), ws)
-    e2e_tokens = len(st2.read()[0])
+    e2e_tokens = len(t2)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = spec_cpu_baseline(path, prompt, G, steps=3)
@@ -506,9 +514,13 @@ def run_spec(args):
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "algorithmic_bytes_per_launch": int(v_bytes), "launch_ms": round(v_ms, 4)},
-            "e2e": {"value": round(e2e_tokens / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(prompt.nbytes / args.steps), "d2h_bytes_per_step": int(d2h / args.steps),
-                    "note": "one request: H2D prompt + prefill + steps x (ifr_spec_step + D2H of the emitted tokens)"},
+            "e2e": {"value": round(e2e_tokens * ws / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(prompt.nbytes / max(1, e2e_steps)),
+                    "d2h_bytes_per_step": int(d2h / max(1, e2e_steps)),
+                    "tokens": e2e_tokens, "steps": e2e_steps, "ms": round(e2e_ms, 3),
+                    "note": "one config-1 request per rank, end to end through the C ABI: H2D of the 128-token prompt + "
+                            "ifr_prefill, then ifr_spec_graph_launch + ifr_state_read (sync, D2H of the emitted tokens) "
+                            "per step until 128 tokens are emitted; graph captured before the timed region"},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
