@@ -37,11 +37,11 @@ namespace ifr {
 
 __device__ int g_dev_error = 0;
 
-// consumer warps per CTA: 8 with exact activations (fp16 hi/lo B fragments
-// of ~200 registers per thread), 16 with Q8_K activations (<= 128 registers:
-// twice the warps to hide the dependent-instruction latency)
+// consumer warps per CTA: 16 in both modes (<= 128 registers per thread).  With
+// exact activations the B fragments live in shared memory (built once per pass
+// by the warps of each unit), so a thread holds only one M-tile's operands.
 template <int ACT>
-__host__ __device__ constexpr int consumers() { return ACT == 1 ? 16 : 8; }
+__host__ __device__ constexpr int consumers() { return 16; }
 constexpr int kMaxFoldUnits = 512;  // folded RMSNorm: K up to 131072
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -128,11 +128,22 @@ struct GemvArgs {
 // the steps each, split them into (hi, lo) and swap halves by one shuffle per
 // register.  Activations are scaled by a power of two per unit (exact) so that
 // hi + lo carries ~22 bits; es undoes it on the f32 sums.
+// One unit's fragments in shared memory, 32-bit words:
+//   b  [step 16][n-tile NT][lane 32] x 2  slots (0,1), (2,3) of each step
+//   m  [n-tile][lane]  Q4_K/Q5_K min MMA: sums of sub-blocks 2t, 2t+1 (x 2^-5)
+//   es [n-tile][lane]  2^-e of the unit for C column 4*nt + t
+__host__ __device__ constexpr int bunit_words(int NT) { return 16 * NT * 32 * 2 + 2 * NT * 32; }
 template <int NT>
-struct BFrag {
-    uint32_t b[16][NT][2];  // per step: slots (0,1), (2,3)
-    uint32_t m[NT];         // Q4_K/Q5_K min MMA: sums of sub-blocks 2t, 2t+1 (x 2^-5)
-    float es[NT];           // 2^-e of the unit for C column 4*nt + t
+struct BView {
+    const uint2 *b;     // this lane's entries: b[(s * NT + nt) * 32]
+    const uint32_t *m;  // m[nt * 32]
+    const float *es;    // es[nt * 32]
+    IFR_DEV void at(const uint32_t *unit, int lane) {
+        b = reinterpret_cast<const uint2 *>(unit) + lane;
+        m = unit + 16 * NT * 32 * 2 + lane;
+        es = reinterpret_cast<const float *>(unit + 16 * NT * 32 * 2 + NT * 32) + lane;
+    }
+    IFR_DEV uint2 ld(int s, int nt) const { return b[(s * NT + nt) * 32]; }
 };
 
 IFR_DEV uint32_t cvt_h2(float hi_half, float lo_half) {
@@ -206,99 +217,98 @@ IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, 
     xform_runs<XF>(xr, wr, XF == 1 && has ? inv[col] : 0.f, v, ss);
 }
 
+// Builds n-tile nt of unit u's fragments into `unit` (bunit_words(NT) words).
 // ssq (XF 3, may be null): [unit][8] sums of x^2 of the unit's activations
 template <int FMT, int NT, int XF>
-IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, BFrag<NT> &F, float *ssq) {
+IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, int nt, uint32_t *unit, float *ssq) {
     const int g = lane >> 2, t = lane & 3, part = g & 1;
-    // this lane's steps 8 part .. 8 part + 7 (elem_s() of tiles.cuh): the same
-    // positions in every column; every column's loads (and the norm weights)
-    // in flight before the first is used (SwiGLU inputs: per column)
+    // this lane's steps 8 part .. 8 part + 7 (elem_s() of tiles.cuh): every load
+    // (and the norm weights) in flight before the first is used
     const int64_t k0 = u * 256 + 128 * part + 4 * t;
-    float4 xr[NT][8], wr[8];
-    if (XF != 2) {
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            const int col = 4 * nt + (g >> 1);
-            ld_runs(a.X + (int64_t)col * a.ldx, a.K, k0, 16, col < a.ncols, xr[nt]);
-        }
+    const int col = 4 * nt + (g >> 1);
+    float v[32];
+    float ss = 0.f;
+    if (XF == 2) {
+        load_x32<XF>(a, inv, col, k0, 16, col < a.ncols, v, &ss);
+    } else {
+        float4 xr[8], wr[8];
+        ld_runs(a.X + (int64_t)col * a.ldx, a.K, k0, 16, col < a.ncols, xr);
         if (XF == 1 || XF == 3) ld_runs(a.xw, a.K, k0, 16, true, wr);
+        xform_runs<XF>(xr, wr, XF == 1 && col < a.ncols ? inv[col] : 0.f, v, &ss);
+    }
+    if (XF == 3) {
+        // the unit's 256 elements of column col are spread over lanes 8c .. 8c + 7
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+        if (ssq && (lane & 7) == 0) ssq[u * 8 + col] = ss;
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; r++) mx = fmaxf(mx, fabsf(v[r]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    const int ex = unit_exp(mx);
+    const float scl = pow2i(ex);
+    uint2 *ub = reinterpret_cast<uint2 *>(unit) + lane;
+    reinterpret_cast<float *>(unit + 16 * NT * 32 * 2 + NT * 32)[nt * 32 + lane] =
+        __shfl_sync(0xffffffffu, pow2i(-ex), 8 * t);
+    uint32_t keep[8][2], send[8][2];
+    float cs[4] = {0.f, 0.f, 0.f, 0.f};  // this lane's part of chunks 4 part .. 4 part + 3
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float x[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            x[j] = v[4 * i + j] * scl;  // exact
+            cs[i >> 1] += x[j];
+        }
+        const uint32_t h02 = cvt_h2(x[2], x[0]), h13 = cvt_h2(x[3], x[1]);
+        const uint32_t l02 = cvt_h2(x[2] - h2_hi(h02), x[0] - h2_lo(h02));
+        const uint32_t l13 = cvt_h2(x[3] - h2_hi(h13), x[1] - h2_lo(h13));
+        keep[i][0] = part ? l02 : h02;
+        keep[i][1] = part ? l13 : h13;
+        send[i][0] = part ? h02 : l02;
+        send[i][1] = part ? h13 : l13;
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-        const int col = 4 * nt + (g >> 1);
-        float v[32];
-        float ss = 0.f;
-        if (XF == 2) load_x32<XF>(a, inv, col, k0, 16, col < a.ncols, v, &ss);
-        else xform_runs<XF>(xr[nt], wr, XF == 1 && col < a.ncols ? inv[col] : 0.f, v, &ss);
-        if (XF == 3) {
-            // the unit's 256 elements of column col are spread over lanes 8c .. 8c + 7
-            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-            ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-            if (ssq && (lane & 7) == 0) ssq[u * 8 + col] = ss;
+    for (int i = 0; i < 8; i++) {
+        uint32_t lo[2], hi[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t r = __shfl_xor_sync(0xffffffffu, send[i][h], 4);
+            lo[h] = part ? r : keep[i][h];
+            hi[h] = part ? keep[i][h] : r;
         }
-        float mx = 0.f;
+        ub[(i * NT + nt) * 32] = make_uint2(lo[0], lo[1]);
+        ub[((8 + i) * NT + nt) * 32] = make_uint2(hi[0], hi[1]);
+    }
+    if (FMT == 12 || FMT == 13) {
+        // sub-block (= chunk) sums of column col: over the lane quad, then the partner
+        // lane's four chunks; lane (g, t) takes chunks 2t, 2t+1, its hi or lo part
+        float S[8];
 #pragma unroll
-        for (int r = 0; r < 32; r++) mx = fmaxf(mx, fabsf(v[r]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        const int ex = unit_exp(mx);
-        const float scl = pow2i(ex);
-        F.es[nt] = __shfl_sync(0xffffffffu, pow2i(-ex), 8 * t);
-        uint32_t keep[8][2], send[8][2];
-        float cs[4] = {0.f, 0.f, 0.f, 0.f};  // this lane's part of chunks 4 part .. 4 part + 3
+        for (int k = 0; k < 4; k++) {
+            float v2 = cs[k];
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 1);
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
+            const float o = __shfl_xor_sync(0xffffffffu, v2, 4);
+            S[k] = part ? o : v2;
+            S[4 + k] = part ? v2 : o;
+        }
+        float sa = S[0], sb = S[1];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float x[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                x[j] = v[4 * i + j] * scl;  // exact
-                cs[i >> 1] += x[j];
+        for (int k = 1; k < 4; k++)
+            if (t == k) {
+                sa = S[2 * k];
+                sb = S[2 * k + 1];
             }
-            const uint32_t h02 = cvt_h2(x[2], x[0]), h13 = cvt_h2(x[3], x[1]);
-            const uint32_t l02 = cvt_h2(x[2] - h2_hi(h02), x[0] - h2_lo(h02));
-            const uint32_t l13 = cvt_h2(x[3] - h2_hi(h13), x[1] - h2_lo(h13));
-            keep[i][0] = part ? l02 : h02;
-            keep[i][1] = part ? l13 : h13;
-            send[i][0] = part ? h02 : l02;
-            send[i][1] = part ? h13 : l13;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const uint32_t r = __shfl_xor_sync(0xffffffffu, send[i][h], 4);
-                F.b[i][nt][h] = part ? r : keep[i][h];
-                F.b[8 + i][nt][h] = part ? keep[i][h] : r;
-            }
-        }
-        if (FMT == 12 || FMT == 13) {
-            // sub-block (= chunk) sums of column col: over the lane quad, then the partner
-            // lane's four chunks; lane (g, t) takes chunks 2t, 2t+1, its hi or lo part
-            float S[8];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                float v2 = cs[k];
-                v2 += __shfl_xor_sync(0xffffffffu, v2, 1);
-                v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
-                const float o = __shfl_xor_sync(0xffffffffu, v2, 4);
-                S[k] = part ? o : v2;
-                S[4 + k] = part ? v2 : o;
-            }
-            float sa = S[0], sb = S[1];
-#pragma unroll
-            for (int k = 1; k < 4; k++)
-                if (t == k) {
-                    sa = S[2 * k];
-                    sb = S[2 * k + 1];
-                }
-            sa *= 0.03125f;  // x 2^-5 keeps the sums in fp16 range
-            sb *= 0.03125f;
-            const uint32_t hs = cvt_h2(sb, sa);
-            const uint32_t ls = cvt_h2(sb - h2_hi(hs), sa - h2_lo(hs));
-            F.m[nt] = part ? ls : hs;
-        }
+        sa *= 0.03125f;  // x 2^-5 keeps the sums in fp16 range
+        sb *= 0.03125f;
+        const uint32_t hs = cvt_h2(sb, sa);
+        const uint32_t ls = cvt_h2(sb - h2_hi(hs), sa - h2_lo(hs));
+        unit[16 * NT * 32 * 2 + nt * 32 + lane] = part ? ls : hs;
     }
 }
 
@@ -329,7 +339,7 @@ IFR_DEV void qk_scales(const uint4 &h, uint32_t (&sc)[2], uint32_t (&mn)[2]) {
 // 2048), low-nibble chunks as fma(1024+q, sc, -1024 sc), high-nibble chunks as
 // fma(1024+16q, sc/16, -64 sc); one qs word serves the steps of chunks 2p, 2p+1
 template <bool Q5, int NT>
-IFR_DEV void mtile_qk_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_qk_h(const uint8_t *tile, int lane, const BView<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const uint4 h0 = lds128(tile + qk_hdr(g)), h1 = lds128(tile + qk_hdr(g + 8));
     const uint4 q00 = lds128(tile + qk_qs(Q5, 0, g, t)), q01 = lds128(tile + qk_qs(Q5, 1, g, t));
@@ -383,8 +393,9 @@ IFR_DEV void mtile_qk_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float
             const int sl = 2 * cl + h, shs = 2 * chh + h;
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                mma16816(c[0][nt], a0, a1, a2, a3, F.b[sl][nt][0], F.b[sl][nt][1]);
-                mma16816(c[1][nt], b0, b1, b2, b3, F.b[shs][nt][0], F.b[shs][nt][1]);
+                const uint2 bl = F.ld(sl, nt), bh = F.ld(shs, nt);
+                mma16816(c[0][nt], a0, a1, a2, a3, bl.x, bl.y);
+                mma16816(c[1][nt], b0, b1, b2, b3, bh.x, bh.y);
             }
         }
     }
@@ -392,11 +403,12 @@ IFR_DEV void mtile_qk_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float
     const float d1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16)) * 32.0f;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        mma1688(cm[nt], mA0, mA1, F.m[nt]);
+        mma1688(cm[nt], mA0, mA1, F.m[nt * 32]);
+        const float es = F.es[nt * 32];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const float d = i < 2 ? d0 : d1, dm = i < 2 ? dm0 : dm1;
-            tot[nt][i] = fmaf(F.es[nt], d * (c[0][nt][i] + c[1][nt][i]) - dm * cm[nt][i], tot[nt][i]);
+            tot[nt][i] = fmaf(es, d * (c[0][nt][i] + c[1][nt][i]) - dm * cm[nt][i], tot[nt][i]);
         }
     }
 }
@@ -405,7 +417,7 @@ IFR_DEV void mtile_qk_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float
 // (1024 + q) - 1056 (low nibbles) or (1024 + 16 q) / 16 - 96 (high nibbles); the
 // int8 group scale multiplies each step's f32 MMA result
 template <int NT>
-IFR_DEV void mtile_q6_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_q6_h(const uint8_t *tile, int lane, const BView<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const float d0 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g)));
     const float d1 = h2f(*reinterpret_cast<const uint16_t *>(tile + q6_d(g + 8)));
@@ -445,7 +457,8 @@ IFR_DEV void mtile_q6_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 float cc[4];
-                mma16816_z(cc, a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+                const uint2 bb = F.ld(s, nt);
+                mma16816_z(cc, a0, a1, a2, a3, bb.x, bb.y);
                 acc[nt][0] = fmaf(f0, cc[0], acc[nt][0]);
                 acc[nt][1] = fmaf(f0, cc[1], acc[nt][1]);
                 acc[nt][2] = fmaf(f1, cc[2], acc[nt][2]);
@@ -455,17 +468,18 @@ IFR_DEV void mtile_q6_h(const uint8_t *tile, int lane, const BFrag<NT> &F, float
     }
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        tot[nt][0] = fmaf(F.es[nt] * d0, acc[nt][0], tot[nt][0]);
-        tot[nt][1] = fmaf(F.es[nt] * d0, acc[nt][1], tot[nt][1]);
-        tot[nt][2] = fmaf(F.es[nt] * d1, acc[nt][2], tot[nt][2]);
-        tot[nt][3] = fmaf(F.es[nt] * d1, acc[nt][3], tot[nt][3]);
+        const float es = F.es[nt * 32];
+        tot[nt][0] = fmaf(es * d0, acc[nt][0], tot[nt][0]);
+        tot[nt][1] = fmaf(es * d0, acc[nt][1], tot[nt][1]);
+        tot[nt][2] = fmaf(es * d1, acc[nt][2], tot[nt][2]);
+        tot[nt][3] = fmaf(es * d1, acc[nt][3], tot[nt][3]);
     }
 }
 
 // Q8_0: steps 2b, 2b+1 = block b; int8 -> fp16 as ((x ^ 0x80) | 0x6400) - 1152,
 // the block scale multiplies the f32 MMA result of its two steps
 template <int NT>
-IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<NT> &F, float (&tot)[NT][4]) {
+IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BView<NT> &F, float (&tot)[NT][4]) {
     const int g = lane >> 2, t = lane & 3;
     const uint4 dd0 = lds128(tile + q8_d(g)), dd1 = lds128(tile + q8_d(g + 8));
     constexpr uint32_t k1152 = 0x64806480u;
@@ -491,8 +505,9 @@ IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<NT> &F, float 
                 const uint32_t a3 = hsub2_u(lop_and_or(W1 >> 8, 0x00FF00FFu, kMagic), k1152);
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
-                    if (h == 0) mma16816_z(c[nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
-                    else mma16816(c[nt], a0, a1, a2, a3, F.b[s][nt][0], F.b[s][nt][1]);
+                    const uint2 bb = F.ld(s, nt);
+                    if (h == 0) mma16816_z(c[nt], a0, a1, a2, a3, bb.x, bb.y);
+                    else mma16816(c[nt], a0, a1, a2, a3, bb.x, bb.y);
                 }
             }
             const float db0 = h2f((uint16_t)(u4w(dd0, blk >> 1) >> (16 * (blk & 1))));
@@ -509,7 +524,7 @@ IFR_DEV void mtile_q80(const uint8_t *tile, int lane, const BFrag<NT> &F, float 
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) tot[nt][i] = fmaf(F.es[nt], acc[nt][i], tot[nt][i]);
+        for (int i = 0; i < 4; i++) tot[nt][i] = fmaf(F.es[nt * 32], acc[nt][i], tot[nt][i]);
 }
 
 // ---- K-quants with Q8_K activations on the integer tensor cores ---------------
@@ -769,6 +784,8 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
     // one barrier per stage suffices
     float *acc = red + 2 * CW * NRED * 32;  // [sweep_rg * MTG * 16 rows][8 cols]
     float *ssq = acc + a.sweep_rg * MTG * 16 * 8;  // XF 3: [nu][8] sums of x^2 per unit and column
+    // exact activations: the B fragments of the pass's UW units
+    uint32_t *bsm = reinterpret_cast<uint32_t *>(ssq + (XF == 3 ? a.nu * 8 : 0));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nrg = (a.nrb + MTG - 1) / MTG;
     Order o;
@@ -822,7 +839,7 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
 
     const int ui = warp % UW, mp = warp / UW;
     constexpr bool kI8 = FMT != 8 && ACT == 1;
-    std::conditional_t<kI8, BFragI8, BFrag<NT>> F;
+    std::conditional_t<kI8, BFragI8, BView<NT>> F;
     int it = 0;
     bool dead = false;
     for (int sw = o.rg_lo; sw < o.rg_hi; sw += o.sweep_rg) {
@@ -832,9 +849,15 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
         for (int p = 0; p < o.passes; p++) {
             const int64_t u = (int64_t)p * UW + ui;
             const bool active = u < a.nu;
-            if (active) {
-                if constexpr (kI8) build_b_i8<FMT, XF>(a, inv_s, u, lane, F);
-                else build_b<FMT, NT, XF>(a, inv_s, u, lane, F, sw == o.rg_lo ? ssq : nullptr);
+            if constexpr (kI8) {
+                if (active) build_b_i8<FMT, XF>(a, inv_s, u, lane, F);
+            } else {
+                // the unit's warps split its n-tiles; the previous pass's fragments
+                // were last read before the barrier that closed its final stage
+                uint32_t *unit = bsm + ui * bunit_words(NT);
+                if (active && mp < NT) build_b<FMT, NT, XF>(a, inv_s, u, lane, mp, unit, sw == o.rg_lo ? ssq : nullptr);
+                consumer_bar();
+                F.at(unit, lane);
             }
             for (int rg = sw; rg < sw_hi; rg++, it++) {
                 const int s = it % a.S;
@@ -967,16 +990,19 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     // ring stages first (2..5), then the shared accumulator gets the rest
     const int64_t per_cta = (nrg + grid - 1) / grid;
     const int64_t stages_per_cta = per_cta * ((T.nu + UW - 1) / UW);
-    int S = (kSmemMax - 128 - red - 16 * 1024) / STAGE;
+    constexpr bool kExact = FMT == 8 || ACT == 0;
+    const int bsm_bytes = kExact ? UW * bunit_words(NT) * 4 : 0;
+    int S = (kSmemMax - 128 - red - bsm_bytes - 16 * 1024) / STAGE;
     S = S < 2 ? 2 : (S > 5 ? 5 : S);
     if (S > stages_per_cta) S = (int)stages_per_cta;  // small matrices: request only what is used
     const int ssq_bytes = XF == 3 ? (int)T.nu * 8 * 4 : 0;
-    const int acc_bytes_avail = kSmemMax - 128 - S * STAGE - red - ssq_bytes;
+    const int acc_bytes_avail = kSmemMax - 128 - S * STAGE - red - ssq_bytes - bsm_bytes;
     const int rg_bytes = MTG * 16 * 8 * 4;
     int sweep_rg = acc_bytes_avail / rg_bytes;
     if (sweep_rg < 1) return cudaErrorInvalidConfiguration;
     if (sweep_rg > per_cta) sweep_rg = (int)per_cta;
-    const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes + ssq_bytes;
+    const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes + ssq_bytes + bsm_bytes;
+    if (smem > kSmemMax) return cudaErrorInvalidConfiguration;
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT>,
@@ -992,17 +1018,19 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a);
 }
 
-// Work split: UW warps share each row block's units, two M-tiles per warp and
-// stage.  (One M-tile per warp doubles the CTAs of small matrices, but measured
-// over a whole decode step it is slower: more kernel variants in flight.)
+// Work split: UW warps share each row block's units.  A stage: 16 warps x 1
+// M-tile (exact activations: the fragments of UW units take shared memory),
+// 16 warps x 2 (Q8_K activations; x 1 for Q6_K, whose larger tiles would leave
+// one ring stage).  Exact Q8_0 (4352-byte M-tiles) takes at most 4 units per
+// pass, so that two ring stages and the fragments fit.
 template <int FMT, int NT, int XF, int ACT>
 static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                           cudaStream_t s, const XForm &xf) {
+    constexpr bool kExact = FMT == 8 || ACT == 0;
+    const int uw_max = kExact && mtile_bytes(FMT) > 3360 ? 4 : 8;
     int UW = 1;
-    while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
-    // a stage: 8 warps x 2 M-tiles (exact activations), 16 warps x 2 (Q8_K
-    // activations; x 1 for Q6_K, whose larger tiles would leave one ring stage)
-    constexpr int MPW = ACT == 1 && mtile_bytes(FMT) > 2816 ? 1 : 2;
+    while (UW < uw_max && UW * 2 <= T.nu) UW *= 2;
+    constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
     return launch_mpw<FMT, NT, XF, MPW, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
 }
 

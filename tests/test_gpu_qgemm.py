@@ -52,7 +52,8 @@ def test_dequant_bit_exact(O, ctx, qt):
     assert np.array_equal(got.view(np.uint32), g[f"{NAMES[qt]}_gguf_py"].view(np.uint32))
 
 
-SHAPES = [(256, 256), (1000, 1024), (96, 3584), (130, 4096)]
+# (96, 3584), (130, 4096), (64, 12288): few row groups over several K passes
+SHAPES = [(256, 256), (1000, 1024), (96, 3584), (130, 4096), (64, 12288)]
 
 
 @pytest.mark.parametrize("act", [0, 1])
@@ -83,8 +84,9 @@ def _rmsnorm(X, w, eps):
     return (X * scale[:, None] * w[None, :]).astype(np.float32)
 
 
+# (12, 32, 20480): the folded norm's sums of squares over ten K passes
 NORM_CASES = [(12, 256, 256), (12, 1000, 1024), (13, 130, 4096), (14, 300, 2048), (8, 256, 1024),
-              (8, 200, 1152), (8, 64, 800)]
+              (8, 200, 1152), (8, 64, 800), (12, 32, 20480)]
 
 
 @pytest.mark.parametrize("act", [0, 1])
