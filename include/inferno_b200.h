@@ -179,6 +179,26 @@ int ifr_accept_noalloc(ifr_ctx *ctx, const float *target, const float *draft,
 int ifr_accept_greedy(ifr_ctx *ctx, const float *target, const int32_t *draft_tokens,
                       int batch, int gamma, int vocab, int32_t *accept_count,
                       int32_t *out_tokens);
+/* filtered sampling, one token per row: CommonOps.softmax_sample_scratch!
+ * (src/CommonOps.jl:196-318) with uniforms[row] in [0, 1) in place of
+ * rand().  logits [rows][vocab] and uniforms [rows] on the device;
+ * out_tokens [rows] (device, 0-based).  temperature >= 0 (0 = argmax),
+ * top_k >= 0 (0 or >= vocab: off), top_p in [0, 1] (1: off), min_p in
+ * [0, 1] (0: off); values the reference rejects with ArgumentError
+ * (:126-139), vocab < 1 and vocab > 524288 give IFR_ERR_ARG.  A row holding
+ * NaN or +Inf (which the reference also rejects) gets token -1; a row of
+ * -Inf only gets token 0.  Ties at the top-k and top-p cuts go to the lower
+ * token id, and the top-p running sum is exact (integer weights). */
+int ifr_sample(ifr_ctx *ctx, const float *logits, int rows, int vocab, float temperature, int top_k,
+               float top_p, float min_p, const float *uniforms, int32_t *out_tokens);
+/* in place on logits [rows][vocab] (device): for every distinct token t of
+ * seen[row][0 .. n_seen) with 0 <= t < vocab (others, e.g. -1 padding, are
+ * skipped), the presence penalty l -= presence, then the repetition penalty
+ * l = l > 0 ? l / repetition : l * repetition (src/ModelCPU.jl:1202-1211,
+ * 1237-1238; src/CommonOps.jl:63-76).  presence 0 and repetition 1 are
+ * no-ops as there; repetition must be finite and > 0, vocab <= 1048576. */
+int ifr_apply_penalties(ifr_ctx *ctx, float *logits, int rows, int vocab, const int32_t *seen, int n_seen,
+                        float presence, float repetition);
 
 /* --- model and speculative-decoding state ---------------------------------
  * A Qwen3.5-hybrid GGUF (general.architecture "qwen35": GatedDeltaNet layers

@@ -194,6 +194,32 @@ class Context:
                                 _ptr(dout)))
         return acc, out, dout
 
+    def sample(self, logits, uniforms, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, out=None):
+        """logits [..., vocab] f32 (device), one uniform per row -> int32 tokens
+        (0-based; -1 marks a row with NaN or +Inf)"""
+        torch = self.torch
+        assert logits.dtype == torch.float32 and logits.is_contiguous()
+        V = logits.shape[-1]
+        rows = logits.numel() // V
+        assert uniforms.dtype == torch.float32 and uniforms.is_contiguous() and uniforms.numel() == rows
+        if out is None:
+            out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+        check(load().ifr_sample(self.handle, _ptr(logits), rows, V, ctypes.c_float(temperature), int(top_k),
+                                ctypes.c_float(top_p), ctypes.c_float(min_p), _ptr(uniforms), _ptr(out)))
+        return out
+
+    def apply_penalties(self, logits, seen, presence=0.0, repetition=1.0):
+        """in place on logits [rows, vocab] (device); seen [rows, n] int32 (device)"""
+        torch = self.torch
+        assert logits.dtype == torch.float32 and logits.is_contiguous()
+        assert seen.dtype == torch.int32 and seen.is_contiguous()
+        V = logits.shape[-1]
+        rows = logits.numel() // V
+        n = seen.numel() // max(rows, 1)
+        check(load().ifr_apply_penalties(self.handle, _ptr(logits), rows, V, _ptr(seen), n,
+                                         ctypes.c_float(presence), ctypes.c_float(repetition)))
+        return logits
+
     def accept_greedy(self, target, draft_tokens):
         torch = self.torch
         B, G1, V = target.shape

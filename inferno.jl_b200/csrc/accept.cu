@@ -552,6 +552,396 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
                     draft_tokens, G, nch, accept_count, out_tokens);
 }
 
+// ------------------------------------------------------ filtered sampling ---
+// CommonOps.softmax_sample_scratch! (src/CommonOps.jl:196-318), one CTA per
+// row, with the supplied uniform u in place of rand().  Fixed evaluation,
+// shared with the oracle (oracle/accept.c, or_sample_filtered):
+//   validation: NaN or +Inf -> token -1 (the reference throws, :145-160);
+//     M = max finite logit and g its first index; all -Inf -> 0; T == 0 or
+//     V == 1 -> g (:207-210)
+//   top_k, 0 < k < V (:217-230): the k largest logits, ties at the k-th value
+//     to the lower index; found by a 4 x 8-bit radix select on order-preserving
+//     keys (counts per digit bin), the tie cut by an index-ordered count
+//   e_i = ifr_exp((l_i - M) / T) for kept i, else 0 (:234-243); the
+//     renormalisations scale all weights alike and fold into the draw's sum
+//   top_p < 1 (:249-278): integer weights E_i = trunc(e_i 2^30), target =
+//     top_p * sum E (double); keep the first m elements in (e desc, index asc)
+//     order, m minimal with E_(1) + ... + E_(m) >= target - a radix select on
+//     the keys of e with exact 64-bit sums per digit bin, then the smallest
+//     count of the crossing value's elements, taken by index
+//   min_p > 0 (:280-299): keep e_i >= min_p (max_p sits at e = 1)
+//   draw (:301-317): w_i = kept ? e_i : 0; chunk sums in the canonical order
+//     above; tau = u W; first i with w_i > 0 and tau <= cumsum, else the last
+//     i with w_i > 0
+constexpr int kSampleMaxChunks = 256;  // vocab <= 256 x 2048
+
+__device__ __forceinline__ uint32_t f_key(float x) {
+    const uint32_t u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long e_fixed(float e) {
+    return (unsigned long long)__fmul_rn(e, 1073741824.0f);
+}
+
+struct SampleFSmem {
+    unsigned cnt[256];
+    unsigned long long sum[256];
+    float cs[kSampleMaxChunks];
+    float lsum[kNL];
+    unsigned lcnt[kNL];
+    float wsum[8];
+    float bv[8];
+    int bi[8];
+    int res[2];
+    unsigned long long S, above;
+    unsigned prefix, need, eq, before, total;
+    int sel, found, idx;
+    float tau;
+    int csel;
+};
+
+// the filters' state; w(i, l) = the final weight of element i with logit l
+struct SampleFilter {
+    float M, T, min_p;
+    bool topk, topp;
+    uint32_t key_k, key_p;
+    int cut_k, cut_p;
+    __device__ float ek(int i, float l) const {
+        if (topk) {
+            const uint32_t k = f_key(l);
+            if (!(k > key_k || (k == key_k && i <= cut_k))) return 0.f;
+        }
+        return elem_e(l, M, T);
+    }
+    __device__ float w(int i, float l) const {
+        float e = ek(i, l);
+        if (topp && e > 0.f) {
+            const uint32_t k = __float_as_uint(e);
+            if (!(k > key_p || (k == key_p && i <= cut_p))) e = 0.f;
+        }
+        if (min_p > 0.f && e < min_p) e = 0.f;
+        return e;
+    }
+};
+
+// Radix select, descending, over 32-bit keys key(i, l) of every element, with
+// 64-bit weights weight(i, l) when BY_SUM.  BY_SUM: the largest key value v
+// with sum_{key >= v} weight >= target; else the value of the rank-th largest
+// key.  Leaves in sm: prefix (that key), eq (elements holding it), above (the
+// weight above it), need (its rank among the equal ones, count select); sel <
+// 0 if no bin reaches the target (BY_SUM only).
+template <bool BY_SUM, class KeyF, class WF>
+__device__ void radix_desc(const float *row, int V, int nch, KeyF key, WF weight, unsigned rank, double target,
+                           SampleFSmem &sm) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    if (tid == 0) { sm.prefix = 0u; sm.above = 0ull; sm.need = rank; sm.sel = 0; sm.eq = 0u; }
+    uint32_t mask = 0u;
+    for (int d = 3; d >= 0; d--) {
+        const int shift = 8 * d;
+        __syncthreads();
+        sm.cnt[tid] = 0u;
+        sm.sum[tid] = 0ull;
+        __syncthreads();
+        const uint32_t prefix = sm.prefix;
+        if (sm.sel >= 0) {
+            for (int c = 0; c < nch; c++) {
+                float x[8];
+                const int n = load8(row, V, c, x);
+                for (int q = 0; q < n; q++) {
+                    const int i = c * kCH + kPER * tid + q;
+                    const uint32_t k = key(i, x[q]);
+                    if (((k ^ prefix) & mask) == 0u) {
+                        const int b = (int)((k >> shift) & 255u);
+                        atomicAdd(&sm.cnt[b], 1u);
+                        if (BY_SUM) atomicAdd(&sm.sum[b], weight(i, x[q]));
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && sm.sel >= 0) {
+            int sel = -1;
+            unsigned cum = 0u;
+            unsigned long long cs = 0ull;
+            for (int b = 255; b >= 0; b--) {
+                if (sm.cnt[b] == 0u) continue;
+                if (BY_SUM ? ((double)(sm.above + cs + sm.sum[b]) >= target) : (cum + sm.cnt[b] >= sm.need)) {
+                    sel = b;
+                    break;
+                }
+                cum += sm.cnt[b];
+                cs += sm.sum[b];
+            }
+            if (sel >= 0) {
+                sm.prefix = prefix | ((uint32_t)sel << shift);
+                sm.above += cs;
+                if (!BY_SUM) sm.need -= cum;
+                sm.eq = sm.cnt[sel];
+            }
+            sm.sel = sel;
+        }
+        mask |= 255u << shift;
+    }
+    __syncthreads();
+}
+
+// index of the n-th element (1-based, index order) with pred(i, l); INT_MAX
+// if there are fewer
+template <class Pred>
+__device__ int nth_index(const float *row, int V, int nch, Pred pred, unsigned n, SampleFSmem &sm) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    if (tid == 0) { sm.before = 0u; sm.idx = INT_MAX; }
+    for (int c = 0; c < nch; c++) {
+        float x[8];
+        const int nv = load8(row, V, c, x);
+        unsigned m = 0u;
+        for (int q = 0; q < nv; q++) m += pred(c * kCH + kPER * tid + q, x[q]) ? 1u : 0u;
+        __syncthreads();
+        sm.lcnt[tid] = m;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned cum = sm.before;
+            int found = -1;
+            for (int j = 0; j < kNL; j++) {
+                if (cum + sm.lcnt[j] >= n) { found = j; break; }
+                cum += sm.lcnt[j];
+            }
+            sm.found = found;
+            sm.total = cum;  // matches before lane `found` (or in all lanes, when none)
+        }
+        __syncthreads();
+        const int found = sm.found;
+        if (found >= 0) {
+            if (tid == found) {
+                unsigned k = sm.total;
+                for (int q = 0; q < nv; q++) {
+                    const int i = c * kCH + kPER * tid + q;
+                    if (pred(i, x[q]) && ++k == n) { sm.idx = i; break; }
+                }
+            }
+            __syncthreads();
+            return sm.idx;
+        }
+        if (tid == 0) sm.before = sm.total;
+    }
+    __syncthreads();
+    return INT_MAX;
+}
+
+// smallest n >= 1 with above + n unit >= target (unit > 0)
+__device__ unsigned long long cut_count(unsigned long long above, unsigned long long unit, double target) {
+    const double q = ceil((target - (double)above) / (double)unit);
+    unsigned long long n = q < 1.0 ? 1ull : (unsigned long long)q;
+    while (n > 1ull && (double)(above + (n - 1ull) * unit) >= target) n--;
+    while ((double)(above + n * unit) < target) n++;
+    return n;
+}
+
+__global__ void __launch_bounds__(kNL) sample_kernel(const float *__restrict__ logits, int V, float T, int top_k,
+                                                     float top_p, float min_p, const float *__restrict__ uniforms,
+                                                     int32_t *__restrict__ out) {
+    __shared__ SampleFSmem sm;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
+    const float *row = logits + (int64_t)r * V;
+    const int nch = (V + kCH - 1) / kCH;
+    pdl_trigger();
+    pdl_wait();
+    // validation, max and its first index
+    float bv = -CUDART_INF_F;
+    int bi = INT_MAX, bad = 0;
+    for (int c = 0; c < nch; c++) {
+        float x[8];
+        const int n = load8(row, V, c, x);
+        for (int q = 0; q < n; q++) {
+            const float v = x[q];
+            if (v != v || v == CUDART_INF_F) bad = 1;
+            else if (v != -CUDART_INF_F && v > bv) { bv = v; bi = c * kCH + kPER * tid + q; }
+        }
+    }
+    bad = __syncthreads_or(bad);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { sm.bv[warp] = bv; sm.bi[warp] = bi; }
+    __syncthreads();
+    float M = sm.bv[0];
+    int g = sm.bi[0];
+    for (int w = 1; w < kNL / 32; w++)
+        if (sm.bi[w] != INT_MAX && (g == INT_MAX || sm.bv[w] > M || (sm.bv[w] == M && sm.bi[w] < g))) {
+            M = sm.bv[w];
+            g = sm.bi[w];
+        }
+    if (bad || g == INT_MAX || T == 0.f || V == 1) {
+        if (tid == 0) out[r] = bad ? -1 : (g == INT_MAX ? 0 : g);
+        return;
+    }
+    SampleFilter F;
+    F.M = M;
+    F.T = T;
+    F.min_p = min_p;
+    F.topk = top_k > 0 && top_k < V;
+    F.topp = false;
+    F.key_k = 0u;
+    F.cut_k = INT_MAX;
+    F.key_p = 0u;
+    F.cut_p = INT_MAX;
+    auto none = [](int, float) { return 0ull; };
+    if (F.topk) {
+        radix_desc<false>(row, V, nch, [](int, float l) { return f_key(l); }, none, (unsigned)top_k, 0.0, sm);
+        F.key_k = sm.prefix;
+        const unsigned need = sm.need, eq = sm.eq;
+        if (need < eq) {
+            const uint32_t kk = F.key_k;
+            F.cut_k = nth_index(row, V, nch, [kk](int, float l) { return f_key(l) == kk; }, need, sm);
+        }
+    }
+    if (top_p < 1.0f) {
+        // exact integer total of the top-k weights
+        unsigned long long part = 0ull;
+        for (int c = 0; c < nch; c++) {
+            float x[8];
+            const int n = load8(row, V, c, x);
+            for (int q = 0; q < n; q++) part += e_fixed(F.ek(c * kCH + kPER * tid + q, x[q]));
+        }
+        __syncthreads();
+        if (tid == 0) sm.S = 0ull;
+        __syncthreads();
+        atomicAdd(&sm.S, part);
+        __syncthreads();
+        const double target = (double)top_p * (double)sm.S;
+        const SampleFilter Fk = F;
+        radix_desc<true>(row, V, nch, [Fk](int i, float l) { return __float_as_uint(Fk.ek(i, l)); },
+                         [Fk](int i, float l) { return e_fixed(Fk.ek(i, l)); }, 0u, target, sm);
+        if (sm.sel >= 0) {
+            F.topp = true;
+            F.key_p = sm.prefix;
+            const unsigned long long unit = e_fixed(__uint_as_float(F.key_p));
+            const unsigned long long need =
+                unit > 0ull ? cut_count(sm.above, unit, target) : (unsigned long long)sm.eq;
+            if (need < (unsigned long long)sm.eq) {
+                const uint32_t kp = F.key_p;
+                F.cut_p = nth_index(row, V, nch, [Fk, kp](int i, float l) { return __float_as_uint(Fk.ek(i, l)) == kp; },
+                                    (unsigned)need, sm);
+            }
+        }
+    }
+    // draw: chunk sums of the final weights in the canonical order
+    for (int c = 0; c < nch; c++) {
+        float x[8];
+        const int n = load8(row, V, c, x);
+        float t = 0.f;
+        for (int q = 0; q < n; q++) t = __fadd_rn(t, F.w(c * kCH + kPER * tid + q, x[q]));
+        const float sc = canon_sum(t, sm.wsum);
+        if (tid == 0) sm.cs[c] = sc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float W = 0.f;
+        for (int c = 0; c < nch; c++) W = __fadd_rn(W, sm.cs[c]);
+        float tau = __fmul_rn(uniforms[r], W), P = 0.f;
+        int csel = -1;
+        for (int c = 0; c < nch; c++) {
+            const float nP = __fadd_rn(P, sm.cs[c]);
+            if (sm.cs[c] > 0.f && tau <= nP) { csel = c; break; }
+            P = nP;
+        }
+        if (csel < 0) {
+            for (int c = nch - 1; c >= 0; c--) if (sm.cs[c] > 0.f) { csel = c; break; }
+            if (csel < 0) csel = nch - 1;
+            P = 0.f;
+            for (int c = 0; c < csel; c++) P = __fadd_rn(P, sm.cs[c]);
+            tau = __fadd_rn(P, sm.cs[csel]);
+        }
+        sm.csel = csel;
+        sm.tau = __fsub_rn(tau, P);
+        sm.res[0] = INT_MAX;
+        sm.res[1] = -1;
+    }
+    __syncthreads();
+    const int csel = sm.csel;
+    const float taup = sm.tau;
+    float x[8], v[8];
+    const int n = load8(row, V, csel, x);
+    float t = 0.f;
+    for (int q = 0; q < kPER; q++) {
+        v[q] = q < n ? F.w(csel * kCH + kPER * tid + q, x[q]) : 0.f;
+        if (q < n) t = __fadd_rn(t, v[q]);
+    }
+    sm.lsum[tid] = t;
+    __syncthreads();
+    if (tid == 0) {  // exclusive prefix, sequential
+        float pre = 0.f;
+        for (int j = 0; j < kNL; j++) { const float tj = sm.lsum[j]; sm.lsum[j] = pre; pre = __fadd_rn(pre, tj); }
+    }
+    __syncthreads();
+    float cum = sm.lsum[tid];
+    int hit = -1, lastpos = -1;
+    for (int q = 0; q < n; q++) {
+        cum = __fadd_rn(cum, v[q]);
+        if (v[q] > 0.f) {
+            if (hit < 0 && taup <= cum) hit = kPER * tid + q;
+            lastpos = kPER * tid + q;
+        }
+    }
+    if (hit >= 0) atomicMin(&sm.res[0], hit);
+    if (lastpos >= 0) atomicMax(&sm.res[1], lastpos);
+    __syncthreads();
+    if (tid == 0) {
+        const int base = csel * kCH;
+        const int last = min(V, base + kCH) - 1;
+        out[r] = sm.res[0] != INT_MAX ? base + sm.res[0] : (sm.res[1] >= 0 ? base + sm.res[1] : last);
+    }
+}
+
+cudaError_t sample_filtered(const float *logits, int rows, int V, float T, int top_k, float top_p, float min_p,
+                            const float *uniforms, int32_t *out, cudaStream_t s) {
+    if ((V + kCH - 1) / kCH > kSampleMaxChunks) return cudaErrorInvalidValue;
+    return launch_k(sample_kernel, dim3(rows), dim3(kNL), 0, s, logits, V, T, top_k, top_p, min_p, uniforms, out);
+}
+
+// presence then repetition penalty (src/ModelCPU.jl:1202-1211,1237-1238;
+// src/CommonOps.jl:63-76) on each row's distinct seen tokens: a shared bitmap
+// of the vocabulary lets exactly one thread apply each distinct token
+__global__ void __launch_bounds__(256) penalty_kernel(float *__restrict__ logits, int V,
+                                                      const int32_t *__restrict__ seen, int n_seen,
+                                                      float presence, float repetition) {
+    extern __shared__ unsigned bitmap[];
+    const int r = blockIdx.x, words = (V + 31) >> 5;
+    pdl_trigger();
+    pdl_wait();
+    for (int i = threadIdx.x; i < words; i += blockDim.x) bitmap[i] = 0u;
+    __syncthreads();
+    float *l = logits + (int64_t)r * V;
+    const int32_t *sn = seen + (int64_t)r * n_seen;
+    for (int j = threadIdx.x; j < n_seen; j += blockDim.x) {
+        const int t = sn[j];
+        if (t < 0 || t >= V) continue;
+        const unsigned bit = 1u << (t & 31);
+        if (atomicOr(&bitmap[t >> 5], bit) & bit) continue;
+        float x = l[t];
+        if (presence != 0.f) x = __fsub_rn(x, presence);
+        if (repetition != 1.f) x = x > 0.f ? __fdiv_rn(x, repetition) : __fmul_rn(x, repetition);
+        l[t] = x;
+    }
+}
+
+cudaError_t apply_penalties(float *logits, int rows, int V, const int32_t *seen, int n_seen, float presence,
+                            float repetition, cudaStream_t s) {
+    const size_t smem = (size_t)((V + 31) / 32) * 4;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(penalty_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    return launch_k(penalty_kernel, dim3(rows), dim3(256), smem, s, logits, V, seen, n_seen, presence, repetition);
+}
+
 }  // namespace ifr
 
 // ------------------------------------------------ allocation-free entry ------

@@ -2,6 +2,7 @@
 #include "../../include/inferno_b200.h"
 #include "common.cuh"
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -410,6 +411,40 @@ int ifr_accept_greedy(ifr_ctx *c, const float *target, const int32_t *draft_toke
     IFR_CHECK_CUDA(ifr::accept_greedy(target, draft_tokens, batch, gamma, vocab, accept_count, out_tokens,
                                       c->scratch, c->stream),
                    "accept_greedy launch");
+    return IFR_OK;
+}
+
+int ifr_sample(ifr_ctx *c, const float *logits, int rows, int vocab, float temperature, int top_k, float top_p,
+               float min_p, const float *uniforms, int32_t *out_tokens) {
+    if (!c || !logits || !uniforms || !out_tokens) return fail(IFR_ERR_ARG, "NULL argument");
+    if (rows < 0 || vocab < 1 || vocab > 524288)
+        return fail(IFR_ERR_ARG, "invalid sizes rows=%d vocab=%d (vocab must be in 1..524288)", rows, vocab);
+    // _validate_sampling_parameters (src/CommonOps.jl:126-139)
+    if (!std::isfinite(temperature) || temperature < 0.f)
+        return fail(IFR_ERR_ARG, "temperature must be finite and non-negative");
+    if (!std::isfinite(top_p) || top_p < 0.f || top_p > 1.f) return fail(IFR_ERR_ARG, "top_p must be in [0, 1]");
+    if (top_k < 0) return fail(IFR_ERR_ARG, "top_k must be non-negative");
+    if (!std::isfinite(min_p) || min_p < 0.f || min_p > 1.f) return fail(IFR_ERR_ARG, "min_p must be in [0, 1]");
+    if (rows == 0) return IFR_OK;
+    DeviceGuard g(c->device);
+    IFR_CHECK_CUDA(ifr::sample_filtered(logits, rows, vocab, temperature, top_k, top_p, min_p, uniforms, out_tokens,
+                                        c->stream),
+                   "sample launch");
+    return IFR_OK;
+}
+
+int ifr_apply_penalties(ifr_ctx *c, float *logits, int rows, int vocab, const int32_t *seen, int n_seen,
+                        float presence, float repetition) {
+    if (!c || !logits || (!seen && n_seen > 0)) return fail(IFR_ERR_ARG, "NULL argument");
+    if (rows < 0 || vocab < 1 || vocab > (1 << 20) || n_seen < 0)
+        return fail(IFR_ERR_ARG, "invalid sizes rows=%d vocab=%d n_seen=%d", rows, vocab, n_seen);
+    if (!std::isfinite(presence)) return fail(IFR_ERR_ARG, "presence penalty must be finite");
+    if (!std::isfinite(repetition) || !(repetition > 0.f))
+        return fail(IFR_ERR_ARG, "repetition penalty must be finite and > 0");
+    if (rows == 0 || n_seen == 0 || (presence == 0.f && repetition == 1.f)) return IFR_OK;
+    DeviceGuard g(c->device);
+    IFR_CHECK_CUDA(ifr::apply_penalties(logits, rows, vocab, seen, n_seen, presence, repetition, c->stream),
+                   "penalty launch");
     return IFR_OK;
 }
 

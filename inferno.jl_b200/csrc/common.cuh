@@ -83,6 +83,12 @@ cudaError_t tp_accept(const float *cand, int W, int rows, const int32_t *drafts,
 cudaError_t accept_greedy_fused(const float *target, const int32_t *draft_tokens, int batch, int gamma, int vocab,
                                 int32_t *accept_count, int32_t *out_tokens, void *scratch, unsigned *counter,
                                 cudaStream_t s, int draft_ld = 0, int out_ld = 0);
+// filtered sampling, one token per row (vocab <= 524288), and the in-place
+// presence / repetition penalties (vocab <= 1048576)
+cudaError_t sample_filtered(const float *logits, int rows, int vocab, float T, int top_k, float top_p, float min_p,
+                            const float *uniforms, int32_t *out_tokens, cudaStream_t s);
+cudaError_t apply_penalties(float *logits, int rows, int vocab, const int32_t *seen, int n_seen, float presence,
+                            float repetition, cudaStream_t s);
 
 }  // namespace ifr
 

@@ -338,3 +338,190 @@ int or_accept_greedy(const float *target, const int32_t *draft_tokens, int batch
     }
     return 0;
 }
+
+/* ===================================================================== *
+ * Filtered sampling: CommonOps.softmax_sample_scratch!
+ * (src/CommonOps.jl:196-318) with a supplied uniform u in place of rand(),
+ * and the presence / repetition penalties that precede it
+ * (src/ModelCPU.jl:1202-1211,1237-1238; src/CommonOps.jl:63-76).
+ * Shared with the device code (csrc/accept.cu, sample_kernel):
+ *   validation (:145-160): NaN or +Inf anywhere -> -1 (the reference throws);
+ *     M = max finite logit, g = its first index; every logit -Inf -> 0;
+ *     T == 0 or V == 1 -> g (:207-210)
+ *   top_k, 0 < k < V (:217-230): the k largest logits; ties at the k-th value
+ *     go to the lower index (the reference's heap order leaves them open)
+ *   e_i = or_exp((l_i - M) / T) for kept i, else 0 (:234-243).  The
+ *     renormalisations (:244-247, :269-277, :292-298) scale every weight
+ *     alike; they are folded into the sampling sum
+ *   top_p < 1 (:249-278): weights as integers E_i = trunc(e_i * 2^30);
+ *     target = (double)top_p * sum E; keep the first m elements in
+ *     (e desc, index asc) order, m minimal with E_(1) + ... + E_(m) >= target
+ *     (the reference's running cumsum, summed exactly)
+ *   min_p > 0 (:280-299): keep e_i >= min_p (p >= max_p * min_p, max_p at e = 1)
+ *   draw (:301-317): w_i = kept ? e_i : 0; chunk sums in the acceptance's
+ *     canonical order; tau = u * W; first i with w_i > 0 and tau <= cumsum,
+ *     else the last i with w_i > 0 (the reference's r <= cumsum alone would
+ *     return a filtered-out first token when rand() gives exactly 0)
+ * ===================================================================== */
+
+static inline uint32_t f_key(float x) {     /* order-preserving key of a float */
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+static inline uint64_t e_fixed(float e) { return (uint64_t)(e * 1073741824.0f); }
+
+typedef struct { uint32_t key; int idx; } kidx;
+static int kidx_desc(const void *a, const void *b) {
+    const kidx *x = (const kidx *)a, *y = (const kidx *)b;
+    if (x->key != y->key) return x->key > y->key ? -1 : 1;
+    return x->idx - y->idx;
+}
+
+/* smallest n >= 1 with above + n * unit >= target (unit > 0) */
+static uint64_t or_cut_count(uint64_t above, uint64_t unit, double target) {
+    double q = ceil((target - (double)above) / (double)unit);
+    uint64_t n = q < 1.0 ? 1 : (uint64_t)q;
+    while (n > 1 && (double)(above + (n - 1) * unit) >= target) n--;
+    while ((double)(above + n * unit) < target) n++;
+    return n;
+}
+
+int or_sample_filtered(const float *l, int V, float T, int top_k, float top_p, float min_p, float u) {
+    if (V < 1) return -1;
+    float M = -INFINITY;
+    int g = 0, finite = 0;
+    for (int i = 0; i < V; i++) {
+        float x = l[i];
+        if (isnan(x) || x == INFINITY) return -1;
+        if (x != -INFINITY) {
+            if (!finite || x > M) { M = x; g = i; }
+            finite = 1;
+        }
+    }
+    if (!finite) return 0;
+    if (T == 0.0f || V == 1) return g;
+    char *keep = (char *)malloc(V);
+    float *w = (float *)malloc(sizeof(float) * V);
+    kidx *ord = (kidx *)malloc(sizeof(kidx) * V);
+    for (int i = 0; i < V; i++) keep[i] = 1;
+    if (top_k > 0 && top_k < V) {
+        for (int i = 0; i < V; i++) { ord[i].key = f_key(l[i]); ord[i].idx = i; }
+        qsort(ord, V, sizeof(kidx), kidx_desc);
+        for (int i = 0; i < V; i++) keep[i] = 0;
+        for (int j = 0; j < top_k; j++) keep[ord[j].idx] = 1;
+    }
+    for (int i = 0; i < V; i++) w[i] = keep[i] ? or_exp((l[i] - M) / T) : 0.0f;
+    if (top_p < 1.0f) {
+        uint64_t S = 0;
+        int n = 0;
+        for (int i = 0; i < V; i++) {
+            S += e_fixed(w[i]);
+            if (keep[i]) { uint32_t k; memcpy(&k, &w[i], 4); ord[n].key = k; ord[n].idx = i; n++; }
+        }
+        const double target = (double)top_p * (double)S;
+        qsort(ord, n, sizeof(kidx), kidx_desc);
+        /* whole groups of equal e first, then the lowest indices of the
+           group where the running sum reaches the target */
+        uint64_t cum = 0;
+        int j = 0, m = n;
+        while (j < n) {
+            int j2 = j;
+            while (j2 < n && ord[j2].key == ord[j].key) j2++;
+            float ev;
+            memcpy(&ev, &ord[j].key, 4);
+            const uint64_t unit = e_fixed(ev), grp = (uint64_t)(j2 - j) * unit;
+            if ((double)(cum + grp) >= target) {
+                uint64_t need = unit > 0 ? or_cut_count(cum, unit, target) : (uint64_t)(j2 - j);
+                if (need > (uint64_t)(j2 - j)) need = (uint64_t)(j2 - j);
+                m = j + (int)need;
+                break;
+            }
+            cum += grp;
+            j = j2;
+        }
+        for (int i = 0; i < V; i++) keep[i] = 0;
+        for (int q = 0; q < m; q++) keep[ord[q].idx] = 1;
+        for (int i = 0; i < V; i++) if (!keep[i]) w[i] = 0.0f;
+    }
+    if (min_p > 0.0f)
+        for (int i = 0; i < V; i++) if (w[i] < min_p) w[i] = 0.0f;
+    /* canonical chunked draw */
+    const int nch = (V + CH - 1) / CH;
+    float *cs = (float *)malloc(sizeof(float) * nch);
+    float lanes[NL];
+    for (int c = 0; c < nch; c++) {
+        int b = c * CH, e = b + CH < V ? b + CH : V;
+        for (int jn = 0; jn < NL; jn++) {
+            float t = 0.f;
+            for (int q = 0; q < PER; q++) { int i = b + PER * jn + q; if (i < e) t = t + w[i]; }
+            lanes[jn] = t;
+        }
+        cs[c] = butterfly_sum(lanes);
+    }
+    float W = 0.f;
+    for (int c = 0; c < nch; c++) W = W + cs[c];
+    float tau = u * W, P = 0.f;
+    int csel = -1;
+    for (int c = 0; c < nch; c++) {
+        float nP = P + cs[c];
+        if (cs[c] > 0.f && tau <= nP) { csel = c; break; }
+        P = nP;
+    }
+    if (csel < 0) {
+        for (int c = nch - 1; c >= 0; c--) if (cs[c] > 0.f) { csel = c; break; }
+        if (csel < 0) csel = nch - 1;
+        P = 0.f;
+        for (int c = 0; c < csel; c++) P = P + cs[c];
+        tau = P + cs[csel];
+    }
+    int b = csel * CH, e = b + CH < V ? b + CH : V;
+    /* blocked in-chunk search over positive weights */
+    const float taup = tau - P;
+    float pre = 0.f;
+    int tok = -1;
+    for (int jn = 0; jn < NL && tok < 0; jn++) {
+        float cum = pre, t = 0.f;
+        for (int q = 0; q < PER; q++) {
+            int i = b + PER * jn + q;
+            if (i >= e) break;
+            t = t + w[i];
+            cum = cum + w[i];
+            if (w[i] > 0.f && taup <= cum) { tok = i; break; }
+        }
+        pre = pre + t;
+    }
+    if (tok < 0) {
+        tok = e - 1;
+        for (int i = e - 1; i >= b; i--) if (w[i] > 0.f) { tok = i; break; }
+    }
+    free(cs); free(ord); free(w); free(keep);
+    return tok;
+}
+
+int or_sample_rows(const float *logits, int rows, int V, float T, int top_k, float top_p, float min_p,
+                   const float *uniforms, int32_t *out) {
+    for (int r = 0; r < rows; r++)
+        out[r] = or_sample_filtered(logits + (int64_t)r * V, V, T, top_k, top_p, min_p, uniforms[r]);
+    return 0;
+}
+
+/* presence then repetition penalty on every distinct seen token (0 <= t < V) */
+void or_apply_penalties(float *logits, int rows, int V, const int32_t *seen, int n_seen, float presence,
+                        float repetition) {
+    char *mark = (char *)malloc(V > 0 ? V : 1);
+    for (int r = 0; r < rows; r++) {
+        float *l = logits + (int64_t)r * V;
+        memset(mark, 0, V);
+        for (int j = 0; j < n_seen; j++) {
+            int t = seen[(int64_t)r * n_seen + j];
+            if (t < 0 || t >= V || mark[t]) continue;
+            mark[t] = 1;
+            float x = l[t];
+            if (presence != 0.0f) x = x - presence;
+            if (repetition != 1.0f) x = x > 0.0f ? x / repetition : x * repetition;
+            l[t] = x;
+        }
+    }
+    free(mark);
+}

@@ -65,6 +65,13 @@ int   or_accept(const float *target, const float *draft, const int32_t *draft_to
 int   or_accept_greedy(const float *target, const int32_t *draft_tokens, int batch,
                        int gamma, int vocab, int32_t *accept_count, int32_t *out_tokens);
 int   or_argmax(const float *row, int n);
+/* filtered sampling (CommonOps.jl:196-318) and penalties (ModelCPU.jl:1202-1238) */
+int   or_sample_filtered(const float *logits, int vocab, float temperature, int top_k, float top_p,
+                         float min_p, float u);                 /* 0-based; -1 on NaN/+Inf */
+int   or_sample_rows(const float *logits, int rows, int vocab, float temperature, int top_k,
+                     float top_p, float min_p, const float *uniforms, int32_t *out_tokens);
+void  or_apply_penalties(float *logits, int rows, int vocab, const int32_t *seen, int n_seen,
+                         float presence, float repetition);
 
 /* ---- model forward (model.c) ---- */
 typedef struct {

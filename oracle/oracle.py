@@ -60,6 +60,13 @@ def lib():
         L.or_accept_greedy.argtypes = [_fp, _i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        _i32p, _i32p]
         L.or_argmax.argtypes = [_fp, ctypes.c_int]
+        L.or_sample_filtered.argtypes = [_fp, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                         ctypes.c_float, ctypes.c_float]
+        L.or_sample_rows.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                     ctypes.c_float, ctypes.c_float, _fp, _i32p]
+        L.or_apply_penalties.argtypes = [_fp, ctypes.c_int, ctypes.c_int, _i32p, ctypes.c_int, ctypes.c_float,
+                                         ctypes.c_float]
+        L.or_apply_penalties.restype = None
         _lib = L
     return _lib
 
@@ -208,6 +215,30 @@ def accept(target, draft, uniforms, temperature, draft_tokens=None):
                          _p(acc, _i32p), _p(out, _i32p), _p(dout, _i32p))
     assert rc == 0
     return acc, out, dout
+
+
+def sample(logits, uniforms, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0):
+    """filtered sampling per row (CommonOps.jl:196-318): 0-based tokens, -1
+    for a row holding NaN or +Inf"""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    V = logits.shape[-1]
+    rows = logits.size // V
+    u = np.ascontiguousarray(uniforms, dtype=np.float32).reshape(rows)
+    out = np.empty(rows, dtype=np.int32)
+    lib().or_sample_rows(_p(logits, _fp), rows, V, float(temperature), int(top_k), float(top_p), float(min_p),
+                         _p(u, _fp), _p(out, _i32p))
+    return out
+
+
+def apply_penalties(logits, seen, presence=0.0, repetition=1.0):
+    """presence then repetition penalty on each row's distinct seen tokens
+    (ModelCPU.jl:1202-1238, CommonOps.jl:63-76); returns a new array"""
+    out = np.array(logits, dtype=np.float32, order="C", copy=True)
+    V = out.shape[-1]
+    rows = out.size // V
+    sn = np.ascontiguousarray(seen, dtype=np.int32).reshape(rows, -1)
+    lib().or_apply_penalties(_p(out, _fp), rows, V, _p(sn, _i32p), sn.shape[1], float(presence), float(repetition))
+    return out
 
 
 def accept_greedy(target, draft_tokens):
