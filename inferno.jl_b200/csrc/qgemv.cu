@@ -1021,16 +1021,25 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
 // Work split: UW warps share each row block's units.  A stage: 16 warps x 1
 // M-tile (exact activations: the fragments of UW units take shared memory),
 // 16 warps x 2 (Q8_K activations; x 1 for Q6_K, whose larger tiles would leave
-// one ring stage).  Exact Q8_0 (4352-byte M-tiles) takes at most 4 units per
-// pass, so that two ring stages and the fragments fit.
+// one ring stage).  UW is the largest power of two <= 8 (and <= the units)
+// whose two ring stages, fragments and partials fit in shared memory: exact
+// Q8_0 (4352-byte M-tiles) with two n-tiles takes 4.
 template <int FMT, int NT, int XF, int ACT>
 static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                           cudaStream_t s, const XForm &xf) {
     constexpr bool kExact = FMT == 8 || ACT == 0;
-    const int uw_max = kExact && mtile_bytes(FMT) > 3360 ? 4 : 8;
-    int UW = 1;
-    while (UW < uw_max && UW * 2 <= T.nu) UW *= 2;
     constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
+    constexpr int CW = consumers<ACT>();
+    constexpr int kSmemMax = 226 * 1024;
+    int UW = 1;
+    while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
+    for (; UW > 1; UW /= 2) {
+        const int MTG = CW * MPW / UW;
+        const int need = 128 + 2 * CW * MPW * mtile_bytes(FMT) + 2 * CW * (MPW * NT * 4) * 32 * 4 +
+                         (kExact ? UW * bunit_words(NT) * 4 : 0) + MTG * 16 * 8 * 4 +
+                         (XF == 3 ? (int)T.nu * 8 * 4 : 0);
+        if (need <= kSmemMax) break;
+    }
     return launch_mpw<FMT, NT, XF, MPW, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
 }
 
