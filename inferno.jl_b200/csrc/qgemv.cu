@@ -852,12 +852,18 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
             if constexpr (kI8) {
                 if (active) build_b_i8<FMT, XF>(a, inv_s, u, lane, F);
             } else {
-                // the unit's warps split its n-tiles; the previous pass's fragments
-                // were last read before the barrier that closed its final stage
-                uint32_t *unit = bsm + ui * bunit_words(NT);
-                if (active && mp < NT) build_b<FMT, NT, XF>(a, inv_s, u, lane, mp, unit, sw == o.rg_lo ? ssq : nullptr);
+                // the warps split the pass's (unit, n-tile) builds; the previous
+                // pass's fragments were last read before the barrier that closed
+                // its final stage
+                for (int task = warp; task < UW * NT; task += CW) {
+                    const int bu = task % UW;
+                    const int64_t uu = (int64_t)p * UW + bu;
+                    if (uu < a.nu)
+                        build_b<FMT, NT, XF>(a, inv_s, uu, lane, task / UW, bsm + bu * bunit_words(NT),
+                                             sw == o.rg_lo ? ssq : nullptr);
+                }
                 consumer_bar();
-                F.at(unit, lane);
+                F.at(bsm + ui * bunit_words(NT), lane);
             }
             for (int rg = sw; rg < sw_hi; rg++, it++) {
                 const int s = it % a.S;
@@ -875,7 +881,7 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
 #pragma unroll
                     for (int mm = 0; mm < MPW; mm++) {
                         const int m = MPW * mp + mm;
-                        if (rg * MTG + m < a.nrb) {
+                        if (m < MTG && rg * MTG + m < a.nrb) {
                             const uint8_t *tile = st + (size_t)(m * UW + ui) * MTB;
                             if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot[mm]);
                             else if constexpr (kI8 && FMT == 14) mtile_q6_i8(tile, lane, F, tot[mm][0]);
@@ -1031,6 +1037,13 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
     constexpr int CW = consumers<ACT>();
     constexpr int kSmemMax = 226 * 1024;
+    // exact activations, 3..16 units that are not a power of two (K = 3584:
+    // 14): one pass of UW = all units (MTG = 16 / UW row blocks, the leftover
+    // warps idle) when its layout fits, instead of two or more passes
+    if (kExact && T.nu > 2 && T.nu <= CW && (T.nu & (T.nu - 1)) != 0) {
+        const cudaError_t e = launch_mpw<FMT, NT, XF, MPW, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, (int)T.nu);
+        if (e != cudaErrorInvalidConfiguration) return e;
+    }
     int UW = 1;
     while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
     for (; UW > 1; UW /= 2) {
