@@ -1037,13 +1037,6 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
     constexpr int CW = consumers<ACT>();
     constexpr int kSmemMax = 226 * 1024;
-    // exact activations, 3..16 units that are not a power of two (K = 3584:
-    // 14): one pass of UW = all units (MTG = 16 / UW row blocks, the leftover
-    // warps idle) when its layout fits, instead of two or more passes
-    if (kExact && T.nu > 2 && T.nu <= CW && (T.nu & (T.nu - 1)) != 0) {
-        const cudaError_t e = launch_mpw<FMT, NT, XF, MPW, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, (int)T.nu);
-        if (e != cudaErrorInvalidConfiguration) return e;
-    }
     int UW = 1;
     while (UW < 8 && UW * 2 <= T.nu) UW *= 2;
     for (; UW > 1; UW /= 2) {
