@@ -452,6 +452,7 @@ struct ifr_state {
     ifr::EngineScalars *sc = nullptr;   // device
     int32_t *vtok = nullptr, *acc = nullptr, *outtok = nullptr, *log = nullptr, *mtp_pos = nullptr;
     int32_t *h_tok = nullptr;           // pinned staging
+    int32_t *prompt = nullptr;          // device copy of the prompts being prefilled [B][max_ctx]
     float *x, *xn, *proj, *y, *gu, *hmid, *hid, *logits;
     float *mtp_h, *mtp_cat;
     float *cand = nullptr;              // tensor parallel: per-row (max, argmax) of every rank
@@ -1064,6 +1065,7 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     auto chk = [&](int r) { if (!rc) rc = r; };
     chk(dalloc(s, &s->sc, B));
     chk(dalloc(s, &s->vtok, N));
+    chk(dalloc(s, &s->prompt, (size_t)B * max_ctx));
     chk(dalloc(s, &s->acc, B + 4));
     chk(dalloc(s, &s->outtok, N + B));
     chk(dalloc(s, &s->mtp_pos, B + 4));
@@ -1238,12 +1240,16 @@ int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first
     cudaGetDevice(&prev);
     cudaSetDevice(ifr_ctx_device(s->m->ctx));
     int rc = IFR_OK;
+    // the whole prompt goes to the device once; every chunk's tokens are a
+    // device-to-device copy, so the chunks queue without host round trips
+    cudaError_t e0 = cudaMemcpyAsync(s->prompt, tokens, sizeof(int32_t) * B * n, cudaMemcpyHostToDevice, st);
+    if (e0 != cudaSuccess) rc = ifr_cuda_fail(e0, "H2D prompt");
     for (int i0 = 0; !rc && i0 < n;) {
         const bool last = i0 == n - 1;
         const int k = last ? 1 : std::min(kNMax, n - 1 - i0);
-        for (int b = 0; b < B; b++) memcpy(s->h_tok + (int64_t)b * kNMax, tokens + (int64_t)b * n + i0, sizeof(int32_t) * k);
-        cudaError_t e = cudaMemcpyAsync(s->vtok, s->h_tok, sizeof(int32_t) * kNMax * B, cudaMemcpyHostToDevice, st);
-        if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "H2D prompt"); break; }
+        cudaError_t e = cudaMemcpy2DAsync(s->vtok, sizeof(int32_t) * kNMax, s->prompt + i0, sizeof(int32_t) * n,
+                                          sizeof(int32_t) * k, B, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prompt chunk"); break; }
         rc = target_forward(s, k, last, false, st);
         if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, B, st);
         if (!rc && last) {
@@ -1253,10 +1259,9 @@ int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first
                               (const float *)s->hid, s->mtp_h, (int)c.hidden, s->log, (int)s->log_cap);
             if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prefill finish"); break; }
         }
-        // the prompt tokens buffer is reused by the next chunk
-        if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = ifr_cuda_fail(cudaGetLastError(), "prefill");
         i0 += k;
     }
+    if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = ifr_cuda_fail(cudaGetLastError(), "prefill");
     if (!rc && first_tokens) {
         cudaError_t e = cudaMemcpy(first_tokens, s->outtok, sizeof(int32_t) * B, cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) rc = ifr_cuda_fail(e, "D2H first token");
