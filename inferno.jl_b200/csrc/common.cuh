@@ -34,6 +34,23 @@ cudaError_t dequant(const QTensor &t, float *out, cudaStream_t s);
 cudaError_t dequant_rows(const QTensor &t, const int32_t *idx, int64_t nrows, float *out, cudaStream_t s);
 
 // activation transform applied by the GEMV while it reads X
+// Greedy decision folded into a GEMV's epilogue (qgemm_small, one launch):
+// the argmax of every output column (ties to the lower row), then per
+// sequence b of G + 1 consecutive columns the longest prefix whose argmax
+// equals its draft, as accept_greedy_fused does: out[b * out_ld + i] = argmax
+// of column b (G + 1) + i up to the first mismatch (-1 after it), acc[b] =
+// accepted drafts.  cand: 8 x (grid) 64-bit scratch; counter: one unsigned at
+// zero, returned to zero (launches sharing it must not overlap).
+struct GemvArgmax {
+    unsigned long long *cand = nullptr;
+    unsigned *counter = nullptr;
+    const int32_t *drafts = nullptr;  // draft b's tokens at drafts + b * draft_ld (G > 0)
+    int draft_ld = 0;
+    int G = 0;
+    int32_t *acc = nullptr;           // may be null (G = 0)
+    int32_t *out = nullptr;
+    int out_ld = 0;
+};
 struct XForm {
     int kind = 0;              // 0: none; 1: RMSNorm x * (1/sqrt(mean x^2 + eps)) * w; 2: SwiGLU
                                // silu(X[c][k]) * X[c][K + k] (X holds [gate | up] per column)
@@ -45,6 +62,7 @@ struct XForm {
     int ep = 0;                // 1: the rows are 16-row blocks of gate and up interleaved
                                // (gate 0-15, up 0-15, gate 16-31, ...); Y gets silu(gate) * up,
                                // rows/2 rows (not with accumulate)
+    const GemvArgmax *am = nullptr;  // greedy decision on Y (not with ep or accumulate)
 };
 // Y[ncols][rows] (+)= W * f(X), ncols <= 8 per call; X 16-byte aligned, ldx a multiple of 4
 cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,

@@ -457,6 +457,8 @@ struct ifr_state {
     float *mtp_h, *mtp_cat;
     float *cand = nullptr;              // tensor parallel: per-row (max, argmax) of every rank
     unsigned *gcount = nullptr;         // fused argmax/accept: per-launch completion counter (returns to 0)
+    unsigned long long *am_cand = nullptr;  // lm_head GEMV epilogue argmax: per-CTA candidates [8][1024]
+    unsigned *am_count = nullptr;       // its completion counter (returns to 0)
     float *rope_cos, *rope_sin;
     std::vector<float *> S, hist, rq, rkv;      // per layer (SSM) else null
     std::vector<float *> kc, vc;                // per layer (attention) else null
@@ -788,7 +790,8 @@ int greedy_accept(ifr_state *s, const int32_t *drafts, int draft_ld, int B, int 
 // target forward of the n tokens per request in vtok (request b: vtok[b *
 // kNMax ..], positions sc[b].pos ..; device); final-normed hidden of every
 // column in s->hid; logits of every column in s->logits when `logits` is set
-int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cudaStream_t st) {
+int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cudaStream_t st,
+                   const ifr::GemvArgmax *am = nullptr) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
     const int B = s->B, nc = B * n;
@@ -804,7 +807,9 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
     }
     ifr::rmsnorm(s->x, m->final_norm, s->hid, nc, c.hidden, c.rms_eps, c.hidden, c.hidden, st);
     if (logits) {
-        int rc = gemv(s, CAT_LM_HEAD, m->lm_head, s->hid, nc, s->logits, false, st);
+        ifr::XForm f;
+        f.am = am;
+        int rc = gemv(s, CAT_LM_HEAD, m->lm_head, s->hid, nc, s->logits, false, st, f);
         if (rc) return rc;
     }
     s->last_n = n;
@@ -835,6 +840,14 @@ __global__ void prefill_finish_kernel(ifr::EngineScalars *sc, const int32_t *tok
     for (int i = threadIdx.x; i < d; i += blockDim.x) mtp_h[i] = hid[i];
 }
 
+// the lm_head of nc columns can make the greedy decision in its own epilogue:
+// one small-N launch over an unsharded, single-part lm_head
+bool lm_head_decides(const ifr_state *s, int nc) {
+    const ifr_model *m = s->m;
+    return !m->comm && m->lm_head.parts.size() == 1 && nc <= kNMax &&
+           !(nc >= ifr_ctx_dense_min(m->ctx) && s->dense) && m->lm_head.parts[0].rows <= 0x7FFFFFFF;
+}
+
 // MTP draft of gamma tokens into vtok[b * kNMax + 1 .. gamma] of every request
 int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
     ifr_model *m = s->m;
@@ -859,12 +872,24 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
         if (rc) return rc;
         if ((rc = layer_forward(s, m->mtp_layer, -1, 1, s->mtp_kc, s->mtp_vc, s->mtp_pos, 1, kv_ld, true, st)))
             return rc;
-        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->x, B, s->logits, false, st, norm_out))) return rc;
-        // greedy draft token straight into the verify tokens
-        ECHECK(ifr::accept_greedy_fused(s->logits, nullptr, B, 0, c.vocab, s->acc, s->vtok + j, s->acc_scratch,
-                                        s->gcount, st, 1, kNMax),
-               "draft argmax");
-        s->launches += 2;  // prep, argmax
+        // greedy draft token straight into the verify tokens: in the lm_head's
+        // epilogue when it runs as one small-N launch, else a separate argmax
+        ifr::GemvArgmax am;
+        am.cand = s->am_cand;
+        am.counter = s->am_count;
+        am.out = s->vtok + j;
+        am.out_ld = kNMax;
+        const bool fused = lm_head_decides(s, B);
+        ifr::XForm f = norm_out;
+        if (fused) f.am = &am;
+        if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->x, B, s->logits, false, st, f))) return rc;
+        if (!fused) {
+            ECHECK(ifr::accept_greedy_fused(s->logits, nullptr, B, 0, c.vocab, s->acc, s->vtok + j, s->acc_scratch,
+                                            s->gcount, st, 1, kNMax),
+                   "draft argmax");
+            s->launches++;
+        }
+        s->launches++;  // prep
     }
     return IFR_OK;
 }
@@ -1082,6 +1107,8 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     chk(dalloc(s, &s->mtp_h, (size_t)B * d));
     chk(dalloc(s, &s->mtp_cat, (size_t)B * 2 * d));
     chk(dalloc(s, &s->gcount, B + 4));
+    chk(dalloc(s, &s->am_cand, (size_t)8 * 1024));
+    chk(dalloc(s, &s->am_count, 4));
     const int half = c.rotary_dim / 2;
     chk(dalloc(s, &s->rope_cos, (size_t)max_ctx * half));
     chk(dalloc(s, &s->rope_sin, (size_t)max_ctx * half));
@@ -1338,13 +1365,26 @@ int spec_step_device(ifr_state *s, int gamma, bool mtp, cudaStream_t st) {
     const int B = s->B;
     int rc = IFR_OK;
     if (gamma > 0 && mtp) rc = mtp_draft(s, gamma, st);
-    if (!rc) rc = target_forward(s, gamma + 1, true, true, st);
-    if (!rc) {
+    // greedy acceptance in the lm_head's epilogue when it runs as one small-N
+    // launch (one request), else its own launch
+    ifr::GemvArgmax am;
+    am.cand = s->am_cand;
+    am.counter = s->am_count;
+    am.drafts = s->vtok + 1;
+    am.draft_ld = kNMax;
+    am.G = gamma;
+    am.acc = s->acc;
+    am.out = s->outtok;
+    am.out_ld = gamma + 1;
+    const bool fused = lm_head_decides(s, B * (gamma + 1));
+    if (!rc) rc = target_forward(s, gamma + 1, true, true, st, fused ? &am : nullptr);
+    if (!rc && !fused) {
         rc = greedy_accept(s, s->vtok + 1, kNMax, B, gamma, s->outtok, gamma + 1, st);
+        s->launches++;
     }
     if (!rc)
         ifr::commit(s->sc, s->acc, s->outtok, gamma + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, B, st);
-    s->launches += 2;  // accept, commit
+    s->launches++;  // commit
     return rc;
 }
 }  // namespace

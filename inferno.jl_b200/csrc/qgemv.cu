@@ -118,7 +118,16 @@ struct GemvArgs {
     const float *xw;   // RMSNorm weights [K]
     float eps;
     int ep;            // 1: SwiGLU epilogue over interleaved gate/up 16-row blocks
+    GemvArgmax am;     // am.cand != null: greedy decision on Y in the epilogue
 };
+
+// order-preserving key of (value, row) for a 64-bit max: larger value first,
+// then the lower row
+IFR_DEV unsigned long long argmax_key(float v, int64_t row) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)row);
+}
 
 // ---- exact f32 activations on the fp16 tensor cores ----------------------------
 // Lane (g, t) feeds B column g of every step: activation column 4 nt + g/2,
@@ -808,6 +817,9 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
     // (rmsnorm_cpu!, ModelCPU.jl:111-123), applied while building B
     __shared__ float inv_s[8];
     __shared__ float part_s[CW][8];
+    __shared__ unsigned long long best_s[8];
+    __shared__ bool last_s;
+    if (tid < 8) best_s[tid] = 0ull;
     if (XF == 1) {
         float ss[8];
 #pragma unroll
@@ -956,19 +968,69 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
                 }
             }
         } else {
+            int bcol = -1;
+            unsigned long long bkey = 0ull;
             for (int i = tid; i < sw_rows * a.ncols; i += NTH) {
                 const int col = i / sw_rows, r = i % sw_rows;
                 if (row0 + r < a.M && !dead) {
                     float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
-                    *y = a.accumulate ? *y + accv(r, col) : accv(r, col);
+                    const float v = a.accumulate ? *y + accv(r, col) : accv(r, col);
+                    *y = v;
+                    if (a.am.cand) {
+                        if (col != bcol) {
+                            if (bcol >= 0) atomicMax(&best_s[bcol], bkey);
+                            bcol = col;
+                            bkey = 0ull;
+                        }
+                        const unsigned long long k = argmax_key(v, row0 + r);
+                        bkey = k > bkey ? k : bkey;
+                    }
                 }
             }
+            if (bcol >= 0) atomicMax(&best_s[bcol], bkey);
         }
         consumer_bar();
     }
     // stages issued but not consumed (only after a timeout) must land before exit
     if (tid == 0 && dead)
         for (int q = it; q < min(it + a.S, total); q++) mbar_wait(full + (q % a.S), (uint32_t)(q / a.S) & 1);
+    if (a.am.cand) {
+        // every CTA leaves its per-column best, then counts itself done; the
+        // CTA that finishes last (fenced counter, nothing waits) decides
+        __syncthreads();
+        if (tid < a.ncols) a.am.cand[tid * gridDim.x + blockIdx.x] = best_s[tid];
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last_s = atomicAdd(a.am.counter, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (last_s) {
+            __threadfence();
+            if (tid < a.ncols) {
+                unsigned long long b = 0ull;
+                for (unsigned c = 0; c < gridDim.x; c++) {
+                    const unsigned long long k = __ldcg(a.am.cand + tid * gridDim.x + c);
+                    b = k > b ? k : b;
+                }
+                best_s[tid] = b;
+            }
+            __syncthreads();
+            const int G1 = a.am.G + 1;
+            if (tid < a.ncols / G1) {
+                const int b = tid;
+                int32_t *ot = a.am.out + (int64_t)b * a.am.out_ld;
+                for (int i = 0; i < G1; i++) ot[i] = -1;
+                int accn = 0;
+                for (int i = 0; i < G1; i++) {
+                    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(best_s[b * G1 + i] & 0xFFFFFFFFull));
+                    ot[i] = tok;
+                    if (i == a.am.G || tok != a.am.drafts[(int64_t)b * a.am.draft_ld + i]) break;
+                    accn++;
+                }
+                if (a.am.acc) a.am.acc[b] = accn;
+            }
+            if (tid == 0) *a.am.counter = 0u;
+        }
+    }
 }
 
 static int num_sms() {
@@ -1020,7 +1082,8 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
         attr_set = true;
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
-               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
+               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep,
+               xf.am ? *xf.am : GemvArgmax()};
     return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a);
 }
 
@@ -1079,6 +1142,9 @@ cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, b
     if (ncols < 1 || ncols > 8) return cudaErrorInvalidValue;
     if (xf.kind < 0 || xf.kind > 2 || (xf.kind == 1 && !xf.w)) return cudaErrorInvalidValue;
     if (xf.ep && (accumulate || T.rows % 32)) return cudaErrorInvalidValue;
+    if (xf.am && (xf.ep || accumulate || !xf.am->cand || !xf.am->counter || !xf.am->out || xf.am->G < 0 ||
+                  ncols % (xf.am->G + 1) || (xf.am->G > 0 && !xf.am->drafts)))
+        return cudaErrorInvalidValue;
     if (xf.act != 0 && xf.act != 1) return cudaErrorInvalidValue;
     switch (T.type) {
     case 12: return launch_fmt<12>(T, X, ncols, Y, accumulate, ldy, s, xf);
