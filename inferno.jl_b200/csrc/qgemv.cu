@@ -118,8 +118,10 @@ struct GemvArgs {
     const float *xw;   // RMSNorm weights [K]
     float eps;
     int ep;            // 1: SwiGLU epilogue over interleaved gate/up 16-row blocks
-    GemvArgmax am;     // am.cand != null: greedy decision on Y in the epilogue
 };
+// the greedy decision's arguments, a kernel parameter of the AM variants only
+template <bool AM> struct AmArg { GemvArgmax am; };
+template <> struct AmArg<false> {};
 
 // order-preserving key of (value, row) for a 64-bit max: larger value first,
 // then the lower row
@@ -778,8 +780,10 @@ IFR_DEV void issue_stage(const GemvArgs &a, const Order &o, int q, uint8_t *ring
 // blocks x UW units); 1 halves each warp's serial work for small matrices
 // ACT: K-quant activations, 0 exact f32 (fp16 tensor cores), 1 Q8_K (integer
 // tensor cores, the reference's kernels); Q8_0 is always exact
-template <int FMT, int NT, int XF, int MPW, int ACT>
-__global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArgs a) {
+// AM: the greedy decision of GemvArgs::am in the epilogue (its own
+// instantiations, so the plain GEMVs carry none of its state)
+template <int FMT, int NT, int XF, int MPW, int ACT, bool AM>
+__global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArgs a, AmArg<AM> aa) {
     constexpr int CW = consumers<ACT>(), NTH = 32 * CW;
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int MTB = mtile_bytes(FMT);
@@ -817,9 +821,11 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
     // (rmsnorm_cpu!, ModelCPU.jl:111-123), applied while building B
     __shared__ float inv_s[8];
     __shared__ float part_s[CW][8];
-    __shared__ unsigned long long best_s[8];
+    __shared__ unsigned long long best_s[AM ? 8 : 1];
     __shared__ bool last_s;
-    if (tid < 8) best_s[tid] = 0ull;
+    if constexpr (AM) {
+        if (tid < 8) best_s[tid] = 0ull;
+    }
     if (XF == 1) {
         float ss[8];
 #pragma unroll
@@ -864,16 +870,11 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
             if constexpr (kI8) {
                 if (active) build_b_i8<FMT, XF>(a, inv_s, u, lane, F);
             } else {
-                // the warps split the pass's (unit, n-tile) builds; the previous
-                // pass's fragments were last read before the barrier that closed
-                // its final stage
-                for (int task = warp; task < UW * NT; task += CW) {
-                    const int bu = task % UW;
-                    const int64_t uu = (int64_t)p * UW + bu;
-                    if (uu < a.nu)
-                        build_b<FMT, NT, XF>(a, inv_s, uu, lane, task / UW, bsm + bu * bunit_words(NT),
-                                             sw == o.rg_lo ? ssq : nullptr);
-                }
+                // the unit's warps split its n-tiles (UW divides the warps); the
+                // previous pass's fragments were last read before the barrier
+                // that closed its final stage
+                if (active && mp < NT)
+                    build_b<FMT, NT, XF>(a, inv_s, u, lane, mp, bsm + ui * bunit_words(NT), sw == o.rg_lo ? ssq : nullptr);
                 consumer_bar();
                 F.at(bsm + ui * bunit_words(NT), lane);
             }
@@ -893,7 +894,7 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
 #pragma unroll
                     for (int mm = 0; mm < MPW; mm++) {
                         const int m = MPW * mp + mm;
-                        if (m < MTG && rg * MTG + m < a.nrb) {
+                        if (rg * MTG + m < a.nrb) {
                             const uint8_t *tile = st + (size_t)(m * UW + ui) * MTB;
                             if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot[mm]);
                             else if constexpr (kI8 && FMT == 14) mtile_q6_i8(tile, lane, F, tot[mm][0]);
@@ -968,15 +969,14 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
                 }
             }
         } else {
-            int bcol = -1;
-            unsigned long long bkey = 0ull;
-            for (int i = tid; i < sw_rows * a.ncols; i += NTH) {
-                const int col = i / sw_rows, r = i % sw_rows;
-                if (row0 + r < a.M && !dead) {
-                    float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
-                    const float v = a.accumulate ? *y + accv(r, col) : accv(r, col);
-                    *y = v;
-                    if (a.am.cand) {
+            if constexpr (AM) {
+                int bcol = -1;
+                unsigned long long bkey = 0ull;
+                for (int i = tid; i < sw_rows * a.ncols; i += NTH) {
+                    const int col = i / sw_rows, r = i % sw_rows;
+                    if (row0 + r < a.M && !dead) {
+                        const float v = accv(r, col);
+                        a.Y[(int64_t)col * a.ldy + row0 + r] = v;
                         if (col != bcol) {
                             if (bcol >= 0) atomicMax(&best_s[bcol], bkey);
                             bcol = col;
@@ -986,49 +986,57 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
                         bkey = k > bkey ? k : bkey;
                     }
                 }
+                if (bcol >= 0) atomicMax(&best_s[bcol], bkey);
+            } else {
+                for (int i = tid; i < sw_rows * a.ncols; i += NTH) {
+                    const int col = i / sw_rows, r = i % sw_rows;
+                    if (row0 + r < a.M && !dead) {
+                        float *y = a.Y + (int64_t)col * a.ldy + row0 + r;
+                        *y = a.accumulate ? *y + accv(r, col) : accv(r, col);
+                    }
+                }
             }
-            if (bcol >= 0) atomicMax(&best_s[bcol], bkey);
         }
         consumer_bar();
     }
     // stages issued but not consumed (only after a timeout) must land before exit
     if (tid == 0 && dead)
         for (int q = it; q < min(it + a.S, total); q++) mbar_wait(full + (q % a.S), (uint32_t)(q / a.S) & 1);
-    if (a.am.cand) {
+    if constexpr (AM) {
         // every CTA leaves its per-column best, then counts itself done; the
         // CTA that finishes last (fenced counter, nothing waits) decides
         __syncthreads();
-        if (tid < a.ncols) a.am.cand[tid * gridDim.x + blockIdx.x] = best_s[tid];
+        if (tid < a.ncols) aa.am.cand[tid * gridDim.x + blockIdx.x] = best_s[tid];
         __threadfence();
         __syncthreads();
-        if (tid == 0) last_s = atomicAdd(a.am.counter, 1u) == gridDim.x - 1;
+        if (tid == 0) last_s = atomicAdd(aa.am.counter, 1u) == gridDim.x - 1;
         __syncthreads();
         if (last_s) {
             __threadfence();
             if (tid < a.ncols) {
                 unsigned long long b = 0ull;
                 for (unsigned c = 0; c < gridDim.x; c++) {
-                    const unsigned long long k = __ldcg(a.am.cand + tid * gridDim.x + c);
+                    const unsigned long long k = __ldcg(aa.am.cand + tid * gridDim.x + c);
                     b = k > b ? k : b;
                 }
                 best_s[tid] = b;
             }
             __syncthreads();
-            const int G1 = a.am.G + 1;
+            const int G1 = aa.am.G + 1;
             if (tid < a.ncols / G1) {
                 const int b = tid;
-                int32_t *ot = a.am.out + (int64_t)b * a.am.out_ld;
+                int32_t *ot = aa.am.out + (int64_t)b * aa.am.out_ld;
                 for (int i = 0; i < G1; i++) ot[i] = -1;
                 int accn = 0;
                 for (int i = 0; i < G1; i++) {
                     const int tok = (int)(0xFFFFFFFFu - (uint32_t)(best_s[b * G1 + i] & 0xFFFFFFFFull));
                     ot[i] = tok;
-                    if (i == a.am.G || tok != a.am.drafts[(int64_t)b * a.am.draft_ld + i]) break;
+                    if (i == aa.am.G || tok != aa.am.drafts[(int64_t)b * aa.am.draft_ld + i]) break;
                     accn++;
                 }
-                if (a.am.acc) a.am.acc[b] = accn;
+                if (aa.am.acc) aa.am.acc[b] = accn;
             }
-            if (tid == 0) *a.am.counter = 0u;
+            if (tid == 0) *aa.am.counter = 0u;
         }
     }
 }
@@ -1044,7 +1052,7 @@ static int num_sms() {
     return n;
 }
 
-template <int FMT, int NT, int XF, int MPW, int ACT>
+template <int FMT, int NT, int XF, int MPW, int ACT, bool AM>
 static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                               cudaStream_t s, const XForm &xf, int UW) {
     constexpr int MTB = mtile_bytes(FMT);
@@ -1073,18 +1081,19 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     if (smem > kSmemMax) return cudaErrorInvalidConfiguration;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT>,
+        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+        e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
-               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep,
-               xf.am ? *xf.am : GemvArgmax()};
-    return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a);
+               sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
+    AmArg<AM> aa{};
+    if constexpr (AM) aa.am = *xf.am;
+    return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a, aa);
 }
 
 // Work split: UW warps share each row block's units.  A stage: 16 warps x 1
@@ -1109,7 +1118,8 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
                          (XF == 3 ? (int)T.nu * 8 * 4 : 0);
         if (need <= kSmemMax) break;
     }
-    return launch_mpw<FMT, NT, XF, MPW, ACT>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
+    if (xf.am) return launch_mpw<FMT, NT, XF, MPW, ACT, true>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
+    return launch_mpw<FMT, NT, XF, MPW, ACT, false>(T, X, ncols, Y, accumulate, ldy, s, xf, UW);
 }
 
 template <int FMT, int NT, int XF>
