@@ -1041,6 +1041,212 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
     }
 }
 
+// ---- tall matrices, exact activations: one row block per warp --------------
+// For matrices of many row blocks (lm_heads, 151936 rows) a consumer warp owns
+// a whole row block over all of K, so its sums stay in registers and go
+// straight to Y: no per-stage block barrier and no shared-memory reduction.
+// The B fragments of every unit are built once per CTA.  Warp 15 produces:
+// stage q = (row group g, unit u) is the 15 M-tiles of rows blocks
+// 15 g .. 15 g + 14 at unit u, copied with cp.async.bulk into a ring of S
+// slots; full barriers count the bytes, empty barriers count the 15 consumer
+// warps.  Every wait is bounded; after a timeout the kernel drains its copies
+// and returns (IFR_ERR_TIMEOUT on the host).
+constexpr int kRowsCW = 15;  // consumer warps (and row blocks per group)
+
+template <int FMT, int NT, int XF, bool AM>
+__global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM> aa) {
+    constexpr int MTB = mtile_bytes(FMT);
+    constexpr int STAGE = kRowsCW * MTB;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + 8;
+    uint8_t *ring = smem + 128;
+    uint32_t *bsm = reinterpret_cast<uint32_t *>(ring + (size_t)a.S * STAGE);
+    float *ssq = reinterpret_cast<float *>(bsm + (size_t)a.nu * bunit_words(NT));  // XF 3: [nu][8]
+    __shared__ float inv_s[8];
+    __shared__ float part_s[16][8];
+    __shared__ unsigned long long best_s[AM ? 8 : 1];
+    __shared__ bool last_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ngr = (a.nrb + kRowsCW - 1) / kRowsCW;
+    const int g_lo = (int)((int64_t)blockIdx.x * ngr / gridDim.x);
+    const int g_hi = (int)((int64_t)(blockIdx.x + 1) * ngr / gridDim.x);
+    const int total = (g_hi - g_lo) * a.nu;
+    if constexpr (AM) {
+        if (tid < 8) best_s[tid] = 0ull;
+    }
+    auto issue = [&](int q) {  // one thread: stage q into its slot
+        const int slot = q % a.S;
+        const int g = g_lo + q / a.nu, u = q % a.nu;
+        const int nrow = min(kRowsCW, a.nrb - g * kRowsCW);
+        fence_proxy_async();
+        mbar_expect_tx(full + slot, (uint32_t)(nrow * MTB));
+        for (int w = 0; w < nrow; w++) {
+            const uint8_t *src = a.W + ((int64_t)(g * kRowsCW + w) * a.nu + u) * MTB;
+            bulk_g2s(ring + (size_t)slot * STAGE + (size_t)w * MTB, src, (uint32_t)MTB, full + slot);
+        }
+    };
+    pdl_trigger();
+    // the weights are constant: the first stages stream in before the
+    // previous kernel (producer of X) has finished
+    if (tid == 0) {
+        for (int s = 0; s < a.S; s++) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kRowsCW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int q = 0; q < min(a.S, total); q++) issue(q);
+    }
+    pdl_wait();
+    if (XF == 1) {  // RMSNorm of the input columns (rmsnorm_cpu!, ModelCPU.jl:111-123)
+        float ss[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) ss[c] = 0.f;
+        for (int64_t k = 4 * tid; k < a.K; k += 4 * 512) {
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                if (c < a.ncols) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(a.X + c * a.ldx + k));
+                    ss[c] += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+                }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            float v = ss[c];
+#pragma unroll
+            for (int o2 = 16; o2; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
+            if (lane == 0) part_s[warp][c] = v;
+        }
+        __syncthreads();
+        if (tid < 8) {
+            float v = 0.f;
+            for (int w = 0; w < 16; w++) v += part_s[w][tid];
+            inv_s[tid] = 1.0f / sqrtf(v / (float)a.K + a.eps);
+        }
+        __syncthreads();
+    }
+    // every unit's fragments, once per CTA
+    for (int task = warp; task < a.nu * NT; task += 16)
+        build_b<FMT, NT, XF>(a, inv_s, task % a.nu, lane, task / a.nu, bsm + (size_t)(task % a.nu) * bunit_words(NT), ssq);
+    __syncthreads();
+    if (XF == 3) {  // W (x w) / rms(x) per column; the sums of squares in unit order
+        if (tid < 8) {
+            float v = 0.f;
+            if (tid < a.ncols)
+                for (int uu = 0; uu < a.nu; uu++) v += ssq[uu * 8 + tid];
+            inv_s[tid] = tid < a.ncols ? 1.0f / sqrtf(v / (float)a.K + a.eps) : 0.f;
+        }
+        __syncthreads();
+    }
+    bool dead = false;
+    if (warp == kRowsCW) {
+        // producer: refill each slot once its 15 consumers have released it
+        if (lane == 0) {
+            int q = min(a.S, total);  // stages issued so far
+            while (q < total) {
+                if (!mbar_wait(empty + (q % a.S), (uint32_t)((q / a.S) - 1) & 1)) break;
+                issue(q++);
+            }
+            // the last copy into each slot has landed before the CTA exits
+            // (consumed ones return at once)
+            for (int r = max(0, q - a.S); r < q; r++) mbar_wait(full + (r % a.S), (uint32_t)(r / a.S) & 1);
+        }
+    } else {
+        const int g = lane >> 2, t = lane & 3;
+        unsigned long long best[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) best[nt] = 0ull;
+        int q = 0;
+        for (int gr = g_lo; gr < g_hi; gr++) {
+            const int rb = gr * kRowsCW + warp;
+            float tot[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) tot[nt][i] = 0.f;
+            for (int u = 0; u < a.nu; u++, q++) {
+                const int slot = q % a.S;
+                if (!dead && !mbar_wait(full + slot, (uint32_t)(q / a.S) & 1)) dead = true;
+                if (!dead && rb < a.nrb) {
+                    BView<NT> F;
+                    F.at(bsm + (size_t)u * bunit_words(NT), lane);
+                    const uint8_t *tile = ring + (size_t)slot * STAGE + (size_t)warp * MTB;
+                    if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot);
+                    else if constexpr (FMT == 14) mtile_q6_h<NT>(tile, lane, F, tot);
+                    else mtile_qk_h<FMT == 13, NT>(tile, lane, F, tot);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + slot);
+            }
+            if (rb < a.nrb && !dead) {
+                // C columns 2t, 2t+1 of n-tile nt: hi and lo parts of column 4 nt + t
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    const int col = 4 * nt + t;
+                    if (col >= a.ncols) continue;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int64_t row = (int64_t)rb * 16 + g + 8 * h;
+                        if (row >= a.M) continue;
+                        float v = tot[nt][2 * h] + tot[nt][2 * h + 1];
+                        if (XF == 3) v *= inv_s[col];
+                        float *y = a.Y + (int64_t)col * a.ldy + row;
+                        if (a.accumulate) v += *y;
+                        *y = v;
+                        if constexpr (AM) {
+                            const unsigned long long k = argmax_key(v, row);
+                            best[nt] = k > best[nt] ? k : best[nt];
+                        }
+                    }
+                }
+            }
+        }
+        if constexpr (AM) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+                if (4 * nt + t < a.ncols) atomicMax(&best_s[4 * nt + t], best[nt]);
+        }
+    }
+    if constexpr (AM) {
+        // every CTA leaves its per-column best, then counts itself done; the
+        // CTA that finishes last (fenced counter, nothing waits) decides
+        __syncthreads();
+        if (tid < a.ncols) aa.am.cand[tid * gridDim.x + blockIdx.x] = best_s[tid];
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last_s = atomicAdd(aa.am.counter, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (last_s) {
+            __threadfence();
+            if (tid < a.ncols) {
+                unsigned long long b = 0ull;
+                for (unsigned c = 0; c < gridDim.x; c++) {
+                    const unsigned long long k = __ldcg(aa.am.cand + tid * gridDim.x + c);
+                    b = k > b ? k : b;
+                }
+                best_s[tid] = b;
+            }
+            __syncthreads();
+            const int G1 = aa.am.G + 1;
+            if (tid < a.ncols / G1) {
+                const int b = tid;
+                int32_t *ot = aa.am.out + (int64_t)b * aa.am.out_ld;
+                for (int i = 0; i < G1; i++) ot[i] = -1;
+                int accn = 0;
+                for (int i = 0; i < G1; i++) {
+                    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(best_s[b * G1 + i] & 0xFFFFFFFFull));
+                    ot[i] = tok;
+                    if (i == aa.am.G || tok != aa.am.drafts[(int64_t)b * aa.am.draft_ld + i]) break;
+                    accn++;
+                }
+                if (aa.am.acc) aa.am.acc[b] = accn;
+            }
+            if (tid == 0) *aa.am.counter = 0u;
+        }
+    }
+}
+
 static int num_sms() {
     static int n = 0;
     if (n == 0) {
@@ -1096,6 +1302,38 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a, aa);
 }
 
+// Tall matrices (>= 2 row groups of 15 row blocks per SM) with exact
+// activations and no SwiGLU epilogue take the row-block-per-warp kernel when
+// every unit's fragments and two ring slots fit in shared memory; returns
+// cudaErrorNotSupported (nothing launched) otherwise.
+template <int FMT, int NT, int XF, bool AM>
+static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                               cudaStream_t s, const XForm &xf) {
+    constexpr int MTB = mtile_bytes(FMT);
+    constexpr int STAGE = kRowsCW * MTB;
+    constexpr int kSmemMax = 226 * 1024;
+    const int64_t ngr = (T.nrb + kRowsCW - 1) / kRowsCW;
+    if (xf.ep || ngr < 2 * num_sms()) return cudaErrorNotSupported;
+    const int fixed = 128 + (int)T.nu * bunit_words(NT) * 4 + (XF == 3 ? (int)T.nu * 8 * 4 : 0);
+    int S = (kSmemMax - fixed) / STAGE;
+    if (S < 2) return cudaErrorNotSupported;
+    if (S > 8) S = 8;
+    const int smem = fixed + S * STAGE;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(qgemv_rows_kernel<FMT, NT, XF, AM>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int grid = num_sms();
+    GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, 0, S,
+               0, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
+    AmArg<AM> aa{};
+    if constexpr (AM) aa.am = *xf.am;
+    return launch_k(qgemv_rows_kernel<FMT, NT, XF, AM>, dim3(grid), dim3(512), (size_t)smem, s, a, aa);
+}
+
 // Work split: UW warps share each row block's units.  A stage: 16 warps x 1
 // M-tile (exact activations: the fragments of UW units take shared memory),
 // 16 warps x 2 (Q8_K activations; x 1 for Q6_K, whose larger tiles would leave
@@ -1108,6 +1346,11 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     constexpr bool kExact = FMT == 8 || ACT == 0;
     constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
     constexpr int CW = consumers<ACT>();
+    if constexpr (kExact && XF != 2) {
+        const cudaError_t e = xf.am ? launch_rows<FMT, NT, XF, true>(T, X, ncols, Y, accumulate, ldy, s, xf)
+                                    : launch_rows<FMT, NT, XF, false>(T, X, ncols, Y, accumulate, ldy, s, xf);
+        if (e != cudaErrorNotSupported) return e;
+    }
     constexpr int kSmemMax = 226 * 1024;
     int UW = 1;
     while (UW < 8 && UW * 2 <= T.nu) UW *= 2;

@@ -236,3 +236,32 @@ def test_argument_errors(O, ctx, pkg):
     assert L.ifr_weights_upload(ctx.handle, 12, qp, 0, 256, ctypes.byref(h)) == 1   # rows
     W = ctx.upload(12, q, 4, 256)
     assert L.ifr_qgemm(ctx.handle, W.handle, ctypes.c_void_p(16), 0, ctypes.c_void_p(16)) == 1
+
+
+# tall matrices (>= 2 x 148 groups of 15 row blocks): the row-block-per-warp
+# kernel, which keeps every unit's fragments in shared memory; Q6_K and Q8_0 at
+# K = 4096 with 5+ columns do not fit it and take the unit-split kernel
+TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (14, 4096)]
+
+
+@pytest.mark.parametrize("qt,K", TALL)
+def test_qgemm_tall(O, ctx, qt, K):
+    torch = _torch()
+    M = 71040 + 37  # ragged last row block and group
+    rng = np.random.default_rng(qt * 31 + K)
+    pool = O.quantize(qt, rng.normal(0, 0.02, (512, K)).astype(np.float32))
+    rb = pool.size // 512
+    q = pool.reshape(512, rb)[np.arange(M) % 512].ravel()
+    W = ctx.upload(qt, q, M, K)
+    X = rng.normal(0, 1, (8, K)).astype(np.float32)
+    ref = O.gemm_ref(qt, pool, 512, K, X)  # rows repeat with period 512
+    idx = np.arange(M) % 512
+    Xd = torch.from_numpy(X).cuda()
+    for n in (1, 5, 8):
+        Y = ctx.qgemm(W, Xd[:n].contiguous()).cpu().numpy()
+        err = O.norm_rel(Y, ref[:n][:, idx])
+        assert err.max() < TOL, (NAMES[qt], K, n, err)
+    w = (1.0 + rng.normal(0, 0.2, K)).astype(np.float32)
+    Yn = ctx.qgemm_rmsnorm(W, Xd[:5].contiguous(), torch.from_numpy(w).cuda(), 1e-6).cpu().numpy()
+    refn = O.gemm_ref(qt, pool, 512, K, _rmsnorm(X[:5], w, 1e-6))
+    assert O.norm_rel(Yn, refn[:, idx]).max() < 5 * TOL
