@@ -1304,7 +1304,7 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
 
 // Tall matrices (>= 2 row groups of 15 row blocks per SM) with exact
 // activations and no SwiGLU epilogue take the row-block-per-warp kernel when
-// every unit's fragments and two ring slots fit in shared memory; returns
+// every unit's fragments and three ring slots fit in shared memory; returns
 // cudaErrorNotSupported (nothing launched) otherwise.
 template <int FMT, int NT, int XF, bool AM>
 static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
@@ -1316,7 +1316,7 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
     if (xf.ep || ngr < 2 * num_sms()) return cudaErrorNotSupported;
     const int fixed = 128 + (int)T.nu * bunit_words(NT) * 4 + (XF == 3 ? (int)T.nu * 8 * 4 : 0);
     int S = (kSmemMax - fixed) / STAGE;
-    if (S < 2) return cudaErrorNotSupported;
+    if (S < 3) return cudaErrorNotSupported;  // two one-unit stages hide too little DRAM latency (measured)
     if (S > 8) S = 8;
     const int smem = fixed + S * STAGE;
     static bool attr_set = false;

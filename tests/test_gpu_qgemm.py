@@ -239,8 +239,9 @@ def test_argument_errors(O, ctx, pkg):
 
 
 # tall matrices (>= 2 x 148 groups of 15 row blocks): the row-block-per-warp
-# kernel, which keeps every unit's fragments in shared memory; Q6_K and Q8_0 at
-# K = 4096 with 5+ columns do not fit it and take the unit-split kernel
+# kernel, which keeps every unit's fragments in shared memory (K = 1024); at
+# K = 4096 with 5+ columns three ring slots no longer fit beside them and the
+# unit-split kernel runs (N = 1 of Q4_K still takes the row kernel)
 TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (14, 4096)]
 
 
