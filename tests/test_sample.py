@@ -136,11 +136,11 @@ FILTERS = [
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("V", [7, 2048, 5000, 151936])
+@pytest.mark.parametrize("V", [7, 2048, 5000, 151936, 262144])
 @pytest.mark.parametrize("kw", FILTERS, ids=lambda d: ",".join(f"{k}={v}" for k, v in d.items()))
 def test_sample_bit_exact(O, ctx, V, kw):
     rng = np.random.default_rng(V + 7 * len(kw))
-    rows = 12 if V > 100000 else 24
+    rows = 6 if V > 200000 else (12 if V > 100000 else 24)
     logits = rng.normal(0, 3, (rows, V)).astype(np.float32)
     u = rng.random(rows, dtype=np.float32)
     u[0] = 0.0
