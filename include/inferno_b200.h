@@ -284,6 +284,26 @@ int ifr_spec_graph_launch(ifr_state *s);
  * `steps` such steps into the target state's graph (ifr_spec_graph_launch). */
 int ifr_spec_step_draft(ifr_state *target, ifr_state *draft, int gamma);
 int ifr_spec_graph_draft(ifr_state *target, ifr_state *draft, int gamma, int steps);
+/* The step in parts, for acceptance decided by the caller (e.g. sampled with
+ * ifr_accept): speculate_and_verify (src/SpeculativeDecoding.jl:37-104) as
+ * draft, verify, accept, commit.
+ * ifr_draft_mtp: gamma (1..7) greedy MTP draft tokens per request into the
+ * state (the input of the next ifr_verify_step with drafts == NULL); copied
+ * to drafts_out [batch][gamma] (host) when given (synchronizes).
+ * ifr_verify_step: the target forward over [last token, drafts] (drafts host
+ * [batch][gamma], or NULL for the state's MTP drafts) at the state's position
+ * (ModelCPU.jl:2099-2115); logits [batch][gamma+1][vocab] (device) copied to
+ * logits_out when given.  Nothing is committed: KV entries of the columns are
+ * written, the GatedDeltaNet state is not advanced.
+ * ifr_rollback: commits accept_count[b] (0..gamma) drafts and the emitted
+ * token of request b: tokens [batch][gamma+1] (host), tokens[b][0..a] with
+ * a = accept_count[b] the accepted drafts then the correction or bonus token.
+ * The rest of the verify is rolled back (the SSM state replays only the
+ * accepted columns; later KV entries are overwritten).  Each verify needs its
+ * rollback before the next draft, verify or spec step (IFR_ERR_ARG). */
+int ifr_draft_mtp(ifr_state *s, int gamma, int32_t *drafts_out);
+int ifr_verify_step(ifr_state *s, int gamma, const int32_t *drafts, float *logits_out);
+int ifr_rollback(ifr_state *s, const int32_t *accept_count, const int32_t *tokens);
 /* per-launch CUDA-event timing of the state's work (0 = off, default), and
  * its totals per category since enabling: 0 verify lm_head, 1 draft lm_head,
  * 2 decoder-layer GEMVs, 3 draft GEMVs, 4 SSM steps, 5 attention steps

@@ -48,6 +48,9 @@ SIGNATURES = {
     "ifr_accept_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
     "ifr_accept_greedy": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "ifr_sample": (_i, [_vp, _vp, _i, _i, _f, _i, _f, _f, _vp, _vp]),
+    "ifr_draft_mtp": (_i, [_vp, _i, _vp]),
+    "ifr_verify_step": (_i, [_vp, _i, _vp, _vp]),
+    "ifr_rollback": (_i, [_vp, _vp, _vp]),
     "ifr_apply_penalties": (_i, [_vp, _vp, _i, _i, _vp, _i, _f, _f]),
     "ifr_model_load_gguf": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "ifr_model_load_gguf_tp": (_i, [_vp, ctypes.c_char_p, _vp, ctypes.POINTER(_vp)]),

@@ -468,6 +468,7 @@ struct ifr_state {
     void *dense = nullptr;              // scratch of the dense tensor-core GEMMs
     int64_t dense_bytes = 0;
     int last_n = 0;
+    int pending = -1;                   // gamma of a verify awaiting ifr_rollback, else -1
     // kernel launches enqueued (for the benchmark's launch count)
     int64_t launches = 0;
     // optional per-category CUDA-event timing of the launches
@@ -1228,6 +1229,7 @@ int ifr_state_reset(ifr_state *s) {
     init.a_prev = -1;
     std::vector<ifr::EngineScalars> all(s->B, init);
     ECHECK(cudaStreamSynchronize(st), "reset");
+    s->pending = -1;
     ECHECK(cudaMemcpy(s->sc, all.data(), sizeof(init) * s->B, cudaMemcpyHostToDevice), "reset scalars");
     for (int i = 0; i < c.n_layers; i++)
         if (s->S[i]) {
@@ -1257,6 +1259,7 @@ int ifr_prefill(ifr_state *s, const int32_t *tokens, int n, int32_t *first_token
 // to kNMax tokens per request; the last token alone, with logits
 int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first_tokens) {
     if (!s || !tokens || n < 1) return ifr_fail(IFR_ERR_ARG, "invalid prefill arguments");
+    if (s->pending >= 0) return ifr_fail(IFR_ERR_ARG, "a verify awaits ifr_rollback");
     const ifr_model_info &c = s->m->info;
     const int B = s->B;
     for (int64_t i = 0; i < (int64_t)B * n; i++)
@@ -1393,6 +1396,7 @@ extern "C" {
 
 int ifr_spec_step(ifr_state *s, int gamma, const int32_t *drafts) {
     if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (s->pending >= 0) return ifr_fail(IFR_ERR_ARG, "a verify awaits ifr_rollback");
     if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
     if (gamma > 0 && !drafts && !s->m->has_mtp) return ifr_fail(IFR_ERR_ARG, "no drafts given and the model has no MTP head");
     const ifr_model_info &c = s->m->info;
@@ -1482,6 +1486,101 @@ int ifr_spec_graph_draft(ifr_state *t, ifr_state *d, int gamma, int steps) {
     return rc;
 }
 
+// ---- the step in parts: draft, verify, acceptance by the caller, commit ----
+int ifr_draft_mtp(ifr_state *s, int gamma, int32_t *drafts_out) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (gamma < 1 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 1..%d", kNMax - 1);
+    if (!s->m->has_mtp) return ifr_fail(IFR_ERR_ARG, "the model has no MTP head");
+    if (s->pending >= 0) return ifr_fail(IFR_ERR_ARG, "a verify awaits ifr_rollback");
+    const int B = s->B;
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    int rc = mtp_draft(s, gamma, st);
+    if (!rc && drafts_out) {
+        cudaError_t e = cudaMemcpy2DAsync(drafts_out, sizeof(int32_t) * gamma, s->vtok + 1, sizeof(int32_t) * kNMax,
+                                          sizeof(int32_t) * gamma, B, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "D2H drafts");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int ifr_verify_step(ifr_state *s, int gamma, const int32_t *drafts, float *logits_out) {
+    if (!s) return ifr_fail(IFR_ERR_ARG, "NULL state");
+    if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
+    if (s->pending >= 0) return ifr_fail(IFR_ERR_ARG, "a verify awaits ifr_rollback");
+    const ifr_model_info &c = s->m->info;
+    const int B = s->B;
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    int rc = IFR_OK;
+    if (gamma > 0 && drafts) {
+        for (int64_t i = 0; i < (int64_t)B * gamma; i++)
+            if (drafts[i] < 0 || drafts[i] >= c.vocab) { cudaSetDevice(prev); return ifr_fail(IFR_ERR_ARG, "draft token out of range"); }
+        cudaError_t e = cudaStreamSynchronize(st);  // staging buffer reuse
+        for (int b = 0; b < B && e == cudaSuccess; b++) {
+            memcpy(s->h_tok + (int64_t)b * kNMax + 1, drafts + (int64_t)b * gamma, sizeof(int32_t) * gamma);
+            e = cudaMemcpyAsync(s->vtok + (int64_t)b * kNMax + 1, s->h_tok + (int64_t)b * kNMax + 1,
+                                sizeof(int32_t) * gamma, cudaMemcpyHostToDevice, st);
+        }
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "H2D drafts");
+    }
+    if (!rc) rc = target_forward(s, gamma + 1, true, true, st);
+    if (!rc && logits_out) {
+        cudaError_t e = cudaMemcpyAsync(logits_out, s->logits, sizeof(float) * B * (gamma + 1) * s->m->vocab,
+                                        cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "logits copy");
+    }
+    if (!rc) s->pending = gamma;
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int ifr_rollback(ifr_state *s, const int32_t *accept_count, const int32_t *tokens) {
+    if (!s || !accept_count || !tokens) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    if (s->pending < 0) return ifr_fail(IFR_ERR_ARG, "no verify awaits ifr_rollback");
+    const ifr_model_info &c = s->m->info;
+    const int B = s->B, G = s->pending;
+    for (int b = 0; b < B; b++) {
+        const int a = accept_count[b];
+        if (a < 0 || a > G) return ifr_fail(IFR_ERR_ARG, "accept count %d of request %d outside 0..%d", a, b, G);
+        for (int i = 0; i <= a; i++) {
+            const int t = tokens[(int64_t)b * (G + 1) + i];
+            if (t < 0 || t >= c.vocab) return ifr_fail(IFR_ERR_ARG, "token %d out of range", t);
+        }
+    }
+    cudaStream_t st = ifr_ctx_stream_of(s->m->ctx);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ifr_ctx_device(s->m->ctx));
+    int rc = IFR_OK;
+    // staged through the pinned buffer (B * kNMax + 64 ints): tokens, then counts
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) {
+        memcpy(s->h_tok, tokens, sizeof(int32_t) * B * (G + 1));
+        e = cudaMemcpyAsync(s->outtok, s->h_tok, sizeof(int32_t) * B * (G + 1), cudaMemcpyHostToDevice, st);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) {
+        memcpy(s->h_tok, accept_count, sizeof(int32_t) * B);
+        e = cudaMemcpyAsync(s->acc, s->h_tok, sizeof(int32_t) * B, cudaMemcpyHostToDevice, st);
+    }
+    if (e != cudaSuccess) rc = ifr_cuda_fail(e, "H2D acceptance");
+    if (!rc) {
+        ifr::commit(s->sc, s->acc, s->outtok, G + 1, false, s->hid, s->mtp_h, c.hidden, s->log, s->log_cap, B, st);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) rc = ifr_cuda_fail(e, "commit");
+        else s->pending = -1;
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
 int ifr_spec_graph(ifr_state *s, int gamma, int steps) {
     if (!s || steps < 1) return ifr_fail(IFR_ERR_ARG, "invalid graph arguments");
     if (gamma < 0 || gamma + 1 > kNMax) return ifr_fail(IFR_ERR_ARG, "gamma must be in 0..%d", kNMax - 1);
@@ -1514,6 +1613,7 @@ int ifr_spec_graph(ifr_state *s, int gamma, int steps) {
 
 int ifr_spec_graph_launch(ifr_state *s) {
     if (!s || !s->graph_exec) return ifr_fail(IFR_ERR_ARG, "no captured graph (call ifr_spec_graph first)");
+    if (s->pending >= 0) return ifr_fail(IFR_ERR_ARG, "a verify awaits ifr_rollback");
     ECHECK(cudaGraphLaunch(s->graph_exec, ifr_ctx_stream_of(s->m->ctx)), "graph launch");
     return IFR_OK;
 }

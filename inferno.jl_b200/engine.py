@@ -131,6 +131,28 @@ class State:
         same context) decodes gamma tokens -> verify -> accept -> commit"""
         check(load().ifr_spec_step_draft(self.handle, draft.handle, int(gamma)))
 
+    def draft_mtp(self, gamma):
+        """greedy MTP drafts [batch][gamma] (synchronizes)"""
+        d = np.empty((self.batch, gamma), np.int32)
+        check(load().ifr_draft_mtp(self.handle, int(gamma), d.ctypes.data_as(ctypes.c_void_p)))
+        return d
+
+    def verify_step(self, gamma, drafts=None, logits_out=None):
+        """target forward over [last, drafts]; logits_out: a device tensor of
+        batch * (gamma + 1) * vocab f32 (torch), or None"""
+        d = None
+        if drafts is not None:
+            d = np.ascontiguousarray(drafts, dtype=np.int32)
+            assert d.size == gamma * self.batch
+        check(load().ifr_verify_step(self.handle, int(gamma), d.ctypes.data_as(ctypes.c_void_p) if d is not None else None,
+                                     ctypes.c_void_p(logits_out.data_ptr()) if logits_out is not None else None))
+
+    def rollback(self, accept_count, tokens):
+        """commit accept_count[b] drafts + the emitted token of each request"""
+        a = np.ascontiguousarray(accept_count, dtype=np.int32).reshape(self.batch)
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(self.batch, -1)
+        check(load().ifr_rollback(self.handle, a.ctypes.data_as(ctypes.c_void_p), t.ctypes.data_as(ctypes.c_void_p)))
+
     def capture_draft(self, draft, gamma, steps):
         check(load().ifr_spec_graph_draft(self.handle, draft.handle, int(gamma), int(steps)))
 

@@ -133,3 +133,65 @@ def test_config1_tiny_model_matches_oracle(O, pkg, ctx):
     toks, *_ = st.read()
     assert list(toks) == out_o
     del om
+
+
+def test_step_in_parts_matches_fused_step(mini):
+    """ifr_draft_mtp + ifr_verify_step + the caller's greedy acceptance (host
+    argmax of the returned logits) + ifr_rollback reproduce ifr_spec_step:
+    same drafts, logits, emitted tokens and positions"""
+    import torch
+    model, om, prompt = mini
+    G, steps = 4, 5
+    a, b = _state(model), _state(model)
+    a.prefill(prompt)
+    b.prefill(prompt)
+    V = model.info.vocab
+    lg = torch.empty((G + 1) * V, dtype=torch.float32, device="cuda")
+    for s in range(steps):
+        a.spec_step(G)
+        la, _, ta = a.last_verify()
+        d = b.draft_mtp(G)
+        b.verify_step(G, None, lg)
+        lb = lg.view(G + 1, V).cpu().numpy()
+        assert list(d[0]) == list(ta[1:]), (s, d, ta)
+        assert np.array_equal(lb, la), s
+        am = lb.argmax(axis=1)
+        acc = 0
+        while acc < G and am[acc] == d[0][acc]:
+            acc += 1
+        toks = np.full(G + 1, -1, np.int32)
+        toks[:acc] = d[0][:acc]
+        toks[acc] = am[acc]
+        b.rollback([acc], toks[None])
+        ra, rb = a.read(), b.read()
+        assert list(ra[0]) == list(rb[0]) and ra[1:] == rb[1:], (s, ra, rb)
+
+
+def test_step_in_parts_forced_and_errors(mini):
+    """caller-chosen drafts and acceptance: a rejection at the first draft with
+    a token of the caller's choice, then the fused step continues from it;
+    out-of-order calls are rejected"""
+    from inferno_b200._lib import IfrError
+    model, om, prompt = mini
+    G = 3
+    st = _state(model)
+    st.prefill(prompt)
+    n0, pos0 = len(st.read()[0]), st.read()[1]
+    st.verify_step(G, np.array([[1, 2, 3]], np.int32))
+    with pytest.raises(IfrError):
+        st.verify_step(G, np.array([[1, 2, 3]], np.int32))
+    with pytest.raises(IfrError):
+        st.spec_step(G)
+    with pytest.raises(IfrError):
+        st.rollback([G + 1], np.zeros((1, G + 1), np.int32))
+    st.rollback([0], np.array([[77, -1, -1, -1]], np.int32))
+    toks, pos, acc, _ = st.read()
+    assert len(toks) == n0 + 1 and toks[-1] == 77 and pos == pos0 + 1 and acc == 0
+    with pytest.raises(IfrError):
+        st.rollback([0], np.array([[77, -1, -1, -1]], np.int32))
+    # the next fused step continues from 77: its first emitted token is the
+    # greedy successor of prompt + [77] (a fresh state's prefill)
+    ref = _state(model)
+    first = ref.prefill(np.concatenate([np.asarray(prompt, np.int32), np.array([77], np.int32)]))
+    st.spec_step(G)
+    assert st.read()[0][n0 + 1] == first
