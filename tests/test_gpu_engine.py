@@ -175,7 +175,7 @@ def test_step_in_parts_forced_and_errors(mini):
     model, om, prompt = mini
     G = 3
     st = _state(model)
-    st.prefill(prompt)
+    g0 = st.prefill(prompt)
     n0, pos0 = len(st.read()[0]), st.read()[1]
     st.verify_step(G, np.array([[1, 2, 3]], np.int32))
     with pytest.raises(IfrError):
@@ -189,9 +189,9 @@ def test_step_in_parts_forced_and_errors(mini):
     assert len(toks) == n0 + 1 and toks[-1] == 77 and pos == pos0 + 1 and acc == 0
     with pytest.raises(IfrError):
         st.rollback([0], np.array([[77, -1, -1, -1]], np.int32))
-    # the next fused step continues from 77: its first emitted token is the
-    # greedy successor of prompt + [77] (a fresh state's prefill)
+    # the sequence is now prompt, g0, 77: the next fused step's first emitted
+    # token is the greedy successor of that (a fresh state's prefill)
     ref = _state(model)
-    first = ref.prefill(np.concatenate([np.asarray(prompt, np.int32), np.array([77], np.int32)]))
+    first = ref.prefill(np.concatenate([np.asarray(prompt, np.int32), np.array([g0, 77], np.int32)]))
     st.spec_step(G)
     assert st.read()[0][n0 + 1] == first
