@@ -550,7 +550,7 @@ IFR_DEV uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
            ((uint32_t)(q3 & 0xff) << 24);
 }
 
-struct BFragI8 {
+struct __align__(16) BFragI8 {
     uint32_t b[8][2];  // chunk c: int8 of k-slots 4t..4t+3 and 16+4t..16+4t+3, column g
     // B of the correction MMA (k16): the block sums of column g as 7-bit limbs,
     // [0] = sum & 127, [1] = sum >> 7 (k-slots 4t..4t+3); Q4_K/Q5_K: the 8
@@ -1042,7 +1042,8 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
 }
 
 // ---- tall matrices, exact activations: one row block per warp --------------
-// For matrices of many row blocks (lm_heads, 151936 rows) a consumer warp owns
+// For matrices of many row blocks (lm_heads, 151936 rows), in both activation
+// modes, a consumer warp owns
 // a whole row block over all of K, so its sums stay in registers and go
 // straight to Y: no per-stage block barrier and no shared-memory reduction.
 // The B fragments of every unit are built once per CTA.  Warp 15 produces:
@@ -1053,8 +1054,12 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
 // and returns (IFR_ERR_TIMEOUT on the host).
 constexpr int kRowsCW = 15;  // consumer warps (and row blocks per group)
 
-template <int FMT, int NT, int XF, bool AM>
+template <int FMT, int NT, int XF, int ACT, bool AM>
 __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM> aa) {
+    // kI8: Q8_K activations (one n-tile: columns 2t, 2t+1 of lane t), fragments
+    // stored as BFragI8 [unit][lane] (80 bytes a lane: conflict-free 16-byte loads)
+    constexpr bool kI8 = FMT != 8 && ACT == 1;
+    constexpr int UNITW = kI8 ? (int)(sizeof(BFragI8) / 4) * 32 : bunit_words(NT);
     constexpr int MTB = mtile_bytes(FMT);
     constexpr int STAGE = kRowsCW * MTB;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1062,7 +1067,7 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
     uint64_t *empty = full + 8;
     uint8_t *ring = smem + 128;
     uint32_t *bsm = reinterpret_cast<uint32_t *>(ring + (size_t)a.S * STAGE);
-    float *ssq = reinterpret_cast<float *>(bsm + (size_t)a.nu * bunit_words(NT));  // XF 3: [nu][8]
+    float *ssq = reinterpret_cast<float *>(bsm + (size_t)a.nu * UNITW);  // XF 3: [nu][8]
     __shared__ float inv_s[8];
     __shared__ float part_s[16][8];
     __shared__ unsigned long long best_s[AM ? 8 : 1];
@@ -1127,8 +1132,16 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
         __syncthreads();
     }
     // every unit's fragments, once per CTA
-    for (int task = warp; task < a.nu * NT; task += 16)
-        build_b<FMT, NT, XF>(a, inv_s, task % a.nu, lane, task / a.nu, bsm + (size_t)(task % a.nu) * bunit_words(NT), ssq);
+    if constexpr (kI8) {
+        for (int u = warp; u < a.nu; u += 16) {
+            BFragI8 Fr;
+            build_b_i8<FMT, XF>(a, inv_s, u, lane, Fr);
+            reinterpret_cast<BFragI8 *>(bsm)[u * 32 + lane] = Fr;
+        }
+    } else {
+        for (int task = warp; task < a.nu * NT; task += 16)
+            build_b<FMT, NT, XF>(a, inv_s, task % a.nu, lane, task / a.nu, bsm + (size_t)(task % a.nu) * UNITW, ssq);
+    }
     __syncthreads();
     if (XF == 3) {  // W (x w) / rms(x) per column; the sums of squares in unit order
         if (tid < 8) {
@@ -1154,9 +1167,8 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
         }
     } else {
         const int g = lane >> 2, t = lane & 3;
-        unsigned long long best[NT];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) best[nt] = 0ull;
+        // greedy keys: exact, column 4 nt + t of n-tile nt; Q8_K, column 2 t + j
+        unsigned long long best[2] = {0ull, 0ull};
         int q = 0;
         for (int gr = g_lo; gr < g_hi; gr++) {
             const int rb = gr * kRowsCW + warp;
@@ -1169,17 +1181,44 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
                 const int slot = q % a.S;
                 if (!dead && !mbar_wait(full + slot, (uint32_t)(q / a.S) & 1)) dead = true;
                 if (!dead && rb < a.nrb) {
-                    BView<NT> F;
-                    F.at(bsm + (size_t)u * bunit_words(NT), lane);
                     const uint8_t *tile = ring + (size_t)slot * STAGE + (size_t)warp * MTB;
-                    if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot);
-                    else if constexpr (FMT == 14) mtile_q6_h<NT>(tile, lane, F, tot);
-                    else mtile_qk_h<FMT == 13, NT>(tile, lane, F, tot);
+                    if constexpr (kI8) {
+                        const BFragI8 F = reinterpret_cast<const BFragI8 *>(bsm)[u * 32 + lane];
+                        if constexpr (FMT == 14) mtile_q6_i8(tile, lane, F, tot[0]);
+                        else mtile_qk_i8<FMT == 13>(tile, lane, F, tot[0]);
+                    } else {
+                        BView<NT> F;
+                        F.at(bsm + (size_t)u * UNITW, lane);
+                        if constexpr (FMT == 8) mtile_q80<NT>(tile, lane, F, tot);
+                        else if constexpr (FMT == 14) mtile_q6_h<NT>(tile, lane, F, tot);
+                        else mtile_qk_h<FMT == 13, NT>(tile, lane, F, tot);
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty + slot);
             }
-            if (rb < a.nrb && !dead) {
+            if (kI8 && rb < a.nrb && !dead) {
+                // C columns 2t, 2t+1: activation columns 2t, 2t+1
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int col = 2 * t + j;
+                    if (col >= a.ncols) continue;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int64_t row = (int64_t)rb * 16 + g + 8 * h;
+                        if (row >= a.M) continue;
+                        float v = tot[0][2 * h + j];
+                        float *y = a.Y + (int64_t)col * a.ldy + row;
+                        if (a.accumulate) v += *y;
+                        *y = v;
+                        if constexpr (AM) {
+                            const unsigned long long k = argmax_key(v, row);
+                            best[j] = k > best[j] ? k : best[j];
+                        }
+                    }
+                }
+            }
+            if (!kI8 && rb < a.nrb && !dead) {
                 // C columns 2t, 2t+1 of n-tile nt: hi and lo parts of column 4 nt + t
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
@@ -1204,8 +1243,10 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
         }
         if constexpr (AM) {
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++)
-                if (4 * nt + t < a.ncols) atomicMax(&best_s[4 * nt + t], best[nt]);
+            for (int j = 0; j < 2; j++) {
+                const int col = kI8 ? 2 * t + j : 4 * j + t;
+                if ((kI8 || j < NT) && col < a.ncols) atomicMax(&best_s[col], best[j]);
+            }
         }
     }
     if constexpr (AM) {
@@ -1302,11 +1343,12 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     return launch_k(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>, dim3(grid), dim3(32 * CW), (size_t)smem, s, a, aa);
 }
 
-// Tall matrices (>= 2 row groups of 15 row blocks per SM) with exact
-// activations and no SwiGLU epilogue take the row-block-per-warp kernel when
-// every unit's fragments and three ring slots fit in shared memory; returns
+// Tall matrices (>= 2 row groups of 15 row blocks per SM) without a SwiGLU
+// input or epilogue take the row-block-per-warp kernel (either activation
+// mode) when every unit's fragments and three ring slots fit in shared
+// memory; returns
 // cudaErrorNotSupported (nothing launched) otherwise.
-template <int FMT, int NT, int XF, bool AM>
+template <int FMT, int NT, int XF, int ACT, bool AM>
 static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                                cudaStream_t s, const XForm &xf) {
     constexpr int MTB = mtile_bytes(FMT);
@@ -1314,14 +1356,16 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
     constexpr int kSmemMax = 226 * 1024;
     const int64_t ngr = (T.nrb + kRowsCW - 1) / kRowsCW;
     if (xf.ep || ngr < 2 * num_sms()) return cudaErrorNotSupported;
-    const int fixed = 128 + (int)T.nu * bunit_words(NT) * 4 + (XF == 3 ? (int)T.nu * 8 * 4 : 0);
+    constexpr bool kI8 = FMT != 8 && ACT == 1;
+    const int unit_bytes = kI8 ? (int)sizeof(BFragI8) * 32 : bunit_words(NT) * 4;
+    const int fixed = 128 + (int)T.nu * unit_bytes + (XF == 3 ? (int)T.nu * 8 * 4 : 0);
     int S = (kSmemMax - fixed) / STAGE;
     if (S < 3) return cudaErrorNotSupported;  // two one-unit stages hide too little DRAM latency (measured)
     if (S > 8) S = 8;
     const int smem = fixed + S * STAGE;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_rows_kernel<FMT, NT, XF, AM>,
+        cudaError_t e = cudaFuncSetAttribute(qgemv_rows_kernel<FMT, NT, XF, ACT, AM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;
         attr_set = true;
@@ -1331,7 +1375,7 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
                0, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
     AmArg<AM> aa{};
     if constexpr (AM) aa.am = *xf.am;
-    return launch_k(qgemv_rows_kernel<FMT, NT, XF, AM>, dim3(grid), dim3(512), (size_t)smem, s, a, aa);
+    return launch_k(qgemv_rows_kernel<FMT, NT, XF, ACT, AM>, dim3(grid), dim3(512), (size_t)smem, s, a, aa);
 }
 
 // Work split: UW warps share each row block's units.  A stage: 16 warps x 1
@@ -1346,9 +1390,9 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     constexpr bool kExact = FMT == 8 || ACT == 0;
     constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
     constexpr int CW = consumers<ACT>();
-    if constexpr (kExact && XF != 2) {
-        const cudaError_t e = xf.am ? launch_rows<FMT, NT, XF, true>(T, X, ncols, Y, accumulate, ldy, s, xf)
-                                    : launch_rows<FMT, NT, XF, false>(T, X, ncols, Y, accumulate, ldy, s, xf);
+    if constexpr (XF != 2) {
+        const cudaError_t e = xf.am ? launch_rows<FMT, NT, XF, ACT, true>(T, X, ncols, Y, accumulate, ldy, s, xf)
+                                    : launch_rows<FMT, NT, XF, ACT, false>(T, X, ncols, Y, accumulate, ldy, s, xf);
         if (e != cudaErrorNotSupported) return e;
     }
     constexpr int kSmemMax = 226 * 1024;

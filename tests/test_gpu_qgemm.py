@@ -239,14 +239,15 @@ def test_argument_errors(O, ctx, pkg):
 
 
 # tall matrices (>= 2 x 148 groups of 15 row blocks): the row-block-per-warp
-# kernel, which keeps every unit's fragments in shared memory (K = 1024); at
-# K = 4096 with 5+ columns three ring slots no longer fit beside them and the
-# unit-split kernel runs (N = 1 of Q4_K still takes the row kernel)
+# kernel, which keeps every unit's fragments in shared memory (K = 1024, and
+# K = 4096 with Q8_K activations); exact activations at K = 4096 with 5+
+# columns leave no room for three ring slots and take the unit-split kernel
 TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (14, 4096)]
 
 
+@pytest.mark.parametrize("act", [0, 1])
 @pytest.mark.parametrize("qt,K", TALL)
-def test_qgemm_tall(O, ctx, qt, K):
+def test_qgemm_tall(O, ctx, qt, K, act):
     torch = _torch()
     M = 71040 + 37  # ragged last row block and group
     rng = np.random.default_rng(qt * 31 + K)
@@ -255,14 +256,19 @@ def test_qgemm_tall(O, ctx, qt, K):
     q = pool.reshape(512, rb)[np.arange(M) % 512].ravel()
     W = ctx.upload(qt, q, M, K)
     X = rng.normal(0, 1, (8, K)).astype(np.float32)
-    ref = O.gemm_ref(qt, pool, 512, K, X)  # rows repeat with period 512
+    a = act if qt != 8 else 0  # Q8_0 is always exact
+    ref = O.gemm_ref(qt, pool, 512, K, X, act=a)  # rows repeat with period 512
     idx = np.arange(M) % 512
     Xd = torch.from_numpy(X).cuda()
-    for n in (1, 5, 8):
-        Y = ctx.qgemm(W, Xd[:n].contiguous()).cpu().numpy()
-        err = O.norm_rel(Y, ref[:n][:, idx])
-        assert err.max() < TOL, (NAMES[qt], K, n, err)
-    w = (1.0 + rng.normal(0, 0.2, K)).astype(np.float32)
-    Yn = ctx.qgemm_rmsnorm(W, Xd[:5].contiguous(), torch.from_numpy(w).cuda(), 1e-6).cpu().numpy()
-    refn = O.gemm_ref(qt, pool, 512, K, _rmsnorm(X[:5], w, 1e-6))
-    assert O.norm_rel(Yn, refn[:, idx]).max() < 5 * TOL
+    ctx.set_activation(act)
+    try:
+        for n in (1, 5, 8):
+            Y = ctx.qgemm(W, Xd[:n].contiguous()).cpu().numpy()
+            err = O.norm_rel(Y, ref[:n][:, idx])
+            assert err.max() < TOL, (NAMES[qt], K, n, act, err)
+        w = (1.0 + rng.normal(0, 0.2, K)).astype(np.float32)
+        Yn = ctx.qgemm_rmsnorm(W, Xd[:5].contiguous(), torch.from_numpy(w).cuda(), 1e-6).cpu().numpy()
+        refn = O.gemm_ref(qt, pool, 512, K, _rmsnorm(X[:5], w, 1e-6), act=a)
+        assert O.norm_rel(Yn, refn[:, idx]).max() < 5 * (TOL if a == 0 else 1e-3)
+    finally:
+        ctx.set_activation(0)
