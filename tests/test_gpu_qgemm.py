@@ -241,7 +241,8 @@ def test_argument_errors(O, ctx, pkg):
 # tall matrices (>= 2 x 148 groups of 15 row blocks): the row-block-per-warp
 # kernel, which keeps every unit's fragments in shared memory (K = 1024, and
 # K = 4096 with Q8_K activations); exact activations at K = 4096 with 5+
-# columns leave no room for three ring slots and take the unit-split kernel
+# columns leave no room for three ring slots, and Q4_K with Q8_K activations
+# streams faster unit-split: those take the unit-split kernel
 TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (14, 4096)]
 
 
