@@ -50,6 +50,12 @@ def test_version_and_errors_without_gpu(pkg):
     assert L.ifr_sync(None) == pkg._lib.IFR_ERR_ARG
     assert L.ifr_tensor_free(None) == 0
     assert L.ifr_ctx_destroy(None) == 0
+    # the step in parts: NULL states and arguments fail before any device work
+    assert L.ifr_draft_mtp(None, 4, None) == pkg._lib.IFR_ERR_ARG
+    assert L.ifr_verify_step(None, 4, None, None) == pkg._lib.IFR_ERR_ARG
+    assert L.ifr_rollback(None, None, None) == pkg._lib.IFR_ERR_ARG
+    assert L.ifr_sample(None, None, 1, 4, ctypes.c_float(1.0), 0, ctypes.c_float(1.0), ctypes.c_float(0.0),
+                        None, None) == pkg._lib.IFR_ERR_ARG
     del h
 
 
