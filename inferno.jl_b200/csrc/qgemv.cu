@@ -17,15 +17,19 @@
 //     accumulators; the Q4_K/Q5_K "min" term is one m16n8k8 against
 //     per-sub-block activation sums.
 //
-// Data movement (one persistent CTA per SM, 8 warps):
+// Data movement, unit-split kernel (qgemv_kernel; one persistent CTA per SM,
+// 16 warps):
 //   * thread 0 streams weight stages (16 M-tiles = one row group x the
 //     units of one K pass) global -> shared with cp.async.bulk into a ring of
 //     S stages guarded by mbarriers, keeping ~S x 37..70 KB in flight per SM;
-//   * consumer warp w owns one unit of the pass (w % UW) and two M-tiles of
-//     the row group; its B fragments for that unit stay in registers for the
-//     whole pass, built straight from X (no separate packing launch);
-//   * the UW unit-warps of an M-tile pair reduce through shared memory; K
-//     passes accumulate into Y (read-modify-write by the same thread).
+//   * consumer warp w owns one unit of the pass (w % UW) and one M-tile of the
+//     row group (two with Q8_K activations); exact activations: the pass's B
+//     fragments are built once into shared memory by the unit's warps, Q8_K:
+//     each warp builds its unit's fragments in registers; both straight from
+//     X (no separate packing launch);
+//   * the UW unit-warps of a row block reduce through shared memory; K passes
+//     accumulate in shared memory until the rows are final.
+// Tall matrices (qgemv_rows_kernel, below) keep a whole row block per warp.
 // Every mbarrier wait is bounded (~2 s); on expiry the kernel records an
 // error flag, stops waiting and drains, and the host reports IFR_ERR_TIMEOUT.
 #include "common.cuh"
