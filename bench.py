@@ -18,7 +18,8 @@ N=5 columns (draft length 4 + 1) over each of the 16 seeded weights
 (Q4_K/Q5_K/Q6_K/Q8_0 x 4096x4096, 12288x4096, 4096x12288, 151936x4096),
 weights resident in HBM (2.3 GB per step, larger than the 126 MB L2, so
 every step streams them from DRAM).  value = quantized weight bytes streamed
-per second (all ranks); `roofline` is the largest launch (Q4_K 151936x4096).
+per second (all ranks); `roofline` is the Q4_K 151936x4096 launch (the model's
+matmul format), `per_launch` every launch's own time and fraction of peak.
 
 Multi-GPU: every rank runs the same workload on its own GPU (replicas, no
 collective); value sums the ranks' units over the max-over-ranks time.
@@ -212,6 +213,18 @@ def run_sweep(args):
     o_ms, o_big = timed(other)
     with ClockSampler(local) as clk:
         ms_max, big_ms = timed(act)
+    # every launch's own time in the line's mode: CUDA events around each
+    # launch, in a separate pass after the timed region (3 passes, mean)
+    per_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in Ws]
+              for _ in range(3)]
+    for r in range(3):
+        for i, W in enumerate(Ws):
+            per_ev[r][i][0].record(stream)
+            ctx.qgemm(W, Xs[i], Ys[i])
+            per_ev[r][i][1].record(stream)
+    torch.cuda.synchronize()
+    per_us = [float(np.mean([per_ev[r][i][0].elapsed_time(per_ev[r][i][1]) for r in range(3)])) * 1e3
+              for i in range(len(Ws))]
 
     # end to end through the C ABI with host buffers: pinned X in, Y out, every call
     hX = [x.cpu().pin_memory() for x in Xs]
@@ -245,6 +258,9 @@ def run_sweep(args):
         cpu = cpu_baseline(O, pkg, args)
     if rank == 0:
         peak, peak_kind = measured_peaks()
+        names = [f"{name} {M}x{K}" for _, name in FORMATS for (M, K) in SHAPES]
+        per_launch = {nm: {"us": round(per_us[i], 2), "GBps": round(byts[i] / per_us[i] / 1e3, 1),
+                           "frac": round(byts[i] / per_us[i] / 1e3 / peak, 3)} for i, nm in enumerate(names)}
         big_bytes = byts[big_i]
         achieved = big_bytes / (big_ms * 1e-3) / 1e9
         value = step_bytes * args.steps * ws / (ms_max * 1e-3) / 1e9
@@ -268,6 +284,7 @@ def run_sweep(args):
                        "parallelism": f"replicas x{ws}"},
             "per_gpu_GBps": round(value / ws, 2),
             "hbm_frac_of_measured_peak": round(value / ws / peak, 4),
+            "per_launch": per_launch,
             "roofline": {"bound": "hbm", "kernel": "qgemv Q4_K 151936x4096 N=5",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
