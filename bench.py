@@ -132,9 +132,18 @@ def max_over_ranks(v, ws):
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    t = torch.tensor([v], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def rank_requests(total, ws, rank):
+    """the requests (seed offsets) rank owns when `total` independent requests
+    are split evenly over ws ranks: a contiguous block of total / ws"""
+    if total % ws:
+        raise SystemExit(f"--batch {total} does not split over {ws} ranks")
+    B = total // ws
+    return list(range(rank * B, (rank + 1) * B))
 
 
 def barrier(ws):
@@ -568,9 +577,8 @@ def run_batch(args):
     from inferno_b200 import synth
     from inferno_b200.engine import Model, State
     G = args.gamma
-    if args.batch % ws:
-        raise SystemExit(f"--batch {args.batch} does not split over {ws} ranks")
-    B = args.batch // ws
+    mine = rank_requests(args.batch, ws, rank)
+    B = len(mine)
     ctx = pkg.Context(local, torch_stream=False)
     t_load = time.time()
     path = synth.cached(BATCH_PRESET, BATCH_SEED)
@@ -578,7 +586,7 @@ def run_batch(args):
     info = model.info
     t_load = time.time() - t_load
     P = args.prompt
-    prompts = np.stack([synth.prompt(info.vocab, P, BATCH_SEED + 1000 + rank * B + b) for b in range(B)])
+    prompts = np.stack([synth.prompt(info.vocab, P, BATCH_SEED + 1000 + r) for r in mine])
     max_ctx = P + (args.warmup + args.steps + 4) * (G + 1) + 16
     st = State(model, max_ctx, batch=B)
     ctx.sync()
