@@ -387,22 +387,11 @@ static uint64_t or_cut_count(uint64_t above, uint64_t unit, double target) {
     return n;
 }
 
-int or_sample_filtered(const float *l, int V, float T, int top_k, float top_p, float min_p, float u) {
-    if (V < 1) return -1;
-    float M = -INFINITY;
-    int g = 0, finite = 0;
-    for (int i = 0; i < V; i++) {
-        float x = l[i];
-        if (isnan(x) || x == INFINITY) return -1;
-        if (x != -INFINITY) {
-            if (!finite || x > M) { M = x; g = i; }
-            finite = 1;
-        }
-    }
-    if (!finite) return 0;
-    if (T == 0.0f || V == 1) return g;
+/* the filters' weights of one row: w_i = e_i = or_exp((l_i - M) / T) for the
+   tokens top-k, top-p and min-p keep, else 0 (M = the row's max finite logit) */
+static void filter_weights(const float *l, int V, float M, float T, int top_k, float top_p, float min_p,
+                           float *w) {
     char *keep = (char *)malloc(V);
-    float *w = (float *)malloc(sizeof(float) * V);
     kidx *ord = (kidx *)malloc(sizeof(kidx) * V);
     for (int i = 0; i < V; i++) keep[i] = 1;
     if (top_k > 0 && top_k < V) {
@@ -446,6 +435,26 @@ int or_sample_filtered(const float *l, int V, float T, int top_k, float top_p, f
     }
     if (min_p > 0.0f)
         for (int i = 0; i < V; i++) if (w[i] < min_p) w[i] = 0.0f;
+    free(ord);
+    free(keep);
+}
+
+int or_sample_filtered(const float *l, int V, float T, int top_k, float top_p, float min_p, float u) {
+    if (V < 1) return -1;
+    float M = -INFINITY;
+    int g = 0, finite = 0;
+    for (int i = 0; i < V; i++) {
+        float x = l[i];
+        if (isnan(x) || x == INFINITY) return -1;
+        if (x != -INFINITY) {
+            if (!finite || x > M) { M = x; g = i; }
+            finite = 1;
+        }
+    }
+    if (!finite) return 0;
+    if (T == 0.0f || V == 1) return g;
+    float *w = (float *)malloc(sizeof(float) * V);
+    filter_weights(l, V, M, T, top_k, top_p, min_p, w);
     /* canonical chunked draw */
     const int nch = (V + CH - 1) / CH;
     float *cs = (float *)malloc(sizeof(float) * nch);
@@ -495,7 +504,7 @@ int or_sample_filtered(const float *l, int V, float T, int top_k, float top_p, f
         tok = e - 1;
         for (int i = e - 1; i >= b; i--) if (w[i] > 0.f) { tok = i; break; }
     }
-    free(cs); free(ord); free(w); free(keep);
+    free(cs); free(w);
     return tok;
 }
 
@@ -524,4 +533,214 @@ void or_apply_penalties(float *logits, int rows, int V, const int32_t *seen, int
         }
     }
     free(mark);
+}
+
+
+/* ===================================================================== *
+ * Filtered speculative acceptance: the verification of or_accept on the
+ * distributions that the filters of or_sample_filtered leave (top-k, top-p,
+ * min-p applied to every target and draft row with the same temperature).
+ * The reference's speculate_and_verify (src/SpeculativeDecoding.jl:37-104)
+ * filters only its draft draws and bonus token; filtering both distributions
+ * keeps the emitted tokens distributed as the filtered target.  Per row: the
+ * kept set K = {i : filter_weights(row)_i > 0}; chunk statistics as in
+ * or_chunk_stats with the sums over K only (the chunk max over every
+ * element); weights rs_w are 0 outside K; every draw (draft, residual, bonus)
+ * takes the first i with a positive weight and tau <= cumsum.
+ * TEST INFRASTRUCTURE: the restatement a device kernel is checked against.
+ * ===================================================================== */
+
+typedef struct {
+    rowstat rs;
+    char *keep;
+} mrow;
+
+static void mrow_init(mrow *m, const float *row, int V, float T, int top_k, float top_p, float min_p) {
+    float M = -INFINITY;
+    for (int i = 0; i < V; i++) if (row[i] > M) M = row[i];
+    float *w = (float *)malloc(sizeof(float) * V);
+    filter_weights(row, V, M, T, top_k, top_p, min_p, w);
+    m->keep = (char *)malloc(V);
+    for (int i = 0; i < V; i++) m->keep[i] = w[i] > 0.f;
+    free(w);
+    rowstat *rs = &m->rs;
+    rs->V = V; rs->T = T;
+    rs->nch = (V + CH - 1) / CH;
+    rs->cmax = (float *)malloc(sizeof(float) * rs->nch);
+    rs->csum = (float *)malloc(sizeof(float) * rs->nch);
+    float lanes[NL];
+    for (int c = 0; c < rs->nch; c++) {
+        int b = c * CH, e = b + CH < V ? b + CH : V;
+        float mc = -INFINITY;
+        for (int i = b; i < e; i++) if (row[i] > mc) mc = row[i];
+        for (int j = 0; j < NL; j++) {
+            float t = 0.f;
+            for (int q = 0; q < PER; q++) {
+                int i = b + PER * j + q;
+                if (i < e && m->keep[i]) t = t + elem_e(row[i], mc, T);
+            }
+            lanes[j] = t;
+        }
+        rs->cmax[c] = mc;
+        rs->csum[c] = butterfly_sum(lanes);
+    }
+    or_row_stats(rs->cmax, rs->csum, rs->nch, T, &rs->M, &rs->S);
+}
+static void mrow_free(mrow *m) { rowstat_free(&m->rs); free(m->keep); }
+static inline float mrow_w(const mrow *m, const float *row, int i) {
+    return m->keep[i] ? rs_w(&m->rs, row, i) : 0.0f;
+}
+
+/* first element with a positive value and tau <= cumsum (blocked order), else
+   the last positive one, else the last element */
+static int chunk_search_pos(const float *vals, int b, int e, float tau) {
+    float pre = 0.f;
+    for (int j = 0; j < NL; j++) {
+        float cum = pre, t = 0.f;
+        for (int q = 0; q < PER; q++) {
+            int i = b + PER * j + q;
+            if (i >= e) break;
+            t = t + vals[i - b];
+            cum = cum + vals[i - b];
+            if (vals[i - b] > 0.f && tau <= cum) return i;
+        }
+        pre = pre + t;
+    }
+    for (int i = e - 1; i >= b; i--) if (vals[i - b] > 0.f) return i;
+    return e - 1;
+}
+
+/* draw from per-chunk masses cm[c] (and element values by vfun) with u */
+typedef float (*vfun)(const void *ctx, int i);
+static int draw_chunked(const float *cm, int nch, int V, float total, float u, vfun f, const void *ctx) {
+    float tau = u * total, P = 0.f;
+    int cs = -1;
+    for (int c = 0; c < nch; c++) {
+        float nP = P + cm[c];
+        if (cm[c] > 0.f && tau <= nP) { cs = c; break; }
+        P = nP;
+    }
+    if (cs < 0) {
+        for (int c = nch - 1; c >= 0; c--) if (cm[c] > 0.f) { cs = c; break; }
+        if (cs < 0) cs = nch - 1;
+        P = 0.f;
+        for (int c = 0; c < cs; c++) P = P + cm[c];
+        tau = P + cm[cs];
+    }
+    int b = cs * CH, e = b + CH < V ? b + CH : V;
+    float vals[CH];
+    for (int i = b; i < e; i++) vals[i - b] = f(ctx, i);
+    return chunk_search_pos(vals, b, e, tau - P);
+}
+
+typedef struct { const mrow *m; const float *row; int c; } mctx;
+static float m_elem(const void *x, int i) {   /* element weight inside chunk c, relative to its max */
+    const mctx *k = (const mctx *)x;
+    return k->m->keep[i] ? elem_e(k->row[i], k->m->rs.cmax[k->c], k->m->rs.T) : 0.0f;
+}
+
+static int sample_mrow(const mrow *m, const float *row, float u) {
+    const rowstat *rs = &m->rs;
+    float *cm = (float *)malloc(sizeof(float) * rs->nch);
+    for (int c = 0; c < rs->nch; c++) cm[c] = rs->csum[c] * rs_f(rs, c);
+    /* chunk choice on the row-scaled masses, then the element search on the
+       chunk's own weights with tau rescaled by the chunk factor */
+    float tau = u * rs->S, P = 0.f;
+    int cs = -1;
+    for (int c = 0; c < rs->nch; c++) {
+        float nP = P + cm[c];
+        if (cm[c] > 0.f && tau <= nP) { cs = c; break; }
+        P = nP;
+    }
+    if (cs < 0) {
+        for (int c = rs->nch - 1; c >= 0; c--) if (cm[c] > 0.f) { cs = c; break; }
+        if (cs < 0) cs = rs->nch - 1;
+        P = 0.f;
+        for (int c = 0; c < cs; c++) P = P + cm[c];
+        tau = P + cm[cs];
+    }
+    float taup = (tau - P) / rs_f(rs, cs);
+    int b = cs * CH, e = b + CH < rs->V ? b + CH : rs->V;
+    float vals[CH];
+    mctx k = {m, row, cs};
+    for (int i = b; i < e; i++) vals[i - b] = m_elem(&k, i);
+    free(cm);
+    return chunk_search_pos(vals, b, e, taup);
+}
+
+typedef struct { const mrow *t; const float *trow; const mrow *d; const float *drow; } rctx;
+static float r_elem(const void *x, int i) {
+    const rctx *k = (const rctx *)x;
+    float r = mrow_w(k->t, k->trow, i) / k->t->rs.S - mrow_w(k->d, k->drow, i) / k->d->rs.S;
+    return r > 0.f ? r : 0.f;
+}
+
+static int sample_mresidual(const mrow *t, const float *trow, const mrow *d, const float *drow, float u) {
+    int V = t->rs.V, nch = t->rs.nch;
+    float *rc = (float *)malloc(sizeof(float) * nch);
+    float lanes[NL];
+    rctx k = {t, trow, d, drow};
+    for (int c = 0; c < nch; c++) {
+        int b = c * CH, e = b + CH < V ? b + CH : V;
+        for (int j = 0; j < NL; j++) {
+            float s2 = 0.f;
+            for (int q = 0; q < PER; q++) { int i = b + PER * j + q; if (i < e) s2 = s2 + r_elem(&k, i); }
+            lanes[j] = s2;
+        }
+        rc[c] = butterfly_sum(lanes);
+    }
+    float R = 0.f;
+    for (int c = 0; c < nch; c++) R = R + rc[c];
+    int y = R > 0.f ? draw_chunked(rc, nch, V, R, u, r_elem, &k) : -1;
+    free(rc);
+    return y;
+}
+
+int or_accept_filtered(const float *target, const float *draft, const float *uniforms, int batch, int gamma,
+                       int vocab, float T, int top_k, float top_p, float min_p, int32_t *accept_count,
+                       int32_t *out_tokens, int32_t *draft_out) {
+    if (batch < 0 || gamma < 1 || gamma > 64 || vocab < 1 || !(T > 0.f)) return -1;
+    for (int b = 0; b < batch; b++) {
+        const float *tb = target + (int64_t)b * (gamma + 1) * vocab;
+        const float *db = draft + (int64_t)b * gamma * vocab;
+        const float *u = uniforms + (int64_t)b * (2 * gamma + 1);
+        int32_t *ot = out_tokens + (int64_t)b * (gamma + 1);
+        for (int i = 0; i <= gamma; i++) ot[i] = -1;
+        int32_t x[64];
+        mrow ds[64];
+        for (int i = 0; i < gamma; i++) {
+            mrow_init(&ds[i], db + (int64_t)i * vocab, vocab, T, top_k, top_p, min_p);
+            x[i] = sample_mrow(&ds[i], db + (int64_t)i * vocab, u[i]);
+            if (draft_out) draft_out[(int64_t)b * gamma + i] = x[i];
+        }
+        int acc = 0, done = 0;
+        for (int i = 0; i < gamma && !done; i++) {
+            const float *trow = tb + (int64_t)i * vocab, *drow = db + (int64_t)i * vocab;
+            mrow ts;
+            mrow_init(&ts, trow, vocab, T, top_k, top_p, min_p);
+            float pt = mrow_w(&ts, trow, x[i]) / ts.rs.S;
+            float pd = mrow_w(&ds[i], drow, x[i]) / ds[i].rs.S;
+            int ok = pd > 0.f ? (u[gamma + i] < pt / pd) : (pt > 0.f);
+            if (ok) {
+                ot[i] = x[i];
+                acc++;
+            } else {
+                int y = sample_mresidual(&ts, trow, &ds[i], drow, u[2 * gamma]);
+                if (y < 0) y = sample_mrow(&ts, trow, u[2 * gamma]);
+                ot[i] = y;
+                done = 1;
+            }
+            mrow_free(&ts);
+        }
+        if (!done) {
+            const float *trow = tb + (int64_t)gamma * vocab;
+            mrow ts;
+            mrow_init(&ts, trow, vocab, T, top_k, top_p, min_p);
+            ot[gamma] = sample_mrow(&ts, trow, u[2 * gamma]);
+            mrow_free(&ts);
+        }
+        accept_count[b] = acc;
+        for (int i = 0; i < gamma; i++) mrow_free(&ds[i]);
+    }
+    return 0;
 }

@@ -72,6 +72,10 @@ int   or_sample_rows(const float *logits, int rows, int vocab, float temperature
                      float top_p, float min_p, const float *uniforms, int32_t *out_tokens);
 void  or_apply_penalties(float *logits, int rows, int vocab, const int32_t *seen, int n_seen,
                          float presence, float repetition);
+/* or_accept on the filtered target and draft distributions (accept.c) */
+int   or_accept_filtered(const float *target, const float *draft, const float *uniforms, int batch,
+                         int gamma, int vocab, float temperature, int top_k, float top_p, float min_p,
+                         int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out);
 
 /* ---- model forward (model.c) ---- */
 typedef struct {

@@ -67,6 +67,8 @@ def lib():
         L.or_apply_penalties.argtypes = [_fp, ctypes.c_int, ctypes.c_int, _i32p, ctypes.c_int, ctypes.c_float,
                                          ctypes.c_float]
         L.or_apply_penalties.restype = None
+        L.or_accept_filtered.argtypes = [_fp, _fp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                         ctypes.c_int, ctypes.c_float, ctypes.c_float, _i32p, _i32p, _i32p]
         _lib = L
     return _lib
 
@@ -228,6 +230,24 @@ def sample(logits, uniforms, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0):
     lib().or_sample_rows(_p(logits, _fp), rows, V, float(temperature), int(top_k), float(top_p), float(min_p),
                          _p(u, _fp), _p(out, _i32p))
     return out
+
+
+def accept_filtered(target, draft, uniforms, temperature, top_k=0, top_p=1.0, min_p=0.0):
+    """sampled verification on the filtered target and draft distributions:
+    (accept counts [B], emitted tokens [B][G+1] (-1 padded), drawn drafts [B][G])"""
+    target = np.ascontiguousarray(target, dtype=np.float32)
+    draft = np.ascontiguousarray(draft, dtype=np.float32)
+    uniforms = np.ascontiguousarray(uniforms, dtype=np.float32)
+    B, G1, V = target.shape
+    G = G1 - 1
+    acc = np.empty(B, dtype=np.int32)
+    out = np.empty((B, G + 1), dtype=np.int32)
+    dout = np.empty((B, G), dtype=np.int32)
+    rc = lib().or_accept_filtered(_p(target, _fp), _p(draft, _fp), _p(uniforms, _fp), B, G, V, float(temperature),
+                                  int(top_k), float(top_p), float(min_p), _p(acc, _i32p), _p(out, _i32p),
+                                  _p(dout, _i32p))
+    assert rc == 0
+    return acc, out, dout
 
 
 def apply_penalties(logits, seen, presence=0.0, repetition=1.0):

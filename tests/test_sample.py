@@ -217,3 +217,61 @@ def test_penalties_bit_exact(O, ctx):
     got = ctx.sample(d, _dev(u), temperature=0.8, top_k=40, top_p=0.95).cpu().numpy()
     ref = O.sample(O.apply_penalties(logits, seen, 0.5, 1.3), u, temperature=0.8, top_k=40, top_p=0.95)
     assert np.array_equal(got, ref)
+
+
+# ---- filtered speculative acceptance (oracle restatement) -----------------------
+
+def test_accept_filtered_without_filters_is_accept(O):
+    """with every filter off the filtered verification is the plain one"""
+    rng = np.random.default_rng(3)
+    B, G, V = 4, 3, 5000
+    tgt = rng.normal(0, 3, (B, G + 1, V)).astype(np.float32)
+    dft = (tgt[:, :G] + rng.normal(0, 1, (B, G, V))).astype(np.float32)
+    u = rng.random((B, 2 * G + 1), dtype=np.float32) * 0.999 + 0.0005
+    got = O.accept_filtered(tgt, dft, u, 0.8)
+    ref = O.accept(tgt, dft, u, 0.8)
+    for g, r in zip(got, ref):
+        assert np.array_equal(g, r)
+
+
+def _filtered_probs(l, T, top_k, top_p, min_p):
+    """the filtered, renormalised distribution in float64 (no ties assumed)"""
+    l = np.asarray(l, np.float64)
+    keep = np.ones(len(l), bool)
+    if 0 < top_k < len(l):
+        keep[:] = False
+        keep[np.argsort(-l, kind="stable")[:top_k]] = True
+    e = np.where(keep, np.exp((l - l.max()) / T), 0.0)
+    p = e / e.sum()
+    if top_p < 1:
+        o = np.argsort(-p, kind="stable")
+        m = int(np.searchsorted(np.cumsum(p[o]), top_p)) + 1
+        k2 = np.zeros(len(l), bool)
+        k2[o[:m]] = True
+        p = np.where(k2, p, 0.0)
+        p /= p.sum()
+    if min_p > 0:
+        p = np.where(p >= p.max() * min_p, p, 0.0)
+        p /= p.sum()
+    return p
+
+
+def test_accept_filtered_emits_the_filtered_target(O):
+    """speculative sampling on filtered distributions leaves the first emitted
+    token distributed as the filtered target (drafts from the filtered draft)"""
+    rng = np.random.default_rng(11)
+    V, T, kw = 16, 0.9, dict(top_k=9, top_p=0.9, min_p=0.03)
+    t = rng.normal(0, 1.5, V).astype(np.float32)
+    d = (t + rng.normal(0, 1.0, V)).astype(np.float32)
+    n = 40000
+    tgt = np.broadcast_to(t, (n, 2, V)).copy()
+    dft = np.broadcast_to(d, (n, 1, V)).copy()
+    u = rng.random((n, 3), dtype=np.float32) * 0.9998 + 0.0001
+    acc, out, drafts = O.accept_filtered(tgt, dft, u, T, **kw)
+    pt = _filtered_probs(t, T, **kw)
+    pd = _filtered_probs(d, T, **kw)
+    f0 = np.bincount(out[:, 0], minlength=V) / n
+    fd = np.bincount(drafts[:, 0], minlength=V) / n
+    assert np.abs(fd - pd).max() < 0.015, (fd, pd)
+    assert np.abs(f0 - pt).max() < 0.015, (f0, pt)
+    assert np.all(f0[pt == 0] == 0)  # nothing the target's filters drop is emitted
