@@ -933,11 +933,11 @@ __global__ void __launch_bounds__(256) penalty_kernel(float *__restrict__ logits
 cudaError_t apply_penalties(float *logits, int rows, int V, const int32_t *seen, int n_seen, float presence,
                             float repetition, cudaStream_t s) {
     const size_t smem = (size_t)((V + 31) / 32) * 4;
-    static bool attr = false;
-    if (!attr) {
+    static DeviceFlags attr;
+    if (!attr.test()) {
         cudaError_t e = cudaFuncSetAttribute(penalty_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr.set();
     }
     return launch_k(penalty_kernel, dim3(rows), dim3(256), smem, s, logits, V, seen, n_seen, presence, repetition);
 }

@@ -1,6 +1,7 @@
 // Shared device helpers and the internal (C++) interface between the kernel
 // files and the C ABI in api.cu.  sm_100a only.
 #pragma once
+#include <atomic>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -203,6 +204,19 @@ IFR_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 IFR_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 bool pdl_enabled();  // IFR_PDL=0 in the environment turns it off (api.cu)
+
+// one bit per device: per-device one-time set-up (cudaFuncSetAttribute applies
+// to the current device only, and one process may drive several GPUs)
+struct DeviceFlags {
+    std::atomic<unsigned long long> bits{0};
+    static unsigned long long bit() {
+        int d = 0;
+        cudaGetDevice(&d);
+        return 1ull << (d & 63);
+    }
+    bool test() const { return (bits.load() & bit()) != 0; }
+    void set() { bits.fetch_or(bit()); }
+};
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,

@@ -1050,12 +1050,12 @@ int64_t attn_part_floats(int nh, int nkv, int hd, int batch, int max_ctx) {
 
 template <int HD>
 static cudaError_t launch_split(const AttnArgs &a, int batch, cudaStream_t s) {
-    static bool attr = false;
-    if (!attr) {
+    static DeviceFlags attr;
+    if (!attr.test()) {
         cudaError_t e = cudaFuncSetAttribute(attn_part_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              GrpSmem<HD>::bytes(kGrpRows, kMaxN));
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr.set();
     }
     const int ratio = a.nh / a.nkv, hg = split_heads(ratio, a.N), nrg = (ratio + hg - 1) / hg;
     const int R = std::min(hg, ratio) * a.N;

@@ -1330,15 +1330,15 @@ static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float
     if (sweep_rg > per_cta) sweep_rg = (int)per_cta;
     const int smem = 128 + S * STAGE + red + sweep_rg * rg_bytes + ssq_bytes + bsm_bytes;
     if (smem > kSmemMax) return cudaErrorInvalidConfiguration;
-    static bool attr_set = false;
-    if (!attr_set) {
+    static DeviceFlags attr_set;
+    if (!attr_set.test()) {
         cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(qgemv_kernel<FMT, NT, XF, MPW, ACT, AM>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        attr_set.set();
     }
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, UW, S,
                sweep_rg, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
@@ -1370,12 +1370,12 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
     if (S < 3) return cudaErrorNotSupported;  // two one-unit stages hide too little DRAM latency (measured)
     if (S > 8) S = 8;
     const int smem = fixed + S * STAGE;
-    static bool attr_set = false;
-    if (!attr_set) {
+    static DeviceFlags attr_set;
+    if (!attr_set.test()) {
         cudaError_t e = cudaFuncSetAttribute(qgemv_rows_kernel<FMT, NT, XF, ACT, AM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        attr_set.set();
     }
     const int grid = num_sms();
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, 0, S,

@@ -710,12 +710,12 @@ bool make_plan(const QTensor &T, int ncols, Plan &p) {
 
 template <int FMT, int KS>
 cudaError_t launch_qmma_ks(const MmaArgs &a, const Plan &p, cudaStream_t s) {
-    static bool attr = false;
-    if (!attr) {
+    static DeviceFlags attr;
+    if (!attr.test()) {
         cudaError_t e = cudaFuncSetAttribute(qmma_kernel<FMT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kMaxSmem - 1024);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr.set();
     }
     return launch_k(qmma_kernel<FMT, KS>, dim3(p.rtiles * p.ntiles, p.splits), dim3(kMmaThreads), (size_t)p.smem, s,
                     a);
