@@ -79,6 +79,13 @@ cudaError_t read_mma_error(int *flag, cudaStream_t s);
 int quantize_host(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
 // device-side error flag set by bounded waits that ran out (read and cleared)
 cudaError_t read_device_error(int *flag, cudaStream_t s);
+// the small-N kernels of one weight format (one translation unit per format,
+// qgemv_q4k.cu .. qgemv_q80.cu) and that unit's error flag
+template <int FMT>
+cudaError_t qgemm_small_fmt(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
+                            cudaStream_t s, const XForm &xf);
+template <int FMT>
+cudaError_t read_dev_error_fmt(int *flag, cudaStream_t s);
 
 cudaError_t accept_sampled(const float *target, const float *draft, const int32_t *draft_tokens,
                            const float *uniforms, int batch, int gamma, int vocab, float T,
@@ -217,6 +224,21 @@ struct DeviceFlags {
     bool test() const { return (bits.load() & bit()) != 0; }
     void set() { bits.fetch_or(bit()); }
 };
+
+// multiprocessor count of the current device, cached per device (one
+// process may drive several GPUs from several host threads)
+inline int device_sm_count() {
+    static std::atomic<int> cache[64];
+    int d = 0;
+    cudaGetDevice(&d);
+    d &= 63;
+    int n = cache[d].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0) n = 148;
+        cache[d].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,

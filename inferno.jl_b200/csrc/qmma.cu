@@ -643,16 +643,7 @@ __global__ void qmma_reduce_kernel(const float *__restrict__ ws, int splits, int
 
 namespace {
 
-int sm_count() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int sm_count() { return device_sm_count(); }
 
 struct Plan {
     int ntiles, npad, nch, ks, splits, RS, ST, rtiles, smem;
