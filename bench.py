@@ -401,6 +401,23 @@ SPEC_PRESET, SPEC_SEED, SPEC_PROMPT = "tiny", 0, 128
 SPEC_GEN = 128  # config 1: 128 greedy tokens per request
 
 
+def spec_bytes_per_step_gguf(gf, gamma):
+    """spec_bytes_per_step from the GGUF's own tensors (no library loaded):
+    quantized bytes of the decoder layers and the lm_head per verify, plus
+    per draft the MTP fc, its layer and the lm_head"""
+    layers = mtp = 0
+    for name, t in gf.tensors.items():
+        if t.type in (8, 12, 13, 14) and name != "token_embd.weight":
+            nb = t.nbytes
+            if name.startswith("mtp."):
+                mtp += nb
+            else:
+                layers += nb
+    lm = gf.tensors["token_embd.weight"]
+    lm_b = lm.nbytes
+    return layers + lm_b + gamma * (mtp + lm_b)
+
+
 def spec_bytes_per_step(info, gamma):
     """algorithmic weight bytes one spec step reads: the verify (decoder layers
     + lm_head) and, per draft, the MTP fc + layer + lm_head"""
@@ -411,6 +428,16 @@ def spec_bytes_per_step(info, gamma):
     mtp = sum(r * k for r, k in mtp_rows_k) * 144 // 256
     lm = info.vocab * d * 210 // 256
     return info.weight_bytes + gamma * (mtp + lm)
+
+
+def spec_config(G, step_bytes, ws):
+    """the config-1 workload, identical on both arms"""
+    return {"workload": "greedy spec-decode, BASELINE config 1 (tiny Qwen3.5-shape hybrid)",
+            "model": "hidden 1024, 24 layers (18 GatedDeltaNet + 6 attention), 8q/2kv x 256, FFN 3584, vocab 151936, 1-layer MTP head",
+            "gamma": G, "verify_columns": G + 1, "prompt": SPEC_PROMPT, "batch": 1,
+            "weight_bytes_per_step": int(step_bytes),
+            "l2": "inputs larger than L2: %.0f MB of weights read per step" % (step_bytes / 1e6),
+            "parallelism": f"replicas x{ws}"}
 
 
 def run_spec(args):
@@ -527,14 +554,10 @@ def run_spec(args):
             "vs_baseline": None,
             "dtype": ACT_DTYPE[args.act],
             "data": "synthetic: seeded random-init Qwen3.5-shape hybrid GGUF (N(0,0.02) weights, the library's encoder), seeded uniform 128-token prompt",
-            "config": {"workload": "greedy spec-decode, BASELINE config 1 (tiny Qwen3.5-shape hybrid)",
-                       "model": "hidden 1024, 24 layers (18 GatedDeltaNet + 6 attention), 8q/2kv x 256, FFN 3584, vocab 151936, 1-layer MTP head",
-                       "gamma": G, "verify_columns": G + 1, "prompt": SPEC_PROMPT, "batch": 1,
-                       "activations": ["exact f32", "Q8_K"][args.act],
-                       "tokens_emitted_timed": emitted, "accept_rate": round((emitted / args.steps - 1) / G, 4),
-                       "weight_bytes_per_step": step_bytes,
-                       "l2": "inputs larger than L2: %.0f MB of weights read per step" % (step_bytes / 1e6),
-                       "parallelism": f"replicas x{ws}", "graph": "one CUDA graph per spec step"},
+            "config": spec_config(G, step_bytes, ws),
+            "activations": ["exact f32", "Q8_K"][args.act],
+            "tokens_emitted_timed": emitted, "accept_rate": round((emitted / args.steps - 1) / G, 4),
+            "graph": "one CUDA graph per spec step",
             "step_hbm_GBps": round(step_bytes / (ms_max / args.steps * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "kernel": "qgemv: the 97 dequant-GEMV launches of one verify (24 layers x 4 + Q6_K lm_head), N=5, back to back",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
@@ -867,23 +890,29 @@ def run_reference_spec(args):
     if rank != 0:
         return
     import __graft_entry__ as ge
-    ge.load_package()
+    O = ge.load_oracle()
+    ge.load_package()  # python modules only: libinferno_b200.so is never loaded on this arm
     from inferno_b200 import synth
-    path = synth.cached(SPEC_PRESET, SPEC_SEED)
+    # the model's bytes come from the oracle's encoder (identical to the
+    # library's, tests/test_oracle.py), so this arm maps no library of ours
+    path = synth.cached(SPEC_PRESET, SPEC_SEED, quantize=O.quantize)
     from inferno_b200 import gguf
-    V = int(gguf.GGUFFile(path).tensors["token_embd.weight"].dims[1])
+    gf = gguf.GGUFFile(path)
+    V = int(gf.tensors["token_embd.weight"].dims[1])
     prompt = synth.prompt(V, SPEC_PROMPT, SPEC_SEED)
-    steps = max(1, min(args.steps, 4))
-    tps, dt, _ = _oracle_spec(path, prompt, args.gamma, steps, warmup=1)
+    # every step is one whole spec step of the workload (draft, verify,
+    # accept) on the host cores; the steps and warm-up match the GPU arm's
+    steps = max(1, args.steps)
+    tps, dt, _ = _oracle_spec(path, prompt, args.gamma, steps, warmup=args.warmup)
     cores = os.cpu_count() or 1
     sample = (f"reference CPU path restated in C (oracle/model.c: forward_cpu! + MTP head + fixed greedy spec-decode "
-              f"loop, {cores} threads): {steps} spec steps, gamma {args.gamma}, after a 128-token prefill")
+              f"loop, {cores} threads): {steps} spec steps after {args.warmup} warm-up steps, gamma {args.gamma}, "
+              f"after a 128-token prefill")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tokens/s", "n_gpus": ws,
-        "steps": steps, "warmup": 1, "ms_per_step": round(dt / steps * 1e3, 1), "higher_is_better": True,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(dt / steps * 1e3, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantized weights)", "data": "synthetic",
-        "config": {"workload": "greedy spec-decode, BASELINE config 1 (tiny Qwen3.5-shape hybrid), CPU sample",
-                   "gamma": args.gamma},
+        "config": spec_config(args.gamma, spec_bytes_per_step_gguf(gf, args.gamma), ws),
         "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)

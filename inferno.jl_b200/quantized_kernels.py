@@ -6,10 +6,15 @@ the raw GGUF block bytes of an (outer_dim x inner_dim) matrix.  The reference
 binds src/kernels/libquant_kernels.so (QuantizedKernels.jl:22); this module
 binds the same C symbols exported by libinferno_b200.so, which run on the GPU.
 
-Differences, on purpose: the activations are not rounded to Q8_K first (the
-GPU path keeps them f32), so results are closer to the dequantize-then-dot
-path of src/ModelCPU.jl than the reference C kernel is; and there is no Q8_K
-scratch pool (QuantizedKernels.jl:60-72) because nothing needs one.
+Arithmetic: like the reference's kernels, these symbols round the
+activation column to Q8_K first (d = amax/127, roundf; quantize_row_q8_K,
+quant_kernels.c:166-194) and form exact int32 sub-block sums (on the GPU's
+integer tensor cores), so results match the reference C kernel up to f32
+summation order.  Differences, on purpose: there is no Q8_K scratch pool
+(QuantizedKernels.jl:60-72), because the quantized column never leaves the
+GPU; and every call copies the whole weight matrix to the device (these are
+host-pointer compatibility shims - a model should upload its weights once
+through the native ifr_* API instead).
 """
 import os
 

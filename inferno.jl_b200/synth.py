@@ -59,8 +59,12 @@ def _quant(qtype, x):
     return quantize(qtype, x)
 
 
-def build(path, preset="tiny", seed=0, **overrides):
-    """Write the seeded model to `path` (GGUF v3)."""
+def build(path, preset="tiny", seed=0, quantize=None, **overrides):
+    """Write the seeded model to `path` (GGUF v3).  `quantize(qtype, rows)`
+    encodes the matrices (default: the library's host encoder; the CPU
+    reference leg passes the oracle's, which writes the same bytes, so that
+    it never loads the library)."""
+    quant = quantize or _quant
     cfg = dict(PRESETS[preset])
     cfg.update(overrides)
     d, L = cfg["hidden"], cfg["n_layers"]
@@ -94,7 +98,7 @@ def build(path, preset="tiny", seed=0, **overrides):
     def mat(name, rows, cols, qtype, std=0.02):
         n = min(rows, pool) if pool else rows
         x = rng().standard_normal((n, cols), dtype=np.float32) * np.float32(std)
-        q = _quant(qtype, x)
+        q = quant(qtype, x)
         if n < rows:  # quantization is row-wise: repeat the quantized rows
             q = np.tile(q.reshape(n, -1), ((rows + n - 1) // n, 1))[:rows].ravel()
         w.add_tensor(name, [cols, rows], qtype, q)
@@ -151,14 +155,15 @@ def build(path, preset="tiny", seed=0, **overrides):
     return path
 
 
-def cached(preset="tiny", seed=0, directory=None):
-    """Path of the seeded model, built on first use (per machine)."""
+def cached(preset="tiny", seed=0, directory=None, quantize=None):
+    """Path of the seeded model, built on first use (per machine); `quantize`
+    as in build()."""
     directory = directory or os.path.join(tempfile.gettempdir(), "inferno_b200_models")
     os.makedirs(directory, exist_ok=True)
     path = os.path.join(directory, f"{preset}_seed{seed}.gguf")
     if not os.path.exists(path):
         tmp = path + f".{os.getpid()}.tmp"
-        build(tmp, preset, seed)
+        build(tmp, preset, seed, quantize=quantize)
         os.replace(tmp, path)
     return path
 

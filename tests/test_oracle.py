@@ -178,3 +178,21 @@ def test_argmax_ties_first_index(O):
     import ctypes
     a = np.array([0.0, 2.0, 1.0, 2.0], np.float32)
     assert L.or_argmax(a.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), 4) == 1
+
+
+@pytest.mark.parametrize("qt", [12, 13, 14, 8])
+def test_oracle_encoder_matches_library(O, pkg, qt):
+    """the oracle's GGUF encoder writes the library's bytes, so the CPU
+    reference arm of bench.py can build the seeded model without loading
+    libinferno_b200.so and still run the same model as the GPU arm"""
+    rng = np.random.default_rng(11 + qt)
+    for std in (0.02, 0.5, 3.0):
+        x = (rng.standard_normal((48, 1024)) * std).astype(np.float32)
+        assert np.array_equal(O.quantize(qt, x), pkg.quantize(qt, x))
+
+
+def test_synth_model_same_bytes_with_oracle_encoder(O, pkg, tmp_path):
+    from inferno_b200 import synth
+    a = synth.build(str(tmp_path / "lib.gguf"), "mini", 3)
+    b = synth.build(str(tmp_path / "oracle.gguf"), "mini", 3, quantize=O.quantize)
+    assert open(a, "rb").read() == open(b, "rb").read()
