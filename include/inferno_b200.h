@@ -152,7 +152,8 @@ int ifr_quantize(int type, const float *x, int64_t rows, int64_t cols, uint8_t *
  *           softmax(draft/T) with u_d
  *   uniforms [batch][2*gamma+1] (dev): u_d[gamma], u_a[gamma], u_rb
  *   accept_count [batch], out_tokens [batch][gamma+1] (-1 past the emitted
- *   tokens), draft_out [batch][gamma] or NULL.  Bit-exact with the oracle. */
+ *   tokens), draft_out [batch][gamma] or NULL.  Bit-exact with the oracle.
+ *   batch * (2 * gamma + 1) <= 65535, else IFR_ERR_ARG. */
 int ifr_accept(ifr_ctx *ctx, const float *target, const float *draft,
                const int32_t *draft_tokens, const float *uniforms, int batch,
                int gamma, int vocab, float temperature, int32_t *accept_count,
@@ -169,7 +170,9 @@ int ifr_accept(ifr_ctx *ctx, const float *target, const float *draft,
  * one-time set-up (module load, symbol lookup): make it once before stream
  * capture or timed work.  The array is shared by all callers on the device:
  * calls that can overlap (other streams or contexts on that device) race and
- * must be ordered by the caller. */
+ * must be ordered by the caller.  The set-up is cached for the life of the
+ * process: after a device reset (cudaDeviceReset, or a host runtime that
+ * resets the device's primary context) do not call it on that device again. */
 int ifr_accept_noalloc(ifr_ctx *ctx, const float *target, const float *draft,
                        const int32_t *draft_tokens, const float *uniforms, int batch,
                        int gamma, int vocab, float temperature, int32_t *accept_count,

@@ -947,6 +947,11 @@ cudaError_t apply_penalties(float *logits, int rows, int V, const int32_t *seen,
 // ------------------------------------------------ allocation-free entry ------
 // ifr_accept_noalloc: the sampled verification of ifr_accept with its scratch
 // in a file-scope device array instead of the context's cudaMalloc'd buffer.
+// The array's device address is looked up once per device and cached for the
+// life of the process; a device reset (cudaDeviceReset, or a host runtime
+// resetting the device's primary context) reloads the module at another
+// address, so the cached set-up is then stale and this entry point must not
+// be used on that device again.
 // Every scratch word is written by an earlier launch of the same call before
 // it is read (chunk_stats -> cmax/csum, row_decide -> rstat/xdraft/okflag,
 // finish -> rchunk), so nothing has to start at zero.  The one array per
@@ -999,6 +1004,9 @@ extern "C" int ifr_accept_noalloc(ifr_ctx *c, const float *target, const float *
         return ifr_fail(IFR_ERR_ARG, "NULL argument");
     if (batch < 1 || gamma < 1 || gamma > 64 || vocab < 1)
         return ifr_fail(IFR_ERR_ARG, "invalid sizes batch=%d gamma=%d vocab=%d", batch, gamma, vocab);
+    if ((int64_t)batch * (2 * gamma + 1) > ifr::kAcceptMaxRows)
+        return ifr_fail(IFR_ERR_ARG, "batch=%d gamma=%d: batch * (2 gamma + 1) logits rows exceed %d", batch, gamma,
+                        ifr::kAcceptMaxRows);
     if (!(temperature > 0.f) || !(temperature < 1e30f))
         return ifr_fail(IFR_ERR_ARG, "temperature must be finite and > 0 (got %g)", (double)temperature);
     const int64_t need = ifr::accept_scratch_bytes(batch, gamma, vocab);

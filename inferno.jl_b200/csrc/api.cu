@@ -387,6 +387,9 @@ int ifr_accept(ifr_ctx *c, const float *target, const float *draft, const int32_
         return fail(IFR_ERR_ARG, "NULL argument");
     if (batch < 1 || gamma < 1 || gamma > 64 || vocab < 1)
         return fail(IFR_ERR_ARG, "invalid sizes batch=%d gamma=%d vocab=%d", batch, gamma, vocab);
+    if ((int64_t)batch * (2 * gamma + 1) > ifr::kAcceptMaxRows)
+        return fail(IFR_ERR_ARG, "batch=%d gamma=%d: batch * (2 gamma + 1) logits rows exceed %d", batch, gamma,
+                    ifr::kAcceptMaxRows);
     if (!(temperature > 0.f) || !(temperature < 1e30f))
         return fail(IFR_ERR_ARG, "temperature must be finite and > 0 (got %g); use ifr_accept_greedy for T=0", (double)temperature);
     DeviceGuard g(c->device);

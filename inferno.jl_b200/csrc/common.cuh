@@ -77,6 +77,9 @@ int64_t qgemm_dense_scratch_bytes(const QTensor &t, int ncols);  // -1: unsuppor
 cudaError_t read_mma_error(int *flag, cudaStream_t s);
 // host encoder (encode.cpp): 0 on success
 int quantize_host(int type, const float *x, int64_t rows, int64_t cols, uint8_t *out);
+// sampled acceptance: its per-row statistics kernel has one grid row per
+// logits row (gridDim.y), so batch * (2 gamma + 1) is bounded by 65535
+constexpr int kAcceptMaxRows = 65535;
 // device-side error flag set by bounded waits that ran out (read and cleared)
 cudaError_t read_device_error(int *flag, cudaStream_t s);
 // the small-N kernels of one weight format (one translation unit per format,

@@ -78,3 +78,17 @@ def test_row_bytes(pkg):
     assert pkg.row_bytes(pkg.TYPE_Q8_0, 1152) == 36 * 34
     with pytest.raises(ValueError):
         pkg.row_bytes(pkg.TYPE_Q4_K, 1000)
+
+
+def test_accept_rejects_too_many_rows_without_gpu(pkg):
+    """batch * (2 gamma + 1) logits rows above 65535 (the statistics kernel's
+    grid rows) are IFR_ERR_ARG in both acceptance entry points, checked
+    before the context is used (a dummy context pointer is never touched)"""
+    L = pkg.load()
+    dummy = ctypes.create_string_buffer(4096)
+    p = ctypes.cast(dummy, ctypes.c_void_p)
+    for fn in ("ifr_accept", "ifr_accept_noalloc"):
+        # 8000 x 9 rows at a tiny vocabulary: small scratch, too many rows
+        rc = getattr(L, fn)(p, p, p, None, p, 8000, 4, 16, ctypes.c_float(1.0), p, p, None)
+        assert rc == pkg._lib.IFR_ERR_ARG, fn
+        assert b"rows exceed 65535" in L.ifr_last_error(), fn

@@ -80,3 +80,60 @@ def test_accept_noalloc_rejects_oversize(pkg, ctx):
     rc, _ = _call(load(), "ifr_accept_noalloc", ctx, dev, B, G, V, 1.0)
     assert rc == IFR_ERR_ARG
     assert "scratch" in _err() and "ifr_accept" in _err()
+
+
+def _torch_case(B, G, V, seed, device="cuda"):
+    import torch
+    gen = torch.Generator(device=device).manual_seed(seed)
+    tgt = torch.randn(B, G + 1, V, generator=gen, device=device) * 3
+    dft = tgt[:, :G] + torch.randn(B, G, V, generator=gen, device=device)
+    u = torch.rand(B, 2 * G + 1, generator=gen, device=device)
+    return [tgt.contiguous(), dft.contiguous(), u]
+
+
+def test_accept_noalloc_at_scratch_limit(pkg, ctx):
+    """batch 341, gamma 5, vocab 65536 needs exactly the 1 MiB of fixed
+    scratch: accepted and identical to ifr_accept; one more sequence is above
+    the limit and rejected"""
+    import torch
+    from inferno_b200._lib import IFR_ERR_ARG, load
+    lib = load()
+    B, G, V = 341, 5, 65536
+    dev = _torch_case(B, G, V, 5)
+    rc, ref = _call(lib, "ifr_accept", ctx, dev, B, G, V, 0.8)
+    assert rc == 0, _err()
+    rc, got = _call(lib, "ifr_accept_noalloc", ctx, dev, B, G, V, 0.8)
+    assert rc == 0, _err()
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    del dev
+    rc, _ = _call(lib, "ifr_accept_noalloc", ctx, [torch.zeros(1, device="cuda")] * 3, B + 1, G, V, 0.8)
+    assert rc == IFR_ERR_ARG and "scratch" in _err()
+
+
+def test_accept_noalloc_other_device(pkg):
+    """a context on device 1 while device 0 is current: the one-time set-up
+    looks the array up on device 1, and results match ifr_accept there"""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from inferno_b200._lib import load
+    lib = load()
+    torch.cuda.set_device(0)
+    c1 = pkg.Context(1)
+    B, G, V = 8, 4, 151936
+    dev = _torch_case(B, G, V, 9, device="cuda:1")
+    with torch.cuda.device(1):
+        outs_ref = tuple(t.to("cuda:1") for t in _outputs(B, G))
+        outs_got = tuple(t.to("cuda:1") for t in _outputs(B, G))
+    assert torch.cuda.current_device() == 0
+    rc, ref = _call(lib, "ifr_accept", c1, dev, B, G, V, 1.1, outs_ref)
+    assert rc == 0, _err()
+    rc, got = _call(lib, "ifr_accept_noalloc", c1, dev, B, G, V, 1.1, outs_got)
+    assert rc == 0, _err()
+    assert torch.cuda.current_device() == 0
+    torch.cuda.synchronize(1)
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    c1.close()
