@@ -536,6 +536,12 @@ def run_spec(args):
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = spec_cpu_baseline(path, prompt, G, steps=3)
+    # the other single-GPU configs as extra keys of the same line (one GPU
+    # only; at N > 1 the line is the replicas' throughput)
+    extras = {}
+    if ws == 1 and not args.no_extras:
+        extras["config3_accept"] = accept_extra(pkg, local, reps=max(3, args.steps // 2))
+        extras["config2_sweep"] = sweep_extra(pkg, local)
     if rank == 0:
         peak, peak_kind = measured_peaks()
         step_bytes = spec_bytes_per_step(info, G)
@@ -574,11 +580,95 @@ def run_spec(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     barrier(ws)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def accept_extra(pkg, device, reps=5):
+    """BASELINE config 3 on this GPU: sampled acceptance (ifr_accept) of 64
+    sequences x draft length 5 over vocab 151936 at T = 0.8, target ~N(0, 3),
+    draft = target + N(0, 1), seeded uniforms; logits resident in HBM (428 MB,
+    above L2).  CUDA events around each call on the context's stream; the
+    roofline bytes are one read of all logits."""
+    import torch
+    B, G, V, T = 64, 5, 151936, 0.8
+    ctx = pkg.Context(device)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    tgt = torch.randn(B, G + 1, V, generator=gen, device="cuda") * 3
+    dft = (tgt[:, :G] + torch.randn(B, G, V, generator=gen, device="cuda")).contiguous()
+    u = torch.rand(B, 2 * G + 1, generator=gen, device="cuda")
+    for _ in range(3):
+        ctx.accept(tgt, dft, u, T)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in ev:
+        a.record(stream)
+        acc, _, _ = ctx.accept(tgt, dft, u, T)
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    nbytes = B * (2 * G + 1) * V * 4
+    peak, kind = measured_peaks()
+    r = {"workload": "BASELINE config 3: 64 x gamma 5 x vocab 151936, T 0.8, supplied uniforms",
+         "kernels": "chunk_stats + row_decide + finish (3 launches per call)",
+         "ms_per_call": round(ms, 4), "sequences_per_s": round(B / (ms * 1e-3), 1),
+         "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1), "peak": peak,
+                      "peak_kind": kind, "unit": "GB/s", "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                      "algorithmic_bytes_per_call": nbytes},
+         "mean_accept": round(float(acc.float().mean()), 3), "calls_timed": reps}
+    del tgt, dft
+    ctx.close()
+    return r
+
+
+def sweep_extra(pkg, device):
+    """BASELINE config 2 on this GPU: every format x shape at N = 5 columns,
+    one CUDA-event pair per launch (mean of 3 after 2 warm-up passes), in the
+    reference's arithmetic (Q8_K activations, the default) and with exact f32
+    activations; weights resident, 2.3 GB per pass (above L2)"""
+    import torch
+    ctx = pkg.Context(device)
+    rng = np.random.default_rng(1234)
+    Ws, Xs, Ys, byts, names = [], [], [], [], []
+    for qt, name in FORMATS:
+        for (M, K) in SHAPES:
+            Ws.append(ctx.upload(qt, make_weights(pkg, qt, M, K, rng), M, K))
+            Xs.append(torch.from_numpy(rng.normal(0, 1, (NCOLS, K)).astype(np.float32)).cuda())
+            Ys.append(torch.empty(NCOLS, M, dtype=torch.float32, device="cuda"))
+            byts.append(Ws[-1].algorithmic_bytes())
+            names.append(f"{name} {M}x{K}")
+    stream = torch.cuda.current_stream()
+    peak, kind = measured_peaks()
+    out = {"workload": "BASELINE config 2: Q4_K/Q5_K/Q6_K/Q8_0 x (4096x4096, 12288x4096, 4096x12288, 151936x4096), N = 5",
+           "peak": peak, "peak_kind": kind}
+    for act, label in ((1, "q8k_activations"), (0, "exact_activations")):
+        ctx.set_activation(act)
+        for _ in range(2):
+            for i, W in enumerate(Ws):
+                ctx.qgemm(W, Xs[i], Ys[i])
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in Ws]
+              for _ in range(3)]
+        for r in range(3):
+            for i, W in enumerate(Ws):
+                ev[r][i][0].record(stream)
+                ctx.qgemm(W, Xs[i], Ys[i])
+                ev[r][i][1].record(stream)
+        torch.cuda.synchronize()
+        d = {}
+        for i, nm in enumerate(names):
+            us = float(np.mean([ev[r][i][0].elapsed_time(ev[r][i][1]) for r in range(3)])) * 1e3
+            d[nm] = {"us": round(us, 2), "GBps": round(byts[i] / us / 1e3, 1),
+                     "frac": round(byts[i] / us / 1e3 / peak, 3)}
+        out[label] = d
+    for W in Ws:
+        W.free()
+    ctx.close()
+    return out
 
 
 BATCH_PRESET, BATCH_SEED = "9b", 0
@@ -998,6 +1088,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048, help="prompt tokens per request (batch workload)")
     ap.add_argument("--gamma", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="spec workload: skip the config-2/3 extra keys")
     ap.add_argument("--act", type=int, default=None, choices=[0, 1],
                     help="K-quant GEMV activations: 0 = exact f32 (default of the model workloads), "
                          "1 = Q8_K (the reference's kernels; default of the sweep)")

@@ -8,6 +8,7 @@ Presets follow the benchmark configurations:
   9b    hidden 4096, 32 layers, 16 q / 4 kv heads x 256, SSM 32 heads x 128,
         FFN 12288, vocab 151936; Q4_K matmuls, Q6_K ffn_down and lm_head
   mini  a small model of the same structure for fast tests
+  9b_narrow, gemma_narrow  the large configs' widths with 4 / 2 layers (parity)
 Weights are N(0, 0.02) (the layer norms, which GGUF stores as 1 + w, are
 1 + N(0, 0.02); ssm_a = -exp(N(0, 0.5)); conv1d N(0, 0.5)), quantized with the
 library's own encoder.  Presets with `row_pool` (9b) draw that many rows per
@@ -46,6 +47,19 @@ PRESETS = {
                         ffn=6912, vocab=262144, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
                         attn_every=1, mat=G.GGML_Q8_0, down=G.GGML_Q8_0, emb=G.GGML_Q8_0, mtp=False,
                         context=8192, row_pool=1024),
+    # parity models at the large configs' widths with few layers, so the CPU
+    # oracle can follow them: 9b_narrow keeps every width of "9b" (the batched
+    # SSM kernel at head dim 128, attention at head dim 256, FFN 12288, Q6_K
+    # down) with 3 SSM layers + 1 attention layer; gemma_narrow keeps the
+    # Gemma4-shape target's widths with 2 layers and a 32768-token vocabulary
+    "9b_narrow": dict(hidden=4096, n_layers=4, n_head=16, n_kv_head=4, head_dim=256, rope_frac=0.25,
+                      ffn=12288, vocab=151936, ssm_heads=32, ssm_head_dim=128, conv_kernel=4,
+                      attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q6_K, emb=G.GGML_Q6_K, mtp=True,
+                      context=8192, row_pool=1024),
+    "gemma_narrow": dict(hidden=5376, n_layers=2, n_head=32, n_kv_head=16, head_dim=128, rope_frac=0.25,
+                         ffn=21504, vocab=32768, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                         attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q4_K, mtp=False,
+                         context=8192, row_pool=1024),
     # attention-only test model whose heads and FFN units split over 2 ranks
     "tp_mini": dict(hidden=256, n_layers=4, n_head=8, n_kv_head=4, head_dim=64, rope_frac=0.25,
                     ffn=1024, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,

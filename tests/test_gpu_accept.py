@@ -41,6 +41,20 @@ def test_accept_config3_shape_subset(O, ctx):
         assert np.array_equal(g, r)
 
 
+def test_accept_config3_full_batch(O, ctx):
+    """BASELINE config 3 at its stated shape: 64 sequences x draft length 5,
+    vocab 151936, target ~N(0, 3), draft = target + N(0, 1), T = 0.8,
+    supplied seeded uniforms; accept counts, emitted and drawn tokens
+    bit-exact"""
+    rng = np.random.default_rng(3)
+    tgt, dft, u = _case(rng, 64, 5, 151936)
+    got = _run(ctx, tgt, dft, u, 0.8)
+    ref = O.accept(tgt, dft, u, 0.8)
+    for g, r, name in zip(got, ref, ("accept_count", "out_tokens", "draft_tokens")):
+        assert np.array_equal(g, r), name
+    assert 0 < ref[0].mean() < 5  # a mix of acceptances, not a degenerate case
+
+
 def test_accept_given_drafts(O, ctx):
     rng = np.random.default_rng(34)
     B, G, V = 6, 4, 4000

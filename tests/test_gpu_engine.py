@@ -195,3 +195,49 @@ def test_step_in_parts_forced_and_errors(mini):
     first = ref.prefill(np.concatenate([np.asarray(prompt, np.int32), np.array([g0, 77], np.int32)]))
     st.spec_step(G)
     assert st.read()[0][n0 + 1] == first
+
+
+def test_config1_128_greedy_tokens_every_step(O, pkg, ctx):
+    """BASELINE config 1 end to end: the seeded tiny model, 128-token prompt,
+    128 greedy tokens by speculative decoding (gamma 4).  Random weights make
+    the MTP drafts miss, so the drafts are forced from the oracle's greedy
+    continuation in a repeating plan - all accepted, a wrong third draft, a
+    wrong first draft - which runs the full-accept and partial-accept
+    rollbacks (SSM replay record, conv history, KV overwrite) at config-1
+    shapes.  Every step: verify logits within 1e-4 of the oracle, accept
+    counts and emitted tokens equal; the 128 tokens equal plain greedy."""
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model, State
+    path = synth.cached("tiny", seed=0)
+    model = Model(ctx, path)
+    V = model.info.vocab
+    om = O.OracleModel(gguf.GGUFFile(path), 300)
+    prompt = synth.prompt(V, 128, seed=0)
+    n_gen, G = 128, 4
+    greedy = om.greedy(list(prompt), n_gen + G + 1)
+    st = State(model, 300)
+    emitted = [int(st.prefill(prompt))]
+    plans, kinds, accs, logits = [], [0, 1, 0, 2], [], []
+    while len(emitted) < n_gen:
+        k = kinds[len(plans) % len(kinds)]
+        d = list(greedy[len(emitted):len(emitted) + G])
+        if k == 1:
+            d[2] = (d[2] + 1) % V
+        elif k == 2:
+            d[0] = (d[0] + 1) % V
+        plans.append(d)
+        st.spec_step(G, d)
+        logits.append(st.last_verify()[0])
+        toks, pos, acc, _ = st.read()
+        accs.append(acc)
+        assert acc == {0: G, 1: 2, 2: 0}[k], (len(plans), acc)
+        emitted = [int(t) for t in toks]
+    assert emitted[:n_gen] == greedy[:n_gen]
+    out, ref = om.spec_decode(list(prompt), len(plans), G, drafts=lambda s: plans[s])
+    assert emitted == out
+    for s, r in enumerate(ref):
+        assert r["acc"] == accs[s], s
+        assert O.norm_rel(logits[s], r["logits"]).max() < LOGIT_TOL, s
+    st.free()
+    model.free()
+    om.close()

@@ -107,16 +107,20 @@ def _rank_main(rank, world, uid, path, prompt, G, steps, drafts_all, q):
     q.put((rank, toks, logits))
 
 
-def test_tp_two_ranks_match_oracle(O, tpm):
+@pytest.mark.parametrize("preset", ["tp_mini", "gemma_narrow"])
+def test_tp_two_ranks_match_oracle(O, preset):
+    """tp_mini, and gemma_narrow: the Gemma4-shape target's widths (hidden
+    5376, 32 q / 16 kv x 128, FFN 21504 = 84 units split 42/42) with 2 layers"""
     import torch
     import torch.multiprocessing as mp
     from inferno_b200.engine import Comm
-    from inferno_b200 import synth
+    from inferno_b200 import synth, gguf
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     if not Comm.available():
         pytest.skip("NCCL not available")
-    path, om = tpm
+    path = synth.cached(preset, seed=1)
+    om = O.OracleModel(gguf.GGUFFile(path), 512)
     prompt = synth.prompt(om.vocab, 20, seed=4)
     G, steps = 3, 4
     greedy = om.greedy(list(prompt), 64)
@@ -140,6 +144,7 @@ def test_tp_two_ranks_match_oracle(O, tpm):
     for s in range(steps):
         full = np.concatenate([res[0][1][s], res[1][1][s]], axis=1)
         assert O.norm_rel(full, ref[s]["logits"]).max() < LOGIT_TOL, s
+    om.close()
 
 
 def _fixed(greedy, s, G, vocab):
