@@ -615,7 +615,7 @@ def accept_extra(pkg, device, reps=5):
     nbytes = B * (2 * G + 1) * V * 4
     peak, kind = measured_peaks()
     r = {"workload": "BASELINE config 3: 64 x gamma 5 x vocab 151936, T 0.8, supplied uniforms",
-         "kernels": "chunk_stats + row_decide + finish (3 launches per call)",
+         "kernels": "chunk_stats + row_decide + resid_chunks + finish (4 launches per call)",
          "ms_per_call": round(ms, 4), "sequences_per_s": round(B / (ms * 1e-3), 1),
          "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1), "peak": peak,
                       "peak_kind": kind, "unit": "GB/s", "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),

@@ -177,6 +177,19 @@ int ifr_accept_noalloc(ifr_ctx *ctx, const float *target, const float *draft,
                        const int32_t *draft_tokens, const float *uniforms, int batch,
                        int gamma, int vocab, float temperature, int32_t *accept_count,
                        int32_t *out_tokens, int32_t *draft_out);
+/* sampled verification with the sampler's filters (replaces the filtered
+ * draws of src/SpeculativeDecoding.jl:57,102, which call
+ * CommonOps.softmax_sample_scratch!, src/CommonOps.jl:196-318): top_k,
+ * top_p and min_p (as in ifr_sample: 0 / 1 / 0 turn them off) and the
+ * temperature applied to every target and draft row; drafts drawn from the
+ * filtered draft rows with u_d, the ratio test and the residual
+ * max(p_t - p_d, 0) over the filtered distributions, the bonus token from
+ * the filtered last target row.  Same layouts as ifr_accept (drafts are
+ * always drawn here); finite logits; vocab <= 524288; parameter errors as in
+ * ifr_sample.  Bit-exact with the oracle (or_accept_filtered). */
+int ifr_accept_filtered(ifr_ctx *ctx, const float *target, const float *draft, const float *uniforms,
+                        int batch, int gamma, int vocab, float temperature, int top_k, float top_p,
+                        float min_p, int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out);
 /* greedy verification (src/ModelCPU.jl:2099-2115): accept while
  * argmax(target[i]) == draft[i], then emit the target argmax */
 int ifr_accept_greedy(ifr_ctx *ctx, const float *target, const int32_t *draft_tokens,

@@ -194,6 +194,21 @@ class Context:
                                 _ptr(dout)))
         return acc, out, dout
 
+    def accept_filtered(self, target, draft, uniforms, temperature, top_k=0, top_p=1.0, min_p=0.0):
+        """sampled verification on the top-k / top-p / min-p filtered
+        distributions; returns (accept_count, out_tokens, draft_tokens)"""
+        torch = self.torch
+        B, G1, V = target.shape
+        G = G1 - 1
+        dev = target.device
+        acc = torch.empty(B, dtype=torch.int32, device=dev)
+        out = torch.empty(B, G + 1, dtype=torch.int32, device=dev)
+        dout = torch.empty(B, G, dtype=torch.int32, device=dev)
+        check(load().ifr_accept_filtered(self.handle, _ptr(target), _ptr(draft), _ptr(uniforms), B, G, V,
+                                         float(temperature), int(top_k), float(top_p), float(min_p), _ptr(acc),
+                                         _ptr(out), _ptr(dout)))
+        return acc, out, dout
+
     def sample(self, logits, uniforms, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, out=None):
         """logits [..., vocab] f32 (device), one uniform per row -> int32 tokens
         (0-based; -1 marks a row with NaN or +Inf)"""

@@ -46,6 +46,7 @@ SIGNATURES = {
     "ifr_accept": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
     "ifr_ctx_set_activation": (_i, [_vp, _i]),
     "ifr_accept_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp]),
+    "ifr_accept_filtered": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _f, _f, _vp, _vp, _vp]),
     "ifr_accept_greedy": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "ifr_sample": (_i, [_vp, _vp, _i, _i, _f, _i, _f, _f, _vp, _vp]),
     "ifr_draft_mtp": (_i, [_vp, _i, _vp]),

@@ -14,7 +14,8 @@
 //
 // Launches: chunk_stats (one CTA per row chunk, the only full pass over the
 // logits), row_decide (per sequence and row: row stats, draft draw, ratio
-// test), finish (per sequence: residual or bonus sample).
+// test), resid_chunks (one CTA per chunk of each sequence's rejected row:
+// residual chunk sums), finish (per sequence: residual or bonus sample).
 #include "common.cuh"
 #include <math_constants.h>
 #include <climits>
@@ -50,6 +51,38 @@ __device__ __forceinline__ float ifr_exp(float x) {
 __device__ __forceinline__ float elem_e(float l, float m, float T) {
     return ifr_exp(__fdiv_rn(__fsub_rn(l, m), T));
 }
+
+__device__ __forceinline__ uint32_t f_key(float x) {
+    const uint32_t u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long e_fixed(float e) {
+    return (unsigned long long)__fmul_rn(e, 1073741824.0f);
+}
+
+// the filters' state; w(i, l) = the final weight of element i with logit l
+struct SampleFilter {
+    float M, T, min_p;
+    bool topk, topp;
+    uint32_t key_k, key_p;
+    int cut_k, cut_p;
+    __device__ float ek(int i, float l) const {
+        if (topk) {
+            const uint32_t k = f_key(l);
+            if (!(k > key_k || (k == key_k && i <= cut_k))) return 0.f;
+        }
+        return elem_e(l, M, T);
+    }
+    __device__ float w(int i, float l) const {
+        float e = ek(i, l);
+        if (topp && e > 0.f) {
+            const uint32_t k = __float_as_uint(e);
+            if (!(k > key_p || (k == key_p && i <= cut_p))) e = 0.f;
+        }
+        if (min_p > 0.f && e < min_p) e = 0.f;
+        return e;
+    }
+};
 
 // 256-lane canonical sum; all threads get the result.
 __device__ float canon_sum(float t, float *wsum /* smem [8] */) {
@@ -101,9 +134,15 @@ __device__ __forceinline__ int load8(const float *row, int V, int c, float (&x)[
     return n;
 }
 
+// FILT (filtered acceptance, accept_filtered below): element i of row r
+// counts only when the row's filters keep it (filt[r].w(i, l) > 0); the chunk
+// max stays over every element; draws take the first element with a
+// positive weight and tau <= cumsum, and chunks with a positive mass only.
+template <bool FILT>
 __global__ void __launch_bounds__(kNL) chunk_stats_kernel(const float *__restrict__ target,
                                                           const float *__restrict__ draft, int B,
                                                           int G, int V, float T, int nch,
+                                                          const SampleFilter *__restrict__ filt,
                                                           float *__restrict__ cmax,
                                                           float *__restrict__ csum) {
     __shared__ float wbuf[8];
@@ -115,9 +154,18 @@ __global__ void __launch_bounds__(kNL) chunk_stats_kernel(const float *__restric
 #pragma unroll
     for (int q = 0; q < kPER; q++) if (q < n) m = fmaxf(m, x[q]);
     m = block_max(m, wbuf);
+    SampleFilter F;
+    if constexpr (FILT) F = filt[r];
     float t = 0.f;
 #pragma unroll
-    for (int q = 0; q < kPER; q++) if (q < n) t = __fadd_rn(t, elem_e(x[q], m, T));
+    for (int q = 0; q < kPER; q++) {
+        if (q < n) {
+            if constexpr (FILT) {
+                if (!(F.w(c * kCH + kPER * threadIdx.x + q, x[q]) > 0.f)) continue;
+            }
+            t = __fadd_rn(t, elem_e(x[q], m, T));
+        }
+    }
     const float s = canon_sum(t, wbuf);
     if (threadIdx.x == 0) {
         cmax[(int64_t)r * nch + c] = m;
@@ -136,7 +184,9 @@ __device__ RowStat row_stat(const float *cm, const float *cs, int nch, float T) 
 }
 
 // Blocked in-chunk search (all threads): first element with tau <= cumsum of
-// vals; else the last element with val > 0; else the last element.
+// vals (POS: and val > 0); else the last element with val > 0; else the last
+// element.
+template <bool POS = false>
 __device__ int chunk_search(const float (&v)[8], int n, int64_t base, float tau, float *lsum,
                             int *res) {
     const int tid = threadIdx.x;
@@ -158,7 +208,7 @@ __device__ int chunk_search(const float (&v)[8], int n, int64_t base, float tau,
     for (int q = 0; q < kPER; q++) {
         if (q < n) {
             cum = __fadd_rn(cum, v[q]);
-            if (hit < 0 && tau <= cum) hit = kPER * tid + q;
+            if (hit < 0 && tau <= cum && (!POS || v[q] > 0.f)) hit = kPER * tid + q;
             if (v[q] > 0.f) lastpos = kPER * tid + q;
             lastany = kPER * tid + q;
         }
@@ -180,19 +230,25 @@ struct SampleSmem {
     float wsum[8];
 };
 
-// sample from softmax(row/T) with uniform u; row stats (M,S) and chunk stats given
+// sample from softmax(row/T) with uniform u; row stats (M,S) and chunk stats
+// given; FILT: over the elements F keeps (F non-null), positive masses only
+template <bool FILT = false>
 __device__ int sample_row(const float *row, int V, const float *cm, const float *cs, int nch,
-                          float T, RowStat st, float u, SampleSmem &sm) {
+                          float T, RowStat st, float u, SampleSmem &sm, const SampleFilter *F = nullptr) {
     if (threadIdx.x == 0) {
         float tau = __fmul_rn(u, st.S), P = 0.f;
         int csel = -1;
         for (int c = 0; c < nch; c++) {
-            float nP = __fadd_rn(P, __fmul_rn(cs[c], ifr_exp(__fdiv_rn(__fsub_rn(cm[c], st.M), T))));
-            if (tau <= nP) { csel = c; break; }
+            const float mc = __fmul_rn(cs[c], ifr_exp(__fdiv_rn(__fsub_rn(cm[c], st.M), T)));
+            float nP = __fadd_rn(P, mc);
+            if ((!FILT || mc > 0.f) && tau <= nP) { csel = c; break; }
             P = nP;
         }
         if (csel < 0) {
-            for (int c = nch - 1; c >= 0; c--) if (cs[c] > 0.f) { csel = c; break; }
+            for (int c = nch - 1; c >= 0; c--) {
+                const float mc = FILT ? __fmul_rn(cs[c], ifr_exp(__fdiv_rn(__fsub_rn(cm[c], st.M), T))) : cs[c];
+                if (mc > 0.f) { csel = c; break; }
+            }
             if (csel < 0) csel = nch - 1;
             P = 0.f;
             for (int c = 0; c < csel; c++)
@@ -210,21 +266,37 @@ __device__ int sample_row(const float *row, int V, const float *cm, const float 
     const int n = load8(row, V, csel, x);
     const float mc = cm[csel];
 #pragma unroll
-    for (int q = 0; q < kPER; q++) v[q] = q < n ? elem_e(x[q], mc, T) : 0.f;
-    return chunk_search(v, n, (int64_t)csel * kCH, taup, sm.lsum, sm.res);
+    for (int q = 0; q < kPER; q++) {
+        v[q] = q < n ? elem_e(x[q], mc, T) : 0.f;
+        if constexpr (FILT) {
+            if (q < n && !(F->w(csel * kCH + kPER * threadIdx.x + q, x[q]) > 0.f)) v[q] = 0.f;
+        }
+    }
+    return chunk_search<FILT>(v, n, (int64_t)csel * kCH, taup, sm.lsum, sm.res);
 }
 
 __device__ __forceinline__ float weight_of(const float *row, int i, const float *cm, RowStat st, float T) {
     const int c = i / kCH;
     return __fmul_rn(elem_e(__ldg(row + i), cm[c], T), ifr_exp(__fdiv_rn(__fsub_rn(cm[c], st.M), T)));
 }
+// the weight of element i under the row's filters (0 where they drop it)
+template <bool FILT>
+__device__ __forceinline__ float kept_weight_of(const float *row, int i, const float *cm, RowStat st, float T,
+                                                const SampleFilter *F) {
+    if constexpr (FILT) {
+        if (!(F->w(i, __ldg(row + i)) > 0.f)) return 0.f;
+    }
+    return weight_of(row, i, cm, st, T);
+}
 
 // grid (B, G+1): row stats of target row i (and draft row i < G), draft token, ratio test
+template <bool FILT>
 __global__ void __launch_bounds__(kNL) row_decide_kernel(
     const float *__restrict__ target, const float *__restrict__ draft,
     const int32_t *__restrict__ draft_tokens, const float *__restrict__ uniforms, int B, int G, int V,
-    float T, int nch, const float *__restrict__ cmax, const float *__restrict__ csum,
-    float *__restrict__ rstat, int32_t *__restrict__ xdraft, int32_t *__restrict__ okflag) {
+    float T, int nch, const SampleFilter *__restrict__ filt, const float *__restrict__ cmax,
+    const float *__restrict__ csum, float *__restrict__ rstat, int32_t *__restrict__ xdraft,
+    int32_t *__restrict__ okflag) {
     __shared__ SampleSmem sm;
     __shared__ RowStat st_s[2];
     const int b = blockIdx.x, i = blockIdx.y;
@@ -244,21 +316,26 @@ __global__ void __launch_bounds__(kNL) row_decide_kernel(
         rstat[2 * dr + 1] = st_s[1].S;
     }
     __syncthreads();
+    SampleFilter Ft, Fd;
+    if constexpr (FILT) {
+        Ft = filt[tr];
+        Fd = filt[dr];
+    }
     const float *u = uniforms + (int64_t)b * (2 * G + 1);
     int x;
     if (draft_tokens) {
         x = draft_tokens[b * G + i];
     } else {
-        x = sample_row(drow, V, cmax + (int64_t)dr * nch, csum + (int64_t)dr * nch, nch, T, st_s[1],
-                       u[i], sm);
+        x = sample_row<FILT>(drow, V, cmax + (int64_t)dr * nch, csum + (int64_t)dr * nch, nch, T, st_s[1],
+                             u[i], sm, &Fd);
     }
     if (threadIdx.x == 0) {
         int ok;
         if (x < 0 || x >= V) {
             ok = 0;  // invalid supplied draft token: reject
         } else {
-            float pt = __fdiv_rn(weight_of(trow, x, cmax + (int64_t)tr * nch, st_s[0], T), st_s[0].S);
-            float pd = __fdiv_rn(weight_of(drow, x, cmax + (int64_t)dr * nch, st_s[1], T), st_s[1].S);
+            float pt = __fdiv_rn(kept_weight_of<FILT>(trow, x, cmax + (int64_t)tr * nch, st_s[0], T, &Ft), st_s[0].S);
+            float pd = __fdiv_rn(kept_weight_of<FILT>(drow, x, cmax + (int64_t)dr * nch, st_s[1], T, &Fd), st_s[1].S);
             ok = pd > 0.f ? (u[G + i] < __fdiv_rn(pt, pd)) : (pt > 0.f);
         }
         xdraft[b * G + i] = x;
@@ -266,12 +343,66 @@ __global__ void __launch_bounds__(kNL) row_decide_kernel(
     }
 }
 
+// the residual weight max(p_t - p_d, 0) of one element (FILT: 0 for either
+// side where its filters drop the element)
+template <bool FILT>
+__device__ __forceinline__ float resid_w(float lt, float ld, int i, float tcm, float ft, RowStat ts, float dcm,
+                                         float fd, RowStat ds, float T, const SampleFilter &Ft,
+                                         const SampleFilter &Fd) {
+    float pt = __fdiv_rn(__fmul_rn(elem_e(lt, tcm, T), ft), ts.S);
+    float pd = __fdiv_rn(__fmul_rn(elem_e(ld, dcm, T), fd), ds.S);
+    if constexpr (FILT) {
+        if (!(Ft.w(i, lt) > 0.f)) pt = 0.f;
+        if (!(Fd.w(i, ld) > 0.f)) pd = 0.f;
+    }
+    const float r = __fsub_rn(pt, pd);
+    return r > 0.f ? r : 0.f;
+}
+
+// grid (nch, B): chunk c of the residual max(p_t - p_d, 0) of sequence b's
+// rejected row (none when every draft was accepted), canonical sum into
+// rchunk[b][c]; one CTA per chunk, so the pass runs at full width
+template <bool FILT>
+__global__ void __launch_bounds__(kNL) resid_chunks_kernel(
+    const float *__restrict__ target, const float *__restrict__ draft, int B, int G, int V, float T, int nch,
+    const SampleFilter *__restrict__ filt, const float *__restrict__ cmax, const float *__restrict__ rstat,
+    const int32_t *__restrict__ okflag, float *__restrict__ rchunk) {
+    __shared__ float wsum[8];
+    const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    int acc = 0;
+    while (acc < G && okflag[b * G + acc]) acc++;
+    if (acc == G) return;
+    const int tr = b * (G + 1) + acc, dr = B * (G + 1) + b * G + acc;
+    const float *trow = target + (int64_t)tr * V, *drow = draft + (int64_t)(b * G + acc) * V;
+    const float tcm = cmax[(int64_t)tr * nch + c], dcm = cmax[(int64_t)dr * nch + c];
+    const RowStat ts{rstat[2 * tr], rstat[2 * tr + 1]}, ds{rstat[2 * dr], rstat[2 * dr + 1]};
+    SampleFilter Ft, Fd;
+    if constexpr (FILT) {
+        Ft = filt[tr];
+        Fd = filt[dr];
+    }
+    float xt[8], xd[8];
+    const int n = load8(trow, V, c, xt);
+    load8(drow, V, c, xd);
+    const float ft = ifr_exp(__fdiv_rn(__fsub_rn(tcm, ts.M), T));
+    const float fd = ifr_exp(__fdiv_rn(__fsub_rn(dcm, ds.M), T));
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < kPER; q++)
+        if (q < n)
+            t = __fadd_rn(t, resid_w<FILT>(xt[q], xd[q], c * kCH + kPER * tid + q, tcm, ft, ts, dcm, fd, ds, T, Ft,
+                                           Fd));
+    const float sum = canon_sum(t, wsum);
+    if (tid == 0) rchunk[(int64_t)b * nch + c] = sum;
+}
+
 // grid (B): accept count, emitted tokens, residual or bonus sample
+template <bool FILT>
 __global__ void __launch_bounds__(kNL) finish_kernel(
     const float *__restrict__ target, const float *__restrict__ draft,
     const float *__restrict__ uniforms, int B, int G, int V, float T, int nch,
-    const float *__restrict__ cmax, const float *__restrict__ csum, const float *__restrict__ rstat,
-    const int32_t *__restrict__ xdraft, const int32_t *__restrict__ okflag,
+    const SampleFilter *__restrict__ filt, const float *__restrict__ cmax, const float *__restrict__ csum,
+    const float *__restrict__ rstat, const int32_t *__restrict__ xdraft, const int32_t *__restrict__ okflag,
     int32_t *__restrict__ accept_count, int32_t *__restrict__ out_tokens,
     int32_t *__restrict__ draft_out, float *__restrict__ rchunk /* [B][nch] */) {
     __shared__ SampleSmem sm;
@@ -289,35 +420,21 @@ __global__ void __launch_bounds__(kNL) finish_kernel(
     if (acc == G) {
         const int tr = b * (G + 1) + G;
         RowStat st{rstat[2 * tr], rstat[2 * tr + 1]};
-        y = sample_row(target + (int64_t)tr * V, V, cmax + (int64_t)tr * nch, csum + (int64_t)tr * nch,
-                       nch, T, st, ub, sm);
+        SampleFilter Ft;
+        if constexpr (FILT) Ft = filt[tr];
+        y = sample_row<FILT>(target + (int64_t)tr * V, V, cmax + (int64_t)tr * nch, csum + (int64_t)tr * nch,
+                             nch, T, st, ub, sm, &Ft);
     } else {
         const int tr = b * (G + 1) + acc, dr = B * (G + 1) + b * G + acc;
         const float *trow = target + (int64_t)tr * V, *drow = draft + (int64_t)(b * G + acc) * V;
         const float *tcm = cmax + (int64_t)tr * nch, *dcm = cmax + (int64_t)dr * nch;
         const RowStat ts{rstat[2 * tr], rstat[2 * tr + 1]}, ds{rstat[2 * dr], rstat[2 * dr + 1]};
-        float *rc = rchunk + (int64_t)b * nch;
-        // residual chunk sums
-        for (int c = 0; c < nch; c++) {
-            float xt[8], xd[8];
-            const int n = load8(trow, V, c, xt);
-            load8(drow, V, c, xd);
-            const float ft = ifr_exp(__fdiv_rn(__fsub_rn(tcm[c], ts.M), T));
-            const float fd = ifr_exp(__fdiv_rn(__fsub_rn(dcm[c], ds.M), T));
-            float t = 0.f;
-#pragma unroll
-            for (int q = 0; q < kPER; q++) {
-                if (q < n) {
-                    float pt = __fdiv_rn(__fmul_rn(elem_e(xt[q], tcm[c], T), ft), ts.S);
-                    float pd = __fdiv_rn(__fmul_rn(elem_e(xd[q], dcm[c], T), fd), ds.S);
-                    float r = __fsub_rn(pt, pd);
-                    t = __fadd_rn(t, r > 0.f ? r : 0.f);
-                }
-            }
-            float s = canon_sum(t, sm.wsum);
-            if (tid == 0) rc[c] = s;
+        SampleFilter Ft, Fd;
+        if constexpr (FILT) {
+            Ft = filt[tr];
+            Fd = filt[dr];
         }
-        __syncthreads();
+        const float *rc = rchunk + (int64_t)b * nch;  // residual chunk sums (resid_chunks_kernel)
         if (tid == 0) {
             float R = 0.f;
             for (int c = 0; c < nch; c++) R = __fadd_rn(R, rc[c]);
@@ -328,7 +445,7 @@ __global__ void __launch_bounds__(kNL) finish_kernel(
                 csel = -1;
                 for (int c = 0; c < nch; c++) {
                     float nP = __fadd_rn(P, rc[c]);
-                    if (tau <= nP) { csel = c; break; }
+                    if ((!FILT || rc[c] > 0.f) && tau <= nP) { csel = c; break; }
                     P = nP;
                 }
                 if (csel < 0) {
@@ -344,7 +461,7 @@ __global__ void __launch_bounds__(kNL) finish_kernel(
         __syncthreads();
         const int csel = sm.ibc[1];
         if (csel == -2) {
-            y = sample_row(trow, V, tcm, csum + (int64_t)tr * nch, nch, T, ts, ub, sm);
+            y = sample_row<FILT>(trow, V, tcm, csum + (int64_t)tr * nch, nch, T, ts, ub, sm, &Ft);
         } else {
             float xt[8], xd[8], v[8];
             const int n = load8(trow, V, csel, xt);
@@ -352,17 +469,11 @@ __global__ void __launch_bounds__(kNL) finish_kernel(
             const float ft = ifr_exp(__fdiv_rn(__fsub_rn(tcm[csel], ts.M), T));
             const float fd = ifr_exp(__fdiv_rn(__fsub_rn(dcm[csel], ds.M), T));
 #pragma unroll
-            for (int q = 0; q < kPER; q++) {
-                if (q < n) {
-                    float pt = __fdiv_rn(__fmul_rn(elem_e(xt[q], tcm[csel], T), ft), ts.S);
-                    float pd = __fdiv_rn(__fmul_rn(elem_e(xd[q], dcm[csel], T), fd), ds.S);
-                    float r = __fsub_rn(pt, pd);
-                    v[q] = r > 0.f ? r : 0.f;
-                } else {
-                    v[q] = 0.f;
-                }
-            }
-            y = chunk_search(v, n, (int64_t)csel * kCH, sm.bc[1], sm.lsum, sm.res);
+            for (int q = 0; q < kPER; q++)
+                v[q] = q < n ? resid_w<FILT>(xt[q], xd[q], csel * kCH + kPER * tid + q, tcm[csel], ft, ts,
+                                             dcm[csel], fd, ds, T, Ft, Fd)
+                             : 0.f;
+            y = chunk_search<FILT>(v, n, (int64_t)csel * kCH, sm.bc[1], sm.lsum, sm.res);
         }
     }
     if (tid == 0) ot[acc] = y;
@@ -373,9 +484,13 @@ int64_t accept_scratch_bytes(int B, int G, int V) {
     return 2 * rows * nch * 4 + 2 * rows * 4 + 2 * (int64_t)B * G * 4 + (int64_t)B * nch * 4 + 1024;
 }
 
-cudaError_t accept_sampled(const float *target, const float *draft, const int32_t *draft_tokens,
-                           const float *uniforms, int B, int G, int V, float T, int32_t *accept_count,
-                           int32_t *out_tokens, int32_t *draft_out, void *scratch, cudaStream_t s) {
+namespace {
+// the three acceptance launches over the scratch layout of accept_scratch_bytes
+template <bool FILT>
+cudaError_t accept_launch(const float *target, const float *draft, const int32_t *draft_tokens,
+                          const float *uniforms, int B, int G, int V, float T, const SampleFilter *filt,
+                          int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out, void *scratch,
+                          cudaStream_t s) {
     const int nch = (V + kCH - 1) / kCH;
     const int64_t rows = (int64_t)B * (2 * G + 1);
     char *p = (char *)scratch;
@@ -385,12 +500,23 @@ cudaError_t accept_sampled(const float *target, const float *draft, const int32_
     int32_t *xdraft = (int32_t *)p; p += (int64_t)B * G * 4;
     int32_t *okflag = (int32_t *)p; p += (int64_t)B * G * 4;
     float *rchunk = (float *)p;
-    chunk_stats_kernel<<<dim3(nch, (unsigned)rows), kNL, 0, s>>>(target, draft, B, G, V, T, nch, cmax, csum);
-    row_decide_kernel<<<dim3(B, G + 1), kNL, 0, s>>>(target, draft, draft_tokens, uniforms, B, G, V, T,
-                                                     nch, cmax, csum, rstat, xdraft, okflag);
-    finish_kernel<<<B, kNL, 0, s>>>(target, draft, uniforms, B, G, V, T, nch, cmax, csum, rstat, xdraft,
-                                    okflag, accept_count, out_tokens, draft_out, rchunk);
+    chunk_stats_kernel<FILT><<<dim3(nch, (unsigned)rows), kNL, 0, s>>>(target, draft, B, G, V, T, nch, filt, cmax,
+                                                                       csum);
+    row_decide_kernel<FILT><<<dim3(B, G + 1), kNL, 0, s>>>(target, draft, draft_tokens, uniforms, B, G, V, T,
+                                                           nch, filt, cmax, csum, rstat, xdraft, okflag);
+    resid_chunks_kernel<FILT><<<dim3(nch, B), kNL, 0, s>>>(target, draft, B, G, V, T, nch, filt, cmax, rstat,
+                                                           okflag, rchunk);
+    finish_kernel<FILT><<<B, kNL, 0, s>>>(target, draft, uniforms, B, G, V, T, nch, filt, cmax, csum, rstat,
+                                          xdraft, okflag, accept_count, out_tokens, draft_out, rchunk);
     return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t accept_sampled(const float *target, const float *draft, const int32_t *draft_tokens,
+                           const float *uniforms, int B, int G, int V, float T, int32_t *accept_count,
+                           int32_t *out_tokens, int32_t *draft_out, void *scratch, cudaStream_t s) {
+    return accept_launch<false>(target, draft, draft_tokens, uniforms, B, G, V, T, nullptr, accept_count,
+                                out_tokens, draft_out, scratch, s);
 }
 
 // ------------------------------------------------------------- greedy -------
@@ -575,14 +701,6 @@ cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int 
 //     i with w_i > 0
 constexpr int kSampleMaxChunks = 256;  // vocab <= 256 x 2048
 
-__device__ __forceinline__ uint32_t f_key(float x) {
-    const uint32_t u = __float_as_uint(x);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ unsigned long long e_fixed(float e) {
-    return (unsigned long long)__fmul_rn(e, 1073741824.0f);
-}
-
 struct SampleFSmem {
     unsigned cnt[256];
     unsigned long long sum[256];
@@ -598,30 +716,6 @@ struct SampleFSmem {
     int sel, found, idx;
     float tau;
     int csel;
-};
-
-// the filters' state; w(i, l) = the final weight of element i with logit l
-struct SampleFilter {
-    float M, T, min_p;
-    bool topk, topp;
-    uint32_t key_k, key_p;
-    int cut_k, cut_p;
-    __device__ float ek(int i, float l) const {
-        if (topk) {
-            const uint32_t k = f_key(l);
-            if (!(k > key_k || (k == key_k && i <= cut_k))) return 0.f;
-        }
-        return elem_e(l, M, T);
-    }
-    __device__ float w(int i, float l) const {
-        float e = ek(i, l);
-        if (topp && e > 0.f) {
-            const uint32_t k = __float_as_uint(e);
-            if (!(k > key_p || (k == key_p && i <= cut_p))) e = 0.f;
-        }
-        if (min_p > 0.f && e < min_p) e = 0.f;
-        return e;
-    }
 };
 
 // Radix select, descending, over 32-bit keys key(i, l) of every element, with
@@ -739,47 +833,12 @@ __device__ unsigned long long cut_count(unsigned long long above, unsigned long 
     return n;
 }
 
-__global__ void __launch_bounds__(kNL) sample_kernel(const float *__restrict__ logits, int V, float T, int top_k,
-                                                     float top_p, float min_p, const float *__restrict__ uniforms,
-                                                     int32_t *__restrict__ out) {
-    __shared__ SampleFSmem sm;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
-    const float *row = logits + (int64_t)r * V;
-    const int nch = (V + kCH - 1) / kCH;
-    pdl_trigger();
-    pdl_wait();
-    // validation, max and its first index
-    float bv = -CUDART_INF_F;
-    int bi = INT_MAX, bad = 0;
-    for (int c = 0; c < nch; c++) {
-        float x[8];
-        const int n = load8(row, V, c, x);
-        for (int q = 0; q < n; q++) {
-            const float v = x[q];
-            if (v != v || v == CUDART_INF_F) bad = 1;
-            else if (v != -CUDART_INF_F && v > bv) { bv = v; bi = c * kCH + kPER * tid + q; }
-        }
-    }
-    bad = __syncthreads_or(bad);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-    }
-    if (lane == 0) { sm.bv[warp] = bv; sm.bi[warp] = bi; }
-    __syncthreads();
-    float M = sm.bv[0];
-    int g = sm.bi[0];
-    for (int w = 1; w < kNL / 32; w++)
-        if (sm.bi[w] != INT_MAX && (g == INT_MAX || sm.bv[w] > M || (sm.bv[w] == M && sm.bi[w] < g))) {
-            M = sm.bv[w];
-            g = sm.bi[w];
-        }
-    if (bad || g == INT_MAX || T == 0.f || V == 1) {
-        if (tid == 0) out[r] = bad ? -1 : (g == INT_MAX ? 0 : g);
-        return;
-    }
+// the filters of one row (all threads; M = the row's max finite logit):
+// top-k by radix select on the logits' keys, the exact top-p cut on the
+// integer weights, min-p as a threshold (the rules above)
+__device__ SampleFilter build_filter(const float *row, int V, int nch, float M, float T, int top_k, float top_p,
+                                     float min_p, SampleFSmem &sm) {
+    const int tid = threadIdx.x;
     SampleFilter F;
     F.M = M;
     F.T = T;
@@ -830,6 +889,51 @@ __global__ void __launch_bounds__(kNL) sample_kernel(const float *__restrict__ l
             }
         }
     }
+    return F;
+}
+
+__global__ void __launch_bounds__(kNL) sample_kernel(const float *__restrict__ logits, int V, float T, int top_k,
+                                                     float top_p, float min_p, const float *__restrict__ uniforms,
+                                                     int32_t *__restrict__ out) {
+    __shared__ SampleFSmem sm;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
+    const float *row = logits + (int64_t)r * V;
+    const int nch = (V + kCH - 1) / kCH;
+    pdl_trigger();
+    pdl_wait();
+    // validation, max and its first index
+    float bv = -CUDART_INF_F;
+    int bi = INT_MAX, bad = 0;
+    for (int c = 0; c < nch; c++) {
+        float x[8];
+        const int n = load8(row, V, c, x);
+        for (int q = 0; q < n; q++) {
+            const float v = x[q];
+            if (v != v || v == CUDART_INF_F) bad = 1;
+            else if (v != -CUDART_INF_F && v > bv) { bv = v; bi = c * kCH + kPER * tid + q; }
+        }
+    }
+    bad = __syncthreads_or(bad);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { sm.bv[warp] = bv; sm.bi[warp] = bi; }
+    __syncthreads();
+    float M = sm.bv[0];
+    int g = sm.bi[0];
+    for (int w = 1; w < kNL / 32; w++)
+        if (sm.bi[w] != INT_MAX && (g == INT_MAX || sm.bv[w] > M || (sm.bv[w] == M && sm.bi[w] < g))) {
+            M = sm.bv[w];
+            g = sm.bi[w];
+        }
+    if (bad || g == INT_MAX || T == 0.f || V == 1) {
+        if (tid == 0) out[r] = bad ? -1 : (g == INT_MAX ? 0 : g);
+        return;
+    }
+    const SampleFilter F = build_filter(row, V, nch, M, T, top_k, top_p, min_p, sm);
     // draw: chunk sums of the final weights in the canonical order
     for (int c = 0; c < nch; c++) {
         float x[8];
@@ -902,6 +1006,53 @@ cudaError_t sample_filtered(const float *logits, int rows, int V, float T, int t
                             const float *uniforms, int32_t *out, cudaStream_t s) {
     if ((V + kCH - 1) / kCH > kSampleMaxChunks) return cudaErrorInvalidValue;
     return launch_k(sample_kernel, dim3(rows), dim3(kNL), 0, s, logits, V, T, top_k, top_p, min_p, uniforms, out);
+}
+
+// ------------------------------------------------ filtered acceptance ------
+// The sampled verification on the distributions the sampler's filters leave:
+// top-k, top-p and min-p (the rules of sample_kernel) applied with the same
+// temperature to every target and draft row.  The reference draws its drafts
+// and the bonus token from filtered distributions
+// (src/SpeculativeDecoding.jl:57,102 via CommonOps.softmax_sample_scratch!);
+// filtering the target and draft rows of the ratio test and the residual as
+// well keeps every emitted token distributed as the filtered target.  One
+// filter pass per row (filter_rows_kernel: a CTA per row, the filter's few
+// scalars into scratch), then the three acceptance launches with FILT.
+// Restated on the CPU by oracle/accept.c (or_accept_filtered).
+__global__ void __launch_bounds__(kNL) filter_rows_kernel(const float *__restrict__ target,
+                                                          const float *__restrict__ draft, int B, int G, int V,
+                                                          float T, int top_k, float top_p, float min_p,
+                                                          SampleFilter *__restrict__ filt) {
+    __shared__ SampleFSmem sm;
+    __shared__ float wbuf[8];
+    const int r = blockIdx.x;
+    const float *row = row_ptr(target, draft, r, B, G, V);
+    const int nch = (V + kCH - 1) / kCH;
+    float m = -CUDART_INF_F;
+    for (int c = 0; c < nch; c++) {
+        float x[8];
+        const int n = load8(row, V, c, x);
+        for (int q = 0; q < n; q++) m = fmaxf(m, x[q]);
+    }
+    const float M = block_max(m, wbuf);
+    const SampleFilter F = build_filter(row, V, nch, M, T, top_k, top_p, min_p, sm);
+    if (threadIdx.x == 0) filt[r] = F;
+}
+
+int64_t accept_filtered_scratch_bytes(int B, int G, int V) {
+    return accept_scratch_bytes(B, G, V) + (int64_t)B * (2 * G + 1) * (int64_t)sizeof(SampleFilter) + 256;
+}
+
+cudaError_t accept_filtered(const float *target, const float *draft, const float *uniforms, int B, int G, int V,
+                            float T, int top_k, float top_p, float min_p, int32_t *accept_count,
+                            int32_t *out_tokens, int32_t *draft_out, void *scratch, cudaStream_t s) {
+    if ((V + kCH - 1) / kCH > kSampleMaxChunks) return cudaErrorInvalidValue;
+    const int64_t rows = (int64_t)B * (2 * G + 1);
+    const int64_t base = (accept_scratch_bytes(B, G, V) + 255) / 256 * 256;
+    SampleFilter *filt = reinterpret_cast<SampleFilter *>((char *)scratch + base);
+    filter_rows_kernel<<<(unsigned)rows, kNL, 0, s>>>(target, draft, B, G, V, T, top_k, top_p, min_p, filt);
+    return accept_launch<true>(target, draft, nullptr, uniforms, B, G, V, T, filt, accept_count, out_tokens,
+                               draft_out, scratch, s);
 }
 
 // presence then repetition penalty (src/ModelCPU.jl:1202-1211,1237-1238;

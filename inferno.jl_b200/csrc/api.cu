@@ -225,7 +225,7 @@ int ifr_ctx_reserve_accept(ifr_ctx *c, int batch, int gamma, int vocab) {
     if (!c || batch < 1 || gamma < 0 || gamma > 64 || vocab < 1)
         return fail(IFR_ERR_ARG, "invalid reserve arguments");
     DeviceGuard g(c->device);
-    int64_t need = ifr::accept_scratch_bytes(batch, gamma < 1 ? 1 : gamma, vocab);
+    int64_t need = ifr::accept_filtered_scratch_bytes(batch, gamma < 1 ? 1 : gamma, vocab);
     int64_t g2 = ifr::accept_greedy_scratch_bytes(batch, gamma, vocab);
     return ensure_scratch(c, (size_t)(need > g2 ? need : g2));
 }
@@ -399,6 +399,32 @@ int ifr_accept(ifr_ctx *c, const float *target, const float *draft, const int32_
                                        temperature, accept_count, out_tokens, draft_out, c->scratch,
                                        c->stream),
                    "accept launch");
+    return IFR_OK;
+}
+
+int ifr_accept_filtered(ifr_ctx *c, const float *target, const float *draft, const float *uniforms, int batch,
+                        int gamma, int vocab, float temperature, int top_k, float top_p, float min_p,
+                        int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out) {
+    if (!c || !target || !draft || !uniforms || !accept_count || !out_tokens)
+        return fail(IFR_ERR_ARG, "NULL argument");
+    if (batch < 1 || gamma < 1 || gamma > 64 || vocab < 1 || vocab > 524288)
+        return fail(IFR_ERR_ARG, "invalid sizes batch=%d gamma=%d vocab=%d (vocab must be in 1..524288)", batch,
+                    gamma, vocab);
+    if ((int64_t)batch * (2 * gamma + 1) > ifr::kAcceptMaxRows)
+        return fail(IFR_ERR_ARG, "batch=%d gamma=%d: batch * (2 gamma + 1) logits rows exceed %d", batch, gamma,
+                    ifr::kAcceptMaxRows);
+    if (!(temperature > 0.f) || !(temperature < 1e30f))
+        return fail(IFR_ERR_ARG, "temperature must be finite and > 0 (got %g)", (double)temperature);
+    // _validate_sampling_parameters (src/CommonOps.jl:126-139)
+    if (!std::isfinite(top_p) || top_p < 0.f || top_p > 1.f) return fail(IFR_ERR_ARG, "top_p must be in [0, 1]");
+    if (top_k < 0) return fail(IFR_ERR_ARG, "top_k must be non-negative");
+    if (!std::isfinite(min_p) || min_p < 0.f || min_p > 1.f) return fail(IFR_ERR_ARG, "min_p must be in [0, 1]");
+    DeviceGuard g(c->device);
+    int rc = ensure_scratch(c, (size_t)ifr::accept_filtered_scratch_bytes(batch, gamma, vocab));
+    if (rc) return rc;
+    IFR_CHECK_CUDA(ifr::accept_filtered(target, draft, uniforms, batch, gamma, vocab, temperature, top_k, top_p,
+                                        min_p, accept_count, out_tokens, draft_out, c->scratch, c->stream),
+                   "accept_filtered launch");
     return IFR_OK;
 }
 

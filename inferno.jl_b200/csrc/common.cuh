@@ -95,6 +95,12 @@ cudaError_t accept_sampled(const float *target, const float *draft, const int32_
                            int32_t *accept_count, int32_t *out_tokens, int32_t *draft_out,
                            void *scratch, cudaStream_t s);
 int64_t accept_scratch_bytes(int batch, int gamma, int vocab);
+// the sampled verification on top-k / top-p / min-p filtered distributions
+// (drafts drawn from the filtered draft rows); scratch >= accept_filtered_scratch_bytes
+cudaError_t accept_filtered(const float *target, const float *draft, const float *uniforms, int batch, int gamma,
+                            int vocab, float T, int top_k, float top_p, float min_p, int32_t *accept_count,
+                            int32_t *out_tokens, int32_t *draft_out, void *scratch, cudaStream_t s);
+int64_t accept_filtered_scratch_bytes(int batch, int gamma, int vocab);
 cudaError_t accept_greedy(const float *target, const int32_t *draft_tokens, int batch, int gamma,
                           int vocab, int32_t *accept_count, int32_t *out_tokens, void *scratch,
                           cudaStream_t s);

@@ -112,3 +112,83 @@ def test_accept_argument_errors(ctx, pkg):
         ctx.accept(t, d, u, 0.0)
     with pytest.raises(pkg.IfrError, match="temperature"):
         ctx.accept(t, d, u, float("nan"))
+
+
+# ---- filtered acceptance (ifr_accept_filtered) vs the oracle's restatement ----
+
+ACCEPT_FILTERS = [  # the sampler tests' filter settings with a positive temperature
+    dict(temperature=0.8),
+    dict(temperature=0.8, top_k=20),
+    dict(temperature=0.8, top_p=0.9),
+    dict(temperature=1.0, top_p=0.3),
+    dict(temperature=0.8, min_p=0.05),
+    dict(temperature=0.6, top_k=50, top_p=0.95, min_p=0.02),
+    dict(temperature=1.3, top_k=1),
+    dict(temperature=0.8, top_p=0.0),
+]
+
+
+def _run_filtered(ctx, tgt, dft, u, kw):
+    import torch
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    kw = dict(kw)
+    T = kw.pop("temperature")
+    acc, out, dout = ctx.accept_filtered(d(tgt), d(dft), d(u), T, **kw)
+    return acc.cpu().numpy(), out.cpu().numpy(), dout.cpu().numpy()
+
+
+def _oracle_filtered(O, tgt, dft, u, kw):
+    kw = dict(kw)
+    T = kw.pop("temperature")
+    return O.accept_filtered(tgt, dft, u, T, **kw)
+
+
+@pytest.mark.parametrize("kw", ACCEPT_FILTERS, ids=lambda d: ",".join(f"{k}={v}" for k, v in d.items()))
+@pytest.mark.parametrize("B,G,V", [(4, 5, 151936), (6, 3, 5000), (3, 2, 7)])
+def test_accept_filtered_bit_exact(O, ctx, kw, B, G, V):
+    rng = np.random.default_rng(V + 31 * G + len(kw))
+    for noise in (0.5, 2.0):
+        tgt, dft, u = _case(rng, B, G, V, noise)
+        got = _run_filtered(ctx, tgt, dft, u, kw)
+        ref = _oracle_filtered(O, tgt, dft, u, kw)
+        for g, r, name in zip(got, ref, ("accept_count", "out_tokens", "draft_tokens")):
+            assert np.array_equal(g, r), (name, noise, g, r)
+
+
+@pytest.mark.parametrize("kw", [ACCEPT_FILTERS[2], ACCEPT_FILTERS[5]],
+                         ids=lambda d: ",".join(f"{k}={v}" for k, v in d.items()))
+def test_accept_filtered_config3_full_batch(O, ctx, kw):
+    """BASELINE config 3's shape (64 x gamma 5 x vocab 151936) with filters"""
+    rng = np.random.default_rng(303)
+    tgt, dft, u = _case(rng, 64, 5, 151936)
+    got = _run_filtered(ctx, tgt, dft, u, kw)
+    ref = _oracle_filtered(O, tgt, dft, u, kw)
+    for g, r, name in zip(got, ref, ("accept_count", "out_tokens", "draft_tokens")):
+        assert np.array_equal(g, r), name
+
+
+def test_accept_filtered_no_filters_equals_accept(ctx):
+    """with every filter off, the filtered entry point gives ifr_accept's
+    results (drafts drawn in both)"""
+    rng = np.random.default_rng(41)
+    tgt, dft, u = _case(rng, 8, 4, 32000)
+    u = u * np.float32(0.999) + np.float32(0.0005)
+    a = _run(ctx, tgt, dft, u, 0.8)
+    b = _run_filtered(ctx, tgt, dft, u, dict(temperature=0.8))
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y)
+
+
+def test_accept_filtered_argument_errors(ctx, pkg):
+    import torch
+    t = torch.zeros(1, 2, 10, device="cuda")
+    d = torch.zeros(1, 1, 10, device="cuda")
+    u = torch.zeros(1, 3, device="cuda")
+    with pytest.raises(pkg.IfrError, match="temperature"):
+        ctx.accept_filtered(t, d, u, 0.0)
+    with pytest.raises(pkg.IfrError, match="top_p"):
+        ctx.accept_filtered(t, d, u, 0.8, top_p=1.5)
+    with pytest.raises(pkg.IfrError, match="top_k"):
+        ctx.accept_filtered(t, d, u, 0.8, top_k=-1)
+    with pytest.raises(pkg.IfrError, match="min_p"):
+        ctx.accept_filtered(t, d, u, 0.8, min_p=2.0)
