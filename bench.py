@@ -399,6 +399,9 @@ def run_reference_sweep(args):
 
 SPEC_PRESET, SPEC_SEED, SPEC_PROMPT = "tiny", 0, 128
 SPEC_GEN = 128  # config 1: 128 greedy tokens per request
+# DRAM bytes (read + write) of the verify's 97 GEMV launches, from one ncu
+# capture of `bench.py --profile spec` (profiles/spec_step_launches_config1.md)
+SPEC_VERIFY_TRAFFIC = 417682432
 
 
 def spec_bytes_per_step_gguf(gf, gamma):
@@ -567,7 +570,8 @@ def run_spec(args):
             "step_hbm_GBps": round(step_bytes / (ms_max / args.steps * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "kernel": "qgemv: the 97 dequant-GEMV launches of one verify (24 layers x 4 + Q6_K lm_head), N=5, back to back",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4), "traffic": SPEC_VERIFY_TRAFFIC,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the same 97 launches (profiles/spec_step_launches_config1.md)",
                          "algorithmic_bytes_per_launch": int(v_bytes), "launch_ms": round(v_ms, 4)},
             "e2e": {"value": round(e2e_tokens * ws / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(prompt.nbytes / max(1, e2e_steps)),
