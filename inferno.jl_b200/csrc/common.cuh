@@ -62,7 +62,7 @@ struct XForm {
                                // 1 = Q8_K (the reference's kernels, integer tensor cores)
     int ep = 0;                // 1: the rows are 16-row blocks of gate and up interleaved
                                // (gate 0-15, up 0-15, gate 16-31, ...); Y gets silu(gate) * up,
-                               // rows/2 rows (not with accumulate)
+                               // rows/2 rows (not with accumulate); 2: gelu_tanh(gate) * up
     const GemvArgmax *am = nullptr;  // greedy decision on Y (not with ep or accumulate)
 };
 // Y[ncols][rows] (+)= W * f(X), ncols <= 8 per call; X 16-byte aligned, ldx a multiple of 4
@@ -204,6 +204,22 @@ IFR_DEV void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
 }
 
 IFR_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// gelu_tanh (reference src/Gemma4.jl:253-257): 0.5 x (1 + tanh(c (x + 0.044715 x^3))),
+// c = sqrt(2 / pi) in f32, evaluated left to right without contraction
+IFR_DEV float gelu_tanh(float x) {
+    const float c = 0.797884523868560791f;  // sqrtf(2.0f / (float)pi), correctly rounded
+    const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+    const float t = tanhf(__fmul_rn(c, __fadd_rn(x, x3)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
+// the gated MLP's activation of an interleaved gate/up epilogue (XForm::ep):
+// 1 silu(gate) * up (Qwen3.5, ModelCPU.jl:482-508), 2 gelu_tanh(gate) * up
+// (Gemma4, Gemma4.jl:556-581)
+IFR_DEV float glu_act(int ep, float g, float u) {
+    if (ep == 2) return __fmul_rn(gelu_tanh(g), u);
+    return g / (1.0f + expf(-g)) * u;
+}
 
 IFR_DEV uint4 ldg_nc4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 IFR_DEV uint2 ldg_nc2(const void *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }

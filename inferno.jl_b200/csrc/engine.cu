@@ -203,6 +203,11 @@ struct DevLayer {
     Proj proj, out, gate_up, down;
     float *conv_w = nullptr, *ab_w = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
+    // Gemma4 blocks: post_norm follows the attention output, ffn_norm precedes
+    // the MLP and post_ffw_norm follows it; layer_scalar [1] scales the layer's
+    // output; sliding layers attend within the window
+    bool sliding = false;
+    float *ffn_norm = nullptr, *post_ffw_norm = nullptr, *layer_scalar = nullptr;
 };
 
 struct ifr_model {
@@ -221,6 +226,12 @@ struct ifr_model {
     ifr_comm *comm = nullptr;
     int tp_rank = 0, tp_world = 1;
     int nh = 0, nkv = 0, ffn = 0, ffn_off = 0, vocab = 0, vocab_off = 0;
+    // Gemma4 blocks (general.architecture "gemma4", src/Gemma4.jl): layer i is
+    // full attention iff (i + 1) % sliding_pattern == 0, else sliding-window
+    bool gemma = false;
+    int window = 0, sliding_pattern = 0;
+    float attn_softcap = 0.f, final_softcap = 0.f, embed_scale = 1.f;
+    float rope_theta_swa = 10000.f, partial_rotary = 0.25f;
     std::vector<void *> dev_allocs;
     ~ifr_model() {
         for (void *p : dev_allocs) cudaFree(p);
@@ -385,10 +396,45 @@ int upload_gate_up(ifr_model *m, const Gguf &g, const std::string &gate, const s
     return IFR_OK;
 }
 
-int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L) {
+int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L, int li = -1) {
     const ifr_model_info &c = m->info;
     int rc;
     L.ssm = g.has(pre + "ssm_a");
+    if (m->gemma) {
+        // attention-only Gemma4 layer (Gemma4Loader.jl:180-260): q rows nh x hd
+        // (no gate), four norms, the layer scalar
+        if (L.ssm) return ifr_fail(IFR_ERR_UNSUPPORTED, "%s: gemma4 layers are attention layers", pre.c_str());
+        L.sliding = m->sliding_pattern <= 0 || (li + 1) % m->sliding_pattern != 0;
+        const int64_t hd = c.head_dim, h0 = (int64_t)m->tp_rank * m->nh, kv0 = (int64_t)m->tp_rank * m->nkv;
+        Slice sq, sk, so;
+        sq.r0 = h0 * hd;
+        sq.r1 = (h0 + m->nh) * hd;
+        sk.r0 = kv0 * hd;
+        sk.r1 = (kv0 + m->nkv) * hd;
+        so.k0 = h0 * hd;
+        so.k1 = (h0 + m->nh) * hd;
+        if ((rc = upload_f32(m, g, pre + "attn_norm.weight", c.hidden, &L.attn_norm))) return rc;
+        if ((rc = upload_f32(m, g, pre + "post_attention_norm.weight", c.hidden, &L.post_norm))) return rc;
+        if ((rc = upload_f32(m, g, pre + "ffn_norm.weight", c.hidden, &L.ffn_norm))) return rc;
+        if ((rc = upload_f32(m, g, pre + "post_ffw_norm.weight", c.hidden, &L.post_ffw_norm))) return rc;
+        if (g.has(pre + "layer_scalar") && (rc = upload_f32(m, g, pre + "layer_scalar", 1, &L.layer_scalar)))
+            return rc;
+        if ((rc = upload_proj(m, g, {pre + "attn_q.weight", pre + "attn_k.weight", pre + "attn_v.weight"}, &L.proj,
+                              {sq, sk, sk})))
+            return rc;
+        if ((rc = upload_proj(m, g, {pre + "attn_output.weight"}, &L.out, {so}))) return rc;
+        if ((rc = upload_f32(m, g, pre + "attn_q_norm.weight", c.head_dim, &L.q_norm))) return rc;
+        if ((rc = upload_f32(m, g, pre + "attn_k_norm.weight", c.head_dim, &L.k_norm))) return rc;
+        if (L.proj.rows != (int64_t)(m->nh + 2 * m->nkv) * c.head_dim)
+            return ifr_fail(IFR_ERR_ARG, "%s: attention projection shapes do not match the config", pre.c_str());
+        Slice sf, sd;
+        sf.r0 = sd.k0 = m->ffn_off;
+        sf.r1 = sd.k1 = m->ffn_off + m->ffn;
+        if ((rc = upload_gate_up(m, g, pre + "ffn_gate.weight", pre + "ffn_up.weight", &L.gate_up, sf))) return rc;
+        if (!L.gate_up.glu)
+            return ifr_fail(IFR_ERR_UNSUPPORTED, "%s: gemma4 gate/up must share a type and 16-row blocks", pre.c_str());
+        return upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down, {sd});
+    }
     if ((rc = upload_f32(m, g, pre + "attn_norm.weight", c.hidden, &L.attn_norm))) return rc;
     if ((rc = upload_f32(m, g, pre + "post_attention_norm.weight", c.hidden, &L.post_norm))) return rc;
     if (L.ssm) {
@@ -460,6 +506,7 @@ struct ifr_state {
     unsigned long long *am_cand = nullptr;  // lm_head GEMV epilogue argmax: per-CTA candidates [8][1024]
     unsigned *am_count = nullptr;       // its completion counter (returns to 0)
     float *rope_cos, *rope_sin;
+    float *rope_cos_full = nullptr, *rope_sin_full = nullptr;  // Gemma4 full-attention layers
     std::vector<float *> S, hist, rq, rkv;      // per layer (SSM) else null
     std::vector<float *> kc, vc;                // per layer (attention) else null
     float *mtp_kc = nullptr, *mtp_vc = nullptr;
@@ -554,6 +601,12 @@ int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, 
     return IFR_OK;
 }
 
+// Gemma4 full-attention layers rotate Int(partial * hd / 2) pairs
+// (precompute_rope, Gemma4.jl:214-228); the remaining pairs have cos 1, sin 0
+int gemma_full_pairs(const ifr_model *m) {
+    return (int)(m->partial_rotary * (float)m->info.head_dim) / 2;
+}
+
 // one decoder layer (attention or SSM) on n columns of s->x
 // n tokens per request, s->B requests (columns b * n + t); pos of request b at
 // pos + b * pos_ld; kc / vc of request b at + b * kv_ld
@@ -574,6 +627,56 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     in_norm.eps = c.rms_eps;
     s->launches += (L.ssm || !s->attn_part) ? 1 : 2;  // the SSM / attention step (split-KV: two kernels)
     if ((rc = gemv(s, gcat, L.proj, s->x, nc, s->proj, false, st, in_norm))) return rc;
+    if (m->gemma) {
+        // Gemma4 layer (Gemma4.jl:622-650): x = x + RMSNorm(wo attn(norm_in(x)));
+        // x = (x + RMSNorm(down(gelu_tanh(gate) up)(norm_ff(x)))) * layer_scalar
+        ProfScope ps(s, CAT_ATTN, 0, st);
+        ifr::AttnArgs a{};
+        a.qkv = s->proj;
+        a.ldq = L.proj.rows;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.kc = kc;
+        a.vc = vc;
+        a.pos = pos;
+        a.out = s->y;
+        a.ldo = (int64_t)m->nh * c.head_dim;
+        a.N = n;
+        a.nh = m->nh;
+        a.nkv = m->nkv;
+        a.hd = c.head_dim;
+        a.rotary_dim = c.rotary_dim;
+        a.eps = c.rms_eps;
+        a.b_kv = kv_ld;
+        a.b_pos = pos_ld;
+        a.gated = 0;
+        a.vnorm = 1;
+        a.scale = 1.0f;
+        a.softcap = m->attn_softcap;
+        a.window = L.sliding ? m->window : 0;
+        a.rope_off = a.rope_ld = c.head_dim / 2;
+        a.rope_cos = L.sliding ? s->rope_cos : s->rope_cos_full;
+        a.rope_sin = L.sliding ? s->rope_sin : s->rope_sin_full;
+        a.rope_pairs = L.sliding ? c.head_dim / 2 : gemma_full_pairs(m);
+        if (s->attn_part) {
+            a.part = s->attn_part;
+            a.splits = ifr::attn_splits(m->nh, m->nkv, n, B, s->max_ctx);
+        }
+        ECHECK(ifr::attn_step(a, B, st), "attn_step");
+        // row-parallel projections: every rank's partial, summed over the ranks
+        if ((rc = gemv(s, gcat, L.out, s->y, nc, s->xn, false, st))) return rc;
+        if ((rc = comm_allreduce_sum(m->comm, s->xn, (size_t)nc * d, st))) return rc;
+        ifr::norm_add(s->xn, L.post_norm, s->x, nc, d, c.rms_eps, nullptr, st);
+        ifr::XForm glu = in_norm;
+        glu.w = L.ffn_norm;
+        glu.ep = 2;  // gelu_tanh(gate) * up
+        if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->hmid, false, st, glu))) return rc;
+        if ((rc = gemv(s, gcat, L.down, s->hmid, nc, s->xn, false, st))) return rc;
+        if ((rc = comm_allreduce_sum(m->comm, s->xn, (size_t)nc * d, st))) return rc;
+        ifr::norm_add(s->xn, L.post_ffw_norm, s->x, nc, d, c.rms_eps, L.layer_scalar, st);
+        s->launches += 2;
+        return IFR_OK;
+    }
     if (L.ssm) {
         ProfScope ps(s, CAT_SSM, 0, st);
         ifr::SsmArgs a{};
@@ -664,7 +767,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
 template <int T>
 __global__ void embed_kernel(const uint8_t *__restrict__ w, int64_t nu, int64_t nb_raw, int64_t rows, int64_t cols,
                              int32_t *vtok, const int32_t *first, int first_ld, int n, int B,
-                             float *__restrict__ out) {
+                             float *__restrict__ out, float scale) {
     ifr::pdl_trigger();
     ifr::pdl_wait();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -676,7 +779,10 @@ __global__ void embed_kernel(const uint8_t *__restrict__ w, int64_t nu, int64_t 
     int64_t tok = (t == 0 && first) ? first[(int64_t)b * first_ld] : vt[t];
     if (t == 0 && u == 0 && sub == 0 && first) vt[0] = (int32_t)tok;
     tok = tok < 0 ? 0 : (tok >= rows ? rows - 1 : tok);
-    ifr::dequant_group<T>(w, nu, nb_raw, tok, u, sub, out + (int64_t)tg * cols + u * 256 + 32 * sub);
+    float *o = out + (int64_t)tg * cols + u * 256 + 32 * sub;
+    ifr::dequant_group<T>(w, nu, nb_raw, tok, u, sub, o);
+    if (scale != 1.0f)  // Gemma4: the embedding row times embed_scale (Gemma4.jl:612-615)
+        for (int i = 0; i < 32; i++) o[i] = __fmul_rn(o[i], scale);
 }
 
 __device__ float block_sum_256(float v, float *red) {
@@ -730,19 +836,19 @@ __global__ void __launch_bounds__(256) mtp_prep_kernel(const uint8_t *__restrict
 
 template <int T>
 cudaError_t launch_embed_t(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int first_ld, int n, int B,
-                           float *out, cudaStream_t st) {
+                           float *out, float scale, cudaStream_t st) {
     const int64_t tot = (int64_t)B * n * e.nu * 8;
     return ifr::launch_k(embed_kernel<T>, dim3((unsigned)((tot + 127) / 128)), dim3(128), 0, st, (const uint8_t *)e.data,
                          (int64_t)e.nu, (int64_t)e.nb, (int64_t)e.rows, (int64_t)e.cols, vtok, first, first_ld, n, B,
-                         out);
+                         out, scale);
 }
 cudaError_t launch_embed(const ifr::QTensor &e, int32_t *vtok, const int32_t *first, int first_ld, int n, int B,
-                         float *out, cudaStream_t st) {
+                         float *out, float scale, cudaStream_t st) {
     switch (e.type) {
-    case 12: return launch_embed_t<12>(e, vtok, first, first_ld, n, B, out, st);
-    case 13: return launch_embed_t<13>(e, vtok, first, first_ld, n, B, out, st);
-    case 14: return launch_embed_t<14>(e, vtok, first, first_ld, n, B, out, st);
-    case 8: return launch_embed_t<8>(e, vtok, first, first_ld, n, B, out, st);
+    case 12: return launch_embed_t<12>(e, vtok, first, first_ld, n, B, out, scale, st);
+    case 13: return launch_embed_t<13>(e, vtok, first, first_ld, n, B, out, scale, st);
+    case 14: return launch_embed_t<14>(e, vtok, first, first_ld, n, B, out, scale, st);
+    case 8: return launch_embed_t<8>(e, vtok, first, first_ld, n, B, out, scale, st);
     }
     return cudaErrorInvalidValue;
 }
@@ -798,7 +904,7 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
     const int B = s->B, nc = B * n;
     const int sc_ld = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
     ECHECK(launch_embed(m->embed.parts[0], s->vtok, first_from_state ? &s->sc->last_token : nullptr, sc_ld, n, B,
-                        s->x, st),
+                        s->x, m->embed_scale, st),
            "embedding");
     s->launches += 2;  // embedding, final norm
     const int64_t kv_ld = (int64_t)s->max_ctx * m->nkv * c.head_dim;
@@ -812,6 +918,10 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
         f.am = am;
         int rc = gemv(s, CAT_LM_HEAD, m->lm_head, s->hid, nc, s->logits, false, st, f);
         if (rc) return rc;
+        if (m->final_softcap > 0.f) {  // get_logits (Gemma4.jl:678-693): logit_softcap!
+            ifr::softcap(s->logits, (int64_t)nc * m->vocab, m->final_softcap, st);
+            s->launches++;
+        }
     }
     s->last_n = n;
     return IFR_OK;
@@ -845,7 +955,7 @@ __global__ void prefill_finish_kernel(ifr::EngineScalars *sc, const int32_t *tok
 // one small-N launch over an unsharded, single-part lm_head
 bool lm_head_decides(const ifr_state *s, int nc) {
     const ifr_model *m = s->m;
-    return !m->comm && m->lm_head.parts.size() == 1 && nc <= kNMax &&
+    return !m->comm && !(m->final_softcap > 0.f) && m->lm_head.parts.size() == 1 && nc <= kNMax &&
            !(nc >= ifr_ctx_dense_min(m->ctx) && s->dense) && m->lm_head.parts[0].rows <= 0x7FFFFFFF;
 }
 
@@ -939,6 +1049,20 @@ int ifr_model_load_gguf_tp(ifr_ctx *ctx, const char *path, ifr_comm *comm, ifr_m
     c.conv_kernel = (int)md("ssm.conv_kernel", 4);
     c.rotary_dim = (int)std::lround(c.head_dim * (float)md("rope.partial_rotary_factor", 0.25));  // LoaderCPU.jl:421
     int rc = IFR_OK;
+    if (arch == "gemma4") {
+        // Gemma4Loader.jl:60-123 (our GGUF keys): sliding window and its layer
+        // pattern, softcaps, the two RoPE bases, embed_scale = Float32(sqrt(hidden))
+        m->gemma = true;
+        m->window = (int)md("attention.sliding_window", 512);
+        m->sliding_pattern = (int)md("attention.sliding_window_pattern", 6);
+        m->attn_softcap = (float)md("attn_logit_softcapping", 0.0);
+        m->final_softcap = (float)md("final_logit_softcapping", 0.0);
+        m->rope_theta_swa = (float)md("rope.freq_base_swa", 10000.0);
+        c.rope_theta = (float)md("rope.freq_base", 1000000.0);
+        m->partial_rotary = (float)md("rope.partial_rotary_factor", 0.25);
+        m->embed_scale = (float)std::sqrt((double)c.hidden);
+        if (g.has("mtp.fc.weight")) rc = ifr_fail(IFR_ERR_UNSUPPORTED, "gemma4 models have no MTP head here");
+    }
     auto te = g.t.find("token_embd.weight");
     if (te == g.t.end() || te->second.dims.size() != 2) rc = ifr_fail(IFR_ERR_ARG, "token_embd.weight missing");
     if (!rc) {
@@ -1007,7 +1131,7 @@ int ifr_model_load_gguf_tp(ifr_ctx *ctx, const char *path, ifr_comm *comm, ifr_m
     if (!rc) rc = upload_f32(m, g, "output_norm.weight", c.hidden, &m->final_norm);
     m->layers.resize(c.n_layers);
     for (int i = 0; !rc && i < c.n_layers; i++) {
-        rc = load_layer(m, g, "blk." + std::to_string(i) + ".", m->layers[i]);
+        rc = load_layer(m, g, "blk." + std::to_string(i) + ".", m->layers[i], i);
         if (!rc && !m->layers[i].ssm) c.n_attention_layers++;
     }
     if (!rc && g.has("mtp.fc.weight")) {
@@ -1110,9 +1234,13 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     chk(dalloc(s, &s->gcount, B + 4));
     chk(dalloc(s, &s->am_cand, (size_t)8 * 1024));
     chk(dalloc(s, &s->am_count, 4));
-    const int half = c.rotary_dim / 2;
+    const int half = m->gemma ? c.head_dim / 2 : c.rotary_dim / 2;
     chk(dalloc(s, &s->rope_cos, (size_t)max_ctx * half));
     chk(dalloc(s, &s->rope_sin, (size_t)max_ctx * half));
+    if (m->gemma) {
+        chk(dalloc(s, &s->rope_cos_full, (size_t)max_ctx * half));
+        chk(dalloc(s, &s->rope_sin_full, (size_t)max_ctx * half));
+    }
     s->S.assign(c.n_layers, nullptr);
     s->hist.assign(c.n_layers, nullptr);
     s->rq.assign(c.n_layers, nullptr);
@@ -1175,7 +1303,28 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     }
     if (!rc && cudaMallocHost((void **)&s->h_tok, sizeof(int32_t) * (N + 64)) != cudaSuccess)
         rc = ifr_fail(IFR_ERR_NOMEM, "cudaMallocHost failed");
-    if (!rc) {
+    if (!rc && m->gemma) {
+        // precompute_rope (Gemma4.jl:205-249): frequencies and angles in
+        // Float64, cos / sin as Float32; sliding layers: every pair, theta_swa;
+        // full layers: the first gemma_full_pairs pairs, frequencies over head_dim
+        const int hd = c.head_dim, np = gemma_full_pairs(m);
+        std::vector<float> cs((size_t)max_ctx * half), sn(cs.size()), cf(cs.size()), sf(cs.size());
+        for (int k = 0; k < half; k++) {
+            const double fs = 1.0 / std::pow((double)m->rope_theta_swa, 2.0 * k / (double)hd);
+            const double ff = k < np ? 1.0 / std::pow((double)c.rope_theta, 2.0 * k / (double)hd) : 0.0;
+            for (int p = 0; p < max_ctx; p++) {
+                cs[(size_t)p * half + k] = (float)std::cos(p * fs);
+                sn[(size_t)p * half + k] = (float)std::sin(p * fs);
+                cf[(size_t)p * half + k] = (float)std::cos(p * ff);
+                sf[(size_t)p * half + k] = (float)std::sin(p * ff);
+            }
+        }
+        if (cudaMemcpy(s->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(s->rope_cos_full, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(s->rope_sin_full, sf.data(), sf.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = ifr_fail(IFR_ERR_CUDA, "H2D rope tables");
+    } else if (!rc) {
         // RoPE tables as the reference builds them (ModelCPU.jl:136-154):
         // inv_freq = Float32(1/theta^(2(i-1)/rd)) in f64; angle = inv_freq * pos in f32
         std::vector<float> cs((size_t)max_ctx * half), sn((size_t)max_ctx * half);

@@ -55,6 +55,46 @@ void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float 
     launch_k(rmsnorm_kernel, dim3(rows), dim3(256), 0, s, x, w, out, n, eps, ldx, ldo);
 }
 
+// ------------------------------------------------- Gemma4 block tails -------
+// forward! (Gemma4.jl:622-650) after a sub-block: x = (x + RMSNorm(y) w) * s -
+// the post-attention (s = 1) and post-feed-forward (s = layer scalar) norms
+// added to the residual; one CTA per column
+__global__ void __launch_bounds__(256) norm_add_kernel(const float *__restrict__ y, const float *__restrict__ w,
+                                                       float *x, int n, float eps, const float *scalar) {
+    __shared__ float red[8];
+    pdl_trigger();
+    pdl_wait();
+    const float *yr = y + (int64_t)blockIdx.x * n;
+    float *xr = x + (int64_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += 256) ss += yr[i] * yr[i];
+    ss = block_sum256(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+    const float sc = scalar ? *scalar : 1.0f;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        const float v = __fadd_rn(xr[i], yr[i] * inv * w[i]);
+        xr[i] = scalar ? __fmul_rn(v, sc) : v;
+    }
+}
+
+void norm_add(const float *y, const float *w, float *x, int cols, int n, float eps, const float *scalar,
+              cudaStream_t s) {
+    launch_k(norm_add_kernel, dim3(cols), dim3(256), 0, s, y, w, x, n, eps, scalar);
+}
+
+// logit_softcap! (CommonOps.jl:326-333) in place: l = tanh(l / cap) cap
+__global__ void softcap_kernel(float *l, int64_t n, float cap) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        l[i] = tanhf(l[i] / cap) * cap;
+}
+
+void softcap(float *l, int64_t n, float cap, cudaStream_t s) {
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
+    launch_k(softcap_kernel, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256), 0, s, l, n, cap);
+}
+
 // ------------------------------------------------------------- SwiGLU -------
 // mlp_forward (ModelCPU.jl:482-508): h = silu(g) * u with g, u from one GEMV
 // whose output rows are [gate (ffn) | up (ffn)]
@@ -581,6 +621,22 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// the RoPE pairs of an attention call: pair i < pairs rotates dims
+// (i, i + off) with table entries [pos * ld + i]
+struct RopeSpec { int pairs, off, ld; };
+__host__ __device__ inline RopeSpec rope_spec(const AttnArgs &a) {
+    const int h = a.rotary_dim / 2;
+    return {a.rope_pairs > 0 ? a.rope_pairs : h, a.rope_off > 0 ? a.rope_off : h, a.rope_ld > 0 ? a.rope_ld : h};
+}
+// causal, and within the sliding window when there is one
+__device__ __forceinline__ bool key_visible(const AttnArgs &a, int j, int qpos) {
+    return j <= qpos && (a.window <= 0 || j > qpos - a.window);
+}
+// attention logit softcap (Gemma4.jl:420-423): tanh(s / cap) cap
+__device__ __forceinline__ float score_cap(const AttnArgs &a, float s) {
+    return a.softcap > 0.f ? tanhf(s / a.softcap) * a.softcap : s;
+}
+
 template <int HD>
 __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_step_kernel(AttnArgs a) {
     namespace cg = cooperative_groups;
@@ -611,15 +667,16 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     __shared__ __align__(16) float po[kMaxN][HD];  // this slice's P.V (unnormalised)
     __shared__ float sc[kMaxN][64];
     __shared__ float ms[kMaxN], ls[kMaxN], fs[kMaxN];
-    const int half = a.rotary_dim / 2;
+    const RopeSpec rs = rope_spec(a);
+    const int qs = a.gated ? 2 : 1;  // q rows per head: [q; gate] or q
 
     // 1. q of this head, new k and v of its KV head; RMSNorm + RoPE (warp t = token t)
     for (int i = tid; i < N * HD; i += 256) {
         const int t = i / HD, d = i % HD;
         const float *row = a.qkv + (int64_t)t * a.ldq;
-        q[t][d] = row[(int64_t)h * 2 * HD + d];
-        kn[t][d] = row[(int64_t)a.nh * 2 * HD + kvh * HD + d];
-        vn[t][d] = row[(int64_t)a.nh * 2 * HD + a.nkv * HD + kvh * HD + d];
+        q[t][d] = row[(int64_t)h * qs * HD + d];
+        kn[t][d] = row[(int64_t)a.nh * qs * HD + kvh * HD + d];
+        vn[t][d] = row[(int64_t)a.nh * qs * HD + a.nkv * HD + kvh * HD + d];
     }
     if (tid < kMaxN) {
         ms[tid] = -CUDART_INF_F;
@@ -640,17 +697,24 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
             q[t][d] = q[t][d] * iq * a.q_norm[d];
             kn[t][d] = kn[t][d] * ik * a.k_norm[d];
         }
+        if (a.vnorm) {  // rmsnorm_no_scale! (CommonOps.jl:43-53)
+            float sv = 0.f;
+            for (int d = lane; d < HD; d += 32) sv += vn[t][d] * vn[t][d];
+            sv = warp_sum(sv);
+            const float iv = 1.0f / sqrtf(sv / (float)HD + a.eps);
+            for (int d = lane; d < HD; d += 32) vn[t][d] = vn[t][d] * iv;
+        }
         __syncwarp();
-        const float *cs = a.rope_cos + (int64_t)(p0 + t) * half, *sn = a.rope_sin + (int64_t)(p0 + t) * half;
-        for (int i = lane; i < half; i += 32) {
+        const float *cs = a.rope_cos + (int64_t)(p0 + t) * rs.ld, *sn = a.rope_sin + (int64_t)(p0 + t) * rs.ld;
+        for (int i = lane; i < rs.pairs; i += 32) {
             const float c = cs[i], s_ = sn[i];
-            float x1 = q[t][i], x2 = q[t][i + half];
+            float x1 = q[t][i], x2 = q[t][i + rs.off];
             q[t][i] = x1 * c - x2 * s_;
-            q[t][i + half] = x1 * s_ + x2 * c;
+            q[t][i + rs.off] = x1 * s_ + x2 * c;
             x1 = kn[t][i];
-            x2 = kn[t][i + half];
+            x2 = kn[t][i + rs.off];
             kn[t][i] = x1 * c - x2 * s_;
-            kn[t][i + half] = x1 * s_ + x2 * c;
+            kn[t][i + rs.off] = x1 * s_ + x2 * c;
         }
     }
     __syncthreads();
@@ -664,7 +728,7 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     }
 
     // 2. keys lo..hi: scores, online softmax, P.V, in chunks of 64
-    const float scale = 1.0f / sqrtf((float)HD);
+    const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf((float)HD);
     const int d = tid % HD, g = tid / HD;
     float o[kMaxN];
 #pragma unroll
@@ -684,7 +748,7 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
 #pragma unroll
                     for (int e = 0; e < DL; e++) part += q[t][lane + 32 * e] * kd[e];
                     part = warp_sum(part);
-                    if (lane == 0) sc[t][jj] = (j <= p0 + t) ? part * scale : -CUDART_INF_F;
+                    if (lane == 0) sc[t][jj] = key_visible(a, j, p0 + t) ? score_cap(a, part * scale) : -CUDART_INF_F;
                 }
             }
         }
@@ -747,8 +811,12 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
             L += cluster.map_shared_rank(&ls[0], r)[t] * w;
             O += cluster.map_shared_rank(&po[0][0], r)[t * HD + dd] * w;
         }
-        const float gv = a.qkv[(int64_t)t * a.ldq + (int64_t)h * 2 * HD + HD + dd];
-        a.out[(int64_t)t * a.ldo + (int64_t)h * HD + dd] = O / L * (1.0f / (1.0f + expf(-gv)));
+        float y = O / L;
+        if (a.gated) {
+            const float gv = a.qkv[(int64_t)t * a.ldq + (int64_t)h * 2 * HD + HD + dd];
+            y *= 1.0f / (1.0f + expf(-gv));
+        }
+        a.out[(int64_t)t * a.ldo + (int64_t)h * HD + dd] = y;
     }
     cluster.sync();  // peers may still read this CTA's shared memory
 }
@@ -810,16 +878,29 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
     const int nkeys = p0 + N, kps = attn_kps(nkeys, S);
     const int lo = sl * kps, hi = min(nkeys, lo + kps);
     if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
-    const int half = a.rotary_dim / 2;
+    const RopeSpec rs = rope_spec(a);
+    const int qs = a.gated ? 2 : 1;
+    const int64_t rows_all = (int64_t)gridDim.z * a.nh * N, rid_base = ((int64_t)b * a.nh + h0) * N;
+    if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
+        // every key of this slice is outside every query's window (this
+        // request's new keys are written by slice 0): an empty partial state
+        float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
+        for (int i = tid; i < R * HD; i += 256) po[(rid_base + i / HD) * HD + i % HD] = 0.f;
+        if (tid < R) {
+            pm[rid_base + tid] = -CUDART_INF_F;
+            pl[rid_base + tid] = 0.f;
+        }
+        return;
+    }
 
     // 1. the row group's q rows, the new k and v; RMSNorm + RoPE (warp per row)
     for (int i = tid; i < R * HD; i += 256) {
         const int r = i / HD, d = i % HD, hh = r / N, t = r % N;
-        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * 2 * HD + d];
+        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * qs * HD + d];
     }
     for (int i = tid; i < N * HD; i += 256) {
         const int t = i / HD, d = i % HD;
-        const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * 2 * HD;
+        const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * qs * HD;
         kn[i] = row[g * HD + d];
         vn[i] = row[a.nkv * HD + g * HD + d];
     }
@@ -828,7 +909,16 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
         ls[tid] = 0.f;
     }
     __syncthreads();
-    for (int rr = warp; rr < R + N; rr += 8) {
+    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
+        if (rr >= R + N) {  // v rows: RMSNorm without weights (CommonOps.jl:43-53)
+            float *x = vn + (rr - R - N) * HD;
+            float ss = 0.f;
+            for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
+            ss = warp_sum(ss);
+            const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+            for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv;
+            continue;
+        }
         const bool isq = rr < R;
         float *x = isq ? q + rr * HD : kn + (rr - R) * HD;
         const float *w = isq ? a.q_norm : a.k_norm;
@@ -839,12 +929,12 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
         const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
         for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv * w[d];
         __syncwarp();
-        const float *cs = a.rope_cos + (int64_t)(p0 + t) * half, *sn = a.rope_sin + (int64_t)(p0 + t) * half;
-        for (int i = lane; i < half; i += 32) {
+        const float *cs = a.rope_cos + (int64_t)(p0 + t) * rs.ld, *sn = a.rope_sin + (int64_t)(p0 + t) * rs.ld;
+        for (int i = lane; i < rs.pairs; i += 32) {
             const float c = cs[i], s_ = sn[i];
-            const float x1 = x[i], x2 = x[i + half];
+            const float x1 = x[i], x2 = x[i + rs.off];
             x[i] = x1 * c - x2 * s_;
-            x[i + half] = x1 * s_ + x2 * c;
+            x[i + rs.off] = x1 * s_ + x2 * c;
         }
     }
     __syncthreads();
@@ -859,7 +949,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
     }
 
     // 2. keys lo..hi in chunks: scores, online softmax, P.V
-    const float scale = 1.0f / sqrtf((float)HD);
+    const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf((float)HD);
     float o[RPT];
 #pragma unroll
     for (int k = 0; k < RPT; k++) o[k] = 0.f;
@@ -913,7 +1003,9 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
 #pragma unroll
             for (int k = 0; k < RG; k++) {
                 const int r = warp + 8 * k;
-                if (r < R) sc[r * kGrpKeys + jj] = (jj < nj && j <= p0 + r % N) ? acc[k] * scale : -CUDART_INF_F;
+                if (r < R)
+                    sc[r * kGrpKeys + jj] = (jj < nj && key_visible(a, j, p0 + r % N)) ? score_cap(a, acc[k] * scale)
+                                                                                      : -CUDART_INF_F;
             }
         }
         __syncthreads();
@@ -1027,8 +1119,12 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch
         for (int g2 = 1; g2 < NG; g2++) O += og[g2][d];
     }
     const int64_t tok = (int64_t)b * N + t;
-    const float gv = a.qkv[tok * a.ldq + (int64_t)h * 2 * HD + HD + d];
-    a.out[tok * a.ldo + (int64_t)h * HD + d] = O / L * (1.0f / (1.0f + expf(-gv)));
+    float y = O / L;
+    if (a.gated) {
+        const float gv = a.qkv[tok * a.ldq + (int64_t)h * 2 * HD + HD + d];
+        y *= 1.0f / (1.0f + expf(-gv));
+    }
+    a.out[tok * a.ldo + (int64_t)h * HD + d] = y;
 }
 
 static int split_heads(int ratio, int N) { return std::max(1, std::min(ratio, kGrpRows / N)); }

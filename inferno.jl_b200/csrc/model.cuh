@@ -44,7 +44,7 @@ struct SsmArgs {
 };
 
 struct AttnArgs {
-    const float *qkv;    // [N][ldq]: per head [q; gate] (2 nh hd), then k (nkv hd), then v
+    const float *qkv;    // [N][ldq]: per head [q; gate] (2 nh hd; gated 0: q only, nh hd), then k (nkv hd), then v
     int64_t ldq;
     const float *q_norm, *k_norm;
     float *kc, *vc;      // [max_ctx][nkv][hd]
@@ -60,11 +60,26 @@ struct AttnArgs {
     // scratch of their partial softmax states (attn_part_floats floats)
     int splits = 0;
     float *part = nullptr;
+    // Gemma4 attention (src/Gemma4.jl:296-456); the defaults are the Qwen3.5
+    // attention.  gated 0: q rows nh x hd (no per-head gate, no output gate);
+    // vnorm 1: RMSNorm of v without weights; scale: score scale (0: 1/sqrt(hd));
+    // softcap: scores become tanh(s / cap) cap (0: off); window: a query at
+    // position p sees keys p - window + 1 .. p (0: all); RoPE pair i < rope_pairs
+    // rotates dims (i, i + rope_off) with table entries [pos * rope_ld + i]
+    // (0: rotary_dim / 2 for each)
+    int gated = 1, vnorm = 0;
+    float scale = 0.f, softcap = 0.f;
+    int window = 0, rope_pairs = 0, rope_off = 0, rope_ld = 0;
 };
 
 void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float eps, int64_t ldx, int64_t ldo,
              cudaStream_t s);
 void swiglu(const float *gu, float *h, int n, int ffn, cudaStream_t s);
+// Gemma4 sub-block tail on `cols` columns of width n: x = (x + RMSNorm(y) w) * (*scalar or 1)
+void norm_add(const float *y, const float *w, float *x, int cols, int n, float eps, const float *scalar,
+              cudaStream_t s);
+// l = tanh(l / cap) cap in place (final logit softcap)
+void softcap(float *l, int64_t n, float cap, cudaStream_t s);
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s);
 cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s);
 // key slices of a split-KV call of N tokens per request, and the scratch

@@ -973,7 +973,7 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
                 const int gr = (rr >> 4) * 32 + (rr & 15);
                 if (j0 + rr < a.M / 2 && !dead) {
                     const float gv = accv(gr, col), uv = accv(gr + 16, col);
-                    a.Y[(int64_t)col * a.ldy + j0 + rr] = gv / (1.0f + expf(-gv)) * uv;
+                    a.Y[(int64_t)col * a.ldy + j0 + rr] = glu_act(a.ep, gv, uv);
                 }
             }
         } else {

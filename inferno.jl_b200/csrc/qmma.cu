@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
                     const float up = __shfl_down_sync(0xffffffffu, val, 16);
                     const int64_t j = (row >> 5) * 16 + lane;
                     if (lane < 16 && col < a.ncols && j < a.M / 2)
-                        a.Y[(int64_t)col * a.ldy + j] = val / (1.0f + expf(-val)) * up;
+                        a.Y[(int64_t)col * a.ldy + j] = glu_act(a.ep, val, up);
                 } else if (col < a.ncols && row < a.M) {
                     float *y = a.Y + (int64_t)col * a.ldy + row;
                     *y = a.accumulate ? *y + val : val;
@@ -633,7 +633,7 @@ __global__ void qmma_reduce_kernel(const float *__restrict__ ws, int splits, int
     if (ep) {
         const int64_t g = (r >> 4) * 32 + (r & 15);
         const float gv = sum(g), uv = sum(g + 16);
-        Y[(int64_t)col * ldy + r] = gv / (1.0f + expf(-gv)) * uv;
+        Y[(int64_t)col * ldy + r] = glu_act(ep, gv, uv);
     } else {
         const float v = sum(r);
         float *y = Y + (int64_t)col * ldy + r;

@@ -36,17 +36,20 @@ PRESETS = {
                  ffn=512, vocab=4096, ssm_heads=4, ssm_head_dim=64, conv_kernel=4,
                  attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=True,
                  context=1024),
-    # config 5: Gemma4 shapes (hidden 5376, 62 layers, 32 q / 16 kv x 128, FFN
-    # 21504, vocab 262144, Q4_K) built from the same Qwen-style attention blocks,
-    # and its Q8_0 draft model (hidden 1152, 26 layers); attention-only
-    "gemma": dict(hidden=5376, n_layers=62, n_head=32, n_kv_head=16, head_dim=128, rope_frac=0.25,
+    # config 5: the Gemma4-shape target (hidden 5376, 62 layers, 32 q / 16 kv x
+    # 128, FFN 21504, vocab 262144, Q4_K) and its Q8_0 draft model (hidden
+    # 1152, 26 layers), both with Gemma4 blocks (architecture "gemma4"): five
+    # sliding-window layers to one full layer, GELU-tanh MLP, Q/K/V norms,
+    # norms around both blocks, a layer scalar, attention and final logit
+    # softcaps, the embedding scaled by sqrt(hidden)
+    "gemma": dict(arch="gemma4", hidden=5376, n_layers=62, n_head=32, n_kv_head=16, head_dim=128, rope_frac=0.25,
                   ffn=21504, vocab=262144, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
                   attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q4_K, mtp=False,
-                  context=8192, row_pool=1024),
-    "gemma_draft": dict(hidden=1152, n_layers=26, n_head=4, n_kv_head=1, head_dim=256, rope_frac=0.25,
-                        ffn=6912, vocab=262144, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                  context=8192, row_pool=1024, window=1024, pattern=6),
+    "gemma_draft": dict(arch="gemma4", hidden=1152, n_layers=26, n_head=4, n_kv_head=1, head_dim=256,
+                        rope_frac=0.25, ffn=6912, vocab=262144, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
                         attn_every=1, mat=G.GGML_Q8_0, down=G.GGML_Q8_0, emb=G.GGML_Q8_0, mtp=False,
-                        context=8192, row_pool=1024),
+                        context=8192, row_pool=1024, window=1024, pattern=6),
     # parity models at the large configs' widths with few layers, so the CPU
     # oracle can follow them: 9b_narrow keeps every width of "9b" (the batched
     # SSM kernel at head dim 128, attention at head dim 256, FFN 12288, Q6_K
@@ -56,10 +59,16 @@ PRESETS = {
                       ffn=12288, vocab=151936, ssm_heads=32, ssm_head_dim=128, conv_kernel=4,
                       attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q6_K, emb=G.GGML_Q6_K, mtp=True,
                       context=8192, row_pool=1024),
-    "gemma_narrow": dict(hidden=5376, n_layers=2, n_head=32, n_kv_head=16, head_dim=128, rope_frac=0.25,
-                         ffn=21504, vocab=32768, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+    "gemma_narrow": dict(arch="gemma4", hidden=5376, n_layers=2, n_head=32, n_kv_head=16, head_dim=128,
+                         rope_frac=0.25, ffn=21504, vocab=32768, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
                          attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q4_K, mtp=False,
-                         context=8192, row_pool=1024),
+                         context=8192, row_pool=1024, window=8, pattern=2, attn_cap=20.0, final_cap=2.0),
+    # a small Gemma4-block model: the sliding window (6 keys) and both layer
+    # kinds within a short prompt, split-KV attention reachable at 1024 tokens
+    "gemma_mini": dict(arch="gemma4", hidden=256, n_layers=4, n_head=4, n_kv_head=2, head_dim=128,
+                       rope_frac=0.25, ffn=512, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                       attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=False,
+                       context=2048, window=6, pattern=2, attn_cap=10.0, final_cap=1.0),
     # attention-only test model whose heads and FFN units split over 2 ranks
     "tp_mini": dict(hidden=256, n_layers=4, n_head=8, n_kv_head=4, head_dim=64, rope_frac=0.25,
                     ffn=1024, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
@@ -90,6 +99,8 @@ def build(path, preset="tiny", seed=0, quantize=None, **overrides):
     ffn, V = cfg["ffn"], cfg["vocab"]
     root = np.random.default_rng(seed)
     w = G.GGUFWriter(path)
+    if cfg.get("arch") == "gemma4":
+        return _build_gemma(w, cfg, preset, seed, root, quant)
     arch = "qwen35"
     w.add("general.architecture", arch)
     w.add("general.name", f"inferno-b200 synthetic {preset} seed {seed}")
@@ -167,6 +178,69 @@ def build(path, preset="tiny", seed=0, quantize=None, **overrides):
         mlp(pre)
     w.write()
     return path
+
+
+def _build_gemma(w, cfg, preset, seed, root, quant):
+    """a Gemma4-block model (src/Gemma4.jl): attention-only layers, every
+    `pattern`-th a full-attention layer and the others sliding-window ones;
+    q rows n_head x head_dim (no output gate); norms stored as their weights
+    (no 1 + w offset, CommonOps.rmsnorm! multiplies by w)"""
+    d, L = cfg["hidden"], cfg["n_layers"]
+    nh, nkv, hd = cfg["n_head"], cfg["n_kv_head"], cfg["head_dim"]
+    ffn, V = cfg["ffn"], cfg["vocab"]
+    arch = "gemma4"
+    w.add("general.architecture", arch)
+    w.add("general.name", f"inferno-b200 synthetic {preset} seed {seed}")
+    for k, v in [("embedding_length", d), ("feed_forward_length", ffn), ("block_count", L),
+                 ("attention.head_count", nh), ("attention.head_count_kv", nkv),
+                 ("attention.key_length", hd), ("attention.value_length", hd),
+                 ("context_length", cfg["context"]), ("attention.sliding_window", cfg["window"]),
+                 ("attention.sliding_window_pattern", cfg["pattern"])]:
+        w.add(f"{arch}.{k}", int(v))
+    w.add(f"{arch}.attention.layer_norm_rms_epsilon", 1e-6)
+    w.add(f"{arch}.rope.freq_base", 1000000.0)
+    w.add(f"{arch}.rope.freq_base_swa", 10000.0)
+    w.add(f"{arch}.rope.partial_rotary_factor", float(cfg["rope_frac"]))
+    w.add(f"{arch}.attn_logit_softcapping", float(cfg.get("attn_cap", 50.0)))
+    w.add(f"{arch}.final_logit_softcapping", float(cfg.get("final_cap", 30.0)))
+
+    def rng():
+        return np.random.default_rng(root.integers(1 << 62))
+
+    pool = cfg.get("row_pool", 0)
+
+    def mat(name, rows, cols, qtype, std=0.02):
+        n = min(rows, pool) if pool else rows
+        x = rng().standard_normal((n, cols), dtype=np.float32) * np.float32(std)
+        q = quant(qtype, x)
+        if n < rows:
+            q = np.tile(q.reshape(n, -1), ((rows + n - 1) // n, 1))[:rows].ravel()
+        w.add_tensor(name, [cols, rows], qtype, q)
+
+    def f32(name, dims, values):
+        w.add_tensor(name, dims, G.GGML_F32, np.ascontiguousarray(values, dtype=np.float32))
+
+    def norm(name, n):
+        f32(name, [n], 1.0 + 0.02 * rng().standard_normal(n, dtype=np.float32))
+
+    mat("token_embd.weight", V, d, cfg["emb"])
+    norm("output_norm.weight", d)
+    for i in range(L):
+        pre = f"blk.{i}."
+        for nm in ("attn_norm", "post_attention_norm", "ffn_norm", "post_ffw_norm"):
+            norm(pre + nm + ".weight", d)
+        mat(pre + "attn_q.weight", nh * hd, d, cfg["mat"])
+        mat(pre + "attn_k.weight", nkv * hd, d, cfg["mat"])
+        mat(pre + "attn_v.weight", nkv * hd, d, cfg["mat"])
+        mat(pre + "attn_output.weight", d, nh * hd, cfg["mat"])
+        norm(pre + "attn_q_norm.weight", hd)
+        norm(pre + "attn_k_norm.weight", hd)
+        mat(pre + "ffn_gate.weight", ffn, d, cfg["mat"])
+        mat(pre + "ffn_up.weight", ffn, d, cfg["mat"])
+        mat(pre + "ffn_down.weight", d, ffn, cfg["down"])
+        f32(pre + "layer_scalar", [1], [1.0 + 0.05 * float(rng().standard_normal())])
+    w.write()
+    return w.path
 
 
 def cached(preset="tiny", seed=0, directory=None, quantize=None):

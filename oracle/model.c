@@ -22,6 +22,21 @@
  * layer between fc and the final norm; its input hidden is the final-normed
  * hidden of the last verified token for the first draft, then the layer
  * output of the previous draft.
+ * Gemma4 mode (or_model_set_gemma; src/Gemma4.jl): attention-only blocks
+ *   forward!                :604-676  embedding x embed_scale; per layer
+ *                                     x = x + norm_pa(attn(norm_in(x)));
+ *                                     x = (x + norm_pf(mlp(norm_ff(x)))) * layer_scalar
+ *   attention_forward!      :296-456  q / k RMSNorm with weights, v RMSNorm without,
+ *                                     RoPE on pairs (k, k + hd/2) (sliding layers: every
+ *                                     pair, theta_swa; full layers: the first
+ *                                     partial * hd / 2 pairs, frequencies over hd,
+ *                                     theta_full), scores q.k (scale 1) capped by
+ *                                     tanh(s / cap) cap, sliding window of `window`
+ *                                     keys, softmax, no output gate
+ *   mlp_forward!            :556-581  down(gelu_tanh(gate x) * up x)
+ *   get_logits              :678-693  tied lm_head, then logit_softcap!
+ *                                     (CommonOps.jl:326-333)
+ *   per-layer inputs (:459-554) are not part of this model (config 5 has none)
  * Matrix-vector products accumulate in f32 in index order (activation mode
  * 0, default: the GPU engine's exact f32 activations).  In mode 1 those with
  * K-quant weights (Q4_K/Q5_K/Q6_K) follow the reference's quantized kernels:
@@ -40,6 +55,7 @@
 typedef struct {
     int ssm;
     float *attn_norm, *post_norm;
+    float *ffn_norm, *post_ffw_norm, *layer_scalar;   /* Gemma4 */
     /* ssm */
     float *in_proj, *gate_proj, *ssm_out, *conv_w, *alpha_w, *beta_w, *ssm_a, *dt_bias, *ssm_norm;
     float *conv_state, *h;                  /* [C][K], [heads][vd][kd] */
@@ -62,6 +78,9 @@ struct or_model {
     const float *kq[1024];          /* weight slots holding K-quant matrices */
     int nkq;
     int act;                        /* K-quant activation mode: 0 exact f32, 1 Q8_K */
+    int gemma;                      /* Gemma4 block semantics */
+    or_gemma_config g;
+    float *cos_swa, *sin_swa, *cos_full, *sin_full;   /* [max_ctx][hd/2] */
 };
 
 static void *xcalloc(size_t n, size_t s) { void *p = calloc(n, s); if (!p) abort(); return p; }
@@ -93,7 +112,7 @@ static void free_layer(or_layer *L) {
     float **f[] = {&L->attn_norm, &L->post_norm, &L->in_proj, &L->gate_proj, &L->ssm_out, &L->conv_w,
                    &L->alpha_w, &L->beta_w, &L->ssm_a, &L->dt_bias, &L->ssm_norm, &L->conv_state, &L->h,
                    &L->wq, &L->wk, &L->wv, &L->wo, &L->q_norm, &L->k_norm, &L->kc, &L->vc,
-                   &L->ffn_gate, &L->ffn_up, &L->ffn_down};
+                   &L->ffn_gate, &L->ffn_up, &L->ffn_down, &L->ffn_norm, &L->post_ffw_norm, &L->layer_scalar};
     for (size_t i = 0; i < sizeof f / sizeof f[0]; i++) { free(*f[i]); *f[i] = NULL; }
 }
 
@@ -104,6 +123,7 @@ void or_model_free(or_model *m) {
     free(m->layers);
     free(m->embed); free(m->final_norm); free(m->mtp_fc); free(m->mtp_norm_e); free(m->mtp_norm_h);
     free(m->mtp_norm); free(m->cos_cache); free(m->sin_cache);
+    free(m->cos_swa); free(m->sin_swa); free(m->cos_full); free(m->sin_full);
     free(m);
 }
 
@@ -142,6 +162,9 @@ static float **slot(or_model *m, int layer, int kind) {
     case OR_T_FFN_GATE: return &L->ffn_gate;
     case OR_T_FFN_UP: return &L->ffn_up;
     case OR_T_FFN_DOWN: return &L->ffn_down;
+    case OR_T_FFN_NORM: return &L->ffn_norm;
+    case OR_T_POST_FFW_NORM: return &L->post_ffw_norm;
+    case OR_T_LAYER_SCALAR: return &L->layer_scalar;
     }
     return NULL;
 }
@@ -440,10 +463,166 @@ static void decoder_layer(or_model *m, or_layer *L, float *x, int pos) {
     free(xn); free(r);
 }
 
+/* ---------------- Gemma4 blocks (src/Gemma4.jl) ---------------- */
+
+/* precompute_rope (:205-249): inverse frequencies and angles in Float64,
+   cos / sin stored as Float32; pair k rotates dims (k, k + hd/2) */
+void or_model_set_gemma(or_model *m, const or_gemma_config *g) {
+    m->gemma = 1;
+    m->g = *g;
+    const int hd = m->c.head_dim, half = hd / 2, T = m->c.max_ctx;
+    const int angles = (int)(g->partial_rotary_factor * (float)hd) / 2;  /* Int(partial * hd / 2) */
+    free(m->cos_swa); free(m->sin_swa); free(m->cos_full); free(m->sin_full);
+    m->cos_swa = (float *)xcalloc((size_t)T * half, 4);
+    m->sin_swa = (float *)xcalloc((size_t)T * half, 4);
+    m->cos_full = (float *)xcalloc((size_t)T * half, 4);
+    m->sin_full = (float *)xcalloc((size_t)T * half, 4);
+    for (int k = 0; k < half; k++) {
+        const double fs = 1.0 / pow((double)g->rope_theta_swa, 2.0 * k / (double)hd);
+        const double ff = k < angles ? 1.0 / pow((double)g->rope_theta_full, 2.0 * k / (double)hd) : 0.0;
+        for (int p = 0; p < T; p++) {
+            m->cos_swa[(size_t)p * half + k] = (float)cos(p * fs);
+            m->sin_swa[(size_t)p * half + k] = (float)sin(p * fs);
+            m->cos_full[(size_t)p * half + k] = (float)cos(p * ff);
+            m->sin_full[(size_t)p * half + k] = (float)sin(p * ff);
+        }
+    }
+}
+
+static int gemma_sliding(const or_model *m, int layer) {
+    return m->g.sliding_pattern <= 0 || (layer + 1) % m->g.sliding_pattern != 0;
+}
+
+/* gelu_tanh (:253-257) */
+static inline float gelu_tanh(float x) {
+    const float c = sqrtf(2.0f / (float)M_PI);
+    return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+}
+
+/* apply_rope! (:263-293) on nheads heads with the layer's table */
+static void gemma_rope(float *x, int nheads, int hd, const float *cs, const float *sn) {
+    const int half = hd / 2;
+    for (int h = 0; h < nheads; h++) {
+        float *v = x + (size_t)h * hd;
+        for (int k = 0; k < half; k++) {
+            const float q0 = v[k], q1 = v[k + half];
+            v[k] = q0 * cs[k] - q1 * sn[k];
+            v[k + half] = q0 * sn[k] + q1 * cs[k];
+        }
+    }
+}
+
+/* attention_forward! (:296-456) for one token at pos */
+static void gemma_attn(or_model *m, or_layer *L, int layer, const float *x, int pos, float *out) {
+    const or_model_config *c = &m->c;
+    const int nh = c->n_head, nkv = c->n_kv_head, hd = c->head_dim, d = c->hidden, half = hd / 2;
+    const int sliding = gemma_sliding(m, layer);
+    const float *cs = (sliding ? m->cos_swa : m->cos_full) + (size_t)pos * half;
+    const float *sn = (sliding ? m->sin_swa : m->sin_full) + (size_t)pos * half;
+    float *q = (float *)malloc((size_t)nh * hd * 4), *k = (float *)malloc((size_t)nkv * hd * 4);
+    float *v = (float *)malloc((size_t)nkv * hd * 4), *o = (float *)malloc((size_t)nh * hd * 4);
+    float *sc = (float *)malloc((size_t)(pos + 1) * 4);
+    matvec_w(m, q, L->wq, x, nh * hd, d);
+    for (int h = 0; h < nh; h++) rmsnorm(q + (size_t)h * hd, q + (size_t)h * hd, L->q_norm, hd, c->rms_eps);
+    gemma_rope(q, nh, hd, cs, sn);
+    matvec_w(m, k, L->wk, x, nkv * hd, d);
+    matvec_w(m, v, L->wv, x, nkv * hd, d);
+    for (int h = 0; h < nkv; h++) {  /* rmsnorm_no_scale! (CommonOps.jl:43-53) */
+        float *vh = v + (size_t)h * hd, ss = 0.f;
+        for (int i = 0; i < hd; i++) ss += vh[i] * vh[i];
+        const float inv = 1.0f / sqrtf(ss / (float)hd + c->rms_eps);
+        for (int i = 0; i < hd; i++) vh[i] = vh[i] * inv;
+    }
+    for (int h = 0; h < nkv; h++) rmsnorm(k + (size_t)h * hd, k + (size_t)h * hd, L->k_norm, hd, c->rms_eps);
+    gemma_rope(k, nkv, hd, cs, sn);
+    memcpy(L->kc + (size_t)pos * nkv * hd, k, (size_t)nkv * hd * 4);
+    memcpy(L->vc + (size_t)pos * nkv * hd, v, (size_t)nkv * hd * 4);
+    const int start = sliding && m->g.window > 0 ? (pos + 1 - m->g.window > 0 ? pos + 1 - m->g.window : 0) : 0;
+    const int ratio = nh / nkv;
+    const float cap = m->g.attn_softcap;
+    for (int h = 0; h < nh; h++) {
+        const int kvh = h / ratio;
+        const float *qh = q + (size_t)h * hd;
+        float mx = -INFINITY;
+        for (int t = start; t <= pos; t++) {
+            const float *kt = L->kc + ((size_t)t * nkv + kvh) * hd;
+            float s = 0.f;
+            for (int i = 0; i < hd; i++) s += qh[i] * kt[i];
+            if (cap > 0.f) s = tanhf(s / cap) * cap;
+            sc[t - start] = s;
+            if (s > mx) mx = s;
+        }
+        float sum = 0.f;
+        for (int t = start; t <= pos; t++) {
+            sc[t - start] = expf(sc[t - start] - mx);
+            sum += sc[t - start];
+        }
+        const float inv = 1.0f / sum;
+        float *oh = o + (size_t)h * hd;
+        for (int i = 0; i < hd; i++) oh[i] = 0.f;
+        for (int t = start; t <= pos; t++) {
+            const float w = sc[t - start] * inv;
+            const float *vt = L->vc + ((size_t)t * nkv + kvh) * hd;
+            for (int i = 0; i < hd; i++) oh[i] += w * vt[i];
+        }
+    }
+    matvec_w(m, out, L->wo, o, d, nh * hd);
+    free(q); free(k); free(v); free(o); free(sc);
+}
+
+/* mlp_forward! (:556-581) */
+static void gemma_mlp(or_model *m, or_layer *L, const float *x, float *out) {
+    const int f = m->c.ffn, d = m->c.hidden;
+    float *g = (float *)malloc(f * 4), *u = (float *)malloc(f * 4);
+    matvec_w(m, g, L->ffn_gate, x, f, d);
+    for (int i = 0; i < f; i++) g[i] = gelu_tanh(g[i]);
+    matvec_w(m, u, L->ffn_up, x, f, d);
+    for (int i = 0; i < f; i++) g[i] = g[i] * u[i];
+    matvec_w(m, out, L->ffn_down, g, d, f);
+    free(g); free(u);
+}
+
+/* the layer body of forward! (:622-650) */
+static void gemma_layer(or_model *m, or_layer *L, int layer, float *x, int pos) {
+    const int d = m->c.hidden;
+    const float eps = m->c.rms_eps;
+    float *xn = (float *)malloc(d * 4), *r = (float *)malloc(d * 4);
+    rmsnorm(xn, x, L->attn_norm, d, eps);
+    gemma_attn(m, L, layer, xn, pos, r);
+    rmsnorm(r, r, L->post_norm, d, eps);
+    for (int i = 0; i < d; i++) x[i] = r[i] + x[i];
+    rmsnorm(xn, x, L->ffn_norm, d, eps);
+    gemma_mlp(m, L, xn, r);
+    rmsnorm(r, r, L->post_ffw_norm, d, eps);
+    for (int i = 0; i < d; i++) x[i] = x[i] + r[i];
+    const float s = L->layer_scalar ? L->layer_scalar[0] : 1.0f;
+    for (int i = 0; i < d; i++) x[i] *= s;
+    free(xn); free(r);
+}
+
+static int gemma_forward_token(or_model *m, int token, int pos, float *logits, float *hidden) {
+    const or_model_config *c = &m->c;
+    const int d = c->hidden;
+    float *x = (float *)malloc(d * 4), *xn = (float *)malloc(d * 4);
+    for (int i = 0; i < d; i++) x[i] = m->embed[(size_t)token * d + i] * m->g.embed_scale;
+    for (int i = 0; i < c->n_layers; i++) gemma_layer(m, &m->layers[i], i, x, pos);
+    rmsnorm(xn, x, m->final_norm, d, c->rms_eps);
+    if (hidden) memcpy(hidden, xn, d * 4);
+    if (logits) {
+        matvec_w(m, logits, m->embed, xn, c->vocab, d);
+        const float cap = m->g.final_softcap;
+        if (cap > 0.f)
+            for (int i = 0; i < c->vocab; i++) logits[i] = tanhf(logits[i] / cap) * cap;
+    }
+    free(x); free(xn);
+    return 0;
+}
+
 /* one token of forward_cpu!: logits (vocab) and the final-normed hidden (d) */
 int or_forward_token(or_model *m, int token, int pos, float *logits, float *hidden) {
     const or_model_config *c = &m->c;
     if (token < 0 || token >= c->vocab || pos < 0 || pos >= c->max_ctx) return -1;
+    if (m->gemma) return gemma_forward_token(m, token, pos, logits, hidden);
     const int d = c->hidden;
     float *x = (float *)malloc(d * 4), *xn = (float *)malloc(d * 4);
     memcpy(x, m->embed + (size_t)token * d, d * 4);

@@ -89,8 +89,20 @@ enum {
     OR_T_EMBED = 0, OR_T_FINAL_NORM, OR_T_MTP_FC, OR_T_MTP_NORM_E, OR_T_MTP_NORM_H, OR_T_MTP_NORM,
     OR_T_ATTN_NORM = 10, OR_T_POST_NORM, OR_T_IN_PROJ, OR_T_GATE_PROJ, OR_T_SSM_OUT, OR_T_CONV,
     OR_T_ALPHA, OR_T_BETA, OR_T_SSM_A, OR_T_DT_BIAS, OR_T_SSM_NORM, OR_T_WQ, OR_T_WK, OR_T_WV,
-    OR_T_WO, OR_T_Q_NORM, OR_T_K_NORM, OR_T_FFN_GATE, OR_T_FFN_UP, OR_T_FFN_DOWN
+    OR_T_WO, OR_T_Q_NORM, OR_T_K_NORM, OR_T_FFN_GATE, OR_T_FFN_UP, OR_T_FFN_DOWN,
+    /* Gemma4 blocks: pre-MLP norm, post-MLP norm, layer scalar (1 element) */
+    OR_T_FFN_NORM, OR_T_POST_FFW_NORM, OR_T_LAYER_SCALAR
 };
+/* Gemma4 block semantics (src/Gemma4.jl:253-688, src/CommonOps.jl:326-333),
+ * switched on by or_model_set_gemma: layer i is a full-attention layer iff
+ * (i + 1) % sliding_pattern == 0, else a sliding one (window keys) */
+typedef struct {
+    int32_t window, sliding_pattern;
+    float attn_softcap, final_softcap;   /* 0: off */
+    float rope_theta_swa, rope_theta_full, partial_rotary_factor;
+    float embed_scale;
+} or_gemma_config;
+void or_model_set_gemma(or_model *m, const or_gemma_config *g);
 or_model *or_model_new(const or_model_config *c);
 void or_model_free(or_model *m);
 /* layer >= 0: decoder layer; -1: global tensors; -2: the MTP decoder layer */

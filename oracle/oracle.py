@@ -346,14 +346,33 @@ _KIND = {"attn_norm.weight": 10, "post_attention_norm.weight": 11, "attn_qkv.wei
          "ssm_beta.weight": 17, "ssm_a": 18, "ssm_dt.bias": 19, "ssm_norm.weight": 20,
          "attn_q.weight": 21, "attn_k.weight": 22, "attn_v.weight": 23, "attn_output.weight": 24,
          "attn_q_norm.weight": 25, "attn_k_norm.weight": 26, "ffn_gate.weight": 27, "ffn_up.weight": 28,
-         "ffn_down.weight": 29}
+         "ffn_down.weight": 29, "ffn_norm.weight": 30, "post_ffw_norm.weight": 31, "layer_scalar": 32}
 _GLOBAL = {"token_embd.weight": 0, "output_norm.weight": 1, "mtp.fc.weight": 2,
            "mtp.pre_fc_norm_embedding.weight": 3, "mtp.pre_fc_norm_hidden.weight": 4, "mtp.norm.weight": 5}
+
+
+class _GemmaCfg(ctypes.Structure):
+    _fields_ = [("window", ctypes.c_int32), ("sliding_pattern", ctypes.c_int32)] + [
+        (n, ctypes.c_float) for n in ("attn_softcap", "final_softcap", "rope_theta_swa", "rope_theta_full",
+                                      "partial_rotary_factor", "embed_scale")]
+
+
+def gemma_config(md, hidden):
+    """Gemma4 block parameters from GGUF metadata (general.architecture
+    "gemma4"; keys as the synthetic models write them)"""
+    g = lambda k, dflt: md.get(f"gemma4.{k}", dflt)  # noqa: E731
+    return _GemmaCfg(int(g("attention.sliding_window", 512)), int(g("attention.sliding_window_pattern", 6)),
+                     float(g("attn_logit_softcapping", 0.0)), float(g("final_logit_softcapping", 0.0)),
+                     float(g("rope.freq_base_swa", 10000.0)), float(g("rope.freq_base", 1000000.0)),
+                     float(g("rope.partial_rotary_factor", 0.25)),
+                     float(np.float32(np.sqrt(np.float64(hidden)))))
 
 
 def _model_lib():
     L = lib()
     if not hasattr(L, "_model_init"):
+        L.or_model_set_gemma.argtypes = [ctypes.c_void_p, ctypes.POINTER(_GemmaCfg)]
+        L.or_model_set_gemma.restype = None
         L.or_model_new.restype = ctypes.c_void_p
         L.or_model_new.argtypes = [ctypes.POINTER(_Cfg)]
         L.or_model_free.argtypes = [ctypes.c_void_p]
@@ -412,6 +431,10 @@ class OracleModel:
             raw = np.ascontiguousarray(f.raw(name))
             assert L.or_model_set(self.h, layer, kind, ti.type, raw.ctypes.data, ti.n_elements) == 0, name
         self.has_mtp = "mtp.fc.weight" in f.tensors
+        self.gemma = arch == "gemma4"
+        if self.gemma:
+            self.gcfg = gemma_config(md, self.hidden)
+            L.or_model_set_gemma(self.h, ctypes.byref(self.gcfg))
         L.or_model_reset(self.h)
 
     def close(self):

@@ -196,3 +196,20 @@ def test_synth_model_same_bytes_with_oracle_encoder(O, pkg, tmp_path):
     a = synth.build(str(tmp_path / "lib.gguf"), "mini", 3)
     b = synth.build(str(tmp_path / "oracle.gguf"), "mini", 3, quantize=O.quantize)
     assert open(a, "rb").read() == open(b, "rb").read()
+
+
+def test_gemma_oracle_blocks(O, pkg, tmp_path):
+    """the oracle's Gemma4 restatement on the small Gemma4-block model: the
+    final softcap bounds every logit, the embedding scale is sqrt(hidden),
+    and the forward is deterministic across a reset"""
+    from inferno_b200 import synth, gguf
+    path = synth.build(str(tmp_path / "g.gguf"), "gemma_mini", 1, quantize=O.quantize)
+    om = O.OracleModel(gguf.GGUFFile(path), 64)
+    assert om.gemma and om.gcfg.window == 6 and om.gcfg.sliding_pattern == 2
+    assert om.gcfg.embed_scale == np.float32(16.0)
+    prompt = synth.prompt(om.vocab, 20, seed=2)
+    a = om.greedy(list(prompt), 6)
+    b = om.greedy(list(prompt), 6)
+    assert a == b
+    lg, _ = om.forward_token(a[-1], len(prompt) + 5)
+    assert np.isfinite(lg).all() and np.abs(lg).max() <= om.gcfg.final_softcap
