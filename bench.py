@@ -543,6 +543,7 @@ def run_spec(args):
     # only; at N > 1 the line is the replicas' throughput)
     extras = {}
     if ws == 1 and not args.no_extras:
+        extras["prefill_2048"] = prefill_extra(model, prompt_len=2048)
         extras["config3_accept"] = accept_extra(pkg, local, reps=max(3, args.steps // 2))
         extras["config2_sweep"] = sweep_extra(pkg, local)
     if rank == 0:
@@ -590,6 +591,32 @@ def run_spec(args):
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def prefill_extra(model, prompt_len=2048, reps=2):
+    """one request of the config-1 model with a seeded prompt of prompt_len
+    tokens through ifr_prefill (H2D of the prompt, chunks of 64 tokens: every
+    projection over the chunk's columns, the SSM layers scanning a chunk in
+    one launch, then the last token with logits; synchronous), wall clock per
+    call after one warm-up call on a fresh state each time"""
+    from inferno_b200 import synth
+    from inferno_b200.engine import State
+    prompt = synth.prompt(model.info.vocab, prompt_len, 77)
+    times = []
+    for i in range(reps + 1):
+        st = State(model, prompt_len + 64)
+        model.ctx.sync()
+        t0 = time.perf_counter()
+        st.prefill(prompt)
+        dt = time.perf_counter() - t0
+        if i:
+            times.append(dt)
+        st.free()
+    ms = float(np.median(times)) * 1e3
+    return {"workload": f"ifr_prefill of one config-1 request, {prompt_len}-token seeded prompt",
+            "chunk_tokens": 64, "ms": round(ms, 2), "tokens_per_s": round(prompt_len / (ms * 1e-3), 1),
+            "calls_timed": reps,
+            "path": "projections on the dense tcgen05 GEMM (64 columns), GatedDeltaNet chunk scan, attention in 8-token sub-calls"}
 
 
 def accept_extra(pkg, device, reps=5):
@@ -908,8 +935,8 @@ def run_tp(args):
             "dtype": ACT_DTYPE[0].replace("q4_k/q6_k", "q4_k target, q8_0 draft"),
             "data": "synthetic: seeded random-init Gemma4-shape target and draft GGUFs (rows drawn from a 1024-row pool per matrix), seeded uniform prompt",
             "config": {"workload": "greedy spec-decode with a draft model, BASELINE config 5 (Gemma4-shape target, tensor parallel)",
-                       "target": "hidden 5376, 62 attention layers (Qwen-style blocks), 32q/16kv x 128, FFN 21504, vocab 262144, Q4_K",
-                       "draft": "hidden 1152, 26 attention layers, 4q/1kv x 256, FFN 6912, Q8_0, replicated",
+                       "target": "hidden 5376, 62 Gemma4 attention layers (5 sliding-window : 1 full, window 1024, GELU-tanh MLP, softcaps), 32q/16kv x 128, FFN 21504, vocab 262144, Q4_K",
+                       "draft": "hidden 1152, 26 Gemma4 attention layers, 4q/1kv x 256, FFN 6912, Q8_0, replicated",
                        "gamma": G, "prompt": P, "batch": 1, "tp": ws, "prefill_s": round(prefill_s, 2),
                        "load_s": round(t_load, 1), "tokens_emitted_timed": emitted,
                        "l2": "inputs larger than L2: %.2f GB of target weights per rank per verify" % (shard_bytes / 1e9),

@@ -498,6 +498,7 @@ struct ifr_state {
     ifr::EngineScalars *sc = nullptr;   // device
     int32_t *vtok = nullptr, *acc = nullptr, *outtok = nullptr, *log = nullptr, *mtp_pos = nullptr;
     int32_t *h_tok = nullptr;           // pinned staging
+    int32_t *chunk_pos = nullptr;       // prefill chunk: positions of its 8-token attention sub-calls
     int32_t *prompt = nullptr;          // device copy of the prompts being prefilled [B][max_ctx]
     float *x, *xn, *proj, *y, *gu, *hmid, *hid, *logits;
     float *mtp_h, *mtp_cat;
@@ -601,6 +602,29 @@ int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, 
     return IFR_OK;
 }
 
+// the attention of n tokens per request; a prefill chunk (n > kNMax, one
+// request) runs as sub-calls of kNMax tokens in order, each at its own
+// position (s->chunk_pos), so every sub-call finds the earlier ones' keys in
+// the cache
+int attn_call(ifr_state *s, ifr::AttnArgs a, int n, int B, cudaStream_t st) {
+    if (n <= kNMax) {
+        ECHECK(ifr::attn_step(a, B, st), "attn_step");
+        return IFR_OK;
+    }
+    const float *qkv = a.qkv;
+    float *out = a.out;
+    for (int t0 = 0, i = 0; t0 < n; t0 += kNMax, i++) {
+        a.N = std::min(kNMax, n - t0);
+        a.qkv = qkv + (int64_t)t0 * a.ldq;
+        a.out = out + (int64_t)t0 * a.ldo;
+        a.pos = s->chunk_pos + i;
+        if (s->attn_part) a.splits = ifr::attn_splits(a.nh, a.nkv, a.N, B, s->max_ctx);
+        ECHECK(ifr::attn_step(a, B, st), "attn_step");
+        s->launches += s->attn_part ? 2 : 1;
+    }
+    return IFR_OK;
+}
+
 // Gemma4 full-attention layers rotate Int(partial * hd / 2) pairs
 // (precompute_rope, Gemma4.jl:214-228); the remaining pairs have cos 1, sin 0
 int gemma_full_pairs(const ifr_model *m) {
@@ -662,7 +686,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
             a.part = s->attn_part;
             a.splits = ifr::attn_splits(m->nh, m->nkv, n, B, s->max_ctx);
         }
-        ECHECK(ifr::attn_step(a, B, st), "attn_step");
+        if ((rc = attn_call(s, a, n, B, st))) return rc;
         // row-parallel projections: every rank's partial, summed over the ranks
         if ((rc = gemv(s, gcat, L.out, s->y, nc, s->xn, false, st))) return rc;
         if ((rc = comm_allreduce_sum(m->comm, s->xn, (size_t)nc * d, st))) return rc;
@@ -708,7 +732,10 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.b_rq = (int64_t)kNMax * m->conv_channels;
         a.b_rkv = (int64_t)c.ssm_heads * kNMax * (2 * hd + 2);
         a.b_prev = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
-        ECHECK(ifr::ssm_step(a, c.ssm_head_dim, B, st), "ssm_step");
+        if (n > kNMax)  // a prefill chunk of one request: scanned and committed in one launch
+            ECHECK(ifr::ssm_chunk(a, c.ssm_head_dim, st), "ssm_chunk");
+        else
+            ECHECK(ifr::ssm_step(a, c.ssm_head_dim, B, st), "ssm_step");
     } else {
         ProfScope ps(s, CAT_ATTN, 0, st);
         ifr::AttnArgs a{};
@@ -735,7 +762,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
             a.part = s->attn_part;
             a.splits = ifr::attn_splits(m->nh, m->nkv, n, B, s->max_ctx);
         }
-        ECHECK(ifr::attn_step(a, B, st), "attn_step");
+        if ((rc = attn_call(s, a, n, B, st))) return rc;
     }
     // row-parallel projections: rank 0 adds its partial to the residual, the
     // others write theirs, and one sum all-reduce leaves x + sum on every rank
@@ -907,6 +934,10 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
                         s->x, m->embed_scale, st),
            "embedding");
     s->launches += 2;  // embedding, final norm
+    if (n > kNMax) {
+        ifr::chunk_positions(s->chunk_pos, s->sc, (n + kNMax - 1) / kNMax, kNMax, st);
+        s->launches++;
+    }
     const int64_t kv_ld = (int64_t)s->max_ctx * m->nkv * c.head_dim;
     for (int li = 0; li < c.n_layers; li++) {
         int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, sc_ld, kv_ld, false, st);
@@ -1207,7 +1238,8 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     s->B = batch;
     s->max_ctx = max_ctx;
     s->log_cap = max_ctx + 16;
-    const int d = c.hidden, N = kNMax * batch, B = batch;
+    // one request: columns for a prefill chunk of kPrefillChunk tokens
+    const int d = c.hidden, N = batch == 1 ? ifr::kPrefillChunk : kNMax * batch, B = batch;
     int64_t maxproj = (int64_t)(2 * m->nh + 2 * m->nkv) * c.head_dim;
     if (m->conv_channels + m->inner > maxproj) maxproj = m->conv_channels + m->inner;
     const int64_t ymax = std::max<int64_t>(m->inner, (int64_t)m->nh * c.head_dim);
@@ -1219,6 +1251,7 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     chk(dalloc(s, &s->acc, B + 4));
     chk(dalloc(s, &s->outtok, N + B));
     chk(dalloc(s, &s->mtp_pos, B + 4));
+    chk(dalloc(s, &s->chunk_pos, 32));
     chk(dalloc(s, &s->log, (size_t)B * s->log_cap));
     chk(dalloc(s, &s->x, (size_t)N * d));
     chk(dalloc(s, &s->xn, (size_t)N * d));
@@ -1423,14 +1456,22 @@ int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first
     // device-to-device copy, so the chunks queue without host round trips
     cudaError_t e0 = cudaMemcpyAsync(s->prompt, tokens, sizeof(int32_t) * B * n, cudaMemcpyHostToDevice, st);
     if (e0 != cudaSuccess) rc = ifr_cuda_fail(e0, "H2D prompt");
+    // one request: chunks of kPrefillChunk tokens (the SSM layers scan and
+    // commit a chunk in one launch); a batch: kNMax tokens per request
+    const int chunk = B == 1 ? ifr::kPrefillChunk : kNMax;
     for (int i0 = 0; !rc && i0 < n;) {
         const bool last = i0 == n - 1;
-        const int k = last ? 1 : std::min(kNMax, n - 1 - i0);
-        cudaError_t e = cudaMemcpy2DAsync(s->vtok, sizeof(int32_t) * kNMax, s->prompt + i0, sizeof(int32_t) * n,
-                                          sizeof(int32_t) * k, B, cudaMemcpyDeviceToDevice, st);
+        const int k = last ? 1 : std::min(chunk, n - 1 - i0);
+        cudaError_t e = B == 1 ? cudaMemcpyAsync(s->vtok, s->prompt + i0, sizeof(int32_t) * k,
+                                                 cudaMemcpyDeviceToDevice, st)
+                               : cudaMemcpy2DAsync(s->vtok, sizeof(int32_t) * kNMax, s->prompt + i0,
+                                                   sizeof(int32_t) * n, sizeof(int32_t) * k, B,
+                                                   cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prompt chunk"); break; }
         rc = target_forward(s, k, last, false, st);
-        if (!rc) ifr::commit(s->sc, s->acc, s->outtok, k, true, nullptr, nullptr, c.hidden, s->log, s->log_cap, B, st);
+        if (!rc)
+            ifr::commit(s->sc, s->acc, s->outtok, k, k > kNMax ? 2 : 1, nullptr, nullptr, c.hidden, s->log,
+                        s->log_cap, B, st);
         if (!rc && last) {
             rc = greedy_accept(s, nullptr, 0, B, 0, s->outtok, 1, st);
             if (rc) break;

@@ -585,6 +585,253 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
     }
 }
 
+// Prefill chunk of up to kChunkMax tokens of one request (GatedDeltaNetCPU,
+// ModelCPU.jl:566-731, over the chunk's tokens in order, as forward_cpu! feeds
+// a prompt): the scan of the chunk runs inside one launch with each CTA's
+// state rows in registers, and the result is committed at once - S holds the
+// state after the last token, the conv history the chunk's last K-1 inputs,
+// and no replay record is written (the caller's commit leaves nothing to
+// replay).  A pending replay of the previous call's tokens is applied first,
+// as in ssm_step_kernel.  Grid (kSsmSplit, H), one cluster per head; the
+// per-token arrays live in dynamic shared memory (ChunkSmem).
+constexpr int kChunkMax = 64;
+
+template <int HD>
+struct ChunkSmem {
+    static constexpr int RPC = HD / kSsmSplit;
+    float cq[kChunkMax][RPC], ck[kChunkMax][RPC], cv[kChunkMax][RPC];
+    float xq[kChunkMax][HD], xk[kChunkMax][HD];
+    float rk[kMaxN][HD], rv[kMaxN][RPC];
+    float rdec[kMaxN], rbeta[kMaxN], ndec[kChunkMax], nbeta[kChunkMax];
+    float ab[3][kChunkMax], ab_part[3][kChunkMax];
+    float ys[kChunkMax][RPC];
+    float ssq[kChunkMax];
+    float red_n[8][3 * kChunkMax];
+};
+
+template <int HD>
+__global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_chunk_kernel(SsmArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    constexpr int RPC = HD / kSsmSplit, TPR = 256 / RPC, CPT = HD / TPR, REC = 2 * HD + 2;
+    extern __shared__ __align__(16) unsigned char chunk_smem[];
+    ChunkSmem<HD> &m = *reinterpret_cast<ChunkSmem<HD> *>(chunk_smem);
+    const int rank = (int)cluster.block_rank();
+    const int h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int N = a.N, K = a.K, C = a.C, qk = a.H * HD;
+    const int r0 = rank * RPC;
+    pdl_trigger();
+    pdl_wait();
+    const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
+
+    // 1. conv of the owned channels over committed history, replayed and new tokens
+    auto win = [&](int i, int ch) -> const float * {
+        if (i < K - 1) return a.hist + (int64_t)i * C + ch;
+        if (i < K - 1 + r) return a.rq + (int64_t)(i - K + 1) * C + ch;
+        return a.proj + (int64_t)(i - K + 1 - r) * a.ldp + ch;
+    };
+    for (int lc = tid; lc < 3 * RPC; lc += 256) {
+        const int part = lc / RPC, i = lc % RPC;
+        const int ch = part * qk + h * HD + r0 + i;
+        float w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) w[k] = k < K ? a.conv_w[(int64_t)ch * K + k] : 0.f;
+        for (int t = 0; t < N; t++) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (k < K) acc += *win(r + t + k, ch) * w[k];
+            const float o = acc / (1.0f + expf(-acc));
+            if (part == 0) m.cq[t][i] = o;
+            else if (part == 1) m.ck[t][i] = o;
+            else m.cv[t][i] = o;
+        }
+    }
+    // 2. alpha / beta projections of the new tokens, this CTA's d slice
+    {
+        const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
+        const int per = (a.d + kSsmSplit - 1) / kSsmSplit;
+        const int i0 = rank * per, i1 = min(a.d, i0 + per);
+        for (int t0 = 0; t0 < N; t0 += kMaxN) {
+            float pa[kMaxN], pb[kMaxN], ps[kMaxN];
+#pragma unroll
+            for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = ps[t] = 0.f;
+            for (int i = i0 + tid; i < i1; i += 256) {
+                const float al = wa[i], be = wb[i], nw = a.in_norm ? a.in_norm[i] : 1.f;
+#pragma unroll
+                for (int t = 0; t < kMaxN; t++)
+                    if (t0 + t < N) {
+                        const float xv = a.xn[(int64_t)(t0 + t) * a.d + i], xn = xv * nw;
+                        pa[t] += al * xn;
+                        pb[t] += be * xn;
+                        ps[t] += xv * xv;
+                    }
+            }
+#pragma unroll
+            for (int t = 0; t < kMaxN; t++) {
+                const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]), vs = warp_sum(ps[t]);
+                if (lane == 0 && t0 + t < N) {
+                    m.red_n[warp][t0 + t] = va;
+                    m.red_n[warp][kChunkMax + t0 + t] = vb;
+                    m.red_n[warp][2 * kChunkMax + t0 + t] = vs;
+                }
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < 3 * N; i += 256) {
+            const int which = i / N, t = i % N;
+            float v = 0.f;
+            for (int w8 = 0; w8 < 8; w8++) v += m.red_n[w8][which * kChunkMax + t];
+            m.ab_part[which][t] = v;
+        }
+    }
+    // 3. the previous call's replay record
+    float *rec = a.rkv + (int64_t)h * kMaxN * REC;
+    for (int i = tid; i < r * HD; i += 256) m.rk[i / HD][i % HD] = rec[(i / HD) * REC + i % HD];
+    for (int i = tid; i < r * RPC; i += 256) m.rv[i / RPC][i % RPC] = rec[(i / RPC) * REC + HD + r0 + i % RPC];
+    if (tid < r) {
+        m.rdec[tid] = rec[tid * REC + 2 * HD];
+        m.rbeta[tid] = rec[tid * REC + 2 * HD + 1];
+    }
+    cluster.sync();  // conv slices and alpha/beta partials visible to the cluster
+    // 4. the head's q and k from their owners; alpha / beta over the slices in rank order
+    for (int i = tid; i < N * HD; i += 256) {
+        const int t = i / HD, c = i % HD, src = c / RPC, ci = c % RPC;
+        ChunkSmem<HD> &o = *cluster.map_shared_rank(&m, src);
+        m.xq[t][c] = o.cq[t][ci];
+        m.xk[t][c] = o.ck[t][ci];
+    }
+    for (int i = tid; i < 3 * N; i += 256) {
+        const int which = i / N, t = i % N;
+        float v = 0.f;
+        for (int q = 0; q < kSsmSplit; q++) v += cluster.map_shared_rank(&m, q)->ab_part[which][t];
+        m.ab[which][t] = v;
+    }
+    __syncthreads();
+    if (a.in_norm)
+        for (int t = tid; t < N; t += 256) {
+            const float iv = 1.0f / sqrtf(m.ab[2][t] / (float)a.d + a.eps);
+            m.ab[0][t] *= iv;
+            m.ab[1][t] *= iv;
+        }
+    __syncthreads();
+    // 5. L2 norms of q, k and the f64 gates, one warp per token
+    for (int t = warp; t < N; t += 8) {
+        float qs = 0.f, ks = 0.f;
+        for (int i = lane; i < HD; i += 32) {
+            qs += m.xq[t][i] * m.xq[t][i];
+            ks += m.xk[t][i] * m.xk[t][i];
+        }
+        qs = warp_sum(qs);
+        ks = warp_sum(ks);
+        const float scale = 1.0f / sqrtf((float)HD);
+        const float qn = 1.0f / (sqrtf(qs) + 1e-6f) * scale, kn = 1.0f / (sqrtf(ks) + 1e-6f);
+        __syncwarp();
+        for (int i = lane; i < HD; i += 32) {
+            m.xq[t][i] *= qn;
+            m.xk[t][i] *= kn;
+        }
+        if (lane == 0) {
+            double av = (double)m.ab[0][t] + (double)a.dt_bias[h];
+            av = av < -20.0 ? -20.0 : (av > 20.0 ? 20.0 : av);
+            const double sp = log(1.0 + exp(av));
+            const float dec = (float)((double)a.ssm_a[h] * sp);
+            m.ndec[t] = expf(dec);
+            double bv = (double)m.ab[1][t];
+            bv = bv < -20.0 ? -20.0 : (bv > 20.0 ? 20.0 : bv);
+            m.nbeta[t] = (float)(1.0 / (1.0 + exp(-bv)));
+        }
+    }
+    __syncthreads();
+    // 6. committed conv history: the last K-1 inputs of history + replayed + new tokens
+    //    (every owned channel's window was read in step 1, before the cluster barrier)
+    for (int lc = tid; lc < 3 * RPC; lc += 256) {
+        const int part = lc / RPC, i = lc % RPC;
+        const int ch = part * qk + h * HD + r0 + i;
+        float nh[3];
+#pragma unroll
+        for (int j = 0; j < 3; j++) nh[j] = j < K - 1 ? *win(r + N + j, ch) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            if (j < K - 1) a.hist[(int64_t)j * C + ch] = nh[j];
+    }
+    // 7. the state rows through the replayed and the new tokens, committed at the end
+    const int row = tid / TPR, lc = tid % TPR;
+    float *Sp = a.S + ((int64_t)h * HD + r0 + row) * HD + lc;
+    float st[CPT];
+#pragma unroll
+    for (int e = 0; e < CPT; e++) st[e] = Sp[TPR * e];
+    auto update = [&](const float *kv, float dec, float beta, float vrow) {
+        float sk = 0.f;
+#pragma unroll
+        for (int e = 0; e < CPT; e++) {
+            st[e] *= dec;
+            sk += st[e] * kv[lc + TPR * e];
+        }
+#pragma unroll
+        for (int o = 1; o < TPR; o <<= 1) sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        const float dd = beta * (vrow - sk);
+#pragma unroll
+        for (int e = 0; e < CPT; e++) st[e] += dd * kv[lc + TPR * e];
+    };
+    for (int j = 0; j < r; j++) update(m.rk[j], m.rdec[j], m.rbeta[j], m.rv[j][row]);
+    for (int t = 0; t < N; t++) {
+        update(m.xk[t], m.ndec[t], m.nbeta[t], m.cv[t][row]);
+        float y = 0.f;
+#pragma unroll
+        for (int e = 0; e < CPT; e++) y += st[e] * m.xq[t][lc + TPR * e];
+#pragma unroll
+        for (int o = 1; o < TPR; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+        if (lc == 0) m.ys[t][row] = y;
+    }
+#pragma unroll
+    for (int e = 0; e < CPT; e++) Sp[TPR * e] = st[e];
+    __syncthreads();
+    // 8. per-head RMSNorm (partial sums of squares over the cluster in rank order), gate
+    for (int t = warp; t < N; t += 8) {
+        const float v = lane < RPC ? m.ys[t][lane] * m.ys[t][lane] : 0.f;
+        const float t2 = warp_sum(v);
+        if (lane == 0) m.ssq[t] = t2;
+    }
+    cluster.sync();
+    for (int i = tid; i < N * RPC; i += 256) {
+        const int t = i / RPC, c = i % RPC;
+        float ss = 0.f;
+        for (int q = 0; q < kSsmSplit; q++) ss += cluster.map_shared_rank(&m, q)->ssq[t];
+        const float scale = 1.0f / sqrtf(ss / (float)HD + a.eps);
+        const float z = a.proj[(int64_t)t * a.ldp + C + h * HD + r0 + c];
+        const float yn = m.ys[t][c] * scale * a.norm_w[r0 + c];
+        a.y[(int64_t)t * a.ldy + h * HD + r0 + c] = yn * z * (1.0f / (1.0f + expf(-z)));
+    }
+    cluster.sync();  // peers may still read this CTA's shared memory
+}
+
+cudaError_t ssm_chunk(const SsmArgs &a, int head_dim, cudaStream_t s) {
+    if (a.N < 1 || a.N > kChunkMax || a.K < 1 || a.K > 4) return cudaErrorInvalidValue;
+    const dim3 grid(kSsmSplit, a.H, 1);
+    if (head_dim == 128) {
+        static DeviceFlags attr;
+        if (!attr.test()) {
+            cudaError_t e = cudaFuncSetAttribute(ssm_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)sizeof(ChunkSmem<128>));
+            if (e != cudaSuccess) return e;
+            attr.set();
+        }
+        return launch_k(ssm_chunk_kernel<128>, grid, dim3(256), sizeof(ChunkSmem<128>), s, a);
+    }
+    if (head_dim == 64) {
+        static DeviceFlags attr;
+        if (!attr.test()) {
+            cudaError_t e = cudaFuncSetAttribute(ssm_chunk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)sizeof(ChunkSmem<64>));
+            if (e != cudaSuccess) return e;
+            attr.set();
+        }
+        return launch_k(ssm_chunk_kernel<64>, grid, dim3(256), sizeof(ChunkSmem<64>), s, a);
+    }
+    return cudaErrorInvalidValue;
+}
+
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4 || batch < 1) return cudaErrorInvalidValue;
     if (batch > 1) {
@@ -1201,7 +1448,7 @@ __global__ void commit_kernel(EngineScalars *sc, const int32_t *acc_dev, const i
     if (threadIdx.x == 0) {
         const int acc = all ? n - 1 : *acc_dev;
         acc_s = acc;
-        sc->a_prev = acc;
+        sc->a_prev = all == 2 ? -1 : acc;  // 2: committed by the layers themselves (prefill chunks)
         sc->pos += acc + 1;
         if (!all) {
             for (int i = 0; i <= acc; i++)
@@ -1216,10 +1463,19 @@ __global__ void commit_kernel(EngineScalars *sc, const int32_t *acc_dev, const i
         for (int i = threadIdx.x; i < d; i += blockDim.x) mtp_h[i] = hid[(int64_t)acc_s * d + i];
 }
 
-void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,
+void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, int all, const float *hid,
             float *mtp_h, int d, int32_t *log, int log_cap, int batch, cudaStream_t s) {
-    launch_k(commit_kernel, dim3(batch), dim3(256), 0, s, sc, acc, out_tok, n, all ? 1 : 0, hid, mtp_h, d, log,
-             log_cap);
+    launch_k(commit_kernel, dim3(batch), dim3(256), 0, s, sc, acc, out_tok, n, all, hid, mtp_h, d, log, log_cap);
+}
+
+// positions of the sub-chunks of a prefill chunk: dst[i] = pos + step * i
+__global__ void chunk_pos_kernel(int32_t *dst, const EngineScalars *sc, int count, int step) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x < count) dst[threadIdx.x] = sc->pos + step * (int)threadIdx.x;
+}
+void chunk_positions(int32_t *dst, const EngineScalars *sc, int count, int step, cudaStream_t s) {
+    launch_k(chunk_pos_kernel, dim3(1), dim3(32), 0, s, dst, sc, count, step);
 }
 
 // copy a device scalar token into a slot of the verify token vector

@@ -81,15 +81,23 @@ void norm_add(const float *y, const float *w, float *x, int cols, int n, float e
 // l = tanh(l / cap) cap in place (final logit softcap)
 void softcap(float *l, int64_t n, float cap, cudaStream_t s);
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s);
+// a prefill chunk of a.N <= 64 tokens of one request, committed at once (no
+// replay record; the caller's commit must leave nothing to replay)
+cudaError_t ssm_chunk(const SsmArgs &a, int head_dim, cudaStream_t s);
+constexpr int kPrefillChunk = 64;
 cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s);
 // key slices of a split-KV call of N tokens per request, and the scratch
 // (floats) that every call on a state of `batch` requests and max_ctx fits in
 int attn_splits(int nh, int nkv, int N, int batch, int max_ctx);
 int64_t attn_part_floats(int nh, int nkv, int hd, int batch, int max_ctx);
 // per request b (grid of `batch` CTAs): sc + b, acc + b, out_tok + b * n,
-// hid + b * n * d, mtp_h + b * d, log + b * log_cap
-void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, bool all, const float *hid,
+// hid + b * n * d, mtp_h + b * d, log + b * log_cap.  all: 0 commit acc + 1
+// verify tokens; 1 commit all n (prefill; the SSM layers replay them next
+// call); 2 commit all n that the layers already committed (prefill chunks)
+void commit(EngineScalars *sc, const int32_t *acc, const int32_t *out_tok, int n, int all, const float *hid,
             float *mtp_h, int d, int32_t *log, int log_cap, int batch, cudaStream_t s);
+// dst[i] = sc->pos + step * i for i < count (<= 32)
+void chunk_positions(int32_t *dst, const EngineScalars *sc, int count, int step, cudaStream_t s);
 void set_token(int32_t *dst, const int32_t *src, cudaStream_t s);
 
 }  // namespace ifr
