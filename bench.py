@@ -546,6 +546,12 @@ def run_spec(args):
         extras["prefill_2048"] = prefill_extra(model, prompt_len=2048)
         extras["config3_accept"] = accept_extra(pkg, local, reps=max(3, args.steps // 2))
         extras["config2_sweep"] = sweep_extra(pkg, local)
+    # the configs that shard, at this N: config 4 (64 requests split over the
+    # ranks) always, config 5 (tensor parallel) from 2 GPUs on; a few steps each
+    if not args.no_extras and not args.no_shard_legs:
+        extras["config4_batch"] = batch_leg(args, pkg, ws, rank, local, 5, 3)
+        if ws > 1:
+            extras["config5_tp"] = tp_leg(args, pkg, ws, rank, local, 5, 3)
     if rank == 0:
         peak, peak_kind = measured_peaks()
         step_bytes = spec_bytes_per_step(info, G)
@@ -602,21 +608,29 @@ def prefill_extra(model, prompt_len=2048, reps=2):
     from inferno_b200 import synth
     from inferno_b200.engine import State
     prompt = synth.prompt(model.info.vocab, prompt_len, 77)
-    times = []
-    for i in range(reps + 1):
-        st = State(model, prompt_len + 64)
-        model.ctx.sync()
-        t0 = time.perf_counter()
-        st.prefill(prompt)
-        dt = time.perf_counter() - t0
-        if i:
-            times.append(dt)
-        st.free()
-    ms = float(np.median(times)) * 1e3
+
+    def timed(dense):
+        model.ctx.set_prefill_dense(dense)
+        times = []
+        for i in range(reps + 1):
+            st = State(model, prompt_len + 64)
+            model.ctx.sync()
+            t0 = time.perf_counter()
+            st.prefill(prompt)
+            dt = time.perf_counter() - t0
+            if i:
+                times.append(dt)
+            st.free()
+        model.ctx.set_prefill_dense(False)
+        return float(np.median(times)) * 1e3
+
+    ms, ms_d = timed(False), timed(True)
     return {"workload": f"ifr_prefill of one config-1 request, {prompt_len}-token seeded prompt",
             "chunk_tokens": 64, "ms": round(ms, 2), "tokens_per_s": round(prompt_len / (ms * 1e-3), 1),
-            "calls_timed": reps,
-            "path": "projections on the dense tcgen05 GEMM (64 columns), GatedDeltaNet chunk scan, attention in 8-token sub-calls"}
+            "path": "default (exact): projections on the exact small-N kernel in passes of 8 columns over each 64-token chunk, GatedDeltaNet chunk scan, attention in 8-token sub-calls",
+            "dense_ms": round(ms_d, 2), "dense_tokens_per_s": round(prompt_len / (ms_d * 1e-3), 1),
+            "dense_path": "ifr_ctx_set_prefill_dense: the chunk's projections on the tcgen05 GEMM (fp16 operands)",
+            "calls_timed": reps}
 
 
 def accept_extra(pkg, device, reps=5):
@@ -706,18 +720,31 @@ BATCH_PRESET, BATCH_SEED = "9b", 0
 
 
 def run_batch(args):
-    """BASELINE config 4: the ~9B-shape hybrid, `--batch` independent requests
-    (64) split evenly over the ranks, each with a seeded prompt of `--prompt`
-    tokens (2048); one step = MTP draft of gamma tokens for every request +
-    one verify of batch x (gamma+1) columns (dense tcgen05 GEMMs) + greedy
-    acceptance + rollback, replayed as a CUDA graph."""
-    import ctypes
+    """BASELINE config 4 as its own line (`--workload batch`)"""
     import torch
     import __graft_entry__ as ge
     ws, rank, local = dist_init()
     torch.cuda.set_device(local)
     pkg = ge.load_package()
     pkg.load()
+    line = batch_leg(args, pkg, ws, rank, local, args.steps, args.warmup)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def batch_leg(args, pkg, ws, rank, local, steps, warmup):
+    """BASELINE config 4: the ~9B-shape hybrid, `--batch` independent requests
+    (64) split evenly over the ranks, each with a seeded prompt of `--prompt`
+    tokens (2048); one step = MTP draft of gamma tokens for every request +
+    one verify of batch x (gamma+1) columns (dense tcgen05 GEMMs) + greedy
+    acceptance + rollback, replayed as a CUDA graph.  Every rank runs it (no
+    collective on the data path); returns the line on rank 0."""
+    import ctypes
+    import torch
     from inferno_b200 import synth
     from inferno_b200.engine import Model, State
     G = args.gamma
@@ -725,13 +752,16 @@ def run_batch(args):
     B = len(mine)
     ctx = pkg.Context(local, torch_stream=False)
     t_load = time.time()
+    if rank == 0:
+        synth.cached(BATCH_PRESET, BATCH_SEED)
+    barrier(ws)
     path = synth.cached(BATCH_PRESET, BATCH_SEED)
     model = Model(ctx, path)
     info = model.info
     t_load = time.time() - t_load
     P = args.prompt
     prompts = np.stack([synth.prompt(info.vocab, P, BATCH_SEED + 1000 + r) for r in mine])
-    max_ctx = P + (args.warmup + args.steps + 4) * (G + 1) + 16
+    max_ctx = P + (warmup + steps + 4) * (G + 1) + 16
     st = State(model, max_ctx, batch=B)
     ctx.sync()
     t0 = time.time()
@@ -743,7 +773,7 @@ def run_batch(args):
     sp = ctypes.c_void_p()
     pkg.check(pkg.load().ifr_ctx_get_stream(ctx.handle, ctypes.byref(sp)))
     stream = torch.cuda.ExternalStream(sp.value)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         st.launch()
     ctx.sync()
     n0 = sum(len(st.read(b)[0]) for b in range(B))
@@ -751,7 +781,7 @@ def run_batch(args):
     barrier(ws)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             st.launch()
         e1.record(stream)
         e1.synchronize()
@@ -766,10 +796,11 @@ def run_batch(args):
     # end to end through the public API with host buffers: per step ifr_spec_step
     # + D2H of every request's emitted tokens
     ctx.sync()
+    barrier(ws)
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ee0.record(stream)
     d2h = 0
-    k2 = max(1, min(args.steps, 4))
+    k2 = max(1, min(steps, 4))
     for _ in range(k2):
         st.spec_step(G)
         for b in range(B):
@@ -777,8 +808,9 @@ def run_batch(args):
     ee1.record(stream)
     ee1.synchronize()
     e2e_ms = max_over_ranks(ee0.elapsed_time(ee1), ws)
+    line = None
     if rank == 0:
-        d, hd = info.hidden, info.head_dim
+        hd = info.head_dim
         kv_bytes = 2 * info.n_attention_layers * info.n_kv_head * hd * 4 * (P + G + 1) * args.batch // ws
         flops = 2.0 * verify_weight_count(info) * B * (G + 1)
         line = {
@@ -786,9 +818,9 @@ def run_batch(args):
             "value": round(emitted_all / (ms_max * 1e-3), 2),
             "unit": "tokens/s",
             "n_gpus": ws,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms_max / args.steps, 4),
+            "steps": steps,
+            "warmup": warmup,
+            "ms_per_step": round(ms_max / steps, 4),
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
@@ -802,23 +834,23 @@ def run_batch(args):
                        "l2": "inputs larger than L2: %.1f GB of weights + %.1f GB of KV per step per GPU" % (info.weight_bytes / 1e9, kv_bytes / 1e9),
                        "parallelism": f"requests split over {ws} GPU(s), weights replicated, no collective",
                        "graph": "one CUDA graph per spec step"},
+            "per_gpu_tokens_per_s": round(emitted_all / ws / (ms_max * 1e-3), 2),
             "roofline": {"bound": "tensor", "kernel": "whole verify step (dense GEMMs dominate)",
-                         "achieved": round(flops / (ms_max / args.steps * 1e-3) / 1e12, 1),
+                         "achieved": round(flops / (ms_max / steps * 1e-3) / 1e12, 1),
                          "peak": measured_peaks_tensor(), "unit": "TFLOP/s", "traffic": None,
                          "note": "verify weights x columns x 2 flop per step, over the step time"},
             "e2e": {"value": round(k2 * B * ws / (e2e_ms * 1e-3), 2), "unit": "tokens/s (lower bound: 1 token per request per step)",
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": int(d2h / k2)},
-            "gpu_launches": int(launches_per_step * args.steps),
+            "gpu_launches": int(launches_per_step * steps),
             "clocks": clk.summary(),
             "cpu_baseline": None,
         }
         line["roofline"]["frac"] = round(line["roofline"]["achieved"] / line["roofline"]["peak"], 4)
-        print(json.dumps(line), flush=True)
     barrier(ws)
-    del st
-    if ws > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    st.free()
+    model.free()
+    ctx.close()
+    return line
 
 
 def verify_weight_count(info):
@@ -837,20 +869,33 @@ TP_PRESET, TP_DRAFT, TP_SEED = "gemma", "gemma_draft", 0
 
 
 def run_tp(args):
-    """BASELINE config 5: the Gemma4-shape target (hidden 5376, 62 layers,
-    32 q / 16 kv x 128, FFN 21504, vocab 262144, Q4_K) tensor-parallel over all
-    ranks (NCCL all-reduce of the residual after the row-parallel projections,
-    vocab-parallel lm_head), the Q8_0 draft model (hidden 1152, 26 layers)
-    replicated on every rank; one request with a seeded prompt of `--prompt`
-    tokens (4096); one step = gamma (5) draft tokens + one verify of gamma+1
-    columns + greedy acceptance, as a CUDA graph."""
-    import ctypes
+    """BASELINE config 5 as its own line (`--workload tp`)"""
     import torch
     import __graft_entry__ as ge
     ws, rank, local = dist_init()
     torch.cuda.set_device(local)
     pkg = ge.load_package()
     pkg.load()
+    line = tp_leg(args, pkg, ws, rank, local, args.steps, args.warmup)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def tp_leg(args, pkg, ws, rank, local, steps, warmup):
+    """BASELINE config 5: the Gemma4-shape target (hidden 5376, 62 layers,
+    32 q / 16 kv x 128, FFN 21504, vocab 262144, Q4_K, Gemma4 blocks)
+    tensor-parallel over all ranks (NCCL all-reduce of each sub-block's output
+    after the row-parallel projections, vocab-parallel lm_head), the Q8_0
+    draft model (hidden 1152, 26 layers) replicated on every rank; one request
+    with a seeded prompt of 4096 tokens; one step = 5 draft tokens + one
+    verify of 6 columns + greedy acceptance, as a CUDA graph.  Returns the
+    line on rank 0."""
+    import ctypes
+    import torch
     from inferno_b200 import synth
     from inferno_b200.engine import Comm, Model, State
     G = args.gamma if args.gamma != 4 else 5  # config 5: draft length 5
@@ -875,7 +920,7 @@ def run_tp(args):
     info = target.info
     t_load = time.time() - t_load
     prompt = synth.prompt(info.vocab, P, TP_SEED)
-    max_ctx = P + (args.warmup + 2 * args.steps + 8) * (G + 1) + 16
+    max_ctx = P + (warmup + 2 * steps + 8) * (G + 1) + 16
     ts, ds = State(target, max_ctx), State(draft, max_ctx)
     ctx.sync()
     t0 = time.time()
@@ -888,7 +933,7 @@ def run_tp(args):
     sp = ctypes.c_void_p()
     pkg.check(pkg.load().ifr_ctx_get_stream(ctx.handle, ctypes.byref(sp)))
     stream = torch.cuda.ExternalStream(sp.value)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         ts.launch()
     ctx.sync()
     n0 = len(ts.read()[0])
@@ -896,7 +941,7 @@ def run_tp(args):
     barrier(ws)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             ts.launch()
         e1.record(stream)
         e1.synchronize()
@@ -909,25 +954,40 @@ def run_tp(args):
     barrier(ws)
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ee0.record(stream)
-    d2h, k2 = 0, max(1, min(args.steps, 8))
+    d2h, k2 = 0, max(1, min(steps, 8))
     for _ in range(k2):
         ts.spec_step_draft(ds, G)
         d2h += ts.read()[0].nbytes
     ee1.record(stream)
     ee1.synchronize()
     e2e_ms = max_over_ranks(ee0.elapsed_time(ee1), ws)
+    # the all-reduce share: one eager step with the target's launches timed
+    # per category (CUDA events on the context stream); the draft state's
+    # launches are not categorised
+    ts.profile(True)
     barrier(ws)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    ts.spec_step_draft(ds, G)
+    p1.record(stream)
+    p1.synchronize()
+    prof, _ = ts.profile_read()
+    ts.profile(False)
+    prof_step = p0.elapsed_time(p1)
+    comm_ms = max_over_ranks(prof["allreduce"]["ms"], ws)
+    barrier(ws)
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         shard_bytes = info.weight_bytes  # this rank's target shard (decoder layers + lm_head rows)
-        step_ms = ms_max / args.steps
+        step_ms = ms_max / steps
         line = {
             "metric": METRIC,
             "value": round(emitted / (ms_max * 1e-3), 2),
             "unit": "tokens/s",
             "n_gpus": ws,
-            "steps": args.steps,
-            "warmup": args.warmup,
+            "steps": steps,
+            "warmup": warmup,
             "ms_per_step": round(step_ms, 4),
             "higher_is_better": True,
             "scaling": "strong",
@@ -942,27 +1002,28 @@ def run_tp(args):
                        "l2": "inputs larger than L2: %.2f GB of target weights per rank per verify" % (shard_bytes / 1e9),
                        "parallelism": f"tensor parallel x{ws}: NCCL sum all-reduce after attention-output and down projections, vocab-parallel lm_head",
                        "graph": "one CUDA graph per spec step"},
+            "allreduce": {"ms_per_step": round(comm_ms, 4), "share_of_eager_step": round(comm_ms / prof_step, 4),
+                          "eager_step_ms": round(prof_step, 3), "per_step": 2 * info.n_layers,
+                          "note": "one eager step, CUDA events around each NCCL all-reduce of the target (max over ranks)"},
             "roofline": {"bound": "hbm", "kernel": "whole spec step per rank: the target shard's weights once per verify",
                          "achieved": round(shard_bytes / (step_ms * 1e-3) / 1e9, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(shard_bytes / (step_ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
                          "note": "target shard bytes per step / step time (the draft's 26 small forwards and the all-reduces are inside the step)"},
-            "e2e": {"value": round(k2 * (emitted / args.steps) / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+            "e2e": {"value": round(k2 * (emitted / steps) / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": int(d2h / k2)},
             "gpu_launches": None,
             "clocks": clk.summary(),
             "cpu_baseline": None,
         }
-        print(json.dumps(line), flush=True)
     barrier(ws)
     ts.free()
     ds.free()
     target.free()
     draft.free()
     comm.free()
-    if ws > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    ctx.close()
+    return line
 
 
 def measured_peaks_tensor():
@@ -1119,7 +1180,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048, help="prompt tokens per request (batch workload)")
     ap.add_argument("--gamma", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-extras", action="store_true", help="spec workload: skip the config-2/3 extra keys")
+    ap.add_argument("--no-extras", action="store_true", help="spec workload: skip every extra key")
+    ap.add_argument("--no-shard-legs", action="store_true", help="spec workload: skip the config-4/5 legs")
     ap.add_argument("--act", type=int, default=None, choices=[0, 1],
                     help="K-quant GEMV activations: 0 = exact f32 (default of the model workloads), "
                          "1 = Q8_K (the reference's kernels; default of the sweep)")

@@ -84,8 +84,15 @@ int ifr_ctx_set_activation(ifr_ctx *ctx, int mode);
  * tokens) with the exact small-N kernel in passes of 8 columns while
  * n < ncols, and with the dense tensor-core path of ifr_qgemm_dense (fp16
  * operands, f32 accumulation) from ncols columns on.  Default
- * IFR_DENSE_MIN_COLS_DEFAULT; a state of one request never reaches it. */
+ * IFR_DENSE_MIN_COLS_DEFAULT; a state of one request reaches it only in the
+ * prefill chunks that ifr_ctx_set_prefill_dense allows. */
 int ifr_ctx_set_dense_min_cols(ifr_ctx *ctx, int ncols);
+/* one-request prefill (forward_cpu! over the prompt, src/ModelCPU.jl:1325)
+ * runs in chunks of 64 tokens; enable = 1 lets a chunk's projections take
+ * the dense tensor-core path (fp16 operands: logits within 1e-2 of the exact
+ * product instead of 1e-4), 0 (default) keeps them exact.  No counterpart in
+ * the reference (its prefill is the f32 token loop). */
+int ifr_ctx_set_prefill_dense(ifr_ctx *ctx, int enable);
 /* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
  * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);

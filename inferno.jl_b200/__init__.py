@@ -112,6 +112,10 @@ class Context:
         """engine projections of >= ncols columns use the dense tensor-core path"""
         check(load().ifr_ctx_set_dense_min_cols(self.handle, int(ncols)))
 
+    def set_prefill_dense(self, enable=True):
+        """let one-request prefill chunks use the dense tensor-core path"""
+        check(load().ifr_ctx_set_prefill_dense(self.handle, 1 if enable else 0))
+
     def set_stream(self, stream):
         check(load().ifr_ctx_set_stream(self.handle, ctypes.c_void_p(stream.cuda_stream)))
 

@@ -36,6 +36,7 @@ SIGNATURES = {
     "ifr_dequant": (_i, [_vp, _vp, _vp]),
     "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
     "ifr_ctx_set_dense_min_cols": (_i, [_vp, _i]),
+    "ifr_ctx_set_prefill_dense": (_i, [_vp, _i]),
     "ifr_state_read_request": (_i, [_vp, _i, _vp, _i, _vp, _vp]),
     "ifr_prefill_batch": (_i, [_vp, _vp, _i, _vp]),
     "ifr_state_create_batch": (_i, [_vp, _i, _i, ctypes.POINTER(_vp)]),

@@ -31,6 +31,7 @@ int ifr_cuda_fail(cudaError_t e, const char *what);
 int ifr_ctx_device(const ifr_ctx *c);
 int ifr_ctx_activation(const ifr_ctx *c);
 int ifr_ctx_dense_min(const ifr_ctx *c);
+int ifr_ctx_prefill_dense(const ifr_ctx *c);
 void ifr_ctx_retain(ifr_ctx *c);
 void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
@@ -517,6 +518,7 @@ struct ifr_state {
     int64_t dense_bytes = 0;
     int last_n = 0;
     int pending = -1;                   // gamma of a verify awaiting ifr_rollback, else -1
+    bool prefill_chunk = false;         // a one-request prefill chunk is being enqueued
     // kernel launches enqueued (for the benchmark's launch count)
     int64_t launches = 0;
     // optional per-category CUDA-event timing of the launches
@@ -550,7 +552,7 @@ int dalloc(ifr_state *s, T **p, size_t n) {
 }
 
 // categories of timed launches (ifr_state_profile_read)
-enum { CAT_LM_HEAD = 0, CAT_DRAFT_LM_HEAD, CAT_LAYER_GEMV, CAT_DRAFT_GEMV, CAT_SSM, CAT_ATTN, CAT_NCAT = 8 };
+enum { CAT_LM_HEAD = 0, CAT_DRAFT_LM_HEAD, CAT_LAYER_GEMV, CAT_DRAFT_GEMV, CAT_SSM, CAT_ATTN, CAT_COMM, CAT_NCAT = 8 };
 
 struct ProfScope {
     ifr_state *s;
@@ -575,6 +577,14 @@ struct ProfScope {
 
 int64_t proj_bytes(const Proj &p);
 
+// tensor parallelism: the sum all-reduce of n floats over the ranks (timed as
+// CAT_COMM when profiling); no-op for one rank
+int allreduce(ifr_state *s, float *x, size_t n, cudaStream_t st) {
+    if (!s->m->comm) return IFR_OK;
+    ProfScope ps(s, CAT_COMM, (int64_t)n * 4, st);
+    return comm_allreduce_sum(s->m->comm, x, n, st);
+}
+
 // Y (+)= W X over n columns: the exact small-N kernel in passes of 8 columns,
 // or the dense tensor-core kernel once n reaches the context's threshold
 int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, bool accumulate, cudaStream_t st,
@@ -584,7 +594,9 @@ int gemv(ifr_state *s, int cat, const Proj &p, const float *X, int n, float *Y, 
     const int64_t ldy = xf.ep ? p.rows / 2 : p.rows;
     ifr::XForm f = xf;
     f.act = ifr_ctx_activation(s->m->ctx);
-    const bool dense = n >= ifr_ctx_dense_min(s->m->ctx) && s->dense;
+    // one request: dense only for the prefill chunks the context allows
+    const bool dense = n >= ifr_ctx_dense_min(s->m->ctx) && s->dense &&
+                       (s->B > 1 || (s->prefill_chunk && ifr_ctx_prefill_dense(s->m->ctx)));
     for (auto &q : p.parts) {
         if (dense) {
             ECHECK(ifr::qgemm_dense(q, X, n, Y + r0, accumulate, ldy, st, f, s->dense, s->dense_bytes), "qgemm_dense");
@@ -689,14 +701,14 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         if ((rc = attn_call(s, a, n, B, st))) return rc;
         // row-parallel projections: every rank's partial, summed over the ranks
         if ((rc = gemv(s, gcat, L.out, s->y, nc, s->xn, false, st))) return rc;
-        if ((rc = comm_allreduce_sum(m->comm, s->xn, (size_t)nc * d, st))) return rc;
+        if ((rc = allreduce(s, s->xn, (size_t)nc * d, st))) return rc;
         ifr::norm_add(s->xn, L.post_norm, s->x, nc, d, c.rms_eps, nullptr, st);
         ifr::XForm glu = in_norm;
         glu.w = L.ffn_norm;
         glu.ep = 2;  // gelu_tanh(gate) * up
         if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->hmid, false, st, glu))) return rc;
         if ((rc = gemv(s, gcat, L.down, s->hmid, nc, s->xn, false, st))) return rc;
-        if ((rc = comm_allreduce_sum(m->comm, s->xn, (size_t)nc * d, st))) return rc;
+        if ((rc = allreduce(s, s->xn, (size_t)nc * d, st))) return rc;
         ifr::norm_add(s->xn, L.post_ffw_norm, s->x, nc, d, c.rms_eps, L.layer_scalar, st);
         s->launches += 2;
         return IFR_OK;
@@ -767,7 +779,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     // row-parallel projections: rank 0 adds its partial to the residual, the
     // others write theirs, and one sum all-reduce leaves x + sum on every rank
     if ((rc = gemv(s, gcat, L.out, s->y, nc, s->x, m->tp_rank == 0, st))) return rc;
-    if ((rc = comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st))) return rc;
+    if ((rc = allreduce(s, s->x, (size_t)nc * d, st))) return rc;
     ifr::XForm post_norm = in_norm;
     post_norm.w = L.post_norm;
     if (L.gate_up.glu) {
@@ -776,7 +788,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         glu.ep = 1;
         if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->hmid, false, st, glu))) return rc;
         if ((rc = gemv(s, gcat, L.down, s->hmid, nc, s->x, m->tp_rank == 0, st))) return rc;
-        return comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st);
+        return allreduce(s, s->x, (size_t)nc * d, st);
     }
     if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->gu, false, st, post_norm))) return rc;
     // silu(gate) * up formed while the down GEMV reads [gate | up]
@@ -784,7 +796,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     swiglu.kind = 2;
     swiglu.ldx = 2 * (int64_t)m->ffn;
     if ((rc = gemv(s, gcat, L.down, s->gu, nc, s->x, m->tp_rank == 0, st, swiglu))) return rc;
-    return comm_allreduce_sum(m->comm, s->x, (size_t)nc * d, st);
+    return allreduce(s, s->x, (size_t)nc * d, st);
 }
 
 // embedding rows of the n verify tokens of each of B requests (row b * n + t):
@@ -1468,7 +1480,9 @@ int ifr_prefill_batch(ifr_state *s, const int32_t *tokens, int n, int32_t *first
                                                    sizeof(int32_t) * n, sizeof(int32_t) * k, B,
                                                    cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) { rc = ifr_cuda_fail(e, "prompt chunk"); break; }
+        s->prefill_chunk = k > kNMax;
         rc = target_forward(s, k, last, false, st);
+        s->prefill_chunk = false;
         if (!rc)
             ifr::commit(s->sc, s->acc, s->outtok, k, k > kNMax ? 2 : 1, nullptr, nullptr, c.hidden, s->log,
                         s->log_cap, B, st);

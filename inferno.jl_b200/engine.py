@@ -166,7 +166,7 @@ class State:
     def profile(self, enable=True):
         check(load().ifr_state_profile(self.handle, 1 if enable else 0))
 
-    CATEGORIES = ("lm_head", "draft_lm_head", "layer_gemv", "draft_gemv", "ssm", "attention")
+    CATEGORIES = ("lm_head", "draft_lm_head", "layer_gemv", "draft_gemv", "ssm", "attention", "allreduce")
 
     def profile_read(self):
         ms = (ctypes.c_double * 8)()

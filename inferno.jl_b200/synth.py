@@ -35,7 +35,7 @@ PRESETS = {
     "mini": dict(hidden=256, n_layers=4, n_head=4, n_kv_head=2, head_dim=64, rope_frac=0.25,
                  ffn=512, vocab=4096, ssm_heads=4, ssm_head_dim=64, conv_kernel=4,
                  attn_every=4, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=True,
-                 context=1024),
+                 context=4096),
     # config 5: the Gemma4-shape target (hidden 5376, 62 layers, 32 q / 16 kv x
     # 128, FFN 21504, vocab 262144, Q4_K) and its Q8_0 draft model (hidden
     # 1152, 26 layers), both with Gemma4 blocks (architecture "gemma4"): five

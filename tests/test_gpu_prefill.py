@@ -7,9 +7,11 @@ positions.  Checked against the oracle's token-by-token forward: the first
 token, the final hidden state and the logits after the prompt, and the spec
 steps that continue from the committed state.
 
-  * exact path (every projection on the exact small-N kernel): 1e-4;
-  * default path (the chunk's projections on the dense tcgen05 GEMM, fp16
-    operands): 1e-2, the north star's bound for reduced-precision accumulation.
+  * default, exact path (every projection on the exact small-N kernel, in
+    passes of 8 columns over the chunk): 1e-4;
+  * ifr_ctx_set_prefill_dense (the chunk's projections on the dense tcgen05
+    GEMM, fp16 operands): 1e-2, the north star's bound for reduced-precision
+    accumulation.
 """
 import numpy as np
 import pytest
@@ -33,8 +35,8 @@ def _check_prefill(O, ctx, path, P, max_ctx, seed, exact, steps=2, G=4):
     model = Model(ctx, path)
     om = O.OracleModel(gguf.GGUFFile(path), max_ctx)
     prompt = synth.prompt(model.info.vocab, P, seed=seed)
-    if exact:
-        ctx.set_dense_min_cols(10**6)
+    if not exact:
+        ctx.set_prefill_dense(True)
     try:
         st = State(model, max_ctx)
         first = int(st.prefill(prompt))
@@ -58,7 +60,7 @@ def _check_prefill(O, ctx, path, P, max_ctx, seed, exact, steps=2, G=4):
             assert [int(t) for t in st.read()[0]] == out
         st.free()
     finally:
-        ctx.set_dense_min_cols(24)
+        ctx.set_prefill_dense(False)
         om.close()
         model.free()
 
@@ -79,7 +81,7 @@ def test_chunked_prefill_config1_shapes_exact(O, ctx):
 
 
 def test_chunked_prefill_dense_path(O, ctx):
-    """the default path: the chunk's projections on the dense tcgen05 GEMM"""
+    """opt-in: the chunk's projections on the dense tcgen05 GEMM"""
     from inferno_b200 import synth
     _check_prefill(O, ctx, synth.cached("mini", seed=1), 1500, 1600, seed=3, exact=False)
 
