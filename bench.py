@@ -1132,7 +1132,8 @@ def run_profile(args):
         from inferno_b200 import synth
         from inferno_b200.engine import Model, State
         ctx = pkg.Context(0, torch_stream=False)
-        model = Model(ctx, synth.cached(BATCH_PRESET, BATCH_SEED))
+        # --preset 9b_narrow: config 4's widths with 4 layers (a small case for ncu)
+        model = Model(ctx, synth.cached(args.preset or BATCH_PRESET, BATCH_SEED))
         B, P = args.batch, args.prompt
         prompts = np.stack([synth.prompt(model.info.vocab, P, BATCH_SEED + 1000 + b) for b in range(B)])
         st = State(model, P + 64, batch=B)
@@ -1186,6 +1187,7 @@ def main():
                     help="K-quant GEMV activations: 0 = exact f32 (default of the model workloads), "
                          "1 = Q8_K (the reference's kernels; default of the sweep)")
     ap.add_argument("--profile", choices=["spec", "qgemv", "dense", "batch"], help="small case for ncu (no JSON line)")
+    ap.add_argument("--preset", default=None, help="--profile batch: model preset (default: the config-4 model)")
     ap.add_argument("--qtype", default="Q4_K")
     ap.add_argument("--shape", default="65536x4096")
     ap.add_argument("--ncols", type=int, default=5)

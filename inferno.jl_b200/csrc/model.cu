@@ -175,6 +175,13 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
         a.a_prev += b * a.b_prev;
     }
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
+    // this thread's state row slice, loaded first so that its memory latency
+    // overlaps the conv, the projections and the cluster exchange below
+    const int row = tid / TPR, lc = tid % TPR;
+    float *Sp = a.S + ((int64_t)h * HD + r0 + row) * HD + lc;
+    float s[CPT];
+#pragma unroll
+    for (int e = 0; e < CPT; e++) s[e] = Sp[TPR * e];
 
     // 1. conv of the owned channels over the window: committed history (K-1),
     //    replayed tokens (r), new tokens (N).  Element i of the window is read
@@ -322,12 +329,7 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
         }
     }
     for (int i = tid; i < N * RPC; i += 256) rec[(i / RPC) * REC + HD + r0 + i % RPC] = cv[i / RPC][i % RPC];
-    // 7. the state rows: row r0 + tid / TPR, columns lc + TPR * e
-    const int row = tid / TPR, lc = tid % TPR;
-    float *Sp = a.S + ((int64_t)h * HD + r0 + row) * HD + lc;
-    float s[CPT];
-#pragma unroll
-    for (int e = 0; e < CPT; e++) s[e] = Sp[TPR * e];
+    // 7. the state rows (loaded at the start): row r0 + tid / TPR, columns lc + TPR * e
     auto update = [&](const float *kv, float dec, float beta, float vrow) {
         float sk = 0.f;
 #pragma unroll
@@ -908,6 +910,14 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     const int nkeys = p0 + N;
     const int per = (nkeys + kAttnSplit - 1) / kAttnSplit;
     const int lo = min(nkeys, rank * per), hi = min(nkeys, lo + per);
+    {  // the slice's cached K and V rows toward L2 while q, k, v are normalised
+        const int hic = min(hi, p0), lines = HD * 4 / 128;
+        for (int i = tid; i < (hic > lo ? hic - lo : 0) * lines; i += 256) {
+            const int64_t o = ((int64_t)(lo + i / lines) * a.nkv + kvh) * HD + (i % lines) * 32;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.kc + o));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.vc + o));
+        }
+    }
     __shared__ __align__(16) float q[kMaxN][HD];
     __shared__ __align__(16) float kn[kMaxN][HD];
     __shared__ __align__(16) float vn[kMaxN][HD];
