@@ -574,6 +574,8 @@ def run_spec(args):
             "activations": ["exact f32", "Q8_K"][args.act],
             "tokens_emitted_timed": emitted, "accept_rate": round((emitted / args.steps - 1) / G, 4),
             "graph": "one CUDA graph per spec step",
+            "per_gpu_value": round(value / ws, 2),
+            "value_is": "the aggregate over all GPUs (tokens/s of the whole job); per_gpu_value = value / n_gpus",
             "step_hbm_GBps": round(step_bytes / (ms_max / args.steps * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "kernel": "qgemv: the 97 dequant-GEMV launches of one verify (24 layers x 4 + Q6_K lm_head), N=5, back to back",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
