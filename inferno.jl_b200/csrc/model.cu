@@ -1322,6 +1322,302 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
     }
 }
 
+// ---- split-KV attention on the tensor cores ----------------------------------
+// attn_part_kernel's work (same slices, rows, masks, online softmax and
+// partial states) with the two products on mma.sync m16n8k8 tf32: scores
+// S = Q K^T over a chunk of kGrpKeys keys (2 x 4 tiles of 16 x 8, one per
+// warp) and O += P V (2 x HD / 8 tiles, HD / 64 per warp, accumulators in
+// registers across chunks).  Each operand is split into tf32 hi + lo and
+// every product is formed as hi hi + hi lo + lo hi ("3xTF32"), which keeps
+// the f32 accuracy of the CUDA-core kernel (relative error ~2^-21 per
+// product).  The chunks of cached keys stream global -> shared with
+// cp.async into two buffers, the next chunk's copies in flight while the
+// current chunk is computed.  One CTA per SM (the two K/V buffers and the
+// split q take up to ~220 KB of shared memory).
+__device__ __forceinline__ uint32_t tf32_of(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t &hi, uint32_t &lo) {
+    hi = tf32_of(x);
+    lo = tf32_of(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// hi hi + hi lo + lo hi
+__device__ __forceinline__ void mma_3xtf32(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                           uint32_t bh0, uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+    mma_tf32(d, ah, bh0, bh1);
+    mma_tf32(d, ah, bl0, bl1);
+    mma_tf32(d, al, bh0, bh1);
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int NPEND>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
+
+template <int HD>
+struct MmaSmem {
+    static constexpr int QS = HD + 4, KS = HD + 4, VS = HD + 8, SS = kGrpKeys + 4;
+    // uint32/float words: qh[R][QS] | ql[R][QS] | Ks[2][kGrpKeys][KS] | Vs[2][kGrpKeys][VS] |
+    // kn[N][HD] | vn[N][HD] | sc[R][SS] | ms, ls, fs [R]; the f32 q rows are staged in Vs[1]
+    static __host__ __device__ int words(int R, int N) {
+        return 2 * R * QS + 2 * kGrpKeys * KS + 2 * kGrpKeys * VS + 2 * N * HD + R * SS + 3 * R;
+    }
+    static __host__ __device__ int bytes(int R, int N) { return 4 * words(R, N); }
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int hg, int S) {
+    using M = MmaSmem<HD>;
+    constexpr int QS = M::QS, KS = M::KS, VS = M::VS, SS = M::SS;
+    constexpr int NTW = HD / 64;  // P.V n-tiles per warp and m-tile
+    extern __shared__ __align__(16) float ms_buf[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g8 = lane >> 2, t4 = lane & 3;
+    const int N = a.N, ratio = a.nh / a.nkv, nrg = (ratio + hg - 1) / hg;
+    const int g = blockIdx.y / nrg, hb = blockIdx.y % nrg, h0 = g * ratio + hb * hg;
+    const int R = min(hg, ratio - hb * hg) * N;
+    const int sl = blockIdx.x, b = blockIdx.z;
+    uint32_t *qh = reinterpret_cast<uint32_t *>(ms_buf), *ql = qh + R * QS;
+    float *Ks = reinterpret_cast<float *>(ql + R * QS), *Vs = Ks + 2 * kGrpKeys * KS;
+    float *kn = Vs + 2 * kGrpKeys * VS, *vn = kn + N * HD, *sc = vn + N * HD;
+    float *ms = sc + R * SS, *ls = ms + R, *fs = ls + R;
+    float *q = Vs + kGrpKeys * VS;  // f32 q rows [R][HD], staged in the second V buffer
+    pdl_trigger();
+    pdl_wait();
+    a.qkv += (int64_t)b * N * a.ldq;
+    a.kc += b * a.b_kv;
+    a.vc += b * a.b_kv;
+    const int p0 = a.pos[(int64_t)b * a.b_pos];
+    const int nkeys = p0 + N, kps = attn_kps(nkeys, S);
+    const int lo = sl * kps, hi = min(nkeys, lo + kps);
+    if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
+    const RopeSpec rs = rope_spec(a);
+    const int qs = a.gated ? 2 : 1;
+    const int64_t rows_all = (int64_t)gridDim.z * a.nh * N, rid0 = ((int64_t)b * a.nh + h0) * N;
+    if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
+        float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
+        for (int i = tid; i < R * HD; i += 256) po[(rid0 + i / HD) * HD + i % HD] = 0.f;
+        if (tid < R) {
+            pm[rid0 + tid] = -CUDART_INF_F;
+            pl[rid0 + tid] = 0.f;
+        }
+        return;
+    }
+    // the cached keys of chunk c (j < p0) into buffer bf with cp.async; the new
+    // keys (j >= p0) and the zero V rows past the slice by plain stores
+    auto stage = [&](int c, int bf) {
+        const int j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
+        float *kb = Ks + bf * kGrpKeys * KS, *vb = Vs + bf * kGrpKeys * VS;
+        for (int i = tid; i < kGrpKeys * (HD / 4); i += 256) {
+            const int jj = i / (HD / 4), d = 4 * (i % (HD / 4)), j = j0 + jj;
+            if (jj < nj && j < p0) {
+                const int64_t o = ((int64_t)j * a.nkv + g) * HD + d;
+                cp_async16(kb + jj * KS + d, a.kc + o);
+                cp_async16(vb + jj * VS + d, a.vc + o);
+            } else if (jj < nj) {
+                *reinterpret_cast<float4 *>(kb + jj * KS + d) = *reinterpret_cast<const float4 *>(kn + (j - p0) * HD + d);
+                *reinterpret_cast<float4 *>(vb + jj * VS + d) = *reinterpret_cast<const float4 *>(vn + (j - p0) * HD + d);
+            } else {
+                *reinterpret_cast<float4 *>(kb + jj * KS + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4 *>(vb + jj * VS + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        cp_async_commit();
+    };
+    const int nch = (hi - lo + kGrpKeys - 1) / kGrpKeys;
+
+    // 1. the new k and v rows and the row group's q rows; RMSNorm + RoPE
+    for (int i = tid; i < N * HD; i += 256) {
+        const int t = i / HD, d = i % HD;
+        const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * qs * HD;
+        kn[i] = row[g * HD + d];
+        vn[i] = row[a.nkv * HD + g * HD + d];
+    }
+    for (int i = tid; i < R * HD; i += 256) {
+        const int r = i / HD, d = i % HD, hh = r / N, t = r % N;
+        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * qs * HD + d];
+    }
+    if (tid < R) {
+        ms[tid] = -CUDART_INF_F;
+        ls[tid] = 0.f;
+    }
+    __syncthreads();
+    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
+        if (rr >= R + N) {  // v rows: RMSNorm without weights (CommonOps.jl:43-53)
+            float *x = vn + (rr - R - N) * HD;
+            float ss = 0.f;
+            for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
+            ss = warp_sum(ss);
+            const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+            for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv;
+            continue;
+        }
+        const bool isq = rr < R;
+        float *x = isq ? q + rr * HD : kn + (rr - R) * HD;
+        const float *w = isq ? a.q_norm : a.k_norm;
+        const int t = isq ? rr % N : rr - R;
+        float ss = 0.f;
+        for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
+        ss = warp_sum(ss);
+        const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+        for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv * w[d];
+        __syncwarp();
+        const float *cs = a.rope_cos + (int64_t)(p0 + t) * rs.ld, *sn = a.rope_sin + (int64_t)(p0 + t) * rs.ld;
+        for (int i = lane; i < rs.pairs; i += 32) {
+            const float c = cs[i], s_ = sn[i];
+            const float x1 = x[i], x2 = x[i + rs.off];
+            x[i] = x1 * c - x2 * s_;
+            x[i + rs.off] = x1 * s_ + x2 * c;
+        }
+    }
+    __syncthreads();
+    // the first chunk's copies start now; the new keys are in kn / vn for it
+    stage(0, 0);
+    // one CTA per (KV head, request) writes the new keys; no CTA reads them from the cache
+    if (sl == 0 && hb == 0) {
+        for (int i = tid; i < N * HD; i += 256) {
+            const int t = i / HD, d = i % HD;
+            const int64_t o = ((int64_t)(p0 + t) * a.nkv + g) * HD + d;
+            a.kc[o] = kn[i];
+            a.vc[o] = vn[i];
+        }
+    }
+    for (int i = tid; i < R * HD; i += 256) {
+        uint32_t h_, l_;
+        split_tf32(q[i], h_, l_);
+        qh[(i / HD) * QS + i % HD] = h_;
+        ql[(i / HD) * QS + i % HD] = l_;
+    }
+    __syncthreads();  // q split (the staging buffer is free for chunk 1)
+
+    const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf((float)HD);
+    float oacc[2][NTW][4];
+#pragma unroll
+    for (int m = 0; m < 2; m++)
+#pragma unroll
+        for (int u = 0; u < NTW; u++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) oacc[m][u][i] = 0.f;
+    for (int c = 0; c < nch; c++) {
+        const int bf = c & 1, j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
+        if (c + 1 < nch) {
+            stage(c + 1, bf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float *kb = Ks + bf * kGrpKeys * KS, *vb = Vs + bf * kGrpKeys * VS;
+        {   // scores: warp (m = warp / 4, key tile nb = warp % 4)
+            const int m = warp >> 2, nb = warp & 3, r0 = 16 * m + g8;
+            if (16 * m < R) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                const float *kr = kb + (8 * nb + g8) * KS;
+#pragma unroll 4
+                for (int kk = 0; kk < HD / 8; kk++) {
+                    const int k0 = 8 * kk + t4;
+                    uint32_t ah[4], al[4];
+                    ah[0] = r0 < R ? qh[r0 * QS + k0] : 0u;
+                    ah[1] = r0 + 8 < R ? qh[(r0 + 8) * QS + k0] : 0u;
+                    ah[2] = r0 < R ? qh[r0 * QS + k0 + 4] : 0u;
+                    ah[3] = r0 + 8 < R ? qh[(r0 + 8) * QS + k0 + 4] : 0u;
+                    al[0] = r0 < R ? ql[r0 * QS + k0] : 0u;
+                    al[1] = r0 + 8 < R ? ql[(r0 + 8) * QS + k0] : 0u;
+                    al[2] = r0 < R ? ql[r0 * QS + k0 + 4] : 0u;
+                    al[3] = r0 + 8 < R ? ql[(r0 + 8) * QS + k0 + 4] : 0u;
+                    uint32_t bh0, bl0, bh1, bl1;
+                    split_tf32(kr[k0], bh0, bl0);
+                    split_tf32(kr[k0 + 4], bh1, bl1);
+                    mma_3xtf32(acc, ah, al, bh0, bh1, bl0, bl1);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int r = r0 + 8 * (i >> 1), jj = 8 * nb + 2 * t4 + (i & 1), j = j0 + jj;
+                    if (r < R)
+                        sc[r * SS + jj] = (jj < nj && key_visible(a, j, p0 + r % N)) ? score_cap(a, acc[i] * scale)
+                                                                                   : -CUDART_INF_F;
+                }
+            }
+        }
+        __syncthreads();
+        for (int r = warp; r < R; r += 8) {  // online softmax, one warp per row
+            const float sv = lane < kGrpKeys ? sc[r * SS + lane] : -CUDART_INF_F;
+            const float mo = ms[r], mn = fmaxf(mo, warp_max(sv));
+            float f = 1.f, e = 0.f;
+            if (mn != -CUDART_INF_F) {
+                f = expf(mo - mn);
+                e = expf(sv - mn);
+            }
+            if (lane < kGrpKeys) sc[r * SS + lane] = e;
+            const float ps = warp_sum(e);
+            if (lane == 0) {
+                ls[r] = ls[r] * f + ps;
+                ms[r] = mn;
+                fs[r] = f;
+            }
+        }
+        __syncthreads();
+        // P.V: warp's n-tiles warp + 8 u, both m-tiles
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            if (16 * m >= R) continue;
+            const int r0 = 16 * m + g8;
+            const float f0 = r0 < R ? fs[r0] : 1.f, f1 = r0 + 8 < R ? fs[r0 + 8] : 1.f;
+#pragma unroll
+            for (int u = 0; u < NTW; u++) {
+                oacc[m][u][0] *= f0;
+                oacc[m][u][1] *= f0;
+                oacc[m][u][2] *= f1;
+                oacc[m][u][3] *= f1;
+            }
+#pragma unroll
+            for (int kk = 0; kk < kGrpKeys / 8; kk++) {
+                const int k0 = 8 * kk + t4;
+                uint32_t ah[4], al[4];
+                split_tf32(r0 < R ? sc[r0 * SS + k0] : 0.f, ah[0], al[0]);
+                split_tf32(r0 + 8 < R ? sc[(r0 + 8) * SS + k0] : 0.f, ah[1], al[1]);
+                split_tf32(r0 < R ? sc[r0 * SS + k0 + 4] : 0.f, ah[2], al[2]);
+                split_tf32(r0 + 8 < R ? sc[(r0 + 8) * SS + k0 + 4] : 0.f, ah[3], al[3]);
+#pragma unroll
+                for (int u = 0; u < NTW; u++) {
+                    const int n0 = 8 * (warp + 8 * u) + g8;
+                    uint32_t bh0, bl0, bh1, bl1;
+                    split_tf32(vb[k0 * VS + n0], bh0, bl0);
+                    split_tf32(vb[(k0 + 4) * VS + n0], bh1, bl1);
+                    mma_3xtf32(oacc[m][u], ah, al, bh0, bh1, bl0, bl1);
+                }
+            }
+        }
+        __syncthreads();  // this chunk's buffer, sc and fs are rewritten next
+    }
+
+    // 3. the slice's partial state
+    float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
+#pragma unroll
+    for (int m = 0; m < 2; m++)
+#pragma unroll
+        for (int u = 0; u < NTW; u++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int r = 16 * m + g8 + 8 * (i >> 1), d = 8 * (warp + 8 * u) + 2 * t4 + (i & 1);
+                if (r < R) po[(rid0 + r) * HD + d] = oacc[m][u][i];
+            }
+    if (tid < R) {
+        pm[rid0 + tid] = ms[tid];
+        pl[rid0 + tid] = ls[tid];
+    }
+}
+
 // Merges the key slices of one row (b, h, t) per CTA: M = max_s m_s,
 // L = sum_s l_s e^(m_s - M), O = sum_s o_s e^(m_s - M) (slice order), and
 // writes O / L x sigmoid(gate).  The slices' (m, l) and weights are formed in
@@ -1386,6 +1682,14 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch
 
 static int split_heads(int ratio, int N) { return std::max(1, std::min(ratio, kGrpRows / N)); }
 
+static bool attn_mma_enabled() {
+    static const bool on = [] {
+        const char *v = getenv("IFR_ATTN_MMA");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 int attn_splits(int nh, int nkv, int N, int batch, int max_ctx) {
     const int ratio = nh / nkv, hg = split_heads(ratio, N), nrg = (ratio + hg - 1) / hg;
     const int64_t ctas = (int64_t)nkv * nrg * batch;
@@ -1407,13 +1711,20 @@ static cudaError_t launch_split(const AttnArgs &a, int batch, cudaStream_t s) {
     if (!attr.test()) {
         cudaError_t e = cudaFuncSetAttribute(attn_part_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              GrpSmem<HD>::bytes(kGrpRows, kMaxN));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_part_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     MmaSmem<HD>::bytes(kGrpRows, kMaxN));
         if (e != cudaSuccess) return e;
         attr.set();
     }
     const int ratio = a.nh / a.nkv, hg = split_heads(ratio, a.N), nrg = (ratio + hg - 1) / hg;
     const int R = std::min(hg, ratio) * a.N;
-    cudaError_t e = launch_k(attn_part_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
-                             (size_t)GrpSmem<HD>::bytes(R, a.N), s, a, hg, a.splits);
+    // the tensor-core kernel (IFR_ATTN_MMA=0 in the environment selects the CUDA-core one)
+    cudaError_t e = attn_mma_enabled()
+                        ? launch_k(attn_part_mma_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
+                                   (size_t)MmaSmem<HD>::bytes(R, a.N), s, a, hg, a.splits)
+                        : launch_k(attn_part_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
+                                   (size_t)GrpSmem<HD>::bytes(R, a.N), s, a, hg, a.splits);
     if (e != cudaSuccess) return e;
     return launch_k(attn_combine_kernel<HD>, dim3((unsigned)(batch * a.nh * a.N)), dim3(256), 0, s, a, batch,
                     a.splits);
