@@ -411,6 +411,14 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
         a.a_prev += b * a.b_prev;
     }
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
+    // the state rows, loaded first (their memory latency overlaps steps 1-5):
+    // thread (row = tid / 4, lc = tid % 4) owns columns 16 e + 4 lc + v of row
+    // `row`, read as 16-byte vectors (a warp reads 64 contiguous bytes per row)
+    const int row = tid >> 2, lc = tid & 3;
+    float4 *Sp = reinterpret_cast<float4 *>(a.S + ((int64_t)h * HD + row) * HD + 4 * lc);
+    float4 sv[CPT / 4];
+#pragma unroll
+    for (int e = 0; e < CPT / 4; e++) sv[e] = Sp[4 * e];
     // 1. conv of the head's channels (ssm_step_kernel step 1)
     auto win = [&](int i, int ch) -> const float * {
         if (i < K - 1) return a.hist + (int64_t)i * C + ch;
@@ -538,33 +546,47 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
         rec[tid * REC + 2 * HD] = ndec[tid];
         rec[tid * REC + 2 * HD + 1] = nbeta[tid];
     }
-    // 6. the state rows: row tid / 4, columns lc + 4 e
-    const int row = tid >> 2, lc = tid & 3;
-    float *Sp = a.S + ((int64_t)h * HD + row) * HD + lc;
-    float sv[CPT];
-#pragma unroll
-    for (int e = 0; e < CPT; e++) sv[e] = Sp[4 * e];
+    // 6. the state rows (loaded at the start) through the replayed and new tokens
     auto update = [&](const float *kv, float dec, float beta, float vrow) {
         float sk = 0.f;
 #pragma unroll
-        for (int e = 0; e < CPT; e++) {
-            sv[e] *= dec;
-            sk += sv[e] * kv[lc + 4 * e];
+        for (int e = 0; e < CPT / 4; e++) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kv + 16 * e + 4 * lc);
+            sv[e].x *= dec;
+            sv[e].y *= dec;
+            sv[e].z *= dec;
+            sv[e].w *= dec;
+            sk += sv[e].x * k4.x;
+            sk += sv[e].y * k4.y;
+            sk += sv[e].z * k4.z;
+            sk += sv[e].w * k4.w;
         }
         sk += __shfl_xor_sync(0xffffffffu, sk, 1);
         sk += __shfl_xor_sync(0xffffffffu, sk, 2);
         const float dd = beta * (vrow - sk);
 #pragma unroll
-        for (int e = 0; e < CPT; e++) sv[e] += dd * kv[lc + 4 * e];
+        for (int e = 0; e < CPT / 4; e++) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kv + 16 * e + 4 * lc);
+            sv[e].x += dd * k4.x;
+            sv[e].y += dd * k4.y;
+            sv[e].z += dd * k4.z;
+            sv[e].w += dd * k4.w;
+        }
     };
     for (int j = 0; j < r; j++) update(rk[j], rdec[j], rbeta[j], rv[j][row]);
 #pragma unroll
-    for (int e = 0; e < CPT; e++) Sp[4 * e] = sv[e];
+    for (int e = 0; e < CPT / 4; e++) Sp[4 * e] = sv[e];
     for (int t = 0; t < N; t++) {
         update(xk[t], ndec[t], nbeta[t], cv[t][row]);
         float yv = 0.f;
 #pragma unroll
-        for (int e = 0; e < CPT; e++) yv += sv[e] * xq[t][lc + 4 * e];
+        for (int e = 0; e < CPT / 4; e++) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(&xq[t][16 * e + 4 * lc]);
+            yv += sv[e].x * q4.x;
+            yv += sv[e].y * q4.y;
+            yv += sv[e].z * q4.z;
+            yv += sv[e].w * q4.w;
+        }
         yv += __shfl_xor_sync(0xffffffffu, yv, 1);
         yv += __shfl_xor_sync(0xffffffffu, yv, 2);
         if (lc == 0) ys[t][row] = yv;
