@@ -455,6 +455,7 @@ def run_spec(args):
     G = args.gamma
     ctx = pkg.Context(local, torch_stream=False)  # own stream: capturable
     ctx.set_activation(args.act)
+    ctx.set_fused_layers(bool(args.fused_layers))
     path = synth.cached(SPEC_PRESET, SPEC_SEED)
     model = Model(ctx, path)
     info = model.info
@@ -1182,6 +1183,8 @@ def main():
     ap.add_argument("--batch", type=int, default=64, help="requests of the batch workload (all ranks)")
     ap.add_argument("--prompt", type=int, default=2048, help="prompt tokens per request (batch workload)")
     ap.add_argument("--gamma", type=int, default=4)
+    ap.add_argument("--fused-layers", type=int, default=0, choices=[0, 1],
+                    help="spec workload: the verify's decoder layers as one persistent launch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="spec workload: skip every extra key")
     ap.add_argument("--no-shard-legs", action="store_true", help="spec workload: skip the config-4/5 legs")

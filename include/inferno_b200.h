@@ -93,6 +93,14 @@ int ifr_ctx_set_dense_min_cols(ifr_ctx *ctx, int ncols);
  * product instead of 1e-4), 0 (default) keeps them exact.  No counterpart in
  * the reference (its prefill is the f32 token loop). */
 int ifr_ctx_set_prefill_dense(ifr_ctx *ctx, int enable);
+/* enable = 1 runs the decoder layers of a one-request verify (<= 8 columns,
+ * exact activations, one rank) as one persistent cooperative launch - every
+ * projection, GatedDeltaNet step and attention step of the layer stack as a
+ * phase separated by grid barriers - instead of ~5 launches per layer
+ * (forward_cpu!, src/ModelCPU.jl:976-1020, same arithmetic and tolerance).
+ * Models it does not cover (Gemma4 blocks, other head dims, formats other
+ * than Q4_K/Q6_K) keep the separate launches.  Default 0. */
+int ifr_ctx_set_fused_layers(ifr_ctx *ctx, int enable);
 /* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
  * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);
@@ -334,6 +342,18 @@ int ifr_rollback(ifr_state *s, const int32_t *accept_count, const int32_t *token
  * launches enqueued by the state so far */
 int ifr_state_profile(ifr_state *s, int enable);
 int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count, int64_t *launches);
+/* with profiling on (ifr_state_profile): the phases of the last fused
+ * layer-stack launch (ifr_ctx_set_fused_layers) - kinds[i] (1 projection,
+ * 2 GatedDeltaNet state update, 3 attention slices, 4 attention combine,
+ * 5 GatedDeltaNet norm, gate and commits) and
+ * us[6 i .. 6 i + 5] in microseconds: the phase from CTA 0's start to the
+ * next phase's start; the slowest CTA's parts (fragments, tiles, epilogue -
+ * projections only, other kinds report the whole phase as the third part -
+ * and its barrier wait to the next phase's start) and its whole phase; when max_phases >= 2 * the phase count, us[6 n + 4 i ..] also
+ * holds phase i's grid barrier: CTA 0's arrival to the last CTA's, the last
+ * arrival to CTA 0 seeing it, CTA 0's acquire fence, and on to the next
+ * phase's start; *n_phases = 0 when none was traced */
+int ifr_state_fused_trace(ifr_state *s, int max_phases, int *kinds, double *us, int *n_phases);
 /* enqueue only the dequant-GEMV launches of one verify forward (every
  * decoder-layer projection + the lm_head) on ncols columns of scratch
  * activations, back to back (capturable): a measurement of the verify GEMVs

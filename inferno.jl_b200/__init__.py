@@ -116,6 +116,10 @@ class Context:
         """let one-request prefill chunks use the dense tensor-core path"""
         check(load().ifr_ctx_set_prefill_dense(self.handle, 1 if enable else 0))
 
+    def set_fused_layers(self, enable=True):
+        """run a one-request verify's decoder layers as one persistent launch"""
+        check(load().ifr_ctx_set_fused_layers(self.handle, 1 if enable else 0))
+
     def set_stream(self, stream):
         check(load().ifr_ctx_set_stream(self.handle, ctypes.c_void_p(stream.cuda_stream)))
 

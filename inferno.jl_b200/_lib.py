@@ -37,6 +37,7 @@ SIGNATURES = {
     "ifr_qgemm": (_i, [_vp, _vp, _vp, _i, _vp]),
     "ifr_ctx_set_dense_min_cols": (_i, [_vp, _i]),
     "ifr_ctx_set_prefill_dense": (_i, [_vp, _i]),
+    "ifr_ctx_set_fused_layers": (_i, [_vp, _i]),
     "ifr_state_read_request": (_i, [_vp, _i, _vp, _i, _vp, _vp]),
     "ifr_prefill_batch": (_i, [_vp, _vp, _i, _vp]),
     "ifr_state_create_batch": (_i, [_vp, _i, _i, ctypes.POINTER(_vp)]),
@@ -74,6 +75,7 @@ SIGNATURES = {
     "ifr_spec_graph_launch": (_i, [_vp]),
     "ifr_state_profile": (_i, [_vp, _i]),
     "ifr_state_profile_read": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    "ifr_state_fused_trace": (_i, [_vp, _i, _vp, _vp, _vp]),
     "ifr_gemv_pass": (_i, [_vp, _i]),
     "ifr_state_read": (_i, [_vp, _vp, _i, _vp, _vp]),
     "ifr_state_last_verify": (_i, [_vp, _vp, _vp, _vp, _vp]),

@@ -186,14 +186,14 @@ __global__ void __launch_bounds__(kNL) chunk_stats_kernel(const float *__restric
     if (u >= units) return;
     const int r = (int)(u / nch), c = (int)(u % nch), lane = threadIdx.x & 31;
     const float *row = row_ptr(target, draft, r, B, G, V);
-    float x[8][8];
-    int n[8];
+    // two passes over the chunk (the second one hits L1): max, then the sums
     float m = -CUDART_INF_F;
-#pragma unroll
+#pragma unroll 2
     for (int v = 0; v < 8; v++) {
-        n[v] = load8w(row, V, c, v, x[v]);
+        float x[8];
+        const int n = load8w(row, V, c, v, x);
 #pragma unroll
-        for (int q = 0; q < kPER; q++) if (q < n[v]) m = fmaxf(m, x[v][q]);
+        for (int q = 0; q < kPER; q++) if (q < n) m = fmaxf(m, x[q]);
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -202,14 +202,16 @@ __global__ void __launch_bounds__(kNL) chunk_stats_kernel(const float *__restric
     float t[8];
 #pragma unroll
     for (int v = 0; v < 8; v++) {
+        float x[8];
+        const int n = load8w(row, V, c, v, x);
         t[v] = 0.f;
 #pragma unroll
         for (int q = 0; q < kPER; q++) {
-            if (q < n[v]) {
+            if (q < n) {
                 if constexpr (FILT) {
-                    if (!(F.w(c * kCH + kPER * (lane + 32 * v) + q, x[v][q]) > 0.f)) continue;
+                    if (!(F.w(c * kCH + kPER * (lane + 32 * v) + q, x[q]) > 0.f)) continue;
                 }
-                t[v] = __fadd_rn(t[v], elem_e(x[v][q], m, T));
+                t[v] = __fadd_rn(t[v], elem_e(x[q], m, T));
             }
         }
     }

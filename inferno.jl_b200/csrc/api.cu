@@ -53,6 +53,7 @@ struct ifr_ctx {
     int act = IFR_ACT_EXACT;       // K-quant activation mode of the GEMVs
     int dense_min = IFR_DENSE_MIN_COLS_DEFAULT;  // engine GEMMs of this many columns use the dense path
     int prefill_dense = 0;                         // one-request prefill chunks may use the dense path
+    int fused_layers = 0;                          // one-request verify: the layer stack as one launch
     std::atomic<int> refs{0};      // live models built on this context
     std::atomic<bool> closing{false};
 };
@@ -133,6 +134,7 @@ int ifr_ctx_device(const ifr_ctx *c) { return c->device; }
 int ifr_ctx_activation(const ifr_ctx *c) { return c->act; }
 int ifr_ctx_dense_min(const ifr_ctx *c) { return c->dense_min; }
 int ifr_ctx_prefill_dense(const ifr_ctx *c) { return c->prefill_dense; }
+int ifr_ctx_fused_layers(const ifr_ctx *c) { return c->fused_layers; }
 static void ctx_destroy_now(ifr_ctx *c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
@@ -214,6 +216,12 @@ int ifr_ctx_set_dense_min_cols(ifr_ctx *c, int ncols) {
 int ifr_ctx_set_prefill_dense(ifr_ctx *c, int enable) {
     if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
     c->prefill_dense = enable ? 1 : 0;
+    return IFR_OK;
+}
+
+int ifr_ctx_set_fused_layers(ifr_ctx *c, int enable) {
+    if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
+    c->fused_layers = enable ? 1 : 0;
     return IFR_OK;
 }
 

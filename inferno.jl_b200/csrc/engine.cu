@@ -9,6 +9,7 @@
 #include "comm.h"
 #include "common.cuh"
 #include "model.cuh"
+#include "fused.cuh"
 #include "dequant.cuh"
 
 #include <fcntl.h>
@@ -32,6 +33,7 @@ int ifr_ctx_device(const ifr_ctx *c);
 int ifr_ctx_activation(const ifr_ctx *c);
 int ifr_ctx_dense_min(const ifr_ctx *c);
 int ifr_ctx_prefill_dense(const ifr_ctx *c);
+int ifr_ctx_fused_layers(const ifr_ctx *c);
 void ifr_ctx_retain(ifr_ctx *c);
 void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
@@ -527,6 +529,18 @@ struct ifr_state {
     struct Rec { int ev0, cat; int64_t bytes; };
     std::vector<Rec> recs;
     int ev_next = 0;
+    // fused layer stack (one request): device phase lists for n = 1..kNMax
+    // columns (null: the model is not covered), its grid-barrier counter and
+    // the split-KV partials of its attention phases
+    ifr::FPhase *fused_ph[kNMax + 1] = {};
+    int fused_np[kNMax + 1] = {};
+    unsigned *fused_ctr = nullptr;
+    float *fused_part = nullptr;
+    float *fused_ssq = nullptr, *fused_stage = nullptr;  // split GatedDeltaNet step scratch
+    // profiling: phase start times of the last fused launch, its phase kinds
+    unsigned long long *fused_trace = nullptr;
+    std::vector<int> fused_kinds[kNMax + 1];
+    int fused_last = 0;
     // a captured CUDA graph of consecutive spec steps
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
@@ -552,7 +566,10 @@ int dalloc(ifr_state *s, T **p, size_t n) {
 }
 
 // categories of timed launches (ifr_state_profile_read)
-enum { CAT_LM_HEAD = 0, CAT_DRAFT_LM_HEAD, CAT_LAYER_GEMV, CAT_DRAFT_GEMV, CAT_SSM, CAT_ATTN, CAT_COMM, CAT_NCAT = 8 };
+enum {
+    CAT_LM_HEAD = 0, CAT_DRAFT_LM_HEAD, CAT_LAYER_GEMV, CAT_DRAFT_GEMV, CAT_SSM, CAT_ATTN, CAT_COMM, CAT_FUSED,
+    CAT_NCAT = 8
+};
 
 struct ProfScope {
     ifr_state *s;
@@ -643,6 +660,71 @@ int gemma_full_pairs(const ifr_model *m) {
     return (int)(m->partial_rotary * (float)m->info.head_dim) / 2;
 }
 
+// the GatedDeltaNet step of layer li over n columns per request (s->proj, s->x -> s->y)
+ifr::SsmArgs ssm_args(ifr_state *s, const DevLayer &L, int li, int n) {
+    const ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    ifr::SsmArgs a{};
+    a.proj = s->proj;
+    a.ldp = L.proj.rows;
+    a.xn = s->x;
+    a.in_norm = L.attn_norm;
+    a.d = c.hidden;
+    a.conv_w = L.conv_w;
+    a.ab_w = L.ab_w;
+    a.ssm_a = L.ssm_a;
+    a.dt_bias = L.dt_bias;
+    a.norm_w = L.ssm_norm;
+    a.S = s->S[li];
+    a.hist = s->hist[li];
+    a.rq = s->rq[li];
+    a.rkv = s->rkv[li];
+    a.a_prev = &s->sc->a_prev;
+    a.y = s->y;
+    a.ldy = m->inner;
+    a.N = n;
+    a.H = c.ssm_heads;
+    a.C = m->conv_channels;
+    a.K = c.conv_kernel;
+    a.eps = c.rms_eps;
+    const int64_t hd = c.ssm_head_dim;
+    a.b_S = (int64_t)c.ssm_heads * hd * hd;
+    a.b_hist = (int64_t)(c.conv_kernel - 1) * m->conv_channels;
+    a.b_rq = (int64_t)kNMax * m->conv_channels;
+    a.b_rkv = (int64_t)c.ssm_heads * kNMax * (2 * hd + 2);
+    a.b_prev = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
+    return a;
+}
+
+// the gated attention step of a Qwen3.5 attention layer over n columns per
+// request (s->proj -> s->y; keys and values of request b at kc / vc + b * kv_ld)
+ifr::AttnArgs attn_args(ifr_state *s, const DevLayer &L, int n, float *kc, float *vc, const int32_t *pos,
+                        int pos_ld, int64_t kv_ld) {
+    const ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    ifr::AttnArgs a{};
+    a.qkv = s->proj;
+    a.ldq = L.proj.rows;
+    a.q_norm = L.q_norm;
+    a.k_norm = L.k_norm;
+    a.kc = kc;
+    a.vc = vc;
+    a.pos = pos;
+    a.rope_cos = s->rope_cos;
+    a.rope_sin = s->rope_sin;
+    a.out = s->y;
+    a.ldo = (int64_t)m->nh * c.head_dim;
+    a.N = n;
+    a.nh = m->nh;
+    a.nkv = m->nkv;
+    a.hd = c.head_dim;
+    a.rotary_dim = c.rotary_dim;
+    a.eps = c.rms_eps;
+    a.b_kv = kv_ld;
+    a.b_pos = pos_ld;
+    return a;
+}
+
 // one decoder layer (attention or SSM) on n columns of s->x
 // n tokens per request, s->B requests (columns b * n + t); pos of request b at
 // pos + b * pos_ld; kc / vc of request b at + b * kv_ld
@@ -715,61 +797,14 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     }
     if (L.ssm) {
         ProfScope ps(s, CAT_SSM, 0, st);
-        ifr::SsmArgs a{};
-        a.proj = s->proj;
-        a.ldp = L.proj.rows;
-        a.xn = s->x;
-        a.in_norm = L.attn_norm;
-        a.d = d;
-        a.conv_w = L.conv_w;
-        a.ab_w = L.ab_w;
-        a.ssm_a = L.ssm_a;
-        a.dt_bias = L.dt_bias;
-        a.norm_w = L.ssm_norm;
-        a.S = s->S[li];
-        a.hist = s->hist[li];
-        a.rq = s->rq[li];
-        a.rkv = s->rkv[li];
-        a.a_prev = &s->sc->a_prev;
-        a.y = s->y;
-        a.ldy = m->inner;
-        a.N = n;
-        a.H = c.ssm_heads;
-        a.C = m->conv_channels;
-        a.K = c.conv_kernel;
-        a.eps = c.rms_eps;
-        const int64_t hd = c.ssm_head_dim;
-        a.b_S = (int64_t)c.ssm_heads * hd * hd;
-        a.b_hist = (int64_t)(c.conv_kernel - 1) * m->conv_channels;
-        a.b_rq = (int64_t)kNMax * m->conv_channels;
-        a.b_rkv = (int64_t)c.ssm_heads * kNMax * (2 * hd + 2);
-        a.b_prev = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
+        const ifr::SsmArgs a = ssm_args(s, L, li, n);
         if (n > kNMax)  // a prefill chunk of one request: scanned and committed in one launch
             ECHECK(ifr::ssm_chunk(a, c.ssm_head_dim, st), "ssm_chunk");
         else
             ECHECK(ifr::ssm_step(a, c.ssm_head_dim, B, st), "ssm_step");
     } else {
         ProfScope ps(s, CAT_ATTN, 0, st);
-        ifr::AttnArgs a{};
-        a.qkv = s->proj;
-        a.ldq = L.proj.rows;
-        a.q_norm = L.q_norm;
-        a.k_norm = L.k_norm;
-        a.kc = kc;
-        a.vc = vc;
-        a.pos = pos;
-        a.rope_cos = s->rope_cos;
-        a.rope_sin = s->rope_sin;
-        a.out = s->y;
-        a.ldo = (int64_t)m->nh * c.head_dim;
-        a.N = n;
-        a.nh = m->nh;
-        a.nkv = m->nkv;
-        a.hd = c.head_dim;
-        a.rotary_dim = c.rotary_dim;
-        a.eps = c.rms_eps;
-        a.b_kv = kv_ld;
-        a.b_pos = pos_ld;
+        ifr::AttnArgs a = attn_args(s, L, n, kc, vc, pos, pos_ld, kv_ld);
         if (s->attn_part) {
             a.part = s->attn_part;
             a.splits = ifr::attn_splits(m->nh, m->nkv, n, B, s->max_ctx);
@@ -797,6 +832,153 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
     swiglu.ldx = 2 * (int64_t)m->ffn;
     if ((rc = gemv(s, gcat, L.down, s->gu, nc, s->x, m->tp_rank == 0, st, swiglu))) return rc;
     return allreduce(s, s->x, (size_t)nc * d, st);
+}
+
+// ---- the layer stack of a one-request verify as one launch (fused_step.cuh)
+
+// the projection's GEMV phases over n columns, one per part (the parts write
+// disjoint rows of Y from the same X: no barrier between them)
+bool fused_proj(std::vector<ifr::FPhase> &v, const Proj &p, const float *X, int n, float *Y, bool acc,
+                const float *xw, float eps, int ep) {
+    if (p.parts.empty() || (ep && p.parts.size() != 1)) return false;
+    int64_t r0 = 0;
+    const int64_t ldy = ep ? p.rows / 2 : p.rows;
+    for (size_t i = 0; i < p.parts.size(); i++) {
+        const ifr::QTensor &q = p.parts[i];
+        ifr::FGemv g{};
+        g.W = q.data;
+        g.M = q.rows;
+        g.K = q.cols;
+        g.nrb = (int)q.nrb;
+        g.nu = (int)q.nu;
+        g.fmt = q.type;
+        g.nt = n <= 4 ? 1 : 2;
+        g.xf = xw ? 3 : 0;
+        g.ep = ep;
+        g.accumulate = acc ? 1 : 0;
+        g.gran = ep ? 2 : 1;
+        g.X = X;
+        g.ldx = q.cols;
+        g.ncols = n;
+        g.Y = Y + r0;
+        g.ldy = ldy;
+        g.xw = xw;
+        g.eps = eps;
+        ifr::FPhase ph;
+        if (!ifr::fused_gemv_phase(g, ph)) return false;
+        ph.nobar = i + 1 < p.parts.size() ? 1 : 0;
+        v.push_back(ph);
+        r0 += q.rows;
+    }
+    return true;
+}
+
+// the phases of the target's decoder layers over n columns (layer_forward's
+// sequence for one request, one rank, SwiGLU MLPs); false when a layer is not
+// covered
+bool fused_plan(ifr_state *s, int n, std::vector<ifr::FPhase> &v) {
+    ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    const int sc_ld = (int)(sizeof(ifr::EngineScalars) / sizeof(int32_t));
+    const int64_t kv_ld = (int64_t)s->max_ctx * m->nkv * c.head_dim;
+    v.clear();
+    for (int li = 0; li < c.n_layers; li++) {
+        const DevLayer &L = m->layers[li];
+        if (!L.gate_up.glu) return false;
+        if (!fused_proj(v, L.proj, s->x, n, s->proj, false, L.attn_norm, c.rms_eps, 0)) return false;
+        if (L.ssm) {
+            ifr::FPhase upd, fin;
+            if (!ifr::fused_ssm_phases(ssm_args(s, L, li, n), c.ssm_head_dim, s->fused_ssq, s->fused_stage, upd, fin))
+                return false;
+            v.push_back(upd);
+            v.push_back(fin);
+        } else {
+            ifr::AttnArgs a = attn_args(s, L, n, s->kc[li], s->vc[li], &s->sc->pos, sc_ld, kv_ld);
+            a.part = s->fused_part;
+            a.splits = ifr::attn_splits(m->nh, m->nkv, n, 1, s->max_ctx);
+            ifr::FPhase part, comb;
+            if (!ifr::fused_attn_phases(a, part, comb)) return false;
+            v.push_back(part);
+            v.push_back(comb);
+        }
+        if (!fused_proj(v, L.out, s->y, n, s->x, true, nullptr, 0.f, 0)) return false;
+        if (!fused_proj(v, L.gate_up, s->x, n, s->hmid, false, L.post_norm, c.rms_eps, 1)) return false;
+        if (!fused_proj(v, L.down, s->hmid, n, s->x, true, nullptr, 0.f, 0)) return false;
+    }
+    // L2 prefetch plan: the first phase sends the next two GEMV phases'
+    // weights, every GEMV phase after it the one two GEMV phases ahead
+    // (phase 0's own weights are sent at the kernel's start)
+    std::vector<int> gi;
+    for (int i = 0; i < (int)v.size(); i++)
+        if (v[i].kind == ifr::FPhase::kGemv) gi.push_back(i);
+    auto pf = [&](int k) {
+        const ifr::FGemv &g = v[gi[k]].g;
+        ifr::FPrefetch p;
+        p.W = g.W;
+        p.nrb = g.nrb;
+        p.nu = g.nu;
+        p.fmt = g.fmt;
+        p.gran = g.gran;
+        return p;
+    };
+    for (int k = 0; k < (int)gi.size(); k++) {
+        if (k == 0) {
+            if (gi.size() > 1) v[gi[0]].pf[0] = pf(1);
+            if (gi.size() > 2) v[gi[0]].pf[1] = pf(2);
+        } else if (k + 2 < (int)gi.size()) {
+            v[gi[k]].pf[0] = pf(k + 2);
+        }
+    }
+    // tile-buffer plan: a GEMV phase's tiles are copied as soon as the previous
+    // GEMV phase has read its own (phase 0's at the kernel's start)
+    for (int k = 1; k < (int)gi.size(); k++)
+        if (v[gi[k]].tiles_smem) v[gi[k - 1]].tl = pf(k);
+    if (!gi.empty() && gi[0] > 0 && v[gi[0]].tiles_smem) v[0].tl = pf(0);
+    return true;
+}
+
+// builds the state's fused phase lists for n = 1..kNMax when the model is
+// covered (one request, one rank, Qwen3.5 blocks); leaves them null otherwise
+int fused_build(ifr_state *s) {
+    ifr_model *m = s->m;
+    const ifr_model_info &c = m->info;
+    if (s->B != 1 || m->comm || m->gemma || c.n_layers < 1) return IFR_OK;
+    bool any_attn = false;
+    for (auto &L : m->layers) any_attn |= !L.ssm;
+    if (any_attn) {
+        int rc = dalloc(s, &s->fused_part, (size_t)ifr::attn_part_floats(m->nh, m->nkv, c.head_dim, 1, s->max_ctx));
+        if (rc) return rc;
+    }
+    if (c.ssm_heads > 0) {
+        const size_t rec = (size_t)c.ssm_heads * kNMax * (2 * c.ssm_head_dim + 2);
+        int rc = dalloc(s, &s->fused_ssq, (size_t)c.ssm_heads * ifr::kFusedSsmSplit * kNMax);
+        if (!rc) rc = dalloc(s, &s->fused_stage, rec);
+        if (rc) return rc;
+    }
+    std::vector<std::vector<ifr::FPhase>> plans(kNMax + 1);
+    for (int n = 1; n <= kNMax; n++)
+        if (!fused_plan(s, n, plans[n])) return IFR_OK;  // not covered: the separate launches
+    int rc = dalloc(s, &s->fused_ctr, 4);
+    size_t most = 0;
+    for (int n = 1; n <= kNMax; n++) {
+        most = std::max(most, plans[n].size());
+        for (auto &ph : plans[n]) s->fused_kinds[n].push_back(ph.kind);
+    }
+    if (!rc) rc = dalloc(s, &s->fused_trace, 4 * most * (ifr::fused_ctas() + 1) + 1);
+    for (int n = 1; !rc && n <= kNMax; n++) {
+        rc = dalloc(s, &s->fused_ph[n], plans[n].size());
+        if (!rc && cudaMemcpy(s->fused_ph[n], plans[n].data(), plans[n].size() * sizeof(ifr::FPhase),
+                              cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = ifr_fail(IFR_ERR_CUDA, "H2D fused phases");
+        s->fused_np[n] = (int)plans[n].size();
+    }
+    return rc;
+}
+
+// the verify of n columns runs as the fused launch
+bool fused_on(const ifr_state *s, int n) {
+    return n >= 1 && n <= kNMax && s->fused_ph[n] && !s->prefill_chunk && ifr_ctx_fused_layers(s->m->ctx) &&
+           ifr_ctx_activation(s->m->ctx) == IFR_ACT_EXACT;
 }
 
 // embedding rows of the n verify tokens of each of B requests (row b * n + t):
@@ -951,9 +1133,21 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
         s->launches++;
     }
     const int64_t kv_ld = (int64_t)s->max_ctx * m->nkv * c.head_dim;
-    for (int li = 0; li < c.n_layers; li++) {
-        int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, sc_ld, kv_ld, false, st);
-        if (rc) return rc;
+    if (fused_on(s, n)) {
+        ProfScope ps(s, CAT_FUSED, 0, st);
+        if (s->prof)
+            ECHECK(cudaMemsetAsync(s->fused_trace, 0,
+                                   (4 * (size_t)s->fused_np[n] * (ifr::fused_ctas() + 1) + 1) * sizeof(unsigned long long), st),
+                   "fused trace reset");
+        ECHECK(ifr::fused_layers(s->fused_ph[n], s->fused_np[n], s->fused_ctr, s->prof ? s->fused_trace : nullptr, st),
+               "fused_layers");
+        s->launches++;
+        s->fused_last = n;
+    } else {
+        for (int li = 0; li < c.n_layers; li++) {
+            int rc = layer_forward(s, m->layers[li], li, n, s->kc[li], s->vc[li], &s->sc->pos, sc_ld, kv_ld, false, st);
+            if (rc) return rc;
+        }
     }
     ifr::rmsnorm(s->x, m->final_norm, s->hid, nc, c.hidden, c.rms_eps, c.hidden, c.hidden, st);
     if (logits) {
@@ -1348,6 +1542,7 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     }
     if (!rc && cudaMallocHost((void **)&s->h_tok, sizeof(int32_t) * (N + 64)) != cudaSuccess)
         rc = ifr_fail(IFR_ERR_NOMEM, "cudaMallocHost failed");
+    if (!rc) rc = fused_build(s);
     if (!rc && m->gemma) {
         // precompute_rope (Gemma4.jl:205-249): frequencies and angles in
         // Float64, cos / sin as Float32; sliding layers: every pair, theta_swa;
@@ -1852,6 +2047,52 @@ int ifr_state_profile_read(ifr_state *s, double *ms, int64_t *bytes, int *count,
     cudaGetLastError();  // a failed elapsed-time query must not surface in a later launch check
     if (launches) *launches = s->launches;
     if (failed) return ifr_fail(IFR_ERR_UNSUPPORTED, "%d timings unavailable (events recorded inside a CUDA graph cannot be timed); profile eagerly", failed);
+    return IFR_OK;
+}
+
+int ifr_state_fused_trace(ifr_state *s, int max_phases, int *kinds, double *us, int *n_phases) {
+    if (!s || !n_phases) return ifr_fail(IFR_ERR_ARG, "NULL argument");
+    *n_phases = 0;
+    const int n = s->fused_last;
+    if (!s->prof || n < 1 || !s->fused_ph[n]) return IFR_OK;  // nothing traced
+    const int np = s->fused_np[n], nc = ifr::fused_ctas();
+    std::vector<unsigned long long> t(4 * (size_t)np * (nc + 1) + 1);
+    ECHECK(cudaStreamSynchronize(ifr_ctx_stream_of(s->m->ctx)), "fused trace sync");
+    ECHECK(cudaMemcpy(t.data(), s->fused_trace, t.size() * sizeof(t[0]), cudaMemcpyDeviceToHost), "fused trace D2H");
+    const int k = std::min(np, max_phases);
+    auto d = [](unsigned long long a, unsigned long long b) { return (double)(long long)(b - a) * 1e-3; };
+    const unsigned long long *bar = t.data() + 4 * (size_t)np * nc, end = t[4 * (size_t)np * nc + 4 * np];
+    for (int i = 0; i < k; i++) {
+        const unsigned long long *c0 = t.data() + 4 * (size_t)i * nc;
+        const unsigned long long next = i + 1 < np ? t[4 * (size_t)(i + 1) * nc] : end;
+        // the slowest CTA of the phase (its own start to its end)
+        int w = 0;
+        for (int c = 1; c < nc; c++)
+            if (c0[4 * c + 3] - c0[4 * c] > c0[4 * w + 3] - c0[4 * w]) w = c;
+        const unsigned long long *cw = c0 + 4 * w;
+        if (kinds) kinds[i] = s->fused_kinds[n][i];
+        if (us) {
+            us[6 * i] = d(c0[0], next);
+            us[6 * i + 1] = d(cw[0], cw[1]);
+            us[6 * i + 2] = d(cw[1], cw[2]);
+            us[6 * i + 3] = d(cw[2], cw[3]);
+            us[6 * i + 4] = d(cw[3], next);
+            us[6 * i + 5] = d(cw[0], cw[3]);
+        }
+        if (us && max_phases >= 2 * np) {
+            const unsigned long long *b = bar + 4 * i;
+            double *o = us + 6 * np + 4 * i;
+            if (b[0] && b[3]) {
+                o[0] = d(b[0], b[3]);
+                o[1] = d(b[3], b[1]);
+                o[2] = d(b[1], b[2]);
+                o[3] = d(b[2], next);
+            } else {
+                o[0] = o[1] = o[2] = o[3] = 0;
+            }
+        }
+    }
+    *n_phases = k;
     return IFR_OK;
 }
 

@@ -6,6 +6,7 @@
 // f64 (:654-667) and so do we.
 #include "common.cuh"
 #include "model.cuh"
+#include "qgemv_kernels.cuh"  // the M-tile code of the fused verify (fused_step.cuh)
 
 #include <algorithm>
 #include <cooperative_groups.h>
@@ -27,6 +28,26 @@ __device__ __forceinline__ float block_sum256(float v, float *red) {
     __syncthreads();
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) s += red[w];
+    return s;
+}
+
+// a barrier over the 256 threads of a (virtual) block: BAR 0 = the whole CTA
+// (__syncthreads), BAR > 0 = named barrier BAR of 256 threads, so that two
+// 256-thread virtual blocks can share one 512-thread CTA (fused.cu)
+template <int BAR>
+__device__ __forceinline__ void bar256() {
+    if constexpr (BAR == 0) __syncthreads();
+    else asm volatile("bar.sync %0, 256;" ::"n"(BAR) : "memory");
+}
+template <int BAR>
+__device__ __forceinline__ float block_sum256_b(float v, float *red, int tid) {
+    v = warp_sum(v);
+    bar256<BAR>();
+    if ((tid & 31) == 0) red[tid >> 5] = v;
+    bar256<BAR>();
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; w++) s += red[w];
@@ -380,13 +401,14 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
 // Same arithmetic as ssm_step_kernel: thread (row = tid / 4, lc = tid % 4) owns
 // columns lc + 4 e of state row `row`; thread c < 3 HD owns conv channel c of
 // the head (q, k, v); the alpha/beta projections are summed block-wide.
+// one (head h, request b) block of 4 HD threads (the whole CTA)
 template <int HD>
-__global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
+__device__ __forceinline__ void ssm_batch_body(SsmArgs a, int h, int64_t b) {
     constexpr int NT = 4 * HD;
     constexpr int CPT = HD / 4;        // state columns per thread
     constexpr int REC = 2 * HD + 2;
     constexpr int NW = NT / 32;
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int N = a.N, K = a.K, C = a.C, qk = a.H * HD;
     __shared__ __align__(16) float xq[kMaxN][HD];
     __shared__ __align__(16) float xk[kMaxN][HD];
@@ -397,10 +419,7 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
     __shared__ float rdec[kMaxN], rbeta[kMaxN], ndec[kMaxN], nbeta[kMaxN];
     __shared__ float ab[3][kMaxN], ssq[kMaxN];
     __shared__ float red_n[NW][3 * kMaxN];
-    pdl_trigger();
-    pdl_wait();
-    {  // request blockIdx.y
-        const int64_t b = blockIdx.y;
+    {  // request b
         a.proj += b * a.N * a.ldp;
         a.xn += b * a.N * a.d;
         a.y += b * a.N * a.ldy;
@@ -607,6 +626,13 @@ __global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
         const float yn = ys[t][c] * scale * a.norm_w[c];
         a.y[(int64_t)t * a.ldy + h * HD + c] = yn * z * (1.0f / (1.0f + expf(-z)));
     }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    ssm_batch_body<HD>(a, blockIdx.x, blockIdx.y);
 }
 
 // Prefill chunk of up to kChunkMax tokens of one request (GatedDeltaNetCPU,
@@ -1136,20 +1162,20 @@ struct GrpSmem {
     }
 };
 
-template <int HD>
-__global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int S) {
+// virtual block (bx, by, bz) of a grid with gz requests; tid < 256; gs its
+// shared memory (GrpSmem<HD>::bytes); BAR as in bar256
+template <int HD, int BAR>
+__device__ __forceinline__ void attn_part_body(AttnArgs a, int hg, int S, int bx, int by, int bz, int gz, int tid,
+                                               float *gs) {
     constexpr int KS = GrpSmem<HD>::KS;
     constexpr int RPT = (kGrpRows * HD + 255) / 256;  // P.V outputs per thread (upper bound)
-    extern __shared__ __align__(16) float gs[];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lane = tid & 31, warp = tid >> 5;
     const int N = a.N, ratio = a.nh / a.nkv, nrg = (ratio + hg - 1) / hg;
-    const int g = blockIdx.y / nrg, hb = blockIdx.y % nrg, h0 = g * ratio + hb * hg;
+    const int g = by / nrg, hb = by % nrg, h0 = g * ratio + hb * hg;
     const int R = min(hg, ratio - hb * hg) * N;
-    const int sl = blockIdx.x, b = blockIdx.z;
+    const int sl = bx, b = bz;
     float *q = gs, *kn = q + R * HD, *vn = kn + N * HD, *Ks = vn + N * HD, *Vs = Ks + kGrpKeys * KS;
     float *sc = Vs + kGrpKeys * HD, *ms = sc + R * kGrpKeys, *ls = ms + R, *fs = ls + R;
-    pdl_trigger();
-    pdl_wait();
     a.qkv += (int64_t)b * N * a.ldq;
     a.kc += b * a.b_kv;
     a.vc += b * a.b_kv;
@@ -1159,7 +1185,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
     if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
     const RopeSpec rs = rope_spec(a);
     const int qs = a.gated ? 2 : 1;
-    const int64_t rows_all = (int64_t)gridDim.z * a.nh * N, rid_base = ((int64_t)b * a.nh + h0) * N;
+    const int64_t rows_all = (int64_t)gz * a.nh * N, rid_base = ((int64_t)b * a.nh + h0) * N;
     if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
         // every key of this slice is outside every query's window (this
         // request's new keys are written by slice 0): an empty partial state
@@ -1187,7 +1213,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
         ms[tid] = -CUDART_INF_F;
         ls[tid] = 0.f;
     }
-    __syncthreads();
+    bar256<BAR>();
     for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
         if (rr >= R + N) {  // v rows: RMSNorm without weights (CommonOps.jl:43-53)
             float *x = vn + (rr - R - N) * HD;
@@ -1216,7 +1242,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
             x[i + rs.off] = x1 * s_ + x2 * c;
         }
     }
-    __syncthreads();
+    bar256<BAR>();
     // one CTA per (KV head, request) writes the new keys; no CTA reads them from the cache
     if (sl == 0 && hb == 0) {
         for (int i = tid; i < N * HD; i += 256) {
@@ -1258,7 +1284,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
                 *reinterpret_cast<float4 *>(Vs + jj * HD + d) = vv[l];
             }
         }
-        __syncthreads();
+        bar256<BAR>();
         {
             // thread (jj = lane, row group = warp): K row jj read once, q rows broadcast
             const int jj = lane, j = j0 + jj;
@@ -1287,7 +1313,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
                                                                                       : -CUDART_INF_F;
             }
         }
-        __syncthreads();
+        bar256<BAR>();
         for (int r = warp; r < R; r += 8) {
             const float sv = lane < kGrpKeys ? sc[r * kGrpKeys + lane] : -CUDART_INF_F;
             const float mo = ms[r], mn = fmaxf(mo, warp_max(sv));
@@ -1304,7 +1330,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
                 fs[r] = f;
             }
         }
-        __syncthreads();
+        bar256<BAR>();
         // thread: dim d = (tid + 256 k) % HD of row (tid + 256 k) / HD; V loaded once per key
 #pragma unroll
         for (int k = 0; k < RPT; k++) {
@@ -1326,11 +1352,11 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
                 }
             }
         }
-        __syncthreads();  // Ks, Vs, sc and fs are rewritten by the next chunk
+        bar256<BAR>();  // Ks, Vs, sc and fs are rewritten by the next chunk
     }
 
     // 3. the slice's partial state
-    const int64_t rows = (int64_t)gridDim.z * a.nh * N;
+    const int64_t rows = (int64_t)gz * a.nh * N;
     float *pm = a.part + (int64_t)sl * rows * (HD + 2), *pl = pm + rows, *po = pl + rows;
     const int64_t rid0 = ((int64_t)b * a.nh + h0) * N;  // row r of this CTA is row id rid0 + r
 #pragma unroll
@@ -1342,6 +1368,14 @@ __global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int 
         pm[rid0 + tid] = ms[tid];
         pl[rid0 + tid] = ls[tid];
     }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) attn_part_kernel(AttnArgs a, int hg, int S) {
+    extern __shared__ __align__(16) float gs[];
+    pdl_trigger();
+    pdl_wait();
+    attn_part_body<HD, 0>(a, hg, S, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z, threadIdx.x, gs);
 }
 
 // ---- split-KV attention on the tensor cores ----------------------------------
@@ -1543,7 +1577,15 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
         {   // scores: warp (m = warp / 4, key tile nb = warp % 4)
             const int m = warp >> 2, nb = warp & 3, r0 = 16 * m + g8;
             if (16 * m < R) {
-                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                // independent accumulators per k-step parity and product term:
+                // six short MMA dependency chains instead of one long one
+                float ac[2][3][4];
+#pragma unroll
+                for (int p2 = 0; p2 < 2; p2++)
+#pragma unroll
+                    for (int q3 = 0; q3 < 3; q3++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) ac[p2][q3][i] = 0.f;
                 const float *kr = kb + (8 * nb + g8) * KS;
 #pragma unroll 4
                 for (int kk = 0; kk < HD / 8; kk++) {
@@ -1560,8 +1602,15 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
                     uint32_t bh0, bl0, bh1, bl1;
                     split_tf32(kr[k0], bh0, bl0);
                     split_tf32(kr[k0 + 4], bh1, bl1);
-                    mma_3xtf32(acc, ah, al, bh0, bh1, bl0, bl1);
+                    const int p2 = kk & 1;
+                    mma_tf32(ac[p2][0], ah, bh0, bh1);
+                    mma_tf32(ac[p2][1], ah, bl0, bl1);
+                    mma_tf32(ac[p2][2], al, bh0, bh1);
                 }
+                float acc[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    acc[i] = (ac[0][0][i] + ac[1][0][i]) + ((ac[0][1][i] + ac[1][1][i]) + (ac[0][2][i] + ac[1][2][i]));
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     const int r = r0 + 8 * (i >> 1), jj = 8 * nb + 2 * t4 + (i & 1), j = j0 + jj;
@@ -1646,14 +1695,19 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
 // parallel in shared memory; thread group q (256 / HD groups) sums P.V over
 // slices q, q + 256 / HD, ... with independent loads in flight, and the groups'
 // sums are added in group order.
+// shared memory of one virtual block of the combine
 template <int HD>
-__global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch, int S) {
+struct CombineSmem {
+    float w[kMaxSplits], red[8], og[256 / HD][HD];
+};
+template <int HD, int BAR>
+__device__ __forceinline__ void attn_combine_body(AttnArgs a, int batch, int S, int64_t rid, int tid,
+                                                  CombineSmem<HD> &cs) {
     constexpr int NG = 256 / HD;
-    __shared__ float w[kMaxSplits], red[8], og[NG][HD];
-    pdl_trigger();
-    pdl_wait();
-    const int N = a.N, tid = threadIdx.x, d = tid % HD, q = tid / HD;
-    const int64_t rows = (int64_t)batch * a.nh * N, rid = blockIdx.x;
+    float *w = cs.w, *red = cs.red;
+    auto &og = cs.og;
+    const int N = a.N, d = tid % HD, q = tid / HD;
+    const int64_t rows = (int64_t)batch * a.nh * N;
     const int t = (int)(rid % N), h = (int)((rid / N) % a.nh), b = (int)(rid / ((int64_t)N * a.nh));
     const int nkeys = a.pos[(int64_t)b * a.b_pos] + N, kps = attn_kps(nkeys, S);
     const int ns = (nkeys + kps - 1) / kps;
@@ -1666,13 +1720,13 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch
     // block max of m (ns <= kMaxSplits <= 256)
     float M = warp_max(mv);
     if ((tid & 31) == 0) red[tid >> 5] = M;
-    __syncthreads();
+    bar256<BAR>();
     M = red[0];
 #pragma unroll
     for (int i = 1; i < 8; i++) M = fmaxf(M, red[i]);
     const float wv = mv == -CUDART_INF_F ? 0.f : expf(mv - M);
     if (tid < ns) w[tid] = wv;
-    const float L = block_sum256(lv * wv, red);  // synchronises: w visible
+    const float L = block_sum256_b<BAR>(lv * wv, red, tid);  // synchronises: w visible
     const float *po = a.part + 2 * rows + rid * HD + d;
     float O = 0.f;
     int sl = q;
@@ -1687,7 +1741,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch
     for (; sl < ns; sl += NG) O += w[sl] * po[sl * stride];
     if (NG > 1) {
         og[q][d] = O;
-        __syncthreads();
+        bar256<BAR>();
         if (q) return;
         O = og[0][d];
 #pragma unroll
@@ -1700,6 +1754,14 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch
         y *= 1.0f / (1.0f + expf(-gv));
     }
     a.out[tok * a.ldo + (int64_t)h * HD + d] = y;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a, int batch, int S) {
+    __shared__ CombineSmem<HD> cs;
+    pdl_trigger();
+    pdl_wait();
+    attn_combine_body<HD, 0>(a, batch, S, blockIdx.x, threadIdx.x, cs);
 }
 
 static int split_heads(int ratio, int N) { return std::max(1, std::min(ratio, kGrpRows / N)); }
@@ -1832,3 +1894,5 @@ void set_token(int32_t *dst, const int32_t *src, cudaStream_t s) {
 }
 
 }  // namespace ifr
+
+#include "fused_step.cuh"

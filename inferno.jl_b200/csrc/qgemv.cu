@@ -4,6 +4,7 @@
 //
 // Replaces q4_k_gemv .. q8_0_gemv (reference src/kernels/quant_kernels.c:602-697).
 #include "common.cuh"
+#include "fused.cuh"
 
 namespace ifr {
 
@@ -27,14 +28,15 @@ cudaError_t qgemm_small(const QTensor &T, const float *X, int ncols, float *Y, b
 
 // the flags of every format's kernels and of the dense kernel, read and cleared
 cudaError_t read_device_error(int *flag, cudaStream_t s) {
-    int f[5] = {0, 0, 0, 0, 0};
+    int f[6] = {0, 0, 0, 0, 0, 0};
     cudaError_t e = read_dev_error_fmt<12>(&f[0], s);
     if (e == cudaSuccess) e = read_dev_error_fmt<13>(&f[1], s);
     if (e == cudaSuccess) e = read_dev_error_fmt<14>(&f[2], s);
     if (e == cudaSuccess) e = read_dev_error_fmt<8>(&f[3], s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) e = read_fused_error(&f[5], s);
     if (e == cudaSuccess) e = read_mma_error(&f[4], s);
-    *flag = (f[0] | f[1] | f[2] | f[3] | f[4]) ? 1 : 0;
+    *flag = (f[0] | f[1] | f[2] | f[3] | f[4] | f[5]) ? 1 : 0;
     return e;
 }
 

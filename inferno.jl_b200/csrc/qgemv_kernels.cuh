@@ -175,17 +175,22 @@ IFR_DEV float h2_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned
 
 // 8 runs of 4 floats at p + k0 + i * step (0 beyond K or when !has).  No
 // value is used here, so every load of the 8 runs is in flight at once.
+// NC: through the read-only path (data no thread of the launch writes);
+// false for activations that earlier phases of the same launch produced
+template <bool NC = true>
 IFR_DEV void ld_runs(const float *p, int64_t K, int64_t k0, int step, bool has, float4 (&r)[8]) {
+    auto ld4 = [](const float *q) { return NC ? __ldg(reinterpret_cast<const float4 *>(q)) : *reinterpret_cast<const float4 *>(q); };
+    auto ld1 = [](const float *q) { return NC ? __ldg(q) : *q; };
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int64_t k = k0 + (int64_t)step * i;
         r[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (has && k + 3 < K) {
-            r[i] = __ldg(reinterpret_cast<const float4 *>(p + k));
+            r[i] = ld4(p + k);
         } else if (has) {  // ragged K: the rare scalar path
-            if (k < K) r[i].x = __ldg(p + k);
-            if (k + 1 < K) r[i].y = __ldg(p + k + 1);
-            if (k + 2 < K) r[i].z = __ldg(p + k + 2);
+            if (k < K) r[i].x = ld1(p + k);
+            if (k + 1 < K) r[i].y = ld1(p + k + 1);
+            if (k + 2 < K) r[i].z = ld1(p + k + 2);
         }
     }
 }
@@ -237,8 +242,10 @@ IFR_DEV void load_x32(const GemvArgs &a, const float *inv, int col, int64_t k0, 
 }
 
 // Builds n-tile nt of unit u's fragments into `unit` (bunit_words(NT) words).
-// ssq (XF 3, may be null): [unit][8] sums of x^2 of the unit's activations
-template <int FMT, int NT, int XF>
+// ssq (XF 3, may be null): [unit][8] sums of x^2 of the unit's activations.
+// COH: the activations are read with coherent loads (the fused launch, whose
+// earlier phases wrote them)
+template <int FMT, int NT, int XF, bool COH = false>
 IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, int nt, uint32_t *unit, float *ssq) {
     const int g = lane >> 2, t = lane & 3, part = g & 1;
     // this lane's steps 8 part .. 8 part + 7 (elem_s() of tiles.cuh): every load
@@ -251,7 +258,7 @@ IFR_DEV void build_b(const GemvArgs &a, const float *inv, int64_t u, int lane, i
         load_x32<XF>(a, inv, col, k0, 16, col < a.ncols, v, &ss);
     } else {
         float4 xr[8], wr[8];
-        ld_runs(a.X + (int64_t)col * a.ldx, a.K, k0, 16, col < a.ncols, xr);
+        ld_runs<!COH>(a.X + (int64_t)col * a.ldx, a.K, k0, 16, col < a.ncols, xr);
         if (XF == 1 || XF == 3) ld_runs(a.xw, a.K, k0, 16, true, wr);
         xform_runs<XF>(xr, wr, XF == 1 && col < a.ncols ? inv[col] : 0.f, v, &ss);
     }
@@ -1436,6 +1443,7 @@ static cudaError_t launch_fmt(const QTensor &T, const float *X, int ncols, float
     return cudaErrorInvalidValue;
 }
 
+#ifdef IFR_QGEMV_FMT
 // this translation unit's weight format (qgemv_q4k.cu .. qgemv_q80.cu)
 template <>
 cudaError_t qgemm_small_fmt<IFR_QGEMV_FMT>(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate,
@@ -1449,5 +1457,6 @@ cudaError_t read_dev_error_fmt<IFR_QGEMV_FMT>(int *flag, cudaStream_t s) {
     if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
     return e;
 }
+#endif  // IFR_QGEMV_FMT
 
 }  // namespace ifr

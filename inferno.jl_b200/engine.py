@@ -166,7 +166,8 @@ class State:
     def profile(self, enable=True):
         check(load().ifr_state_profile(self.handle, 1 if enable else 0))
 
-    CATEGORIES = ("lm_head", "draft_lm_head", "layer_gemv", "draft_gemv", "ssm", "attention", "allreduce")
+    CATEGORIES = ("lm_head", "draft_lm_head", "layer_gemv", "draft_gemv", "ssm", "attention", "allreduce",
+                  "fused_layers")
 
     def profile_read(self):
         ms = (ctypes.c_double * 8)()
@@ -176,6 +177,20 @@ class State:
         check(load().ifr_state_profile_read(self.handle, ms, by, ct, ctypes.byref(nl)))
         out = {c: dict(ms=ms[i], bytes=by[i], count=ct[i]) for i, c in enumerate(self.CATEGORIES)}
         return out, nl.value
+
+    FUSED_KINDS = {1: "projection", 2: "ssm", 3: "attn_slices", 4: "attn_combine", 5: "ssm_final"}
+
+    def fused_trace(self, max_phases=1024):
+        """[(phase kind, total, fragments, tiles, epilogue, barrier, slowest CTA)]
+        in us of the last fused layer-stack launch traced while profiling
+        (empty when none); total = from the phase's start to the next's"""
+        kinds = (ctypes.c_int * max_phases)()
+        us = (ctypes.c_double * (6 * max_phases))()
+        n = ctypes.c_int()
+        check(load().ifr_state_fused_trace(self.handle, max_phases, kinds, us, ctypes.byref(n)))
+        k = n.value
+        self.fused_barriers = [tuple(us[6 * k + 4 * i:6 * k + 4 * i + 4]) for i in range(k)] if max_phases >= 2 * k else []
+        return [(self.FUSED_KINDS.get(kinds[i], str(kinds[i])),) + tuple(us[6 * i:6 * i + 6]) for i in range(k)]
 
     def gemv_pass(self, ncols):
         """enqueue the verify's dequant-GEMV launches alone (scratch activations)"""
