@@ -368,7 +368,20 @@ __device__ void ssm_split_body(const SsmArgs &a, int h, int j, float *ssq_part, 
     }
     // 3. the previous call's replay record: k (every dim), own v rows, decay, beta
     const float *rec = a.rkv + (int64_t)h * kMaxN * REC;
-    for (int i = tid; i < r * HD; i += kFThreads) m.rk[i / HD][i % HD] = rec[(i / HD) * REC + i % HD];
+    {
+        constexpr int LPT = kMaxN * HD / kFThreads;
+        float kr[LPT];
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + kFThreads * k;
+            kr[k] = i < r * HD ? rec[(i / HD) * REC + i % HD] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + kFThreads * k;
+            if (i < r * HD) m.rk[i / HD][i % HD] = kr[k];
+        }
+    }
     if (tid < r * RPC) m.rv[tid / RPC][tid % RPC] = rec[(tid / RPC) * REC + HD + r0 + tid % RPC];
     if (tid < r) {
         m.rdec[tid] = rec[tid * REC + 2 * HD];

@@ -283,9 +283,23 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
             ab_part[which][t] = v;
         }
     }
-    // 3. the previous call's replay record: k (all dims), own v rows, decay, beta
+    // 3. the previous call's replay record: k (all dims), own v rows, decay,
+    //    beta (a thread's loads issued before its shared stores)
     float *rec = a.rkv + (int64_t)h * kMaxN * REC;
-    for (int i = tid; i < r * HD; i += 256) rk[i / HD][i % HD] = rec[(i / HD) * REC + i % HD];
+    {
+        constexpr int LPT = (kMaxN * HD + 255) / 256;
+        float kr[LPT];
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + 256 * k;
+            kr[k] = i < r * HD ? rec[(i / HD) * REC + i % HD] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + 256 * k;
+            if (i < r * HD) rk[i / HD][i % HD] = kr[k];
+        }
+    }
     for (int i = tid; i < r * RPC; i += 256) rv[i / RPC][i % RPC] = rec[(i / RPC) * REC + HD + r0 + i % RPC];
     if (tid < r) {
         rdec[tid] = rec[tid * REC + 2 * HD];
@@ -294,10 +308,23 @@ __global__ void __cluster_dims__(kSsmSplit, 1, 1) __launch_bounds__(256) ssm_ste
     cluster.sync();  // conv slices visible to the cluster; old record read by all
     // 4. the head's q and k, gathered from the owners; alpha / beta summed over
     //    the cluster's slices
-    for (int i = tid; i < N * HD; i += 256) {
-        const int t = i / HD, c = i % HD, src = c / RPC, ci = c % RPC;
-        xq[t][c] = cluster.map_shared_rank(&cq[0][0], src)[t * RPC + ci];
-        xk[t][c] = cluster.map_shared_rank(&ck[0][0], src)[t * RPC + ci];
+    {
+        constexpr int LPT = (kMaxN * HD + 255) / 256;
+        float gq[LPT], gk[LPT];
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + 256 * k, t = i / HD, c = i % HD, src = c / RPC, ci = c % RPC;
+            gq[k] = i < N * HD ? cluster.map_shared_rank(&cq[0][0], src)[t * RPC + ci] : 0.f;
+            gk[k] = i < N * HD ? cluster.map_shared_rank(&ck[0][0], src)[t * RPC + ci] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + 256 * k, t = i / HD, c = i % HD;
+            if (i < N * HD) {
+                xq[t][c] = gq[k];
+                xk[t][c] = gk[k];
+            }
+        }
     }
     if (tid < 3 * N) {
         const int which = tid / N, t = tid % N;
@@ -975,13 +1002,36 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
     const RopeSpec rs = rope_spec(a);
     const int qs = a.gated ? 2 : 1;  // q rows per head: [q; gate] or q
 
-    // 1. q of this head, new k and v of its KV head; RMSNorm + RoPE (warp t = token t)
-    for (int i = tid; i < N * HD; i += 256) {
-        const int t = i / HD, d = i % HD;
-        const float *row = a.qkv + (int64_t)t * a.ldq;
-        q[t][d] = row[(int64_t)h * qs * HD + d];
-        kn[t][d] = row[(int64_t)a.nh * qs * HD + kvh * HD + d];
-        vn[t][d] = row[(int64_t)a.nh * qs * HD + a.nkv * HD + kvh * HD + d];
+    // 1. q of this head, new k and v of its KV head; RMSNorm + RoPE (warp t =
+    //    token t).  A thread's loads are all issued before its shared stores,
+    //    and the norm weights are held in registers.
+    {
+        constexpr int LPT = (kMaxN * HD + 255) / 256;
+        float qv[LPT], kv[LPT], vv[LPT];
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + 256 * k, t = i / HD, d = i % HD;
+            const float *row = a.qkv + (int64_t)t * a.ldq;
+            const bool in = i < N * HD;
+            qv[k] = in ? row[(int64_t)h * qs * HD + d] : 0.f;
+            kv[k] = in ? row[(int64_t)a.nh * qs * HD + kvh * HD + d] : 0.f;
+            vv[k] = in ? row[(int64_t)a.nh * qs * HD + a.nkv * HD + kvh * HD + d] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LPT; k++) {
+            const int i = tid + 256 * k, t = i / HD, d = i % HD;
+            if (i < N * HD) {
+                q[t][d] = qv[k];
+                kn[t][d] = kv[k];
+                vn[t][d] = vv[k];
+            }
+        }
+    }
+    float qw[HD / 32], kw[HD / 32];
+#pragma unroll
+    for (int e = 0; e < HD / 32; e++) {
+        qw[e] = a.q_norm[lane + 32 * e];
+        kw[e] = a.k_norm[lane + 32 * e];
     }
     if (tid < kMaxN) {
         ms[tid] = -CUDART_INF_F;
@@ -998,9 +1048,11 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(256) attn_s
         sq = warp_sum(sq);
         sk = warp_sum(sk);
         const float iq = 1.0f / sqrtf(sq / (float)HD + a.eps), ik = 1.0f / sqrtf(sk / (float)HD + a.eps);
-        for (int d = lane; d < HD; d += 32) {
-            q[t][d] = q[t][d] * iq * a.q_norm[d];
-            kn[t][d] = kn[t][d] * ik * a.k_norm[d];
+#pragma unroll
+        for (int e = 0; e < HD / 32; e++) {
+            const int d = lane + 32 * e;
+            q[t][d] = q[t][d] * iq * qw[e];
+            kn[t][d] = kn[t][d] * ik * kw[e];
         }
         if (a.vnorm) {  // rmsnorm_no_scale! (CommonOps.jl:43-53)
             float sv = 0.f;
@@ -1162,6 +1214,103 @@ struct GrpSmem {
     }
 };
 
+// Step 1 of the split-KV attention of a row group (both split kernels): its
+// R = heads x N q rows and the N new k, v rows into shared memory (q [R][HD],
+// kn / vn [N][HD]), then per row (warp per row) RMSNorm with its weights, RoPE
+// for q and k, the weightless RMSNorm of v when vnorm (CommonOps.jl:43-53).
+// Every global load of a thread is issued before its shared stores (the
+// stores cannot be ordered past loads through a generic pointer otherwise),
+// the norm weights sit in registers and the N positions' RoPE tables are
+// staged in rope_s (2 N pairs floats) first.  BAR as in bar256.
+template <int HD, int BAR>
+__device__ __forceinline__ void attn_rows_in(const AttnArgs &a, float *q, float *kn, float *vn, float *rope_s, int R,
+                                             int h0, int g, int p0, int tid) {
+    constexpr int LB = 8;  // loads in flight per thread per batch
+    const int N = a.N, lane = tid & 31, warp = tid >> 5, qs = a.gated ? 2 : 1;
+    const RopeSpec rs = rope_spec(a);
+    for (int i0 = tid; i0 < R * HD; i0 += 256 * LB) {
+        float v[LB];
+#pragma unroll
+        for (int k = 0; k < LB; k++) {
+            const int i = i0 + 256 * k, r = i / HD, d = i % HD, hh = r / N, t = r % N;
+            v[k] = i < R * HD ? a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * qs * HD + d] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LB; k++)
+            if (i0 + 256 * k < R * HD) q[i0 + 256 * k] = v[k];
+    }
+    for (int i0 = tid; i0 < N * HD; i0 += 256 * LB) {
+        float kv[LB], vv[LB];
+#pragma unroll
+        for (int k = 0; k < LB; k++) {
+            const int i = i0 + 256 * k, t = i / HD, d = i % HD;
+            const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * qs * HD;
+            kv[k] = i < N * HD ? row[g * HD + d] : 0.f;
+            vv[k] = i < N * HD ? row[a.nkv * HD + g * HD + d] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LB; k++)
+            if (i0 + 256 * k < N * HD) {
+                kn[i0 + 256 * k] = kv[k];
+                vn[i0 + 256 * k] = vv[k];
+            }
+    }
+    for (int i0 = tid; i0 < N * rs.pairs; i0 += 256 * LB) {
+        float c[LB], sn[LB];
+#pragma unroll
+        for (int k = 0; k < LB; k++) {
+            const int i = i0 + 256 * k, t = i / rs.pairs, pi = i % rs.pairs;
+            const int64_t o = (int64_t)(p0 + t) * rs.ld + pi;
+            c[k] = i < N * rs.pairs ? a.rope_cos[o] : 0.f;
+            sn[k] = i < N * rs.pairs ? a.rope_sin[o] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < LB; k++)
+            if (i0 + 256 * k < N * rs.pairs) {
+                rope_s[i0 + 256 * k] = c[k];
+                rope_s[N * rs.pairs + i0 + 256 * k] = sn[k];
+            }
+    }
+    float qw[HD / 32], kw[HD / 32];
+#pragma unroll
+    for (int j = 0; j < HD / 32; j++) {
+        qw[j] = a.q_norm[lane + 32 * j];
+        kw[j] = a.k_norm[lane + 32 * j];
+    }
+    bar256<BAR>();
+    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
+        if (rr >= R + N) {
+            float *x = vn + (rr - R - N) * HD;
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < HD / 32; j++) ss += x[lane + 32 * j] * x[lane + 32 * j];
+            ss = warp_sum(ss);
+            const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+            for (int j = 0; j < HD / 32; j++) x[lane + 32 * j] = x[lane + 32 * j] * iv;
+            continue;
+        }
+        const bool isq = rr < R;
+        float *x = isq ? q + rr * HD : kn + (rr - R) * HD;
+        const int t = isq ? rr % N : rr - R;
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < HD / 32; j++) ss += x[lane + 32 * j] * x[lane + 32 * j];
+        ss = warp_sum(ss);
+        const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < HD / 32; j++) x[lane + 32 * j] = x[lane + 32 * j] * iv * (isq ? qw[j] : kw[j]);
+        __syncwarp();
+        const float *cs = rope_s + t * rs.pairs, *sn = rope_s + (N + t) * rs.pairs;
+        for (int i = lane; i < rs.pairs; i += 32) {
+            const float c = cs[i], s_ = sn[i];
+            const float x1 = x[i], x2 = x[i + rs.off];
+            x[i] = x1 * c - x2 * s_;
+            x[i + rs.off] = x1 * s_ + x2 * c;
+        }
+    }
+}
+
 // virtual block (bx, by, bz) of a grid with gz requests; tid < 256; gs its
 // shared memory (GrpSmem<HD>::bytes); BAR as in bar256
 template <int HD, int BAR>
@@ -1198,50 +1347,13 @@ __device__ __forceinline__ void attn_part_body(AttnArgs a, int hg, int S, int bx
         return;
     }
 
-    // 1. the row group's q rows, the new k and v; RMSNorm + RoPE (warp per row)
-    for (int i = tid; i < R * HD; i += 256) {
-        const int r = i / HD, d = i % HD, hh = r / N, t = r % N;
-        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * qs * HD + d];
-    }
-    for (int i = tid; i < N * HD; i += 256) {
-        const int t = i / HD, d = i % HD;
-        const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * qs * HD;
-        kn[i] = row[g * HD + d];
-        vn[i] = row[a.nkv * HD + g * HD + d];
-    }
+    // 1. the row group's q rows, the new k and v; RMSNorm + RoPE (warp per row);
+    //    the RoPE tables staged in the K chunk buffer (free until step 2)
     if (tid < R) {
         ms[tid] = -CUDART_INF_F;
         ls[tid] = 0.f;
     }
-    bar256<BAR>();
-    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
-        if (rr >= R + N) {  // v rows: RMSNorm without weights (CommonOps.jl:43-53)
-            float *x = vn + (rr - R - N) * HD;
-            float ss = 0.f;
-            for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
-            ss = warp_sum(ss);
-            const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-            for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv;
-            continue;
-        }
-        const bool isq = rr < R;
-        float *x = isq ? q + rr * HD : kn + (rr - R) * HD;
-        const float *w = isq ? a.q_norm : a.k_norm;
-        const int t = isq ? rr % N : rr - R;
-        float ss = 0.f;
-        for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
-        ss = warp_sum(ss);
-        const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-        for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv * w[d];
-        __syncwarp();
-        const float *cs = a.rope_cos + (int64_t)(p0 + t) * rs.ld, *sn = a.rope_sin + (int64_t)(p0 + t) * rs.ld;
-        for (int i = lane; i < rs.pairs; i += 32) {
-            const float c = cs[i], s_ = sn[i];
-            const float x1 = x[i], x2 = x[i + rs.off];
-            x[i] = x1 * c - x2 * s_;
-            x[i + rs.off] = x1 * s_ + x2 * c;
-        }
-    }
+    attn_rows_in<HD, BAR>(a, q, kn, vn, Ks, R, h0, g, p0, tid);
     bar256<BAR>();
     // one CTA per (KV head, request) writes the new keys; no CTA reads them from the cache
     if (sl == 0 && hb == 0) {
@@ -1492,50 +1604,13 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
     };
     const int nch = (hi - lo + kGrpKeys - 1) / kGrpKeys;
 
-    // 1. the new k and v rows and the row group's q rows; RMSNorm + RoPE
-    for (int i = tid; i < N * HD; i += 256) {
-        const int t = i / HD, d = i % HD;
-        const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * qs * HD;
-        kn[i] = row[g * HD + d];
-        vn[i] = row[a.nkv * HD + g * HD + d];
-    }
-    for (int i = tid; i < R * HD; i += 256) {
-        const int r = i / HD, d = i % HD, hh = r / N, t = r % N;
-        q[i] = a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * qs * HD + d];
-    }
+    // 1. the new k and v rows and the row group's q rows; RMSNorm + RoPE (the
+    //    RoPE tables staged in the second K buffer, free until chunk 1)
     if (tid < R) {
         ms[tid] = -CUDART_INF_F;
         ls[tid] = 0.f;
     }
-    __syncthreads();
-    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
-        if (rr >= R + N) {  // v rows: RMSNorm without weights (CommonOps.jl:43-53)
-            float *x = vn + (rr - R - N) * HD;
-            float ss = 0.f;
-            for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
-            ss = warp_sum(ss);
-            const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-            for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv;
-            continue;
-        }
-        const bool isq = rr < R;
-        float *x = isq ? q + rr * HD : kn + (rr - R) * HD;
-        const float *w = isq ? a.q_norm : a.k_norm;
-        const int t = isq ? rr % N : rr - R;
-        float ss = 0.f;
-        for (int d = lane; d < HD; d += 32) ss += x[d] * x[d];
-        ss = warp_sum(ss);
-        const float iv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-        for (int d = lane; d < HD; d += 32) x[d] = x[d] * iv * w[d];
-        __syncwarp();
-        const float *cs = a.rope_cos + (int64_t)(p0 + t) * rs.ld, *sn = a.rope_sin + (int64_t)(p0 + t) * rs.ld;
-        for (int i = lane; i < rs.pairs; i += 32) {
-            const float c = cs[i], s_ = sn[i];
-            const float x1 = x[i], x2 = x[i + rs.off];
-            x[i] = x1 * c - x2 * s_;
-            x[i + rs.off] = x1 * s_ + x2 * c;
-        }
-    }
+    attn_rows_in<HD, 0>(a, q, kn, vn, Ks + kGrpKeys * KS, R, h0, g, p0, tid);
     __syncthreads();
     // the first chunk's copies start now; the new keys are in kn / vn for it
     stage(0, 0);
