@@ -457,15 +457,16 @@ __device__ __forceinline__ void ssm_batch_body(SsmArgs a, int h, int64_t b) {
         a.a_prev += b * a.b_prev;
     }
     const int r = min(max(*a.a_prev + 1, 0), kMaxN);  // tokens to replay
-    // the state rows, loaded first (their memory latency overlaps steps 1-5):
-    // thread (row = tid / 4, lc = tid % 4) owns columns 16 e + 4 lc + v of row
-    // `row`, read as 16-byte vectors (a warp reads 64 contiguous bytes per row)
+    // thread (row = tid / 4, lc = tid % 4) owns columns 16 e + 4 lc + v of
+    // state row `row`, read as 16-byte vectors (a warp reads 64 contiguous
+    // bytes per row) once steps 1-5 are done: two CTAs share an SM, so one's
+    // state traffic overlaps the other's arithmetic
     const int row = tid >> 2, lc = tid & 3;
     float4 *Sp = reinterpret_cast<float4 *>(a.S + ((int64_t)h * HD + row) * HD + 4 * lc);
-    float4 sv[CPT / 4];
-#pragma unroll
-    for (int e = 0; e < CPT / 4; e++) sv[e] = Sp[4 * e];
-    // 1. conv of the head's channels (ssm_step_kernel step 1)
+    // 1. conv of the head's channels (ssm_step_kernel step 1): the window
+    //    (committed history K-1, replayed r, new N) read once into registers;
+    //    element r + j of it is the new committed history j, element K-1+r+t
+    //    the new token t's input
     auto win = [&](int i, int ch) -> const float * {
         if (i < K - 1) return a.hist + (int64_t)i * C + ch;
         if (i < K - 1 + r) return a.rq + (int64_t)(i - K + 1) * C + ch;
@@ -474,28 +475,22 @@ __device__ __forceinline__ void ssm_batch_body(SsmArgs a, int h, int64_t b) {
     if (tid < 3 * HD) {
         const int part = tid / HD, i = tid % HD;
         const int ch = part * qk + h * HD + i;
-        float w[4], tap[kMaxN][4], nh[3], pv[kMaxN];
+        float w[4], wv[kMaxN + 3];
 #pragma unroll
         for (int k = 0; k < 4; k++) w[k] = k < K ? a.conv_w[(int64_t)ch * K + k] : 0.f;
 #pragma unroll
-        for (int t = 0; t < kMaxN; t++) {
-            pv[t] = t < N ? a.proj[(int64_t)t * a.ldp + ch] : 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; k++) tap[t][k] = (t < N && k < K) ? *win(r + t + k, ch) : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 3; j++) nh[j] = j < K - 1 ? *win(r + j, ch) : 0.f;
+        for (int j = 0; j < kMaxN + 3; j++) wv[j] = j < N + K - 1 ? *win(r + j, ch) : 0.f;
 #pragma unroll
         for (int j = 0; j < 3; j++)
-            if (j < K - 1) a.hist[(int64_t)j * C + ch] = nh[j];
+            if (j < K - 1) a.hist[(int64_t)j * C + ch] = wv[j];
 #pragma unroll
         for (int t = 0; t < kMaxN; t++) {
             if (t < N) {
-                a.rq[(int64_t)t * C + ch] = pv[t];
+                a.rq[(int64_t)t * C + ch] = wv[K - 1 + t];
                 float acc = 0.f;
 #pragma unroll
                 for (int k = 0; k < 4; k++)
-                    if (k < K) acc += tap[t][k] * w[k];
+                    if (k < K) acc += wv[t + k] * w[k];
                 const float o = acc / (1.0f + expf(-acc));
                 if (part == 0) xq[t][i] = o;
                 else if (part == 1) xk[t][i] = o;
@@ -592,7 +587,10 @@ __device__ __forceinline__ void ssm_batch_body(SsmArgs a, int h, int64_t b) {
         rec[tid * REC + 2 * HD] = ndec[tid];
         rec[tid * REC + 2 * HD + 1] = nbeta[tid];
     }
-    // 6. the state rows (loaded at the start) through the replayed and new tokens
+    // 6. the state rows through the replayed and new tokens
+    float4 sv[CPT / 4];
+#pragma unroll
+    for (int e = 0; e < CPT / 4; e++) sv[e] = Sp[4 * e];
     auto update = [&](const float *kv, float dec, float beta, float vrow) {
         float sk = 0.f;
 #pragma unroll
@@ -656,7 +654,7 @@ __device__ __forceinline__ void ssm_batch_body(SsmArgs a, int h, int64_t b) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(4 * HD) ssm_batch_kernel(SsmArgs a) {
+__global__ void __launch_bounds__(4 * HD, 2) ssm_batch_kernel(SsmArgs a) {
     pdl_trigger();
     pdl_wait();
     ssm_batch_body<HD>(a, blockIdx.x, blockIdx.y);
@@ -911,6 +909,9 @@ cudaError_t ssm_chunk(const SsmArgs &a, int head_dim, cudaStream_t s) {
 
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s) {
     if (a.N < 1 || a.N > kMaxN || a.K < 1 || a.K > 4 || batch < 1) return cudaErrorInvalidValue;
+    // batches: one CTA per (head, request), two per SM (the cluster kernel with
+    // kSsmSplit CTAs per head and request measured 42.9 against 31.7 ms per
+    // config-4 step)
     if (batch > 1) {
         const dim3 grid(a.H, batch);
         if (head_dim == 128) return launch_k(ssm_batch_kernel<128>, grid, dim3(512), 0, s, a);
