@@ -1111,6 +1111,65 @@ def run_profile(args):
     pkg = ge.load_package()
     pkg.load()
     torch.cuda.set_device(0)
+    if args.profile == "fused":
+        import ctypes
+        # the config-1 verify's decoder layers as one persistent launch
+        # (ifr_ctx_set_fused_layers): per-phase times from the kernel's own
+        # global-timer trace over 10 eager spec steps, and the step time of
+        # both paths as CUDA graphs
+        from inferno_b200 import synth
+        from inferno_b200.engine import Model, State
+        ctx = pkg.Context(0, torch_stream=False)
+        model = Model(ctx, synth.cached(SPEC_PRESET, SPEC_SEED))
+        prompt = synth.prompt(model.info.vocab, SPEC_PROMPT, SPEC_SEED)
+        ctx.set_fused_layers(True)
+        st = State(model, SPEC_PROMPT + 160)
+        st.prefill(prompt)
+        for _ in range(3):
+            st.spec_step(args.gamma)
+        st.profile(True)
+        traces, bars = [], []
+        for _ in range(10):
+            st.spec_step(args.gamma)
+            traces.append(st.fused_trace())
+            bars.append(st.fused_barriers)
+        st.free()
+        kinds = [t[0] for t in traces[0]]
+        A = np.array([[t[1:] for t in tr] for tr in traces])
+        Bm = np.array(bars)
+        out = {"profile": "fused", "phases": len(kinds), "layer_stack_us": round(float(A[:, :, 0].sum(1).mean()), 1)}
+        cols = ["us", "slowest_cta_fragments", "slowest_cta_tiles", "slowest_cta_rest", "slowest_cta_to_next",
+                "slowest_cta_whole"]
+        for k in sorted(set(kinds)):
+            idx = [i for i, kk in enumerate(kinds) if kk == k]
+            m = A[:, idx].mean((0, 1))
+            out[k] = {"phases": len(idx), **{c: round(float(v), 2) for c, v in zip(cols, m)},
+                      "barrier": {c: round(float(v), 2) for c, v in zip(
+                          ["arrival_skew", "propagation", "acquire", "to_next_start"], Bm[:, idx].mean((0, 1)))}}
+        step = {}
+        for fused in (1, 0):
+            ctx.set_fused_layers(bool(fused))
+            st = State(model, SPEC_PROMPT + 160)
+            st.prefill(prompt)
+            st.spec_step(args.gamma)
+            st.capture(args.gamma, 1)
+            for _ in range(3):
+                st.launch()
+            ctx.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            sp = ctypes.c_void_p()
+            pkg.check(pkg.load().ifr_ctx_get_stream(ctx.handle, ctypes.byref(sp)))
+            stream = torch.cuda.ExternalStream(sp.value)
+            e0.record(stream)
+            for _ in range(20):
+                st.launch()
+            e1.record(stream)
+            e1.synchronize()
+            step["fused" if fused else "separate"] = round(e0.elapsed_time(e1) / 20, 4)
+            st.free()
+        out["graph_step_ms"] = step
+        print(json.dumps(out))
+        return
     if args.profile == "spec":
         from inferno_b200 import synth
         from inferno_b200.engine import Model, State
@@ -1191,7 +1250,8 @@ def main():
     ap.add_argument("--act", type=int, default=None, choices=[0, 1],
                     help="K-quant GEMV activations: 0 = exact f32 (default of the model workloads), "
                          "1 = Q8_K (the reference's kernels; default of the sweep)")
-    ap.add_argument("--profile", choices=["spec", "qgemv", "dense", "batch"], help="small case for ncu (no JSON line)")
+    ap.add_argument("--profile", choices=["spec", "qgemv", "dense", "batch", "fused"],
+                    help="small case for ncu (no JSON line); fused: the fused layer stack's phase trace")
     ap.add_argument("--preset", default=None, help="--profile batch: model preset (default: the config-4 model)")
     ap.add_argument("--qtype", default="Q4_K")
     ap.add_argument("--shape", default="65536x4096")

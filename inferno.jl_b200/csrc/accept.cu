@@ -12,9 +12,9 @@
 // Every float operation uses the _rn intrinsics so nothing is contracted into
 // an FMA behind our back; exp is ifr_exp below (the oracle's or_exp).
 //
-// Launches: chunk_stats (one warp per row chunk, the only full pass over the
+// Launches: chunk_stats (one CTA per row chunk, the only full pass over the
 // logits), row_decide (per sequence and row: row stats, draft draw, ratio
-// test), resid_chunks (one warp per chunk of each sequence's rejected row:
+// test), resid_chunks (one CTA per chunk of each sequence's rejected row:
 // residual chunk sums), finish (per sequence: residual or bonus sample).
 #include "common.cuh"
 #include <math_constants.h>
@@ -97,42 +97,6 @@ __device__ float canon_sum(float t, float *wsum /* smem [8] */) {
     return s;
 }
 
-// One warp forms a whole chunk's canonical statistics: lane l plays lanes
-// l + 32 v (v < 8) of the 256-lane order, so each virtual warp v's butterfly
-// runs over the real warp's lanes and the 8 results are added left to right -
-// the same operations, in the same order, as canon_sum over 256 threads.
-// load8w: the 8 elements of virtual lane l + 32 v of chunk c (-inf past V)
-__device__ __forceinline__ int load8w(const float *row, int V, int c, int v, float (&x)[8]) {
-    const int64_t b = (int64_t)c * kCH + kPER * (threadIdx.x % 32 + 32 * v);
-    int n = 0;
-    if (b + kPER <= V && (V & 3) == 0) {
-        const float4 *p = reinterpret_cast<const float4 *>(row + b);
-        const float4 a = __ldg(p), d = __ldg(p + 1);
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-        x[4] = d.x; x[5] = d.y; x[6] = d.z; x[7] = d.w;
-        n = kPER;
-    } else {
-#pragma unroll
-        for (int q = 0; q < kPER; q++) {
-            if (b + q < V) { x[q] = __ldg(row + b + q); n = q + 1; }
-            else x[q] = -CUDART_INF_F;
-        }
-    }
-    return n;
-}
-// the canonical sum of the 8 virtual warps' lane partials t[v]
-__device__ __forceinline__ float canon_sum_warp(const float (&t)[8]) {
-    float s = 0.f;
-#pragma unroll
-    for (int v = 0; v < 8; v++) {
-        float w = t[v];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) w = __fadd_rn(w, __shfl_xor_sync(0xffffffffu, w, off));
-        s = v == 0 ? w : __fadd_rn(s, w);
-    }
-    return s;
-}
-
 __device__ float block_max(float m, float *wbuf) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -177,48 +141,35 @@ __device__ __forceinline__ int load8(const float *row, int V, int c, float (&x)[
 template <bool FILT>
 __global__ void __launch_bounds__(kNL) chunk_stats_kernel(const float *__restrict__ target,
                                                           const float *__restrict__ draft, int B,
-                                                          int G, int V, float T, int nch, int64_t units,
+                                                          int G, int V, float T, int nch,
                                                           const SampleFilter *__restrict__ filt,
                                                           float *__restrict__ cmax,
                                                           float *__restrict__ csum) {
-    // one warp per (row, chunk) unit, unit = r * nch + c
-    const int64_t u = (int64_t)blockIdx.x * (kNL / 32) + (threadIdx.x >> 5);
-    if (u >= units) return;
-    const int r = (int)(u / nch), c = (int)(u % nch), lane = threadIdx.x & 31;
+    __shared__ float wbuf[8];
+    const int c = blockIdx.x, r = blockIdx.y;
     const float *row = row_ptr(target, draft, r, B, G, V);
-    // two passes over the chunk (the second one hits L1): max, then the sums
+    float x[8];
+    const int n = load8(row, V, c, x);
     float m = -CUDART_INF_F;
-#pragma unroll 2
-    for (int v = 0; v < 8; v++) {
-        float x[8];
-        const int n = load8w(row, V, c, v, x);
 #pragma unroll
-        for (int q = 0; q < kPER; q++) if (q < n) m = fmaxf(m, x[q]);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    for (int q = 0; q < kPER; q++) if (q < n) m = fmaxf(m, x[q]);
+    m = block_max(m, wbuf);
     SampleFilter F;
     if constexpr (FILT) F = filt[r];
-    float t[8];
+    float t = 0.f;
 #pragma unroll
-    for (int v = 0; v < 8; v++) {
-        float x[8];
-        const int n = load8w(row, V, c, v, x);
-        t[v] = 0.f;
-#pragma unroll
-        for (int q = 0; q < kPER; q++) {
-            if (q < n) {
-                if constexpr (FILT) {
-                    if (!(F.w(c * kCH + kPER * (lane + 32 * v) + q, x[q]) > 0.f)) continue;
-                }
-                t[v] = __fadd_rn(t[v], elem_e(x[q], m, T));
+    for (int q = 0; q < kPER; q++) {
+        if (q < n) {
+            if constexpr (FILT) {
+                if (!(F.w(c * kCH + kPER * threadIdx.x + q, x[q]) > 0.f)) continue;
             }
+            t = __fadd_rn(t, elem_e(x[q], m, T));
         }
     }
-    const float sum = canon_sum_warp(t);
-    if (lane == 0) {
+    const float s = canon_sum(t, wbuf);
+    if (threadIdx.x == 0) {
         cmax[(int64_t)r * nch + c] = m;
-        csum[(int64_t)r * nch + c] = sum;
+        csum[(int64_t)r * nch + c] = s;
     }
 }
 
@@ -416,10 +367,8 @@ __global__ void __launch_bounds__(kNL) resid_chunks_kernel(
     const float *__restrict__ target, const float *__restrict__ draft, int B, int G, int V, float T, int nch,
     const SampleFilter *__restrict__ filt, const float *__restrict__ cmax, const float *__restrict__ rstat,
     const int32_t *__restrict__ okflag, float *__restrict__ rchunk) {
-    // one warp per (sequence b, chunk c), unit = b * nch + c
-    const int64_t u = (int64_t)blockIdx.x * (kNL / 32) + (threadIdx.x >> 5);
-    if (u >= (int64_t)B * nch) return;
-    const int b = (int)(u / nch), c = (int)(u % nch), lane = threadIdx.x & 31;
+    __shared__ float wsum[8];
+    const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     int acc = 0;
     while (acc < G && okflag[b * G + acc]) acc++;
     if (acc == G) return;
@@ -432,23 +381,19 @@ __global__ void __launch_bounds__(kNL) resid_chunks_kernel(
         Ft = filt[tr];
         Fd = filt[dr];
     }
+    float xt[8], xd[8];
+    const int n = load8(trow, V, c, xt);
+    load8(drow, V, c, xd);
     const float ft = ifr_exp(__fdiv_rn(__fsub_rn(tcm, ts.M), T));
     const float fd = ifr_exp(__fdiv_rn(__fsub_rn(dcm, ds.M), T));
-    float t[8];
+    float t = 0.f;
 #pragma unroll
-    for (int v = 0; v < 8; v++) {
-        float xt[8], xd[8];
-        const int n = load8w(trow, V, c, v, xt);
-        load8w(drow, V, c, v, xd);
-        t[v] = 0.f;
-#pragma unroll
-        for (int q = 0; q < kPER; q++)
-            if (q < n)
-                t[v] = __fadd_rn(t[v], resid_w<FILT>(xt[q], xd[q], c * kCH + kPER * (lane + 32 * v) + q, tcm, ft,
-                                                     ts, dcm, fd, ds, T, Ft, Fd));
-    }
-    const float sum = canon_sum_warp(t);
-    if (lane == 0) rchunk[(int64_t)b * nch + c] = sum;
+    for (int q = 0; q < kPER; q++)
+        if (q < n)
+            t = __fadd_rn(t, resid_w<FILT>(xt[q], xd[q], c * kCH + kPER * tid + q, tcm, ft, ts, dcm, fd, ds, T, Ft,
+                                           Fd));
+    const float sum = canon_sum(t, wsum);
+    if (tid == 0) rchunk[(int64_t)b * nch + c] = sum;
 }
 
 // grid (B): accept count, emitted tokens, residual or bonus sample
@@ -555,13 +500,12 @@ cudaError_t accept_launch(const float *target, const float *draft, const int32_t
     int32_t *xdraft = (int32_t *)p; p += (int64_t)B * G * 4;
     int32_t *okflag = (int32_t *)p; p += (int64_t)B * G * 4;
     float *rchunk = (float *)p;
-    const int64_t units = rows * nch;  // (row, chunk) pairs, one warp each
-    chunk_stats_kernel<FILT><<<(unsigned)((units + kNL / 32 - 1) / (kNL / 32)), kNL, 0, s>>>(
-        target, draft, B, G, V, T, nch, units, filt, cmax, csum);
+    chunk_stats_kernel<FILT><<<dim3(nch, (unsigned)rows), kNL, 0, s>>>(target, draft, B, G, V, T, nch, filt, cmax,
+                                                                       csum);
     row_decide_kernel<FILT><<<dim3(B, G + 1), kNL, 0, s>>>(target, draft, draft_tokens, uniforms, B, G, V, T,
                                                            nch, filt, cmax, csum, rstat, xdraft, okflag);
-    resid_chunks_kernel<FILT><<<(unsigned)(((int64_t)B * nch + kNL / 32 - 1) / (kNL / 32)), kNL, 0, s>>>(
-        target, draft, B, G, V, T, nch, filt, cmax, rstat, okflag, rchunk);
+    resid_chunks_kernel<FILT><<<dim3(nch, B), kNL, 0, s>>>(target, draft, B, G, V, T, nch, filt, cmax, rstat,
+                                                           okflag, rchunk);
     finish_kernel<FILT><<<B, kNL, 0, s>>>(target, draft, uniforms, B, G, V, T, nch, filt, cmax, csum, rstat,
                                           xdraft, okflag, accept_count, out_tokens, draft_out, rchunk);
     return cudaGetLastError();
