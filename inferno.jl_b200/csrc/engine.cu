@@ -1017,6 +1017,8 @@ __device__ float block_sum_256(float v, float *red) {
     return r;
 }
 
+constexpr int kMtpPer = 24;  // mtp_prep_kernel: hidden sizes up to 256 x 24 = 6144
+
 // MTP input of one draft (mtp_forward!, ModelCPU.jl:2031-2051), request
 // b = blockIdx.x: cat = [RMSNorm(embed(tok), norm_e); RMSNorm(h, norm_h)], and
 // the draft's position pos + add for the MTP attention layer
@@ -1040,17 +1042,35 @@ __global__ void __launch_bounds__(256) mtp_prep_kernel(const uint8_t *__restrict
     t = t < 0 ? 0 : (t >= rows ? rows - 1 : t);
     for (int gi = threadIdx.x; gi < nu * 8; gi += 256) ifr::dequant_group<T>(w, nu, nb_raw, t, gi >> 3, gi & 7, e_s + 32 * gi);
     __syncthreads();
+    // h and the two norm weights for this thread's elements, loaded once and
+    // up front (each thread owns i = tid + 256 k; d <= 256 kMtpPer)
+    float hv[kMtpPer], wev[kMtpPer], whv[kMtpPer];
+#pragma unroll
+    for (int k = 0; k < kMtpPer; k++) {
+        const int i = threadIdx.x + 256 * k;
+        hv[k] = i < d ? h[i] : 0.f;
+        wev[k] = i < d ? we[i] : 0.f;
+        whv[k] = i < d ? wh[i] : 0.f;
+    }
     float se = 0.f, sh = 0.f;
-    for (int i = threadIdx.x; i < d; i += 256) {
-        se += e_s[i] * e_s[i];
-        sh += h[i] * h[i];
+#pragma unroll
+    for (int k = 0; k < kMtpPer; k++) {
+        const int i = threadIdx.x + 256 * k;
+        if (i < d) {
+            se += e_s[i] * e_s[i];
+            sh += hv[k] * hv[k];
+        }
     }
     se = block_sum_256(se, red);
     sh = block_sum_256(sh, red);
     const float ie = 1.0f / sqrtf(se / (float)d + eps), ih = 1.0f / sqrtf(sh / (float)d + eps);
-    for (int i = threadIdx.x; i < d; i += 256) {
-        cat[i] = e_s[i] * ie * we[i];
-        cat[d + i] = h[i] * ih * wh[i];
+#pragma unroll
+    for (int k = 0; k < kMtpPer; k++) {
+        const int i = threadIdx.x + 256 * k;
+        if (i < d) {
+            cat[i] = e_s[i] * ie * wev[k];
+            cat[d + i] = hv[k] * ih * whv[k];
+        }
     }
     if (threadIdx.x == 0) *pos_out = sc->pos + add;
 }
@@ -1085,6 +1105,7 @@ cudaError_t launch_mtp_prep_t(const ifr::QTensor &e, const int32_t *tok, int tok
 cudaError_t launch_mtp_prep(const ifr::QTensor &e, const int32_t *tok, int tok_ld, const float *h, const float *we,
                             const float *wh, float eps, int d, float *cat, int32_t *pos_out,
                             const ifr::EngineScalars *sc, int add, int B, cudaStream_t st) {
+    if (d > 256 * kMtpPer) return cudaErrorInvalidValue;
     switch (e.type) {
     case 12: return launch_mtp_prep_t<12>(e, tok, tok_ld, h, we, wh, eps, d, cat, pos_out, sc, add, B, st);
     case 13: return launch_mtp_prep_t<13>(e, tok, tok_ld, h, we, wh, eps, d, cat, pos_out, sc, add, B, st);

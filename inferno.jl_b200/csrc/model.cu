@@ -1223,53 +1223,54 @@ struct GrpSmem {
 // stores cannot be ordered past loads through a generic pointer otherwise),
 // the norm weights sit in registers and the N positions' RoPE tables are
 // staged in rope_s (2 N pairs floats) first.  BAR as in bar256.
-template <int HD, int BAR>
+template <int HD, int BAR, int NTH = 256>
 __device__ __forceinline__ void attn_rows_in(const AttnArgs &a, float *q, float *kn, float *vn, float *rope_s, int R,
                                              int h0, int g, int p0, int tid) {
+    static_assert(BAR == 0 || NTH == 256, "named barriers cover 256 threads");
     constexpr int LB = 8;  // loads in flight per thread per batch
     const int N = a.N, lane = tid & 31, warp = tid >> 5, qs = a.gated ? 2 : 1;
     const RopeSpec rs = rope_spec(a);
-    for (int i0 = tid; i0 < R * HD; i0 += 256 * LB) {
+    for (int i0 = tid; i0 < R * HD; i0 += NTH * LB) {
         float v[LB];
 #pragma unroll
         for (int k = 0; k < LB; k++) {
-            const int i = i0 + 256 * k, r = i / HD, d = i % HD, hh = r / N, t = r % N;
+            const int i = i0 + NTH * k, r = i / HD, d = i % HD, hh = r / N, t = r % N;
             v[k] = i < R * HD ? a.qkv[(int64_t)t * a.ldq + (int64_t)(h0 + hh) * qs * HD + d] : 0.f;
         }
 #pragma unroll
         for (int k = 0; k < LB; k++)
-            if (i0 + 256 * k < R * HD) q[i0 + 256 * k] = v[k];
+            if (i0 + NTH * k < R * HD) q[i0 + NTH * k] = v[k];
     }
-    for (int i0 = tid; i0 < N * HD; i0 += 256 * LB) {
+    for (int i0 = tid; i0 < N * HD; i0 += NTH * LB) {
         float kv[LB], vv[LB];
 #pragma unroll
         for (int k = 0; k < LB; k++) {
-            const int i = i0 + 256 * k, t = i / HD, d = i % HD;
+            const int i = i0 + NTH * k, t = i / HD, d = i % HD;
             const float *row = a.qkv + (int64_t)t * a.ldq + (int64_t)a.nh * qs * HD;
             kv[k] = i < N * HD ? row[g * HD + d] : 0.f;
             vv[k] = i < N * HD ? row[a.nkv * HD + g * HD + d] : 0.f;
         }
 #pragma unroll
         for (int k = 0; k < LB; k++)
-            if (i0 + 256 * k < N * HD) {
-                kn[i0 + 256 * k] = kv[k];
-                vn[i0 + 256 * k] = vv[k];
+            if (i0 + NTH * k < N * HD) {
+                kn[i0 + NTH * k] = kv[k];
+                vn[i0 + NTH * k] = vv[k];
             }
     }
-    for (int i0 = tid; i0 < N * rs.pairs; i0 += 256 * LB) {
+    for (int i0 = tid; i0 < N * rs.pairs; i0 += NTH * LB) {
         float c[LB], sn[LB];
 #pragma unroll
         for (int k = 0; k < LB; k++) {
-            const int i = i0 + 256 * k, t = i / rs.pairs, pi = i % rs.pairs;
+            const int i = i0 + NTH * k, t = i / rs.pairs, pi = i % rs.pairs;
             const int64_t o = (int64_t)(p0 + t) * rs.ld + pi;
             c[k] = i < N * rs.pairs ? a.rope_cos[o] : 0.f;
             sn[k] = i < N * rs.pairs ? a.rope_sin[o] : 0.f;
         }
 #pragma unroll
         for (int k = 0; k < LB; k++)
-            if (i0 + 256 * k < N * rs.pairs) {
-                rope_s[i0 + 256 * k] = c[k];
-                rope_s[N * rs.pairs + i0 + 256 * k] = sn[k];
+            if (i0 + NTH * k < N * rs.pairs) {
+                rope_s[i0 + NTH * k] = c[k];
+                rope_s[N * rs.pairs + i0 + NTH * k] = sn[k];
             }
     }
     float qw[HD / 32], kw[HD / 32];
@@ -1279,7 +1280,7 @@ __device__ __forceinline__ void attn_rows_in(const AttnArgs &a, float *q, float 
         kw[j] = a.k_norm[lane + 32 * j];
     }
     bar256<BAR>();
-    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += 8) {
+    for (int rr = warp; rr < R + N + (a.vnorm ? N : 0); rr += NTH / 32) {
         if (rr >= R + N) {
             float *x = vn + (rr - R - N) * HD;
             float ss = 0.f;
@@ -1534,22 +1535,28 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int NPEND>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
 
+constexpr int kMmaThreads = 512;  // 16 warps: the scores' two K halves, the P.V n-tiles
+
 template <int HD>
 struct MmaSmem {
     static constexpr int QS = HD + 4, KS = HD + 4, VS = HD + 8, SS = kGrpKeys + 4;
     // uint32/float words: qh[R][QS] | ql[R][QS] | Ks[2][kGrpKeys][KS] | Vs[2][kGrpKeys][VS] |
-    // kn[N][HD] | vn[N][HD] | sc[R][SS] | ms, ls, fs [R]; the f32 q rows are staged in Vs[1]
+    // kn[N][HD] | vn[N][HD] | sc[R][SS] | sc2[R][SS] | ms, ls, fs [R]; the f32 q rows are
+    // staged in Vs[1]
     static __host__ __device__ int words(int R, int N) {
-        return 2 * R * QS + 2 * kGrpKeys * KS + 2 * kGrpKeys * VS + 2 * N * HD + R * SS + 3 * R;
+        return 2 * R * QS + 2 * kGrpKeys * KS + 2 * kGrpKeys * VS + 2 * N * HD + 2 * R * SS + 3 * R;
     }
     static __host__ __device__ int bytes(int R, int N) { return 4 * words(R, N); }
 };
 
 template <int HD>
-__global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int hg, int S) {
+__global__ void __launch_bounds__(kMmaThreads, 1) attn_part_mma_kernel(AttnArgs a, int hg, int S) {
     using M = MmaSmem<HD>;
     constexpr int QS = M::QS, KS = M::KS, VS = M::VS, SS = M::SS;
-    constexpr int NTW = HD / 64;  // P.V n-tiles per warp and m-tile
+    constexpr int NTH = kMmaThreads, NWP = NTH / 32;
+    // P.V: HD >= 128: every warp both m-tiles and NTW n-tiles (warp + 16 u);
+    // HD 64: warp w the m-tile w / 8 and the n-tile w % 8
+    constexpr int MT = HD >= 128 ? 2 : 1, NTW = HD >= 128 ? HD / 128 : 1;
     extern __shared__ __align__(16) float ms_buf[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g8 = lane >> 2, t4 = lane & 3;
     const int N = a.N, ratio = a.nh / a.nkv, nrg = (ratio + hg - 1) / hg;
@@ -1559,7 +1566,7 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
     uint32_t *qh = reinterpret_cast<uint32_t *>(ms_buf), *ql = qh + R * QS;
     float *Ks = reinterpret_cast<float *>(ql + R * QS), *Vs = Ks + 2 * kGrpKeys * KS;
     float *kn = Vs + 2 * kGrpKeys * VS, *vn = kn + N * HD, *sc = vn + N * HD;
-    float *ms = sc + R * SS, *ls = ms + R, *fs = ls + R;
+    float *sc2 = sc + R * SS, *ms = sc2 + R * SS, *ls = ms + R, *fs = ls + R;
     float *q = Vs + kGrpKeys * VS;  // f32 q rows [R][HD], staged in the second V buffer
     pdl_trigger();
     pdl_wait();
@@ -1575,7 +1582,7 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
     const int64_t rows_all = (int64_t)gridDim.z * a.nh * N, rid0 = ((int64_t)b * a.nh + h0) * N;
     if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
         float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
-        for (int i = tid; i < R * HD; i += 256) po[(rid0 + i / HD) * HD + i % HD] = 0.f;
+        for (int i = tid; i < R * HD; i += NTH) po[(rid0 + i / HD) * HD + i % HD] = 0.f;
         if (tid < R) {
             pm[rid0 + tid] = -CUDART_INF_F;
             pl[rid0 + tid] = 0.f;
@@ -1587,7 +1594,7 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
     auto stage = [&](int c, int bf) {
         const int j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
         float *kb = Ks + bf * kGrpKeys * KS, *vb = Vs + bf * kGrpKeys * VS;
-        for (int i = tid; i < kGrpKeys * (HD / 4); i += 256) {
+        for (int i = tid; i < kGrpKeys * (HD / 4); i += NTH) {
             const int jj = i / (HD / 4), d = 4 * (i % (HD / 4)), j = j0 + jj;
             if (jj < nj && j < p0) {
                 const int64_t o = ((int64_t)j * a.nkv + g) * HD + d;
@@ -1611,20 +1618,20 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
         ms[tid] = -CUDART_INF_F;
         ls[tid] = 0.f;
     }
-    attn_rows_in<HD, 0>(a, q, kn, vn, Ks + kGrpKeys * KS, R, h0, g, p0, tid);
+    attn_rows_in<HD, 0, NTH>(a, q, kn, vn, Ks + kGrpKeys * KS, R, h0, g, p0, tid);
     __syncthreads();
     // the first chunk's copies start now; the new keys are in kn / vn for it
     stage(0, 0);
     // one CTA per (KV head, request) writes the new keys; no CTA reads them from the cache
     if (sl == 0 && hb == 0) {
-        for (int i = tid; i < N * HD; i += 256) {
+        for (int i = tid; i < N * HD; i += NTH) {
             const int t = i / HD, d = i % HD;
             const int64_t o = ((int64_t)(p0 + t) * a.nkv + g) * HD + d;
             a.kc[o] = kn[i];
             a.vc[o] = vn[i];
         }
     }
-    for (int i = tid; i < R * HD; i += 256) {
+    for (int i = tid; i < R * HD; i += NTH) {
         uint32_t h_, l_;
         split_tf32(q[i], h_, l_);
         qh[(i / HD) * QS + i % HD] = h_;
@@ -1633,9 +1640,9 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
     __syncthreads();  // q split (the staging buffer is free for chunk 1)
 
     const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf((float)HD);
-    float oacc[2][NTW][4];
+    float oacc[MT][NTW][4];
 #pragma unroll
-    for (int m = 0; m < 2; m++)
+    for (int m = 0; m < MT; m++)
 #pragma unroll
         for (int u = 0; u < NTW; u++)
 #pragma unroll
@@ -1650,8 +1657,9 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
         }
         __syncthreads();
         const float *kb = Ks + bf * kGrpKeys * KS, *vb = Vs + bf * kGrpKeys * VS;
-        {   // scores: warp (m = warp / 4, key tile nb = warp % 4)
-            const int m = warp >> 2, nb = warp & 3, r0 = 16 * m + g8;
+        {   // scores: warp (k half = warp / 8, m = warp / 4 % 2, key tile nb = warp % 4);
+            //   each half sums its HD / 2 dims into its own buffer (sc, sc2)
+            const int kh = warp >> 3, m = (warp >> 2) & 1, nb = warp & 3, r0 = 16 * m + g8;
             if (16 * m < R) {
                 // independent accumulators per k-step parity and product term:
                 // six short MMA dependency chains instead of one long one
@@ -1664,7 +1672,7 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
                         for (int i = 0; i < 4; i++) ac[p2][q3][i] = 0.f;
                 const float *kr = kb + (8 * nb + g8) * KS;
 #pragma unroll 4
-                for (int kk = 0; kk < HD / 8; kk++) {
+                for (int kk = kh * (HD / 16); kk < (kh + 1) * (HD / 16); kk++) {
                     const int k0 = 8 * kk + t4;
                     uint32_t ah[4], al[4];
                     ah[0] = r0 < R ? qh[r0 * QS + k0] : 0u;
@@ -1687,18 +1695,21 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
 #pragma unroll
                 for (int i = 0; i < 4; i++)
                     acc[i] = (ac[0][0][i] + ac[1][0][i]) + ((ac[0][1][i] + ac[1][1][i]) + (ac[0][2][i] + ac[1][2][i]));
+                float *dst = kh ? sc2 : sc;
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    const int r = r0 + 8 * (i >> 1), jj = 8 * nb + 2 * t4 + (i & 1), j = j0 + jj;
-                    if (r < R)
-                        sc[r * SS + jj] = (jj < nj && key_visible(a, j, p0 + r % N)) ? score_cap(a, acc[i] * scale)
-                                                                                   : -CUDART_INF_F;
+                    const int r = r0 + 8 * (i >> 1), jj = 8 * nb + 2 * t4 + (i & 1);
+                    if (r < R) dst[r * SS + jj] = acc[i];
                 }
             }
         }
         __syncthreads();
-        for (int r = warp; r < R; r += 8) {  // online softmax, one warp per row
-            const float sv = lane < kGrpKeys ? sc[r * SS + lane] : -CUDART_INF_F;
+        for (int r = warp; r < R; r += NWP) {  // online softmax, one warp per row
+            // the two halves' dot products, scaled, capped and masked
+            const int j = j0 + lane;
+            const float sv = lane < kGrpKeys && lane < nj && key_visible(a, j, p0 + r % N)
+                                 ? score_cap(a, (sc[r * SS + lane] + sc2[r * SS + lane]) * scale)
+                                 : -CUDART_INF_F;
             const float mo = ms[r], mn = fmaxf(mo, warp_max(sv));
             float f = 1.f, e = 0.f;
             if (mn != -CUDART_INF_F) {
@@ -1714,18 +1725,19 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
             }
         }
         __syncthreads();
-        // P.V: warp's n-tiles warp + 8 u, both m-tiles
+        // P.V: the warp's m-tiles and n-tiles (see MT, NTW)
 #pragma unroll
-        for (int m = 0; m < 2; m++) {
+        for (int mi = 0; mi < MT; mi++) {
+            const int m = MT == 2 ? mi : warp >> 3;
             if (16 * m >= R) continue;
             const int r0 = 16 * m + g8;
             const float f0 = r0 < R ? fs[r0] : 1.f, f1 = r0 + 8 < R ? fs[r0 + 8] : 1.f;
 #pragma unroll
             for (int u = 0; u < NTW; u++) {
-                oacc[m][u][0] *= f0;
-                oacc[m][u][1] *= f0;
-                oacc[m][u][2] *= f1;
-                oacc[m][u][3] *= f1;
+                oacc[mi][u][0] *= f0;
+                oacc[mi][u][1] *= f0;
+                oacc[mi][u][2] *= f1;
+                oacc[mi][u][3] *= f1;
             }
 #pragma unroll
             for (int kk = 0; kk < kGrpKeys / 8; kk++) {
@@ -1737,11 +1749,12 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
                 split_tf32(r0 + 8 < R ? sc[(r0 + 8) * SS + k0 + 4] : 0.f, ah[3], al[3]);
 #pragma unroll
                 for (int u = 0; u < NTW; u++) {
-                    const int n0 = 8 * (warp + 8 * u) + g8;
+                    const int nt = MT == 2 ? warp + NWP * u : (warp & 7);
+                    const int n0 = 8 * nt + g8;
                     uint32_t bh0, bl0, bh1, bl1;
                     split_tf32(vb[k0 * VS + n0], bh0, bl0);
                     split_tf32(vb[(k0 + 4) * VS + n0], bh1, bl1);
-                    mma_3xtf32(oacc[m][u], ah, al, bh0, bh1, bl0, bl1);
+                    mma_3xtf32(oacc[mi][u], ah, al, bh0, bh1, bl0, bl1);
                 }
             }
         }
@@ -1751,13 +1764,14 @@ __global__ void __launch_bounds__(256, 1) attn_part_mma_kernel(AttnArgs a, int h
     // 3. the slice's partial state
     float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
 #pragma unroll
-    for (int m = 0; m < 2; m++)
+    for (int mi = 0; mi < MT; mi++)
 #pragma unroll
         for (int u = 0; u < NTW; u++)
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const int r = 16 * m + g8 + 8 * (i >> 1), d = 8 * (warp + 8 * u) + 2 * t4 + (i & 1);
-                if (r < R) po[(rid0 + r) * HD + d] = oacc[m][u][i];
+                const int m = MT == 2 ? mi : warp >> 3, nt = MT == 2 ? warp + NWP * u : (warp & 7);
+                const int r = 16 * m + g8 + 8 * (i >> 1), d = 8 * nt + 2 * t4 + (i & 1);
+                if (r < R) po[(rid0 + r) * HD + d] = oacc[mi][u][i];
             }
     if (tid < R) {
         pm[rid0 + tid] = ms[tid];
@@ -1881,7 +1895,7 @@ static cudaError_t launch_split(const AttnArgs &a, int batch, cudaStream_t s) {
     const int R = std::min(hg, ratio) * a.N;
     // the tensor-core kernel (IFR_ATTN_MMA=0 in the environment selects the CUDA-core one)
     cudaError_t e = attn_mma_enabled()
-                        ? launch_k(attn_part_mma_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
+                        ? launch_k(attn_part_mma_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(kMmaThreads),
                                    (size_t)MmaSmem<HD>::bytes(R, a.N), s, a, hg, a.splits)
                         : launch_k(attn_part_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
                                    (size_t)GrpSmem<HD>::bytes(R, a.N), s, a, hg, a.splits);
