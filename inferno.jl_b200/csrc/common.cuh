@@ -64,6 +64,9 @@ struct XForm {
                                // (gate 0-15, up 0-15, gate 16-31, ...); Y gets silu(gate) * up,
                                // rows/2 rows (not with accumulate); 2: gelu_tanh(gate) * up
     const GemvArgmax *am = nullptr;  // greedy decision on Y (not with ep or accumulate)
+    int rev = 0;               // tall matrices: each CTA streams its row groups last to first
+                               // (consecutive passes over a matrix a little larger than L2 then
+                               // start on the rows the previous pass left in L2)
 };
 // Y[ncols][rows] (+)= W * f(X), ncols <= 8 per call; X 16-byte aligned, ldx a multiple of 4
 cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,

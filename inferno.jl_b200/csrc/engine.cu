@@ -1251,6 +1251,7 @@ int mtp_draft(ifr_state *s, int gamma, cudaStream_t st) {
         const bool fused = lm_head_decides(s, B);
         ifr::XForm f = norm_out;
         if (fused) f.am = &am;
+        f.rev = j % 2 == 0;  // alternate directions: a draft starts on the rows the previous one left in L2
         if ((rc = gemv(s, CAT_DRAFT_LM_HEAD, m->lm_head, s->x, B, s->logits, false, st, f))) return rc;
         if (!fused) {
             ECHECK(ifr::accept_greedy_fused(s->logits, nullptr, B, 0, c.vocab, s->acc, s->vtok + j, s->acc_scratch,

@@ -126,6 +126,7 @@ struct GemvArgs {
     const float *xw;   // RMSNorm weights [K]
     float eps;
     int ep;            // 1: SwiGLU epilogue over interleaved gate/up 16-row blocks
+    int rev;           // qgemv_rows_kernel: row groups last to first (XForm::rev)
 };
 // the greedy decision's arguments, a kernel parameter of the AM variants only
 template <bool AM> struct AmArg { GemvArgmax am; };
@@ -1097,7 +1098,7 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
     }
     auto issue = [&](int q) {  // one thread: stage q into its slot
         const int slot = q % a.S;
-        const int g = g_lo + q / a.nu, u = q % a.nu;
+        const int g = a.rev ? g_hi - 1 - q / a.nu : g_lo + q / a.nu, u = q % a.nu;
         const int nrow = min(kRowsCW, a.nrb - g * kRowsCW);
         fence_proxy_async();
         mbar_expect_tx(full + slot, (uint32_t)(nrow * MTB));
@@ -1185,7 +1186,8 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
         // greedy keys: exact, column 4 nt + t of n-tile nt; Q8_K, column 2 t + j
         unsigned long long best[2] = {0ull, 0ull};
         int q = 0;
-        for (int gr = g_lo; gr < g_hi; gr++) {
+        for (int gi = 0; gi < g_hi - g_lo; gi++) {
+            const int gr = a.rev ? g_hi - 1 - gi : g_lo + gi;
             const int rb = gr * kRowsCW + warp;
             float tot[NT][4];
 #pragma unroll
@@ -1381,7 +1383,7 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
     }
     const int grid = num_sms();
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, 0, S,
-               0, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep};
+               0, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep, xf.rev};
     AmArg<AM> aa{};
     if constexpr (AM) aa.am = *xf.am;
     return launch_k(qgemv_rows_kernel<FMT, NT, XF, ACT, AM>, dim3(grid), dim3(512), (size_t)smem, s, a, aa);
