@@ -101,6 +101,13 @@ int ifr_ctx_set_prefill_dense(ifr_ctx *ctx, int enable);
  * Models it does not cover (Gemma4 blocks, other head dims, formats other
  * than Q4_K/Q6_K) keep the separate launches.  Default 0. */
 int ifr_ctx_set_fused_layers(ifr_ctx *ctx, int enable);
+/* enable = 1 (default): a batched state (ifr_state_create_batch, batch > 1)
+ * gives every projection of its model an fp16 copy of the dequantized weights
+ * in the dense GEMM's operand layout (~3.6 x the Q4_K bytes of HBM), which the
+ * dense path (ifr_qgemm_dense's kernel) then copies instead of dequantizing.
+ * Results are identical either way: each weight is rounded to fp16 once in
+ * both.  Takes effect for states created afterwards. */
+int ifr_ctx_set_dense_f16_weights(ifr_ctx *ctx, int enable);
 /* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
  * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);
@@ -115,6 +122,10 @@ int ifr_weights_upload(ifr_ctx *ctx, int type, const void *host_bytes,
 int ifr_weights_from_device(ifr_ctx *ctx, int type, const void *dev_bytes,
                             int64_t rows, int64_t cols, ifr_tensor **out);
 int ifr_tensor_free(ifr_tensor *t);
+/* the fp16 operand stages of t for ifr_qgemm_dense (see
+ * ifr_ctx_set_dense_f16_weights); ifr_tensor_free releases them.  No
+ * counterpart in the reference. */
+int ifr_tensor_prepare_dense(ifr_ctx *ctx, ifr_tensor *t);
 int ifr_tensor_info(const ifr_tensor *t, int *type, int64_t *rows, int64_t *cols,
                     int64_t *device_bytes);
 

@@ -116,6 +116,14 @@ class Context:
         """let one-request prefill chunks use the dense tensor-core path"""
         check(load().ifr_ctx_set_prefill_dense(self.handle, 1 if enable else 0))
 
+    def set_dense_f16_weights(self, enable=True):
+        """batched states keep fp16 operand stages of the weights for the dense GEMM"""
+        check(load().ifr_ctx_set_dense_f16_weights(self.handle, 1 if enable else 0))
+
+    def prepare_dense(self, W):
+        """fp16 operand stages of tensor W for qgemm_dense (same results, no dequant)"""
+        check(load().ifr_tensor_prepare_dense(self.handle, W.handle))
+
     def set_fused_layers(self, enable=True):
         """run a one-request verify's decoder layers as one persistent launch"""
         check(load().ifr_ctx_set_fused_layers(self.handle, 1 if enable else 0))

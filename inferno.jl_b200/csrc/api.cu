@@ -54,6 +54,7 @@ struct ifr_ctx {
     int dense_min = IFR_DENSE_MIN_COLS_DEFAULT;  // engine GEMMs of this many columns use the dense path
     int prefill_dense = 0;                         // one-request prefill chunks may use the dense path
     int fused_layers = 0;                          // one-request verify: the layer stack as one launch
+    int dense_f16 = 1;                             // batched states keep fp16 operand stages of the weights
     std::atomic<int> refs{0};      // live models built on this context
     std::atomic<bool> closing{false};
 };
@@ -135,6 +136,7 @@ int ifr_ctx_activation(const ifr_ctx *c) { return c->act; }
 int ifr_ctx_dense_min(const ifr_ctx *c) { return c->dense_min; }
 int ifr_ctx_prefill_dense(const ifr_ctx *c) { return c->prefill_dense; }
 int ifr_ctx_fused_layers(const ifr_ctx *c) { return c->fused_layers; }
+int ifr_ctx_dense_f16(const ifr_ctx *c) { return c->dense_f16; }
 static void ctx_destroy_now(ifr_ctx *c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
@@ -216,6 +218,29 @@ int ifr_ctx_set_dense_min_cols(ifr_ctx *c, int ncols) {
 int ifr_ctx_set_prefill_dense(ifr_ctx *c, int enable) {
     if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
     c->prefill_dense = enable ? 1 : 0;
+    return IFR_OK;
+}
+
+int ifr_ctx_set_dense_f16_weights(ifr_ctx *c, int enable) {
+    if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
+    c->dense_f16 = enable ? 1 : 0;
+    return IFR_OK;
+}
+
+int ifr_tensor_prepare_dense(ifr_ctx *c, ifr_tensor *t) {
+    if (!c || !t) return fail(IFR_ERR_ARG, "NULL argument");
+    if (t->device != c->device) return fail(IFR_ERR_ARG, "tensor lives on device %d, context on %d", t->device, c->device);
+    if (t->q.f16) return IFR_OK;
+    DeviceGuard g(c->device);
+    void *p = nullptr;
+    IFR_CHECK_CUDA(cudaMalloc(&p, ifr::qgemm_dense_f16_bytes(t->q)), "cudaMalloc(fp16 stages)");
+    cudaError_t e = ifr::qgemm_dense_prepare_f16(t->q, static_cast<uint8_t *>(p), c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) {
+        t->q.f16 = nullptr;
+        cudaFree(p);
+        return cuda_fail(e, "fp16 stages");
+    }
     return IFR_OK;
 }
 
@@ -304,6 +329,7 @@ int ifr_tensor_free(ifr_tensor *t) {
     if (!t) return IFR_OK;
     DeviceGuard g(t->device);
     cudaFree(t->q.data);
+    if (t->q.f16) cudaFree(t->q.f16);
     delete t;
     return IFR_OK;
 }

@@ -23,7 +23,12 @@ struct QTensor {
     int64_t nu;         // units of 256 columns (cols padded up for Q8_0)
     uint8_t *data;      // device base
     int64_t bytes;      // device bytes
+    // optional (qgemm_dense_prepare_f16): the dequantized weights rounded to fp16
+    // as the dense GEMM's shared-memory operand stages, [row tile][unit][stage]
+    // of kF16StageBytes each; the dense GEMM then copies them instead of dequantizing
+    uint8_t *f16 = nullptr;
 };
+constexpr int64_t kF16StageBytes = 16896;  // one 128-row x 64-K operand stage (padded chunks)
 
 int64_t raw_row_bytes(int type, int64_t cols);
 int64_t device_bytes(int type, int64_t rows, int64_t cols);
@@ -76,6 +81,11 @@ cudaError_t qgemm_small(const QTensor &t, const float *X, int ncols, float *Y, b
 // power of two per column), f32 accumulation.  scratch >= qgemm_dense_scratch_bytes.
 cudaError_t qgemm_dense(const QTensor &t, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                         cudaStream_t s, const XForm &xf, void *scratch, int64_t scratch_bytes);
+// bytes of t's fp16 operand stages, and their construction (into t.f16, device
+// memory the caller allocated, on stream s); the dense GEMM's results are the
+// same with and without them
+int64_t qgemm_dense_f16_bytes(const QTensor &t);
+cudaError_t qgemm_dense_prepare_f16(QTensor &t, uint8_t *dst, cudaStream_t s);
 int64_t qgemm_dense_scratch_bytes(const QTensor &t, int ncols);  // -1: unsupported
 cudaError_t read_mma_error(int *flag, cudaStream_t s);
 // host encoder (encode.cpp): 0 on success

@@ -34,6 +34,7 @@ int ifr_ctx_activation(const ifr_ctx *c);
 int ifr_ctx_dense_min(const ifr_ctx *c);
 int ifr_ctx_prefill_dense(const ifr_ctx *c);
 int ifr_ctx_fused_layers(const ifr_ctx *c);
+int ifr_ctx_dense_f16(const ifr_ctx *c);
 void ifr_ctx_retain(ifr_ctx *c);
 void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
@@ -975,6 +976,36 @@ int fused_build(ifr_state *s) {
     return rc;
 }
 
+// the fp16 operand stages of every projection of the model for the dense GEMM
+// (ifr_ctx_set_dense_f16_weights); a part that cannot get its memory keeps
+// the dequantizing path (same results)
+int model_prepare_f16(ifr_model *m, cudaStream_t st) {
+    auto prep = [&](Proj &p) {
+        for (auto &q : p.parts) {
+            if (q.f16) continue;
+            void *d = nullptr;
+            if (cudaMalloc(&d, ifr::qgemm_dense_f16_bytes(q)) != cudaSuccess) {
+                cudaGetLastError();
+                return IFR_OK;
+            }
+            m->dev_allocs.push_back(d);
+            ECHECK(ifr::qgemm_dense_prepare_f16(q, static_cast<uint8_t *>(d), st), "fp16 stages");
+        }
+        return IFR_OK;
+    };
+    int rc = IFR_OK;
+    for (auto &L : m->layers)
+        for (Proj *p : {&L.proj, &L.out, &L.gate_up, &L.down})
+            if (!rc) rc = prep(*p);
+    if (!rc) rc = prep(m->lm_head);
+    if (!rc && m->has_mtp) {
+        for (Proj *p : {&m->mtp_fc, &m->mtp_layer.proj, &m->mtp_layer.out, &m->mtp_layer.gate_up, &m->mtp_layer.down})
+            if (!rc) rc = prep(*p);
+    }
+    if (!rc) ECHECK(cudaStreamSynchronize(st), "fp16 stages sync");
+    return rc;
+}
+
 // the verify of n columns runs as the fused launch
 bool fused_on(const ifr_state *s, int n) {
     return n >= 1 && n <= kNMax && s->fused_ph[n] && !s->prefill_chunk && ifr_ctx_fused_layers(s->m->ctx) &&
@@ -1565,6 +1596,7 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     if (!rc && cudaMallocHost((void **)&s->h_tok, sizeof(int32_t) * (N + 64)) != cudaSuccess)
         rc = ifr_fail(IFR_ERR_NOMEM, "cudaMallocHost failed");
     if (!rc) rc = fused_build(s);
+    if (!rc && B > 1 && ifr_ctx_dense_f16(m->ctx)) rc = model_prepare_f16(m, ifr_ctx_stream_of(m->ctx));
     if (!rc && m->gemma) {
         // precompute_rope (Gemma4.jl:205-249): frequencies and angles in
         // Float64, cos / sin as Float32; sliding layers: every pair, theta_swa;

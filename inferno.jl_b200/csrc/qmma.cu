@@ -349,6 +349,7 @@ struct MmaArgs {
     int64_t ldy, M;
     int accumulate, ep;
     float *ws;             // split partials [splits][ncols][nrb * 16] (splits > 1)
+    const uint8_t *wf16;   // fp16 operand stages of W (QTensor::f16), or null: dequantize
 };
 
 // KS: 64-wide K sub-stages per pipeline stage (2 when the column tile is <= 256,
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *dead = reinterpret_cast<volatile int *>(tmem_holder + 1);
     uint8_t *raw = smem + 1024;
-    const int raw_bytes = (RS * RAW + 1023) & ~1023;
+    const int raw_bytes = a.wf16 ? 0 : (RS * RAW + 1023) & ~1023;  // fp16 stages: no raw ring (make_plan)
     constexpr int kAStage = a_stage_bytes(KS);
     const int bstage = npad * 128 * KS;
     const int stage_bytes = (kAStage + bstage + 1023) & ~1023;
@@ -403,9 +404,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
+    const bool f16w = a.wf16 != nullptr;
     if (warp == 0) {
         // ---------------- weight producer (constant data: no dependency wait) ----------------
-        if (lane == 0) {
+        if (lane == 0 && !f16w) {
             Ring rr{RS};
             const uint8_t *src = a.W + ((int64_t)rb0 * a.nu + u0) * MTB;
             const int64_t rb_stride = (int64_t)a.nu * MTB;
@@ -434,7 +436,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
             const uint64_t da = smem_desc(s0, kALbo, 128), db = smem_desc(s0 + kAStage, npad * 16, 128);
             Ring ab{ST};
             for (int q = 0; q < nst; q++, ab.next()) {
-                if (!mb_wait(a_full + ab.slot, ab.full_par(), dead) || !mb_wait(b_full + ab.slot, ab.full_par(), dead))
+                if ((!f16w && !mb_wait(a_full + ab.slot, ab.full_par(), dead)) ||
+                    !mb_wait(b_full + ab.slot, ab.full_par(), dead))
                     break;
                 tc_fence_after();
                 const uint32_t so = (uint32_t)(ab.slot * stage_bytes) >> 4;  // descriptor start fields advance in 16 B
@@ -455,10 +458,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
             pdl_wait();  // the activations come from the previous kernel
             Ring ab{ST};
             const uint16_t *src = a.Xp + ((int64_t)nt * a.nu * 4 + 4 * u0) * (int64_t)npad * 64;
+            // fp16 weights: the row tile's operand stages from unit u0 on, KS per stage
+            const uint8_t *wsrc = f16w ? a.wf16 + ((int64_t)rt * a.nu + u0) * 4 * kF16StageBytes : nullptr;
             int issued = 0;
             for (int q = 0; q < nst && !*dead; q++, ab.next(), src += npad * 64 * KS) {
                 if (ab.round > 0 && !mb_wait(ab_empty + ab.slot, ab.empty_par(), dead)) break;
-                mb_expect_tx(b_full + ab.slot, (uint32_t)bstage);
+                mb_expect_tx(b_full + ab.slot, (uint32_t)(bstage + (f16w ? kAStage : 0)));
+                if (f16w)
+                    bulk_copy(stages + ab.slot * stage_bytes, wsrc + (int64_t)q * kAStage, (uint32_t)kAStage,
+                              b_full + ab.slot);
                 bulk_copy(stages + ab.slot * stage_bytes + kAStage, src, (uint32_t)bstage, b_full + ab.slot);
                 issued = q + 1;
             }
@@ -477,7 +485,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
         const bool has_rows = m < nmt;
         Deq<FMT> dq;
         Ring rr{RS}, ab{ST};
-        for (int i = 0; i < nunits && !*dead; i++, rr.next()) {
+        for (int i = 0; i < nunits && !*dead && !f16w; i++, rr.next()) {
             if (!mb_wait(raw_full + rr.slot, rr.full_par(), dead)) break;
             if (has_rows) dq.unit(raw + rr.slot * RAW + m * MTB, r, t);
             bool ok = true;
@@ -542,6 +550,37 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmma_kernel(MmaArgs a) {
     if (warp == 1) {
         tc_fence_after();
         tmem_free(tmem, tcols);
+    }
+}
+
+// The fp16 operand stages of W (QTensor::f16): block (row tile rt, unit u),
+// 512 threads, each the piece (M-tile m, row r, lane quad t) the dequant
+// warps of qmma_kernel form, written for the unit's four 64-K stages at the
+// same offsets - so a stage copied from here equals the stage the kernel
+// would have built (rows past the matrix are zero).
+template <int FMT>
+__global__ void __launch_bounds__(kDqThreads) qmma_f16_stages_kernel(const uint8_t *__restrict__ W, int nrb, int nu,
+                                                                     uint8_t *__restrict__ out) {
+    constexpr int MTB = mtile_bytes(FMT);
+    const int rt = blockIdx.x, u = blockIdx.y, P = threadIdx.x;
+    const int m = P >> 6, r = (P >> 2) & 15, t = P & 3;
+    const int off = (t >> 1) * kALbo + (16 * m + r) * 16 + (t & 1) * 8;
+    const bool has_rows = rt * 8 + m < nrb;
+    Deq<FMT> dq;
+    if (has_rows) dq.unit(W + ((int64_t)(rt * 8 + m) * nu + u) * MTB, r, t);
+    uint8_t *base = out + ((int64_t)rt * nu + u) * 4 * kF16StageBytes + off;
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+        uint32_t o[8];
+        if (has_rows) {
+            dq.stage(p, o);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = 0u;
+        }
+#pragma unroll
+        for (int w = 0; w < 4; w++)
+            *reinterpret_cast<uint2 *>(base + p * kF16StageBytes + 2 * w * kALbo) = make_uint2(o[2 * w], o[2 * w + 1]);
     }
 }
 
@@ -655,7 +694,7 @@ struct Plan {
 // minimises waves x (units + start-up) per CTA
 bool make_plan(const QTensor &T, int ncols, Plan &p) {
     if (ncols < 1) return false;
-    const int raw1 = 8 * mtile_bytes(T.type);
+    const int raw1 = T.f16 ? 0 : 8 * mtile_bytes(T.type);  // fp16 stages: no raw weight ring
     bool ok = false;
     for (int cap = 512; cap >= 256 && !ok; cap -= 256) {
         p.ntiles = (ncols + cap - 1) / cap;
@@ -718,6 +757,27 @@ cudaError_t launch_qmma(const MmaArgs &a, const Plan &p, cudaStream_t s) {
 
 }  // namespace
 
+int64_t qgemm_dense_f16_bytes(const QTensor &T) { return (T.nrb + 7) / 8 * T.nu * 4 * kF16StageBytes; }
+
+cudaError_t qgemm_dense_prepare_f16(QTensor &T, uint8_t *dst, cudaStream_t s) {
+    if (!dst || ((uintptr_t)dst & 15)) return cudaErrorInvalidValue;
+    static_assert(a_stage_bytes(1) == kF16StageBytes && a_stage_bytes(2) == 2 * kF16StageBytes,
+                  "a KS-stage is KS consecutive 64-K stages");
+    const dim3 grid((unsigned)((T.nrb + 7) / 8), (unsigned)T.nu);
+    cudaError_t e = cudaMemsetAsync(dst, 0, qgemm_dense_f16_bytes(T), s);
+    if (e != cudaSuccess) return e;
+    switch (T.type) {
+    case 12: qmma_f16_stages_kernel<12><<<grid, kDqThreads, 0, s>>>(T.data, (int)T.nrb, (int)T.nu, dst); break;
+    case 13: qmma_f16_stages_kernel<13><<<grid, kDqThreads, 0, s>>>(T.data, (int)T.nrb, (int)T.nu, dst); break;
+    case 14: qmma_f16_stages_kernel<14><<<grid, kDqThreads, 0, s>>>(T.data, (int)T.nrb, (int)T.nu, dst); break;
+    case 8: qmma_f16_stages_kernel<8><<<grid, kDqThreads, 0, s>>>(T.data, (int)T.nrb, (int)T.nu, dst); break;
+    default: return cudaErrorInvalidValue;
+    }
+    e = cudaGetLastError();
+    if (e == cudaSuccess) T.f16 = dst;
+    return e;
+}
+
 int64_t qgemm_dense_scratch_bytes(const QTensor &T, int ncols) {
     Plan p;
     if (!make_plan(T, ncols, p)) return -1;
@@ -745,7 +805,7 @@ cudaError_t qgemm_dense(const QTensor &T, const float *X, int ncols, float *Y, b
     }
     if (e != cudaSuccess) return e;
     MmaArgs a{T.data, (int)T.nrb, (int)T.nu, Xp, xinv, ncols, p.npad, p.ntiles, p.nch, p.splits, p.RS, p.ST,
-              Y, ldy, T.rows, accumulate ? 1 : 0, xf.ep, ws};
+              Y, ldy, T.rows, accumulate ? 1 : 0, xf.ep, ws, T.f16};
     switch (T.type) {
     case 12: e = launch_qmma<12>(a, p, s); break;
     case 13: e = launch_qmma<13>(a, p, s); break;

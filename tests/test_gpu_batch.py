@@ -145,3 +145,34 @@ def test_split_kv_attention_matches_oracle(O, ctx, mini, B, P, max_ctx):
         st.free()
     finally:
         ctx.set_dense_min_cols(24)
+
+
+def test_batch_dense_fp16_stages_bit_exact(pkg, ctx):
+    """ifr_ctx_set_dense_f16_weights: a batched state whose model keeps fp16
+    operand stages of every projection gives bit-for-bit the logits and
+    tokens of one whose dense GEMMs dequantize on the fly"""
+    from inferno_b200 import synth
+    from inferno_b200.engine import Model, State
+    path = synth.cached("mini", seed=1)
+    out = []
+    for f16 in (False, True):
+        ctx.set_dense_f16_weights(f16)
+        ctx.set_dense_min_cols(8)
+        model = Model(ctx, path)
+        try:
+            B, G = 6, 4
+            prompts = _prompts(model.info.vocab, B, 30)
+            st = State(model, 256, batch=B)
+            st.prefill(prompts)
+            for _ in range(2):
+                st.spec_step(G)
+            lg, _, tk = st.last_verify()
+            out.append((lg.copy(), tk.copy(), [list(st.read(b)[0]) for b in range(B)]))
+            st.free()
+        finally:
+            ctx.set_dense_min_cols(24)
+            ctx.set_dense_f16_weights(True)
+            model.free()
+    (l0, t0, e0), (l1, t1, e1) = out
+    assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+    assert list(t0) == list(t1) and e0 == e1

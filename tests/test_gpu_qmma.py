@@ -70,3 +70,21 @@ def test_dense_zero_and_repeat(O, ctx):
     Y2 = ctx.qgemm_dense(W, torch.from_numpy(X[:17].copy()).cuda()).cpu().numpy()
     assert np.allclose(Y2, Y[:17], rtol=0, atol=1e-6 * np.abs(Y).max())
     ctx.sync()
+
+
+@pytest.mark.parametrize("qt", FORMATS)
+@pytest.mark.parametrize("M,K,N", [(300, 768, 40), (512, 2048, 160), (136, 1024, 300), (2048, 4096, 64),
+                                   (256, 512, 700)])
+def test_dense_fp16_stages_bit_exact(O, ctx, qt, M, K, N):
+    """ifr_tensor_prepare_dense: the dense GEMM copying fp16 operand stages
+    built once gives bit-for-bit the results of the dequantizing kernel
+    (ragged rows, split-K partials, several column tiles)"""
+    import torch
+    rng = np.random.default_rng(M * 7 + K + N + qt)
+    q = O.quantize(qt, rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    W = ctx.upload(qt, q, M, K)
+    X = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).cuda()
+    Y0 = ctx.qgemm_dense(W, X).cpu().numpy()
+    ctx.prepare_dense(W)
+    Y1 = ctx.qgemm_dense(W, X).cpu().numpy()
+    assert np.array_equal(Y0.view(np.uint32), Y1.view(np.uint32)), (NAMES[qt], M, K, N)
