@@ -1111,6 +1111,24 @@ def run_profile(args):
     pkg = ge.load_package()
     pkg.load()
     torch.cuda.set_device(0)
+    if args.profile == "accept":
+        # config 3: one sampled acceptance call (64 x gamma 5 x 151936, T 0.8)
+        # between profiler start / stop, after three warm-up calls
+        B, G, V, T = 64, 5, 151936, 0.8
+        ctx = pkg.Context(0)
+        gen = torch.Generator(device="cuda").manual_seed(3)
+        tgt = torch.randn(B, G + 1, V, generator=gen, device="cuda") * 3
+        dft = (tgt[:, :G] + torch.randn(B, G, V, generator=gen, device="cuda")).contiguous()
+        u = torch.rand(B, 2 * G + 1, generator=gen, device="cuda")
+        for _ in range(3):
+            ctx.accept(tgt, dft, u, T)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        ctx.accept(tgt, dft, u, T)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profile": "accept", "batch": B, "gamma": G, "vocab": V}))
+        return
     if args.profile == "fused":
         import ctypes
         # the config-1 verify's decoder layers as one persistent launch
@@ -1250,7 +1268,7 @@ def main():
     ap.add_argument("--act", type=int, default=None, choices=[0, 1],
                     help="K-quant GEMV activations: 0 = exact f32 (default of the model workloads), "
                          "1 = Q8_K (the reference's kernels; default of the sweep)")
-    ap.add_argument("--profile", choices=["spec", "qgemv", "dense", "batch", "fused"],
+    ap.add_argument("--profile", choices=["spec", "qgemv", "dense", "batch", "fused", "accept"],
                     help="small case for ncu (no JSON line); fused: the fused layer stack's phase trace")
     ap.add_argument("--preset", default=None, help="--profile batch: model preset (default: the config-4 model)")
     ap.add_argument("--qtype", default="Q4_K")

@@ -230,16 +230,55 @@ struct SampleSmem {
     float wsum[8];
 };
 
+// row_stat with every thread of the block: the chunk maxima and the chunk
+// masses cs[c] e^((cm[c] - M) / T) formed in parallel (the loads of a serial
+// loop would each wait a memory round trip), then summed left to right by
+// thread 0 - the same operations in the same order as row_stat.  All threads
+// get the result.
+__device__ RowStat row_stat_blk(const float *cm, const float *cs, int nch, float T, SampleSmem &sm) {
+    if (nch > kNL) {  // more chunks than threads (vocabularies above 512K): the serial form
+        if (threadIdx.x == 0) {
+            const RowStat r = row_stat(cm, cs, nch, T);
+            sm.bc[2] = r.M;
+            sm.bc[3] = r.S;
+        }
+        __syncthreads();
+        const RowStat r{sm.bc[2], sm.bc[3]};
+        __syncthreads();
+        return r;
+    }
+    const int tid = threadIdx.x;
+    const float mv = tid < nch ? cm[tid] : -CUDART_INF_F;
+    const float csv = tid < nch ? cs[tid] : 0.f;
+    const float M = block_max(mv, sm.wsum);
+    if (tid < nch) sm.lsum[tid] = __fmul_rn(csv, ifr_exp(__fdiv_rn(__fsub_rn(mv, M), T)));
+    __syncthreads();
+    if (tid == 0) {
+        float S = 0.f;
+        for (int c = 0; c < nch; c++) S = __fadd_rn(S, sm.lsum[c]);
+        sm.bc[2] = S;
+    }
+    __syncthreads();
+    const RowStat r{M, sm.bc[2]};
+    __syncthreads();  // lsum and bc are reused by the caller
+    return r;
+}
+
 // sample from softmax(row/T) with uniform u; row stats (M,S) and chunk stats
 // given; FILT: over the elements F keeps (F non-null), positive masses only
 template <bool FILT = false>
 __device__ int sample_row(const float *row, int V, const float *cm, const float *cs, int nch,
                           float T, RowStat st, float u, SampleSmem &sm, const SampleFilter *F = nullptr) {
+    // the chunk masses in parallel first (thread 0's scan then reads shared memory)
+    const bool pre = nch <= kNL;
+    if (pre && (int)threadIdx.x < nch)
+        sm.lsum[threadIdx.x] = __fmul_rn(cs[threadIdx.x], ifr_exp(__fdiv_rn(__fsub_rn(cm[threadIdx.x], st.M), T)));
+    __syncthreads();
     if (threadIdx.x == 0) {
         float tau = __fmul_rn(u, st.S), P = 0.f;
         int csel = -1;
         for (int c = 0; c < nch; c++) {
-            const float mc = __fmul_rn(cs[c], ifr_exp(__fdiv_rn(__fsub_rn(cm[c], st.M), T)));
+            const float mc = pre ? sm.lsum[c] : __fmul_rn(cs[c], ifr_exp(__fdiv_rn(__fsub_rn(cm[c], st.M), T)));
             float nP = __fadd_rn(P, mc);
             if ((!FILT || mc > 0.f) && tau <= nP) { csel = c; break; }
             P = nP;
@@ -302,18 +341,24 @@ __global__ void __launch_bounds__(kNL) row_decide_kernel(
     const int b = blockIdx.x, i = blockIdx.y;
     const int tr = b * (G + 1) + i;
     const float *trow = target + (int64_t)tr * V;
-    if (threadIdx.x == 0) {
-        st_s[0] = row_stat(cmax + (int64_t)tr * nch, csum + (int64_t)tr * nch, nch, T);
-        rstat[2 * tr] = st_s[0].M;
-        rstat[2 * tr + 1] = st_s[0].S;
+    {
+        const RowStat st = row_stat_blk(cmax + (int64_t)tr * nch, csum + (int64_t)tr * nch, nch, T, sm);
+        if (threadIdx.x == 0) {
+            st_s[0] = st;
+            rstat[2 * tr] = st.M;
+            rstat[2 * tr + 1] = st.S;
+        }
     }
     if (i == G) return;
     const int dr = B * (G + 1) + b * G + i;
     const float *drow = draft + (int64_t)(b * G + i) * V;
-    if (threadIdx.x == 0) {
-        st_s[1] = row_stat(cmax + (int64_t)dr * nch, csum + (int64_t)dr * nch, nch, T);
-        rstat[2 * dr] = st_s[1].M;
-        rstat[2 * dr + 1] = st_s[1].S;
+    {
+        const RowStat st = row_stat_blk(cmax + (int64_t)dr * nch, csum + (int64_t)dr * nch, nch, T, sm);
+        if (threadIdx.x == 0) {
+            st_s[1] = st;
+            rstat[2 * dr] = st.M;
+            rstat[2 * dr + 1] = st.S;
+        }
     }
     __syncthreads();
     SampleFilter Ft, Fd;
@@ -434,7 +479,11 @@ __global__ void __launch_bounds__(kNL) finish_kernel(
             Ft = filt[tr];
             Fd = filt[dr];
         }
-        const float *rc = rchunk + (int64_t)b * nch;  // residual chunk sums (resid_chunks_kernel)
+        const float *rcg = rchunk + (int64_t)b * nch;  // residual chunk sums (resid_chunks_kernel)
+        const bool pre = nch <= kNL;
+        if (pre && tid < nch) sm.lsum[tid] = rcg[tid];
+        __syncthreads();
+        const float *rc = pre ? sm.lsum : rcg;
         if (tid == 0) {
             float R = 0.f;
             for (int c = 0; c < nch; c++) R = __fadd_rn(R, rc[c]);
