@@ -101,6 +101,11 @@ int ifr_ctx_set_prefill_dense(ifr_ctx *ctx, int enable);
  * Models it does not cover (Gemma4 blocks, other head dims, formats other
  * than Q4_K/Q6_K) keep the separate launches.  Default 0. */
 int ifr_ctx_set_fused_layers(ifr_ctx *ctx, int enable);
+/* failure detection of the fused launch, for tests: runs a two-phase fused
+ * launch in which one CTA never arrives at the grid barrier; the other CTAs'
+ * bounded waits (~2 s) run out and the call returns IFR_ERR_TIMEOUT, with the
+ * context still usable afterwards.  No counterpart in the reference. */
+int ifr_test_fused_timeout(ifr_ctx *ctx);
 /* enable = 1 (default): a batched state (ifr_state_create_batch, batch > 1)
  * gives every projection of its model an fp16 copy of the dequantized weights
  * in the dense GEMM's operand layout (~3.6 x the Q4_K bytes of HBM), which the

@@ -1,6 +1,7 @@
 // C ABI of libinferno_b200 (declared in include/inferno_b200.h).
 #include "../../include/inferno_b200.h"
 #include "common.cuh"
+#include "fused.cuh"
 
 #include <cmath>
 #include <cstdarg>
@@ -242,6 +243,13 @@ int ifr_tensor_prepare_dense(ifr_ctx *c, ifr_tensor *t) {
         return cuda_fail(e, "fp16 stages");
     }
     return IFR_OK;
+}
+
+int ifr_test_fused_timeout(ifr_ctx *c) {
+    if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
+    DeviceGuard g(c->device);
+    IFR_CHECK_CUDA(ifr::fused_absent_cta_test(c->stream), "fused failure test launch");
+    return ifr_sync(c);
 }
 
 int ifr_ctx_set_fused_layers(ifr_ctx *c, int enable) {

@@ -34,7 +34,9 @@ struct FPrefetch {
 };
 
 struct FPhase {
-    enum : int { kNone = 0, kGemv = 1, kSsm = 2, kAttnPart = 3, kAttnCombine = 4, kSsmFinal = 5 };
+    // kTestAbsent: CTA 0 leaves the launch without arriving at the barrier
+    // after this phase (the failure test: the other CTAs' bounded waits run out)
+    enum : int { kNone = 0, kGemv = 1, kSsm = 2, kAttnPart = 3, kAttnCombine = 4, kSsmFinal = 5, kTestAbsent = 9 };
     int kind;
     int nobar;              // 1: the next phase does not read this one's output (no grid barrier)
     int vblocks;            // SSM: heads x row splits; attention: slices x row groups (part) or rows (combine)
@@ -77,5 +79,8 @@ bool fused_attn_phases(const AttnArgs &a, FPhase &part, FPhase &comb);
 // arrival); then CTA 0's end
 cudaError_t fused_layers(const FPhase *phases, int n, unsigned *ctr, unsigned long long *trace, cudaStream_t s);
 cudaError_t read_fused_error(int *flag, cudaStream_t s);
+// the failure test: a two-phase launch in which CTA 0 never arrives at the
+// barrier; the other CTAs wait ~2 s, set the error flag and return
+cudaError_t fused_absent_cta_test(cudaStream_t s);
 
 }  // namespace ifr

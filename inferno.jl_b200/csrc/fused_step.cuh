@@ -617,6 +617,9 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const FPhase
             }
             break;
         }
+        case FPhase::kTestAbsent:
+            if (cta == 0) return;  // uniform over CTA 0: it never arrives at the barrier below
+            break;
         default:
             break;
         }
@@ -671,6 +674,22 @@ cudaError_t fused_layers(const FPhase *phases, int n, unsigned *ctr, unsigned lo
     cfg.attrs = at;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, fused_layers_kernel, phases, n, ctr, trace);
+}
+
+cudaError_t fused_absent_cta_test(cudaStream_t s) {
+    FPhase h[2] = {};
+    h[0].kind = FPhase::kTestAbsent;
+    h[1].kind = FPhase::kNone;
+    void *buf = nullptr;
+    cudaError_t e = cudaMalloc(&buf, sizeof(h) + 256);
+    if (e != cudaSuccess) return e;
+    FPhase *dph = static_cast<FPhase *>(buf);
+    unsigned *ctr = reinterpret_cast<unsigned *>(static_cast<char *>(buf) + sizeof(h) + 128);
+    e = cudaMemcpyAsync(dph, h, sizeof(h), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = fused_layers(dph, 2, ctr, nullptr, s);
+    const cudaError_t e2 = cudaStreamSynchronize(s);
+    cudaFree(buf);
+    return e != cudaSuccess ? e : e2;
 }
 
 bool fused_gemv_phase(const FGemv &g, FPhase &ph) {

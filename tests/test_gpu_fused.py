@@ -169,3 +169,29 @@ def test_fused_graph_capture(pkg, ctx, tiny):
     finally:
         torch.cuda.synchronize()
         c2.close()
+
+
+def test_fused_barrier_timeout_reported_and_context_usable(O, pkg, ctx, tiny):
+    """failure detection without a fault: one CTA of a fused launch leaves
+    without arriving at the grid barrier; the others' bounded waits (~2 s)
+    run out, the launch returns, ifr_sync reports IFR_ERR_TIMEOUT, and the
+    context then runs a fused spec step that matches the separate launches"""
+    from inferno_b200 import _lib, synth
+    from inferno_b200.engine import State
+    rc = _lib.load().ifr_test_fused_timeout(ctx.handle)
+    assert rc == _lib.IFR_ERR_TIMEOUT, rc
+    ctx.sync()  # the error flag was read and cleared
+    prompt = synth.prompt(tiny.info.vocab, 24, seed=77)
+    fa, sep = State(tiny, 128), State(tiny, 128)
+    fa.prefill(prompt)
+    sep.prefill(prompt)
+    ctx.set_fused_layers(True)
+    fa.spec_step(4)
+    ctx.set_fused_layers(False)
+    sep.spec_step(4)
+    lg_f, _, tk_f = fa.last_verify()
+    lg_s, _, tk_s = sep.last_verify()
+    assert list(tk_f) == list(tk_s)
+    assert np.abs(lg_f - lg_s).max() / np.abs(lg_s).max() < PATH_TOL
+    fa.free()
+    sep.free()
