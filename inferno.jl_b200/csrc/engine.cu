@@ -212,6 +212,9 @@ struct DevLayer {
     // output; sliding layers attend within the window
     bool sliding = false;
     float *ffn_norm = nullptr, *post_ffw_norm = nullptr, *layer_scalar = nullptr;
+    // Gemma4 per-layer input block: gate (pli x d), projection (d x pli), post norm
+    Proj pli_gate, pli_proj;
+    float *pli_post_norm = nullptr;
 };
 
 struct ifr_model {
@@ -236,6 +239,12 @@ struct ifr_model {
     int window = 0, sliding_pattern = 0;
     float attn_softcap = 0.f, final_softcap = 0.f, embed_scale = 1.f;
     float rope_theta_swa = 10000.f, partial_rotary = 0.25f;
+    // Gemma4 per-layer inputs (compute_per_layer_inputs!, Gemma4.jl:459-503):
+    // pli values per layer (0: none), the token table (vocab x L pli), the model
+    // projection (L pli x d, stored pre-scaled by d^-1/2) and its norm
+    int pli = 0;
+    Proj pli_token_embd, pli_model_proj;
+    float *pli_proj_norm = nullptr;
     std::vector<void *> dev_allocs;
     ~ifr_model() {
         for (void *p : dev_allocs) cudaFree(p);
@@ -437,7 +446,17 @@ int load_layer(ifr_model *m, const Gguf &g, const std::string &pre, DevLayer &L,
         if ((rc = upload_gate_up(m, g, pre + "ffn_gate.weight", pre + "ffn_up.weight", &L.gate_up, sf))) return rc;
         if (!L.gate_up.glu)
             return ifr_fail(IFR_ERR_UNSUPPORTED, "%s: gemma4 gate/up must share a type and 16-row blocks", pre.c_str());
-        return upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down, {sd});
+        if ((rc = upload_proj(m, g, {pre + "ffn_down.weight"}, &L.down, {sd}))) return rc;
+        if (m->pli) {
+            // per-layer input block (Gemma4Loader.jl:230-239), whole on every rank
+            if ((rc = upload_proj(m, g, {pre + "pli_gate.weight"}, &L.pli_gate))) return rc;
+            if ((rc = upload_proj(m, g, {pre + "pli_proj.weight"}, &L.pli_proj))) return rc;
+            if ((rc = upload_f32(m, g, pre + "pli_post_norm.weight", c.hidden, &L.pli_post_norm))) return rc;
+            if (L.pli_gate.rows != m->pli || L.pli_gate.cols != c.hidden || L.pli_proj.rows != c.hidden ||
+                L.pli_proj.cols != m->pli)
+                return ifr_fail(IFR_ERR_ARG, "%s: per-layer input shapes do not match the config", pre.c_str());
+        }
+        return IFR_OK;
     }
     if ((rc = upload_f32(m, g, pre + "attn_norm.weight", c.hidden, &L.attn_norm))) return rc;
     if ((rc = upload_f32(m, g, pre + "post_attention_norm.weight", c.hidden, &L.post_norm))) return rc;
@@ -512,6 +531,7 @@ struct ifr_state {
     unsigned *am_count = nullptr;       // its completion counter (returns to 0)
     float *rope_cos, *rope_sin;
     float *rope_cos_full = nullptr, *rope_sin_full = nullptr;  // Gemma4 full-attention layers
+    float *pli_emb = nullptr, *pli_tmp = nullptr, *pli_in = nullptr, *pli_g = nullptr;  // Gemma4 per-layer inputs
     std::vector<float *> S, hist, rq, rkv;      // per layer (SSM) else null
     std::vector<float *> kc, vc;                // per layer (attention) else null
     float *mtp_kc = nullptr, *mtp_vc = nullptr;
@@ -792,8 +812,18 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         if ((rc = gemv(s, gcat, L.gate_up, s->x, nc, s->hmid, false, st, glu))) return rc;
         if ((rc = gemv(s, gcat, L.down, s->hmid, nc, s->xn, false, st))) return rc;
         if ((rc = allreduce(s, s->xn, (size_t)nc * d, st))) return rc;
-        ifr::norm_add(s->xn, L.post_ffw_norm, s->x, nc, d, c.rms_eps, L.layer_scalar, st);
+        const bool pli = m->pli && !draft && li >= 0;
+        ifr::norm_add(s->xn, L.post_ffw_norm, s->x, nc, d, c.rms_eps, pli ? nullptr : L.layer_scalar, st);
         s->launches += 2;
+        if (pli) {
+            // per_layer_input_forward! (Gemma4.jl:505-533, :626-634):
+            // x = (x + RMSNorm(proj(gelu_tanh(gate x) * pli_i))) * layer_scalar
+            if ((rc = gemv(s, gcat, L.pli_gate, s->x, nc, s->pli_g, false, st))) return rc;
+            ECHECK(ifr::pli_gate(s->pli_g, s->pli_in, m->pli, (int64_t)c.n_layers * m->pli, li, nc, st), "pli gate");
+            if ((rc = gemv(s, gcat, L.pli_proj, s->pli_g, nc, s->xn, false, st))) return rc;
+            ifr::norm_add(s->xn, L.pli_post_norm, s->x, nc, d, c.rms_eps, L.layer_scalar, st);
+            s->launches += 2;
+        }
         return IFR_OK;
     }
     if (L.ssm) {
@@ -1180,6 +1210,22 @@ int target_forward(ifr_state *s, int n, bool logits, bool first_from_state, cuda
                         s->x, m->embed_scale, st),
            "embedding");
     s->launches += 2;  // embedding, final norm
+    if (m->pli) {
+        // compute_per_layer_inputs! (Gemma4.jl:459-503) for every column: the
+        // token table rows, the model projection of the scaled embedding, then
+        // per layer (RMSNorm(proj) + row sqrt(pli)) 2^-1/2
+        const int64_t lp = (int64_t)c.n_layers * m->pli;
+        ECHECK(launch_embed(m->pli_token_embd.parts[0], s->vtok, first_from_state ? &s->sc->last_token : nullptr, sc_ld,
+                            n, B, s->pli_emb, 1.0f, st),
+               "per-layer input table");
+        int rc = gemv(s, CAT_LAYER_GEMV, m->pli_model_proj, s->x, nc, s->pli_tmp, false, st);
+        if (rc) return rc;
+        ECHECK(ifr::pli_inputs(s->pli_tmp, s->pli_emb, m->pli_proj_norm, m->pli, c.n_layers, nc, c.rms_eps,
+                               s->pli_in, st),
+               "per-layer inputs");
+        (void)lp;
+        s->launches += 2;
+    }
     if (n > kNMax) {
         ifr::chunk_positions(s->chunk_pos, s->sc, (n + kNMax - 1) / kNMax, kNMax, st);
         s->launches++;
@@ -1351,7 +1397,9 @@ int ifr_model_load_gguf_tp(ifr_ctx *ctx, const char *path, ifr_comm *comm, ifr_m
         c.rope_theta = (float)md("rope.freq_base", 1000000.0);
         m->partial_rotary = (float)md("rope.partial_rotary_factor", 0.25);
         m->embed_scale = (float)std::sqrt((double)c.hidden);
+        m->pli = (int)md("embedding_length_per_layer_input", 0);
         if (g.has("mtp.fc.weight")) rc = ifr_fail(IFR_ERR_UNSUPPORTED, "gemma4 models have no MTP head here");
+        if (!rc && (m->pli < 0 || m->pli % 32)) rc = ifr_fail(IFR_ERR_ARG, "per-layer input size %d", m->pli);
     }
     auto te = g.t.find("token_embd.weight");
     if (te == g.t.end() || te->second.dims.size() != 2) rc = ifr_fail(IFR_ERR_ARG, "token_embd.weight missing");
@@ -1418,6 +1466,16 @@ int ifr_model_load_gguf_tp(ifr_ctx *ctx, const char *path, ifr_comm *comm, ifr_m
         }
     }
     if (!rc && m->embed.parts.size() != 1) rc = ifr_fail(IFR_ERR_ARG, "bad embedding");
+    if (!rc && m->pli) {
+        // per-layer input tables (Gemma4Loader.jl:142-151), whole on every rank
+        rc = upload_proj(m, g, {"pli_token_embd.weight"}, &m->pli_token_embd);
+        if (!rc) rc = upload_proj(m, g, {"pli_model_proj.weight"}, &m->pli_model_proj);
+        if (!rc) rc = upload_f32(m, g, "pli_proj_norm.weight", m->pli, &m->pli_proj_norm);
+        const int64_t lp = (int64_t)c.n_layers * m->pli;
+        if (!rc && (m->pli_token_embd.parts.size() != 1 || m->pli_token_embd.cols != lp ||
+                    m->pli_model_proj.rows != lp || m->pli_model_proj.cols != c.hidden))
+            rc = ifr_fail(IFR_ERR_ARG, "per-layer input tables do not match the config");
+    }
     if (!rc) rc = upload_f32(m, g, "output_norm.weight", c.hidden, &m->final_norm);
     m->layers.resize(c.n_layers);
     for (int i = 0; !rc && i < c.n_layers; i++) {
@@ -1532,6 +1590,13 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     if (m->gemma) {
         chk(dalloc(s, &s->rope_cos_full, (size_t)max_ctx * half));
         chk(dalloc(s, &s->rope_sin_full, (size_t)max_ctx * half));
+    }
+    if (m->pli) {
+        const size_t lp = (size_t)c.n_layers * m->pli;
+        chk(dalloc(s, &s->pli_emb, (size_t)N * lp));
+        chk(dalloc(s, &s->pli_tmp, (size_t)N * lp));
+        chk(dalloc(s, &s->pli_in, (size_t)N * lp));
+        chk(dalloc(s, &s->pli_g, (size_t)N * m->pli));
     }
     s->S.assign(c.n_layers, nullptr);
     s->hist.assign(c.n_layers, nullptr);

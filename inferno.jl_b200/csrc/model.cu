@@ -116,6 +116,52 @@ void softcap(float *l, int64_t n, float cap, cudaStream_t s) {
     launch_k(softcap_kernel, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256), 0, s, l, n, cap);
 }
 
+// Gemma4 per-layer inputs (compute_per_layer_inputs!, Gemma4.jl:459-503):
+// block (layer i, column c), 256 threads: RMSNorm of the projection slice
+// (CommonOps.rmsnorm!), plus the table row slice times sqrt(P), times 2^-1/2
+__global__ void __launch_bounds__(256) pli_inputs_kernel(const float *__restrict__ proj, const float *__restrict__ emb,
+                                                         const float *__restrict__ w, int P, int L, float eps,
+                                                         float *__restrict__ out) {
+    __shared__ float red[8];
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
+    const int64_t base = (int64_t)c * L * P + (int64_t)i * P;
+    float ss = 0.f;
+    for (int j = tid; j < P; j += 256) ss += proj[base + j] * proj[base + j];
+    ss = block_sum256_b<0>(ss, red, tid);
+    const float inv = 1.0f / sqrtf(ss / (float)P + eps);
+    const float scale = sqrtf((float)P), in_scale = 0.707106781186547524f;  // Float32(2^-1/2)
+    for (int j = tid; j < P; j += 256) {
+        const float o = proj[base + j] * inv * w[j];
+        out[base + j] = (o + emb[base + j] * scale) * in_scale;
+    }
+}
+
+cudaError_t pli_inputs(const float *proj, const float *emb, const float *w, int P, int L, int nc, float eps,
+                       float *out, cudaStream_t s) {
+    if (P < 1 || L < 1 || nc < 1) return cudaErrorInvalidValue;
+    return launch_k(pli_inputs_kernel, dim3(L, nc), dim3(256), 0, s, proj, emb, w, P, L, eps, out);
+}
+
+// per_layer_input_forward! (Gemma4.jl:514-524): g = gelu_tanh(g) * pli slice
+__global__ void pli_gate_kernel(float *__restrict__ g, const float *__restrict__ pli, int P, int64_t lp, int layer,
+                                int64_t n) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t c = i / P;
+    const int j = (int)(i % P);
+    const float v = gelu_tanh(g[i]);
+    g[i] = v * pli[c * lp + (int64_t)layer * P + j];
+}
+
+cudaError_t pli_gate(float *g, const float *pli, int P, int64_t lp, int layer, int nc, cudaStream_t s) {
+    const int64_t n = (int64_t)nc * P;
+    return launch_k(pli_gate_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, g, pli, P, lp, layer, n);
+}
+
 // ------------------------------------------------------------- SwiGLU -------
 // mlp_forward (ModelCPU.jl:482-508): h = silu(g) * u with g, u from one GEMV
 // whose output rows are [gate (ffn) | up (ffn)]

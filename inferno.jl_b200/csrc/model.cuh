@@ -80,6 +80,13 @@ void norm_add(const float *y, const float *w, float *x, int cols, int n, float e
               cudaStream_t s);
 // l = tanh(l / cap) cap in place (final logit softcap)
 void softcap(float *l, int64_t n, float cap, cudaStream_t s);
+// Gemma4 per-layer inputs (compute_per_layer_inputs!, Gemma4.jl:459-503), nc
+// columns: out[c][i P + j] = (RMSNorm(proj[c][i P ..], w)_j + emb[c][i P + j]
+// sqrt(P)) 2^-1/2 for each of the L layers
+cudaError_t pli_inputs(const float *proj, const float *emb, const float *w, int P, int L, int nc, float eps,
+                       float *out, cudaStream_t s);
+// per_layer_input_forward! (:514-524): g[c][j] = gelu_tanh(g[c][j]) pli[c][layer P + j]
+cudaError_t pli_gate(float *g, const float *pli, int P, int64_t lp, int layer, int nc, cudaStream_t s);
 cudaError_t ssm_step(const SsmArgs &a, int head_dim, int batch, cudaStream_t s);
 // a prefill chunk of a.N <= 64 tokens of one request, committed at once (no
 // replay record; the caller's commit must leave nothing to replay)

@@ -69,6 +69,12 @@ PRESETS = {
                        rope_frac=0.25, ffn=512, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
                        attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=False,
                        context=2048, window=6, pattern=2, attn_cap=10.0, final_cap=1.0),
+    # gemma_mini with Gemma4 per-layer inputs (256 per layer)
+    "gemma_pli": dict(arch="gemma4", hidden=256, n_layers=4, n_head=4, n_kv_head=2, head_dim=128,
+                      rope_frac=0.25, ffn=512, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
+                      attn_every=1, mat=G.GGML_Q4_K, down=G.GGML_Q4_K, emb=G.GGML_Q6_K, mtp=False,
+                      context=2048, window=6, pattern=2, attn_cap=10.0, final_cap=1.0, pli=256,
+                      pli_emb=G.GGML_Q8_0),
     # attention-only test model whose heads and FFN units split over 2 ranks
     "tp_mini": dict(hidden=256, n_layers=4, n_head=8, n_kv_head=4, head_dim=64, rope_frac=0.25,
                     ffn=1024, vocab=4096, ssm_heads=0, ssm_head_dim=0, conv_kernel=4,
@@ -203,6 +209,9 @@ def _build_gemma(w, cfg, preset, seed, root, quant):
     w.add(f"{arch}.rope.partial_rotary_factor", float(cfg["rope_frac"]))
     w.add(f"{arch}.attn_logit_softcapping", float(cfg.get("attn_cap", 50.0)))
     w.add(f"{arch}.final_logit_softcapping", float(cfg.get("final_cap", 30.0)))
+    P = int(cfg.get("pli", 0))
+    if P:
+        w.add(f"{arch}.embedding_length_per_layer_input", P)
 
     def rng():
         return np.random.default_rng(root.integers(1 << 62))
@@ -239,6 +248,17 @@ def _build_gemma(w, cfg, preset, seed, root, quant):
         mat(pre + "ffn_up.weight", ffn, d, cfg["mat"])
         mat(pre + "ffn_down.weight", d, ffn, cfg["down"])
         f32(pre + "layer_scalar", [1], [1.0 + 0.05 * float(rng().standard_normal())])
+        if P:
+            # per-layer input block: gate (P x d), projection (d x P), post norm
+            mat(pre + "pli_gate.weight", P, d, cfg["mat"])
+            mat(pre + "pli_proj.weight", d, P, cfg["mat"])
+            norm(pre + "pli_post_norm.weight", d)
+    if P:
+        # the token table (vocab x L P), the model projection (L P x d, stored
+        # already scaled by d^-1/2, as the reference scales it at load) and its norm
+        mat("pli_token_embd.weight", V, L * P, cfg.get("pli_emb", cfg["emb"]))
+        mat("pli_model_proj.weight", L * P, d, cfg["mat"], std=0.02 / float(np.sqrt(d)))
+        norm("pli_proj_norm.weight", P)
     w.write()
     return w.path
 

@@ -36,7 +36,13 @@
  *   mlp_forward!            :556-581  down(gelu_tanh(gate x) * up x)
  *   get_logits              :678-693  tied lm_head, then logit_softcap!
  *                                     (CommonOps.jl:326-333)
- *   per-layer inputs (:459-554) are not part of this model (config 5 has none)
+ *   compute_per_layer_inputs! / per_layer_input_forward! (:459-533, :626-634):
+ *                                     per-layer inputs when the config's pli > 0
+ *                                     (config 5 has none): per token, per layer
+ *                                     (RMSNorm(proj_i) + table_i sqrt(pli)) 2^-1/2;
+ *                                     after each MLP block
+ *                                     x += RMSNorm(proj(gelu_tanh(gate x) * pli_i)),
+ *                                     before the layer scalar
  * Matrix-vector products accumulate in f32 in index order (activation mode
  * 0, default: the GPU engine's exact f32 activations).  In mode 1 those with
  * K-quant weights (Q4_K/Q5_K/Q6_K) follow the reference's quantized kernels:
@@ -56,6 +62,7 @@ typedef struct {
     int ssm;
     float *attn_norm, *post_norm;
     float *ffn_norm, *post_ffw_norm, *layer_scalar;   /* Gemma4 */
+    float *pli_gate, *pli_proj, *pli_post_norm;       /* Gemma4 per-layer inputs */
     /* ssm */
     float *in_proj, *gate_proj, *ssm_out, *conv_w, *alpha_w, *beta_w, *ssm_a, *dt_bias, *ssm_norm;
     float *conv_state, *h;                  /* [C][K], [heads][vd][kd] */
@@ -81,6 +88,8 @@ struct or_model {
     int gemma;                      /* Gemma4 block semantics */
     or_gemma_config g;
     float *cos_swa, *sin_swa, *cos_full, *sin_full;   /* [max_ctx][hd/2] */
+    float *pli_token_embd, *pli_model_proj, *pli_proj_norm;  /* Gemma4 per-layer inputs */
+    float *pli_in;                                   /* [n_layers][pli] of the current token */
 };
 
 static void *xcalloc(size_t n, size_t s) { void *p = calloc(n, s); if (!p) abort(); return p; }
@@ -112,7 +121,8 @@ static void free_layer(or_layer *L) {
     float **f[] = {&L->attn_norm, &L->post_norm, &L->in_proj, &L->gate_proj, &L->ssm_out, &L->conv_w,
                    &L->alpha_w, &L->beta_w, &L->ssm_a, &L->dt_bias, &L->ssm_norm, &L->conv_state, &L->h,
                    &L->wq, &L->wk, &L->wv, &L->wo, &L->q_norm, &L->k_norm, &L->kc, &L->vc,
-                   &L->ffn_gate, &L->ffn_up, &L->ffn_down, &L->ffn_norm, &L->post_ffw_norm, &L->layer_scalar};
+                   &L->ffn_gate, &L->ffn_up, &L->ffn_down, &L->ffn_norm, &L->post_ffw_norm, &L->layer_scalar,
+                   &L->pli_gate, &L->pli_proj, &L->pli_post_norm};
     for (size_t i = 0; i < sizeof f / sizeof f[0]; i++) { free(*f[i]); *f[i] = NULL; }
 }
 
@@ -124,6 +134,7 @@ void or_model_free(or_model *m) {
     free(m->embed); free(m->final_norm); free(m->mtp_fc); free(m->mtp_norm_e); free(m->mtp_norm_h);
     free(m->mtp_norm); free(m->cos_cache); free(m->sin_cache);
     free(m->cos_swa); free(m->sin_swa); free(m->cos_full); free(m->sin_full);
+    free(m->pli_token_embd); free(m->pli_model_proj); free(m->pli_proj_norm); free(m->pli_in);
     free(m);
 }
 
@@ -138,6 +149,9 @@ static float **slot(or_model *m, int layer, int kind) {
         case OR_T_MTP_NORM_E: return &m->mtp_norm_e;
         case OR_T_MTP_NORM_H: return &m->mtp_norm_h;
         case OR_T_MTP_NORM: return &m->mtp_norm;
+        case OR_T_PLI_TOKEN_EMBD: return &m->pli_token_embd;
+        case OR_T_PLI_MODEL_PROJ: return &m->pli_model_proj;
+        case OR_T_PLI_PROJ_NORM: return &m->pli_proj_norm;
         }
         return NULL;
     }
@@ -165,6 +179,9 @@ static float **slot(or_model *m, int layer, int kind) {
     case OR_T_FFN_NORM: return &L->ffn_norm;
     case OR_T_POST_FFW_NORM: return &L->post_ffw_norm;
     case OR_T_LAYER_SCALAR: return &L->layer_scalar;
+    case OR_T_PLI_GATE: return &L->pli_gate;
+    case OR_T_PLI_PROJ: return &L->pli_proj;
+    case OR_T_PLI_POST_NORM: return &L->pli_post_norm;
     }
     return NULL;
 }
@@ -470,6 +487,8 @@ static void decoder_layer(or_model *m, or_layer *L, float *x, int pos) {
 void or_model_set_gemma(or_model *m, const or_gemma_config *g) {
     m->gemma = 1;
     m->g = *g;
+    free(m->pli_in);
+    m->pli_in = g->pli > 0 ? (float *)xcalloc((size_t)m->c.n_layers * g->pli, 4) : NULL;
     const int hd = m->c.head_dim, half = hd / 2, T = m->c.max_ctx;
     const int angles = (int)(g->partial_rotary_factor * (float)hd) / 2;  /* Int(partial * hd / 2) */
     free(m->cos_swa); free(m->sin_swa); free(m->cos_full); free(m->sin_full);
@@ -582,6 +601,37 @@ static void gemma_mlp(or_model *m, or_layer *L, const float *x, float *out) {
     free(g); free(u);
 }
 
+/* compute_per_layer_inputs! (:459-503) for the token: per layer i,
+   (RMSNorm(proj_i, w) + table_row_i * sqrt(pli)) * 2^-1/2, proj = the model
+   projection (pre-scaled) of the scaled embedding x */
+static void gemma_pli_inputs(or_model *m, int token, const float *x) {
+    const int P = m->g.pli, n = m->c.n_layers, d = m->c.hidden;
+    float *proj = (float *)malloc((size_t)n * P * 4);
+    matvec_w(m, proj, m->pli_model_proj, x, n * P, d);
+    const float scale = sqrtf((float)P), in_scale = (float)pow(2.0, -0.5);
+    const float *row = m->pli_token_embd + (size_t)token * n * P;
+    for (int i = 0; i < n; i++) {
+        float *o = m->pli_in + (size_t)i * P;
+        rmsnorm(o, proj + (size_t)i * P, m->pli_proj_norm, P, m->c.rms_eps);
+        for (int j = 0; j < P; j++) o[j] = (o[j] + row[(size_t)i * P + j] * scale) * in_scale;
+    }
+    free(proj);
+}
+
+/* per_layer_input_forward! (:505-533): x += RMSNorm(proj(gelu_tanh(gate x) * pli_i)) */
+static void gemma_pli_block(or_model *m, or_layer *L, int layer, float *x) {
+    const int P = m->g.pli, d = m->c.hidden;
+    float *g = (float *)malloc((size_t)P * 4), *o = (float *)malloc((size_t)d * 4);
+    matvec_w(m, g, L->pli_gate, x, P, d);
+    const float *pl = m->pli_in + (size_t)layer * P;
+    for (int j = 0; j < P; j++) g[j] = gelu_tanh(g[j]);
+    for (int j = 0; j < P; j++) g[j] *= pl[j];
+    matvec_w(m, o, L->pli_proj, g, d, P);
+    rmsnorm(o, o, L->pli_post_norm, d, m->c.rms_eps);
+    for (int i = 0; i < d; i++) x[i] = x[i] + o[i];
+    free(g); free(o);
+}
+
 /* the layer body of forward! (:622-650) */
 static void gemma_layer(or_model *m, or_layer *L, int layer, float *x, int pos) {
     const int d = m->c.hidden;
@@ -595,6 +645,7 @@ static void gemma_layer(or_model *m, or_layer *L, int layer, float *x, int pos) 
     gemma_mlp(m, L, xn, r);
     rmsnorm(r, r, L->post_ffw_norm, d, eps);
     for (int i = 0; i < d; i++) x[i] = x[i] + r[i];
+    if (m->g.pli > 0 && L->pli_gate) gemma_pli_block(m, L, layer, x);
     const float s = L->layer_scalar ? L->layer_scalar[0] : 1.0f;
     for (int i = 0; i < d; i++) x[i] *= s;
     free(xn); free(r);
@@ -605,6 +656,7 @@ static int gemma_forward_token(or_model *m, int token, int pos, float *logits, f
     const int d = c->hidden;
     float *x = (float *)malloc(d * 4), *xn = (float *)malloc(d * 4);
     for (int i = 0; i < d; i++) x[i] = m->embed[(size_t)token * d + i] * m->g.embed_scale;
+    if (m->g.pli > 0) gemma_pli_inputs(m, token, x);
     for (int i = 0; i < c->n_layers; i++) gemma_layer(m, &m->layers[i], i, x, pos);
     rmsnorm(xn, x, m->final_norm, d, c->rms_eps);
     if (hidden) memcpy(hidden, xn, d * 4);

@@ -91,7 +91,12 @@ enum {
     OR_T_ALPHA, OR_T_BETA, OR_T_SSM_A, OR_T_DT_BIAS, OR_T_SSM_NORM, OR_T_WQ, OR_T_WK, OR_T_WV,
     OR_T_WO, OR_T_Q_NORM, OR_T_K_NORM, OR_T_FFN_GATE, OR_T_FFN_UP, OR_T_FFN_DOWN,
     /* Gemma4 blocks: pre-MLP norm, post-MLP norm, layer scalar (1 element) */
-    OR_T_FFN_NORM, OR_T_POST_FFW_NORM, OR_T_LAYER_SCALAR
+    OR_T_FFN_NORM, OR_T_POST_FFW_NORM, OR_T_LAYER_SCALAR,
+    /* Gemma4 per-layer inputs: per layer gate (pli x d), projection (d x pli),
+       post norm (d); global token table (vocab x L pli), model projection
+       (L pli x d, pre-scaled by d^-1/2) and its norm (pli) */
+    OR_T_PLI_GATE = 40, OR_T_PLI_PROJ, OR_T_PLI_POST_NORM,
+    OR_T_PLI_TOKEN_EMBD = 50, OR_T_PLI_MODEL_PROJ, OR_T_PLI_PROJ_NORM
 };
 /* Gemma4 block semantics (src/Gemma4.jl:253-688, src/CommonOps.jl:326-333),
  * switched on by or_model_set_gemma: layer i is a full-attention layer iff
@@ -101,6 +106,7 @@ typedef struct {
     float attn_softcap, final_softcap;   /* 0: off */
     float rope_theta_swa, rope_theta_full, partial_rotary_factor;
     float embed_scale;
+    int32_t pli;                         /* per-layer input size (0: none) */
 } or_gemma_config;
 void or_model_set_gemma(or_model *m, const or_gemma_config *g);
 or_model *or_model_new(const or_model_config *c);

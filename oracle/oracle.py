@@ -346,15 +346,17 @@ _KIND = {"attn_norm.weight": 10, "post_attention_norm.weight": 11, "attn_qkv.wei
          "ssm_beta.weight": 17, "ssm_a": 18, "ssm_dt.bias": 19, "ssm_norm.weight": 20,
          "attn_q.weight": 21, "attn_k.weight": 22, "attn_v.weight": 23, "attn_output.weight": 24,
          "attn_q_norm.weight": 25, "attn_k_norm.weight": 26, "ffn_gate.weight": 27, "ffn_up.weight": 28,
-         "ffn_down.weight": 29, "ffn_norm.weight": 30, "post_ffw_norm.weight": 31, "layer_scalar": 32}
+         "ffn_down.weight": 29, "ffn_norm.weight": 30, "post_ffw_norm.weight": 31, "layer_scalar": 32,
+         "pli_gate.weight": 40, "pli_proj.weight": 41, "pli_post_norm.weight": 42}
 _GLOBAL = {"token_embd.weight": 0, "output_norm.weight": 1, "mtp.fc.weight": 2,
-           "mtp.pre_fc_norm_embedding.weight": 3, "mtp.pre_fc_norm_hidden.weight": 4, "mtp.norm.weight": 5}
+           "mtp.pre_fc_norm_embedding.weight": 3, "mtp.pre_fc_norm_hidden.weight": 4, "mtp.norm.weight": 5,
+           "pli_token_embd.weight": 50, "pli_model_proj.weight": 51, "pli_proj_norm.weight": 52}
 
 
 class _GemmaCfg(ctypes.Structure):
     _fields_ = [("window", ctypes.c_int32), ("sliding_pattern", ctypes.c_int32)] + [
         (n, ctypes.c_float) for n in ("attn_softcap", "final_softcap", "rope_theta_swa", "rope_theta_full",
-                                      "partial_rotary_factor", "embed_scale")]
+                                      "partial_rotary_factor", "embed_scale")] + [("pli", ctypes.c_int32)]
 
 
 def gemma_config(md, hidden):
@@ -365,7 +367,8 @@ def gemma_config(md, hidden):
                      float(g("attn_logit_softcapping", 0.0)), float(g("final_logit_softcapping", 0.0)),
                      float(g("rope.freq_base_swa", 10000.0)), float(g("rope.freq_base", 1000000.0)),
                      float(g("rope.partial_rotary_factor", 0.25)),
-                     float(np.float32(np.sqrt(np.float64(hidden)))))
+                     float(np.float32(np.sqrt(np.float64(hidden)))),
+                     int(g("embedding_length_per_layer_input", 0)))
 
 
 def _model_lib():

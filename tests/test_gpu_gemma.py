@@ -131,3 +131,78 @@ def test_gemma_draft_model_spec_decode(O, ctx, gmini):
     ts.free()
     ds.free()
     draft.free()
+
+
+@pytest.fixture(scope="module")
+def gpli(pkg, O, ctx):
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model
+    path = synth.cached("gemma_pli", seed=1)
+    model = Model(ctx, path)
+    om = O.OracleModel(gguf.GGUFFile(path), 256)
+    assert om.gemma and om.gcfg.pli == 256
+    yield path, model, om
+    model.free()
+
+
+def test_gemma_per_layer_inputs_match_oracle(O, ctx, gpli):
+    """Gemma4 per-layer inputs (compute_per_layer_inputs! and
+    per_layer_input_forward!, Gemma4.jl:459-533): the per-token table rows
+    and model projection, and after every MLP block the gated per-layer
+    projection before the layer scalar; one request through a 70-token
+    prompt (a 64-token prefill chunk and single tokens) and spec steps with
+    forced drafts: tokens equal, verify logits within 1e-4"""
+    from inferno_b200 import synth
+    from inferno_b200.engine import State
+    _, model, om = gpli
+    G, steps = 3, 5
+    prompt = synth.prompt(om.vocab, 70, seed=9)
+    greedy, drafts = _forced_plan(om, prompt, G, steps)
+    st = State(model, 200)
+    emitted = [int(st.prefill(prompt))]
+    assert emitted[0] == greedy[0]
+    used, logits = [], []
+    for s in range(steps):
+        d = drafts(s, emitted)
+        used.append(d)
+        st.spec_step(G, d)
+        logits.append(st.last_verify()[0])
+        emitted = [int(t) for t in st.read()[0]]
+    out, ref = om.spec_decode(list(prompt), steps, G, drafts=lambda s: used[s])
+    assert emitted == out
+    for s in range(steps):
+        err = O.norm_rel(logits[s], ref[s]["logits"]).max()
+        assert err < LOGIT_TOL, (s, err)
+    st.free()
+
+
+def test_gemma_per_layer_inputs_batch(O, ctx, gpli):
+    """two requests in one state with per-layer inputs, exact path"""
+    from inferno_b200 import synth
+    from inferno_b200.engine import State
+    _, model, om = gpli
+    B, G, steps = 2, 2, 3
+    prompts = np.stack([synth.prompt(om.vocab, 15, seed=60 + b) for b in range(B)])
+    plans = [_forced_plan(om, p, G, steps) for p in prompts]
+    ctx.set_dense_min_cols(10**6)
+    try:
+        st = State(model, 128, batch=B)
+        firsts = st.prefill(prompts)
+        emitted = [[int(firsts[b])] for b in range(B)]
+        used = [[] for _ in range(B)]
+        logits = []
+        for s in range(steps):
+            d = np.array([plans[b][1](s, emitted[b]) for b in range(B)], np.int32)
+            for b in range(B):
+                used[b].append(list(d[b]))
+            st.spec_step(G, d)
+            logits.append(st.last_verify()[0].reshape(B, G + 1, -1))
+            emitted = [[int(t) for t in st.read(b)[0]] for b in range(B)]
+        for b in range(B):
+            out, ref = om.spec_decode(list(prompts[b]), steps, G, drafts=lambda s: used[b][s])
+            assert emitted[b] == out, b
+            for s in range(steps):
+                assert O.norm_rel(logits[s][b], ref[s]["logits"]).max() < LOGIT_TOL, (b, s)
+        st.free()
+    finally:
+        ctx.set_dense_min_cols(24)

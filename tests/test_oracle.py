@@ -213,3 +213,56 @@ def test_gemma_oracle_blocks(O, pkg, tmp_path):
     assert a == b
     lg, _ = om.forward_token(a[-1], len(prompt) + 5)
     assert np.isfinite(lg).all() and np.abs(lg).max() <= om.gcfg.final_softcap
+
+
+def test_gemma_oracle_per_layer_inputs_first_token(O, pkg, tmp_path):
+    """the oracle's Gemma4 per-layer inputs against an independent numpy
+    restatement of forward! for the first token (Gemma4.jl:459-533, 604-676):
+    at position 0 every attention head sees one key, so the block reduces to
+    norms and projections and the whole layer stack is a few matrix products"""
+    from inferno_b200 import synth, gguf
+    path = synth.build(str(tmp_path / "p.gguf"), "gemma_pli", 1, quantize=O.quantize)
+    f = gguf.GGUFFile(path)
+    om = O.OracleModel(f, 16)
+    cfg = om.gcfg
+    assert cfg.pli == 256
+    d, L, P = om.hidden, om.cfg.n_layers, cfg.pli
+    nh, nkv, hd = om.cfg.n_head, om.cfg.n_kv_head, om.cfg.head_dim
+    eps = np.float32(om.cfg.rms_eps)
+
+    def W(name):
+        ti = f.tensors[name]
+        v = O.dequantize(ti.type, np.ascontiguousarray(f.raw(name)), ti.n_elements).astype(np.float64)
+        return v.reshape(list(reversed(ti.dims))) if len(ti.dims) == 2 else v
+
+    def rms(x, w):
+        return x / np.sqrt(np.mean(x * x) + eps) * w
+
+    def gelu(x):
+        c = np.sqrt(2.0 / np.pi)
+        return 0.5 * x * (1.0 + np.tanh(c * (x + 0.044715 * x ** 3)))
+
+    tok = 123
+    x = W("token_embd.weight")[tok] * np.float64(cfg.embed_scale)
+    proj = W("pli_model_proj.weight") @ x
+    row = W("pli_token_embd.weight")[tok]
+    pli = np.empty(L * P)
+    for i in range(L):
+        s = slice(i * P, (i + 1) * P)
+        pli[s] = (rms(proj[s], W("pli_proj_norm.weight")) + row[s] * np.sqrt(P)) * 2.0 ** -0.5
+    for i in range(L):
+        pre = f"blk.{i}."
+        xn = rms(x, W(pre + "attn_norm.weight"))
+        v = (W(pre + "attn_v.weight") @ xn).reshape(nkv, hd)
+        v = v / np.sqrt(np.mean(v * v, axis=1, keepdims=True) + eps)  # V norm without weights
+        o = np.repeat(v, nh // nkv, axis=0).reshape(-1)  # one key: softmax weight 1
+        x = x + rms(W(pre + "attn_output.weight") @ o, W(pre + "post_attention_norm.weight"))
+        xn = rms(x, W(pre + "ffn_norm.weight"))
+        h = gelu(W(pre + "ffn_gate.weight") @ xn) * (W(pre + "ffn_up.weight") @ xn)
+        x = x + rms(W(pre + "ffn_down.weight") @ h, W(pre + "post_ffw_norm.weight"))
+        g = gelu(W(pre + "pli_gate.weight") @ x) * pli[i * P:(i + 1) * P]
+        x = x + rms(W(pre + "pli_proj.weight") @ g, W(pre + "pli_post_norm.weight"))
+        x = x * W(pre + "layer_scalar")[0]
+    hid = rms(x, W("output_norm.weight"))
+    _, hd_o = om.forward_token(tok, 0)
+    assert O.norm_rel(hd_o.reshape(1, -1), hid.reshape(1, -1)).max() < 1e-5
