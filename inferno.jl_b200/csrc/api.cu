@@ -365,10 +365,21 @@ int ifr_qgemm(ifr_ctx *c, const ifr_tensor *W, const float *X, int ncols, float 
     if (W->device != c->device) return fail(IFR_ERR_ARG, "tensor lives on device %d, context on %d", W->device, c->device);
     if (((uintptr_t)X & 15) || ((uintptr_t)Y & 3)) return fail(IFR_ERR_ARG, "X must be 16-byte and Y 4-byte aligned");
     DeviceGuard g(c->device);
+    // scratch for the K halves of tall matrices (second half's partials);
+    // not grown while the stream is being captured
+    const int64_t kp = W->q.rows * (ncols < IFR_MAX_VERIFY_COLS ? ncols : IFR_MAX_VERIFY_COLS);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    IFR_CHECK_CUDA(cudaStreamIsCapturing(c->stream, &cap), "cudaStreamIsCapturing");
+    if (cap == cudaStreamCaptureStatusNone) {
+        const int rc = ensure_scratch(c, (size_t)kp * 4);
+        if (rc != IFR_OK) return rc;
+    }
     for (int n0 = 0; n0 < ncols; n0 += IFR_MAX_VERIFY_COLS) {
         int n = ncols - n0 < IFR_MAX_VERIFY_COLS ? ncols - n0 : IFR_MAX_VERIFY_COLS;
         ifr::XForm xf;
         xf.act = c->act;
+        xf.kpart = (float *)c->scratch;
+        xf.kpart_floats = (int64_t)(c->scratch_cap / 4);
         IFR_CHECK_CUDA(ifr::qgemm_small(W->q, X + (int64_t)n0 * W->q.cols, n, Y + (int64_t)n0 * W->q.rows, false,
                                         W->q.rows, c->stream, xf),
                        "qgemm launch");

@@ -69,6 +69,9 @@ struct XForm {
                                // (gate 0-15, up 0-15, gate 16-31, ...); Y gets silu(gate) * up,
                                // rows/2 rows (not with accumulate); 2: gelu_tanh(gate) * up
     const GemvArgmax *am = nullptr;  // greedy decision on Y (not with ep or accumulate)
+    float *kpart = nullptr;    // tall matrices, exact activations, no transform or epilogue:
+    int64_t kpart_floats = 0;  // scratch for the second K half's partial sums (>= rows * ncols),
+                               // which lets the row-block-per-warp kernel split K over CTA pairs
     int rev = 0;               // tall matrices: each CTA streams its row groups last to first
                                // (consecutive passes over a matrix a little larger than L2 then
                                // start on the rows the previous pass left in L2)

@@ -127,6 +127,8 @@ struct GemvArgs {
     float eps;
     int ep;            // 1: SwiGLU epilogue over interleaved gate/up 16-row blocks
     int rev;           // qgemv_rows_kernel: row groups last to first (XForm::rev)
+    int khalves;       // qgemv_rows_kernel: 2 = CTA 2b + h takes K half h of pair b's row groups
+    float *kpart;      // khalves 2: the second half's partials [ncols][M]
 };
 // the greedy decision's arguments, a kernel parameter of the AM variants only
 template <bool AM> struct AmArg { GemvArgmax am; };
@@ -752,6 +754,152 @@ IFR_DEV void mtile_q6_i8(const uint8_t *tile, int lane, const BFragI8 &F, float 
     }
 }
 
+// ---- exact f32 activations on the integer tensor cores (Q4_K / Q5_K, tall) ----
+// Each 256-element unit of a column is written as three int8 limbs over one
+// scale d = amax / 127: x / d = l1 + l2 / 254 + l3 / 254^2 + r, |r| <= 0.5 /
+// 254^2, so x is carried to ~6e-8 of the unit's amax (plus the f32 rounding
+// of x / d) - the precision of the fp16 (hi, lo) split, with int8 weights
+// taken from the nibbles directly (no fp16 conversion per weight).  The
+// weight side is the Q8_K path's (exact integer sums per sub-block, scaled
+// per sub-block); each limb level has its own sums, combined in f32 at the end.
+// One unit's fragments in shared memory, uint2 entries [.][lane 32]:
+//   [3 c + l]   chunk c, level l: int8 of k-slots 4t..4t+3 | 16+4t..16+4t+3, column g
+//   [24 + l]    level l's chunk sums as 7-bit limbs (lo, hi), lanes t < 2: chunks 4t..4t+3
+//   [27]        d of C columns 2t, 2t+1 (f32 bits)
+constexpr int kL8Entries = 28;
+constexpr int kL8Words = kL8Entries * 32 * 2;
+constexpr float kL8Step = 254.0f;
+constexpr float kL8Inv1 = 1.0f / 254.0f, kL8Inv2 = 1.0f / 64516.0f;
+
+IFR_DEV int l8_limb(float v) { return (int)fminf(fmaxf(rintf(v), -127.f), 127.f); }
+
+template <int FMT, int XF>
+IFR_DEV void build_b_l8(const GemvArgs &a, const float *inv, int64_t u, int lane, uint32_t *unit, float *ssq) {
+    const int g = lane >> 2, t = lane & 3;
+    const bool has = g < a.ncols;
+    // elements 32c + 16h + 4t + {0..3} of run i = 2c + h: v[8c + 4h + j]
+    float v[64];
+    float ss = 0.f;
+    load_x32<XF>(a, inv, g, u * 256 + 4 * t, 16, has, v, &ss);
+    load_x32<XF>(a, inv, g, u * 256 + 128 + 4 * t, 16, has, v + 32, &ss);
+    if (XF == 3) {  // the unit's 256 elements of column g are spread over the quad
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        if (ssq && t == 0) ssq[u * 8 + g] = ss;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i++) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    uint2 *ub = reinterpret_cast<uint2 *>(unit) + lane;
+    int keep[3][4];  // level l's sums of chunks 4t .. 4t + 3 (lanes t < 2)
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        int l[3][8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float x = v[8 * c + j];
+            l[0][j] = l8_limb(__fmul_rn(x, id));
+            const float r1 = fmaf(x, id, -(float)l[0][j]);
+            l[1][j] = l8_limb(r1 * kL8Step);
+            const float r2 = fmaf(r1, kL8Step, -(float)l[1][j]);
+            l[2][j] = l8_limb(r2 * kL8Step);
+        }
+#pragma unroll
+        for (int lv = 0; lv < 3; lv++) {
+            ub[(3 * c + lv) * 32] = make_uint2(pack4_s8(l[lv][0], l[lv][1], l[lv][2], l[lv][3]),
+                                               pack4_s8(l[lv][4], l[lv][5], l[lv][6], l[lv][7]));
+            int cs = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) cs += l[lv][j];
+            cs += __shfl_xor_sync(0xffffffffu, cs, 1);
+            cs += __shfl_xor_sync(0xffffffffu, cs, 2);
+            if ((c >> 2) == t) keep[lv][c & 3] = cs;
+        }
+    }
+#pragma unroll
+    for (int lv = 0; lv < 3; lv++) {
+        uint32_t lo = 0u, hi = 0u;
+        if (t < 2) limbs4(keep[lv][0], keep[lv][1], keep[lv][2], keep[lv][3], lo, hi);
+        ub[(24 + lv) * 32] = make_uint2(lo, hi);
+    }
+    ub[27 * 32] = make_uint2(__float_as_uint(__shfl_sync(0xffffffffu, d, 8 * t)),
+                             __float_as_uint(__shfl_sync(0xffffffffu, d, 8 * t + 4)));
+}
+
+// Q4_K / Q5_K with limb activations: per level l and output, the exact
+// integer sums S_l = sum_c sc_c (q . l)_c and M_l = sum_c m_c bsum_c; then
+// d * dq * sum_l S_l / 254^l - d * dmin * sum_l M_l / 254^l in f32
+template <bool Q5>
+IFR_DEV void mtile_qk_l8(const uint8_t *tile, int lane, const uint2 *fb, float (&tot)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint4 h0 = lds128(tile + qk_hdr(g)), h1 = lds128(tile + qk_hdr(g + 8));
+    const uint4 q00 = lds128(tile + qk_qs(Q5, 0, g, t)), q01 = lds128(tile + qk_qs(Q5, 1, g, t));
+    const uint4 q10 = lds128(tile + qk_qs(Q5, 0, g + 8, t)), q11 = lds128(tile + qk_qs(Q5, 1, g + 8, t));
+    uint4 hb = {};
+    if (Q5) hb = lds128(tile + q5_qh(g, t));
+    uint32_t sc[2][2], mn[2][2];
+    qk_scales(h0, sc[0], mn[0]);
+    qk_scales(h1, sc[1], mn[1]);
+    int S[3][4];
+#pragma unroll
+    for (int lv = 0; lv < 3; lv++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) S[lv][i] = 0;
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const int p = c >> 1, sh = 4 * (c & 1), wi = 2 * (p & 1);
+        const uint4 Q0 = (p >> 1) ? q01 : q00, Q1 = (p >> 1) ? q11 : q10;
+        uint32_t a0 = (u4w(Q0, wi) >> sh) & 0x0f0f0f0fu, a2 = (u4w(Q0, wi + 1) >> sh) & 0x0f0f0f0fu;
+        uint32_t a1 = (u4w(Q1, wi) >> sh) & 0x0f0f0f0fu, a3 = (u4w(Q1, wi + 1) >> sh) & 0x0f0f0f0fu;
+        if (Q5) {
+            a0 |= ((hb.x >> c) & 0x01010101u) << 4;
+            a2 |= ((hb.y >> c) & 0x01010101u) << 4;
+            a1 |= ((hb.z >> c) & 0x01010101u) << 4;
+            a3 |= ((hb.w >> c) & 0x01010101u) << 4;
+        }
+        const int s0 = ubyte(sc[0][c >> 2], c & 3), s1 = ubyte(sc[1][c >> 2], c & 3);
+#pragma unroll
+        for (int lv = 0; lv < 3; lv++) {
+            const uint2 b = fb[(3 * c + lv) * 32];
+            int cc[4];
+            imma16832_z(cc, a0, a1, a2, a3, b.x, b.y);
+            S[lv][0] += s0 * cc[0];
+            S[lv][1] += s0 * cc[1];
+            S[lv][2] += s1 * cc[2];
+            S[lv][3] += s1 * cc[3];
+        }
+    }
+    // mins: A = the 6-bit mins (k-slot = chunk; lanes t < 2), B = each level's
+    // chunk sums as 7-bit limbs
+    const uint32_t ma0 = t == 0 ? mn[0][0] : (t == 1 ? mn[0][1] : 0u);
+    const uint32_t ma1 = t == 0 ? mn[1][0] : (t == 1 ? mn[1][1] : 0u);
+    int M[3][4];
+#pragma unroll
+    for (int lv = 0; lv < 3; lv++) {
+        const uint2 bc = fb[(24 + lv) * 32];
+        int ml[4], mh[4];
+        imma16816_z(ml, ma0, ma1, bc.x);
+        imma16816_z(mh, ma0, ma1, bc.y);
+#pragma unroll
+        for (int i = 0; i < 4; i++) M[lv][i] = ml[i] + mh[i] * 128;
+    }
+    const uint2 dw = fb[27 * 32];
+    const float dc[2] = {__uint_as_float(dw.x), __uint_as_float(dw.y)};
+    const float d0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16));
+    const float d1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16));
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float sv = fmaf((float)S[2][i], kL8Inv2, fmaf((float)S[1][i], kL8Inv1, (float)S[0][i]));
+        const float mv = fmaf((float)M[2][i], kL8Inv2, fmaf((float)M[1][i], kL8Inv1, (float)M[0][i]));
+        const float dd = dc[i & 1];
+        tot[i] += (dd * (i < 2 ? d0 : d1)) * sv - (dd * (i < 2 ? dm0 : dm1)) * mv;
+    }
+}
+
 // Work order of one CTA: its contiguous range of row groups, cut into sweeps;
 // per sweep all K passes; per pass the sweep's row groups (one stage each).
 // Partial sums of a sweep live in shared memory, so no K pass touches global
@@ -1062,9 +1210,10 @@ __global__ void __launch_bounds__(32 * consumers<ACT>(), 1) qgemv_kernel(GemvArg
 // modes, a consumer warp owns
 // a whole row block over all of K, so its sums stay in registers and go
 // straight to Y: no per-stage block barrier and no shared-memory reduction.
-// The B fragments of every unit are built once per CTA.  Warp 15 produces:
-// stage q = (row group g, unit u) is the 15 M-tiles of rows blocks
-// 15 g .. 15 g + 14 at unit u, copied with cp.async.bulk into a ring of S
+// The B fragments of every unit are built once per CTA.  Each CTA owns an
+// even share of the row blocks, in groups of 15 from its first.  Warp 15
+// produces: stage q = (group g, unit u) is the (up to) 15 M-tiles of the
+// group's row blocks at unit u, copied with cp.async.bulk into a ring of S
 // slots; full barriers count the bytes, empty barriers count the 15 consumer
 // warps.  Every wait is bounded; after a timeout the kernel drains its copies
 // and returns (IFR_ERR_TIMEOUT on the host).
@@ -1073,9 +1222,12 @@ constexpr int kRowsCW = 15;  // consumer warps (and row blocks per group)
 template <int FMT, int NT, int XF, int ACT, bool AM>
 __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM> aa) {
     // kI8: Q8_K activations (one n-tile: columns 2t, 2t+1 of lane t), fragments
-    // stored as BFragI8 [unit][lane] (80 bytes a lane: conflict-free 16-byte loads)
+    // stored as BFragI8 [unit][lane] (80 bytes a lane: conflict-free 16-byte loads);
+    // kL8: exact activations as int8 limbs (Q4_K / Q5_K; same C layout as kI8)
     constexpr bool kI8 = FMT != 8 && ACT == 1;
-    constexpr int UNITW = kI8 ? (int)(sizeof(BFragI8) / 4) * 32 : bunit_words(NT);
+    constexpr bool kL8 = ACT == 0 && (FMT == 12 || FMT == 13);
+    constexpr bool kIC = kI8 || kL8;  // C columns 2t, 2t+1 (else the exact fp16 layout)
+    constexpr int UNITW = kI8 ? (int)(sizeof(BFragI8) / 4) * 32 : kL8 ? kL8Words : bunit_words(NT);
     constexpr int MTB = mtile_bytes(FMT);
     constexpr int STAGE = kRowsCW * MTB;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1089,21 +1241,31 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
     __shared__ unsigned long long best_s[AM ? 8 : 1];
     __shared__ bool last_s;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ngr = (a.nrb + kRowsCW - 1) / kRowsCW;
-    const int g_lo = (int)((int64_t)blockIdx.x * ngr / gridDim.x);
-    const int g_hi = (int)((int64_t)(blockIdx.x + 1) * ngr / gridDim.x);
-    const int total = (g_hi - g_lo) * a.nu;
+    // K halves (khalves 2): CTAs 2b and 2b + 1 take the same row groups, units
+    // [0, nu/2) and [nu/2, nu); the second writes its partials to kpart
+    const int kh = a.khalves == 2 ? (int)(blockIdx.x & 1) : 0;
+    const int cb = a.khalves == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int ncb = a.khalves == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int ku0 = kh ? a.nu / 2 : 0, nku = a.khalves == 2 ? (kh ? a.nu - a.nu / 2 : a.nu / 2) : a.nu;
+    // this CTA's row blocks [rb_lo, rb_hi), an even share (not whole groups:
+    // the SM is issue-bound, so a last group of a few row blocks costs in
+    // proportion), in groups of kRowsCW from rb_lo
+    const int rb_lo = (int)((int64_t)cb * a.nrb / ncb);
+    const int rb_hi = (int)((int64_t)(cb + 1) * a.nrb / ncb);
+    const int ng = (rb_hi - rb_lo + kRowsCW - 1) / kRowsCW;
+    const int total = ng * nku;
     if constexpr (AM) {
         if (tid < 8) best_s[tid] = 0ull;
     }
     auto issue = [&](int q) {  // one thread: stage q into its slot
         const int slot = q % a.S;
-        const int g = a.rev ? g_hi - 1 - q / a.nu : g_lo + q / a.nu, u = q % a.nu;
-        const int nrow = min(kRowsCW, a.nrb - g * kRowsCW);
+        const int gi = a.rev ? ng - 1 - q / nku : q / nku, u = ku0 + q % nku;
+        const int rb0 = rb_lo + gi * kRowsCW;
+        const int nrow = min(kRowsCW, rb_hi - rb0);
         fence_proxy_async();
         mbar_expect_tx(full + slot, (uint32_t)(nrow * MTB));
         for (int w = 0; w < nrow; w++) {
-            const uint8_t *src = a.W + ((int64_t)(g * kRowsCW + w) * a.nu + u) * MTB;
+            const uint8_t *src = a.W + ((int64_t)(rb0 + w) * a.nu + u) * MTB;
             bulk_g2s(ring + (size_t)slot * STAGE + (size_t)w * MTB, src, (uint32_t)MTB, full + slot);
         }
     };
@@ -1154,9 +1316,13 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
             build_b_i8<FMT, XF>(a, inv_s, u, lane, Fr);
             reinterpret_cast<BFragI8 *>(bsm)[u * 32 + lane] = Fr;
         }
+    } else if constexpr (kL8) {
+        for (int uu = warp; uu < nku; uu += 16)
+            build_b_l8<FMT, XF>(a, inv_s, ku0 + uu, lane, bsm + (size_t)uu * UNITW, ssq);
     } else {
-        for (int task = warp; task < a.nu * NT; task += 16)
-            build_b<FMT, NT, XF>(a, inv_s, task % a.nu, lane, task / a.nu, bsm + (size_t)(task % a.nu) * UNITW, ssq);
+        for (int task = warp; task < nku * NT; task += 16)
+            build_b<FMT, NT, XF>(a, inv_s, ku0 + task % nku, lane, task / nku, bsm + (size_t)(task % nku) * UNITW,
+                                 ssq);
     }
     __syncthreads();
     if (XF == 3) {  // W (x w) / rms(x) per column; the sums of squares in unit order
@@ -1186,23 +1352,26 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
         // greedy keys: exact, column 4 nt + t of n-tile nt; Q8_K, column 2 t + j
         unsigned long long best[2] = {0ull, 0ull};
         int q = 0;
-        for (int gi = 0; gi < g_hi - g_lo; gi++) {
-            const int gr = a.rev ? g_hi - 1 - gi : g_lo + gi;
-            const int rb = gr * kRowsCW + warp;
+        for (int gi = 0; gi < ng; gi++) {
+            const int gr = a.rev ? ng - 1 - gi : gi;
+            const int rb = rb_lo + gr * kRowsCW + warp;
             float tot[NT][4];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                 for (int i = 0; i < 4; i++) tot[nt][i] = 0.f;
-            for (int u = 0; u < a.nu; u++, q++) {
+            for (int u = 0; u < nku; u++, q++) {
                 const int slot = q % a.S;
                 if (!dead && !mbar_wait(full + slot, (uint32_t)(q / a.S) & 1)) dead = true;
-                if (!dead && rb < a.nrb) {
+                if (!dead && rb < rb_hi) {
                     const uint8_t *tile = ring + (size_t)slot * STAGE + (size_t)warp * MTB;
                     if constexpr (kI8) {
                         const BFragI8 F = reinterpret_cast<const BFragI8 *>(bsm)[u * 32 + lane];
                         if constexpr (FMT == 14) mtile_q6_i8(tile, lane, F, tot[0]);
                         else mtile_qk_i8<FMT == 13>(tile, lane, F, tot[0]);
+                    } else if constexpr (kL8) {
+                        mtile_qk_l8<FMT == 13>(tile, lane, reinterpret_cast<const uint2 *>(bsm + (size_t)u * UNITW) + lane,
+                                               tot[0]);
                     } else {
                         BView<NT> F;
                         F.at(bsm + (size_t)u * UNITW, lane);
@@ -1214,7 +1383,7 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty + slot);
             }
-            if (kI8 && rb < a.nrb && !dead) {
+            if (kIC && rb < rb_hi && !dead) {
                 // C columns 2t, 2t+1: activation columns 2t, 2t+1
 #pragma unroll
                 for (int j = 0; j < 2; j++) {
@@ -1225,6 +1394,11 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
                         const int64_t row = (int64_t)rb * 16 + g + 8 * h;
                         if (row >= a.M) continue;
                         float v = tot[0][2 * h + j];
+                        if (XF == 3) v *= inv_s[col];
+                        if (kh) {  // the second K half: its partial, added by rows_khalf_add_kernel
+                            a.kpart[(int64_t)col * a.M + row] = v;
+                            continue;
+                        }
                         float *y = a.Y + (int64_t)col * a.ldy + row;
                         if (a.accumulate) v += *y;
                         *y = v;
@@ -1235,7 +1409,7 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
                     }
                 }
             }
-            if (!kI8 && rb < a.nrb && !dead) {
+            if (!kIC && rb < rb_hi && !dead) {
                 // C columns 2t, 2t+1 of n-tile nt: hi and lo parts of column 4 nt + t
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
@@ -1247,6 +1421,10 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
                         if (row >= a.M) continue;
                         float v = tot[nt][2 * h] + tot[nt][2 * h + 1];
                         if (XF == 3) v *= inv_s[col];
+                        if (kh) {  // the second K half: its partial, added by rows_khalf_add_kernel
+                            a.kpart[(int64_t)col * a.M + row] = v;
+                            continue;
+                        }
                         float *y = a.Y + (int64_t)col * a.ldy + row;
                         if (a.accumulate) v += *y;
                         *y = v;
@@ -1261,8 +1439,8 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
         if constexpr (AM) {
 #pragma unroll
             for (int j = 0; j < 2; j++) {
-                const int col = kI8 ? 2 * t + j : 4 * j + t;
-                if ((kI8 || j < NT) && col < a.ncols) atomicMax(&best_s[col], best[j]);
+                const int col = kIC ? 2 * t + j : 4 * j + t;
+                if ((kIC || j < NT) && col < a.ncols) atomicMax(&best_s[col], best[j]);
             }
         }
     }
@@ -1306,6 +1484,19 @@ __global__ void __launch_bounds__(512, 1) qgemv_rows_kernel(GemvArgs a, AmArg<AM
 }
 
 static int num_sms() { return device_sm_count(); }
+
+// qgemv_rows_kernel with K halves: Y += the second half's partials, one add
+// per output ((y + first half) + second half: a fixed order)
+static __global__ void __launch_bounds__(256) rows_khalf_add_kernel(float *Y, int64_t ldy, const float *kpart, int64_t M,
+                                                             int ncols) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t n = M * ncols;
+    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+        const int64_t col = i / M, row = i - col * M;
+        Y[col * ldy + row] += kpart[i];
+    }
+}
 
 template <int FMT, int NT, int XF, int MPW, int ACT, bool AM>
 static cudaError_t launch_mpw(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
@@ -1368,9 +1559,20 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
     // Q4_K with Q8_K activations: the unit-split kernel (two M-tiles per warp)
     // streams faster (151936 x 4096, N = 5: 78.7 vs 90.9 us, measured)
     if (kI8 && FMT == 12) return cudaErrorNotSupported;
-    const int unit_bytes = kI8 ? (int)sizeof(BFragI8) * 32 : bunit_words(NT) * 4;
-    const int fixed = 128 + (int)T.nu * unit_bytes + (XF == 3 ? (int)T.nu * 8 * 4 : 0);
+    constexpr bool kL8 = ACT == 0 && (FMT == 12 || FMT == 13);
+    const int unit_bytes = kI8 ? (int)sizeof(BFragI8) * 32 : kL8 ? kL8Words * 4 : bunit_words(NT) * 4;
+    int fixed = 128 + (int)T.nu * unit_bytes + (XF == 3 ? (int)T.nu * 8 * 4 : 0);
     int S = (kSmemMax - fixed) / STAGE;
+    int khalves = 1;
+    // exact activations over a long K (4096 with two n-tiles: 139 KB of
+    // fragments): CTA pairs split K, each holding half the units' fragments,
+    // when the caller gave scratch for the second half's partials (not with
+    // the folded RMSNorm, whose scale needs every unit's sum of squares)
+    if (S < 3 && !kI8 && XF != 3 && !AM && xf.kpart && xf.kpart_floats >= T.rows * ncols && T.nu >= 2) {
+        fixed = 128 + (int)((T.nu + 1) / 2) * unit_bytes;
+        S = (kSmemMax - fixed) / STAGE;
+        khalves = 2;
+    }
     if (S < 3) return cudaErrorNotSupported;  // two one-unit stages hide too little DRAM latency (measured)
     if (S > 8) S = 8;
     const int smem = fixed + S * STAGE;
@@ -1381,12 +1583,15 @@ static cudaError_t launch_rows(const QTensor &T, const float *X, int ncols, floa
         if (e != cudaSuccess) return e;
         attr_set.set();
     }
-    const int grid = num_sms();
+    const int grid = khalves == 2 ? num_sms() & ~1 : num_sms();
     GemvArgs a{T.data, T.rows, T.cols, (int)T.nrb, (int)T.nu, X, xf.ldx > 0 ? xf.ldx : T.cols, ncols, Y, 0, S,
-               0, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep, xf.rev};
+               0, accumulate ? 1 : 0, ldy, xf.kind, xf.w, xf.eps, xf.ep, xf.rev, khalves, xf.kpart};
     AmArg<AM> aa{};
     if constexpr (AM) aa.am = *xf.am;
-    return launch_k(qgemv_rows_kernel<FMT, NT, XF, ACT, AM>, dim3(grid), dim3(512), (size_t)smem, s, a, aa);
+    cudaError_t e = launch_k(qgemv_rows_kernel<FMT, NT, XF, ACT, AM>, dim3(grid), dim3(512), (size_t)smem, s, a, aa);
+    if (e != cudaSuccess || khalves == 1) return e;
+    return launch_k(rows_khalf_add_kernel, dim3(2 * num_sms()), dim3(256), 0, s, Y, ldy, (const float *)xf.kpart,
+                    (int64_t)T.rows, ncols);
 }
 
 // Work split: UW warps share each row block's units.  A stage: 16 warps x 1
@@ -1402,8 +1607,10 @@ static cudaError_t launch(const QTensor &T, const float *X, int ncols, float *Y,
     constexpr int MPW = kExact ? 1 : (mtile_bytes(FMT) > 2816 ? 1 : 2);
     constexpr int CW = consumers<ACT>();
     if constexpr (XF != 2) {
-        const cudaError_t e = xf.am ? launch_rows<FMT, NT, XF, ACT, true>(T, X, ncols, Y, accumulate, ldy, s, xf)
-                                    : launch_rows<FMT, NT, XF, ACT, false>(T, X, ncols, Y, accumulate, ldy, s, xf);
+        // exact Q4_K / Q5_K: the limb kernel (one n-tile of 8 columns whatever NT)
+        constexpr int RNT = ACT == 0 && (FMT == 12 || FMT == 13) ? 1 : NT;
+        const cudaError_t e = xf.am ? launch_rows<FMT, RNT, XF, ACT, true>(T, X, ncols, Y, accumulate, ldy, s, xf)
+                                    : launch_rows<FMT, RNT, XF, ACT, false>(T, X, ncols, Y, accumulate, ldy, s, xf);
         if (e != cudaErrorNotSupported) return e;
     }
     constexpr int kSmemMax = 226 * 1024;

@@ -241,9 +241,10 @@ def test_argument_errors(O, ctx, pkg):
 # tall matrices (>= 2 x 148 groups of 15 row blocks): the row-block-per-warp
 # kernel, which keeps every unit's fragments in shared memory (K = 1024, and
 # K = 4096 with Q8_K activations); exact activations at K = 4096 with 5+
-# columns leave no room for three ring slots, and Q4_K with Q8_K activations
-# streams faster unit-split: those take the unit-split kernel
-TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (14, 4096)]
+# columns split K over CTA pairs (half the fragments each, the second half's
+# partials added by a second kernel); Q8_0 at K = 4096 (larger tiles) and Q4_K
+# with Q8_K activations take the unit-split kernel
+TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (13, 4096), (14, 4096), (8, 4096)]
 
 
 @pytest.mark.parametrize("act", [0, 1])
@@ -273,3 +274,29 @@ def test_qgemm_tall(O, ctx, qt, K, act):
         assert O.norm_rel(Yn, refn[:, idx]).max() < 5 * (TOL if a == 0 else 1e-3)
     finally:
         ctx.set_activation(0)
+
+
+@pytest.mark.parametrize("qt", [12, 13])
+def test_qgemm_tall_exact_outlier_channels(O, ctx, qt):
+    """exact activations with a few massive channels (200x the others): the
+    Q4_K / Q5_K tall kernel writes each unit of a column as three int8 limbs
+    over the unit's amax, so small elements beside an outlier keep ~6e-8 of
+    that amax; still within TOL of the oracle's f32 dot products"""
+    torch = _torch()
+    M, K = 71040 + 5, 4096
+    rng = np.random.default_rng(qt + 777)
+    pool = O.quantize(qt, rng.normal(0, 0.02, (512, K)).astype(np.float32))
+    rb = pool.size // 512
+    idx = np.arange(M) % 512
+    W = ctx.upload(qt, pool.reshape(512, rb)[idx].ravel(), M, K)
+    X = rng.normal(0, 1, (8, K)).astype(np.float32)
+    X[:, [5, 1300, 4000]] *= 200.0
+    X[3, 700:956] = 0.0          # an all-zero unit of one column
+    X[6, 2048:2304] *= 1e-30     # a unit of tiny values (its own scale)
+    ref = O.gemm_ref(qt, pool, 512, K, X, act=0)
+    ctx.set_activation(0)
+    Xd = torch.from_numpy(X).cuda()
+    for n in (1, 5, 8):
+        Y = ctx.qgemm(W, Xd[:n].contiguous()).cpu().numpy()
+        err = O.norm_rel(Y, ref[:n][:, idx])
+        assert err.max() < TOL, (NAMES[qt], n, err)
