@@ -754,6 +754,7 @@ def batch_leg(args, pkg, ws, rank, local, steps, warmup):
     mine = rank_requests(args.batch, ws, rank)
     B = len(mine)
     ctx = pkg.Context(local, torch_stream=False)
+    ctx.set_kv_bf16(bool(getattr(args, "kv_bf16", 0)))
     t_load = time.time()
     if rank == 0:
         synth.cached(BATCH_PRESET, BATCH_SEED)
@@ -814,7 +815,8 @@ def batch_leg(args, pkg, ws, rank, local, steps, warmup):
     line = None
     if rank == 0:
         hd = info.head_dim
-        kv_bytes = 2 * info.n_attention_layers * info.n_kv_head * hd * 4 * (P + G + 1) * args.batch // ws
+        kv_bytes = 2 * info.n_attention_layers * info.n_kv_head * hd * (2 if getattr(args, "kv_bf16", 0) else 4) * \
+            (P + G + 1) * args.batch // ws
         flops = 2.0 * verify_weight_count(info) * B * (G + 1)
         line = {
             "metric": METRIC,
@@ -832,7 +834,8 @@ def batch_leg(args, pkg, ws, rank, local, steps, warmup):
             "config": {"workload": "batched greedy spec-decode, BASELINE config 4 (~9B-shape hybrid)",
                        "model": "hidden 4096, 32 layers (24 GatedDeltaNet + 8 attention), 16q/4kv x 256, SSM 32 x 128, FFN 12288, vocab 151936, Q4_K matmuls, Q6_K ffn_down/lm_head, 1-layer MTP head",
                        "requests": args.batch, "requests_per_gpu": B, "gamma": G, "verify_columns_per_gpu": B * (G + 1),
-                       "prompt": P, "kv": "f32", "prefill_s": round(prefill_s, 2), "load_s": round(t_load, 1),
+                       "prompt": P, "kv": "bf16" if getattr(args, "kv_bf16", 0) else "f32",
+                       "prefill_s": round(prefill_s, 2), "load_s": round(t_load, 1),
                        "tokens_emitted_timed": emitted_all,
                        "l2": "inputs larger than L2: %.1f GB of weights + %.1f GB of KV per step per GPU" % (info.weight_bytes / 1e9, kv_bytes / 1e9),
                        "parallelism": f"requests split over {ws} GPU(s), weights replicated, no collective",
@@ -1212,6 +1215,7 @@ def run_profile(args):
         from inferno_b200 import synth
         from inferno_b200.engine import Model, State
         ctx = pkg.Context(0, torch_stream=False)
+        ctx.set_kv_bf16(bool(args.kv_bf16))
         # --preset 9b_narrow: config 4's widths with 4 layers (a small case for ncu)
         model = Model(ctx, synth.cached(args.preset or BATCH_PRESET, BATCH_SEED))
         B, P = args.batch, args.prompt
@@ -1262,6 +1266,8 @@ def main():
     ap.add_argument("--gamma", type=int, default=4)
     ap.add_argument("--fused-layers", type=int, default=0, choices=[0, 1],
                     help="spec workload: the verify's decoder layers as one persistent launch")
+    ap.add_argument("--kv-bf16", type=int, default=0, choices=[0, 1],
+                    help="batch workload / --profile batch: bf16 attention caches (ifr_ctx_set_kv_bf16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="spec workload: skip every extra key")
     ap.add_argument("--no-shard-legs", action="store_true", help="spec workload: skip the config-4/5 legs")

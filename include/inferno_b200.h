@@ -113,6 +113,15 @@ int ifr_test_fused_timeout(ifr_ctx *ctx);
  * Results are identical either way: each weight is rounded to fp16 once in
  * both.  Takes effect for states created afterwards. */
 int ifr_ctx_set_dense_f16_weights(ifr_ctx *ctx, int enable);
+/* enable = 1: states created afterwards that take the split-KV attention
+ * (batches, or one request with a long cache) keep their attention caches,
+ * the target's and the MTP layer's, in bf16: each key and value row is
+ * rounded to nearest even as it is written, half the bytes of the f32 cache
+ * for the attention to read.  Scores and outputs stay f32 sums of the stored
+ * values (the oracle's or_model_set_kv_bf16).  Default 0 (f32 caches, the
+ * reference's Float32 KV of src/ModelCPU.jl).  No counterpart in the
+ * reference. */
+int ifr_ctx_set_kv_bf16(ifr_ctx *ctx, int enable);
 /* wait for the context's stream; IFR_ERR_TIMEOUT if a bounded device-side
  * wait of a kernel ran out since the last ifr_sync */
 int ifr_sync(ifr_ctx *ctx);

@@ -116,6 +116,11 @@ class Context:
         """let one-request prefill chunks use the dense tensor-core path"""
         check(load().ifr_ctx_set_prefill_dense(self.handle, 1 if enable else 0))
 
+    def set_kv_bf16(self, enable=True):
+        """ifr_ctx_set_kv_bf16: split-KV states created afterwards keep bf16
+        attention caches (rows rounded to nearest even as they are written)"""
+        check(load().ifr_ctx_set_kv_bf16(self.handle, 1 if enable else 0))
+
     def set_dense_f16_weights(self, enable=True):
         """batched states keep fp16 operand stages of the weights for the dense GEMM"""
         check(load().ifr_ctx_set_dense_f16_weights(self.handle, 1 if enable else 0))

@@ -40,6 +40,7 @@ SIGNATURES = {
     "ifr_ctx_set_fused_layers": (_i, [_vp, _i]),
     "ifr_test_fused_timeout": (_i, [_vp]),
     "ifr_ctx_set_dense_f16_weights": (_i, [_vp, _i]),
+    "ifr_ctx_set_kv_bf16": (_i, [_vp, _i]),
     "ifr_tensor_prepare_dense": (_i, [_vp, _vp]),
     "ifr_state_read_request": (_i, [_vp, _i, _vp, _i, _vp, _vp]),
     "ifr_prefill_batch": (_i, [_vp, _vp, _i, _vp]),

@@ -56,6 +56,7 @@ struct ifr_ctx {
     int prefill_dense = 0;                         // one-request prefill chunks may use the dense path
     int fused_layers = 0;                          // one-request verify: the layer stack as one launch
     int dense_f16 = 1;                             // batched states keep fp16 operand stages of the weights
+    int kv_bf16 = 0;                               // split-KV states keep their attention caches in bf16
     std::atomic<int> refs{0};      // live models built on this context
     std::atomic<bool> closing{false};
 };
@@ -138,6 +139,7 @@ int ifr_ctx_dense_min(const ifr_ctx *c) { return c->dense_min; }
 int ifr_ctx_prefill_dense(const ifr_ctx *c) { return c->prefill_dense; }
 int ifr_ctx_fused_layers(const ifr_ctx *c) { return c->fused_layers; }
 int ifr_ctx_dense_f16(const ifr_ctx *c) { return c->dense_f16; }
+int ifr_ctx_kv_bf16(const ifr_ctx *c) { return c->kv_bf16; }
 static void ctx_destroy_now(ifr_ctx *c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
@@ -225,6 +227,12 @@ int ifr_ctx_set_prefill_dense(ifr_ctx *c, int enable) {
 int ifr_ctx_set_dense_f16_weights(ifr_ctx *c, int enable) {
     if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
     c->dense_f16 = enable ? 1 : 0;
+    return IFR_OK;
+}
+
+int ifr_ctx_set_kv_bf16(ifr_ctx *c, int enable) {
+    if (!c) return fail(IFR_ERR_ARG, "ctx is NULL");
+    c->kv_bf16 = enable ? 1 : 0;
     return IFR_OK;
 }
 

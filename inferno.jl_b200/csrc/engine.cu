@@ -35,6 +35,7 @@ int ifr_ctx_dense_min(const ifr_ctx *c);
 int ifr_ctx_prefill_dense(const ifr_ctx *c);
 int ifr_ctx_fused_layers(const ifr_ctx *c);
 int ifr_ctx_dense_f16(const ifr_ctx *c);
+int ifr_ctx_kv_bf16(const ifr_ctx *c);
 void ifr_ctx_retain(ifr_ctx *c);
 void ifr_ctx_release(ifr_ctx *c);
 cudaStream_t ifr_ctx_stream_of(const ifr_ctx *c);
@@ -537,6 +538,7 @@ struct ifr_state {
     float *mtp_kc = nullptr, *mtp_vc = nullptr;
     void *acc_scratch = nullptr;
     float *attn_part = nullptr;         // split-KV attention: partial softmax states (null: cluster kernel)
+    bool kv16 = false;                  // kc / vc / mtp_kc / mtp_vc hold bf16 rows (ifr_ctx_set_kv_bf16)
     void *dense = nullptr;              // scratch of the dense tensor-core GEMMs
     int64_t dense_bytes = 0;
     int last_n = 0;
@@ -743,6 +745,7 @@ ifr::AttnArgs attn_args(ifr_state *s, const DevLayer &L, int n, float *kc, float
     a.eps = c.rms_eps;
     a.b_kv = kv_ld;
     a.b_pos = pos_ld;
+    a.kv16 = s->kv16 ? 1 : 0;
     return a;
 }
 
@@ -788,6 +791,7 @@ int layer_forward(ifr_state *s, const DevLayer &L, int li, int n, float *kc, flo
         a.eps = c.rms_eps;
         a.b_kv = kv_ld;
         a.b_pos = pos_ld;
+        a.kv16 = s->kv16 ? 1 : 0;
         a.gated = 0;
         a.vnorm = 1;
         a.scale = 1.0f;
@@ -973,7 +977,7 @@ bool fused_plan(ifr_state *s, int n, std::vector<ifr::FPhase> &v) {
 int fused_build(ifr_state *s) {
     ifr_model *m = s->m;
     const ifr_model_info &c = m->info;
-    if (s->B != 1 || m->comm || m->gemma || c.n_layers < 1) return IFR_OK;
+    if (s->B != 1 || m->comm || m->gemma || s->kv16 || c.n_layers < 1) return IFR_OK;
     bool any_attn = false;
     for (auto &L : m->layers) any_attn |= !L.ssm;
     if (any_attn) {
@@ -1604,7 +1608,9 @@ int ifr_state_create_batch(ifr_model *m, int max_ctx, int batch, ifr_state **out
     s->rkv.assign(c.n_layers, nullptr);
     s->kc.assign(c.n_layers, nullptr);
     s->vc.assign(c.n_layers, nullptr);
-    const size_t kvn = (size_t)B * max_ctx * m->nkv * c.head_dim;
+    // bf16 caches (split-KV states only): half the floats, read as uint16
+    s->kv16 = ifr_ctx_kv_bf16(m->ctx) && (B > 1 || max_ctx >= kSplitMinCtx);
+    const size_t kvn = (size_t)B * max_ctx * m->nkv * c.head_dim / (s->kv16 ? 2 : 1);
     for (int i = 0; !rc && i < c.n_layers; i++) {
         if (m->layers[i].ssm) {
             const int hd = c.ssm_head_dim;
@@ -1749,7 +1755,7 @@ int ifr_state_reset(ifr_state *s) {
     // the MTP layer attends over positions that only its drafts write: they
     // read as zeros until then, as after creation
     if (s->mtp_kc) {
-        const size_t kvb = (size_t)s->B * s->max_ctx * s->m->nkv * c.head_dim * 4;
+        const size_t kvb = (size_t)s->B * s->max_ctx * s->m->nkv * c.head_dim * (s->kv16 ? 2 : 4);
         ECHECK(cudaMemsetAsync(s->mtp_kc, 0, kvb, st), "reset mtp cache");
         ECHECK(cudaMemsetAsync(s->mtp_vc, 0, kvb, st), "reset mtp cache");
     }

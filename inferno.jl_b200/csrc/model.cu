@@ -9,6 +9,7 @@
 #include "qgemv_kernels.cuh"  // the M-tile code of the fused verify (fused_step.cuh)
 
 #include <algorithm>
+#include <cuda_bf16.h>
 #include <cooperative_groups.h>
 #include <math_constants.h>
 
@@ -1381,7 +1382,6 @@ __device__ __forceinline__ void attn_part_body(AttnArgs a, int hg, int S, int bx
     const int lo = sl * kps, hi = min(nkeys, lo + kps);
     if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
     const RopeSpec rs = rope_spec(a);
-    const int qs = a.gated ? 2 : 1;
     const int64_t rows_all = (int64_t)gz * a.nh * N, rid_base = ((int64_t)b * a.nh + h0) * N;
     if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
         // every key of this slice is outside every query's window (this
@@ -1624,7 +1624,6 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_part_mma_kernel(AttnArgs 
     const int lo = sl * kps, hi = min(nkeys, lo + kps);
     if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
     const RopeSpec rs = rope_spec(a);
-    const int qs = a.gated ? 2 : 1;
     const int64_t rows_all = (int64_t)gridDim.z * a.nh * N, rid0 = ((int64_t)b * a.nh + h0) * N;
     if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
         float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
@@ -1825,6 +1824,345 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_part_mma_kernel(AttnArgs 
     }
 }
 
+// ---- split-KV attention over a bf16 KV cache (AttnArgs::kv16) ---------------
+// attn_part_mma_kernel's slices, masks, online softmax and partial states
+// with the cache rows in bf16 (as the cache stores them: round to nearest
+// even of the f32 rows) on mma.sync m16n8k16 bf16.  K and V enter the MMAs
+// exactly; q and the probabilities P are split into three bf16 pieces
+// (hi + mid + lo, ~24 bits), so every product is the f32 one of the stored
+// operands: S = sum_p q_p K^T, O += sum_p P_p V.  Fragments come from shared
+// memory by ldmatrix (V transposed on the fly), rows padded to an odd number
+// of 16-byte units (conflict-free).  Cached rows stream in by cp.async into
+// a ring of four chunk buffers (three chunks in flight), the first two
+// issued before the prologue; the new rows of this step are rounded to bf16
+// on their way into the staged chunk and into the cache.
+template <int HD>
+struct Bf16Smem {
+    static constexpr int kStages = 4;          // K/V chunk buffers: chunks c+1 .. c+3 in flight
+    static constexpr int kRows = 32;           // two m-tiles (R <= kGrpRows)
+    static constexpr int QP = HD + 8;          // bf16 pitch: q pieces, K and V rows
+    static constexpr int PP = kGrpKeys + 8;    // bf16 pitch of the P pieces
+    static constexpr int SS = kGrpKeys + 4;    // f32 pitch of the scores
+    // bytes: qp[3][kRows][QP] | buffer[kStages] {K[kGrpKeys][QP], V[kGrpKeys][QP]} |
+    // kn[N][HD], vn[N][HD] f32 | sc, sc2 [kRows][SS] f32 | pp[3][kRows][PP] | ms, ls, fs [kRows];
+    // the f32 q rows are staged in buffer 3, the RoPE tables in buffer 2
+    static __host__ __device__ int buf_elems() { return 2 * kGrpKeys * QP; }
+    static __host__ __device__ int bytes(int N) {
+        return 2 * (3 * kRows * QP + kStages * buf_elems()) + 4 * (2 * N * HD + 2 * kRows * SS) +
+               2 * 3 * kRows * PP + 4 * 3 * kRows;
+    }
+};
+static_assert(Bf16Smem<256>::kStages == 4, "the prologue stages buffers 0-2 and loads q / RoPE into 3 / 2");
+static_assert(kGrpRows <= Bf16Smem<64>::kRows, "row groups fit two m-tiles");
+
+__device__ __forceinline__ uint16_t bf16_bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float bf16_val(uint16_t h) { return __bfloat162float(__ushort_as_bfloat16(h)); }
+// x = hi + mid + lo (each the bf16 rounding of what is left)
+__device__ __forceinline__ void split_bf16x3(float x, uint16_t &h, uint16_t &m, uint16_t &l) {
+    h = bf16_bits(x);
+    const float r1 = x - bf16_val(h);
+    m = bf16_bits(r1);
+    l = bf16_bits(r1 - bf16_val(m));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return (uint32_t)bf16_bits(lo) | ((uint32_t)bf16_bits(hi) << 16);
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t &r0, uint32_t &r1, const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kMmaThreads, 1) attn_part_bf16_kernel(AttnArgs a, int hg, int S) {
+    using M = Bf16Smem<HD>;
+    constexpr int QP = M::QP, PP = M::PP, SS = M::SS, NR = M::kRows;
+    constexpr int NTH = kMmaThreads, NWP = NTH / 32;
+    // P.V: HD >= 128: every warp both m-tiles and NTW adjacent n-tiles;
+    // HD 64: warp w the m-tile w / 8 and the n-tile w % 8
+    constexpr int MT = HD >= 128 ? 2 : 1, NTW = HD >= 128 ? HD / 128 : 1;
+    extern __shared__ __align__(16) uint8_t b16_buf[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g8 = lane >> 2, t4 = lane & 3;
+    const int N = a.N, ratio = a.nh / a.nkv, nrg = (ratio + hg - 1) / hg;
+    const int g = blockIdx.y / nrg, hb = blockIdx.y % nrg, h0 = g * ratio + hb * hg;
+    const int R = min(hg, ratio - hb * hg) * N;
+    const int sl = blockIdx.x, b = blockIdx.z;
+    uint16_t *qp = reinterpret_cast<uint16_t *>(b16_buf);
+    uint16_t *kvb = qp + 3 * NR * QP;  // [2][K | V][kGrpKeys][QP]
+    float *kn = reinterpret_cast<float *>(kvb + M::kStages * M::buf_elems()), *vn = kn + N * HD;
+    float *sc = vn + N * HD, *sc2 = sc + NR * SS;
+    uint16_t *pp = reinterpret_cast<uint16_t *>(sc2 + NR * SS);
+    float *ms = reinterpret_cast<float *>(pp + 3 * NR * PP), *ls = ms + NR, *fs = ls + NR;
+    constexpr int NST = M::kStages;
+    float *q = reinterpret_cast<float *>(kvb + 3 * M::buf_elems());       // f32 q rows [R][HD] in buffer 3
+    float *rope_s = reinterpret_cast<float *>(kvb + 2 * M::buf_elems());  // RoPE tables in buffer 2
+    pdl_trigger();
+    pdl_wait();
+    a.qkv += (int64_t)b * N * a.ldq;
+    uint16_t *kc = reinterpret_cast<uint16_t *>(a.kc) + b * a.b_kv;
+    uint16_t *vc = reinterpret_cast<uint16_t *>(a.vc) + b * a.b_kv;
+    const int p0 = a.pos[(int64_t)b * a.b_pos];
+    const int nkeys = p0 + N, kps = attn_kps(nkeys, S);
+    const int lo = sl * kps, hi = min(nkeys, lo + kps);
+    if (lo >= nkeys) return;  // the combine reads only the slices below nkeys
+    const int64_t rows_all = (int64_t)gridDim.z * a.nh * N, rid0 = ((int64_t)b * a.nh + h0) * N;
+    if (a.window > 0 && sl > 0 && hi + a.window <= p0 + 1) {
+        float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
+        for (int i = tid; i < R * HD; i += NTH) po[(rid0 + i / HD) * HD + i % HD] = 0.f;
+        if (tid < R) {
+            pm[rid0 + tid] = -CUDART_INF_F;
+            pl[rid0 + tid] = 0.f;
+        }
+        return;
+    }
+    const int nch = (hi - lo + kGrpKeys - 1) / kGrpKeys;
+    // chunk c into buffer c % NST.  Cached rows (j < p0) by cp.async, one
+    // commit group per chunk (empty past the slice, so that group c is the
+    // (c+1)-th of every thread); the buffer's earlier reads ended at a block barrier
+    auto stage_async = [&](int c) {
+        if (c < nch) {
+            const int bf = c % NST, j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
+            const int jc = max(0, min(nj, p0 - j0));
+            uint16_t *kb = kvb + bf * M::buf_elems(), *vb = kb + kGrpKeys * QP;
+            for (int i = tid; i < jc * (HD / 8); i += NTH) {
+                const int jj = i / (HD / 8), d = 8 * (i % (HD / 8));
+                const int64_t o = ((int64_t)(j0 + jj) * a.nkv + g) * HD + d;
+                cp_async16(kb + jj * QP + d, kc + o);
+                cp_async16(vb + jj * QP + d, vc + o);
+            }
+        }
+        cp_async_commit();
+    };
+    // the rest of chunk c: the new rows (j >= p0) rounded from kn / vn, zero
+    // rows past the slice (all threads, plain stores)
+    auto stage_plain = [&](int c) {
+        if (c >= nch) return;
+        const int bf = c % NST, j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
+        const int jc = max(0, min(nj, p0 - j0));  // rows [0, jc) come by bulk copy
+        uint16_t *kb = kvb + bf * M::buf_elems(), *vb = kb + kGrpKeys * QP;
+        for (int i = tid; i < (kGrpKeys - jc) * (HD / 8); i += NTH) {
+            const int jj = jc + i / (HD / 8), d = 8 * (i % (HD / 8)), j = j0 + jj;
+            uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
+            if (jj < nj) {
+                const float *kr = kn + (j - p0) * HD + d, *vr = vn + (j - p0) * HD + d;
+                kw = make_uint4(pack_bf16x2(kr[0], kr[1]), pack_bf16x2(kr[2], kr[3]), pack_bf16x2(kr[4], kr[5]),
+                                pack_bf16x2(kr[6], kr[7]));
+                vw = make_uint4(pack_bf16x2(vr[0], vr[1]), pack_bf16x2(vr[2], vr[3]), pack_bf16x2(vr[4], vr[5]),
+                                pack_bf16x2(vr[6], vr[7]));
+            }
+            *reinterpret_cast<uint4 *>(kb + jj * QP + d) = kw;
+            *reinterpret_cast<uint4 *>(vb + jj * QP + d) = vw;
+        }
+    };
+    stage_async(0);  // the cached rows stream in during the prologue
+    stage_async(1);
+
+    // 1. softmax state, zero P pieces (rows >= R stay zero), the new k / v rows
+    //    and the q rows with RMSNorm + RoPE
+    if (tid < NR) {
+        ms[tid] = -CUDART_INF_F;
+        ls[tid] = 0.f;
+    }
+    for (int i = tid; i < 3 * NR * PP / 2; i += NTH) reinterpret_cast<uint32_t *>(pp)[i] = 0u;
+    attn_rows_in<HD, 0, NTH>(a, q, kn, vn, rope_s, R, h0, g, p0, tid);
+    __syncthreads();
+    stage_plain(0);
+    stage_plain(1);
+    stage_async(2);  // buffer 2 held the RoPE tables
+    stage_plain(2);
+    // one CTA per (KV head, request) writes the new rows; no CTA reads them from the cache
+    if (sl == 0 && hb == 0) {
+        for (int i = tid; i < N * HD; i += NTH) {
+            const int t = i / HD, d = i % HD;
+            const int64_t o = ((int64_t)(p0 + t) * a.nkv + g) * HD + d;
+            kc[o] = bf16_bits(kn[i]);
+            vc[o] = bf16_bits(vn[i]);
+        }
+    }
+    for (int i = tid; i < NR * HD; i += NTH) {
+        const int r = i / HD, d = i % HD;
+        uint16_t h_, m_, l_;
+        split_bf16x3(r < R ? q[r * HD + d] : 0.f, h_, m_, l_);
+        qp[r * QP + d] = h_;
+        qp[NR * QP + r * QP + d] = m_;
+        qp[2 * NR * QP + r * QP + d] = l_;
+    }
+    __syncthreads();  // q pieces (buffer 3 is free for chunk 3)
+
+    const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf((float)HD);
+    // ldmatrix row addresses of this lane: A tiles (16 x 16) and K tiles (8 keys x 16)
+    const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);
+    float oacc[MT][NTW][4];
+#pragma unroll
+    for (int m = 0; m < MT; m++)
+#pragma unroll
+        for (int u = 0; u < NTW; u++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) oacc[m][u][i] = 0.f;
+    for (int c = 0; c < nch; c++) {
+        const int bf = c % NST, j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
+        cp_async_wait<NST - 2>();  // this thread's copies of chunk c (c + 1, c + 2 may be in flight)
+        __syncthreads();           // chunk c complete; every warp is past chunk c - 1
+        // chunk c + 3 into the buffer of chunk c - 1
+        stage_async(c + NST - 1);
+        stage_plain(c + NST - 1);
+        const uint16_t *kb = kvb + bf * M::buf_elems(), *vb = kb + kGrpKeys * QP;
+        {   // scores: warp (k half kh = warp / 8, m-tile m = warp / 4 % 2, key n-tile nb = warp % 4)
+            const int kh = warp >> 3, m = (warp >> 2) & 1, nb = warp & 3;
+            if (16 * m < R) {
+                float ac[3][4];
+#pragma unroll
+                for (int p3 = 0; p3 < 3; p3++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) ac[p3][i] = 0.f;
+                // K rows 8 nb + (lane & 7); matrices j = lane / 8 at dims k0 + 8 j
+                const uint16_t *kr = kb + (8 * nb + (lane & 7)) * QP + 8 * (lane >> 3);
+                const uint16_t *qa = qp + (16 * m + arow) * QP + acol;
+#pragma unroll 2
+                for (int k2 = kh * (HD / 64); k2 < (kh + 1) * (HD / 64); k2++) {  // two k16 steps
+                    uint32_t bk[4];
+                    ldsm_x4(bk, kr + 32 * k2);
+#pragma unroll
+                    for (int s2 = 0; s2 < 2; s2++) {
+                        const int k0 = 32 * k2 + 16 * s2;
+#pragma unroll
+                        for (int p3 = 0; p3 < 3; p3++) {
+                            uint32_t af[4];
+                            ldsm_x4(af, qa + p3 * NR * QP + k0);
+                            mma_bf16(ac[p3], af, bk[2 * s2], bk[2 * s2 + 1]);
+                        }
+                    }
+                }
+                float *dst = kh ? sc2 : sc;
+                const int r0 = 16 * m + g8;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int r = r0 + 8 * (i >> 1), jj = 8 * nb + 2 * t4 + (i & 1);
+                    if (r < R) dst[r * SS + jj] = ac[0][i] + (ac[1][i] + ac[2][i]);
+                }
+            }
+        }
+        __syncthreads();
+        {   // online softmax, one half-warp per row (keys l16 and l16 + 16): all rows in one round
+            const int r = 2 * warp + (lane >> 4), l16 = lane & 15;
+            const bool rv = r < R;
+            float sv[2] = {-CUDART_INF_F, -CUDART_INF_F};
+            if (rv) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int jj = l16 + 16 * h;
+                    if (jj < nj && key_visible(a, j0 + jj, p0 + r % N))
+                        sv[h] = score_cap(a, (sc[r * SS + jj] + sc2[r * SS + jj]) * scale);
+                }
+            }
+            float mx = fmaxf(sv[0], sv[1]);
+#pragma unroll
+            for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mo = rv ? ms[r] : -CUDART_INF_F, mn = fmaxf(mo, mx);
+            float f = 1.f, e[2] = {0.f, 0.f};
+            if (mn != -CUDART_INF_F) {
+                f = expf(mo - mn);
+                e[0] = expf(sv[0] - mn);
+                e[1] = expf(sv[1] - mn);
+            }
+            float ps = e[0] + e[1];
+#pragma unroll
+            for (int o = 8; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            if (rv) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int jj = l16 + 16 * h;
+                    uint16_t h_, m_, l_;
+                    split_bf16x3(e[h], h_, m_, l_);
+                    pp[r * PP + jj] = h_;
+                    pp[NR * PP + r * PP + jj] = m_;
+                    pp[2 * NR * PP + r * PP + jj] = l_;
+                }
+                if (l16 == 0) {
+                    ls[r] = ls[r] * f + ps;
+                    ms[r] = mn;
+                    fs[r] = f;
+                }
+            }
+        }
+        __syncthreads();
+        // P.V: the warp's m-tiles and n-tiles (see MT, NTW)
+#pragma unroll
+        for (int mi = 0; mi < MT; mi++) {
+            const int m = MT == 2 ? mi : warp >> 3;
+            if (16 * m >= R) continue;
+            const int r0 = 16 * m + g8;
+            const float f0 = r0 < R ? fs[r0] : 1.f, f1 = r0 + 8 < R ? fs[r0 + 8] : 1.f;
+#pragma unroll
+            for (int u = 0; u < NTW; u++) {
+                oacc[mi][u][0] *= f0;
+                oacc[mi][u][1] *= f0;
+                oacc[mi][u][2] *= f1;
+                oacc[mi][u][3] *= f1;
+            }
+#pragma unroll
+            for (int kk = 0; kk < kGrpKeys / 16; kk++) {
+                uint32_t af[3][4];
+#pragma unroll
+                for (int p3 = 0; p3 < 3; p3++) ldsm_x4(af[p3], pp + p3 * NR * PP + (16 * m + arow) * PP + 16 * kk + acol);
+                // V rows (keys) 16 kk + arow; matrices (lane / 16) at dims n0 + 8 (lane / 16)
+                const uint16_t *vr = vb + (16 * kk + arow) * QP;
+                if constexpr (NTW == 2) {
+                    const int n0 = 8 * (NTW * warp);
+                    uint32_t bv[4];
+                    ldsm_x4_t(bv, vr + n0 + acol);
+#pragma unroll
+                    for (int u = 0; u < 2; u++)
+#pragma unroll
+                        for (int p3 = 0; p3 < 3; p3++) mma_bf16(oacc[mi][u], af[p3], bv[2 * u], bv[2 * u + 1]);
+                } else {
+                    const int nt = MT == 2 ? NTW * warp : (warp & 7);
+                    uint32_t b0, b1;
+                    ldsm_x2_t(b0, b1, vr + 8 * nt);
+#pragma unroll
+                    for (int p3 = 0; p3 < 3; p3++) mma_bf16(oacc[mi][0], af[p3], b0, b1);
+                }
+            }
+        }
+        // no barrier here: the next chunk's first barrier comes before anything
+        // this chunk read (its buffer, the scores, P, fs) is rewritten
+    }
+
+    // 3. the slice's partial state
+    float *pm = a.part + (int64_t)sl * rows_all * (HD + 2), *pl = pm + rows_all, *po = pl + rows_all;
+#pragma unroll
+    for (int mi = 0; mi < MT; mi++)
+#pragma unroll
+        for (int u = 0; u < NTW; u++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int m = MT == 2 ? mi : warp >> 3, nt = MT == 2 ? NTW * warp + u : (warp & 7);
+                const int r = 16 * m + g8 + 8 * (i >> 1), d = 8 * nt + 2 * t4 + (i & 1);
+                if (r < R) po[(rid0 + r) * HD + d] = oacc[mi][u][i];
+            }
+    if (tid < R) {
+        pm[rid0 + tid] = ms[tid];
+        pl[rid0 + tid] = ls[tid];
+    }
+}
+
 // Merges the key slices of one row (b, h, t) per CTA: M = max_s m_s,
 // L = sum_s l_s e^(m_s - M), O = sum_s o_s e^(m_s - M) (slice order), and
 // writes O / L x sigmoid(gate).  The slices' (m, l) and weights are formed in
@@ -1934,13 +2272,19 @@ static cudaError_t launch_split(const AttnArgs &a, int batch, cudaStream_t s) {
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(attn_part_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      MmaSmem<HD>::bytes(kGrpRows, kMaxN));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_part_bf16_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Bf16Smem<HD>::bytes(kMaxN));
         if (e != cudaSuccess) return e;
         attr.set();
     }
     const int ratio = a.nh / a.nkv, hg = split_heads(ratio, a.N), nrg = (ratio + hg - 1) / hg;
     const int R = std::min(hg, ratio) * a.N;
-    // the tensor-core kernel (IFR_ATTN_MMA=0 in the environment selects the CUDA-core one)
-    cudaError_t e = attn_mma_enabled()
+    // a bf16 cache: its own kernel; else the tensor-core kernel (IFR_ATTN_MMA=0
+    // in the environment selects the CUDA-core one)
+    cudaError_t e = a.kv16 ? launch_k(attn_part_bf16_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch),
+                                      dim3(kMmaThreads), (size_t)Bf16Smem<HD>::bytes(a.N), s, a, hg, a.splits)
+                  : attn_mma_enabled()
                         ? launch_k(attn_part_mma_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(kMmaThreads),
                                    (size_t)MmaSmem<HD>::bytes(R, a.N), s, a, hg, a.splits)
                         : launch_k(attn_part_kernel<HD>, dim3(a.splits, a.nkv * nrg, batch), dim3(256),
@@ -1959,6 +2303,7 @@ cudaError_t attn_step(const AttnArgs &a, int batch, cudaStream_t s) {
         if (a.hd == 64) return launch_split<64>(a, batch, s);
         return cudaErrorInvalidValue;
     }
+    if (a.kv16) return cudaErrorNotSupported;  // bf16 caches take the split path
     const dim3 grid(kAttnSplit, a.nh, batch);
     if (a.hd == 256) return launch_k(attn_step_kernel<256>, grid, dim3(256), 0, s, a);
     if (a.hd == 128) return launch_k(attn_step_kernel<128>, grid, dim3(256), 0, s, a);

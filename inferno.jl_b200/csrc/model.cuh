@@ -70,6 +70,9 @@ struct AttnArgs {
     int gated = 1, vnorm = 0;
     float scale = 0.f, softcap = 0.f;
     int window = 0, rope_pairs = 0, rope_off = 0, rope_ld = 0;
+    // 1: kc / vc hold bf16 rows (round to nearest even of the f32 rows); the
+    // split-KV path only (attn_part_bf16_kernel)
+    int kv16 = 0;
 };
 
 void rmsnorm(const float *x, const float *w, float *out, int rows, int n, float eps, int64_t ldx, int64_t ldo,

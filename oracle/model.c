@@ -53,6 +53,7 @@
 #define _GNU_SOURCE
 #include "oracle.h"
 #include <math.h>
+#include <stdint.h>
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
@@ -85,6 +86,7 @@ struct or_model {
     const float *kq[1024];          /* weight slots holding K-quant matrices */
     int nkq;
     int act;                        /* K-quant activation mode: 0 exact f32, 1 Q8_K */
+    int kv_bf16;                    /* cached keys / values rounded to bf16 */
     int gemma;                      /* Gemma4 block semantics */
     or_gemma_config g;
     float *cos_swa, *sin_swa, *cos_full, *sin_full;   /* [max_ctx][hd/2] */
@@ -316,6 +318,29 @@ static void matvec_w(or_model *m, float *y, const float *W, const float *x, int 
 }
 
 void or_model_set_activation(or_model *m, int mode) { m->act = mode; }
+void or_model_set_kv_bf16(or_model *m, int on) { m->kv_bf16 = on != 0; }
+
+/* f32 -> bf16 -> f32, round to nearest even on the upper 16 bits (NaN kept quiet) */
+static float bf16_round(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u) {
+        if (u & 0x007fffffu) u |= 0x00400000u;
+        u &= 0xffff0000u;
+    } else {
+        u += 0x7fffu + ((u >> 16) & 1u);
+        u &= 0xffff0000u;
+    }
+    memcpy(&x, &u, 4);
+    return x;
+}
+/* the n cached key and value elements of one position, as the cache stores them */
+static void kv_store(const or_model *m, float *kc, float *vc, const float *k, const float *v, size_t n) {
+    for (size_t i = 0; i < n; i++) {
+        kc[i] = m->kv_bf16 ? bf16_round(k[i]) : k[i];
+        vc[i] = m->kv_bf16 ? bf16_round(v[i]) : v[i];
+    }
+}
 
 static inline float silu(float g) { return g / (1.0f + expf(-g)); }
 
@@ -446,8 +471,7 @@ static void attn_forward(or_model *m, or_layer *L, const float *x, int pos, floa
         }
     rmsnorm_rope(m, q, nh, hd, L->q_norm, pos);
     rmsnorm_rope(m, k, nkv, hd, L->k_norm, pos);
-    memcpy(L->kc + (size_t)pos * nkv * hd, k, (size_t)nkv * hd * 4);
-    memcpy(L->vc + (size_t)pos * nkv * hd, v, (size_t)nkv * hd * 4);
+    kv_store(m, L->kc + (size_t)pos * nkv * hd, L->vc + (size_t)pos * nkv * hd, k, v, (size_t)nkv * hd);
     const int ratio = nh / nkv;
     const float scale = 1.0f / sqrtf((float)hd);
     for (int h = 0; h < nh; h++) flash_attn(o + h * hd, q + h * hd, L->kc, L->vc, h / ratio, nkv, pos + 1, scale, hd);
@@ -554,8 +578,7 @@ static void gemma_attn(or_model *m, or_layer *L, int layer, const float *x, int 
     }
     for (int h = 0; h < nkv; h++) rmsnorm(k + (size_t)h * hd, k + (size_t)h * hd, L->k_norm, hd, c->rms_eps);
     gemma_rope(k, nkv, hd, cs, sn);
-    memcpy(L->kc + (size_t)pos * nkv * hd, k, (size_t)nkv * hd * 4);
-    memcpy(L->vc + (size_t)pos * nkv * hd, v, (size_t)nkv * hd * 4);
+    kv_store(m, L->kc + (size_t)pos * nkv * hd, L->vc + (size_t)pos * nkv * hd, k, v, (size_t)nkv * hd);
     const int start = sliding && m->g.window > 0 ? (pos + 1 - m->g.window > 0 ? pos + 1 - m->g.window : 0) : 0;
     const int ratio = nh / nkv;
     const float cap = m->g.attn_softcap;

@@ -114,6 +114,10 @@ void or_model_free(or_model *m);
 /* layer >= 0: decoder layer; -1: global tensors; -2: the MTP decoder layer */
 int  or_model_set(or_model *m, int layer, int kind, int type, const void *data, int64_t n);
 void or_model_set_activation(or_model *m, int mode);  /* 0 exact f32 (default), 1 Q8_K */
+/* 1: every key and value row is rounded to bf16 (round to nearest even) as it
+ * is written to the attention caches, the target's and the MTP layer's; the
+ * engine's bf16 KV cache (ifr_ctx_set_kv_bf16) stores exactly these values */
+void or_model_set_kv_bf16(or_model *m, int on);
 void or_model_reset(or_model *m);
 int  or_forward_token(or_model *m, int token, int pos, float *logits, float *hidden);
 int  or_mtp_step(or_model *m, int token, const float *hidden, int pos, float *logits, float *hidden_out);

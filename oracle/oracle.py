@@ -384,6 +384,8 @@ def _model_lib():
         L.or_model_reset.argtypes = [ctypes.c_void_p]
         L.or_model_set_activation.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.or_model_set_activation.restype = None
+        L.or_model_set_kv_bf16.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.or_model_set_kv_bf16.restype = None
         L.or_forward_token.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _fp, _fp]
         L.or_mtp_step.argtypes = [ctypes.c_void_p, ctypes.c_int, _fp, ctypes.c_int, _fp, _fp]
         L.or_snapshot_take.restype = ctypes.c_void_p
@@ -453,6 +455,11 @@ class OracleModel:
 
     def reset(self):
         self.L.or_model_reset(self.h)
+
+    def set_kv_bf16(self, on):
+        """round cached keys / values to bf16 as they are written (the engine's
+        ifr_ctx_set_kv_bf16 cache); applies to positions written from now on"""
+        self.L.or_model_set_kv_bf16(self.h, 1 if on else 0)
 
     def forward_token(self, token, pos):
         lg = np.empty(self.vocab, np.float32)

@@ -17,6 +17,11 @@ pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 1e-4   # exact path, f32 accumulation on both sides
 DENSE_TOL = 1e-2   # dense path: fp16 operands, f32 accumulation
+# bf16 caches: both sides round every cached row to bf16, but a row value whose
+# f32 differs by ~1e-7 between the two (the norm's summation order) can round
+# to the neighbouring bf16 value, 2^-8 relative away; a few such flips over a
+# few hundred thousand cached values move the logits by ~1e-4
+KV16_TOL = 1e-3
 
 
 @pytest.fixture(scope="module")
@@ -176,3 +181,83 @@ def test_batch_dense_fp16_stages_bit_exact(pkg, ctx):
     (l0, t0, e0), (l1, t1, e1) = out
     assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
     assert list(t0) == list(t1) and e0 == e1
+
+
+def _kv_bf16_run(O, ctx, model, om, B, P, max_ctx, G=4, steps=3):
+    """spec steps of a state with bf16 attention caches against the oracle
+    rounding its cache rows the same way (or_model_set_kv_bf16): drafts,
+    tokens and accept counts equal, verify logits within KV16_TOL"""
+    from inferno_b200.engine import State
+    V = model.info.vocab
+    prompts = _prompts(V, B, P)
+    om.set_kv_bf16(True)
+    try:
+        ref = [om.spec_decode(list(p), steps, G) for p in prompts]
+    finally:
+        om.set_kv_bf16(False)
+    ctx.set_dense_min_cols(10**6)  # every projection on the exact small-N kernel
+    ctx.set_kv_bf16(True)
+    try:
+        st = State(model, max_ctx, batch=B)
+        firsts = np.atleast_1d(st.prefill(prompts if B > 1 else prompts[0]))
+        assert [int(f) for f in firsts] == [r[0][0] for r in ref]
+        for s in range(steps):
+            st.spec_step(G)
+            lg, _, tk = st.last_verify()
+            lg = lg.reshape(B, G + 1, V)
+            tk = tk.reshape(B, G + 1)
+            for b in range(B):
+                r = ref[b][1][s]
+                assert list(tk[b, 1:]) == r["drafts"], (b, s)
+                assert O.norm_rel(lg[b], r["logits"]).max() < KV16_TOL, (b, s)
+        for b in range(B):
+            toks, *_ = st.read(b)
+            assert list(toks) == ref[b][0], b
+        st.free()
+    finally:
+        ctx.set_kv_bf16(False)
+        ctx.set_dense_min_cols(24)
+
+
+@pytest.mark.parametrize("B,P,max_ctx", [(3, 200, 512), (1, 300, 1024)])
+def test_kv_bf16_head_dim_64(O, ctx, mini, B, P, max_ctx):
+    """ifr_ctx_set_kv_bf16 on the mini model (head dim 64, 2 q heads per KV
+    head): a batch, and one request whose long cache takes the split path"""
+    model, om = mini
+    _kv_bf16_run(O, ctx, model, om, B, P, max_ctx)
+
+
+def test_kv_bf16_head_dim_256(O, pkg, ctx):
+    """ifr_ctx_set_kv_bf16 at config-1/4 attention shapes (head dim 256, 4 q
+    heads per KV head: 20 rows of 5 verify columns in two m-tiles)"""
+    from inferno_b200 import synth, gguf
+    from inferno_b200.engine import Model
+    path = synth.cached("tiny", seed=0)
+    model = Model(ctx, path)
+    om = O.OracleModel(gguf.GGUFFile(path), 256)
+    try:
+        _kv_bf16_run(O, ctx, model, om, 2, 90, 256, steps=2)
+    finally:
+        om.close()
+        model.free()
+
+
+def test_kv_bf16_not_on_short_single_request(ctx, mini):
+    """one request with a short cache keeps the single-launch f32 attention
+    (the flag applies to split-KV states only): identical to the flag off"""
+    from inferno_b200.engine import State
+    model, _ = mini
+    prompt = _prompts(model.info.vocab, 1, 40)[0]
+    outs = []
+    for on in (False, True):
+        ctx.set_kv_bf16(on)
+        try:
+            st = State(model, 256)
+            st.prefill(prompt)
+            for _ in range(3):
+                st.spec_step(4)
+            outs.append(st.last_verify()[0].copy())
+            st.free()
+        finally:
+            ctx.set_kv_bf16(False)
+    assert np.array_equal(outs[0], outs[1])
