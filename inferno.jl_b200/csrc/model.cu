@@ -1694,13 +1694,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_part_mma_kernel(AttnArgs 
             for (int i = 0; i < 4; i++) oacc[m][u][i] = 0.f;
     for (int c = 0; c < nch; c++) {
         const int bf = c & 1, j0 = lo + c * kGrpKeys, nj = min(kGrpKeys, hi - j0);
-        if (c + 1 < nch) {
-            stage(c + 1, bf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
+        cp_async_wait<0>();
+        __syncthreads();  // chunk c complete; every warp is past chunk c - 1
+        if (c + 1 < nch) stage(c + 1, bf ^ 1);  // into the buffer of chunk c - 1
         const float *kb = Ks + bf * kGrpKeys * KS, *vb = Vs + bf * kGrpKeys * VS;
         {   // scores: warp (k half = warp / 8, m = warp / 4 % 2, key tile nb = warp % 4);
             //   each half sums its HD / 2 dims into its own buffer (sc, sc2)
@@ -1749,24 +1745,40 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_part_mma_kernel(AttnArgs 
             }
         }
         __syncthreads();
-        for (int r = warp; r < R; r += NWP) {  // online softmax, one warp per row
-            // the two halves' dot products, scaled, capped and masked
-            const int j = j0 + lane;
-            const float sv = lane < kGrpKeys && lane < nj && key_visible(a, j, p0 + r % N)
-                                 ? score_cap(a, (sc[r * SS + lane] + sc2[r * SS + lane]) * scale)
-                                 : -CUDART_INF_F;
-            const float mo = ms[r], mn = fmaxf(mo, warp_max(sv));
-            float f = 1.f, e = 0.f;
+        {   // online softmax, one half-warp per row (keys l16 and l16 + 16): all rows in one
+            // round; the two halves' dot products, scaled, capped and masked
+            const int r = 2 * warp + (lane >> 4), l16 = lane & 15;
+            const bool rv = r < R;
+            float sv[2] = {-CUDART_INF_F, -CUDART_INF_F};
+            if (rv) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int jj = l16 + 16 * h;
+                    if (jj < nj && key_visible(a, j0 + jj, p0 + r % N))
+                        sv[h] = score_cap(a, (sc[r * SS + jj] + sc2[r * SS + jj]) * scale);
+                }
+            }
+            float mx = fmaxf(sv[0], sv[1]);
+#pragma unroll
+            for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mo = rv ? ms[r] : -CUDART_INF_F, mn = fmaxf(mo, mx);
+            float f = 1.f, e[2] = {0.f, 0.f};
             if (mn != -CUDART_INF_F) {
                 f = expf(mo - mn);
-                e = expf(sv - mn);
+                e[0] = expf(sv[0] - mn);
+                e[1] = expf(sv[1] - mn);
             }
-            if (lane < kGrpKeys) sc[r * SS + lane] = e;
-            const float ps = warp_sum(e);
-            if (lane == 0) {
-                ls[r] = ls[r] * f + ps;
-                ms[r] = mn;
-                fs[r] = f;
+            float ps = e[0] + e[1];
+#pragma unroll
+            for (int o = 8; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            if (rv) {
+                sc[r * SS + l16] = e[0];
+                sc[r * SS + l16 + 16] = e[1];
+                if (l16 == 0) {
+                    ls[r] = ls[r] * f + ps;
+                    ms[r] = mn;
+                    fs[r] = f;
+                }
             }
         }
         __syncthreads();
@@ -1803,7 +1815,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_part_mma_kernel(AttnArgs 
                 }
             }
         }
-        __syncthreads();  // this chunk's buffer, sc and fs are rewritten next
+        // no barrier here: the next chunk's first barrier comes before anything
+        // this chunk read (its buffer, sc, fs) is rewritten
     }
 
     // 3. the slice's partial state
