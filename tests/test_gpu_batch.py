@@ -186,7 +186,8 @@ def test_batch_dense_fp16_stages_bit_exact(pkg, ctx):
 def _kv_bf16_run(O, ctx, model, om, B, P, max_ctx, G=4, steps=3):
     """spec steps of a state with bf16 attention caches against the oracle
     rounding its cache rows the same way (or_model_set_kv_bf16): drafts,
-    tokens and accept counts equal, verify logits within KV16_TOL"""
+    tokens and accept counts equal, verify logits within KV16_TOL; the first
+    verify's logits also within DENSE_TOL (1e-2) of the f32-cache oracle"""
     from inferno_b200.engine import State
     V = model.info.vocab
     prompts = _prompts(V, B, P)
@@ -195,6 +196,10 @@ def _kv_bf16_run(O, ctx, model, om, B, P, max_ctx, G=4, steps=3):
         ref = [om.spec_decode(list(p), steps, G) for p in prompts]
     finally:
         om.set_kv_bf16(False)
+    # the f32-cache oracle's first verify (same drafts: the bf16 cache enters
+    # only through the attention), for the north star's 1e-2 bound
+    ref32 = [om.spec_decode(list(p), 1, G, drafts=lambda s, b=b: ref[b][1][0]["drafts"])[1][0]["logits"]
+             for b, p in enumerate(prompts)]
     ctx.set_dense_min_cols(10**6)  # every projection on the exact small-N kernel
     ctx.set_kv_bf16(True)
     try:
@@ -210,6 +215,8 @@ def _kv_bf16_run(O, ctx, model, om, B, P, max_ctx, G=4, steps=3):
                 r = ref[b][1][s]
                 assert list(tk[b, 1:]) == r["drafts"], (b, s)
                 assert O.norm_rel(lg[b], r["logits"]).max() < KV16_TOL, (b, s)
+                if s == 0:
+                    assert O.norm_rel(lg[b], ref32[b]).max() < DENSE_TOL, b
         for b in range(B):
             toks, *_ = st.read(b)
             assert list(toks) == ref[b][0], b
