@@ -551,24 +551,50 @@ __device__ __forceinline__ void ssm_batch_body(SsmArgs a, int h, int64_t b) {
 #pragma unroll
         for (int t = 0; t < kMaxN; t++) pa[t] = pb[t] = ps[t] = 0.f;
         const float *wa = a.ab_w + (int64_t)h * a.d, *wb = a.ab_w + (int64_t)(a.H + h) * a.d;
-        for (int i = tid; i < a.d; i += NT) {
-            const float al = wa[i], be = wb[i], nw = a.in_norm ? a.in_norm[i] : 1.f;
+        if ((a.d & 3) == 0) {
+            // 16-byte loads, every load of an iteration (weights, norm weights,
+            // the N token rows) issued before the first use: d / (4 NT)
+            // memory round trips instead of d / NT
+            for (int i = 4 * tid; i < a.d; i += 4 * NT) {
+                const float4 al = *reinterpret_cast<const float4 *>(wa + i);
+                const float4 be = *reinterpret_cast<const float4 *>(wb + i);
+                const float4 nw = a.in_norm ? *reinterpret_cast<const float4 *>(a.in_norm + i)
+                                            : make_float4(1.f, 1.f, 1.f, 1.f);
+                float4 xv[kMaxN];
 #pragma unroll
-            for (int t = 0; t < kMaxN; t++)
-                if (t < N) {
-                    const float xv = a.xn[(int64_t)t * a.d + i], xn = xv * nw;
-                    pa[t] += al * xn;
-                    pb[t] += be * xn;
-                    ps[t] += xv * xv;
+                for (int t = 0; t < kMaxN; t++)
+                    xv[t] = t < N ? *reinterpret_cast<const float4 *>(a.xn + (int64_t)t * a.d + i)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int t = 0; t < kMaxN; t++) {
+                    const float4 x = xv[t];
+                    pa[t] += al.x * (x.x * nw.x) + al.y * (x.y * nw.y) + al.z * (x.z * nw.z) + al.w * (x.w * nw.w);
+                    pb[t] += be.x * (x.x * nw.x) + be.y * (x.y * nw.y) + be.z * (x.z * nw.z) + be.w * (x.w * nw.w);
+                    ps[t] += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
                 }
+            }
+        } else {
+            for (int i = tid; i < a.d; i += NT) {
+                const float al = wa[i], be = wb[i], nw = a.in_norm ? a.in_norm[i] : 1.f;
+#pragma unroll
+                for (int t = 0; t < kMaxN; t++)
+                    if (t < N) {
+                        const float xv = a.xn[(int64_t)t * a.d + i], xn = xv * nw;
+                        pa[t] += al * xn;
+                        pb[t] += be * xn;
+                        ps[t] += xv * xv;
+                    }
+            }
         }
 #pragma unroll
         for (int t = 0; t < kMaxN; t++) {
-            const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]), vs = warp_sum(ps[t]);
-            if (lane == 0) {
-                red_n[warp][t] = va;
-                red_n[warp][kMaxN + t] = vb;
-                red_n[warp][2 * kMaxN + t] = vs;
+            if (t < N) {  // uniform: only the present tokens' sums
+                const float va = warp_sum(pa[t]), vb = warp_sum(pb[t]), vs = warp_sum(ps[t]);
+                if (lane == 0) {
+                    red_n[warp][t] = va;
+                    red_n[warp][kMaxN + t] = vb;
+                    red_n[warp][2 * kMaxN + t] = vs;
+                }
             }
         }
     }
@@ -1907,7 +1933,7 @@ template <int HD>
 __global__ void __launch_bounds__(kMmaThreads, 1) attn_part_bf16_kernel(AttnArgs a, int hg, int S) {
     using M = Bf16Smem<HD>;
     constexpr int QP = M::QP, PP = M::PP, SS = M::SS, NR = M::kRows;
-    constexpr int NTH = kMmaThreads, NWP = NTH / 32;
+    constexpr int NTH = kMmaThreads;
     // P.V: HD >= 128: every warp both m-tiles and NTW adjacent n-tiles;
     // HD 64: warp w the m-tile w / 8 and the n-tile w % 8
     constexpr int MT = HD >= 128 ? 2 : 1, NTW = HD >= 128 ? HD / 128 : 1;
