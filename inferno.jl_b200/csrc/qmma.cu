@@ -584,12 +584,10 @@ __global__ void __launch_bounds__(kDqThreads) qmma_f16_stages_kernel(const uint8
     }
 }
 
-// pack the columns of one n-tile to fp16 in the per-stage operand layout,
-// scaled by 2^e per column (max |x| 2^e in [2^13, 2^14)), the K slots of each
-// group of four holding the elements (0, 2, 1, 3) like the weights; the
-// activation transform of the GEMV (RMSNorm, SwiGLU) is applied on the way
+// pack_x_kernel for columns too long to hold in shared memory: every pass
+// (sum of squares, max, pack) reads the column again
 template <int XF>
-__global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ X, int64_t ldx, int64_t K, int ncols,
+__global__ void __launch_bounds__(256) pack_x_stream_kernel(const float *__restrict__ X, int64_t ldx, int64_t K, int ncols,
                                                      int npad, int nu, const float *__restrict__ xw, float eps,
                                                      uint16_t *__restrict__ Xp, float *__restrict__ xinv) {
     __shared__ float red[8];
@@ -650,6 +648,112 @@ __global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ X
                                    pack_h2(value(k0 + 1) * scl, value(k0 + 3) * scl),
                                    pack_h2(value(k0 + 4) * scl, value(k0 + 6) * scl),
                                    pack_h2(value(k0 + 5) * scl, value(k0 + 7) * scl));
+        *reinterpret_cast<uint4 *>(Xp + ((((int64_t)tile * nu * 4 + kst) * 8 + ch) * npad + n) * 8) = w;
+    }
+}
+
+// pack the columns of one n-tile to fp16 in the per-stage operand layout,
+// scaled by 2^e per column (max |x| 2^e in [2^13, 2^14)), the K slots of each
+// group of four holding the elements (0, 2, 1, 3) like the weights; the
+// activation transform of the GEMV (RMSNorm, SwiGLU) is applied on the way.
+// One CTA per column; the column is read from global memory once, in batches
+// of eight loads per thread issued before their use, into shared memory
+// (nu * 256 floats), and the max and pack passes read it there.  Every value
+// and sum is formed in the same order as by pack_x_stream_kernel (thread tid
+// sums elements tid, tid + 256, ... in turn), so the results are the same bits.
+constexpr int kPackSmemMax = 192 * 1024;
+template <int XF>
+__global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ X, int64_t ldx, int64_t K, int ncols,
+                                                     int npad, int nu, const float *__restrict__ xw, float eps,
+                                                     uint16_t *__restrict__ Xp, float *__restrict__ xinv) {
+    extern __shared__ __align__(16) float xs[];  // [nu * 256] the column's values (0 past K)
+    __shared__ float red[8];
+    __shared__ float bc;
+    pdl_trigger();
+    pdl_wait();
+    const int col = blockIdx.x, tile = col / npad, n = col % npad;  // tiles hold consecutive columns
+    const int tid = threadIdx.x;
+    const int64_t KP = (int64_t)nu * 256, nchunks = (int64_t)nu * 32;
+    const bool has = col < ncols;
+    const float *xc = X + (int64_t)col * ldx;
+    auto block_reduce = [&](float v, bool is_max) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float w = __shfl_xor_sync(0xffffffffu, v, o);
+            v = is_max ? fmaxf(v, w) : v + w;
+        }
+        __syncthreads();
+        if ((tid & 31) == 0) red[tid >> 5] = v;
+        __syncthreads();
+        if (tid == 0) {
+            float r = red[0];
+            for (int w = 1; w < 8; w++) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+            bc = r;
+        }
+        __syncthreads();
+        return bc;
+    };
+    constexpr int LB = 8;  // loads in flight per thread
+    // 1. the column (SwiGLU: silu(gate) * up) into shared memory; RMSNorm: raw
+    //    values and their sum of squares
+    float ss = 0.f, mx = 0.f;
+    for (int64_t k0 = tid; k0 < KP; k0 += 256 * LB) {
+        float g[LB], u[LB];
+#pragma unroll
+        for (int i = 0; i < LB; i++) {
+            const int64_t k = k0 + 256 * i;
+            const bool in = has && k < K;
+            g[i] = in ? xc[k] : 0.f;
+            u[i] = (XF == 2 && in) ? xc[K + k] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < LB; i++) {
+            const int64_t k = k0 + 256 * i;
+            if (k < KP) {
+                float v = g[i];
+                if (XF == 1) ss += v * v;
+                if (XF == 2) v = (has && k < K) ? v / (1.0f + expf(-v)) * u[i] : 0.f;
+                if (XF != 1) mx = fmaxf(mx, fabsf(v));
+                xs[k] = v;
+            }
+        }
+    }
+    if (XF == 1) {
+        // 2. RMSNorm: x * inv * w in place
+        const float inv = has ? 1.0f / sqrtf(block_reduce(ss, false) / (float)K + eps) : 1.f;
+        for (int64_t k0 = tid; k0 < KP; k0 += 256 * LB) {
+            float w[LB];
+#pragma unroll
+            for (int i = 0; i < LB; i++) {
+                const int64_t k = k0 + 256 * i;
+                w[i] = has && k < K ? xw[k] : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < LB; i++) {
+                const int64_t k = k0 + 256 * i;
+                if (k < KP) {
+                    const float v = has && k < K ? xs[k] * inv * w[i] : 0.f;
+                    mx = fmaxf(mx, fabsf(v));
+                    xs[k] = v;
+                }
+            }
+        }
+    }
+    mx = block_reduce(mx, true);  // its barriers also order the shared stores before the reads below
+    int e = 0;
+    if (mx > 0.f && !isinf(mx)) {
+        int ex;
+        frexpf(mx, &ex);
+        e = 14 - ex;
+        e = e < -100 ? -100 : (e > 100 ? 100 : e);
+    }
+    const float scl = __int_as_float((e + 127) << 23);
+    if (tid == 0) xinv[col] = has ? __int_as_float((127 - e) << 23) : 0.f;
+    for (int64_t c = tid; c < nchunks; c += 256) {
+        const int64_t kst = c >> 3, ch = c & 7, k0 = 8 * c;
+        const float4 a = *reinterpret_cast<const float4 *>(xs + k0), b = *reinterpret_cast<const float4 *>(xs + k0 + 4);
+        const uint4 w = make_uint4(pack_h2(a.x * scl, a.z * scl), pack_h2(a.y * scl, a.w * scl),
+                                   pack_h2(b.x * scl, b.z * scl), pack_h2(b.y * scl, b.w * scl));
         *reinterpret_cast<uint4 *>(Xp + ((((int64_t)tile * nu * 4 + kst) * 8 + ch) * npad + n) * 8) = w;
     }
 }
@@ -784,6 +888,32 @@ int64_t qgemm_dense_scratch_bytes(const QTensor &T, int ncols) {
     return p.xp_bytes + p.xinv_bytes + p.ws_bytes;
 }
 
+// the activation packing of one GEMM: the column held in shared memory
+// (pack_x_kernel) up to kPackSmemMax bytes, else re-read per pass
+template <int XF>
+static cudaError_t launch_pack_xf(dim3 pg, cudaStream_t s, const float *X, int64_t ldx, int64_t K, int ncols, int npad,
+                                  int nu, const float *xw, float eps, uint16_t *Xp, float *xinv) {
+    const int64_t smem = (int64_t)nu * 256 * 4;
+    if (smem > kPackSmemMax)
+        return launch_k(pack_x_stream_kernel<XF>, pg, dim3(256), 0, s, X, ldx, K, ncols, npad, nu, xw, eps, Xp, xinv);
+    static DeviceFlags attr;
+    if (!attr.test()) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(pack_x_kernel<XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmemMax);
+        if (e != cudaSuccess) return e;
+        attr.set();
+    }
+    return launch_k(pack_x_kernel<XF>, pg, dim3(256), (size_t)smem, s, X, ldx, K, ncols, npad, nu, xw, eps, Xp, xinv);
+}
+static cudaError_t launch_pack(int kind, dim3 pg, cudaStream_t s, const float *X, int64_t ldx, int64_t K, int ncols,
+                               int npad, int nu, const float *xw, float eps, uint16_t *Xp, float *xinv) {
+    switch (kind) {
+    case 0: return launch_pack_xf<0>(pg, s, X, ldx, K, ncols, npad, nu, xw, eps, Xp, xinv);
+    case 1: return launch_pack_xf<1>(pg, s, X, ldx, K, ncols, npad, nu, xw, eps, Xp, xinv);
+    default: return launch_pack_xf<2>(pg, s, X, ldx, K, ncols, npad, nu, xw, eps, Xp, xinv);
+    }
+}
+
 cudaError_t qgemm_dense(const QTensor &T, const float *X, int ncols, float *Y, bool accumulate, int64_t ldy,
                         cudaStream_t s, const XForm &xf, void *scratch, int64_t scratch_bytes) {
     Plan p;
@@ -797,12 +927,8 @@ cudaError_t qgemm_dense(const QTensor &T, const float *X, int ncols, float *Y, b
     float *ws = p.ws_bytes ? reinterpret_cast<float *>(sc + p.xp_bytes + p.xinv_bytes) : nullptr;
     const int64_t ldx = xf.ldx > 0 ? xf.ldx : T.cols;
     const dim3 pg((unsigned)(p.ntiles * p.npad));
-    cudaError_t e;
-    switch (xf.kind) {
-    case 0: e = launch_k(pack_x_kernel<0>, pg, dim3(256), 0, s, X, ldx, (int64_t)T.cols, ncols, p.npad, (int)T.nu, xf.w, xf.eps, Xp, xinv); break;
-    case 1: e = launch_k(pack_x_kernel<1>, pg, dim3(256), 0, s, X, ldx, (int64_t)T.cols, ncols, p.npad, (int)T.nu, xf.w, xf.eps, Xp, xinv); break;
-    default: e = launch_k(pack_x_kernel<2>, pg, dim3(256), 0, s, X, ldx, (int64_t)T.cols, ncols, p.npad, (int)T.nu, xf.w, xf.eps, Xp, xinv); break;
-    }
+    cudaError_t e = launch_pack(xf.kind, pg, s, X, ldx, (int64_t)T.cols, ncols, p.npad, (int)T.nu, xf.w, xf.eps, Xp,
+                                xinv);
     if (e != cudaSuccess) return e;
     MmaArgs a{T.data, (int)T.nrb, (int)T.nu, Xp, xinv, ncols, p.npad, p.ntiles, p.nch, p.splits, p.RS, p.ST,
               Y, ldy, T.rows, accumulate ? 1 : 0, xf.ep, ws, T.f16};
