@@ -784,6 +784,58 @@ __global__ void qmma_reduce_kernel(const float *__restrict__ ws, int splits, int
     }
 }
 
+// the same sums four rows per thread: 16-byte loads of every split issued
+// before the adds (each element summed in split order, as above)
+__global__ void qmma_reduce4_kernel(const float *__restrict__ ws, int splits, int ncols, int64_t mpad, float *Y,
+                                    int64_t ldy, int64_t M, int accumulate, int ep) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t mo = ep ? M / 2 : M, mq = mo / 4;
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= mq * ncols) return;
+    const int col = (int)(i / mq);
+    const int64_t r = 4 * (i % mq);
+    auto sum = [&](int64_t row) {
+        constexpr int kMaxSplit = 8;
+        float4 t[kMaxSplit];
+#pragma unroll
+        for (int zz = 0; zz < kMaxSplit; zz++)
+            if (zz < splits) t[zz] = *reinterpret_cast<const float4 *>(ws + ((int64_t)zz * ncols + col) * mpad + row);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int zz = 0; zz < kMaxSplit; zz++)
+            if (zz < splits) {
+                v.x += t[zz].x;
+                v.y += t[zz].y;
+                v.z += t[zz].z;
+                v.w += t[zz].w;
+            }
+        for (int zz = kMaxSplit; zz < splits; zz++) {
+            const float4 u = *reinterpret_cast<const float4 *>(ws + ((int64_t)zz * ncols + col) * mpad + row);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+        }
+        return v;
+    };
+    float4 *y = reinterpret_cast<float4 *>(Y + (int64_t)col * ldy + r);
+    if (ep) {
+        const int64_t g = (r >> 4) * 32 + (r & 15);  // four rows of one 16-row gate block
+        const float4 gv = sum(g), uv = sum(g + 16);
+        *y = make_float4(glu_act(ep, gv.x, uv.x), glu_act(ep, gv.y, uv.y), glu_act(ep, gv.z, uv.z),
+                         glu_act(ep, gv.w, uv.w));
+    } else {
+        const float4 v = sum(r);
+        if (accumulate) {
+            const float4 o = *y;
+            *y = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+        } else {
+            *y = v;
+        }
+    }
+}
+
 namespace {
 
 int sm_count() { return device_sm_count(); }
@@ -940,9 +992,12 @@ cudaError_t qgemm_dense(const QTensor &T, const float *X, int ncols, float *Y, b
     default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess || p.splits == 1) return e;
-    const int64_t n = (xf.ep ? T.rows / 2 : T.rows) * ncols;
+    const int64_t mo = xf.ep ? T.rows / 2 : T.rows, n = mo * ncols, mpad = (int64_t)T.nrb * 16;
+    if (mo % 4 == 0 && ldy % 4 == 0 && ((uintptr_t)Y & 15) == 0 && ((uintptr_t)ws & 15) == 0)
+        return launch_k(qmma_reduce4_kernel, dim3((unsigned)((n / 4 + 255) / 256)), dim3(256), 0, s,
+                        (const float *)ws, p.splits, ncols, mpad, Y, ldy, (int64_t)T.rows, accumulate ? 1 : 0, xf.ep);
     return launch_k(qmma_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, (const float *)ws,
-                    p.splits, ncols, (int64_t)T.nrb * 16, Y, ldy, (int64_t)T.rows, accumulate ? 1 : 0, xf.ep);
+                    p.splits, ncols, mpad, Y, ldy, (int64_t)T.rows, accumulate ? 1 : 0, xf.ep);
 }
 
 cudaError_t read_mma_error(int *flag, cudaStream_t s) {
