@@ -401,7 +401,7 @@ SPEC_PRESET, SPEC_SEED, SPEC_PROMPT = "tiny", 0, 128
 SPEC_GEN = 128  # config 1: 128 greedy tokens per request
 # DRAM bytes (read + write) of the verify's 97 GEMV launches, from one ncu
 # capture of `bench.py --profile spec` (profiles/spec_step_launches_config1.md)
-SPEC_VERIFY_TRAFFIC = 417875968
+SPEC_VERIFY_TRAFFIC = 418144512
 
 
 def spec_bytes_per_step_gguf(gf, gamma):
