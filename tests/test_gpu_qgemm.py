@@ -240,10 +240,11 @@ def test_argument_errors(O, ctx, pkg):
 
 # tall matrices (>= 2 x 148 groups of 15 row blocks): the row-block-per-warp
 # kernel, which keeps every unit's fragments in shared memory (K = 1024, and
-# K = 4096 with Q8_K activations); exact activations at K = 4096 with 5+
-# columns split K over CTA pairs (half the fragments each, the second half's
-# partials added by a second kernel); Q8_0 at K = 4096 (larger tiles) and Q4_K
-# with Q8_K activations take the unit-split kernel
+# K = 4096 with Q8_K activations); exact Q4_K / Q5_K activations as int8
+# limbs; exact activations whose fragments leave too little room split K over
+# CTA pairs (half the fragments each, the second half's partials added by a
+# second kernel); Q8_0 at K = 4096 (larger tiles) and Q4_K with Q8_K
+# activations take the unit-split kernel
 TALL = [(12, 1024), (13, 1024), (14, 1024), (8, 1024), (12, 4096), (13, 4096), (14, 4096), (8, 4096)]
 
 
@@ -264,7 +265,7 @@ def test_qgemm_tall(O, ctx, qt, K, act):
     Xd = torch.from_numpy(X).cuda()
     ctx.set_activation(act)
     try:
-        for n in (1, 5, 8):
+        for n in (1, 2, 3, 5, 6, 8):
             Y = ctx.qgemm(W, Xd[:n].contiguous()).cpu().numpy()
             err = O.norm_rel(Y, ref[:n][:, idx])
             assert err.max() < TOL, (NAMES[qt], K, n, act, err)
@@ -276,12 +277,13 @@ def test_qgemm_tall(O, ctx, qt, K, act):
         ctx.set_activation(0)
 
 
-@pytest.mark.parametrize("qt", [12, 13])
+@pytest.mark.parametrize("qt", [12, 13, 14])
 def test_qgemm_tall_exact_outlier_channels(O, ctx, qt):
     """exact activations with a few massive channels (200x the others): the
     Q4_K / Q5_K tall kernel writes each unit of a column as three int8 limbs
     over the unit's amax, so small elements beside an outlier keep ~6e-8 of
-    that amax; still within TOL of the oracle's f32 dot products"""
+    that amax (Q6_K keeps the fp16 hi/lo split); still within TOL of the
+    oracle's f32 dot products"""
     torch = _torch()
     M, K = 71040 + 5, 4096
     rng = np.random.default_rng(qt + 777)
